@@ -1,0 +1,282 @@
+/*
+ * libsdxcuda -- B200 (sm_100a) CUDA execution backend for SimdOnnx's fused conv/GEMM hot path.
+ *
+ * C ABI: plain pointers, sizes and POD descriptor structs; no C++ exceptions cross it. Every
+ * function returns an int status (SDX_OK = 0); the message of the last failure on the calling
+ * thread is read with sdx_last_error. Device pointers are opaque uint64 (sdx_dptr). A context is
+ * used from one host thread at a time; different devices may run on different threads.
+ *
+ * It is the fourth execution backend beside the reference's CPU, Vulkan and Metal ones
+ * (PlanTarget, src/Sdcb.SimdOnnx/Engine/ExecPlan.cs:320). The reference's Vulkan backend lowers
+ * every ExecNode to a dispatch record (VkGraphModel.Emit, src/Sdcb.SimdOnnx/Backends/Vulkan/
+ * VkGraph.cs:472-1112) over one device arena whose plan offsets map 1:1 to buffer offsets
+ * (VkGraph.cs:362-378) and records them into one command buffer (VkSession.cs:282-337). Here the
+ * same node list is issued through the sdx_* op entry points below on device pointers
+ * (arena base + BufOffset * element size) and captured once into a CUDA graph by a session.
+ *
+ * Paths in comments are relative to the reference project root (src/ = src/Sdcb.SimdOnnx/).
+ */
+#ifndef SDXCUDA_H
+#define SDXCUDA_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#if defined(__GNUC__)
+#pragma GCC visibility push(default)
+#endif
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define SDX_ABI_VERSION 1
+
+/* ---- status codes (VkDevice errors -> exceptions in the reference, src/Backends/Vulkan/VkDevice.cs:11-18) */
+#define SDX_OK 0
+#define SDX_ERR_INVALID 1
+#define SDX_ERR_CUDA 2
+#define SDX_ERR_OOM 3
+#define SDX_ERR_TIMEOUT 4
+#define SDX_ERR_DEVICE 5
+#define SDX_ERR_INJECTED 6
+#define SDX_ERR_POISONED 7
+#define SDX_ERR_NOT_SUPPORTED 8
+
+typedef uint64_t sdx_dptr;
+typedef struct sdx_ctx sdx_ctx;
+typedef struct sdx_session sdx_session;
+typedef void* sdx_stream; /* a cudaStream_t; NULL = the context's own stream */
+
+/* ---- enums of the reference plan (src/Engine/ExecPlan.cs:42-46) */
+enum sdx_act { SDX_ACT_NONE = 0, SDX_ACT_RELU = 1, SDX_ACT_SIGMOID = 2, SDX_ACT_GELU = 3, SDX_ACT_HARDSWISH = 4, SDX_ACT_SWISH = 5 };
+enum sdx_ew { SDX_EW_ADD = 0, SDX_EW_SUB = 1, SDX_EW_MUL = 2, SDX_EW_DIV = 3 };
+enum sdx_dtype { SDX_F16 = 0, SDX_F32 = 1 };
+enum sdx_layout { SDX_NHWC = 0, SDX_NCHW = 1 };
+
+/* ======================================================================================
+ * Runtime (replaces the Vulkan device / buffer / queue layer, src/Backends/Vulkan/VkDevice.cs,
+ * src/Backends/Vulkan/Vk.cs:452 P/Invoke surface)
+ * ====================================================================================== */
+int sdx_abi_version(void);
+int sdx_last_error(char* buf, int len);
+int sdx_device_count(int* count);
+/* One context per device: owns a stream and a device error word (VkBackend.Default, VkBackend.cs:26-47). */
+int sdx_open(int ordinal, sdx_ctx** ctx);
+int sdx_close(sdx_ctx* ctx);
+int sdx_ctx_stream(sdx_ctx* ctx, sdx_stream* stream);
+int sdx_device_info(sdx_ctx* ctx, char* name, int name_len, int* sm_count, int* cc_major, int* cc_minor,
+                    size_t* total_mem);
+/* Device memory (the whole arena is one allocation, VkSession.cs:83-143). */
+int sdx_malloc(sdx_ctx* ctx, size_t bytes, sdx_dptr* out);
+int sdx_free(sdx_ctx* ctx, sdx_dptr p);
+int sdx_host_alloc_pinned(size_t bytes, void** out);
+int sdx_host_free(void* p);
+int sdx_memcpy_htod_async(sdx_ctx* ctx, sdx_dptr dst, const void* src, size_t bytes, sdx_stream s);
+int sdx_memcpy_dtoh_async(sdx_ctx* ctx, void* dst, sdx_dptr src, size_t bytes, sdx_stream s);
+int sdx_memcpy_dtod_async(sdx_ctx* ctx, sdx_dptr dst, sdx_dptr src, size_t bytes, sdx_stream s);
+int sdx_memset_async(sdx_ctx* ctx, sdx_dptr dst, int value, size_t bytes, sdx_stream s);
+/* Streams (queue submit / fence wait, VkDevice.cs:885-898). timeout_ms <= 0 waits without a deadline;
+ * otherwise SDX_ERR_TIMEOUT when the stream is still busy at the deadline (host watchdog). A device
+ * error word set by a kernel turns into SDX_ERR_DEVICE and poisons the context. */
+int sdx_stream_create(sdx_ctx* ctx, sdx_stream* out);
+int sdx_stream_destroy(sdx_ctx* ctx, sdx_stream s);
+int sdx_stream_sync(sdx_ctx* ctx, sdx_stream s, int timeout_ms);
+int sdx_stream_query(sdx_ctx* ctx, sdx_stream s, int* done);
+int sdx_event_create(sdx_ctx* ctx, void** ev);
+int sdx_event_record(sdx_ctx* ctx, void* ev, sdx_stream s);
+int sdx_event_elapsed_ms(void* start, void* stop, float* ms);
+int sdx_event_destroy(void* ev);
+/* CUDA graphs (the pre-recorded command buffer of VkInferenceSession.Record, VkSession.cs:282-337). */
+int sdx_graph_begin(sdx_ctx* ctx, sdx_stream s);
+int sdx_graph_end(sdx_ctx* ctx, sdx_stream s, void** graph_exec);
+int sdx_graph_launch(sdx_ctx* ctx, void* graph_exec, sdx_stream s);
+int sdx_graph_destroy(void* graph_exec);
+/* Device error word: first error code a kernel recorded (bounded waits), 0 = none. */
+int sdx_device_error(sdx_ctx* ctx, unsigned int* code);
+int sdx_clear_device_error(sdx_ctx* ctx);
+/* Fault injection (host side only; no GPU fault is ever provoked): the nth (1-based) call of `kind`
+ * after this call returns SDX_ERR_INJECTED. kind: 1 malloc, 2 kernel launch, 3 graph launch,
+ * 4 device-to-host copy, 5 stream sync. nth = 0 clears. Mirrors the host-faked device loss of
+ * tests/Sdcb.SimdOnnx.Tests/VkDeviceLossTests.cs:28-33. */
+int sdx_fault_inject(int kind, int nth);
+/* Number of kernels this library launched in this process (bench accounting). */
+uint64_t sdx_launch_count(void);
+/* Self-test of the bounded device wait: one tiny kernel spins on a flag nothing sets for at most
+ * `wait_ms` and then records SDX_DEV_TEST_WAIT (0x1F0) in the error word and returns. */
+int sdx_selftest_bounded_wait(sdx_ctx* ctx, int wait_ms, sdx_stream s);
+
+/* ======================================================================================
+ * Weight packing (host): the backend-private const kinds of the GPU backends
+ * (ConstKind / GpuPack, src/Engine/Extensions.cs:125-245); fp16 except biases (fp32).
+ * Call with out == NULL to get the size in bytes in *bytes.
+ * ====================================================================================== */
+/* ConvP weights w [oc][ic/group][kh][kw] for the kernel sdx_conv2d routes `d` to (Nhwc.Pack,
+ * src/Kernels/Nhwc.cs:102-125). */
+struct sdx_conv_desc;
+int sdx_pack_conv(const struct sdx_conv_desc* d, const float* w, void* out, size_t* bytes);
+/* ConvTP weights w [ic][oc][kh][kw] (Nhwc.PackConvT, src/Kernels/Nhwc.Det.cs:26-44). */
+int sdx_pack_convt(int ic, int oc, int kh, int kw, const float* w, void* out, size_t* bytes);
+/* GemmP B [K,N] (or [N,K] when trans_b) (Nhwc.PackGemm, src/Kernels/Nhwc.cs:127-138). */
+int sdx_pack_gemm(int k, int n, int trans_b, const float* b, void* out, size_t* bytes);
+
+/* ======================================================================================
+ * Ops: one entry point per fused ExecNode kind, enqueued on a stream, device pointers only.
+ * ====================================================================================== */
+
+/* Fused conv node: ConvP (src/Engine/ExecPlan.cs:50-65) executed by Nhwc.Conv / ConvPool
+ * (src/Kernels/Nhwc.cs:172-217, :666-727). y = act(conv(x) + bias [+ add]) [then 2x2/2 max pool].
+ * Routing (like VkGraphModel's conv routing, VkGraph.cs:159-320):
+ *   group == ic == oc            -> depthwise bandwidth kernel
+ *   ic % 8 == 0, stride 1, fp16  -> tcgen05 implicit GEMM (1x1 pad 0: batch folded into rows)
+ *   otherwise (stem: ic = 3, stride 2, fp32 / NCHW input) -> direct small-channel kernel. */
+typedef struct sdx_conv_desc {
+  int batch, ih, iw, ic;
+  int oh, ow, oc;
+  int kh, kw, sh, sw;
+  int pad_t, pad_l, pad_b, pad_r;
+  int group;
+  int act;           /* sdx_act */
+  int pool;          /* 1: fused 2x2/2 max pool epilogue (ConvP.Pool); y is then [batch, oh/2, ow/2, oc] */
+  int pool_relu;     /* relu after the pool (PoolP.FuseRelu) */
+  int x_dtype;       /* sdx_dtype */
+  int x_layout;      /* sdx_layout (NCHW only for the direct small-channel kernel: graph inputs) */
+  int y_dtype;       /* sdx_dtype */
+  int add_dtype;     /* sdx_dtype of the residual */
+  int add_layout;    /* sdx_layout of the residual */
+  int y_layout;      /* sdx_layout of the output */
+  int pad_mode;      /* PadMode: 0 constant (the only mode with a CUDA kernel), 1 reflect -> NOT_SUPPORTED */
+  float pad_value;   /* constant-mode fill; only 0 has a CUDA kernel */
+  int64_t y_pix_stride; /* elements between output pixels (0 = oc); > oc writes into a channel slice */
+  int y_ch_off;      /* first output channel in that slice */
+  sdx_dptr x, w, bias, add, y;  /* w: packed by sdx_pack_conv; bias fp32 [oc] or 0; add 0 = none */
+  sdx_dptr in_scale; /* fp32 [batch, ic] per-image channel scale applied to x on load (SE gate), or 0 */
+} sdx_conv_desc;
+int sdx_conv2d(sdx_ctx* ctx, const sdx_conv_desc* d, sdx_stream s);
+
+/* Gemm node: GemmP (src/Engine/ExecPlan.cs:87-93) via Nhwc.Gemm (src/Kernels/Nhwc.Avx512.cs:241-266):
+ * y[m, n] = act(a[m, k] . B + bias[n] [+ add[m, n]]), a fp16 row stride lda, y fp16/fp32. */
+typedef struct sdx_gemm_desc {
+  int m, k, n;
+  int64_t lda;
+  int act;
+  int y_dtype, add_dtype;
+  int64_t ldy, ldadd;
+  sdx_dptr a, w, bias, add, y;
+} sdx_gemm_desc;
+int sdx_gemm(sdx_ctx* ctx, const sdx_gemm_desc* d, sdx_stream s);
+
+/* ConvTranspose node, stride == kernel, no pad (ConvTP, src/Engine/ExecPlan.cs:108-114;
+ * Nhwc.ConvTranspose / ConvTDot, src/Kernels/Nhwc.Det.cs:51-131). x fp16 NHWC, y [b, ih*kh, iw*kw, oc]. */
+typedef struct sdx_convt_desc {
+  int batch, ih, iw, ic, oc, kh, kw;
+  int act, y_dtype;
+  sdx_dptr x, w, bias, y;  /* w packed by sdx_pack_convt (oc >= 8) or raw fp32 [ic][oc][kh][kw] (oc < 8) */
+} sdx_convt_desc;
+int sdx_convt(sdx_ctx* ctx, const sdx_convt_desc* d, sdx_stream s);
+
+/* Max / average pool (PoolP, src/Engine/ExecPlan.cs:67-74; Nhwc.MaxPool src/Kernels/Nhwc.cs:730-770,
+ * Nhwc.AvgPool src/Kernels/Ops.Seq.cs:180-225). fp16 NHWC. */
+typedef struct sdx_pool_desc {
+  int batch, ih, iw, c, oh, ow, kh, kw, sh, sw, pad_t, pad_l;
+  int is_avg, relu, count_include_pad;
+  sdx_dptr x, y;
+} sdx_pool_desc;
+int sdx_pool(sdx_ctx* ctx, const sdx_pool_desc* d, sdx_stream s);
+
+/* Squeeze-excitation gate (ChannelGateP, src/Engine/ExecPlan.cs:151-158; Nhwc.ChannelGate,
+ * src/Kernels/Nhwc.Det.cs:287-314): s[n, c] = gate(b2 + W2 . act1(b1 + W1 . mean_hw x[n])) + offset.
+ * x fp16 NHWC; w1 fp32 [r][c], w2 fp32 [c][r]; s fp32 [batch, c]. `partial` is device scratch of
+ * sdx_channel_gate_scratch_bytes() bytes (per-block channel sums). */
+typedef struct sdx_gate_desc {
+  int batch, hw, c, r;
+  int act1_relu, hard;
+  float alpha, beta, offset;
+  sdx_dptr x, w1, b1, w2, b2, s, partial;
+} sdx_gate_desc;
+size_t sdx_channel_gate_scratch_bytes(int batch, int hw, int c);
+int sdx_channel_gate(sdx_ctx* ctx, const sdx_gate_desc* d, sdx_stream s);
+
+/* Per-image channel broadcast y[n, p, c] = x[n, p, c] op v[n, c] (+relu) (Ew.Channel via
+ * Ops.Elementwise, src/Kernels/Ops.cs:388-420). x, y fp16; v fp32. */
+int sdx_channel_broadcast(sdx_ctx* ctx, int batch, int64_t pixels, int c, int op, int relu, sdx_dptr x,
+                          sdx_dptr v, sdx_dptr y, sdx_stream s);
+
+/* Nearest resize, asymmetric floor, integer scale, + optional addend (ResizeNearestP +
+ * FuseResizeAdd, src/Engine/GraphCompiler.cs:911-948; Nhwc.ResizeNearest, src/Kernels/Nhwc.Det.cs:167-204).
+ * fp16 NHWC; y may be a channel slice (y_pix_stride, y_ch_off) of a wider tensor (fused concat). */
+typedef struct sdx_resize_desc {
+  int batch, ih, iw, c, oh, ow;
+  int add_relu;
+  int64_t y_pix_stride;
+  int y_ch_off;
+  sdx_dptr x, add, y;
+} sdx_resize_desc;
+int sdx_resize_nearest(sdx_ctx* ctx, const sdx_resize_desc* d, sdx_stream s);
+
+/* NHWC channel concat (Nhwc.ConcatInner, src/Kernels/Nhwc.Det.cs:354-370), fp16, up to 8 inputs. */
+int sdx_concat_channels(sdx_ctx* ctx, int64_t pixels, int nin, const int* counts, const sdx_dptr* ins,
+                        sdx_dptr y, sdx_stream s);
+
+/* Elementwise binary on equal shapes (Ew.Binary, src/Kernels/Ew.cs:75-84), fp16, optional relu. */
+int sdx_binary(sdx_ctx* ctx, int64_t n, int op, int relu, sdx_dptr a, sdx_dptr b, sdx_dptr y, sdx_stream s);
+/* Activation node (Act.Apply, src/Kernels/Act.cs:70-81), fp16. */
+int sdx_act(sdx_ctx* ctx, int64_t n, int act, sdx_dptr x, sdx_dptr y, sdx_stream s);
+/* Storage conversion / boundary relayout: fp32 <-> fp16, NCHW <-> NHWC (VkSession f32to16 / f16to32
+ * staging, src/Backends/Vulkan/VkSession.cs:286-310). */
+int sdx_convert(sdx_ctx* ctx, int batch, int c, int64_t hw, int x_dtype, int x_layout, int y_dtype, int y_layout,
+                sdx_dptr x, sdx_dptr y, sdx_stream s);
+
+/* LayerNorm over the last dim (LnP, Ops.LayerNorm src/Kernels/Ops.cs:544-575), fp16 in/out, fp32 w/b. */
+int sdx_layernorm(sdx_ctx* ctx, int64_t rows, int c, float eps, sdx_dptr x, sdx_dptr w, sdx_dptr b, sdx_dptr y,
+                  sdx_stream s);
+/* Row softmax (Ops.Softmax, src/Kernels/Ops.Seq.cs:28-75), fp16 in, fp16/fp32 out. */
+int sdx_softmax(sdx_ctx* ctx, int64_t rows, int c, int y_dtype, sdx_dptr x, sdx_dptr y, sdx_stream s);
+/* Fused attention (AttentionP, src/Engine/ExecPlan.cs:160-174; GPU plans fuse MatMul -> scale ->
+ * Softmax -> MatMul, src/Engine/GraphCompiler.cs:614-770): qkv fp16 [batch, t, 3, heads, d] rows
+ * (one fused projection), out fp16 [batch, t, heads*d]. */
+int sdx_attention(sdx_ctx* ctx, int batch, int t, int heads, int d, float scale, sdx_dptr qkv, sdx_dptr y,
+                  sdx_stream s);
+
+/* ======================================================================================
+ * Session: CudaGraphModel + CudaInferenceSession (the VkGraphModel / VkInferenceSession pair,
+ * src/Backends/Vulkan/VkGraph.cs:44-155, src/Backends/Vulkan/VkSession.cs:63-143). Nodes are added
+ * in plan order with device pointers into the session arena; sdx_session_build captures them into
+ * one CUDA graph; sdx_session_run = H2D of the input + graph launch + D2H of the output + sync.
+ * ====================================================================================== */
+enum sdx_op_kind {
+  SDX_OP_CONV = 1, SDX_OP_GEMM = 2, SDX_OP_CONVT = 3, SDX_OP_POOL = 4, SDX_OP_CHANNEL_GATE = 5,
+  SDX_OP_CHANNEL_BROADCAST = 6, SDX_OP_RESIZE_NEAREST = 7, SDX_OP_CONCAT = 8, SDX_OP_BINARY = 9, SDX_OP_ACT = 10,
+  SDX_OP_CONVERT = 11, SDX_OP_LAYERNORM = 12, SDX_OP_SOFTMAX = 13, SDX_OP_ATTENTION = 14
+};
+/* Generic argument block for the ops without a descriptor struct. */
+typedef struct sdx_misc_desc {
+  int64_t n, rows, pixels;
+  int batch, c, t, heads, d, op, act, relu, x_dtype, x_layout, y_dtype, y_layout, nin;
+  int counts[8];
+  float eps, scale;
+  sdx_dptr a, b, x, y, w, bias;
+  sdx_dptr ins[8];
+} sdx_misc_desc;
+
+/* sizeof the descriptor struct sdx_session_add_node expects for op_kind (0 = unknown kind). */
+size_t sdx_desc_size(int op_kind);
+int sdx_session_create(sdx_ctx* ctx, size_t arena_bytes, sdx_session** out);
+int sdx_session_arena(sdx_session* s, sdx_dptr* base, size_t* bytes);
+int sdx_session_add_node(sdx_session* s, int op_kind, const void* desc, size_t desc_bytes);
+int sdx_session_set_io(sdx_session* s, sdx_dptr in, size_t in_bytes, sdx_dptr out, size_t out_bytes);
+int sdx_session_build(sdx_session* s, int use_graph);
+int sdx_session_stream(sdx_session* s, sdx_stream* stream);
+/* Device-resident run: replay the node list (graph) on the session stream, no copies, no sync. */
+int sdx_session_enqueue(sdx_session* s);
+/* End-to-end run: host input -> device, graph, device -> host output, wait (timeout_ms as sdx_stream_sync). */
+int sdx_session_run(sdx_session* s, const void* host_in, void* host_out, int timeout_ms);
+int sdx_session_node_count(sdx_session* s, int* count);
+int sdx_session_destroy(sdx_session* s);
+
+#ifdef __cplusplus
+}
+#endif
+#if defined(__GNUC__)
+#pragma GCC visibility pop
+#endif
+#endif /* SDXCUDA_H */

@@ -1,0 +1,712 @@
+// Bandwidth-bound kernels of the fused conv path (depthwise, small-channel direct conv, ConvT dot,
+// pools, SE gate, broadcast, nearest resize, concat slices, elementwise, conversion, LayerNorm,
+// softmax, attention). fp16 NHWC storage, fp32 math, 128-bit (8 x fp16) accesses along channels.
+#include <cuda_fp16.h>
+#include <cuda_runtime.h>
+
+#include <algorithm>
+
+#include "sdx_device.cuh"
+#include "sdx_internal.h"
+
+namespace sdx {
+
+static inline int grid_for(int64_t n, int block) {
+  int64_t g = (n + block - 1) / block;
+  return (int)std::min<int64_t>(g, (int64_t)1 << 30);
+}
+
+#define SDX_LAUNCH_CHECK(what)                                  \
+  do {                                                          \
+    cudaError_t e_ = cudaGetLastError();                        \
+    if (e_ != cudaSuccess) return set_cuda_error(e_, what);     \
+    count_launch();                                             \
+  } while (0)
+
+__device__ __forceinline__ void h8_to_f(const uint4& u, float* f) {
+  const __half2* h = reinterpret_cast<const __half2*>(&u);
+#pragma unroll
+  for (int i = 0; i < 4; i++) {
+    float2 t = __half22float2(h[i]);
+    f[2 * i] = t.x;
+    f[2 * i + 1] = t.y;
+  }
+}
+
+__device__ __forceinline__ uint4 f_to_h8(const float* f) {
+  uint4 u;
+  __half2* h = reinterpret_cast<__half2*>(&u);
+#pragma unroll
+  for (int i = 0; i < 4; i++) h[i] = __floats2half2_rn(f[2 * i], f[2 * i + 1]);
+  return u;
+}
+
+// ------------------------------------------------------------------ depthwise
+// Nhwc.Depthwise (src/Kernels/Nhwc.cs:496-631): y[c] = act(b[c] + sum_tap w[tap,c] * x[tap,c] [+ add]);
+// out-of-range taps read the constant 0 pad. Thread = one output pixel x 8 channels.
+__global__ void depthwise_kernel(DwArgs a) {
+  const int cg = a.c >> 3;
+  const int64_t total = (int64_t)a.batch * a.oh * a.ow * cg;
+  for (int64_t idx = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; idx < total;
+       idx += (int64_t)gridDim.x * blockDim.x) {
+    const int g = (int)(idx % cg);
+    int64_t p = idx / cg;
+    const int ox = (int)(p % a.ow);
+    p /= a.ow;
+    const int oy = (int)(p % a.oh);
+    const int n = (int)(p / a.oh);
+    const int c0 = g * 8;
+    float acc[8];
+    {
+      const float4* bp = reinterpret_cast<const float4*>(a.bias + c0);
+      float4 b0 = __ldg(bp), b1 = __ldg(bp + 1);
+      acc[0] = b0.x; acc[1] = b0.y; acc[2] = b0.z; acc[3] = b0.w;
+      acc[4] = b1.x; acc[5] = b1.y; acc[6] = b1.z; acc[7] = b1.w;
+    }
+    float sc[8];
+    if (a.in_scale) {
+      const float4* sp = reinterpret_cast<const float4*>(a.in_scale + (int64_t)n * a.c + c0);
+      float4 s0 = __ldg(sp), s1 = __ldg(sp + 1);
+      sc[0] = s0.x; sc[1] = s0.y; sc[2] = s0.z; sc[3] = s0.w;
+      sc[4] = s1.x; sc[5] = s1.y; sc[6] = s1.z; sc[7] = s1.w;
+    }
+    const __half* xb = a.x + (int64_t)n * a.ih * a.iw * a.c + c0;
+    for (int ky = 0; ky < a.kh; ky++) {
+      const int iy = oy * a.sh + ky - a.pt;
+      if ((unsigned)iy >= (unsigned)a.ih) continue;
+      for (int kx = 0; kx < a.kw; kx++) {
+        const int ix = ox * a.sw + kx - a.pl;
+        if ((unsigned)ix >= (unsigned)a.iw) continue;
+        float xv[8];
+        h8_to_f(__ldg(reinterpret_cast<const uint4*>(xb + ((int64_t)iy * a.iw + ix) * a.c)), xv);
+        const float4* wp = reinterpret_cast<const float4*>(a.w + (int64_t)(ky * a.kw + kx) * a.c + c0);
+        float4 w0 = __ldg(wp), w1 = __ldg(wp + 1);
+        const float wv[8] = {w0.x, w0.y, w0.z, w0.w, w1.x, w1.y, w1.z, w1.w};
+        if (a.in_scale) {
+#pragma unroll
+          for (int j = 0; j < 8; j++) acc[j] = fmaf(xv[j] * sc[j], wv[j], acc[j]);
+        } else {
+#pragma unroll
+          for (int j = 0; j < 8; j++) acc[j] = fmaf(xv[j], wv[j], acc[j]);
+        }
+      }
+    }
+    const int64_t o = (((int64_t)n * a.oh + oy) * a.ow + ox) * a.c + c0;
+    if (a.add) {
+      float r[8];
+      h8_to_f(__ldg(reinterpret_cast<const uint4*>(a.add + o)), r);
+#pragma unroll
+      for (int j = 0; j < 8; j++) acc[j] += r[j];
+    }
+#pragma unroll
+    for (int j = 0; j < 8; j++) acc[j] = act_apply(acc[j], a.act);
+    *reinterpret_cast<uint4*>(a.y + o) = f_to_h8(acc);
+  }
+}
+
+int depthwise_launch(const DwArgs& a, cudaStream_t st) {
+  if (a.c % 8 != 0) return set_error(SDX_ERR_NOT_SUPPORTED, "depthwise: channels must be a multiple of 8");
+  const int64_t total = (int64_t)a.batch * a.oh * a.ow * (a.c / 8);
+  if (total == 0) return SDX_OK;
+  depthwise_kernel<<<grid_for(total, 256), 256, 0, st>>>(a);
+  SDX_LAUNCH_CHECK("depthwise");
+  return SDX_OK;
+}
+
+// ------------------------------------------------------------------ direct small-channel conv
+// Stem convs (ic < 8, fp32 NCHW graph input, stride 2) and other convs the tensor-core path does
+// not take: thread = one output pixel x 8 output channels; weights [tap][ic][oc] staged in smem.
+__device__ __forceinline__ float load_x(const DirectArgs& a, int n, int c, int iy, int ix) {
+  int64_t off = a.x_nchw ? (((int64_t)n * a.ic + c) * a.ih + iy) * a.iw + ix
+                         : (((int64_t)n * a.ih + iy) * a.iw + ix) * a.ic + c;
+  return a.x_f32 ? __ldg(static_cast<const float*>(a.x) + off) : __half2float(static_cast<const __half*>(a.x)[off]);
+}
+
+__global__ void direct_conv_kernel(DirectArgs a) {
+  extern __shared__ float sw[];
+  const int wn = a.kh * a.kw * a.ic * a.oc;
+  for (int i = threadIdx.x; i < wn; i += blockDim.x) sw[i] = a.w[i];
+  __syncthreads();
+  const int og = (a.oc + 7) / 8;
+  const int64_t total = (int64_t)a.batch * a.oh * a.ow * og;
+  for (int64_t idx = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; idx < total;
+       idx += (int64_t)gridDim.x * blockDim.x) {
+    // pixel-fastest order: neighbouring threads read neighbouring input columns
+    int64_t p = idx;
+    const int ox = (int)(p % a.ow);
+    p /= a.ow;
+    const int oy = (int)(p % a.oh);
+    p /= a.oh;
+    const int n = (int)(p % a.batch);
+    const int g = (int)(p / a.batch);
+    const int o0 = g * 8;
+    const int no = min(8, a.oc - o0);
+    float acc[8];
+#pragma unroll
+    for (int j = 0; j < 8; j++) acc[j] = (j < no && a.bias) ? a.bias[o0 + j] : 0.0f;
+    for (int ky = 0; ky < a.kh; ky++) {
+      const int iy = oy * a.sh + ky - a.pt;
+      if ((unsigned)iy >= (unsigned)a.ih) continue;
+      for (int kx = 0; kx < a.kw; kx++) {
+        const int ix = ox * a.sw + kx - a.pl;
+        if ((unsigned)ix >= (unsigned)a.iw) continue;
+        const float* wt = sw + ((ky * a.kw + kx) * a.ic) * a.oc + o0;
+        for (int c = 0; c < a.ic; c++) {
+          const float xv = load_x(a, n, c, iy, ix);
+          const float* wc = wt + c * a.oc;
+#pragma unroll
+          for (int j = 0; j < 8; j++)
+            if (j < no) acc[j] = fmaf(xv, wc[j], acc[j]);
+        }
+      }
+    }
+    for (int j = 0; j < no; j++) {
+      const int o = o0 + j;
+      float v = acc[j];
+      if (a.add) {
+        int64_t ao = a.add_nchw ? (((int64_t)n * a.oc + o) * a.oh + oy) * a.ow + ox
+                                : (((int64_t)n * a.oh + oy) * a.ow + ox) * a.oc + o;
+        v += a.add_f32 ? static_cast<const float*>(a.add)[ao] : __half2float(static_cast<const __half*>(a.add)[ao]);
+      }
+      v = act_apply(v, a.act);
+      int64_t yo = a.y_nchw ? (((int64_t)n * a.oc + o) * a.oh + oy) * a.ow + ox
+                            : (((int64_t)n * a.oh + oy) * a.ow + ox) * a.y_pix_stride + a.y_ch_off + o;
+      if (a.y_f32) static_cast<float*>(a.y)[yo] = v;
+      else static_cast<__half*>(a.y)[yo] = __float2half_rn(v);
+    }
+  }
+}
+
+int direct_conv_launch(const DirectArgs& a, cudaStream_t st) {
+  const size_t wbytes = sizeof(float) * a.kh * a.kw * a.ic * a.oc;
+  if (wbytes > 96 * 1024) return set_error(SDX_ERR_NOT_SUPPORTED, "direct conv: weights exceed the smem stage");
+  const int64_t total = (int64_t)a.batch * a.oh * a.ow * ((a.oc + 7) / 8);
+  if (total == 0) return SDX_OK;
+  static bool attr = false;
+  if (!attr) {
+    cudaFuncSetAttribute(direct_conv_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, 96 * 1024);
+    attr = true;
+  }
+  direct_conv_kernel<<<grid_for(total, 256), 256, wbytes, st>>>(a);
+  SDX_LAUNCH_CHECK("direct_conv");
+  return SDX_OK;
+}
+
+// ------------------------------------------------------------------ ConvT, oc < 8 (dot path)
+// ConvTDot (src/Kernels/Nhwc.Det.cs:96-131): per output element one dot product over ic + bias, act.
+__global__ void convt_dot_kernel(ConvtDotArgs a) {
+  const int taps = a.kh * a.kw;
+  const int64_t total = (int64_t)a.batch * a.ih * a.iw;
+  const int ow = a.iw * a.kw, oh = a.ih * a.kh;
+  for (int64_t idx = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; idx < total;
+       idx += (int64_t)gridDim.x * blockDim.x) {
+    const int x = (int)(idx % a.iw);
+    const int64_t t = idx / a.iw;
+    const int y = (int)(t % a.ih);
+    const int n = (int)(t / a.ih);
+    const __half* xp = a.x + idx * a.ic;
+    for (int tap = 0; tap < taps; tap++) {
+      const int dy = tap / a.kw, dx = tap % a.kw;
+      const int64_t op = ((int64_t)n * oh + y * a.kh + dy) * ow + x * a.kw + dx;
+      for (int o = 0; o < a.oc; o++) {
+        float s = a.bias ? a.bias[o] : 0.0f;
+        for (int c = 0; c < a.ic; c += 8) {
+          float xv[8];
+          h8_to_f(__ldg(reinterpret_cast<const uint4*>(xp + c)), xv);
+#pragma unroll
+          for (int j = 0; j < 8; j++) s = fmaf(xv[j], __ldg(a.w + ((int64_t)(c + j) * a.oc + o) * taps + tap), s);
+        }
+        s = act_apply(s, a.act);
+        if (a.y_f32) static_cast<float*>(a.y)[op * a.oc + o] = s;
+        else static_cast<__half*>(a.y)[op * a.oc + o] = __float2half_rn(s);
+      }
+    }
+  }
+}
+
+int convt_dot_launch(const ConvtDotArgs& a, cudaStream_t st) {
+  if (a.ic % 8 != 0) return set_error(SDX_ERR_NOT_SUPPORTED, "convt dot: ic must be a multiple of 8");
+  const int64_t total = (int64_t)a.batch * a.ih * a.iw;
+  if (total == 0) return SDX_OK;
+  convt_dot_kernel<<<grid_for(total, 256), 256, 0, st>>>(a);
+  SDX_LAUNCH_CHECK("convt_dot");
+  return SDX_OK;
+}
+
+// ------------------------------------------------------------------ pools
+// MaxPool (src/Kernels/Nhwc.cs:730-770): max over in-range taps, 0 when none, optional relu.
+// AvgPool (src/Kernels/Ops.Seq.cs:180-225): sum of in-range taps / count (or kh*kw).
+__global__ void pool_kernel(PoolArgs a) {
+  const int cg = a.c >> 3;
+  const int64_t total = (int64_t)a.batch * a.oh * a.ow * cg;
+  for (int64_t idx = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; idx < total;
+       idx += (int64_t)gridDim.x * blockDim.x) {
+    const int g = (int)(idx % cg);
+    int64_t p = idx / cg;
+    const int ox = (int)(p % a.ow);
+    p /= a.ow;
+    const int oy = (int)(p % a.oh);
+    const int n = (int)(p / a.oh);
+    float acc[8];
+    bool any = false;
+    int cnt = 0;
+    for (int j = 0; j < 8; j++) acc[j] = 0.0f;
+    for (int ky = 0; ky < a.kh; ky++) {
+      const int iy = oy * a.sh + ky - a.pt;
+      if ((unsigned)iy >= (unsigned)a.ih) continue;
+      for (int kx = 0; kx < a.kw; kx++) {
+        const int ix = ox * a.sw + kx - a.pl;
+        if ((unsigned)ix >= (unsigned)a.iw) continue;
+        float v[8];
+        h8_to_f(__ldg(reinterpret_cast<const uint4*>(a.x + (((int64_t)n * a.ih + iy) * a.iw + ix) * a.c + g * 8)), v);
+        if (a.is_avg) {
+#pragma unroll
+          for (int j = 0; j < 8; j++) acc[j] += v[j];
+        } else if (!any) {
+#pragma unroll
+          for (int j = 0; j < 8; j++) acc[j] = v[j];
+        } else {
+#pragma unroll
+          for (int j = 0; j < 8; j++) acc[j] = fmaxf(acc[j], v[j]);
+        }
+        any = true;
+        cnt++;
+      }
+    }
+    if (a.is_avg) {
+      const float inv = 1.0f / (float)(a.incl ? a.kh * a.kw : max(cnt, 1));
+#pragma unroll
+      for (int j = 0; j < 8; j++) acc[j] *= inv;
+    } else if (a.relu) {
+#pragma unroll
+      for (int j = 0; j < 8; j++) acc[j] = fmaxf(acc[j], 0.0f);
+    }
+    *reinterpret_cast<uint4*>(a.y + (((int64_t)n * a.oh + oy) * a.ow + ox) * a.c + g * 8) = f_to_h8(acc);
+  }
+}
+
+int pool_launch(const PoolArgs& a, cudaStream_t st) {
+  if (a.c % 8 != 0) return set_error(SDX_ERR_NOT_SUPPORTED, "pool: channels must be a multiple of 8");
+  const int64_t total = (int64_t)a.batch * a.oh * a.ow * (a.c / 8);
+  if (total == 0) return SDX_OK;
+  pool_kernel<<<grid_for(total, 256), 256, 0, st>>>(a);
+  SDX_LAUNCH_CHECK("pool");
+  return SDX_OK;
+}
+
+// ------------------------------------------------------------------ SE gate
+// Stage 1: per (image, pixel chunk) channel sums into scratch; stage 2: one CTA per image reduces
+// the chunks, forms the means, runs FC1 (+relu) and FC2 and the (hard) sigmoid gate
+// (Nhwc.ChannelGate, src/Kernels/Nhwc.Det.cs:287-314).
+static int gate_chunks(int batch, int hw) {
+  int want = std::max(1, (4 * 148 + batch - 1) / batch);
+  int maxc = std::max(1, (hw + 255) / 256);
+  return std::min(want, maxc);
+}
+
+size_t gate_scratch_bytes(int batch, int hw, int c) {
+  return sizeof(float) * (size_t)batch * gate_chunks(batch, hw) * c;
+}
+
+__global__ void gap_partial_kernel(const __half* __restrict__ x, int hw, int c, int chunks, float* __restrict__ partial) {
+  extern __shared__ float red[];
+  const int n = blockIdx.y, chunk = blockIdx.x;
+  const int cg = c >> 3;
+  const int lanes_p = blockDim.x / cg;  // pixel lanes (blockDim is a multiple of cg)
+  const int g = threadIdx.x % cg, lp = threadIdx.x / cg;
+  const int p0 = (int)((int64_t)chunk * hw / chunks), p1 = (int)((int64_t)(chunk + 1) * hw / chunks);
+  float acc[8] = {0, 0, 0, 0, 0, 0, 0, 0};
+  if (lp < lanes_p) {
+    const __half* base = x + (int64_t)n * hw * c + g * 8;
+    for (int p = p0 + lp; p < p1; p += lanes_p) {
+      float v[8];
+      h8_to_f(__ldg(reinterpret_cast<const uint4*>(base + (int64_t)p * c)), v);
+#pragma unroll
+      for (int j = 0; j < 8; j++) acc[j] += v[j];
+    }
+  }
+  // reduce over pixel lanes through smem: red[lp][c]
+  if (lp < lanes_p)
+    for (int j = 0; j < 8; j++) red[lp * c + g * 8 + j] = acc[j];
+  __syncthreads();
+  for (int ch = threadIdx.x; ch < c; ch += blockDim.x) {
+    float s = 0.0f;
+    for (int l = 0; l < lanes_p; l++) s += red[l * c + ch];
+    partial[((int64_t)n * chunks + chunk) * c + ch] = s;
+  }
+}
+
+__global__ void gate_fc_kernel(GateArgs a, int chunks) {
+  extern __shared__ float sm[];
+  float* mean = sm;         // [c]
+  float* hid = sm + a.c;    // [r]
+  const int n = blockIdx.x;
+  const float inv = 1.0f / (float)a.hw;
+  for (int ch = threadIdx.x; ch < a.c; ch += blockDim.x) {
+    float s = 0.0f;
+    for (int k = 0; k < chunks; k++) s += a.partial[((int64_t)n * chunks + k) * a.c + ch];
+    mean[ch] = s * inv;
+  }
+  __syncthreads();
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, nw = blockDim.x >> 5;
+  for (int j = warp; j < a.r; j += nw) {
+    float s = 0.0f;
+    for (int k = lane; k < a.c; k += 32) s = fmaf(a.w1[(int64_t)j * a.c + k], mean[k], s);
+    for (int off = 16; off; off >>= 1) s += __shfl_xor_sync(0xffffffffu, s, off);
+    if (lane == 0) {
+      s += a.b1 ? a.b1[j] : 0.0f;
+      hid[j] = a.act1_relu ? fmaxf(s, 0.0f) : s;
+    }
+  }
+  __syncthreads();
+  for (int ch = threadIdx.x; ch < a.c; ch += blockDim.x) {
+    float z = a.b2 ? a.b2[ch] : 0.0f;
+    for (int j = 0; j < a.r; j++) z = fmaf(a.w2[(int64_t)ch * a.r + j], hid[j], z);
+    float g = a.hard ? fminf(fmaxf(z * a.alpha + a.beta, 0.0f), 1.0f) : 1.0f / (1.0f + expf(-z));
+    a.s[(int64_t)n * a.c + ch] = g + a.offset;
+  }
+}
+
+int gate_launch(const GateArgs& a, cudaStream_t st) {
+  if (a.c % 8 != 0 || a.c > 4096) return set_error(SDX_ERR_NOT_SUPPORTED, "channel gate: c must be a multiple of 8, <= 4096");
+  if (!a.partial) return set_error(SDX_ERR_INVALID, "channel gate: scratch buffer missing");
+  const int chunks = gate_chunks(a.batch, a.hw);
+  const int cg = a.c / 8;
+  int block = std::max(cg, std::min(256, (256 / cg) * cg));
+  if (block > 1024) return set_error(SDX_ERR_NOT_SUPPORTED, "channel gate: too many channels");
+  const int lanes_p = block / cg;
+  const size_t red = sizeof(float) * lanes_p * a.c;
+  if (red > 48 * 1024) return set_error(SDX_ERR_NOT_SUPPORTED, "channel gate: reduction stage too large");
+  gap_partial_kernel<<<dim3(chunks, a.batch), block, red, st>>>(a.x, a.hw, a.c, chunks, a.partial);
+  SDX_LAUNCH_CHECK("gap_partial");
+  gate_fc_kernel<<<a.batch, 256, sizeof(float) * (a.c + a.r), st>>>(a, chunks);
+  SDX_LAUNCH_CHECK("gate_fc");
+  return SDX_OK;
+}
+
+// ------------------------------------------------------------------ channel broadcast
+__device__ __forceinline__ float ew_op(float a, float b, int op) {
+  switch (op) {
+    case 0: return a + b;
+    case 1: return a - b;
+    case 2: return a * b;
+    default: return a / b;
+  }
+}
+
+__global__ void broadcast_kernel(int batch, int64_t pixels, int c, int op, int relu, const __half* __restrict__ x,
+                                 const float* __restrict__ v, __half* __restrict__ y) {
+  const int cg = c >> 3;
+  const int64_t total = (int64_t)batch * pixels * cg;
+  for (int64_t idx = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; idx < total;
+       idx += (int64_t)gridDim.x * blockDim.x) {
+    const int g = (int)(idx % cg);
+    const int n = (int)(idx / cg / pixels);
+    float xv[8];
+    h8_to_f(__ldg(reinterpret_cast<const uint4*>(x) + idx), xv);
+    const float4* vp = reinterpret_cast<const float4*>(v + (int64_t)n * c + g * 8);
+    float4 v0 = __ldg(vp), v1 = __ldg(vp + 1);
+    const float vv[8] = {v0.x, v0.y, v0.z, v0.w, v1.x, v1.y, v1.z, v1.w};
+#pragma unroll
+    for (int j = 0; j < 8; j++) {
+      float s = ew_op(xv[j], vv[j], op);
+      xv[j] = relu ? fmaxf(s, 0.0f) : s;
+    }
+    reinterpret_cast<uint4*>(y)[idx] = f_to_h8(xv);
+  }
+}
+
+int broadcast_launch(int batch, int64_t pixels, int c, int op, int relu, const __half* x, const float* v, __half* y,
+                     cudaStream_t st) {
+  if (c % 8 != 0) return set_error(SDX_ERR_NOT_SUPPORTED, "broadcast: channels must be a multiple of 8");
+  const int64_t total = (int64_t)batch * pixels * (c / 8);
+  if (total == 0) return SDX_OK;
+  broadcast_kernel<<<grid_for(total, 256), 256, 0, st>>>(batch, pixels, c, op, relu, x, v, y);
+  SDX_LAUNCH_CHECK("broadcast");
+  return SDX_OK;
+}
+
+// ------------------------------------------------------------------ nearest resize (+ addend)
+__global__ void resize_kernel(ResizeArgs a) {
+  const int cg = a.c >> 3;
+  const int64_t total = (int64_t)a.batch * a.oh * a.ow * cg;
+  const int fy = a.oh / a.ih, fx = a.ow / a.iw;
+  for (int64_t idx = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; idx < total;
+       idx += (int64_t)gridDim.x * blockDim.x) {
+    const int g = (int)(idx % cg);
+    int64_t p = idx / cg;
+    const int ox = (int)(p % a.ow);
+    p /= a.ow;
+    const int oy = (int)(p % a.oh);
+    const int n = (int)(p / a.oh);
+    const int iy = min(oy / fy, a.ih - 1), ix = min(ox / fx, a.iw - 1);
+    uint4 u = __ldg(reinterpret_cast<const uint4*>(a.x + (((int64_t)n * a.ih + iy) * a.iw + ix) * a.c + g * 8));
+    const int64_t op = ((int64_t)n * a.oh + oy) * a.ow + ox;
+    if (a.add) {
+      float v[8], r[8];
+      h8_to_f(u, v);
+      h8_to_f(__ldg(reinterpret_cast<const uint4*>(a.add + op * a.c + g * 8)), r);
+#pragma unroll
+      for (int j = 0; j < 8; j++) v[j] += a.add_relu ? fmaxf(r[j], 0.0f) : r[j];
+      u = f_to_h8(v);
+    }
+    *reinterpret_cast<uint4*>(a.y + op * a.y_pix_stride + a.y_ch_off + g * 8) = u;
+  }
+}
+
+int resize_launch(const ResizeArgs& a, cudaStream_t st) {
+  if (a.c % 8 || a.y_pix_stride % 8 || a.y_ch_off % 8)
+    return set_error(SDX_ERR_NOT_SUPPORTED, "resize: channels / slice must be multiples of 8");
+  if (a.oh % a.ih || a.ow % a.iw) return set_error(SDX_ERR_NOT_SUPPORTED, "resize: integer scales only");
+  const int64_t total = (int64_t)a.batch * a.oh * a.ow * (a.c / 8);
+  if (total == 0) return SDX_OK;
+  resize_kernel<<<grid_for(total, 256), 256, 0, st>>>(a);
+  SDX_LAUNCH_CHECK("resize_nearest");
+  return SDX_OK;
+}
+
+__global__ void slice_copy_kernel(int64_t pixels, int c, const __half* __restrict__ x, int64_t ys, int yo,
+                                  __half* __restrict__ y) {
+  const int cg = c >> 3;
+  const int64_t total = pixels * cg;
+  for (int64_t idx = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; idx < total;
+       idx += (int64_t)gridDim.x * blockDim.x) {
+    const int g = (int)(idx % cg);
+    const int64_t p = idx / cg;
+    *reinterpret_cast<uint4*>(y + p * ys + yo + g * 8) = __ldg(reinterpret_cast<const uint4*>(x) + idx);
+  }
+}
+
+int slice_copy_launch(int64_t pixels, int c, const __half* x, int64_t y_pix_stride, int y_ch_off, __half* y,
+                      cudaStream_t st) {
+  if (c % 8 || y_pix_stride % 8 || y_ch_off % 8) return set_error(SDX_ERR_NOT_SUPPORTED, "concat: multiples of 8 only");
+  const int64_t total = pixels * (c / 8);
+  if (total == 0) return SDX_OK;
+  slice_copy_kernel<<<grid_for(total, 256), 256, 0, st>>>(pixels, c, x, y_pix_stride, y_ch_off, y);
+  SDX_LAUNCH_CHECK("concat_slice");
+  return SDX_OK;
+}
+
+// ------------------------------------------------------------------ elementwise
+__global__ void binary_kernel(int64_t n8, int op, int relu, const uint4* __restrict__ a, const uint4* __restrict__ b,
+                              uint4* __restrict__ y) {
+  for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < n8; i += (int64_t)gridDim.x * blockDim.x) {
+    float x[8], z[8];
+    h8_to_f(__ldg(a + i), x);
+    h8_to_f(__ldg(b + i), z);
+#pragma unroll
+    for (int j = 0; j < 8; j++) {
+      float s = ew_op(x[j], z[j], op);
+      x[j] = relu ? fmaxf(s, 0.0f) : s;
+    }
+    y[i] = f_to_h8(x);
+  }
+}
+
+int binary_launch(int64_t n, int op, int relu, const __half* a, const __half* b, __half* y, cudaStream_t st) {
+  if (n % 8) return set_error(SDX_ERR_NOT_SUPPORTED, "binary: element count must be a multiple of 8");
+  if (n == 0) return SDX_OK;
+  binary_kernel<<<grid_for(n / 8, 256), 256, 0, st>>>(n / 8, op, relu, reinterpret_cast<const uint4*>(a),
+                                                      reinterpret_cast<const uint4*>(b), reinterpret_cast<uint4*>(y));
+  SDX_LAUNCH_CHECK("binary");
+  return SDX_OK;
+}
+
+__global__ void act_kernel(int64_t n8, int act, const uint4* __restrict__ x, uint4* __restrict__ y) {
+  for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < n8; i += (int64_t)gridDim.x * blockDim.x) {
+    float v[8];
+    h8_to_f(__ldg(x + i), v);
+#pragma unroll
+    for (int j = 0; j < 8; j++) v[j] = act_apply(v[j], act);
+    y[i] = f_to_h8(v);
+  }
+}
+
+int act_launch(int64_t n, int act, const __half* x, __half* y, cudaStream_t st) {
+  if (n % 8) return set_error(SDX_ERR_NOT_SUPPORTED, "act: element count must be a multiple of 8");
+  if (n == 0) return SDX_OK;
+  act_kernel<<<grid_for(n / 8, 256), 256, 0, st>>>(n / 8, act, reinterpret_cast<const uint4*>(x),
+                                                    reinterpret_cast<uint4*>(y));
+  SDX_LAUNCH_CHECK("act");
+  return SDX_OK;
+}
+
+// fp32 <-> fp16 and NCHW <-> NHWC in one pass. Thread = one element of the output.
+__global__ void convert_kernel(int batch, int c, int64_t hw, int x_f32, int x_nchw, int y_f32, int y_nchw,
+                               const void* __restrict__ x, void* __restrict__ y) {
+  const int64_t total = (int64_t)batch * c * hw;
+  for (int64_t idx = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; idx < total;
+       idx += (int64_t)gridDim.x * blockDim.x) {
+    int64_t n, ch, p;
+    if (y_nchw) {
+      p = idx % hw;
+      ch = (idx / hw) % c;
+      n = idx / hw / c;
+    } else {
+      ch = idx % c;
+      p = (idx / c) % hw;
+      n = idx / c / hw;
+    }
+    const int64_t xi = x_nchw ? (n * c + ch) * hw + p : (n * hw + p) * c + ch;
+    const float v = x_f32 ? __ldg(static_cast<const float*>(x) + xi) : __half2float(static_cast<const __half*>(x)[xi]);
+    if (y_f32) static_cast<float*>(y)[idx] = v;
+    else static_cast<__half*>(y)[idx] = __float2half_rn(v);
+  }
+}
+
+int convert_launch(int batch, int c, int64_t hw, int x_f32, int x_nchw, int y_f32, int y_nchw, const void* x, void* y,
+                   cudaStream_t st) {
+  const int64_t total = (int64_t)batch * c * hw;
+  if (total == 0) return SDX_OK;
+  convert_kernel<<<grid_for(total, 256), 256, 0, st>>>(batch, c, hw, x_f32, x_nchw, y_f32, y_nchw, x, y);
+  SDX_LAUNCH_CHECK("convert");
+  return SDX_OK;
+}
+
+// ------------------------------------------------------------------ LayerNorm / softmax (warp per row)
+__global__ void layernorm_kernel(int64_t rows, int c, float eps, const __half* __restrict__ x,
+                                 const float* __restrict__ w, const float* __restrict__ b, __half* __restrict__ y) {
+  const int lane = threadIdx.x & 31;
+  const int64_t row = (blockIdx.x * (int64_t)blockDim.x + threadIdx.x) >> 5;
+  if (row >= rows) return;
+  const __half* xr = x + row * c;
+  float s = 0.0f, ss = 0.0f;
+  for (int i = lane; i < c; i += 32) {
+    float v = __half2float(xr[i]);
+    s += v;
+    ss = fmaf(v, v, ss);
+  }
+  for (int off = 16; off; off >>= 1) {
+    s += __shfl_xor_sync(0xffffffffu, s, off);
+    ss += __shfl_xor_sync(0xffffffffu, ss, off);
+  }
+  const float mean = s / c;
+  const float inv = rsqrtf(fmaxf(ss / c - mean * mean, 0.0f) + eps);
+  for (int i = lane; i < c; i += 32)
+    y[row * c + i] = __float2half_rn(fmaf(__half2float(xr[i]) - mean, inv * w[i], b[i]));
+}
+
+int layernorm_launch(int64_t rows, int c, float eps, const __half* x, const float* w, const float* b, __half* y,
+                     cudaStream_t st) {
+  if (rows == 0) return SDX_OK;
+  layernorm_kernel<<<grid_for(rows * 32, 256), 256, 0, st>>>(rows, c, eps, x, w, b, y);
+  SDX_LAUNCH_CHECK("layernorm");
+  return SDX_OK;
+}
+
+__global__ void softmax_kernel(int64_t rows, int c, int y_f32, const __half* __restrict__ x, void* __restrict__ y) {
+  const int lane = threadIdx.x & 31;
+  const int64_t row = (blockIdx.x * (int64_t)blockDim.x + threadIdx.x) >> 5;
+  if (row >= rows) return;
+  const __half* xr = x + row * c;
+  float mx = -INFINITY;
+  for (int i = lane; i < c; i += 32) mx = fmaxf(mx, __half2float(xr[i]));
+  for (int off = 16; off; off >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, off));
+  float s = 0.0f;
+  for (int i = lane; i < c; i += 32) s += expf(__half2float(xr[i]) - mx);
+  for (int off = 16; off; off >>= 1) s += __shfl_xor_sync(0xffffffffu, s, off);
+  const float inv = 1.0f / s;
+  for (int i = lane; i < c; i += 32) {
+    float v = expf(__half2float(xr[i]) - mx) * inv;
+    if (y_f32) static_cast<float*>(y)[row * c + i] = v;
+    else static_cast<__half*>(y)[row * c + i] = __float2half_rn(v);
+  }
+}
+
+int softmax_launch(int64_t rows, int c, int y_f32, const __half* x, void* y, cudaStream_t st) {
+  if (rows == 0) return SDX_OK;
+  softmax_kernel<<<grid_for(rows * 32, 256), 256, 0, st>>>(rows, c, y_f32, x, y);
+  SDX_LAUNCH_CHECK("softmax");
+  return SDX_OK;
+}
+
+// ------------------------------------------------------------------ attention (short sequences)
+// out[n, t, h*d + j] = sum_s softmax_s(scale * q[n,t,h,:] . k[n,s,h,:]) v[n,s,h,j], one CTA per (n, h);
+// q/k/v rows of the fused projection [n, t, 3, h, d].
+__global__ void attention_kernel(int t, int heads, int d, float scale, const __half* __restrict__ qkv,
+                                 __half* __restrict__ y) {
+  extern __shared__ float sm[];
+  const int n = blockIdx.x / heads, h = blockIdx.x % heads;
+  float* q = sm;
+  float* k = q + t * d;
+  float* v = k + t * d;
+  float* p = v + t * d;  // [t][t]
+  const int64_t row_stride = 3LL * heads * d;
+  for (int i = threadIdx.x; i < t * d; i += blockDim.x) {
+    const int s = i / d, j = i % d;
+    const __half* r = qkv + ((int64_t)n * t + s) * row_stride + (int64_t)h * d + j;
+    q[i] = __half2float(r[0]);
+    k[i] = __half2float(r[(int64_t)heads * d]);
+    v[i] = __half2float(r[2LL * heads * d]);
+  }
+  __syncthreads();
+  for (int i = threadIdx.x; i < t * t; i += blockDim.x) {
+    const int a = i / t, b = i % t;
+    float s = 0.0f;
+    for (int j = 0; j < d; j++) s = fmaf(q[a * d + j], k[b * d + j], s);
+    p[i] = s * scale;
+  }
+  __syncthreads();
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, nw = blockDim.x >> 5;
+  for (int a = warp; a < t; a += nw) {
+    float mx = -INFINITY;
+    for (int b = lane; b < t; b += 32) mx = fmaxf(mx, p[a * t + b]);
+    for (int off = 16; off; off >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, off));
+    float s = 0.0f;
+    for (int b = lane; b < t; b += 32) {
+      float e = expf(p[a * t + b] - mx);
+      p[a * t + b] = e;
+      s += e;
+    }
+    for (int off = 16; off; off >>= 1) s += __shfl_xor_sync(0xffffffffu, s, off);
+    const float inv = 1.0f / s;
+    __syncwarp();
+    for (int b = lane; b < t; b += 32) p[a * t + b] *= inv;
+  }
+  __syncthreads();
+  for (int i = threadIdx.x; i < t * d; i += blockDim.x) {
+    const int a = i / d, j = i % d;
+    float s = 0.0f;
+    for (int b = 0; b < t; b++) s = fmaf(p[a * t + b], v[b * d + j], s);
+    y[((int64_t)n * t + a) * heads * d + (int64_t)h * d + j] = __float2half_rn(s);
+  }
+}
+
+int attention_launch(int batch, int t, int heads, int d, float scale, const __half* qkv, __half* y, cudaStream_t st) {
+  const size_t smem = sizeof(float) * ((size_t)3 * t * d + (size_t)t * t);
+  if (smem > 160 * 1024) return set_error(SDX_ERR_NOT_SUPPORTED, "attention: sequence too long for the smem kernel");
+  if (batch * heads == 0) return SDX_OK;
+  static bool attr = false;
+  if (!attr) {
+    cudaFuncSetAttribute(attention_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, 160 * 1024);
+    attr = true;
+  }
+  attention_kernel<<<batch * heads, 128, smem, st>>>(t, heads, d, scale, qkv, y);
+  SDX_LAUNCH_CHECK("attention");
+  return SDX_OK;
+}
+
+// ------------------------------------------------------------------ bounded-wait self test
+// Spins on a shared flag that nothing sets, for at most wait_ms, then records SDX_DEV_TEST_WAIT and
+// returns: the failure path of every bounded wait in this library, exercised without a fault.
+__global__ void bounded_wait_kernel(unsigned int* err, uint64_t wait_ns) {
+  __shared__ volatile int flag;
+  if (threadIdx.x == 0) flag = 0;
+  __syncthreads();
+  if (threadIdx.x != 0) return;
+  const uint64_t t0 = global_timer_ns();
+  while (!flag) {
+    if (global_timer_ns() - t0 > wait_ns) {
+      record_error(err, SDX_DEV_TEST_WAIT);
+      return;
+    }
+  }
+}
+
+int bounded_wait_selftest_launch(unsigned int* err, int wait_ms, cudaStream_t st) {
+  bounded_wait_kernel<<<1, 32, 0, st>>>(err, (uint64_t)std::max(1, wait_ms) * 1000000ull);
+  SDX_LAUNCH_CHECK("bounded_wait_selftest");
+  return SDX_OK;
+}
+
+}  // namespace sdx

@@ -1,0 +1,538 @@
+// Dense conv / pointwise conv / Gemm / stride==kernel ConvTranspose on the sm_100a tensor cores.
+//
+// One persistent, warp-specialised kernel (192 threads, one CTA per SM):
+//   warp 0      TMA producer: per 64-channel k-block one A box and one B box into a smem ring
+//               (SWIZZLE_128B, no multicast) signalled through full/empty mbarriers;
+//   warp 1      allocates TMEM, one lane issues tcgen05.mma (M=128, N=BN, K=16 per instruction,
+//               f16 x f16 -> f32) into one of two TMEM accumulators and commits the stage back;
+//   warps 2..5  epilogue: drain the accumulator with tcgen05.ld (thread = output pixel row), apply
+//               bias -> + residual -> activation (the reference's Store16 order,
+//               src/Kernels/Nhwc.cs:376-398) and store fp16 / fp32 NHWC.
+// The double-buffered accumulator lets the epilogue of tile i overlap the MMAs of tile i+1.
+//
+// A operand ("mode"):
+//   TC_ROWS  A is a row-major [M, K] matrix (1x1 conv with the batch folded into rows,
+//            src/Kernels/Nhwc.cs:177-183; Gemm, src/Kernels/Nhwc.Avx512.cs:241-266; ConvT).
+//   TC_CONV  implicit-GEMM k x k conv, stride 1: for tap (ky, kx) and channel block cb the A tile
+//            is the 4-D box {64 ch, BW, BH, 1} of the NHWC input at (ox0+kx-pl, oy0+ky-pt); the
+//            TMA zero-fills out-of-range rows/columns, which is the constant-0 padding. K is
+//            tap-major then channel, the order of the reference's packed weights
+//            (src/Kernels/Nhwc.cs:102-125).
+// B operand: packed weights [taps][n_tiles*BN][ICpad] fp16 (K-major), see sdx_pack_tc_weights.
+//
+// ConvT (stride == kernel, src/Kernels/Nhwc.Det.cs:46-93): one GEMM [pixels, IC] x [IC, taps*OC]
+// whose epilogue scatters column tap*OC + o to output pixel (y*kh + dy, x*kw + dx).
+#include <cuda.h>
+#include <cuda_fp16.h>
+#include <cuda_runtime.h>
+
+#include <algorithm>
+#include <cstdio>
+#include <cstring>
+
+#include "sdx_device.cuh"
+#include "sdx_internal.h"
+
+namespace sdx {
+
+constexpr int TC_BM = 128;
+constexpr int TC_BK = 64;  // halves per 128-byte swizzled row
+constexpr int TC_THREADS = 192;
+constexpr int TC_MAX_STAGES = 8;
+constexpr uint32_t TC_A_STAGE_BYTES = TC_BM * TC_BK * 2;  // 16 KB
+
+struct TcArgs {
+  int mode;
+  int M;
+  int N;
+  int BN;
+  int n_tiles;
+  int m_tiles;
+  int kb_per_tap;
+  int taps, kw;
+  int pad_t, pad_l;
+  int OH, OW, BH, BW, tiles_h, tiles_w;
+  int b_rows_per_tap;
+  int stages;
+  int acc_stride;
+  uint32_t tmem_cols;
+  uint32_t a_box_bytes;
+  const float* bias;
+  const void* res;
+  int res_f32;
+  int64_t res_pix_stride;
+  int res_ch_off;
+  void* out;
+  int out_f32;
+  int64_t out_pix_stride;
+  int out_ch_off;
+  int act;
+  int vec_ok;
+  int convt_kh, convt_kw, convt_oc, convt_H, convt_W;
+  unsigned int* err;
+};
+
+__device__ __forceinline__ void load8_res(const TcArgs& a, int64_t off, float* r) {
+  if (a.res_f32) {
+    const float4* p = reinterpret_cast<const float4*>(static_cast<const float*>(a.res) + off);
+    float4 x = __ldg(p), y = __ldg(p + 1);
+    r[0] = x.x; r[1] = x.y; r[2] = x.z; r[3] = x.w; r[4] = y.x; r[5] = y.y; r[6] = y.z; r[7] = y.w;
+  } else {
+    uint4 u = __ldg(reinterpret_cast<const uint4*>(static_cast<const __half*>(a.res) + off));
+    const __half2* h = reinterpret_cast<const __half2*>(&u);
+#pragma unroll
+    for (int i = 0; i < 4; i++) {
+      float2 f = __half22float2(h[i]);
+      r[2 * i] = f.x;
+      r[2 * i + 1] = f.y;
+    }
+  }
+}
+
+__device__ __forceinline__ void store8(const TcArgs& a, int64_t off, const float* v) {
+  if (a.out_f32) {
+    float4* p = reinterpret_cast<float4*>(static_cast<float*>(a.out) + off);
+    p[0] = make_float4(v[0], v[1], v[2], v[3]);
+    p[1] = make_float4(v[4], v[5], v[6], v[7]);
+  } else {
+    uint4 u;
+    __half2* h = reinterpret_cast<__half2*>(&u);
+#pragma unroll
+    for (int i = 0; i < 4; i++) h[i] = __floats2half2_rn(v[2 * i], v[2 * i + 1]);
+    *reinterpret_cast<uint4*>(static_cast<__half*>(a.out) + off) = u;
+  }
+}
+
+// Output pixel / channel of accumulator column n for GEMM row `row` (ConvT scatter or plain).
+__device__ __forceinline__ void out_coord(const TcArgs& a, int64_t row, int n, int64_t& opix, int& och) {
+  if (a.convt_oc > 0) {
+    int tap = n / a.convt_oc, o = n - tap * a.convt_oc;
+    int dy = tap / a.convt_kw, dx = tap - dy * a.convt_kw;
+    int64_t x = row % a.convt_W, t = row / a.convt_W;
+    int64_t y = t % a.convt_H, img = t / a.convt_H;
+    opix = ((img * a.convt_H + y) * a.convt_kh + dy) * ((int64_t)a.convt_W * a.convt_kw) + x * a.convt_kw + dx;
+    och = o;
+  } else {
+    opix = row;
+    och = n;
+  }
+}
+
+__global__ void __launch_bounds__(TC_THREADS, 1)
+    conv_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB, const TcArgs a) {
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  const int S = a.stages;
+  const uint32_t b_stage_bytes = (uint32_t)a.BN * TC_BK * 2;
+  uint8_t* sA = smem;
+  uint8_t* sB = smem + (size_t)S * TC_A_STAGE_BYTES;
+  uint64_t* bars = reinterpret_cast<uint64_t*>(sB + (size_t)S * b_stage_bytes);
+  uint64_t* full = bars;
+  uint64_t* empty = bars + S;
+  uint64_t* accf = bars + 2 * S;
+  uint64_t* acce = bars + 2 * S + 2;
+  uint64_t* drain = bars + 2 * S + 4;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 2 * S + 5);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < S; s++) {
+      mbar_init(smem_u32(&full[s]), 1);
+      mbar_init(smem_u32(&empty[s]), 1);
+    }
+    for (int i = 0; i < 2; i++) {
+      mbar_init(smem_u32(&accf[i]), 1);
+      mbar_init(smem_u32(&acce[i]), 128);
+    }
+    mbar_init(smem_u32(drain), 1);
+    *abort_flag = 0;
+    mbar_fence_init();
+  }
+  if (warp == 0 && lane == 0) {
+    tma_prefetch_desc(&tmA);
+    tma_prefetch_desc(&tmB);
+  }
+  if (warp == 1) {
+    tmem_alloc(smem_u32(tmem_slot), a.tmem_cols);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem_base = *tmem_slot;
+
+  const int total_tiles = a.m_tiles * a.n_tiles;
+  const int kblocks = a.taps * a.kb_per_tap;
+
+  if (warp == 0) {
+    if (lane == 0) {
+      uint32_t it = 0;
+      uint32_t issued[TC_MAX_STAGES];
+      for (int s = 0; s < TC_MAX_STAGES; s++) issued[s] = 0;
+      bool ok = true;
+      for (int tile = blockIdx.x; tile < total_tiles && ok; tile += gridDim.x) {
+        const int m_tile = tile / a.n_tiles, n_tile = tile - m_tile * a.n_tiles;
+        int img = 0, oy0 = 0, ox0 = 0;
+        if (a.mode == TC_CONV) {
+          const int per_img = a.tiles_h * a.tiles_w;
+          img = m_tile / per_img;
+          const int r = m_tile - img * per_img;
+          oy0 = (r / a.tiles_w) * a.BH;
+          ox0 = (r % a.tiles_w) * a.BW;
+        }
+        for (int kb = 0; kb < kblocks; kb++, it++) {
+          const int s = (int)(it % (uint32_t)S);
+          const uint32_t round = it / (uint32_t)S;
+          if (!mbar_wait(smem_u32(&empty[s]), (round & 1u) ^ 1u, a.err, SDX_DEV_WAIT_EMPTY, abort_flag)) {
+            ok = false;
+            break;
+          }
+          const uint32_t fb = smem_u32(&full[s]);
+          mbar_arrive_expect_tx(fb, a.a_box_bytes + b_stage_bytes);
+          const int tap = kb / a.kb_per_tap, cb = kb - tap * a.kb_per_tap;
+          const uint32_t dA = smem_u32(sA + (size_t)s * TC_A_STAGE_BYTES);
+          if (a.mode == TC_CONV) {
+            const int ky = tap / a.kw, kx = tap - ky * a.kw;
+            tma_load_4d(dA, &tmA, fb, cb * TC_BK, ox0 + kx - a.pad_l, oy0 + ky - a.pad_t, img);
+          } else {
+            tma_load_2d(dA, &tmA, fb, cb * TC_BK, m_tile * TC_BM);
+          }
+          tma_load_2d(smem_u32(sB + (size_t)s * b_stage_bytes), &tmB, fb, cb * TC_BK,
+                      tap * a.b_rows_per_tap + n_tile * a.BN);
+          issued[s] = round + 1;
+        }
+      }
+      // wind-down: every issued copy must land before the CTA's shared memory goes away
+      for (int s = 0; s < S; s++)
+        if (issued[s] > 0) mbar_wait_drain(smem_u32(&full[s]), (issued[s] - 1) & 1u, a.err, SDX_DEV_WAIT_DRAIN);
+    }
+    __syncwarp();
+  } else if (warp == 1) {
+    if (lane == 0) {
+      const uint32_t idesc = umma_idesc_f16(TC_BM, a.BN);
+      uint32_t it = 0, lt = 0;
+      bool ok = true;
+      for (int tile = blockIdx.x; tile < total_tiles && ok; tile += gridDim.x, lt++) {
+        const uint32_t acc = lt & 1u, ar = lt >> 1;
+        if (!mbar_wait(smem_u32(&acce[acc]), (ar & 1u) ^ 1u, a.err, SDX_DEV_WAIT_ACC_EMPTY, abort_flag)) break;
+        tc_fence_after();
+        const uint32_t d = tmem_base + acc * (uint32_t)a.acc_stride;
+        for (int kb = 0; kb < kblocks; kb++, it++) {
+          const int s = (int)(it % (uint32_t)S);
+          const uint32_t round = it / (uint32_t)S;
+          if (!mbar_wait(smem_u32(&full[s]), round & 1u, a.err, SDX_DEV_WAIT_FULL, abort_flag)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          const uint64_t ad = umma_desc_sw128(smem_u32(sA + (size_t)s * TC_A_STAGE_BYTES));
+          const uint64_t bd = umma_desc_sw128(smem_u32(sB + (size_t)s * b_stage_bytes));
+#pragma unroll
+          for (int k = 0; k < TC_BK / 16; k++)
+            umma_f16(d, ad + 2u * k, bd + 2u * k, idesc, (kb > 0 || k > 0) ? 1u : 0u);
+          tc_commit(smem_u32(&empty[s]));
+        }
+        if (!ok) break;
+        tc_commit(smem_u32(&accf[acc]));
+      }
+      // wind-down: all issued MMAs complete before TMEM / smem are released
+      tc_commit(smem_u32(drain));
+      mbar_wait_drain(smem_u32(drain), 0, a.err, SDX_DEV_WAIT_DRAIN);
+    }
+    __syncwarp();
+  } else {
+    // epilogue: warp w reads TMEM lanes 32*(w%4) .. +31 (the lane quadrant it may access)
+    const int q = warp & 3;
+    const int row_in_tile = q * 32 + lane;
+    uint32_t lt = 0;
+    for (int tile = blockIdx.x; tile < total_tiles; tile += gridDim.x, lt++) {
+      const uint32_t acc = lt & 1u, ar = lt >> 1;
+      int ok = 0;
+      if (lane == 0) ok = mbar_wait(smem_u32(&accf[acc]), ar & 1u, a.err, SDX_DEV_WAIT_ACC_FULL, abort_flag) ? 1 : 0;
+      ok = __shfl_sync(0xffffffffu, ok, 0);
+      if (!ok) break;
+      __syncwarp();
+      tc_fence_after();
+
+      const int m_tile = tile / a.n_tiles, n_tile = tile - m_tile * a.n_tiles;
+      bool valid;
+      int64_t pix;
+      if (a.mode == TC_CONV) {
+        const int per_img = a.tiles_h * a.tiles_w;
+        const int img = m_tile / per_img, r = m_tile - img * per_img;
+        const int h = row_in_tile / a.BW, w = row_in_tile - h * a.BW;
+        const int oy = (r / a.tiles_w) * a.BH + h, ox = (r % a.tiles_w) * a.BW + w;
+        valid = row_in_tile < a.BH * a.BW && oy < a.OH && ox < a.OW;
+        pix = ((int64_t)img * a.OH + oy) * a.OW + ox;
+      } else {
+        pix = (int64_t)m_tile * TC_BM + row_in_tile;
+        valid = pix < a.M;
+      }
+      const uint32_t tbase = tmem_base + ((uint32_t)(q * 32) << 16) + acc * (uint32_t)a.acc_stride;
+      for (int c = 0; c < a.BN; c += 16) {
+        float v[16];
+        __syncwarp();
+        tmem_ld_32x32b_x16(tbase + (uint32_t)c, v);
+        if (valid) {
+#pragma unroll
+        for (int g = 0; g < 2; g++) {
+          const int n = n_tile * a.BN + c + 8 * g;
+          if (n >= a.N) break;
+          float* vg = v + 8 * g;
+          int64_t opix;
+          int och;
+          out_coord(a, pix, n, opix, och);
+          if (a.vec_ok && n + 8 <= a.N) {
+            if (a.bias) {
+              const float4* bp = reinterpret_cast<const float4*>(a.bias + (a.convt_oc > 0 ? och : n));
+              float4 b0 = __ldg(bp), b1 = __ldg(bp + 1);
+              vg[0] += b0.x; vg[1] += b0.y; vg[2] += b0.z; vg[3] += b0.w;
+              vg[4] += b1.x; vg[5] += b1.y; vg[6] += b1.z; vg[7] += b1.w;
+            }
+            if (a.res) {
+              float r8[8];
+              load8_res(a, opix * a.res_pix_stride + a.res_ch_off + och, r8);
+#pragma unroll
+              for (int j = 0; j < 8; j++) vg[j] += r8[j];
+            }
+#pragma unroll
+            for (int j = 0; j < 8; j++) vg[j] = act_apply(vg[j], a.act);
+            store8(a, opix * a.out_pix_stride + a.out_ch_off + och, vg);
+          } else {
+            for (int j = 0; j < 8 && n + j < a.N; j++) {
+              int64_t op;
+              int oc;
+              out_coord(a, pix, n + j, op, oc);
+              float x = vg[j];
+              if (a.bias) x += a.bias[a.convt_oc > 0 ? oc : n + j];
+              if (a.res) {
+                const int64_t ro = op * a.res_pix_stride + a.res_ch_off + oc;
+                x += a.res_f32 ? static_cast<const float*>(a.res)[ro] : __half2float(static_cast<const __half*>(a.res)[ro]);
+              }
+              x = act_apply(x, a.act);
+              const int64_t oo = op * a.out_pix_stride + a.out_ch_off + oc;
+              if (a.out_f32) static_cast<float*>(a.out)[oo] = x;
+              else static_cast<__half*>(a.out)[oo] = __float2half_rn(x);
+            }
+          }
+        }
+        }
+      }
+      __syncwarp();
+      tc_fence_before();
+      mbar_arrive(smem_u32(&acce[acc]));
+    }
+  }
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc(tmem_base, a.tmem_cols);
+  }
+}
+
+// ------------------------------------------------------------------------------------------
+// host side
+// ------------------------------------------------------------------------------------------
+void tc_plan_n(int N, int* BN, int* n_tiles) {
+  int npad = (N + 15) / 16 * 16;
+  int nt = (npad + 255) / 256;
+  int bn = ((npad + nt - 1) / nt + 15) / 16 * 16;
+  *BN = bn;
+  *n_tiles = nt;
+}
+
+static int pick_stages(int BN) {
+  const int budget = 200 * 1024;
+  int per = (int)TC_A_STAGE_BYTES + BN * TC_BK * 2;
+  return std::max(2, std::min(TC_MAX_STAGES, budget / per));
+}
+
+static uint32_t pow2_cols(int cols) {
+  uint32_t c = 32;
+  while ((int)c < cols) c <<= 1;
+  return c;
+}
+
+// Conv output tile (BH x BW pixels, BH*BW <= 128) that wastes the fewest MMA rows.
+static void pick_pixel_tile(int OH, int OW, int* BH, int* BW) {
+  double best = -1;
+  int bh = 1, bw = 128;
+  const int cands[] = {128, 112, 96, 80, 64, 56, 48, 40, 32, 28, 24, 20, 16, 14, 12, 10, 8, 7, 6, 5, 4, 3, 2, 1};
+  for (int w : cands) {
+    if (w > 2 * OW && w > 8) continue;
+    int h = std::max(1, std::min(TC_BM / w, OH));
+    int tw = (OW + w - 1) / w, th = (OH + h - 1) / h;
+    double util = (double)OH * OW / ((double)tw * th * TC_BM);
+    if (util > best + 1e-9) {
+      best = util;
+      bh = h;
+      bw = w;
+    }
+  }
+  *BH = bh;
+  *BW = bw;
+}
+
+static int encode_map(CUtensorMap* map, const void* base, int rank, const uint64_t* dims, const uint64_t* strides_bytes,
+                      const uint32_t* box) {
+  PFN_encodeTiled enc = get_encode_tiled();
+  if (!enc) return set_error(SDX_ERR_CUDA, "cuTensorMapEncodeTiled entry point unavailable");
+  uint32_t estr[5] = {1, 1, 1, 1, 1};
+  CUresult r = enc(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, (cuuint32_t)rank, const_cast<void*>(base),
+                   reinterpret_cast<const cuuint64_t*>(dims), reinterpret_cast<const cuuint64_t*>(strides_bytes),
+                   reinterpret_cast<const cuuint32_t*>(box), reinterpret_cast<const cuuint32_t*>(estr),
+                   CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                   CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) return set_error(SDX_ERR_INVALID, "cuTensorMapEncodeTiled failed (%d)", (int)r);
+  return SDX_OK;
+}
+
+static bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
+
+int tc_launch(const TcProblem& p, cudaStream_t stream) {
+  if (p.N <= 0 || p.K <= 0) return set_error(SDX_ERR_INVALID, "tc: empty problem");
+  if (!aligned16(p.a) || !aligned16(p.w)) return set_error(SDX_ERR_INVALID, "tc: operands must be 16-byte aligned");
+  int BN, n_tiles;
+  tc_plan_n(p.N, &BN, &n_tiles);
+  const int kpad = (p.K + TC_BK - 1) / TC_BK * TC_BK;
+  TcArgs a;
+  memset(&a, 0, sizeof(a));
+  a.mode = p.mode;
+  a.N = p.N;
+  a.BN = BN;
+  a.n_tiles = n_tiles;
+  a.kb_per_tap = kpad / TC_BK;
+  a.taps = p.mode == TC_CONV ? p.kh * p.kw : 1;
+  a.kw = p.kw;
+  a.pad_t = p.pad_t;
+  a.pad_l = p.pad_l;
+  a.b_rows_per_tap = BN * n_tiles;
+  a.stages = pick_stages(BN);
+  a.acc_stride = BN;
+  a.tmem_cols = pow2_cols(2 * BN);
+  a.bias = p.bias;
+  a.res = p.res;
+  a.res_f32 = p.res_f32;
+  a.res_pix_stride = p.res_pix_stride;
+  a.res_ch_off = p.res_ch_off;
+  a.out = p.out;
+  a.out_f32 = p.out_f32;
+  a.out_pix_stride = p.out_pix_stride;
+  a.out_ch_off = p.out_ch_off;
+  a.act = p.act;
+  a.err = p.err;
+  a.convt_kh = p.convt_kh;
+  a.convt_kw = p.convt_kw;
+  a.convt_oc = p.convt_oc;
+  a.convt_H = p.convt_H;
+  a.convt_W = p.convt_W;
+  const int esz = p.out_f32 ? 4 : 2;
+  const int rsz = p.res_f32 ? 4 : 2;
+  bool vec = (p.out_pix_stride % 8 == 0) && (p.out_ch_off % 8 == 0) && aligned16(p.out) && (p.N % 8 == 0);
+  if (p.convt_oc > 0) vec = vec && p.convt_oc % 8 == 0;
+  if (p.res) vec = vec && (p.res_pix_stride % 8 == 0) && (p.res_ch_off % 8 == 0) && aligned16(p.res);
+  if (p.bias) vec = vec && aligned16(p.bias);
+  (void)esz;
+  (void)rsz;
+  a.vec_ok = vec ? 1 : 0;
+
+  CUtensorMap mA, mB;
+  if (p.mode == TC_CONV) {
+    if (p.C % 8 != 0) return set_error(SDX_ERR_INVALID, "tc conv: input channels must be a multiple of 8");
+    int BH, BW;
+    pick_pixel_tile(p.OH, p.OW, &BH, &BW);
+    a.BH = BH;
+    a.BW = BW;
+    a.OH = p.OH;
+    a.OW = p.OW;
+    a.tiles_h = (p.OH + BH - 1) / BH;
+    a.tiles_w = (p.OW + BW - 1) / BW;
+    a.m_tiles = p.batch * a.tiles_h * a.tiles_w;
+    a.a_box_bytes = (uint32_t)BH * BW * TC_BK * 2;
+    uint64_t dims[4] = {(uint64_t)p.C, (uint64_t)p.W, (uint64_t)p.H, (uint64_t)p.batch};
+    uint64_t strides[3] = {(uint64_t)p.C * 2, (uint64_t)p.W * p.C * 2, (uint64_t)p.H * p.W * p.C * 2};
+    uint32_t box[4] = {TC_BK, (uint32_t)BW, (uint32_t)BH, 1};
+    int rc = encode_map(&mA, p.a, 4, dims, strides, box);
+    if (rc) return rc;
+  } else {
+    if (p.lda % 8 != 0) return set_error(SDX_ERR_INVALID, "tc rows: A row stride must be a multiple of 8 halves");
+    a.M = p.M;
+    a.m_tiles = (p.M + TC_BM - 1) / TC_BM;
+    a.a_box_bytes = TC_A_STAGE_BYTES;
+    uint64_t dims[2] = {(uint64_t)p.K, (uint64_t)p.M};
+    uint64_t strides[1] = {(uint64_t)p.lda * 2};
+    uint32_t box[2] = {TC_BK, TC_BM};
+    int rc = encode_map(&mA, p.a, 2, dims, strides, box);
+    if (rc) return rc;
+  }
+  {
+    uint64_t dims[2] = {(uint64_t)kpad, (uint64_t)a.taps * a.b_rows_per_tap};
+    uint64_t strides[1] = {(uint64_t)kpad * 2};
+    uint32_t box[2] = {TC_BK, (uint32_t)BN};
+    int rc = encode_map(&mB, p.w, 2, dims, strides, box);
+    if (rc) return rc;
+  }
+  const int total = a.m_tiles * a.n_tiles;
+  if (total == 0) return SDX_OK;
+  const size_t smem = 1024 + (size_t)a.stages * (TC_A_STAGE_BYTES + (size_t)BN * TC_BK * 2) + 8 * (2 * a.stages + 5) + 16;
+  static bool attr_set[64] = {false};
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (dev < 64 && !attr_set[dev]) {
+    cudaError_t e = cudaFuncSetAttribute(conv_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, 227 * 1024);
+    if (e != cudaSuccess) return set_cuda_error(e, "cudaFuncSetAttribute(conv_tc)");
+    attr_set[dev] = true;
+  }
+  const int grid = std::min(total, num_sms(dev));
+  conv_tc_kernel<<<grid, TC_THREADS, smem, stream>>>(mA, mB, a);
+  cudaError_t e = cudaGetLastError();
+  if (e != cudaSuccess) return set_cuda_error(e, "conv_tc launch");
+  count_launch();
+  return SDX_OK;
+}
+
+// Packs ONNX conv weights w [OC][IC][KH][KW] (fp32) into the B operand [taps][n_tiles*BN][ICpad]
+// fp16, zero padded; ConvT weights [IC][OC][KH][KW] pack as one tap whose rows are tap*OC + o.
+size_t tc_weights_halves(int N, int K, int taps) {
+  int BN, nt;
+  tc_plan_n(N, &BN, &nt);
+  size_t kpad = (size_t)(K + TC_BK - 1) / TC_BK * TC_BK;
+  return (size_t)taps * BN * nt * kpad;
+}
+
+void tc_pack_conv(const float* w, int OC, int IC, int KH, int KW, __half* out) {
+  int BN, nt;
+  tc_plan_n(OC, &BN, &nt);
+  const size_t rows = (size_t)BN * nt, kpad = (size_t)(IC + TC_BK - 1) / TC_BK * TC_BK;
+  const int taps = KH * KW;
+  memset(out, 0, sizeof(__half) * taps * rows * kpad);
+  for (int o = 0; o < OC; o++)
+    for (int c = 0; c < IC; c++)
+      for (int t = 0; t < taps; t++)
+        out[((size_t)t * rows + o) * kpad + c] = __float2half_rn(w[((size_t)o * IC + c) * taps + t]);
+}
+
+void tc_pack_convt(const float* w, int IC, int OC, int KH, int KW, __half* out) {
+  const int taps = KH * KW, N = taps * OC;
+  int BN, nt;
+  tc_plan_n(N, &BN, &nt);
+  const size_t rows = (size_t)BN * nt, kpad = (size_t)(IC + TC_BK - 1) / TC_BK * TC_BK;
+  memset(out, 0, sizeof(__half) * rows * kpad);
+  for (int c = 0; c < IC; c++)
+    for (int o = 0; o < OC; o++)
+      for (int t = 0; t < taps; t++)
+        out[((size_t)t * OC + o) * kpad + c] = __float2half_rn(w[((size_t)c * OC + o) * taps + t]);
+}
+
+void tc_pack_gemm(const float* b, int K, int N, int trans_b, __half* out) {
+  int BN, nt;
+  tc_plan_n(N, &BN, &nt);
+  const size_t rows = (size_t)BN * nt, kpad = (size_t)(K + TC_BK - 1) / TC_BK * TC_BK;
+  memset(out, 0, sizeof(__half) * rows * kpad);
+  for (int n = 0; n < N; n++)
+    for (int k = 0; k < K; k++)
+      out[(size_t)n * kpad + k] = __float2half_rn(trans_b ? b[(size_t)n * K + k] : b[(size_t)k * N + n]);
+}
+
+}  // namespace sdx

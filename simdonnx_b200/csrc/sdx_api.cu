@@ -1,0 +1,740 @@
+// The C ABI of libsdxcuda (include/sdxcuda.h): runtime, weight packing, op entry points and the
+// graph-captured session. No C++ exception crosses this boundary; errors are status codes plus a
+// thread-local message.
+#include <cuda.h>
+#include <cuda_fp16.h>
+#include <cuda_runtime.h>
+
+#include <algorithm>
+#include <atomic>
+#include <chrono>
+#include <cstdarg>
+#include <cstdio>
+#include <cstring>
+#include <mutex>
+#include <new>
+#include <thread>
+#include <vector>
+
+#include "../../include/sdxcuda.h"
+#include "sdx_internal.h"
+
+namespace sdx {
+
+static thread_local char t_msg[512] = "";
+static std::atomic<uint64_t> g_launches{0};
+
+int set_error(int code, const char* fmt, ...) {
+  va_list ap;
+  va_start(ap, fmt);
+  vsnprintf(t_msg, sizeof(t_msg), fmt, ap);
+  va_end(ap);
+  return code;
+}
+
+int set_cuda_error(cudaError_t e, const char* what) {
+  snprintf(t_msg, sizeof(t_msg), "%s: %s (%d)", what, cudaGetErrorString(e), (int)e);
+  return e == cudaErrorMemoryAllocation ? SDX_ERR_OOM : SDX_ERR_CUDA;
+}
+
+void clear_error() { t_msg[0] = 0; }
+
+void count_launch() { g_launches.fetch_add(1, std::memory_order_relaxed); }
+
+PFN_encodeTiled get_encode_tiled() {
+  static PFN_encodeTiled fn = nullptr;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<PFN_encodeTiled>(p);
+  });
+  return fn;
+}
+
+int num_sms(int device) {
+  static int cache[64] = {0};
+  if (device >= 0 && device < 64 && cache[device]) return cache[device];
+  int n = 148;
+  cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, device);
+  if (device >= 0 && device < 64) cache[device] = n;
+  return n;
+}
+
+// ---- host-side fault injection (tests only; never touches the GPU)
+static std::mutex g_fault_mu;
+static int g_fault_kind = 0, g_fault_nth = 0, g_fault_seen = 0;
+
+bool inject_fire(int kind) {
+  std::lock_guard<std::mutex> lk(g_fault_mu);
+  if (g_fault_kind != kind || g_fault_nth <= 0) return false;
+  if (++g_fault_seen == g_fault_nth) {
+    g_fault_kind = 0;
+    g_fault_nth = 0;
+    return true;
+  }
+  return false;
+}
+
+}  // namespace sdx
+
+using namespace sdx;
+
+#define CK(call, what)                                   \
+  do {                                                   \
+    cudaError_t e_ = (call);                             \
+    if (e_ != cudaSuccess) return set_cuda_error(e_, what); \
+  } while (0)
+
+static inline cudaStream_t S(sdx_ctx* ctx, sdx_stream s) {
+  return s ? static_cast<cudaStream_t>(s) : ctx->stream;
+}
+
+static int use_ctx(sdx_ctx* ctx) {
+  if (!ctx) return set_error(SDX_ERR_INVALID, "null context");
+  if (ctx->poisoned) return set_error(SDX_ERR_POISONED, "context saw a device error; close and reopen it");
+  CK(cudaSetDevice(ctx->device), "cudaSetDevice");
+  return SDX_OK;
+}
+
+#define USE(ctx)                 \
+  do {                           \
+    int rc_ = use_ctx(ctx);      \
+    if (rc_) return rc_;         \
+  } while (0)
+
+#define LAUNCH_GUARD()                                                                       \
+  do {                                                                                       \
+    if (inject_fire(FAULT_LAUNCH)) return set_error(SDX_ERR_INJECTED, "injected launch fault"); \
+  } while (0)
+
+template <typename T>
+static inline T* P(sdx_dptr p) {
+  return reinterpret_cast<T*>(p);
+}
+
+extern "C" {
+
+int sdx_abi_version(void) { return SDX_ABI_VERSION; }
+
+int sdx_last_error(char* buf, int len) {
+  if (!buf || len <= 0) return SDX_ERR_INVALID;
+  snprintf(buf, (size_t)len, "%s", t_msg);
+  return SDX_OK;
+}
+
+int sdx_device_count(int* count) {
+  if (!count) return set_error(SDX_ERR_INVALID, "null count");
+  int n = 0;
+  cudaError_t e = cudaGetDeviceCount(&n);
+  if (e != cudaSuccess) {
+    cudaGetLastError();
+    *count = 0;
+    return SDX_OK;
+  }
+  *count = n;
+  return SDX_OK;
+}
+
+int sdx_open(int ordinal, sdx_ctx** out) {
+  if (!out) return set_error(SDX_ERR_INVALID, "null out");
+  int n = 0;
+  sdx_device_count(&n);
+  if (ordinal < 0 || ordinal >= n) return set_error(SDX_ERR_INVALID, "device %d not present (%d devices)", ordinal, n);
+  CK(cudaSetDevice(ordinal), "cudaSetDevice");
+  cudaDeviceProp prop;
+  CK(cudaGetDeviceProperties(&prop, ordinal), "cudaGetDeviceProperties");
+  if (prop.major != 10) return set_error(SDX_ERR_NOT_SUPPORTED, "device %d is sm_%d%d; this build targets sm_100a", ordinal, prop.major, prop.minor);
+  sdx_ctx* c = new (std::nothrow) sdx_ctx();
+  if (!c) return set_error(SDX_ERR_OOM, "context allocation");
+  c->device = ordinal;
+  c->poisoned = 0;
+  c->sm_count = prop.multiProcessorCount;
+  cudaError_t e = cudaStreamCreateWithFlags(&c->stream, cudaStreamNonBlocking);
+  if (e != cudaSuccess) {
+    delete c;
+    return set_cuda_error(e, "cudaStreamCreate");
+  }
+  e = cudaMalloc(&c->err_word, sizeof(unsigned int));
+  if (e == cudaSuccess) e = cudaMemset(c->err_word, 0, sizeof(unsigned int));
+  if (e != cudaSuccess) {
+    cudaStreamDestroy(c->stream);
+    delete c;
+    return set_cuda_error(e, "error word");
+  }
+  *out = c;
+  return SDX_OK;
+}
+
+int sdx_close(sdx_ctx* ctx) {
+  if (!ctx) return SDX_OK;
+  cudaSetDevice(ctx->device);
+  cudaStreamSynchronize(ctx->stream);
+  cudaFree(ctx->err_word);
+  cudaStreamDestroy(ctx->stream);
+  delete ctx;
+  return SDX_OK;
+}
+
+int sdx_ctx_stream(sdx_ctx* ctx, sdx_stream* stream) {
+  if (!ctx || !stream) return set_error(SDX_ERR_INVALID, "null argument");
+  *stream = ctx->stream;
+  return SDX_OK;
+}
+
+int sdx_device_info(sdx_ctx* ctx, char* name, int name_len, int* sm_count, int* cc_major, int* cc_minor,
+                    size_t* total_mem) {
+  if (!ctx) return set_error(SDX_ERR_INVALID, "null context");
+  cudaDeviceProp p;
+  CK(cudaGetDeviceProperties(&p, ctx->device), "cudaGetDeviceProperties");
+  if (name && name_len > 0) snprintf(name, (size_t)name_len, "%s", p.name);
+  if (sm_count) *sm_count = p.multiProcessorCount;
+  if (cc_major) *cc_major = p.major;
+  if (cc_minor) *cc_minor = p.minor;
+  if (total_mem) *total_mem = p.totalGlobalMem;
+  return SDX_OK;
+}
+
+int sdx_malloc(sdx_ctx* ctx, size_t bytes, sdx_dptr* out) {
+  USE(ctx);
+  if (!out) return set_error(SDX_ERR_INVALID, "null out");
+  if (inject_fire(FAULT_MALLOC)) return set_error(SDX_ERR_INJECTED, "injected allocation fault");
+  void* p = nullptr;
+  CK(cudaMalloc(&p, std::max<size_t>(bytes, 256)), "cudaMalloc");
+  *out = reinterpret_cast<sdx_dptr>(p);
+  return SDX_OK;
+}
+
+int sdx_free(sdx_ctx* ctx, sdx_dptr p) {
+  if (!ctx) return set_error(SDX_ERR_INVALID, "null context");
+  cudaSetDevice(ctx->device);
+  if (p) CK(cudaFree(reinterpret_cast<void*>(p)), "cudaFree");
+  return SDX_OK;
+}
+
+int sdx_host_alloc_pinned(size_t bytes, void** out) {
+  if (!out) return set_error(SDX_ERR_INVALID, "null out");
+  if (inject_fire(FAULT_MALLOC)) return set_error(SDX_ERR_INJECTED, "injected allocation fault");
+  CK(cudaHostAlloc(out, std::max<size_t>(bytes, 64), cudaHostAllocPortable), "cudaHostAlloc");
+  return SDX_OK;
+}
+
+int sdx_host_free(void* p) {
+  if (p) CK(cudaFreeHost(p), "cudaFreeHost");
+  return SDX_OK;
+}
+
+int sdx_memcpy_htod_async(sdx_ctx* ctx, sdx_dptr dst, const void* src, size_t bytes, sdx_stream s) {
+  USE(ctx);
+  CK(cudaMemcpyAsync(reinterpret_cast<void*>(dst), src, bytes, cudaMemcpyHostToDevice, S(ctx, s)), "H2D copy");
+  return SDX_OK;
+}
+
+int sdx_memcpy_dtoh_async(sdx_ctx* ctx, void* dst, sdx_dptr src, size_t bytes, sdx_stream s) {
+  USE(ctx);
+  if (inject_fire(FAULT_D2H)) return set_error(SDX_ERR_INJECTED, "injected device-to-host copy fault");
+  CK(cudaMemcpyAsync(dst, reinterpret_cast<const void*>(src), bytes, cudaMemcpyDeviceToHost, S(ctx, s)), "D2H copy");
+  return SDX_OK;
+}
+
+int sdx_memcpy_dtod_async(sdx_ctx* ctx, sdx_dptr dst, sdx_dptr src, size_t bytes, sdx_stream s) {
+  USE(ctx);
+  CK(cudaMemcpyAsync(reinterpret_cast<void*>(dst), reinterpret_cast<const void*>(src), bytes, cudaMemcpyDeviceToDevice,
+                     S(ctx, s)),
+     "D2D copy");
+  return SDX_OK;
+}
+
+int sdx_memset_async(sdx_ctx* ctx, sdx_dptr dst, int value, size_t bytes, sdx_stream s) {
+  USE(ctx);
+  CK(cudaMemsetAsync(reinterpret_cast<void*>(dst), value, bytes, S(ctx, s)), "memset");
+  return SDX_OK;
+}
+
+int sdx_stream_create(sdx_ctx* ctx, sdx_stream* out) {
+  USE(ctx);
+  if (!out) return set_error(SDX_ERR_INVALID, "null out");
+  cudaStream_t st;
+  CK(cudaStreamCreateWithFlags(&st, cudaStreamNonBlocking), "cudaStreamCreate");
+  *out = st;
+  return SDX_OK;
+}
+
+int sdx_stream_destroy(sdx_ctx* ctx, sdx_stream s) {
+  if (!ctx) return set_error(SDX_ERR_INVALID, "null context");
+  cudaSetDevice(ctx->device);
+  if (s) CK(cudaStreamDestroy(static_cast<cudaStream_t>(s)), "cudaStreamDestroy");
+  return SDX_OK;
+}
+
+static int check_device_word(sdx_ctx* ctx) {
+  unsigned int code = 0;
+  CK(cudaMemcpy(&code, ctx->err_word, sizeof(code), cudaMemcpyDeviceToHost), "read device error word");
+  if (code) {
+    ctx->poisoned = 1;
+    return set_error(SDX_ERR_DEVICE, "a kernel reported device error 0x%x", code);
+  }
+  return SDX_OK;
+}
+
+int sdx_stream_sync(sdx_ctx* ctx, sdx_stream s, int timeout_ms) {
+  USE(ctx);
+  if (inject_fire(FAULT_SYNC)) return set_error(SDX_ERR_INJECTED, "injected stream-sync fault");
+  cudaStream_t st = S(ctx, s);
+  if (timeout_ms > 0) {
+    auto t0 = std::chrono::steady_clock::now();
+    for (;;) {
+      cudaError_t q = cudaStreamQuery(st);
+      if (q == cudaSuccess) break;
+      if (q != cudaErrorNotReady) return set_cuda_error(q, "cudaStreamQuery");
+      if (std::chrono::steady_clock::now() - t0 > std::chrono::milliseconds(timeout_ms))
+        return set_error(SDX_ERR_TIMEOUT, "stream still busy after %d ms", timeout_ms);
+      std::this_thread::sleep_for(std::chrono::microseconds(50));
+    }
+  } else {
+    CK(cudaStreamSynchronize(st), "cudaStreamSynchronize");
+  }
+  return check_device_word(ctx);
+}
+
+int sdx_stream_query(sdx_ctx* ctx, sdx_stream s, int* done) {
+  USE(ctx);
+  if (!done) return set_error(SDX_ERR_INVALID, "null out");
+  cudaError_t q = cudaStreamQuery(S(ctx, s));
+  if (q == cudaSuccess) *done = 1;
+  else if (q == cudaErrorNotReady) *done = 0;
+  else return set_cuda_error(q, "cudaStreamQuery");
+  return SDX_OK;
+}
+
+int sdx_event_create(sdx_ctx* ctx, void** ev) {
+  USE(ctx);
+  cudaEvent_t e;
+  CK(cudaEventCreate(&e), "cudaEventCreate");
+  *ev = e;
+  return SDX_OK;
+}
+
+int sdx_event_record(sdx_ctx* ctx, void* ev, sdx_stream s) {
+  USE(ctx);
+  CK(cudaEventRecord(static_cast<cudaEvent_t>(ev), S(ctx, s)), "cudaEventRecord");
+  return SDX_OK;
+}
+
+int sdx_event_elapsed_ms(void* start, void* stop, float* ms) {
+  CK(cudaEventSynchronize(static_cast<cudaEvent_t>(stop)), "cudaEventSynchronize");
+  CK(cudaEventElapsedTime(ms, static_cast<cudaEvent_t>(start), static_cast<cudaEvent_t>(stop)), "cudaEventElapsedTime");
+  return SDX_OK;
+}
+
+int sdx_event_destroy(void* ev) {
+  if (ev) CK(cudaEventDestroy(static_cast<cudaEvent_t>(ev)), "cudaEventDestroy");
+  return SDX_OK;
+}
+
+int sdx_graph_begin(sdx_ctx* ctx, sdx_stream s) {
+  USE(ctx);
+  CK(cudaStreamBeginCapture(S(ctx, s), cudaStreamCaptureModeThreadLocal), "cudaStreamBeginCapture");
+  return SDX_OK;
+}
+
+int sdx_graph_end(sdx_ctx* ctx, sdx_stream s, void** graph_exec) {
+  USE(ctx);
+  cudaGraph_t g;
+  CK(cudaStreamEndCapture(S(ctx, s), &g), "cudaStreamEndCapture");
+  cudaGraphExec_t ge;
+  cudaError_t e = cudaGraphInstantiate(&ge, g, 0);
+  cudaGraphDestroy(g);
+  if (e != cudaSuccess) return set_cuda_error(e, "cudaGraphInstantiate");
+  *graph_exec = ge;
+  return SDX_OK;
+}
+
+int sdx_graph_launch(sdx_ctx* ctx, void* graph_exec, sdx_stream s) {
+  USE(ctx);
+  if (inject_fire(FAULT_GRAPH)) return set_error(SDX_ERR_INJECTED, "injected graph-launch fault");
+  CK(cudaGraphLaunch(static_cast<cudaGraphExec_t>(graph_exec), S(ctx, s)), "cudaGraphLaunch");
+  return SDX_OK;
+}
+
+int sdx_graph_destroy(void* graph_exec) {
+  if (graph_exec) CK(cudaGraphExecDestroy(static_cast<cudaGraphExec_t>(graph_exec)), "cudaGraphExecDestroy");
+  return SDX_OK;
+}
+
+int sdx_device_error(sdx_ctx* ctx, unsigned int* code) {
+  if (!ctx || !code) return set_error(SDX_ERR_INVALID, "null argument");
+  cudaSetDevice(ctx->device);
+  CK(cudaMemcpy(code, ctx->err_word, sizeof(*code), cudaMemcpyDeviceToHost), "read device error word");
+  return SDX_OK;
+}
+
+int sdx_clear_device_error(sdx_ctx* ctx) {
+  if (!ctx) return set_error(SDX_ERR_INVALID, "null context");
+  cudaSetDevice(ctx->device);
+  CK(cudaMemset(ctx->err_word, 0, sizeof(unsigned int)), "clear device error word");
+  ctx->poisoned = 0;
+  return SDX_OK;
+}
+
+int sdx_fault_inject(int kind, int nth) {
+  std::lock_guard<std::mutex> lk(g_fault_mu);
+  g_fault_kind = nth > 0 ? kind : 0;
+  g_fault_nth = nth > 0 ? nth : 0;
+  g_fault_seen = 0;
+  return SDX_OK;
+}
+
+uint64_t sdx_launch_count(void) { return g_launches.load(); }
+
+int sdx_selftest_bounded_wait(sdx_ctx* ctx, int wait_ms, sdx_stream s) {
+  USE(ctx);
+  return bounded_wait_selftest_launch(ctx->err_word, wait_ms, S(ctx, s));
+}
+
+// =========================================================================================
+// packing + routing
+// =========================================================================================
+enum Route { R_TC_CONV = 1, R_TC_ROWS = 2, R_DEPTHWISE = 3, R_DIRECT = 4, R_INVALID = 0 };
+
+static int conv_route(const sdx_conv_desc* d) {
+  if (d->pad_mode != 0 || d->pad_value != 0.0f) return R_INVALID;
+  if (d->group > 1) {
+    if (d->group == d->ic && d->oc == d->ic) return R_DEPTHWISE;
+    return R_INVALID;
+  }
+  const bool f16_nhwc = d->x_dtype == SDX_F16 && d->x_layout == SDX_NHWC && d->in_scale == 0;
+  const bool unit = d->sh == 1 && d->sw == 1;
+  if (f16_nhwc && d->ic % 8 == 0 && unit && d->oc >= 8 && d->pool == 0 && d->y_layout == SDX_NHWC &&
+      d->add_layout == SDX_NHWC) {
+    if (d->kh == 1 && d->kw == 1 && d->pad_t == 0 && d->pad_l == 0 && d->pad_b == 0 && d->pad_r == 0) return R_TC_ROWS;
+    return R_TC_CONV;
+  }
+  if (d->pool == 0 && d->in_scale == 0) return R_DIRECT;
+  return R_INVALID;
+}
+
+int sdx_pack_conv(const sdx_conv_desc* d, const float* w, void* out, size_t* bytes) {
+  if (!d || !bytes) return set_error(SDX_ERR_INVALID, "null argument");
+  const int route = conv_route(d);
+  const int taps = d->kh * d->kw;
+  size_t need = 0;
+  switch (route) {
+    case R_TC_CONV:
+    case R_TC_ROWS: need = tc_weights_halves(d->oc, d->ic, taps) * sizeof(__half); break;
+    case R_DEPTHWISE: need = sizeof(float) * (size_t)taps * d->ic; break;
+    case R_DIRECT: need = sizeof(float) * (size_t)taps * d->ic * d->oc; break;
+    default: return set_error(SDX_ERR_NOT_SUPPORTED, "conv: no CUDA kernel for this shape/flags");
+  }
+  if (!out) {
+    *bytes = need;
+    return SDX_OK;
+  }
+  if (*bytes < need) return set_error(SDX_ERR_INVALID, "pack buffer too small");
+  if (!w) return set_error(SDX_ERR_INVALID, "null weights");
+  if (route == R_TC_CONV || route == R_TC_ROWS) {
+    tc_pack_conv(w, d->oc, d->ic, d->kh, d->kw, static_cast<__half*>(out));
+  } else if (route == R_DEPTHWISE) {
+    float* o = static_cast<float*>(out);
+    for (int c = 0; c < d->ic; c++)
+      for (int t = 0; t < taps; t++) o[(size_t)t * d->ic + c] = w[(size_t)c * taps + t];
+  } else {
+    float* o = static_cast<float*>(out);  // [tap][ic][oc]
+    for (int oc = 0; oc < d->oc; oc++)
+      for (int c = 0; c < d->ic; c++)
+        for (int t = 0; t < taps; t++) o[((size_t)t * d->ic + c) * d->oc + oc] = w[((size_t)oc * d->ic + c) * taps + t];
+  }
+  *bytes = need;
+  return SDX_OK;
+}
+
+int sdx_pack_convt(int ic, int oc, int kh, int kw, const float* w, void* out, size_t* bytes) {
+  if (!bytes) return set_error(SDX_ERR_INVALID, "null argument");
+  size_t need = oc >= 8 ? tc_weights_halves(kh * kw * oc, ic, 1) * sizeof(__half) : sizeof(float) * (size_t)ic * oc * kh * kw;
+  if (!out) {
+    *bytes = need;
+    return SDX_OK;
+  }
+  if (*bytes < need) return set_error(SDX_ERR_INVALID, "pack buffer too small");
+  if (oc >= 8) tc_pack_convt(w, ic, oc, kh, kw, static_cast<__half*>(out));
+  else memcpy(out, w, need);
+  *bytes = need;
+  return SDX_OK;
+}
+
+int sdx_pack_gemm(int k, int n, int trans_b, const float* b, void* out, size_t* bytes) {
+  if (!bytes) return set_error(SDX_ERR_INVALID, "null argument");
+  size_t need = tc_weights_halves(n, k, 1) * sizeof(__half);
+  if (!out) {
+    *bytes = need;
+    return SDX_OK;
+  }
+  if (*bytes < need) return set_error(SDX_ERR_INVALID, "pack buffer too small");
+  tc_pack_gemm(b, k, n, trans_b, static_cast<__half*>(out));
+  *bytes = need;
+  return SDX_OK;
+}
+
+// =========================================================================================
+// ops
+// =========================================================================================
+int sdx_conv2d(sdx_ctx* ctx, const sdx_conv_desc* d, sdx_stream s) {
+  USE(ctx);
+  if (!d) return set_error(SDX_ERR_INVALID, "null desc");
+  LAUNCH_GUARD();
+  if (d->batch <= 0 || d->oh <= 0 || d->ow <= 0) return set_error(SDX_ERR_INVALID, "conv: empty shape");
+  // output size must follow the ONNX formula (src/Engine/GraphCompiler.cs:1790-1794)
+  const int oh = (d->ih + d->pad_t + d->pad_b - d->kh) / d->sh + 1, ow = (d->iw + d->pad_l + d->pad_r - d->kw) / d->sw + 1;
+  if (oh != d->oh || ow != d->ow) return set_error(SDX_ERR_INVALID, "conv: output %dx%d, expected %dx%d", d->oh, d->ow, oh, ow);
+  const int route = conv_route(d);
+  const int64_t ystride = d->y_pix_stride > 0 ? d->y_pix_stride : d->oc;
+  cudaStream_t st = S(ctx, s);
+  switch (route) {
+    case R_TC_CONV:
+    case R_TC_ROWS: {
+      TcProblem p;
+      memset(&p, 0, sizeof(p));
+      p.mode = route == R_TC_CONV ? TC_CONV : TC_ROWS;
+      p.a = P<const __half>(d->x);
+      p.lda = d->ic;
+      p.M = d->batch * d->ih * d->iw;
+      p.K = d->ic;
+      p.batch = d->batch;
+      p.H = d->ih;
+      p.W = d->iw;
+      p.C = d->ic;
+      p.OH = d->oh;
+      p.OW = d->ow;
+      p.kh = d->kh;
+      p.kw = d->kw;
+      p.pad_t = d->pad_t;
+      p.pad_l = d->pad_l;
+      p.w = P<const __half>(d->w);
+      p.N = d->oc;
+      p.bias = P<const float>(d->bias);
+      p.res = P<const void>(d->add);
+      p.res_f32 = d->add_dtype == SDX_F32;
+      p.res_pix_stride = d->oc;
+      p.res_ch_off = 0;
+      p.out = P<void>(d->y);
+      p.out_f32 = d->y_dtype == SDX_F32;
+      p.out_pix_stride = ystride;
+      p.out_ch_off = d->y_ch_off;
+      p.act = d->act;
+      p.err = ctx->err_word;
+      return tc_launch(p, st);
+    }
+    case R_DEPTHWISE: {
+      if (d->x_dtype != SDX_F16 || d->y_dtype != SDX_F16 || d->x_layout != SDX_NHWC || d->pool || ystride != d->oc ||
+          (d->add && d->add_dtype != SDX_F16))
+        return set_error(SDX_ERR_NOT_SUPPORTED, "depthwise: fp16 NHWC only");
+      DwArgs a;
+      a.batch = d->batch; a.ih = d->ih; a.iw = d->iw; a.c = d->ic; a.oh = d->oh; a.ow = d->ow;
+      a.kh = d->kh; a.kw = d->kw; a.sh = d->sh; a.sw = d->sw; a.pt = d->pad_t; a.pl = d->pad_l; a.act = d->act;
+      a.x = P<const __half>(d->x);
+      a.w = P<const float>(d->w);
+      a.bias = P<const float>(d->bias);
+      a.in_scale = P<const float>(d->in_scale);
+      a.add = P<const __half>(d->add);
+      a.y = P<__half>(d->y);
+      if (!a.bias) return set_error(SDX_ERR_INVALID, "depthwise: bias required (zeros when absent)");
+      return depthwise_launch(a, st);
+    }
+    case R_DIRECT: {
+      DirectArgs a;
+      a.batch = d->batch; a.ih = d->ih; a.iw = d->iw; a.ic = d->ic; a.oh = d->oh; a.ow = d->ow; a.oc = d->oc;
+      a.kh = d->kh; a.kw = d->kw; a.sh = d->sh; a.sw = d->sw; a.pt = d->pad_t; a.pl = d->pad_l; a.act = d->act;
+      a.x = P<const void>(d->x);
+      a.x_f32 = d->x_dtype == SDX_F32;
+      a.x_nchw = d->x_layout == SDX_NCHW;
+      a.w = P<const float>(d->w);
+      a.bias = P<const float>(d->bias);
+      a.add = P<const void>(d->add);
+      a.add_f32 = d->add_dtype == SDX_F32;
+      a.add_nchw = d->add_layout == SDX_NCHW;
+      a.y = P<void>(d->y);
+      a.y_f32 = d->y_dtype == SDX_F32;
+      a.y_nchw = d->y_layout == SDX_NCHW;
+      a.y_pix_stride = ystride;
+      a.y_ch_off = d->y_ch_off;
+      return direct_conv_launch(a, st);
+    }
+    default: return set_error(SDX_ERR_NOT_SUPPORTED, "conv: no CUDA kernel for this shape/flags");
+  }
+}
+
+int sdx_gemm(sdx_ctx* ctx, const sdx_gemm_desc* d, sdx_stream s) {
+  USE(ctx);
+  if (!d) return set_error(SDX_ERR_INVALID, "null desc");
+  LAUNCH_GUARD();
+  TcProblem p;
+  memset(&p, 0, sizeof(p));
+  p.mode = TC_ROWS;
+  p.a = P<const __half>(d->a);
+  p.lda = d->lda > 0 ? d->lda : d->k;
+  p.M = d->m;
+  p.K = d->k;
+  p.w = P<const __half>(d->w);
+  p.N = d->n;
+  p.bias = P<const float>(d->bias);
+  p.res = P<const void>(d->add);
+  p.res_f32 = d->add_dtype == SDX_F32;
+  p.res_pix_stride = d->ldadd > 0 ? d->ldadd : d->n;
+  p.out = P<void>(d->y);
+  p.out_f32 = d->y_dtype == SDX_F32;
+  p.out_pix_stride = d->ldy > 0 ? d->ldy : d->n;
+  p.act = d->act;
+  p.err = ctx->err_word;
+  return tc_launch(p, S(ctx, s));
+}
+
+int sdx_convt(sdx_ctx* ctx, const sdx_convt_desc* d, sdx_stream s) {
+  USE(ctx);
+  if (!d) return set_error(SDX_ERR_INVALID, "null desc");
+  LAUNCH_GUARD();
+  if (d->oc >= 8) {
+    TcProblem p;
+    memset(&p, 0, sizeof(p));
+    p.mode = TC_ROWS;
+    p.a = P<const __half>(d->x);
+    p.lda = d->ic;
+    p.M = d->batch * d->ih * d->iw;
+    p.K = d->ic;
+    p.w = P<const __half>(d->w);
+    p.N = d->kh * d->kw * d->oc;
+    p.bias = P<const float>(d->bias);
+    p.out = P<void>(d->y);
+    p.out_f32 = d->y_dtype == SDX_F32;
+    p.out_pix_stride = d->oc;
+    p.act = d->act;
+    p.convt_kh = d->kh;
+    p.convt_kw = d->kw;
+    p.convt_oc = d->oc;
+    p.convt_H = d->ih;
+    p.convt_W = d->iw;
+    p.err = ctx->err_word;
+    return tc_launch(p, S(ctx, s));
+  }
+  ConvtDotArgs a;
+  a.batch = d->batch; a.ih = d->ih; a.iw = d->iw; a.ic = d->ic; a.oc = d->oc; a.kh = d->kh; a.kw = d->kw;
+  a.act = d->act;
+  a.y_f32 = d->y_dtype == SDX_F32;
+  a.x = P<const __half>(d->x);
+  a.w = P<const float>(d->w);
+  a.bias = P<const float>(d->bias);
+  a.y = P<void>(d->y);
+  return convt_dot_launch(a, S(ctx, s));
+}
+
+int sdx_pool(sdx_ctx* ctx, const sdx_pool_desc* d, sdx_stream s) {
+  USE(ctx);
+  if (!d) return set_error(SDX_ERR_INVALID, "null desc");
+  LAUNCH_GUARD();
+  PoolArgs a;
+  a.batch = d->batch; a.ih = d->ih; a.iw = d->iw; a.c = d->c; a.oh = d->oh; a.ow = d->ow; a.kh = d->kh; a.kw = d->kw;
+  a.sh = d->sh; a.sw = d->sw; a.pt = d->pad_t; a.pl = d->pad_l; a.is_avg = d->is_avg; a.relu = d->relu;
+  a.incl = d->count_include_pad;
+  a.x = P<const __half>(d->x);
+  a.y = P<__half>(d->y);
+  return pool_launch(a, S(ctx, s));
+}
+
+size_t sdx_channel_gate_scratch_bytes(int batch, int hw, int c) { return gate_scratch_bytes(batch, hw, c); }
+
+int sdx_channel_gate(sdx_ctx* ctx, const sdx_gate_desc* d, sdx_stream s) {
+  USE(ctx);
+  if (!d) return set_error(SDX_ERR_INVALID, "null desc");
+  LAUNCH_GUARD();
+  GateArgs a;
+  a.batch = d->batch; a.hw = d->hw; a.c = d->c; a.r = d->r; a.act1_relu = d->act1_relu; a.hard = d->hard;
+  a.alpha = d->alpha; a.beta = d->beta; a.offset = d->offset;
+  a.x = P<const __half>(d->x);
+  a.w1 = P<const float>(d->w1);
+  a.b1 = P<const float>(d->b1);
+  a.w2 = P<const float>(d->w2);
+  a.b2 = P<const float>(d->b2);
+  a.s = P<float>(d->s);
+  a.partial = P<float>(d->partial);
+  return gate_launch(a, S(ctx, s));
+}
+
+int sdx_channel_broadcast(sdx_ctx* ctx, int batch, int64_t pixels, int c, int op, int relu, sdx_dptr x, sdx_dptr v,
+                          sdx_dptr y, sdx_stream s) {
+  USE(ctx);
+  LAUNCH_GUARD();
+  return broadcast_launch(batch, pixels, c, op, relu, P<const __half>(x), P<const float>(v), P<__half>(y), S(ctx, s));
+}
+
+int sdx_resize_nearest(sdx_ctx* ctx, const sdx_resize_desc* d, sdx_stream s) {
+  USE(ctx);
+  if (!d) return set_error(SDX_ERR_INVALID, "null desc");
+  LAUNCH_GUARD();
+  ResizeArgs a;
+  a.batch = d->batch; a.ih = d->ih; a.iw = d->iw; a.c = d->c; a.oh = d->oh; a.ow = d->ow; a.add_relu = d->add_relu;
+  a.y_pix_stride = d->y_pix_stride > 0 ? d->y_pix_stride : d->c;
+  a.y_ch_off = d->y_ch_off;
+  a.x = P<const __half>(d->x);
+  a.add = P<const __half>(d->add);
+  a.y = P<__half>(d->y);
+  return resize_launch(a, S(ctx, s));
+}
+
+int sdx_concat_channels(sdx_ctx* ctx, int64_t pixels, int nin, const int* counts, const sdx_dptr* ins, sdx_dptr y,
+                        sdx_stream s) {
+  USE(ctx);
+  if (nin <= 0 || nin > 8 || !counts || !ins) return set_error(SDX_ERR_INVALID, "concat: 1..8 inputs");
+  LAUNCH_GUARD();
+  int total = 0;
+  for (int i = 0; i < nin; i++) total += counts[i];
+  int off = 0;
+  for (int i = 0; i < nin; i++) {
+    int rc = slice_copy_launch(pixels, counts[i], P<const __half>(ins[i]), total, off, P<__half>(y), S(ctx, s));
+    if (rc) return rc;
+    off += counts[i];
+  }
+  return SDX_OK;
+}
+
+int sdx_binary(sdx_ctx* ctx, int64_t n, int op, int relu, sdx_dptr a, sdx_dptr b, sdx_dptr y, sdx_stream s) {
+  USE(ctx);
+  LAUNCH_GUARD();
+  return binary_launch(n, op, relu, P<const __half>(a), P<const __half>(b), P<__half>(y), S(ctx, s));
+}
+
+int sdx_act(sdx_ctx* ctx, int64_t n, int act, sdx_dptr x, sdx_dptr y, sdx_stream s) {
+  USE(ctx);
+  LAUNCH_GUARD();
+  return act_launch(n, act, P<const __half>(x), P<__half>(y), S(ctx, s));
+}
+
+int sdx_convert(sdx_ctx* ctx, int batch, int c, int64_t hw, int x_dtype, int x_layout, int y_dtype, int y_layout,
+                sdx_dptr x, sdx_dptr y, sdx_stream s) {
+  USE(ctx);
+  LAUNCH_GUARD();
+  return convert_launch(batch, c, hw, x_dtype == SDX_F32, x_layout == SDX_NCHW, y_dtype == SDX_F32,
+                        y_layout == SDX_NCHW, P<const void>(x), P<void>(y), S(ctx, s));
+}
+
+int sdx_layernorm(sdx_ctx* ctx, int64_t rows, int c, float eps, sdx_dptr x, sdx_dptr w, sdx_dptr b, sdx_dptr y,
+                  sdx_stream s) {
+  USE(ctx);
+  LAUNCH_GUARD();
+  return layernorm_launch(rows, c, eps, P<const __half>(x), P<const float>(w), P<const float>(b), P<__half>(y), S(ctx, s));
+}
+
+int sdx_softmax(sdx_ctx* ctx, int64_t rows, int c, int y_dtype, sdx_dptr x, sdx_dptr y, sdx_stream s) {
+  USE(ctx);
+  LAUNCH_GUARD();
+  return softmax_launch(rows, c, y_dtype == SDX_F32, P<const __half>(x), P<void>(y), S(ctx, s));
+}
+
+int sdx_attention(sdx_ctx* ctx, int batch, int t, int heads, int d, float scale, sdx_dptr qkv, sdx_dptr y,
+                  sdx_stream s) {
+  USE(ctx);
+  LAUNCH_GUARD();
+  return attention_launch(batch, t, heads, d, scale, P<const __half>(qkv), P<__half>(y), S(ctx, s));
+}
+
+}  // extern "C"

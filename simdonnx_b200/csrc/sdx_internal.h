@@ -1,0 +1,147 @@
+// Internal declarations shared by the libsdxcuda translation units.
+#pragma once
+#include <cuda.h>
+#include <cuda_fp16.h>
+#include <cuda_runtime.h>
+#include <stddef.h>
+#include <stdint.h>
+
+#include "sdx_status.h"
+
+struct sdx_ctx {
+  int device;
+  cudaStream_t stream;
+  unsigned int* err_word;  // device error word (one per context)
+  int poisoned;
+  int sm_count;
+};
+
+namespace sdx {
+
+// thread-local last-error message; returns `code`
+int set_error(int code, const char* fmt, ...);
+int set_cuda_error(cudaError_t e, const char* what);
+void clear_error();
+
+typedef CUresult (*PFN_encodeTiled)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
+                                    const cuuint64_t*, const cuuint32_t*, const cuuint32_t*, CUtensorMapInterleave,
+                                    CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+PFN_encodeTiled get_encode_tiled();
+int num_sms(int device);
+void count_launch();
+// fault injection: true when the call of `kind` must fail now (see sdx_fault_inject)
+bool inject_fire(int kind);
+enum { FAULT_MALLOC = 1, FAULT_LAUNCH = 2, FAULT_GRAPH = 3, FAULT_D2H = 4, FAULT_SYNC = 5 };
+
+// ---- tcgen05 implicit GEMM (conv_tc.cu)
+enum { TC_ROWS = 0, TC_CONV = 1 };
+struct TcProblem {
+  int mode;
+  // A: TC_ROWS -> [M, K] rows with stride lda (halves); TC_CONV -> NHWC [batch, H, W, C] fp16
+  const __half* a;
+  int64_t lda;
+  int M, K;
+  int batch, H, W, C, OH, OW, kh, kw, pad_t, pad_l;
+  // B: packed weights (tc_pack_*)
+  const __half* w;
+  int N;
+  // epilogue
+  const float* bias;
+  const void* res;
+  int res_f32;
+  int64_t res_pix_stride;
+  int res_ch_off;
+  void* out;
+  int out_f32;
+  int64_t out_pix_stride;
+  int out_ch_off;
+  int act;
+  int convt_kh, convt_kw, convt_oc, convt_H, convt_W;
+  unsigned int* err;
+};
+void tc_plan_n(int N, int* BN, int* n_tiles);
+int tc_launch(const TcProblem& p, cudaStream_t stream);
+size_t tc_weights_halves(int N, int K, int taps);
+void tc_pack_conv(const float* w, int OC, int IC, int KH, int KW, __half* out);
+void tc_pack_convt(const float* w, int IC, int OC, int KH, int KW, __half* out);
+void tc_pack_gemm(const float* b, int K, int N, int trans_b, __half* out);
+
+// ---- bandwidth kernels (bw_kernels.cu); all return SDX_* status
+struct DwArgs {
+  int batch, ih, iw, c, oh, ow, kh, kw, sh, sw, pt, pl, act;
+  const __half* x;
+  const float* w;  // [kh*kw][c]
+  const float* bias;
+  const float* in_scale;  // [batch, c] or null
+  const __half* add;
+  __half* y;
+};
+int depthwise_launch(const DwArgs& a, cudaStream_t st);
+
+struct DirectArgs {
+  int batch, ih, iw, ic, oh, ow, oc, kh, kw, sh, sw, pt, pl, act;
+  const void* x;
+  int x_f32, x_nchw;
+  const float* w;  // [kh*kw][ic][oc]
+  const float* bias;
+  const void* add;
+  int add_f32, add_nchw;
+  void* y;
+  int y_f32, y_nchw;
+  int64_t y_pix_stride;
+  int y_ch_off;
+};
+int direct_conv_launch(const DirectArgs& a, cudaStream_t st);
+
+struct ConvtDotArgs {
+  int batch, ih, iw, ic, oc, kh, kw, act, y_f32;
+  const __half* x;
+  const float* w;  // [ic][oc][kh][kw]
+  const float* bias;
+  void* y;
+};
+int convt_dot_launch(const ConvtDotArgs& a, cudaStream_t st);
+
+struct PoolArgs {
+  int batch, ih, iw, c, oh, ow, kh, kw, sh, sw, pt, pl, is_avg, relu, incl;
+  const __half* x;
+  __half* y;
+};
+int pool_launch(const PoolArgs& a, cudaStream_t st);
+
+struct GateArgs {
+  int batch, hw, c, r, act1_relu, hard;
+  float alpha, beta, offset;
+  const __half* x;
+  const float *w1, *b1, *w2, *b2;
+  float* s;
+  float* partial;
+};
+size_t gate_scratch_bytes(int batch, int hw, int c);
+int gate_launch(const GateArgs& a, cudaStream_t st);
+
+int broadcast_launch(int batch, int64_t pixels, int c, int op, int relu, const __half* x, const float* v, __half* y,
+                     cudaStream_t st);
+
+struct ResizeArgs {
+  int batch, ih, iw, c, oh, ow, add_relu;
+  int64_t y_pix_stride;
+  int y_ch_off;
+  const __half* x;
+  const __half* add;
+  __half* y;
+};
+int resize_launch(const ResizeArgs& a, cudaStream_t st);
+int slice_copy_launch(int64_t pixels, int c, const __half* x, int64_t y_pix_stride, int y_ch_off, __half* y,
+                      cudaStream_t st);
+int binary_launch(int64_t n, int op, int relu, const __half* a, const __half* b, __half* y, cudaStream_t st);
+int act_launch(int64_t n, int act, const __half* x, __half* y, cudaStream_t st);
+int convert_launch(int batch, int c, int64_t hw, int x_f32, int x_nchw, int y_f32, int y_nchw, const void* x, void* y,
+                   cudaStream_t st);
+int layernorm_launch(int64_t rows, int c, float eps, const __half* x, const float* w, const float* b, __half* y,
+                     cudaStream_t st);
+int softmax_launch(int64_t rows, int c, int y_f32, const __half* x, void* y, cudaStream_t st);
+int attention_launch(int batch, int t, int heads, int d, float scale, const __half* qkv, __half* y, cudaStream_t st);
+int bounded_wait_selftest_launch(unsigned int* err, int wait_ms, cudaStream_t st);
+
+}  // namespace sdx

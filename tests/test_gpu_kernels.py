@@ -1,0 +1,284 @@
+"""CUDA kernels vs the CPU oracle (the reference's CPU kernels restated), through the C ABI.
+
+Tolerance: relative L2 <= 2e-3 and max-abs <= 1e-2 * max|ref| (tests/parity.py). The shape matrix
+follows the reference's own kernel tests (tests/Sdcb.SimdOnnx.Tests/Avx512KernelTests.cs:35-93,
+EngineTests.cs:131-214).
+"""
+import numpy as np
+import pytest
+
+import oracle as O
+from tests.parity import assert_close
+
+torch = pytest.importorskip("torch")
+pytestmark = pytest.mark.gpu
+
+
+@pytest.fixture(scope="module")
+def be():
+    from simdonnx_b200 import backend
+    if not torch.cuda.is_available():
+        pytest.skip("no GPU")
+    return backend.CudaBackend.get(0)
+
+
+def rnd(rng, *shape, scale=1.0):
+    return (rng.uniform(-1, 1, size=shape) * scale).astype(np.float32)
+
+
+def dev16(a):
+    return torch.from_numpy(np.ascontiguousarray(a)).cuda().half()
+
+
+def dev32(a):
+    return torch.from_numpy(np.ascontiguousarray(a, np.float32)).cuda()
+
+
+def host(t):
+    torch.cuda.synchronize()
+    return t.float().cpu().numpy()
+
+
+# ------------------------------------------------------------------------------------------- C1
+def test_c1_fused_conv_full_size(be):
+    """NHWC 3x3 s1 p1, N=8, 128x128, 64->64, bias, residual add, ReLU."""
+    from simdonnx_b200 import backend as B, synth
+    rng = synth.Rng(1)
+    x = rng.normal("c1.x", (8, 128, 128, 64), 0.1)
+    w = rng.normal("c1.w", (64, 64, 3, 3), 0.1)
+    b = rng.normal("c1.b", (64,), 0.01)
+    res = rng.normal("c1.res", (8, 128, 128, 64), 0.1)
+    ref = O.conv(x, O.ConvPlan(w, b), pads=(1, 1, 1, 1), act="relu", add=res)  # Winograd (the reference's path)
+    d = B.conv_desc(8, 128, 128, 64, 64, 3, 3, pads=(1, 1, 1, 1), act="relu", y_dtype=torch.float32,
+                    add_dtype=torch.float32)
+    y = B.conv2d(be, d, dev16(x), B.pack_conv(d, w), bias=dev32(b), add=dev32(res))
+    assert_close(host(y), ref, "C1")
+    assert be.device_error() == 0
+
+
+# ------------------------------------------------------------------------------------------- dense conv
+CONV_CASES = [
+    # ic, oc, k, stride, h, w, residual, act   (Avx512KernelTests.cs:35-43 with zero constant pad)
+    (16, 48, 3, 1, 11, 13, True, "relu"),
+    (20, 20, 3, 2, 17, 19, True, "sigmoid"),
+    (32, 64, 3, 2, 12, 31, False, "gelu"),
+    (24, 3, 3, 1, 9, 10, False, "none"),
+    (40, 36, 1, 1, 7, 33, True, "relu"),
+    (8, 32, 5, 1, 14, 9, False, "relu"),
+    (3, 16, 3, 1, 37, 23, False, "hardswish"),
+    (6, 32, 3, 1, 29, 41, False, "relu"),
+    # Winograd-shaped (Avx512KernelTests.cs:62-66)
+    (64, 16, 3, 1, 17, 23, True, "none"),
+    (128, 64, 3, 1, 30, 41, False, "relu"),
+    (96, 24, 3, 1, 20, 20, False, "none"),
+    (256, 256, 3, 1, 8, 8, True, "relu"),
+]
+
+
+@pytest.mark.parametrize("ic,oc,k,s,h,w,residual,act", CONV_CASES)
+def test_conv_shapes(be, ic, oc, k, s, h, w, residual, act):
+    from simdonnx_b200 import backend as B
+    rng = np.random.default_rng(ic * 131 + oc * 7 + k)
+    n, p = 2, k // 2
+    x = rnd(rng, n, h, w, ic)
+    wt = rnd(rng, oc, ic, k, k, scale=1.0 / np.sqrt(ic * k * k))
+    b = rnd(rng, oc)
+    oh, ow = (h + 2 * p - k) // s + 1, (w + 2 * p - k) // s + 1
+    res = rnd(rng, n, oh, ow, oc) if residual else None
+    ref = O.conv(x, O.ConvPlan(wt, b, winograd=False), strides=(s, s), pads=(p, p, p, p), act=act, add=res)
+    d = B.conv_desc(n, h, w, ic, oc, k, k, stride=(s, s), pads=(p, p, p, p), act=act)
+    y = B.conv2d(be, d, dev16(x), B.pack_conv(d, wt), bias=dev32(b), add=None if res is None else dev16(res))
+    assert_close(host(y), ref, f"conv {ic}->{oc} k{k} s{s}")
+
+
+def test_conv_into_channel_slice(be):
+    """Epilogue writing into a channel slice of a wider tensor (fused concat)."""
+    from simdonnx_b200 import backend as B
+    rng = np.random.default_rng(5)
+    x = rnd(rng, 2, 20, 20, 96)
+    wt = rnd(rng, 24, 96, 3, 3, scale=0.05)
+    b = rnd(rng, 24)
+    ref = O.conv(x, O.ConvPlan(wt, b, winograd=False), pads=(1, 1, 1, 1))
+    d = B.conv_desc(2, 20, 20, 96, 24, 3, 3, pads=(1, 1, 1, 1), y_pix_stride=96, y_ch_off=48)
+    big = torch.zeros((2, 20, 20, 96), dtype=torch.float16, device="cuda")
+    B.conv2d(be, d, dev16(x), B.pack_conv(d, wt), bias=dev32(b), y=big)
+    got = host(big)
+    assert_close(got[..., 48:72], ref, "slice")
+    assert np.all(got[..., :48] == 0) and np.all(got[..., 72:] == 0)
+
+
+def test_stem_nchw_fp32_input(be):
+    """Graph-input stem: fp32 NCHW input read directly (boundary relayout fused), 3x3 s2, HardSwish."""
+    from simdonnx_b200 import backend as B
+    rng = np.random.default_rng(9)
+    x = rng.uniform(0, 1, size=(2, 3, 64, 48)).astype(np.float32)
+    wt = rnd(rng, 16, 3, 3, 3, scale=0.5)
+    b = rnd(rng, 16)
+    ref = O.conv(np.ascontiguousarray(x.transpose(0, 2, 3, 1)), O.ConvPlan(wt, b), strides=(2, 2),
+                 pads=(1, 1, 1, 1), act="hardswish")
+    d = B.conv_desc(2, 64, 48, 3, 16, 3, 3, stride=(2, 2), pads=(1, 1, 1, 1), act="hardswish",
+                    x_dtype=torch.float32, x_layout=1)
+    y = B.conv2d(be, d, dev32(x), B.pack_conv(d, wt), bias=dev32(b))
+    assert_close(host(y), ref, "stem")
+
+
+# ------------------------------------------------------------------------------------------- Gemm
+GEMM_CASES = [
+    (57, 128, 128, False, "none"),
+    (23, 160, 48, True, "gelu"),
+    (5, 64, 20, False, "relu"),
+    (640, 120, 360, True, "none"),
+    (640, 240, 120, True, "hardswish"),
+    (300, 120, 6625, True, "none"),
+]
+
+
+@pytest.mark.parametrize("m,k,n,trans_b,act", GEMM_CASES)
+def test_gemm(be, m, k, n, trans_b, act):
+    from simdonnx_b200 import backend as B
+    rng = np.random.default_rng(m + k + n)
+    a = rnd(rng, m, k)
+    bm = rnd(rng, n, k) if trans_b else rnd(rng, k, n)
+    bias = rnd(rng, n)
+    ref = O.gemm(a, O.GemmPlan(bm, bias, trans_b=trans_b), act=act)
+    y = B.gemm(be, dev16(a), B.pack_gemm(bm, trans_b), n, bias=dev32(bias), act=act, y_dtype=torch.float32)
+    assert_close(host(y), ref, f"gemm {m}x{k}x{n}")
+
+
+def test_gemm_residual(be):
+    from simdonnx_b200 import backend as B
+    rng = np.random.default_rng(77)
+    a, bm, bias, r = rnd(rng, 640, 240), rnd(rng, 120, 240), rnd(rng, 120), rnd(rng, 640, 120)
+    ref = O.gemm(a, O.GemmPlan(bm, bias, trans_b=True)) + r
+    y = B.gemm(be, dev16(a), B.pack_gemm(bm, True), 120, bias=dev32(bias), add=dev16(r))
+    assert_close(host(y), ref, "gemm+res")
+
+
+# ------------------------------------------------------------------------------------------- ConvT
+@pytest.mark.parametrize("ic,oc,h,w,act,f32", [(24, 24, 40, 40, "relu", False), (24, 1, 40, 40, "sigmoid", True),
+                                               (64, 32, 16, 16, "none", False), (512, 256, 8, 8, "none", False)])
+def test_convt(be, ic, oc, h, w, act, f32):
+    from simdonnx_b200 import backend as B
+    rng = np.random.default_rng(ic + oc)
+    x = rnd(rng, 2, h, w, ic)
+    wt = rnd(rng, ic, oc, 2, 2, scale=1 / np.sqrt(ic))
+    b = rnd(rng, oc)
+    ref = O.convt(x, wt, b, act=act)
+    wp = B.pack_convt(wt) if oc >= 8 else dev32(wt)
+    y = B.convt(be, dev16(x), wp, ic, oc, 2, 2, bias=dev32(b), act=act,
+                y_dtype=torch.float32 if f32 else torch.float16)
+    assert_close(host(y), ref, f"convt {ic}->{oc}")
+
+
+# ------------------------------------------------------------------------------------------- bandwidth ops
+@pytest.mark.parametrize("c,k,s,h,w", [(16, 3, 1, 40, 40), (32, 3, 2, 40, 40), (128, 5, 1, 20, 20),
+                                       (256, 5, 2, 21, 19)])
+def test_depthwise(be, c, k, s, h, w):
+    from simdonnx_b200 import backend as B
+    rng = np.random.default_rng(c + k)
+    x = rnd(rng, 2, h, w, c)
+    wt = rnd(rng, c, 1, k, k, scale=0.3)
+    b = rnd(rng, c)
+    p = k // 2
+    ref = O.conv(x, O.ConvPlan(wt, b, group=c), strides=(s, s), pads=(p, p, p, p), act="hardswish")
+    d = B.conv_desc(2, h, w, c, c, k, k, stride=(s, s), pads=(p, p, p, p), group=c, act="hardswish")
+    y = B.conv2d(be, d, dev16(x), B.pack_conv(d, wt), bias=dev32(b))
+    assert_close(host(y), ref, "depthwise")
+
+
+def test_depthwise_with_input_scale(be):
+    """SE gate applied on the depthwise load: dw(x * s) == dw of the materialised product."""
+    from simdonnx_b200 import backend as B
+    rng = np.random.default_rng(3)
+    x = rnd(rng, 2, 16, 16, 32)
+    sc = rng.uniform(0, 1, size=(2, 32)).astype(np.float32)
+    wt = rnd(rng, 32, 1, 3, 3)
+    b = rnd(rng, 32)
+    ref = O.conv(O.channel_broadcast(x, sc), O.ConvPlan(wt, b, group=32), pads=(1, 1, 1, 1), act="hardswish")
+    d = B.conv_desc(2, 16, 16, 32, 32, 3, 3, pads=(1, 1, 1, 1), group=32, act="hardswish")
+    y = B.conv2d(be, d, dev16(x), B.pack_conv(d, wt), bias=dev32(b), in_scale=dev32(sc))
+    assert_close(host(y), ref, "dw+scale")
+
+
+@pytest.mark.parametrize("avg", [False, True])
+def test_pools(be, avg):
+    from simdonnx_b200 import backend as B
+    rng = np.random.default_rng(11)
+    x = rnd(rng, 2, 19, 26, 32)
+    if avg:
+        ref = O.avgpool(x, (2, 1), (2, 1))
+        y = B.pool(be, dev16(x), (2, 1), (2, 1), is_avg=True)
+    else:
+        ref = O.maxpool(x, (3, 3), (2, 2), pads=(1, 1, 1, 1), relu=True)
+        y = B.pool(be, dev16(x), (3, 3), (2, 2), pads=(1, 1, 1, 1), relu=True)
+    assert_close(host(y), ref, "pool")
+
+
+@pytest.mark.parametrize("c,hw", [(32, 80), (512, 20), (64, 160)])
+def test_channel_gate_and_broadcast(be, c, hw):
+    from simdonnx_b200 import backend as B
+    rng = np.random.default_rng(c)
+    r = c // 4
+    x = rnd(rng, 3, hw, hw, c)
+    w1, b1, w2, b2 = rnd(rng, r, c), rnd(rng, r), rnd(rng, c, r), rnd(rng, c)
+    ref_s = O.channel_gate(x, w1, b1, w2, b2, act1_relu=True, hard=True, alpha=0.2, beta=0.5)
+    s = B.channel_gate(be, dev16(x), dev32(w1), dev32(b1), dev32(w2), dev32(b2), alpha=0.2, beta=0.5)
+    assert_close(host(s), ref_s, "gate")
+    y = B.channel_broadcast(be, dev16(x), s)
+    assert_close(host(y), O.channel_broadcast(x, ref_s), "x*s")
+
+
+def test_resize_add_and_concat(be):
+    from simdonnx_b200 import backend as B
+    rng = np.random.default_rng(21)
+    x, lat = rnd(rng, 2, 10, 10, 96), rnd(rng, 2, 20, 20, 96)
+    assert_close(host(B.resize_nearest(be, dev16(x), 2, add=dev16(lat))), O.resize_nearest(x, (2, 2), add=lat), "up+add")
+    parts = [rnd(rng, 2, 8, 8, 24) for _ in range(4)]
+    assert_close(host(B.concat_channels(be, [dev16(p) for p in parts])), O.concat_channels(parts), "concat")
+    big = torch.zeros((2, 40, 40, 96), dtype=torch.float16, device="cuda")
+    B.resize_nearest(be, dev16(parts[0]), 5, y=big, y_pix_stride=96, y_ch_off=24)
+    assert_close(host(big)[..., 24:48], O.resize_nearest(parts[0], (5, 5)), "up into slice")
+
+
+def test_layernorm_softmax_attention(be):
+    from simdonnx_b200 import backend as B
+    rng = np.random.default_rng(31)
+    x = rnd(rng, 4, 40, 120)
+    w, b = rnd(rng, 120), rnd(rng, 120)
+    assert_close(host(B.layernorm(be, dev16(x), dev32(w), dev32(b))), O.layernorm(x, w, b), "layernorm")
+    s = rnd(rng, 64, 40, scale=4.0)
+    assert_close(host(B.softmax(be, dev16(s), torch.float32)), O.softmax(s), "softmax")
+    nb, t, heads, dh = 3, 40, 8, 15
+    qkv = rnd(rng, nb, t, 3, heads, dh)
+    q, k, v = (np.ascontiguousarray(qkv[:, :, i].transpose(0, 2, 1, 3)) for i in range(3))
+    scale = dh ** -0.5
+    p = O.softmax(O.binary(O.matmul(q, np.ascontiguousarray(k.transpose(0, 1, 3, 2))),
+                           np.full((nb, heads, t, t), scale, np.float32), "mul"))
+    ref = O.matmul(p, v).transpose(0, 2, 1, 3).reshape(nb, t, heads * dh)
+    y = B.attention(be, dev16(qkv), nb, t, heads, dh, scale)
+    assert_close(host(y), ref, "attention")
+
+
+def test_convert_layouts(be):
+    from simdonnx_b200 import backend as B, _native as N
+    rng = np.random.default_rng(41)
+    x = rnd(rng, 2, 3, 7, 5)
+    y = B.convert(be, dev32(x), 2, 3, 35, N.NCHW, torch.float16, N.NHWC)
+    assert_close(host(y).reshape(2, 7, 5, 3), x.transpose(0, 2, 3, 1), "nchw->nhwc")
+    z = B.convert(be, y, 2, 3, 35, N.NHWC, torch.float32, N.NCHW)
+    assert_close(host(z).reshape(x.shape), x, "roundtrip")
+
+
+def test_bounded_wait_reports_and_recovers(be):
+    """A kernel whose wait can never end gives up after its limit, records its code and returns;
+    the host sees SDX_ERR_DEVICE, and the context is usable again after clearing."""
+    from simdonnx_b200 import _native as N, backend as B
+    be.clear_device_error()
+    N.call("sdx_selftest_bounded_wait", be.ctx, 50, B.cur_stream())
+    with pytest.raises(N.SdxError) as ei:
+        be.sync()
+    assert ei.value.code == 5
+    assert be.device_error() == 0x1F0
+    be.clear_device_error()
+    test_resize_add_and_concat(be)
+    assert be.device_error() == 0
