@@ -271,6 +271,9 @@ int sdx_session_enqueue(sdx_session* s);
 /* End-to-end run: host input -> device, graph, device -> host output, wait (timeout_ms as sdx_stream_sync). */
 int sdx_session_run(sdx_session* s, const void* host_in, void* host_out, int timeout_ms);
 int sdx_session_node_count(sdx_session* s, int* count);
+/* Runs node `index` alone, eagerly, on the session stream (per-node timing, like the reference's
+ * VkInferenceSession.DebugProfile, src/Backends/Vulkan/VkSession.cs:413-492). */
+int sdx_session_enqueue_node(sdx_session* s, int index);
 int sdx_session_destroy(sdx_session* s);
 
 #ifdef __cplusplus

@@ -1,0 +1,125 @@
+"""CPU executor of an ExecPlan over the oracle kernels -- TEST INFRASTRUCTURE ONLY.
+
+Restates the reference's InferenceSession node loop for NHWC plans (src/Engine/Session.cs:88-112,
+ExecNhwc :322-427, generic ops :148-318): every node runs the oracle's restatement of the
+reference CPU kernel, fp32 end to end. Packed weights are cached per node like the reference's
+CpuKernels.Cache (src/Engine/CpuKernels.cs:16-40).
+"""
+from __future__ import annotations
+
+import numpy as np
+
+import oracle as O
+
+
+class OracleSession:
+    def __init__(self, plan, keep_all: bool = False):
+        self.plan = plan
+        self.keep_all = keep_all
+        self._packs = {}
+
+    def _conv_plan(self, n):
+        kp = self._packs.get(n.name)
+        if kp is None:
+            p = n.p
+            w = self.plan.values[n.ins[1]].const
+            b = self.plan.values[p.bias].const if p.bias else None
+            kp = O.ConvPlan(w, b, group=p.group, strides=p.strides)
+            self._packs[n.name] = kp
+        return kp
+
+    def _gemm_plan(self, n):
+        kp = self._packs.get(n.name)
+        if kp is None:
+            w = self.plan.values[n.ins[1]].const
+            b = self.plan.values[n.p.bias].const if n.p.bias else None
+            kp = O.GemmPlan(w, b, trans_b=n.p.trans_b)
+            self._packs[n.name] = kp
+        return kp
+
+    def run(self, feeds: dict) -> dict:
+        P = self.plan
+        env = {}
+        for name, v in P.values.items():
+            if v.is_const:
+                env[name] = v.const
+        for name in (P.inputs or [P.input]):
+            a = np.ascontiguousarray(feeds[name], np.float32)
+            assert a.shape == P.values[name].shape, (name, a.shape)
+            env[name] = a
+        for n in P.nodes:
+            out = self._exec(n, env)
+            for o, val in zip(n.outs, out if isinstance(out, tuple) else (out,)):
+                env[o] = val
+        return env if self.keep_all else {P.output: env[P.output]}
+
+    def _nhwc(self, name, env):
+        v = self.plan.values[name]
+        a = env[name]
+        if v.layout == "nchw":  # boundary relayout into the NHWC plan
+            a = np.ascontiguousarray(a.transpose(0, 2, 3, 1))
+        return a
+
+    def _exec(self, n, env):
+        P = self.plan
+        op, p = n.op, n.p
+        if op == "Conv":
+            x = self._nhwc(n.ins[0], env)
+            kp = self._conv_plan(n)
+            add = env[p.add] if p.add else None
+            if p.pool is not None:
+                return O.conv_pool(x, kp, pads=p.pads, act=p.act, pool_relu=p.pool.fuse_relu)
+            return O.conv(x, kp, strides=p.strides, pads=p.pads, act=p.act, add=add)
+        if op == "ConvTranspose":
+            w = P.values[n.ins[1]].const
+            b = P.values[p.bias].const if p.bias else None
+            return O.convt(env[n.ins[0]], w, b, act=p.act)
+        if op == "ChannelGate":
+            x = env[n.ins[0]]
+            return O.channel_gate(x, P.values[n.ins[1]].const, P.values[p.b1].const if p.b1 else None,
+                                  P.values[n.ins[2]].const, P.values[p.b2].const if p.b2 else None,
+                                  act1_relu=p.act1 == "relu", hard=p.hard, alpha=p.alpha, beta=p.beta, offset=p.offset)
+        if op == "Elementwise":
+            a, b = env[n.ins[0]], env[n.ins[1]]
+            relu = p.act == "relu"
+            if a.shape == b.shape:
+                y = O.binary(a, b, p.op, relu)
+            elif b.ndim == 2 and a.ndim == 4 and b.shape == (a.shape[0], a.shape[3]):
+                y = O.channel_broadcast(a, b, p.op, relu=relu)
+            else:
+                raise NotImplementedError(f"broadcast {a.shape} {b.shape}")
+            if p.act not in ("none", "relu"):
+                y = O.act(y, p.act)
+            return y
+        if op == "ResizeNearest":
+            add = env[n.ins[1]] if len(n.ins) > 1 else None
+            return O.resize_nearest(env[n.ins[0]], p.scales, add=add, add_relu=p.add_relu)
+        if op == "Concat":
+            return O.concat_channels([env[v] for v in n.ins])
+        if op == "MaxPool":
+            return O.maxpool(env[n.ins[0]], p.kernel, p.strides, p.pads, relu=p.fuse_relu)
+        if op == "AvgPool":
+            return O.avgpool(env[n.ins[0]], p.kernel, p.strides, p.pads, p.count_include_pad)
+        if op == "Gemm":
+            y = O.gemm(env[n.ins[0]], self._gemm_plan(n), act=p.act)
+            if p.add:
+                y = O.binary(y, env[p.add], "add")
+            return y
+        if op == "LayerNorm":
+            return O.layernorm(env[n.ins[0]], P.values[n.ins[1]].const, P.values[n.ins[2]].const, p.eps)
+        if op == "Softmax":
+            return O.softmax(env[n.ins[0]])
+        if op == "Attention":
+            # CPU plans run the unfused MatMul -> scale -> Softmax -> MatMul (attention is fused on GPU
+            # plans only, src/Engine/GraphCompiler.cs:614-770)
+            qkv = env[n.ins[0]]
+            nb, t = qkv.shape[0], qkv.shape[1]
+            q, k, v = (np.ascontiguousarray(qkv.reshape(nb, t, 3, p.heads, p.head_dim)[:, :, i].transpose(0, 2, 1, 3))
+                       for i in range(3))
+            s = O.matmul(q, np.ascontiguousarray(k.transpose(0, 1, 3, 2)))
+            s = O.binary(s, np.full(s.shape, p.scale, np.float32), "mul")
+            y = O.matmul(O.softmax(s), v)
+            return np.ascontiguousarray(y.transpose(0, 2, 1, 3)).reshape(nb, t, p.heads * p.head_dim)
+        if op == "Act":
+            return O.act(env[n.ins[0]], p)
+        raise NotImplementedError(op)

@@ -138,6 +138,7 @@ _SIGS = {
     "sdx_session_enqueue": (_i, [_p]),
     "sdx_session_run": (_i, [_p, _p, _p, _i]),
     "sdx_session_node_count": (_i, [_p, ctypes.POINTER(_i)]),
+    "sdx_session_enqueue_node": (_i, [_p, _i]),
     "sdx_session_destroy": (_i, [_p]),
 }
 

@@ -298,10 +298,11 @@ int pool_launch(const PoolArgs& a, cudaStream_t st) {
 // Stage 1: per (image, pixel chunk) channel sums into scratch; stage 2: one CTA per image reduces
 // the chunks, forms the means, runs FC1 (+relu) and FC2 and the (hard) sigmoid gate
 // (Nhwc.ChannelGate, src/Kernels/Nhwc.Det.cs:287-314).
+// Pixel chunks per image depend on the image size only, so an image's gate (and everything after
+// it) is bit-identical whatever batch it runs in.
 static int gate_chunks(int batch, int hw) {
-  int want = std::max(1, (4 * 148 + batch - 1) / batch);
-  int maxc = std::max(1, (hw + 255) / 256);
-  return std::min(want, maxc);
+  (void)batch;
+  return std::min(64, std::max(1, (hw + 2047) / 2048));
 }
 
 size_t gate_scratch_bytes(int batch, int hw, int c) {

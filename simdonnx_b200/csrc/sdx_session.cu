@@ -216,6 +216,13 @@ int sdx_session_node_count(sdx_session* s, int* count) {
   return SDX_OK;
 }
 
+int sdx_session_enqueue_node(sdx_session* s, int index) {
+  if (!s) return set_error(SDX_ERR_INVALID, "null session");
+  if (index < 0 || index >= (int)s->nodes.size()) return set_error(SDX_ERR_INVALID, "node index %d out of range", index);
+  cudaSetDevice(s->ctx->device);
+  return run_node(s, s->nodes[(size_t)index]);
+}
+
 int sdx_session_destroy(sdx_session* s) {
   if (!s) return SDX_OK;
   cudaSetDevice(s->ctx->device);

@@ -1,0 +1,105 @@
+"""Algorithmic work of each lowered node: FLOPs and HBM bytes, and the kernel class it runs on.
+
+Definitions (fixed for every report):
+  conv   FLOPs = 2 * N * OH * OW * OC * (IC / group) * KH * KW
+  gemm   FLOPs = 2 * M * N * K
+  convT  FLOPs = 2 * N * H * W * IC * OC * KH * KW
+  bytes  = every distinct tensor the node reads once + every tensor it writes once, at storage
+           precision (activations fp16, graph I/O and gates fp32, tensor-core weights fp16,
+           bandwidth-kernel weights and biases fp32); halo re-reads and im2col / tile padding
+           do not count.
+A kernel is tensor-bound when FLOPs / bytes exceeds the ridge peak_flops / peak_bw, else HBM-bound.
+"""
+from __future__ import annotations
+
+import numpy as np
+
+from .plan import ExecPlan
+
+
+def _nb(plan: ExecPlan, v: str) -> int:
+    return plan.values[v].nbytes if v else 0
+
+
+def _nhwc(plan, v):
+    val = plan.values[v]
+    s = val.shape
+    return (s[0], s[2], s[3], s[1]) if val.layout == "nchw" else s
+
+
+def conv_kernel_class(plan: ExecPlan, n) -> str:
+    """Mirrors the routing of sdx_conv2d (csrc/sdx_api.cu conv_route)."""
+    p = n.p
+    xv = plan.values[n.ins[0]]
+    ic = _nhwc(plan, n.ins[0])[3]
+    oc = plan.values[n.ins[1]].const.shape[0]
+    if p.group > 1:
+        return "depthwise"
+    if (xv.dtype == "f16" and xv.layout == "nhwc" and ic % 8 == 0 and p.strides == (1, 1) and oc >= 8 and
+            p.pool is None and getattr(p, "in_scale", None) is None):
+        return "conv_tc_rows" if p.kernel == (1, 1) and not any(p.pads) else "conv_tc"
+    return "direct_conv"
+
+
+def node_cost(plan: ExecPlan, n) -> tuple:
+    """(kernel class, FLOPs, bytes) of one lowered node."""
+    op, p = n.op, n.p
+    out = n.outs[0]
+    if op == "Conv":
+        cls = conv_kernel_class(plan, n)
+        nb, ih, iw, ic = _nhwc(plan, n.ins[0])
+        _, oh, ow, oc = plan.values[out].shape
+        W = plan.values[n.ins[1]].const
+        kh, kw = W.shape[2], W.shape[3]
+        flops = 2 * nb * oh * ow * oc * (ic // p.group) * kh * kw
+        wbytes = W.size * (2 if cls.startswith("conv_tc") else 4)
+        byt = _nb(plan, n.ins[0]) + wbytes + (4 * oc if p.bias else 0) + _nb(plan, p.add) + _nb(plan, out)
+        sc = getattr(p, "in_scale", None)
+        if sc:
+            byt += _nb(plan, sc)
+        return cls, flops, byt
+    if op == "ConvTranspose":
+        nb, ih, iw, ic = plan.values[n.ins[0]].shape
+        W = plan.values[n.ins[1]].const
+        _, oc, kh, kw = W.shape
+        cls = "convt_tc" if oc >= 8 else "convt_dot"
+        flops = 2 * nb * ih * iw * ic * oc * kh * kw
+        byt = _nb(plan, n.ins[0]) + W.size * (2 if oc >= 8 else 4) + 4 * oc + _nb(plan, out)
+        return cls, flops, byt
+    if op == "Gemm":
+        a = n.ins[0]
+        Wb = plan.values[n.ins[1]].const
+        k, nn = (Wb.shape[1], Wb.shape[0]) if p.trans_b else Wb.shape
+        m = int(np.prod(plan.values[a].shape)) // k
+        byt = _nb(plan, a) + Wb.size * 2 + (4 * nn if p.bias else 0) + _nb(plan, p.add) + _nb(plan, out)
+        return "gemm_tc", 2 * m * nn * k, byt
+    if op == "ChannelGate":
+        byt = _nb(plan, n.ins[0]) + plan.values[n.ins[1]].const.size * 4 + plan.values[n.ins[2]].const.size * 4
+        return "channel_gate", 0, byt + _nb(plan, out)
+    if op == "Elementwise":
+        cls = "broadcast" if plan.values[n.ins[0]].shape != plan.values[n.ins[1]].shape else "binary"
+        return cls, 0, _nb(plan, n.ins[0]) + _nb(plan, n.ins[1]) + _nb(plan, out)
+    if op == "ResizeNearest":
+        return "resize_nearest", 0, sum(_nb(plan, v) for v in n.ins) + _nb(plan, out)
+    if op in ("MaxPool", "AvgPool"):
+        return "pool", 0, _nb(plan, n.ins[0]) + _nb(plan, out)
+    if op == "Concat":
+        return "concat", 0, sum(_nb(plan, v) for v in n.ins) + _nb(plan, out)
+    if op == "Convert":
+        return "convert", 0, _nb(plan, n.ins[0]) + _nb(plan, out)
+    if op in ("LayerNorm", "Softmax", "Act"):
+        return op.lower(), 0, _nb(plan, n.ins[0]) + _nb(plan, out)
+    if op == "Attention":
+        nb, t, _ = plan.values[n.ins[0]].shape
+        flops = 4 * nb * p.heads * t * t * p.head_dim
+        return "attention", flops, _nb(plan, n.ins[0]) + _nb(plan, out)
+    return op.lower(), 0, 0
+
+
+def plan_totals(plan: ExecPlan) -> dict:
+    flops = byt = 0
+    for n in plan.nodes:
+        _, f, b = node_cost(plan, n)
+        flops += f
+        byt += b
+    return {"flops": flops, "bytes": byt}

@@ -1,0 +1,371 @@
+"""CudaGraphModel / CudaInferenceSession: lower an ExecPlan onto libsdxcuda and run it.
+
+The reference's Vulkan backend is the template (VkGraphModel, src/Backends/Vulkan/VkGraph.cs:44-155,
+:472-1112; VkInferenceSession, src/Backends/Vulkan/VkSession.cs:63-143, :282-337, :535-556):
+  * backend-side rewrites that change no numerics class (cuda_rewrite): fp32 -> fp16 boundary
+    conversion where a tensor-core conv reads a graph input; the squeeze-excitation product x*s
+    folded into the load of the depthwise convs that consume it; producers of a channel Concat
+    write straight into their slice of its output;
+  * one device arena (int64 byte offsets, plan.plan_arena) + a per-model const store of packed
+    weights; every node becomes one sdx_* descriptor over device pointers arena + offset;
+  * the node list is validated once eagerly and captured into one CUDA graph.
+"""
+from __future__ import annotations
+
+import copy
+import ctypes
+
+import numpy as np
+import torch
+
+from . import _native as N
+from . import backend as B
+from .plan import ExecPlan, Node
+
+_DT = {"f16": N.F16, "f32": N.F32}
+_LAY = {"nhwc": N.NHWC, "nchw": N.NCHW, "raw": N.NHWC}
+
+
+def _nhwc_shape(v):
+    s = v.shape
+    return (s[0], s[2], s[3], s[1]) if v.layout == "nchw" else s
+
+
+def cuda_rewrite(plan: ExecPlan) -> ExecPlan:
+    P = copy.copy(plan)
+    P.values = {k: copy.copy(v) for k, v in plan.values.items()}
+    P.nodes = [Node(n.op, list(n.ins), list(n.outs), copy.copy(n.p), n.name) for n in plan.nodes]
+    P.inputs = list(plan.inputs or [plan.input])
+
+    # 1. fp32 NHWC graph input read by a tensor-core conv -> explicit conversion to fp16
+    out_nodes = []
+    for n in P.nodes:
+        if n.op == "Conv":
+            xv = P.values[n.ins[0]]
+            cin = _nhwc_shape(xv)[3]
+            if xv.dtype == "f32" and xv.layout == "nhwc" and cin % 8 == 0 and n.p.group == 1 and n.p.strides == (1, 1):
+                h = P.add_value(n.ins[0] + ".f16", xv.shape, "f16", "nhwc")
+                out_nodes.append(Node("Convert", [n.ins[0]], [h], None, h))
+                n.ins[0] = h
+        out_nodes.append(n)
+    P.nodes = out_nodes
+
+    # 2. SE product folded into consuming depthwise convs
+    keep = []
+    for n in P.nodes:
+        if n.op == "Elementwise" and n.p.op == "mul" and n.p.act == "none":
+            x, s = n.ins
+            xs, ss = P.values[x].shape, P.values[s].shape
+            cons = P.consumers(n.outs[0])
+            if (len(ss) == 2 and len(xs) == 4 and ss == (xs[0], xs[3]) and cons and n.outs[0] != P.output and
+                    all(c.op == "Conv" and c.p.group > 1 and c.ins[0] == n.outs[0] for c in cons)):
+                for c in cons:
+                    c.ins[0] = x
+                    c.p.in_scale = s
+                continue
+        keep.append(n)
+    P.nodes = keep
+
+    # 3. channel concat: producers write into their slice
+    keep = []
+    for n in P.nodes:
+        if n.op == "Concat":
+            prods = {o: m for m in P.nodes for o in m.outs}
+            ok = True
+            for v in n.ins:
+                m = prods.get(v)
+                if (m is None or m.op not in ("Conv", "ResizeNearest") or len(P.consumers(v)) != 1 or
+                        P.values[v].dtype != "f16" or P.shape(v)[3] % 8 != 0):
+                    ok = False
+            if ok:
+                off = 0
+                for v in n.ins:
+                    P.values[v].alias = (n.outs[0], off)
+                    off += P.shape(v)[3]
+                continue
+        keep.append(n)
+    P.nodes = keep
+    return P
+
+
+class CudaInferenceSession:
+    """One compiled plan on one GPU: arena + const store + a graph-captured node list."""
+
+    def __init__(self, plan: ExecPlan, device: int = 0, use_graph: bool = True, keep_all: bool = False):
+        self.be = B.CudaBackend.get(device)
+        self.device = torch.device("cuda", device)
+        self.src_plan = plan
+        self.plan = P = cuda_rewrite(plan)
+        P.plan_arena(keep_all=keep_all)
+        self._consts = {}
+        self._scratch_bytes = 0
+        for n in P.nodes:
+            if n.op == "ChannelGate":
+                nn, h, w, c = P.shape(n.ins[0])
+                self._scratch_bytes = max(self._scratch_bytes, int(N.lib().sdx_channel_gate_scratch_bytes(nn, h * w, c)))
+        total = P.arena_bytes + self._scratch_bytes + 256
+        h = ctypes.c_void_p()
+        with torch.cuda.device(device):
+            N.call("sdx_session_create", self.be.ctx, total, ctypes.byref(h))
+        self.h = h
+        base = ctypes.c_uint64()
+        N.call("sdx_session_arena", h, ctypes.byref(base), None)
+        self.base = base.value
+        self.scratch = self.base + (P.arena_bytes + 255) // 256 * 256
+        with torch.cuda.device(device):
+            for n in P.nodes:
+                kind, desc = self._lower(n)
+                N.call("sdx_session_add_node", h, kind, ctypes.byref(desc), ctypes.sizeof(desc))
+            ins = P.inputs
+            self.in_off = P.offsets[ins[0]]
+            self.in_bytes = max(P.offsets[v] + P.values[v].nbytes for v in ins) - self.in_off
+            self.out_off = P.offsets[P.output]
+            self.out_bytes = P.values[P.output].nbytes
+            N.call("sdx_session_set_io", h, self.base + self.in_off, self.in_bytes, self.base + self.out_off,
+                   self.out_bytes)
+            torch.cuda.synchronize()
+            N.call("sdx_session_build", h, int(use_graph))
+        st = ctypes.c_void_p()
+        N.call("sdx_session_stream", h, ctypes.byref(st))
+        self.stream_ptr = st.value
+        self.stream = torch.cuda.ExternalStream(st.value, device=self.device)
+        self._pin_in = self._pin_out = None
+
+    # ------------------------------------------------------------------ lowering
+    def ptr(self, v: str) -> int:
+        return self.base + self.plan.offsets[v]
+
+    def _const_dev(self, key, make):
+        t = self._consts.get(key)
+        if t is None:
+            t = self._consts[key] = make()
+        return t
+
+    def _f32(self, name):
+        if name is None:
+            return 0
+        return B.ptr(self._const_dev(name, lambda: torch.from_numpy(self.plan.values[name].const).to(self.device)))
+
+    def _zeros(self, n):
+        return B.ptr(self._const_dev(("zeros", n), lambda: torch.zeros(n, dtype=torch.float32, device=self.device)))
+
+    def _lower(self, n):
+        P = self.plan
+        op, p = n.op, n.p
+        if op == "Conv":
+            xv, yv = P.values[n.ins[0]], P.values[n.outs[0]]
+            nb, ih, iw, ic = _nhwc_shape(xv)
+            W = P.values[n.ins[1]].const
+            oc = W.shape[0]
+            yslice = yv.alias
+            addv = P.values[p.add] if p.add else None
+            d = B.conv_desc(nb, ih, iw, ic, oc, p.kernel[0], p.kernel[1], stride=p.strides, pads=p.pads,
+                            group=p.group, act=p.act, x_dtype=torch.float16 if xv.dtype == "f16" else torch.float32,
+                            x_layout=_LAY[xv.layout], y_dtype=torch.float16 if yv.dtype == "f16" else torch.float32,
+                            y_layout=_LAY[yv.layout],
+                            add_dtype=torch.float16 if (addv is None or addv.dtype == "f16") else torch.float32,
+                            add_layout=_LAY[addv.layout] if addv else N.NHWC,
+                            pool=p.pool is not None, pool_relu=bool(p.pool and p.pool.fuse_relu),
+                            y_pix_stride=P.shape(yslice[0])[3] if yslice else 0, y_ch_off=yslice[1] if yslice else 0)
+            wt = self._const_dev(("convw", n.name), lambda: B.pack_conv(d, W, self.device))
+            d.x = self.ptr(n.ins[0])
+            d.w = B.ptr(wt)
+            d.bias = self._f32(p.bias) if p.bias else (self._zeros(oc) if p.group > 1 else 0)
+            d.add = self.ptr(p.add) if p.add else 0
+            d.y = self.ptr(n.outs[0])
+            scale = getattr(p, "in_scale", None)
+            d.in_scale = self.ptr(scale) if scale else 0
+            return N.OP_CONV, d
+        if op == "ConvTranspose":
+            xv, yv = P.values[n.ins[0]], P.values[n.outs[0]]
+            nb, ih, iw, ic = xv.shape
+            W = P.values[n.ins[1]].const
+            _, oc, kh, kw = W.shape
+            d = N.ConvtDesc()
+            d.batch, d.ih, d.iw, d.ic, d.oc, d.kh, d.kw = nb, ih, iw, ic, oc, kh, kw
+            d.act, d.y_dtype = N.ACT[p.act], _DT[yv.dtype]
+            if oc >= 8:
+                wt = self._const_dev(("convtw", n.name), lambda: B.pack_convt(W, self.device))
+            else:
+                wt = self._const_dev(("convtw", n.name), lambda: torch.from_numpy(W).to(self.device))
+            d.x, d.w, d.y = self.ptr(n.ins[0]), B.ptr(wt), self.ptr(n.outs[0])
+            d.bias = self._f32(p.bias)
+            return N.OP_CONVT, d
+        if op == "ChannelGate":
+            nb, h, w, c = P.shape(n.ins[0])
+            W1, W2 = P.values[n.ins[1]].const, P.values[n.ins[2]].const
+            d = N.GateDesc()
+            d.batch, d.hw, d.c, d.r = nb, h * w, c, W1.shape[0]
+            d.act1_relu, d.hard = int(p.act1 == "relu"), int(p.hard)
+            d.alpha, d.beta, d.offset = p.alpha, p.beta, p.offset
+            d.x, d.w1, d.w2 = self.ptr(n.ins[0]), self._f32(n.ins[1]), self._f32(n.ins[2])
+            d.b1, d.b2 = self._f32(p.b1), self._f32(p.b2)
+            d.s, d.partial = self.ptr(n.outs[0]), self.scratch
+            return N.OP_CHANNEL_GATE, d
+        if op == "Elementwise":
+            a, b = n.ins
+            d = N.MiscDesc()
+            d.op, d.relu = N.EW[p.op], int(p.act == "relu")
+            if P.shape(a) == P.shape(b):
+                d.n = int(np.prod(P.shape(a)))
+                d.a, d.b, d.y = self.ptr(a), self.ptr(b), self.ptr(n.outs[0])
+                return N.OP_BINARY, d
+            nb, c = P.shape(a)[0], P.shape(a)[-1]
+            d.batch, d.c, d.pixels = nb, c, int(np.prod(P.shape(a))) // (nb * c)
+            d.x, d.b, d.y = self.ptr(a), self.ptr(b), self.ptr(n.outs[0])
+            return N.OP_CHANNEL_BROADCAST, d
+        if op == "ResizeNearest":
+            x = n.ins[0]
+            nb, ih, iw, c = P.shape(x)
+            yv = P.values[n.outs[0]]
+            d = N.ResizeDesc()
+            d.batch, d.ih, d.iw, d.c = nb, ih, iw, c
+            d.oh, d.ow = yv.shape[1], yv.shape[2]
+            d.add_relu = int(p.add_relu)
+            d.y_pix_stride = P.shape(yv.alias[0])[3] if yv.alias else c
+            d.y_ch_off = yv.alias[1] if yv.alias else 0
+            d.x = self.ptr(x)
+            d.add = self.ptr(n.ins[1]) if len(n.ins) > 1 else 0
+            d.y = self.ptr(n.outs[0])
+            return N.OP_RESIZE_NEAREST, d
+        if op == "Concat":
+            d = N.MiscDesc()
+            first = P.shape(n.ins[0])
+            d.pixels = int(np.prod(first[:-1]))
+            d.nin = len(n.ins)
+            for i, v in enumerate(n.ins):
+                d.counts[i] = P.shape(v)[-1]
+                d.ins[i] = self.ptr(v)
+            d.y = self.ptr(n.outs[0])
+            return N.OP_CONCAT, d
+        if op in ("MaxPool", "AvgPool"):
+            nb, ih, iw, c = P.shape(n.ins[0])
+            _, oh, ow, _ = P.shape(n.outs[0])
+            d = N.PoolDesc()
+            d.batch, d.ih, d.iw, d.c, d.oh, d.ow = nb, ih, iw, c, oh, ow
+            d.kh, d.kw = p.kernel
+            d.sh, d.sw = p.strides
+            d.pad_t, d.pad_l = p.pads[0], p.pads[1]
+            d.is_avg, d.relu, d.count_include_pad = int(op == "AvgPool"), int(p.fuse_relu), int(p.count_include_pad)
+            d.x, d.y = self.ptr(n.ins[0]), self.ptr(n.outs[0])
+            return N.OP_POOL, d
+        if op == "Gemm":
+            a = n.ins[0]
+            Wb = P.values[n.ins[1]].const
+            k, nn = (Wb.shape[1], Wb.shape[0]) if p.trans_b else Wb.shape
+            m = int(np.prod(P.shape(a))) // k
+            yv = P.values[n.outs[0]]
+            d = N.GemmDesc()
+            d.m, d.k, d.n, d.lda = m, k, nn, k
+            d.act, d.y_dtype = N.ACT[p.act], _DT[yv.dtype]
+            d.add_dtype = _DT[P.values[p.add].dtype] if p.add else N.F16
+            d.ldy, d.ldadd = nn, nn
+            wt = self._const_dev(("gemmw", n.name), lambda: B.pack_gemm(Wb, p.trans_b, self.device))
+            d.a, d.w, d.y = self.ptr(a), B.ptr(wt), self.ptr(n.outs[0])
+            d.bias = self._f32(p.bias)
+            d.add = self.ptr(p.add) if p.add else 0
+            return N.OP_GEMM, d
+        if op == "Convert":
+            xv, yv = P.values[n.ins[0]], P.values[n.outs[0]]
+            nb, h, w, c = _nhwc_shape(xv)
+            d = N.MiscDesc()
+            d.batch, d.c, d.pixels = nb, c, h * w
+            d.x_dtype, d.x_layout, d.y_dtype, d.y_layout = _DT[xv.dtype], _LAY[xv.layout], _DT[yv.dtype], _LAY[yv.layout]
+            d.x, d.y = self.ptr(n.ins[0]), self.ptr(n.outs[0])
+            return N.OP_CONVERT, d
+        if op == "LayerNorm":
+            c = P.shape(n.ins[0])[-1]
+            d = N.MiscDesc()
+            d.rows, d.c, d.eps = int(np.prod(P.shape(n.ins[0]))) // c, c, p.eps
+            d.x, d.w, d.bias, d.y = self.ptr(n.ins[0]), self._f32(n.ins[1]), self._f32(n.ins[2]), self.ptr(n.outs[0])
+            return N.OP_LAYERNORM, d
+        if op == "Softmax":
+            c = P.shape(n.ins[0])[-1]
+            d = N.MiscDesc()
+            d.rows, d.c, d.y_dtype = int(np.prod(P.shape(n.ins[0]))) // c, c, _DT[P.values[n.outs[0]].dtype]
+            d.x, d.y = self.ptr(n.ins[0]), self.ptr(n.outs[0])
+            return N.OP_SOFTMAX, d
+        if op == "Attention":
+            nb, t, _ = P.shape(n.ins[0])
+            d = N.MiscDesc()
+            d.batch, d.t, d.heads, d.d, d.scale = nb, t, p.heads, p.head_dim, p.scale
+            d.x, d.y = self.ptr(n.ins[0]), self.ptr(n.outs[0])
+            return N.OP_ATTENTION, d
+        if op == "Act":
+            d = N.MiscDesc()
+            d.n, d.act = int(np.prod(P.shape(n.ins[0]))), N.ACT[p]
+            d.x, d.y = self.ptr(n.ins[0]), self.ptr(n.outs[0])
+            return N.OP_ACT, d
+        raise NotImplementedError(f"no CUDA lowering for {op}")
+
+    # ------------------------------------------------------------------ running
+    def node_count(self) -> int:
+        c = ctypes.c_int()
+        N.call("sdx_session_node_count", self.h, ctypes.byref(c))
+        return c.value
+
+    def enqueue(self) -> None:
+        """Device-resident run on the session stream (inputs already in the arena)."""
+        N.call("sdx_session_enqueue", self.h)
+
+    def write_inputs(self, feeds: dict) -> None:
+        """Copy host inputs into the arena (synchronous)."""
+        for name in self.plan.inputs:
+            a = np.ascontiguousarray(feeds[name], np.float32)
+            t = torch.from_numpy(a).to(self.device)
+            if self.plan.values[name].dtype == "f16":
+                t = t.half()
+            torch.cuda.synchronize(self.device)
+            N.call("sdx_memcpy_dtod_async", self.be.ctx, self.ptr(name), B.ptr(t), t.numel() * t.element_size(),
+                   ctypes.c_void_p(self.stream_ptr))
+            N.call("sdx_stream_sync", self.be.ctx, ctypes.c_void_p(self.stream_ptr), 0)
+
+    def read(self, name: str) -> np.ndarray:
+        """A value's arena contents as fp32 (dense values only)."""
+        v = self.plan.values[name]
+        dt = np.float16 if v.dtype == "f16" else np.float32
+        out = np.empty(v.shape, dt)
+        N.call("sdx_stream_sync", self.be.ctx, ctypes.c_void_p(self.stream_ptr), 0)
+        N.call("sdx_memcpy_dtoh_async", self.be.ctx, out.ctypes.data_as(ctypes.c_void_p), self.ptr(name), out.nbytes,
+               ctypes.c_void_p(self.stream_ptr))
+        N.call("sdx_stream_sync", self.be.ctx, ctypes.c_void_p(self.stream_ptr), 0)
+        return out.astype(np.float32)
+
+    def pinned_io(self):
+        """Pinned host staging buffers (input region, output) for end-to-end runs."""
+        if self._pin_in is None:
+            self._pin_in = torch.empty(self.in_bytes, dtype=torch.uint8).pin_memory()
+            self._pin_out = torch.empty(self.out_bytes, dtype=torch.uint8).pin_memory()
+        return self._pin_in, self._pin_out
+
+    def stage_inputs(self, feeds: dict) -> None:
+        pin_in, _ = self.pinned_io()
+        buf = pin_in.numpy()
+        for name in self.plan.inputs:
+            a = np.ascontiguousarray(feeds[name], np.float32)
+            if self.plan.values[name].dtype == "f16":
+                a = a.astype(np.float16)
+            off = self.plan.offsets[name] - self.in_off
+            buf[off:off + a.nbytes] = a.view(np.uint8).ravel()
+
+    def run(self, feeds: dict | None = None, timeout_ms: int = 0) -> np.ndarray:
+        """End-to-end: pinned host input -> device, graph, device -> pinned host output, wait."""
+        pin_in, pin_out = self.pinned_io()
+        if feeds is not None:
+            self.stage_inputs(feeds)
+        N.call("sdx_session_run", self.h, ctypes.c_void_p(pin_in.data_ptr()), ctypes.c_void_p(pin_out.data_ptr()),
+               timeout_ms)
+        ov = self.plan.values[self.plan.output]
+        dt = np.float16 if ov.dtype == "f16" else np.float32
+        return pin_out.numpy().view(dt).reshape(ov.shape).astype(np.float32)
+
+    def close(self) -> None:
+        if getattr(self, "h", None):
+            N.call("sdx_session_destroy", self.h)
+            self.h = None
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
