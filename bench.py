@@ -156,6 +156,7 @@ def main() -> None:
     ap.add_argument("--ref-images", type=int, default=1, help="reference arm: images per step")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-e2e", action="store_true")
+    ap.add_argument("--node-times", default="", help="write per-node timings (JSON) to this path")
     args = ap.parse_args()
     args.warmup = max(args.warmup, 3)
 
@@ -226,14 +227,20 @@ def main() -> None:
     evs[-1].synchronize()
     launches_per_step = int(N.lib().sdx_launch_count()) - before
     classes = {}
+    per_node = []
     for i, node in enumerate(sess.plan.nodes):
         cls, fl, by = roofline.node_cost(sess.plan, node)
         t = evs[i].elapsed_time(evs[i + 1])
+        per_node.append({"node": node.name, "op": node.op, "kernel": cls, "ms": t, "bytes": by, "flops": fl,
+                         "gbs": by / t / 1e6 if t > 0 else None, "out": list(sess.plan.values[node.outs[0]].shape)})
         c = classes.setdefault(cls, {"ms": 0.0, "flops": 0, "bytes": 0, "launches": 0})
         c["ms"] += t
         c["flops"] += fl
         c["bytes"] += by
         c["launches"] += 1
+    if args.node_times and rank == 0:
+        with open(args.node_times, "w") as f:
+            json.dump(per_node, f, indent=1)
     dom = max(classes, key=lambda k: classes[k]["ms"])
     dc = classes[dom]
     hbm, tflops, src = peaks()

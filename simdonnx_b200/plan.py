@@ -213,7 +213,7 @@ class ExecPlan:
 def _param_refs(p) -> list:
     """Value ids read through op params (ExecNode.ParamRefs, src/Engine/ExecPlan.cs:246-262)."""
     refs = []
-    for attr in ("bias", "add", "b1", "b2"):
+    for attr in ("bias", "add", "b1", "b2", "in_scale"):
         v = getattr(p, attr, None)
         if isinstance(v, str):
             refs.append(v)
