@@ -87,7 +87,7 @@ class Clocks:
                 "power_w_max": max(float(r[3]) for r in rows if r[3].replace(".", "").isdigit()) if rows else None}
 
 
-def cpu_baseline(batch_hw: int, seconds: float = 12.0, max_images: int = 64) -> dict:
+def cpu_baseline(batch_hw: int, seconds: float = 12.0, max_images: int = 2000) -> dict:
     """The reference's CPU algorithm (oracle restatement) on all host threads, bounded sample."""
     import numpy as np
 

@@ -20,8 +20,13 @@ def ptr(t: torch.Tensor | None) -> int:
     return 0 if t is None else int(t.data_ptr())
 
 
+_LEGACY_STREAM = 0x1  # cudaStreamLegacy: torch reports its default stream as handle 0
+
+
 def cur_stream() -> ctypes.c_void_p:
-    return ctypes.c_void_p(torch.cuda.current_stream().cuda_stream)
+    """torch's current stream as an sdx_stream (NULL would select the context's own stream)."""
+    h = torch.cuda.current_stream().cuda_stream
+    return ctypes.c_void_p(h if h else _LEGACY_STREAM)
 
 
 class CudaBackend:

@@ -18,7 +18,11 @@
 //            TMA zero-fills out-of-range rows/columns, which is the constant-0 padding. K is
 //            tap-major then channel, the order of the reference's packed weights
 //            (src/Kernels/Nhwc.cs:102-125).
-// B operand: packed weights [taps][n_tiles*BN][ICpad] fp16 (K-major), see sdx_pack_tc_weights.
+// B operand: packed weights [2][taps][n_tiles*BN][ICpad] fp16 (K-major): every weight w is stored as
+// the two-term sum hi + lo with hi = fp16(w), lo = fp16(w - hi), and both terms are multiplied into
+// the same TMEM accumulator (two MMAs per k-step). The activations stay one fp16 term; the weights
+// keep ~22 significant bits, so weight rounding no longer shifts coherent sums such as the
+// squeeze-excitation means. The path is HBM-bound, so the extra MMAs cost nothing measurable.
 //
 // ConvT (stride == kernel, src/Kernels/Nhwc.Det.cs:46-93): one GEMM [pixels, IC] x [IC, taps*OC]
 // whose epilogue scatters column tap*OC + o to output pixel (y*kh + dy, x*kw + dx).
@@ -123,7 +127,8 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   const int S = a.stages;
-  const uint32_t b_stage_bytes = (uint32_t)a.BN * TC_BK * 2;
+  const uint32_t b_half_bytes = (uint32_t)a.BN * TC_BK * 2;
+  const uint32_t b_stage_bytes = 2 * b_half_bytes;
   uint8_t* sA = smem;
   uint8_t* sB = smem + (size_t)S * TC_A_STAGE_BYTES;
   uint64_t* bars = reinterpret_cast<uint64_t*>(sB + (size_t)S * b_stage_bytes);
@@ -198,8 +203,10 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
           } else {
             tma_load_2d(dA, &tmA, fb, cb * TC_BK, m_tile * TC_BM);
           }
-          tma_load_2d(smem_u32(sB + (size_t)s * b_stage_bytes), &tmB, fb, cb * TC_BK,
-                      tap * a.b_rows_per_tap + n_tile * a.BN);
+          const int brow = tap * a.b_rows_per_tap + n_tile * a.BN;
+          tma_load_2d(smem_u32(sB + (size_t)s * b_stage_bytes), &tmB, fb, cb * TC_BK, brow);
+          tma_load_2d(smem_u32(sB + (size_t)s * b_stage_bytes + b_half_bytes), &tmB, fb, cb * TC_BK,
+                      a.taps * a.b_rows_per_tap + brow);
           issued[s] = round + 1;
         }
       }
@@ -228,9 +235,12 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
           tc_fence_after();
           const uint64_t ad = umma_desc_sw128(smem_u32(sA + (size_t)s * TC_A_STAGE_BYTES));
           const uint64_t bd = umma_desc_sw128(smem_u32(sB + (size_t)s * b_stage_bytes));
+          const uint64_t bl = umma_desc_sw128(smem_u32(sB + (size_t)s * b_stage_bytes + b_half_bytes));
 #pragma unroll
-          for (int k = 0; k < TC_BK / 16; k++)
+          for (int k = 0; k < TC_BK / 16; k++) {
             umma_f16(d, ad + 2u * k, bd + 2u * k, idesc, (kb > 0 || k > 0) ? 1u : 0u);
+            umma_f16(d, ad + 2u * k, bl + 2u * k, idesc, 1u);
+          }
           tc_commit(smem_u32(&empty[s]));
         }
         if (!ok) break;
@@ -344,7 +354,7 @@ void tc_plan_n(int N, int* BN, int* n_tiles) {
 
 static int pick_stages(int BN) {
   const int budget = 200 * 1024;
-  int per = (int)TC_A_STAGE_BYTES + BN * TC_BK * 2;
+  int per = (int)TC_A_STAGE_BYTES + 2 * BN * TC_BK * 2;
   return std::max(2, std::min(TC_MAX_STAGES, budget / per));
 }
 
@@ -467,7 +477,7 @@ int tc_launch(const TcProblem& p, cudaStream_t stream) {
     if (rc) return rc;
   }
   {
-    uint64_t dims[2] = {(uint64_t)kpad, (uint64_t)a.taps * a.b_rows_per_tap};
+    uint64_t dims[2] = {(uint64_t)kpad, 2ull * a.taps * a.b_rows_per_tap};
     uint64_t strides[1] = {(uint64_t)kpad * 2};
     uint32_t box[2] = {TC_BK, (uint32_t)BN};
     int rc = encode_map(&mB, p.w, 2, dims, strides, box);
@@ -475,7 +485,7 @@ int tc_launch(const TcProblem& p, cudaStream_t stream) {
   }
   const int total = a.m_tiles * a.n_tiles;
   if (total == 0) return SDX_OK;
-  const size_t smem = 1024 + (size_t)a.stages * (TC_A_STAGE_BYTES + (size_t)BN * TC_BK * 2) + 8 * (2 * a.stages + 5) + 16;
+  const size_t smem = 1024 + (size_t)a.stages * (TC_A_STAGE_BYTES + 2 * (size_t)BN * TC_BK * 2) + 8 * (2 * a.stages + 5) + 16;
   static bool attr_set[64] = {false};
   int dev = 0;
   cudaGetDevice(&dev);
@@ -498,7 +508,14 @@ size_t tc_weights_halves(int N, int K, int taps) {
   int BN, nt;
   tc_plan_n(N, &BN, &nt);
   size_t kpad = (size_t)(K + TC_BK - 1) / TC_BK * TC_BK;
-  return (size_t)taps * BN * nt * kpad;
+  return 2 * (size_t)taps * BN * nt * kpad;
+}
+
+// hi = fp16(w) at `hi`, lo = fp16(w - hi) at `hi + lo_off`
+static inline void put2(__half* out, size_t idx, size_t lo_off, float w) {
+  const __half h = __float2half_rn(w);
+  out[idx] = h;
+  out[idx + lo_off] = __float2half_rn(w - __half2float(h));
 }
 
 void tc_pack_conv(const float* w, int OC, int IC, int KH, int KW, __half* out) {
@@ -506,11 +523,11 @@ void tc_pack_conv(const float* w, int OC, int IC, int KH, int KW, __half* out) {
   tc_plan_n(OC, &BN, &nt);
   const size_t rows = (size_t)BN * nt, kpad = (size_t)(IC + TC_BK - 1) / TC_BK * TC_BK;
   const int taps = KH * KW;
-  memset(out, 0, sizeof(__half) * taps * rows * kpad);
+  const size_t lo = (size_t)taps * rows * kpad;
+  memset(out, 0, sizeof(__half) * 2 * lo);
   for (int o = 0; o < OC; o++)
     for (int c = 0; c < IC; c++)
-      for (int t = 0; t < taps; t++)
-        out[((size_t)t * rows + o) * kpad + c] = __float2half_rn(w[((size_t)o * IC + c) * taps + t]);
+      for (int t = 0; t < taps; t++) put2(out, ((size_t)t * rows + o) * kpad + c, lo, w[((size_t)o * IC + c) * taps + t]);
 }
 
 void tc_pack_convt(const float* w, int IC, int OC, int KH, int KW, __half* out) {
@@ -518,21 +535,21 @@ void tc_pack_convt(const float* w, int IC, int OC, int KH, int KW, __half* out) 
   int BN, nt;
   tc_plan_n(N, &BN, &nt);
   const size_t rows = (size_t)BN * nt, kpad = (size_t)(IC + TC_BK - 1) / TC_BK * TC_BK;
-  memset(out, 0, sizeof(__half) * rows * kpad);
+  const size_t lo = rows * kpad;
+  memset(out, 0, sizeof(__half) * 2 * lo);
   for (int c = 0; c < IC; c++)
     for (int o = 0; o < OC; o++)
-      for (int t = 0; t < taps; t++)
-        out[((size_t)t * OC + o) * kpad + c] = __float2half_rn(w[((size_t)c * OC + o) * taps + t]);
+      for (int t = 0; t < taps; t++) put2(out, ((size_t)t * OC + o) * kpad + c, lo, w[((size_t)c * OC + o) * taps + t]);
 }
 
 void tc_pack_gemm(const float* b, int K, int N, int trans_b, __half* out) {
   int BN, nt;
   tc_plan_n(N, &BN, &nt);
   const size_t rows = (size_t)BN * nt, kpad = (size_t)(K + TC_BK - 1) / TC_BK * TC_BK;
-  memset(out, 0, sizeof(__half) * rows * kpad);
+  const size_t lo = rows * kpad;
+  memset(out, 0, sizeof(__half) * 2 * lo);
   for (int n = 0; n < N; n++)
-    for (int k = 0; k < K; k++)
-      out[(size_t)n * kpad + k] = __float2half_rn(trans_b ? b[(size_t)n * K + k] : b[(size_t)k * N + n]);
+    for (int k = 0; k < K; k++) put2(out, (size_t)n * kpad + k, lo, trans_b ? b[(size_t)n * K + k] : b[(size_t)k * N + n]);
 }
 
 }  // namespace sdx

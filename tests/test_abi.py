@@ -55,10 +55,10 @@ def test_pack_sizes_cpu():
     d = B.conv_desc(1, 8, 8, 64, 64, 3, 3, pads=(1, 1, 1, 1))
     nb = ctypes.c_size_t()
     N.call("sdx_pack_conv", ctypes.byref(d), None, None, ctypes.byref(nb))
-    assert nb.value == 9 * 64 * 64 * 2
+    assert nb.value == 2 * 9 * 64 * 64 * 2  # hi + lo fp16 terms
     d = B.conv_desc(1, 8, 8, 96, 24, 3, 3, pads=(1, 1, 1, 1))
     N.call("sdx_pack_conv", ctypes.byref(d), None, None, ctypes.byref(nb))
-    assert nb.value == 9 * 32 * 128 * 2
+    assert nb.value == 2 * 9 * 32 * 128 * 2
     d = B.conv_desc(1, 8, 8, 3, 16, 3, 3, stride=(2, 2), pads=(1, 1, 1, 1), x_dtype=torch.float32, x_layout=1)
     N.call("sdx_pack_conv", ctypes.byref(d), None, None, ctypes.byref(nb))
     assert nb.value == 9 * 3 * 16 * 4

@@ -42,7 +42,7 @@ def test_det_n1_output_and_every_node():
     from simdonnx_b200 import configs
     plan = configs.build_det(batch=1)
     sess, feeds, ref, got = _run_both(plan, keep_all=True)
-    assert_close(got, ref[plan.output], "det output")
+    rel_out = metrics(got, ref[plan.output])[0]
     worst = []
     for n in sess.plan.nodes:
         for o in n.outs:
@@ -50,9 +50,10 @@ def test_det_n1_output_and_every_node():
             if o in ref and v.alias is None and o != plan.output:
                 rel, mabs, mx = metrics(sess.read(o), ref[o])
                 worst.append((rel, o))
-                assert rel < 2e-2, f"{o}: rel-L2 {rel:.2e}"
     worst.sort(reverse=True)
-    print("worst node rel-L2:", worst[:5])
+    print(f"det output rel-L2 {rel_out:.3e}; worst intermediate rel-L2:", [(f"{r:.2e}", o) for r, o in worst[:6]])
+    assert_close(got, ref[plan.output], "det output")
+    assert worst[0][0] < 1e-2, worst[:3]
     sess.close()
 
 
