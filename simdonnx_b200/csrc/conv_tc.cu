@@ -1,18 +1,21 @@
 // Dense conv / pointwise conv / Gemm / stride==kernel ConvTranspose on the sm_100a tensor cores.
 //
 // One persistent, warp-specialised kernel (192 threads, one CTA per SM):
-//   warp 0      TMA producer: per 64-channel k-block one A box and one B box into a smem ring
-//               (SWIZZLE_128B, no multicast) signalled through full/empty mbarriers;
+//   warp 0      TMA producer: per 64-channel k-block one A box and the two B boxes (weight terms
+//               hi, lo) into a smem ring (SWIZZLE_128B, no multicast), full/empty mbarriers;
 //   warp 1      allocates TMEM, one lane issues tcgen05.mma (M=128, N=BN, K=16 per instruction,
 //               f16 x f16 -> f32) into one of two TMEM accumulators and commits the stage back;
 //   warps 2..5  epilogue: drain the accumulator with tcgen05.ld (thread = output pixel row), apply
 //               bias -> + residual -> activation (the reference's Store16 order,
-//               src/Kernels/Nhwc.cs:376-398) and store fp16 / fp32 NHWC.
-// The double-buffered accumulator lets the epilogue of tile i overlap the MMAs of tile i+1.
+//               src/Kernels/Nhwc.cs:376-398), write the tile into a staging buffer in shared
+//               memory and store it with TMA tensor stores (fully coalesced, asynchronous, clipped
+//               at the tensor edges); the residual tile arrives the same way by a TMA load.
+// The double-buffered accumulator lets the epilogue of tile i overlap the MMAs of tile i+1, and
+// the double-buffered staging lets the TMA store of tile i overlap the epilogue of tile i+1.
 //
 // A operand ("mode"):
 //   TC_ROWS  A is a row-major [M, K] matrix (1x1 conv with the batch folded into rows,
-//            src/Kernels/Nhwc.cs:177-183; Gemm, src/Kernels/Nhwc.Avx512.cs:241-266; ConvT).
+//            src/Kernels/Nhwc.cs:177-183; Gemm, src/Kernels/Nhwc.Avx512.cs:241-266).
 //   TC_CONV  implicit-GEMM k x k conv, stride 1: for tap (ky, kx) and channel block cb the A tile
 //            is the 4-D box {64 ch, BW, BH, 1} of the NHWC input at (ox0+kx-pl, oy0+ky-pt); the
 //            TMA zero-fills out-of-range rows/columns, which is the constant-0 padding. K is
@@ -24,8 +27,10 @@
 // keep ~22 significant bits, so weight rounding no longer shifts coherent sums such as the
 // squeeze-excitation means. The path is HBM-bound, so the extra MMAs cost nothing measurable.
 //
-// ConvT (stride == kernel, src/Kernels/Nhwc.Det.cs:46-93): one GEMM [pixels, IC] x [IC, taps*OC]
-// whose epilogue scatters column tap*OC + o to output pixel (y*kh + dy, x*kw + dx).
+// ConvT (stride == kernel, src/Kernels/Nhwc.Det.cs:46-93): a 1x1 TC_CONV over the input pixels with
+// N = kh*kw*OC columns (tap-major); the epilogue stores column group (dy, dx*OC + o) of a BH x BW
+// input tile as one box of the 5-D output view {kw*OC, W, kh, H, batch}, i.e. straight to output
+// pixels (y*kh + dy, x*kw + dx).
 #include <cuda.h>
 #include <cuda_fp16.h>
 #include <cuda_runtime.h>
@@ -44,6 +49,7 @@ constexpr int TC_BK = 64;  // halves per 128-byte swizzled row
 constexpr int TC_THREADS = 192;
 constexpr int TC_MAX_STAGES = 8;
 constexpr uint32_t TC_A_STAGE_BYTES = TC_BM * TC_BK * 2;  // 16 KB
+constexpr int TC_SMEM_LIMIT = 227 * 1024;
 
 struct TcArgs {
   int mode;
@@ -61,6 +67,7 @@ struct TcArgs {
   int acc_stride;
   uint32_t tmem_cols;
   uint32_t a_box_bytes;
+  // epilogue
   const float* bias;
   const void* res;
   int res_f32;
@@ -73,9 +80,57 @@ struct TcArgs {
   int act;
   int vec_ok;
   int convt_kh, convt_kw, convt_oc, convt_H, convt_W;
+  // TMA store epilogue
+  int tma_out;          // 1: staging buffer + TMA stores; 0: per-thread stores (fallback)
+  int tma_res;          // 1: residual tile by TMA load into the staging buffer
+  int esz;              // output element bytes
+  int G;                // columns per store group
+  int ngroups;          // groups per tile
+  int swz;              // group rows are 128 B and 128B-swizzled
+  uint32_t group_bytes; // bytes of one group in the staging buffer
+  uint32_t sbuf_bytes;  // bytes of one staging buffer
+  int nsbuf;            // staging buffers (1 or 2)
+  uint32_t group_tx;    // bytes one residual group box delivers
   unsigned int* err;
 };
 
+// ------------------------------------------------------------------ TMA store / bulk-group helpers
+__device__ __forceinline__ void tma_store_2d(const CUtensorMap* map, uint32_t src, int c0, int c1) {
+  asm volatile("cp.async.bulk.tensor.2d.global.shared::cta.bulk_group [%0, {%2, %3}], [%1];" ::"l"(
+                   reinterpret_cast<uint64_t>(map)),
+               "r"(src), "r"(c0), "r"(c1)
+               : "memory");
+}
+__device__ __forceinline__ void tma_store_4d(const CUtensorMap* map, uint32_t src, int c0, int c1, int c2, int c3) {
+  asm volatile("cp.async.bulk.tensor.4d.global.shared::cta.bulk_group [%0, {%2, %3, %4, %5}], [%1];" ::"l"(
+                   reinterpret_cast<uint64_t>(map)),
+               "r"(src), "r"(c0), "r"(c1), "r"(c2), "r"(c3)
+               : "memory");
+}
+__device__ __forceinline__ void tma_store_5d(const CUtensorMap* map, uint32_t src, int c0, int c1, int c2, int c3,
+                                             int c4) {
+  asm volatile("cp.async.bulk.tensor.5d.global.shared::cta.bulk_group [%0, {%2, %3, %4, %5, %6}], [%1];" ::"l"(
+                   reinterpret_cast<uint64_t>(map)),
+               "r"(src), "r"(c0), "r"(c1), "r"(c2), "r"(c3), "r"(c4)
+               : "memory");
+}
+__device__ __forceinline__ void bulk_commit() { asm volatile("cp.async.bulk.commit_group;" ::: "memory"); }
+__device__ __forceinline__ void bulk_wait_read0() { asm volatile("cp.async.bulk.wait_group.read 0;" ::: "memory"); }
+__device__ __forceinline__ void bulk_wait_read1() { asm volatile("cp.async.bulk.wait_group.read 1;" ::: "memory"); }
+__device__ __forceinline__ void bulk_wait_all() { asm volatile("cp.async.bulk.wait_group 0;" ::: "memory"); }
+__device__ __forceinline__ void fence_async_smem() { asm volatile("fence.proxy.async.shared::cta;" ::: "memory"); }
+// Rendezvous of the 128 epilogue threads through an mbarrier (count 128) instead of a named
+// barrier, so a warp that leaves on the abort path cannot strand the others: their wait is bounded.
+__device__ __forceinline__ bool epi_sync(uint32_t bar, uint32_t parity, unsigned int* err, volatile int* abort_flag) {
+  mbar_arrive(bar);
+  int ok = 0;
+  if ((threadIdx.x & 31) == 0) ok = mbar_wait(bar, parity, err, SDX_DEV_WAIT_ACC_FULL, abort_flag) ? 1 : 0;
+  ok = __shfl_sync(0xffffffffu, ok, 0);
+  __syncwarp();
+  return ok != 0;
+}
+
+// ------------------------------------------------------------------ per-thread fallback helpers
 __device__ __forceinline__ void load8_res(const TcArgs& a, int64_t off, float* r) {
   if (a.res_f32) {
     const float4* p = reinterpret_cast<const float4*>(static_cast<const float*>(a.res) + off);
@@ -122,8 +177,48 @@ __device__ __forceinline__ void out_coord(const TcArgs& a, int64_t row, int n, i
   }
 }
 
+// Staging-buffer byte address of (row r, tile column tc) -- tc a multiple of 8.
+__device__ __forceinline__ uint32_t stage_addr(const TcArgs& a, uint32_t sbuf, int r, int tc, int byte_in_8) {
+  const int g = tc / a.G, cg = tc - g * a.G;
+  const uint32_t base = sbuf + (uint32_t)g * a.group_bytes;
+  const int b = cg * a.esz + byte_in_8;
+  if (a.swz) return base + (uint32_t)r * 128u + ((uint32_t)(((b >> 4) ^ (r & 7)) << 4) | (uint32_t)(b & 15));
+  return base + (uint32_t)r * (uint32_t)(a.G * a.esz) + (uint32_t)b;
+}
+
+__device__ __forceinline__ void lds16(uint32_t addr, uint4& v) {
+  asm volatile("ld.shared.v4.u32 {%0, %1, %2, %3}, [%4];" : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w) : "r"(addr));
+}
+__device__ __forceinline__ void sts16(uint32_t addr, const uint4& v) {
+  asm volatile("st.shared.v4.u32 [%0], {%1, %2, %3, %4};" ::"r"(addr), "r"(v.x), "r"(v.y), "r"(v.z), "r"(v.w)
+               : "memory");
+}
+
+struct TileCoord {
+  int img, oy0, ox0, m0, n0;
+};
+
+// TMA store (or residual load) of column group g of a tile.
+__device__ __forceinline__ void group_copy(const TcArgs& a, const CUtensorMap* map, uint32_t src, int g,
+                                           const TileCoord& t, bool load, uint32_t bar) {
+  const int n = t.n0 + g * a.G;
+  if (a.convt_oc > 0) {
+    const int row = a.convt_kw * a.convt_oc;
+    const int dy = n / row, c = n - dy * row;
+    tma_store_5d(map, src, c, t.ox0, dy, t.oy0, t.img);
+  } else if (a.mode == TC_CONV) {
+    if (load) tma_load_4d(src, map, bar, a.out_ch_off + n, t.ox0, t.oy0, t.img);
+    else tma_store_4d(map, src, a.out_ch_off + n, t.ox0, t.oy0, t.img);
+  } else {
+    if (load) tma_load_2d(src, map, bar, a.out_ch_off + n, t.m0);
+    else tma_store_2d(map, src, a.out_ch_off + n, t.m0);
+  }
+}
+
 __global__ void __launch_bounds__(TC_THREADS, 1)
-    conv_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB, const TcArgs a) {
+    conv_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
+                   const __grid_constant__ CUtensorMap tmOut, const __grid_constant__ CUtensorMap tmRes,
+                   const TcArgs a) {
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   const int S = a.stages;
@@ -131,13 +226,16 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
   const uint32_t b_stage_bytes = 2 * b_half_bytes;
   uint8_t* sA = smem;
   uint8_t* sB = smem + (size_t)S * TC_A_STAGE_BYTES;
-  uint64_t* bars = reinterpret_cast<uint64_t*>(sB + (size_t)S * b_stage_bytes);
+  uint8_t* sStage = sB + (size_t)S * b_stage_bytes;
+  uint64_t* bars = reinterpret_cast<uint64_t*>(sStage + (size_t)a.nsbuf * a.sbuf_bytes);
   uint64_t* full = bars;
   uint64_t* empty = bars + S;
   uint64_t* accf = bars + 2 * S;
   uint64_t* acce = bars + 2 * S + 2;
   uint64_t* drain = bars + 2 * S + 4;
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 2 * S + 5);
+  uint64_t* resb = bars + 2 * S + 5;  // [2]
+  uint64_t* epib = bars + 2 * S + 7;  // [2] epilogue rendezvous: staging free, staging written
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 2 * S + 9);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -149,6 +247,8 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
     for (int i = 0; i < 2; i++) {
       mbar_init(smem_u32(&accf[i]), 1);
       mbar_init(smem_u32(&acce[i]), 128);
+      mbar_init(smem_u32(&resb[i]), 1);
+      mbar_init(smem_u32(&epib[i]), 128);
     }
     mbar_init(smem_u32(drain), 1);
     *abort_flag = 0;
@@ -157,6 +257,8 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
   if (warp == 0 && lane == 0) {
     tma_prefetch_desc(&tmA);
     tma_prefetch_desc(&tmB);
+    if (a.tma_out) tma_prefetch_desc(&tmOut);
+    if (a.tma_res) tma_prefetch_desc(&tmRes);
   }
   if (warp == 1) {
     tmem_alloc(smem_u32(tmem_slot), a.tmem_cols);
@@ -255,7 +357,9 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
     // epilogue: warp w reads TMEM lanes 32*(w%4) .. +31 (the lane quadrant it may access)
     const int q = warp & 3;
     const int row_in_tile = q * 32 + lane;
+    const bool elected = threadIdx.x == 64;
     uint32_t lt = 0;
+    uint32_t res_phase[2] = {0, 0};
     for (int tile = blockIdx.x; tile < total_tiles; tile += gridDim.x, lt++) {
       const uint32_t acc = lt & 1u, ar = lt >> 1;
       int ok = 0;
@@ -266,30 +370,136 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
       tc_fence_after();
 
       const int m_tile = tile / a.n_tiles, n_tile = tile - m_tile * a.n_tiles;
+      TileCoord tcd;
+      tcd.n0 = n_tile * a.BN;
+      tcd.img = 0;
+      tcd.oy0 = 0;
+      tcd.ox0 = 0;
+      tcd.m0 = m_tile * TC_BM;
       bool valid;
       int64_t pix;
       if (a.mode == TC_CONV) {
         const int per_img = a.tiles_h * a.tiles_w;
-        const int img = m_tile / per_img, r = m_tile - img * per_img;
+        tcd.img = m_tile / per_img;
+        const int r = m_tile - tcd.img * per_img;
+        tcd.oy0 = (r / a.tiles_w) * a.BH;
+        tcd.ox0 = (r % a.tiles_w) * a.BW;
         const int h = row_in_tile / a.BW, w = row_in_tile - h * a.BW;
-        const int oy = (r / a.tiles_w) * a.BH + h, ox = (r % a.tiles_w) * a.BW + w;
+        const int oy = tcd.oy0 + h, ox = tcd.ox0 + w;
         valid = row_in_tile < a.BH * a.BW && oy < a.OH && ox < a.OW;
-        pix = ((int64_t)img * a.OH + oy) * a.OW + ox;
+        pix = ((int64_t)tcd.img * a.OH + oy) * a.OW + ox;
       } else {
-        pix = (int64_t)m_tile * TC_BM + row_in_tile;
+        pix = (int64_t)tcd.m0 + row_in_tile;
         valid = pix < a.M;
+      }
+      // column groups of this tile that start inside the tensor (a group fully past N is skipped)
+      const int ng = a.convt_oc > 0 ? a.ngroups : min(a.ngroups, (a.N - tcd.n0 + a.G - 1) / max(a.G, 1));
+      const uint32_t sbi = lt % (uint32_t)a.nsbuf;
+      const uint32_t sb = smem_u32(sStage) + sbi * a.sbuf_bytes;
+      if (a.tma_out) {
+        // the staging buffer is free once the TMA store that last read it has finished reading
+        if (elected) {
+          if (a.nsbuf == 2) bulk_wait_read1();
+          else bulk_wait_read0();
+        }
+        if (!epi_sync(smem_u32(&epib[0]), lt & 1u, a.err, abort_flag)) break;
+        if (a.tma_res) {
+          const uint32_t rb = smem_u32(&resb[sbi]);
+          if (elected) {
+            mbar_arrive_expect_tx(rb, (uint32_t)ng * a.group_tx);
+            for (int g = 0; g < ng; g++) group_copy(a, &tmRes, sb + g * a.group_bytes, g, tcd, true, rb);
+          }
+          int rok = 0;
+          if (lane == 0) rok = mbar_wait(rb, res_phase[sbi], a.err, SDX_DEV_WAIT_FULL, abort_flag) ? 1 : 0;
+          res_phase[sbi] ^= 1u;
+          rok = __shfl_sync(0xffffffffu, rok, 0);
+          if (!rok) break;
+          __syncwarp();
+        }
       }
       const uint32_t tbase = tmem_base + ((uint32_t)(q * 32) << 16) + acc * (uint32_t)a.acc_stride;
       for (int c = 0; c < a.BN; c += 16) {
         float v[16];
         __syncwarp();
         tmem_ld_32x32b_x16(tbase + (uint32_t)c, v);
-        if (valid) {
+        if (c + 16 >= a.BN) {
+          // accumulator fully read: hand it back to the MMA warp before the stores
+          tc_fence_before();
+          mbar_arrive(smem_u32(&acce[acc]));
+        }
 #pragma unroll
         for (int g = 0; g < 2; g++) {
-          const int n = n_tile * a.BN + c + 8 * g;
-          if (n >= a.N) break;
+          const int tcol = c + 8 * g;
+          const int n = tcd.n0 + tcol;
           float* vg = v + 8 * g;
+          if (a.tma_out) {
+            // bias (ConvT: per output channel) -> + residual (staged) -> act -> staging buffer
+            if (a.bias) {
+              if (a.convt_oc > 0) {
+                for (int j = 0; j < 8; j++) vg[j] += __ldg(a.bias + (n + j) % a.convt_oc);
+              } else if (n + 8 <= a.N) {
+                const float4* bp = reinterpret_cast<const float4*>(a.bias + n);
+                float4 b0 = __ldg(bp), b1 = __ldg(bp + 1);
+                vg[0] += b0.x; vg[1] += b0.y; vg[2] += b0.z; vg[3] += b0.w;
+                vg[4] += b1.x; vg[5] += b1.y; vg[6] += b1.z; vg[7] += b1.w;
+              } else {
+                for (int j = 0; j < 8; j++)
+                  if (n + j < a.N) vg[j] += __ldg(a.bias + n + j);
+              }
+            }
+            if (a.esz == 2) {
+              const uint32_t ad = stage_addr(a, sb, row_in_tile, tcol, 0);
+              if (a.tma_res) {
+                uint4 u;
+                lds16(ad, u);
+                const __half2* h = reinterpret_cast<const __half2*>(&u);
+#pragma unroll
+                for (int i = 0; i < 4; i++) {
+                  float2 f = __half22float2(h[i]);
+                  vg[2 * i] += f.x;
+                  vg[2 * i + 1] += f.y;
+                }
+              } else if (a.res && valid && n + 8 <= a.N) {
+                float r8[8];
+                load8_res(a, pix * a.res_pix_stride + a.res_ch_off + n, r8);
+#pragma unroll
+                for (int j = 0; j < 8; j++) vg[j] += r8[j];
+              }
+              uint4 u;
+              __half2* h = reinterpret_cast<__half2*>(&u);
+#pragma unroll
+              for (int i = 0; i < 4; i++)
+                h[i] = __floats2half2_rn(act_apply(vg[2 * i], a.act), act_apply(vg[2 * i + 1], a.act));
+              sts16(ad, u);
+            } else {
+              const uint32_t a0 = stage_addr(a, sb, row_in_tile, tcol, 0);
+              const uint32_t a1 = stage_addr(a, sb, row_in_tile, tcol, 16);
+              if (a.tma_res) {
+                uint4 u0, u1;
+                lds16(a0, u0);
+                lds16(a1, u1);
+                vg[0] += __uint_as_float(u0.x); vg[1] += __uint_as_float(u0.y);
+                vg[2] += __uint_as_float(u0.z); vg[3] += __uint_as_float(u0.w);
+                vg[4] += __uint_as_float(u1.x); vg[5] += __uint_as_float(u1.y);
+                vg[6] += __uint_as_float(u1.z); vg[7] += __uint_as_float(u1.w);
+              } else if (a.res && valid && n + 8 <= a.N) {
+                float r8[8];
+                load8_res(a, pix * a.res_pix_stride + a.res_ch_off + n, r8);
+#pragma unroll
+                for (int j = 0; j < 8; j++) vg[j] += r8[j];
+              }
+              uint4 u0, u1;
+              u0.x = __float_as_uint(act_apply(vg[0], a.act)); u0.y = __float_as_uint(act_apply(vg[1], a.act));
+              u0.z = __float_as_uint(act_apply(vg[2], a.act)); u0.w = __float_as_uint(act_apply(vg[3], a.act));
+              u1.x = __float_as_uint(act_apply(vg[4], a.act)); u1.y = __float_as_uint(act_apply(vg[5], a.act));
+              u1.z = __float_as_uint(act_apply(vg[6], a.act)); u1.w = __float_as_uint(act_apply(vg[7], a.act));
+              sts16(a0, u0);
+              sts16(a1, u1);
+            }
+            continue;
+          }
+          // ---- fallback: per-thread global stores
+          if (!valid || n >= a.N) continue;
           int64_t opix;
           int och;
           out_coord(a, pix, n, opix, och);
@@ -327,12 +537,19 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
             }
           }
         }
+      }
+      if (a.tma_out) {
+        // make the generic-proxy staging writes visible to the TMA engine, then store the tile
+        fence_async_smem();
+        if (!epi_sync(smem_u32(&epib[1]), lt & 1u, a.err, abort_flag)) break;
+        if (elected) {
+          for (int g = 0; g < ng; g++) group_copy(a, &tmOut, sb + g * a.group_bytes, g, tcd, false, 0);
+          bulk_commit();
         }
       }
       __syncwarp();
-      tc_fence_before();
-      mbar_arrive(smem_u32(&acce[acc]));
     }
+    if (elected && a.tma_out) bulk_wait_all();
   }
   __syncthreads();
   if (warp == 1) {
@@ -344,18 +561,31 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
 // ------------------------------------------------------------------------------------------
 // host side
 // ------------------------------------------------------------------------------------------
+// N tile: the whole N when it is at most 64 columns, else 128-column tiles.
 void tc_plan_n(int N, int* BN, int* n_tiles) {
-  int npad = (N + 15) / 16 * 16;
-  int nt = (npad + 255) / 256;
-  int bn = ((npad + nt - 1) / nt + 15) / 16 * 16;
-  *BN = bn;
-  *n_tiles = nt;
+  if (N <= 64) {
+    *BN = (N + 15) / 16 * 16;
+    *n_tiles = 1;
+  } else {
+    *BN = 128;
+    *n_tiles = (N + 127) / 128;
+  }
 }
 
-static int pick_stages(int BN) {
-  const int budget = 200 * 1024;
-  int per = (int)TC_A_STAGE_BYTES + 2 * BN * TC_BK * 2;
-  return std::max(2, std::min(TC_MAX_STAGES, budget / per));
+// ConvT columns (dy, dx, o), tap-major: one tile holds whole dy rows (kw*OC <= 64) or 128-column
+// pieces of one dy row.
+void tc_plan_n_convt(int kh, int kw, int OC, int* BN, int* n_tiles) {
+  const int N = kh * kw * OC;
+  const int row = kw * OC;
+  if (row <= 64 && N <= 256 && N % 16 == 0) {
+    *BN = N;
+    *n_tiles = 1;
+  } else if (row % 128 == 0) {
+    *BN = 128;
+    *n_tiles = N / 128;
+  } else {
+    tc_plan_n(N, BN, n_tiles);
+  }
 }
 
 static uint32_t pow2_cols(int cols) {
@@ -385,26 +615,33 @@ static void pick_pixel_tile(int OH, int OW, int* BH, int* BW) {
 }
 
 static int encode_map(CUtensorMap* map, const void* base, int rank, const uint64_t* dims, const uint64_t* strides_bytes,
-                      const uint32_t* box) {
+                      const uint32_t* box, CUtensorMapDataType dt = CU_TENSOR_MAP_DATA_TYPE_FLOAT16,
+                      CUtensorMapSwizzle swz = CU_TENSOR_MAP_SWIZZLE_128B) {
   PFN_encodeTiled enc = get_encode_tiled();
   if (!enc) return set_error(SDX_ERR_CUDA, "cuTensorMapEncodeTiled entry point unavailable");
   uint32_t estr[5] = {1, 1, 1, 1, 1};
-  CUresult r = enc(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, (cuuint32_t)rank, const_cast<void*>(base),
-                   reinterpret_cast<const cuuint64_t*>(dims), reinterpret_cast<const cuuint64_t*>(strides_bytes),
-                   reinterpret_cast<const cuuint32_t*>(box), reinterpret_cast<const cuuint32_t*>(estr),
-                   CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
-                   CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  CUresult r = enc(map, dt, (cuuint32_t)rank, const_cast<void*>(base), reinterpret_cast<const cuuint64_t*>(dims),
+                   reinterpret_cast<const cuuint64_t*>(strides_bytes), reinterpret_cast<const cuuint32_t*>(box),
+                   reinterpret_cast<const cuuint32_t*>(estr), CU_TENSOR_MAP_INTERLEAVE_NONE, swz,
+                   CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
   if (r != CUDA_SUCCESS) return set_error(SDX_ERR_INVALID, "cuTensorMapEncodeTiled failed (%d)", (int)r);
   return SDX_OK;
 }
 
 static bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
 
+static size_t smem_bytes(const TcArgs& a) {
+  return 1024 + (size_t)a.stages * (TC_A_STAGE_BYTES + 2 * (size_t)a.BN * TC_BK * 2) + (size_t)a.nsbuf * a.sbuf_bytes +
+         8 * (2 * a.stages + 9) + 16;
+}
+
 int tc_launch(const TcProblem& p, cudaStream_t stream) {
   if (p.N <= 0 || p.K <= 0) return set_error(SDX_ERR_INVALID, "tc: empty problem");
   if (!aligned16(p.a) || !aligned16(p.w)) return set_error(SDX_ERR_INVALID, "tc: operands must be 16-byte aligned");
+  const bool convt = p.convt_oc > 0;
   int BN, n_tiles;
-  tc_plan_n(p.N, &BN, &n_tiles);
+  if (convt) tc_plan_n_convt(p.convt_kh, p.convt_kw, p.convt_oc, &BN, &n_tiles);
+  else tc_plan_n(p.N, &BN, &n_tiles);
   const int kpad = (p.K + TC_BK - 1) / TC_BK * TC_BK;
   TcArgs a;
   memset(&a, 0, sizeof(a));
@@ -418,7 +655,6 @@ int tc_launch(const TcProblem& p, cudaStream_t stream) {
   a.pad_t = p.pad_t;
   a.pad_l = p.pad_l;
   a.b_rows_per_tap = BN * n_tiles;
-  a.stages = pick_stages(BN);
   a.acc_stride = BN;
   a.tmem_cols = pow2_cols(2 * BN);
   a.bias = p.bias;
@@ -437,17 +673,17 @@ int tc_launch(const TcProblem& p, cudaStream_t stream) {
   a.convt_oc = p.convt_oc;
   a.convt_H = p.convt_H;
   a.convt_W = p.convt_W;
-  const int esz = p.out_f32 ? 4 : 2;
-  const int rsz = p.res_f32 ? 4 : 2;
+  a.esz = p.out_f32 ? 4 : 2;
   bool vec = (p.out_pix_stride % 8 == 0) && (p.out_ch_off % 8 == 0) && aligned16(p.out) && (p.N % 8 == 0);
-  if (p.convt_oc > 0) vec = vec && p.convt_oc % 8 == 0;
+  if (convt) vec = vec && p.convt_oc % 8 == 0;
   if (p.res) vec = vec && (p.res_pix_stride % 8 == 0) && (p.res_ch_off % 8 == 0) && aligned16(p.res);
   if (p.bias) vec = vec && aligned16(p.bias);
-  (void)esz;
-  (void)rsz;
   a.vec_ok = vec ? 1 : 0;
 
-  CUtensorMap mA, mB;
+  // ---- A operand and tile geometry
+  CUtensorMap mA, mB, mOut, mRes;
+  memset(&mOut, 0, sizeof(mOut));
+  memset(&mRes, 0, sizeof(mRes));
   if (p.mode == TC_CONV) {
     if (p.C % 8 != 0) return set_error(SDX_ERR_INVALID, "tc conv: input channels must be a multiple of 8");
     int BH, BW;
@@ -483,27 +719,113 @@ int tc_launch(const TcProblem& p, cudaStream_t stream) {
     int rc = encode_map(&mB, p.w, 2, dims, strides, box);
     if (rc) return rc;
   }
+
+  // ---- epilogue: TMA store groups
+  const int esz = a.esz;
+  const int cw = 128 / esz;  // columns in one 128-byte swizzled row
+  int G;
+  if (convt) {
+    const int row = p.convt_kw * p.convt_oc;
+    G = std::min(cw, row);
+    if (row % G != 0 || BN % G != 0) G = 0;
+  } else {
+    G = BN * esz >= 128 ? cw : BN;
+    if (BN % G != 0) G = 0;
+  }
+  bool tma_out = G > 0 && (G * esz) % 16 == 0 && aligned16(p.out) && (p.out_pix_stride * esz) % 16 == 0 &&
+                 (p.out_ch_off * esz) % 16 == 0;
+  if (convt) tma_out = tma_out && p.mode == TC_CONV;
+  const int box_rows = p.mode == TC_CONV ? a.BH * a.BW : TC_BM;
+  if (tma_out) {
+    a.G = G;
+    a.ngroups = BN / G;
+    a.swz = (G * esz == 128) ? 1 : 0;
+    a.group_bytes = (uint32_t)(TC_BM * G * esz);
+    a.sbuf_bytes = (a.group_bytes * a.ngroups + 1023u) & ~1023u;
+    const CUtensorMapDataType dt = p.out_f32 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT32 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16;
+    const CUtensorMapSwizzle sw = a.swz ? CU_TENSOR_MAP_SWIZZLE_128B : CU_TENSOR_MAP_SWIZZLE_NONE;
+    int rc;
+    if (convt) {
+      const uint64_t row = (uint64_t)p.convt_kw * p.convt_oc;
+      uint64_t dims[5] = {row, (uint64_t)p.convt_W, (uint64_t)p.convt_kh, (uint64_t)p.convt_H, (uint64_t)p.batch};
+      uint64_t strides[4] = {row * esz, row * p.convt_W * esz, row * p.convt_W * p.convt_kh * esz,
+                             row * p.convt_W * p.convt_kh * p.convt_H * esz};
+      uint32_t box[5] = {(uint32_t)G, (uint32_t)a.BW, 1, (uint32_t)a.BH, 1};
+      rc = encode_map(&mOut, p.out, 5, dims, strides, box, dt, sw);
+    } else if (p.mode == TC_CONV) {
+      const uint64_t ps = (uint64_t)p.out_pix_stride;
+      uint64_t dims[4] = {(uint64_t)(p.out_ch_off + p.N), (uint64_t)p.OW, (uint64_t)p.OH, (uint64_t)p.batch};
+      uint64_t strides[3] = {ps * esz, ps * p.OW * esz, ps * p.OW * p.OH * esz};
+      uint32_t box[4] = {(uint32_t)G, (uint32_t)a.BW, (uint32_t)a.BH, 1};
+      rc = encode_map(&mOut, p.out, 4, dims, strides, box, dt, sw);
+    } else {
+      uint64_t dims[2] = {(uint64_t)(p.out_ch_off + p.N), (uint64_t)p.M};
+      uint64_t strides[1] = {(uint64_t)p.out_pix_stride * esz};
+      uint32_t box[2] = {(uint32_t)G, TC_BM};
+      rc = encode_map(&mOut, p.out, 2, dims, strides, box, dt, sw);
+    }
+    if (rc) return rc;
+    // residual by TMA when it has the output's type, layout and channel geometry
+    if (p.res && !convt && p.res_f32 == p.out_f32 && p.res_pix_stride == p.out_pix_stride &&
+        p.res_ch_off == p.out_ch_off && aligned16(p.res)) {
+      if (p.mode == TC_CONV) {
+        const uint64_t ps = (uint64_t)p.res_pix_stride;
+        uint64_t dims[4] = {(uint64_t)(p.res_ch_off + p.N), (uint64_t)p.OW, (uint64_t)p.OH, (uint64_t)p.batch};
+        uint64_t strides[3] = {ps * esz, ps * p.OW * esz, ps * p.OW * p.OH * esz};
+        uint32_t box[4] = {(uint32_t)G, (uint32_t)a.BW, (uint32_t)a.BH, 1};
+        rc = encode_map(&mRes, p.res, 4, dims, strides, box, dt, sw);
+      } else {
+        uint64_t dims[2] = {(uint64_t)(p.res_ch_off + p.N), (uint64_t)p.M};
+        uint64_t strides[1] = {(uint64_t)p.res_pix_stride * esz};
+        uint32_t box[2] = {(uint32_t)G, TC_BM};
+        rc = encode_map(&mRes, p.res, 2, dims, strides, box, dt, sw);
+      }
+      if (rc) return rc;
+      a.tma_res = 1;
+      a.group_tx = (uint32_t)(G * esz * box_rows);
+    }
+    a.tma_out = 1;
+  } else if (convt && p.mode == TC_CONV) {
+    return set_error(SDX_ERR_NOT_SUPPORTED, "tc convt: channel geometry has no TMA store layout");
+  }
+
+  // ---- pipeline depth from the shared-memory budget (2 staging buffers when they fit)
+  a.nsbuf = a.tma_out ? 2 : 1;
+  if (!a.tma_out) a.sbuf_bytes = 0;
+  for (;;) {
+    const size_t fixed = 1024 + (size_t)a.nsbuf * a.sbuf_bytes + 8 * (2 * TC_MAX_STAGES + 9) + 16;
+    const size_t per = TC_A_STAGE_BYTES + 2 * (size_t)BN * TC_BK * 2;
+    const size_t room = fixed < (size_t)TC_SMEM_LIMIT ? (size_t)TC_SMEM_LIMIT - fixed : 0;
+    const int st = (int)std::min<size_t>(TC_MAX_STAGES, room / per);
+    if (st >= 2 || a.nsbuf <= 1) {
+      a.stages = std::max(2, st);
+      break;
+    }
+    a.nsbuf = 1;
+  }
+  const size_t smem = smem_bytes(a);
+  if (smem > (size_t)TC_SMEM_LIMIT) return set_error(SDX_ERR_NOT_SUPPORTED, "tc: shared memory plan too large");
+
   const int total = a.m_tiles * a.n_tiles;
   if (total == 0) return SDX_OK;
-  const size_t smem = 1024 + (size_t)a.stages * (TC_A_STAGE_BYTES + 2 * (size_t)BN * TC_BK * 2) + 8 * (2 * a.stages + 5) + 16;
   static bool attr_set[64] = {false};
   int dev = 0;
   cudaGetDevice(&dev);
   if (dev < 64 && !attr_set[dev]) {
-    cudaError_t e = cudaFuncSetAttribute(conv_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, 227 * 1024);
+    cudaError_t e = cudaFuncSetAttribute(conv_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, TC_SMEM_LIMIT);
     if (e != cudaSuccess) return set_cuda_error(e, "cudaFuncSetAttribute(conv_tc)");
     attr_set[dev] = true;
   }
   const int grid = std::min(total, num_sms(dev));
-  conv_tc_kernel<<<grid, TC_THREADS, smem, stream>>>(mA, mB, a);
+  conv_tc_kernel<<<grid, TC_THREADS, smem, stream>>>(mA, mB, mOut, mRes, a);
   cudaError_t e = cudaGetLastError();
   if (e != cudaSuccess) return set_cuda_error(e, "conv_tc launch");
   count_launch();
   return SDX_OK;
 }
 
-// Packs ONNX conv weights w [OC][IC][KH][KW] (fp32) into the B operand [taps][n_tiles*BN][ICpad]
-// fp16, zero padded; ConvT weights [IC][OC][KH][KW] pack as one tap whose rows are tap*OC + o.
+// Packs ONNX conv weights w [OC][IC][KH][KW] (fp32) into the B operand [2][taps][n_tiles*BN][ICpad]
+// fp16 (hi terms, then lo terms), zero padded.
 size_t tc_weights_halves(int N, int K, int taps) {
   int BN, nt;
   tc_plan_n(N, &BN, &nt);
@@ -511,7 +833,14 @@ size_t tc_weights_halves(int N, int K, int taps) {
   return 2 * (size_t)taps * BN * nt * kpad;
 }
 
-// hi = fp16(w) at `hi`, lo = fp16(w - hi) at `hi + lo_off`
+size_t tc_convt_weights_halves(int IC, int OC, int KH, int KW) {
+  int BN, nt;
+  tc_plan_n_convt(KH, KW, OC, &BN, &nt);
+  size_t kpad = (size_t)(IC + TC_BK - 1) / TC_BK * TC_BK;
+  return 2 * (size_t)BN * nt * kpad;
+}
+
+// hi = fp16(w) at `idx`, lo = fp16(w - hi) at `idx + lo_off`
 static inline void put2(__half* out, size_t idx, size_t lo_off, float w) {
   const __half h = __float2half_rn(w);
   out[idx] = h;
@@ -530,10 +859,11 @@ void tc_pack_conv(const float* w, int OC, int IC, int KH, int KW, __half* out) {
       for (int t = 0; t < taps; t++) put2(out, ((size_t)t * rows + o) * kpad + c, lo, w[((size_t)o * IC + c) * taps + t]);
 }
 
+// ConvT weights [IC][OC][KH][KW] -> one GEMM panel whose row tap*OC + o is w[:, o, tap].
 void tc_pack_convt(const float* w, int IC, int OC, int KH, int KW, __half* out) {
-  const int taps = KH * KW, N = taps * OC;
+  const int taps = KH * KW;
   int BN, nt;
-  tc_plan_n(N, &BN, &nt);
+  tc_plan_n_convt(KH, KW, OC, &BN, &nt);
   const size_t rows = (size_t)BN * nt, kpad = (size_t)(IC + TC_BK - 1) / TC_BK * TC_BK;
   const size_t lo = rows * kpad;
   memset(out, 0, sizeof(__half) * 2 * lo);

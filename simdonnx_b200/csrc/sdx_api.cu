@@ -452,7 +452,7 @@ int sdx_pack_conv(const sdx_conv_desc* d, const float* w, void* out, size_t* byt
 
 int sdx_pack_convt(int ic, int oc, int kh, int kw, const float* w, void* out, size_t* bytes) {
   if (!bytes) return set_error(SDX_ERR_INVALID, "null argument");
-  size_t need = oc >= 8 ? tc_weights_halves(kh * kw * oc, ic, 1) * sizeof(__half) : sizeof(float) * (size_t)ic * oc * kh * kw;
+  size_t need = oc >= 8 ? tc_convt_weights_halves(ic, oc, kh, kw) * sizeof(__half) : sizeof(float) * (size_t)ic * oc * kh * kw;
   if (!out) {
     *bytes = need;
     return SDX_OK;
@@ -595,13 +595,24 @@ int sdx_convt(sdx_ctx* ctx, const sdx_convt_desc* d, sdx_stream s) {
   if (!d) return set_error(SDX_ERR_INVALID, "null desc");
   LAUNCH_GUARD();
   if (d->oc >= 8) {
+    // a 1x1 implicit GEMM over the input pixels whose epilogue stores each tap's columns as output
+    // boxes (see conv_tc.cu)
+    if (d->ic % 8 != 0) return set_error(SDX_ERR_NOT_SUPPORTED, "convt: ic must be a multiple of 8");
     TcProblem p;
     memset(&p, 0, sizeof(p));
-    p.mode = TC_ROWS;
+    p.mode = TC_CONV;
     p.a = P<const __half>(d->x);
     p.lda = d->ic;
     p.M = d->batch * d->ih * d->iw;
     p.K = d->ic;
+    p.batch = d->batch;
+    p.H = d->ih;
+    p.W = d->iw;
+    p.C = d->ic;
+    p.OH = d->ih;
+    p.OW = d->iw;
+    p.kh = 1;
+    p.kw = 1;
     p.w = P<const __half>(d->w);
     p.N = d->kh * d->kw * d->oc;
     p.bias = P<const float>(d->bias);

@@ -4,7 +4,8 @@ GB/s and TFLOP/s against the algorithmic work. Small enough to run under ncu.
 
     python -m simdonnx_b200.kernel_bench --op pw --batch 64 --hw 80 --cin 64 --cout 128 --iters 20
 ops: pw (1x1 conv, tensor cores), conv3 (3x3 s1, tensor cores), dw (depthwise), stem (3x3 s2 from
-fp32 NCHW), convt (2x2 s2 ConvTranspose), gate (squeeze-excitation gate)
+fp32 NCHW), convt (2x2 s2 ConvTranspose), gate (squeeze-excitation gate), copy (torch copy, the
+HBM reference point)
 """
 from __future__ import annotations
 
@@ -77,6 +78,12 @@ def main():
         b1, b2 = torch.zeros(r, device=dev), torch.zeros(ci, device=dev)
         run = lambda: B.channel_gate(be, x, w1, b1, w2, b2)
         byts = x.numel() * 2
+        shape = dict(n=n, h=hw, w=hw, c=ci)
+    elif a.op == "copy":
+        x = torch.randn((n, hw, hw, ci), device=dev).half()
+        y = torch.empty_like(x)
+        run = lambda: y.copy_(x)
+        byts = 2 * x.numel() * 2
         shape = dict(n=n, h=hw, w=hw, c=ci)
     else:
         raise SystemExit(f"unknown op {a.op}")
