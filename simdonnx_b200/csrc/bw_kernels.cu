@@ -44,6 +44,7 @@ __device__ __forceinline__ uint4 f_to_h8(const float* f) {
 // ------------------------------------------------------------------ depthwise
 // Nhwc.Depthwise (src/Kernels/Nhwc.cs:496-631): y[c] = act(b[c] + sum_tap w[tap,c] * x[tap,c] [+ add]);
 // out-of-range taps read the constant 0 pad. Thread = one output pixel x 8 channels.
+template <int ACT>
 __global__ void depthwise_kernel(DwArgs a) {
   const int cg = a.c >> 3;
   const int64_t total = (int64_t)a.batch * a.oh * a.ow * cg;
@@ -99,7 +100,7 @@ __global__ void depthwise_kernel(DwArgs a) {
       for (int j = 0; j < 8; j++) acc[j] += r[j];
     }
 #pragma unroll
-    for (int j = 0; j < 8; j++) acc[j] = act_apply(acc[j], a.act);
+    for (int j = 0; j < 8; j++) acc[j] = act_t<ACT>(acc[j]);
     *reinterpret_cast<uint4*>(a.y + o) = f_to_h8(acc);
   }
 }
@@ -108,7 +109,7 @@ int depthwise_launch(const DwArgs& a, cudaStream_t st) {
   if (a.c % 8 != 0) return set_error(SDX_ERR_NOT_SUPPORTED, "depthwise: channels must be a multiple of 8");
   const int64_t total = (int64_t)a.batch * a.oh * a.ow * (a.c / 8);
   if (total == 0) return SDX_OK;
-  depthwise_kernel<<<grid_for(total, 256), 256, 0, st>>>(a);
+  SDX_ACT_DISPATCH(a.act, ACTC, depthwise_kernel<ACTC><<<grid_for(total, 256), 256, 0, st>>>(a));
   SDX_LAUNCH_CHECK("depthwise");
   return SDX_OK;
 }
@@ -122,6 +123,7 @@ __device__ __forceinline__ float load_x(const DirectArgs& a, int n, int c, int i
   return a.x_f32 ? __ldg(static_cast<const float*>(a.x) + off) : __half2float(static_cast<const __half*>(a.x)[off]);
 }
 
+template <int ACT>
 __global__ void direct_conv_kernel(DirectArgs a) {
   extern __shared__ float sw[];
   const int wn = a.kh * a.kw * a.ic * a.oc;
@@ -168,7 +170,7 @@ __global__ void direct_conv_kernel(DirectArgs a) {
                                 : (((int64_t)n * a.oh + oy) * a.ow + ox) * a.oc + o;
         v += a.add_f32 ? static_cast<const float*>(a.add)[ao] : __half2float(static_cast<const __half*>(a.add)[ao]);
       }
-      v = act_apply(v, a.act);
+      v = act_t<ACT>(v);
       int64_t yo = a.y_nchw ? (((int64_t)n * a.oc + o) * a.oh + oy) * a.ow + ox
                             : (((int64_t)n * a.oh + oy) * a.ow + ox) * a.y_pix_stride + a.y_ch_off + o;
       if (a.y_f32) static_cast<float*>(a.y)[yo] = v;
@@ -182,18 +184,21 @@ int direct_conv_launch(const DirectArgs& a, cudaStream_t st) {
   if (wbytes > 96 * 1024) return set_error(SDX_ERR_NOT_SUPPORTED, "direct conv: weights exceed the smem stage");
   const int64_t total = (int64_t)a.batch * a.oh * a.ow * ((a.oc + 7) / 8);
   if (total == 0) return SDX_OK;
-  static bool attr = false;
-  if (!attr) {
-    cudaFuncSetAttribute(direct_conv_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, 96 * 1024);
-    attr = true;
-  }
-  direct_conv_kernel<<<grid_for(total, 256), 256, wbytes, st>>>(a);
+  SDX_ACT_DISPATCH(a.act, ACTC, {
+    static bool attr = false;
+    if (!attr) {
+      cudaFuncSetAttribute(direct_conv_kernel<ACTC>, cudaFuncAttributeMaxDynamicSharedMemorySize, 96 * 1024);
+      attr = true;
+    }
+    direct_conv_kernel<ACTC><<<grid_for(total, 256), 256, wbytes, st>>>(a);
+  });
   SDX_LAUNCH_CHECK("direct_conv");
   return SDX_OK;
 }
 
 // ------------------------------------------------------------------ ConvT, oc < 8 (dot path)
 // ConvTDot (src/Kernels/Nhwc.Det.cs:96-131): per output element one dot product over ic + bias, act.
+template <int ACT>
 __global__ void convt_dot_kernel(ConvtDotArgs a) {
   const int taps = a.kh * a.kw;
   const int64_t total = (int64_t)a.batch * a.ih * a.iw;
@@ -216,7 +221,7 @@ __global__ void convt_dot_kernel(ConvtDotArgs a) {
 #pragma unroll
           for (int j = 0; j < 8; j++) s = fmaf(xv[j], __ldg(a.w + ((int64_t)(c + j) * a.oc + o) * taps + tap), s);
         }
-        s = act_apply(s, a.act);
+        s = act_t<ACT>(s);
         if (a.y_f32) static_cast<float*>(a.y)[op * a.oc + o] = s;
         else static_cast<__half*>(a.y)[op * a.oc + o] = __float2half_rn(s);
       }
@@ -228,7 +233,7 @@ int convt_dot_launch(const ConvtDotArgs& a, cudaStream_t st) {
   if (a.ic % 8 != 0) return set_error(SDX_ERR_NOT_SUPPORTED, "convt dot: ic must be a multiple of 8");
   const int64_t total = (int64_t)a.batch * a.ih * a.iw;
   if (total == 0) return SDX_OK;
-  convt_dot_kernel<<<grid_for(total, 256), 256, 0, st>>>(a);
+  SDX_ACT_DISPATCH(a.act, ACTC, convt_dot_kernel<ACTC><<<grid_for(total, 256), 256, 0, st>>>(a));
   SDX_LAUNCH_CHECK("convt_dot");
   return SDX_OK;
 }
@@ -513,12 +518,13 @@ int binary_launch(int64_t n, int op, int relu, const __half* a, const __half* b,
   return SDX_OK;
 }
 
-__global__ void act_kernel(int64_t n8, int act, const uint4* __restrict__ x, uint4* __restrict__ y) {
+template <int ACT>
+__global__ void act_kernel(int64_t n8, const uint4* __restrict__ x, uint4* __restrict__ y) {
   for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < n8; i += (int64_t)gridDim.x * blockDim.x) {
     float v[8];
     h8_to_f(__ldg(x + i), v);
 #pragma unroll
-    for (int j = 0; j < 8; j++) v[j] = act_apply(v[j], act);
+    for (int j = 0; j < 8; j++) v[j] = act_t<ACT>(v[j]);
     y[i] = f_to_h8(v);
   }
 }
@@ -526,8 +532,9 @@ __global__ void act_kernel(int64_t n8, int act, const uint4* __restrict__ x, uin
 int act_launch(int64_t n, int act, const __half* x, __half* y, cudaStream_t st) {
   if (n % 8) return set_error(SDX_ERR_NOT_SUPPORTED, "act: element count must be a multiple of 8");
   if (n == 0) return SDX_OK;
-  act_kernel<<<grid_for(n / 8, 256), 256, 0, st>>>(n / 8, act, reinterpret_cast<const uint4*>(x),
-                                                    reinterpret_cast<uint4*>(y));
+  SDX_ACT_DISPATCH(act, ACTC,
+                   act_kernel<ACTC><<<grid_for(n / 8, 256), 256, 0, st>>>(n / 8, reinterpret_cast<const uint4*>(x),
+                                                                          reinterpret_cast<uint4*>(y)));
   SDX_LAUNCH_CHECK("act");
   return SDX_OK;
 }

@@ -215,6 +215,7 @@ __device__ __forceinline__ void group_copy(const TcArgs& a, const CUtensorMap* m
   }
 }
 
+template <int ACT>
 __global__ void __launch_bounds__(TC_THREADS, 1)
     conv_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
                    const __grid_constant__ CUtensorMap tmOut, const __grid_constant__ CUtensorMap tmRes,
@@ -469,7 +470,7 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
               __half2* h = reinterpret_cast<__half2*>(&u);
 #pragma unroll
               for (int i = 0; i < 4; i++)
-                h[i] = __floats2half2_rn(act_apply(vg[2 * i], a.act), act_apply(vg[2 * i + 1], a.act));
+                h[i] = __floats2half2_rn(act_t<ACT>(vg[2 * i]), act_t<ACT>(vg[2 * i + 1]));
               sts16(ad, u);
             } else {
               const uint32_t a0 = stage_addr(a, sb, row_in_tile, tcol, 0);
@@ -489,10 +490,10 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
                 for (int j = 0; j < 8; j++) vg[j] += r8[j];
               }
               uint4 u0, u1;
-              u0.x = __float_as_uint(act_apply(vg[0], a.act)); u0.y = __float_as_uint(act_apply(vg[1], a.act));
-              u0.z = __float_as_uint(act_apply(vg[2], a.act)); u0.w = __float_as_uint(act_apply(vg[3], a.act));
-              u1.x = __float_as_uint(act_apply(vg[4], a.act)); u1.y = __float_as_uint(act_apply(vg[5], a.act));
-              u1.z = __float_as_uint(act_apply(vg[6], a.act)); u1.w = __float_as_uint(act_apply(vg[7], a.act));
+              u0.x = __float_as_uint(act_t<ACT>(vg[0])); u0.y = __float_as_uint(act_t<ACT>(vg[1]));
+              u0.z = __float_as_uint(act_t<ACT>(vg[2])); u0.w = __float_as_uint(act_t<ACT>(vg[3]));
+              u1.x = __float_as_uint(act_t<ACT>(vg[4])); u1.y = __float_as_uint(act_t<ACT>(vg[5]));
+              u1.z = __float_as_uint(act_t<ACT>(vg[6])); u1.w = __float_as_uint(act_t<ACT>(vg[7]));
               sts16(a0, u0);
               sts16(a1, u1);
             }
@@ -517,7 +518,7 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
               for (int j = 0; j < 8; j++) vg[j] += r8[j];
             }
 #pragma unroll
-            for (int j = 0; j < 8; j++) vg[j] = act_apply(vg[j], a.act);
+            for (int j = 0; j < 8; j++) vg[j] = act_t<ACT>(vg[j]);
             store8(a, opix * a.out_pix_stride + a.out_ch_off + och, vg);
           } else {
             for (int j = 0; j < 8 && n + j < a.N; j++) {
@@ -530,7 +531,7 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
                 const int64_t ro = op * a.res_pix_stride + a.res_ch_off + oc;
                 x += a.res_f32 ? static_cast<const float*>(a.res)[ro] : __half2float(static_cast<const __half*>(a.res)[ro]);
               }
-              x = act_apply(x, a.act);
+              x = act_t<ACT>(x);
               const int64_t oo = op * a.out_pix_stride + a.out_ch_off + oc;
               if (a.out_f32) static_cast<float*>(a.out)[oo] = x;
               else static_cast<__half*>(a.out)[oo] = __float2half_rn(x);
@@ -629,6 +630,21 @@ static int encode_map(CUtensorMap* map, const void* base, int rank, const uint64
 }
 
 static bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
+
+template <int ACT>
+static int launch_tc(int dev, int grid, size_t smem, cudaStream_t stream, const CUtensorMap& mA, const CUtensorMap& mB,
+                     const CUtensorMap& mOut, const CUtensorMap& mRes, const TcArgs& a) {
+  static bool attr_set[64] = {false};
+  if (dev >= 0 && dev < 64 && !attr_set[dev]) {
+    cudaError_t e = cudaFuncSetAttribute(conv_tc_kernel<ACT>, cudaFuncAttributeMaxDynamicSharedMemorySize, TC_SMEM_LIMIT);
+    if (e != cudaSuccess) return set_cuda_error(e, "cudaFuncSetAttribute(conv_tc)");
+    attr_set[dev] = true;
+  }
+  conv_tc_kernel<ACT><<<grid, TC_THREADS, smem, stream>>>(mA, mB, mOut, mRes, a);
+  cudaError_t e = cudaGetLastError();
+  if (e != cudaSuccess) return set_cuda_error(e, "conv_tc launch");
+  return SDX_OK;
+}
 
 static size_t smem_bytes(const TcArgs& a) {
   return 1024 + (size_t)a.stages * (TC_A_STAGE_BYTES + 2 * (size_t)a.BN * TC_BK * 2) + (size_t)a.nsbuf * a.sbuf_bytes +
@@ -808,18 +824,12 @@ int tc_launch(const TcProblem& p, cudaStream_t stream) {
 
   const int total = a.m_tiles * a.n_tiles;
   if (total == 0) return SDX_OK;
-  static bool attr_set[64] = {false};
   int dev = 0;
   cudaGetDevice(&dev);
-  if (dev < 64 && !attr_set[dev]) {
-    cudaError_t e = cudaFuncSetAttribute(conv_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, TC_SMEM_LIMIT);
-    if (e != cudaSuccess) return set_cuda_error(e, "cudaFuncSetAttribute(conv_tc)");
-    attr_set[dev] = true;
-  }
   const int grid = std::min(total, num_sms(dev));
-  conv_tc_kernel<<<grid, TC_THREADS, smem, stream>>>(mA, mB, mOut, mRes, a);
-  cudaError_t e = cudaGetLastError();
-  if (e != cudaSuccess) return set_cuda_error(e, "conv_tc launch");
+  int rc = SDX_OK;
+  SDX_ACT_DISPATCH(a.act, ACTC, rc = launch_tc<ACTC>(dev, grid, smem, stream, mA, mB, mOut, mRes, a));
+  if (rc) return rc;
   count_launch();
   return SDX_OK;
 }

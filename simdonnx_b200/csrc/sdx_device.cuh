@@ -21,6 +21,30 @@ namespace sdx {
 // ActivationKind of the reference plan (src/Engine/ExecPlan.cs:42).
 enum Act : int { ACT_NONE = 0, ACT_RELU = 1, ACT_SIGMOID = 2, ACT_GELU = 3, ACT_HARDSWISH = 4, ACT_SWISH = 5 };
 
+// Compile-time activation: each kernel is instantiated per activation, so its inner loops carry
+// only the one they apply (a runtime switch inlined per element bloats the loop past the
+// instruction cache and stalls on branch resolution).
+template <int ACT>
+__device__ __forceinline__ float act_t(float v) {
+  if constexpr (ACT == ACT_RELU) return fmaxf(v, 0.0f);
+  else if constexpr (ACT == ACT_SIGMOID) return 1.0f / (1.0f + expf(-v));
+  else if constexpr (ACT == ACT_GELU) return 0.5f * v * (1.0f + erff(v * 0.70710678118654752f));
+  else if constexpr (ACT == ACT_HARDSWISH) return v * fminf(fmaxf(fmaf(v, 1.0f / 6.0f, 0.5f), 0.0f), 1.0f);
+  else if constexpr (ACT == ACT_SWISH) return v / (1.0f + expf(-v));
+  else return v;
+}
+
+// Runtime dispatch of a kernel template over the activation kind.
+#define SDX_ACT_DISPATCH(act, ACTC, ...)                   \
+  switch (act) {                                          \
+    case ACT_RELU: { constexpr int ACTC = ACT_RELU; __VA_ARGS__; } break;           \
+    case ACT_SIGMOID: { constexpr int ACTC = ACT_SIGMOID; __VA_ARGS__; } break;     \
+    case ACT_GELU: { constexpr int ACTC = ACT_GELU; __VA_ARGS__; } break;           \
+    case ACT_HARDSWISH: { constexpr int ACTC = ACT_HARDSWISH; __VA_ARGS__; } break; \
+    case ACT_SWISH: { constexpr int ACTC = ACT_SWISH; __VA_ARGS__; } break;         \
+    default: { constexpr int ACTC = ACT_NONE; __VA_ARGS__; } break;                 \
+  }
+
 __device__ __forceinline__ float act_apply(float v, int act) {
   switch (act) {
     case ACT_RELU: return fmaxf(v, 0.0f);
