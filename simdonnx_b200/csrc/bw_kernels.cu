@@ -109,6 +109,10 @@ int depthwise_launch(const DwArgs& a, cudaStream_t st) {
   if (a.c % 8 != 0) return set_error(SDX_ERR_NOT_SUPPORTED, "depthwise: channels must be a multiple of 8");
   const int64_t total = (int64_t)a.batch * a.oh * a.ow * (a.c / 8);
   if (total == 0) return SDX_OK;
+  if (depthwise_tiled_launch(a, st)) {
+    SDX_LAUNCH_CHECK("depthwise_tiled");
+    return SDX_OK;
+  }
   SDX_ACT_DISPATCH(a.act, ACTC, depthwise_kernel<ACTC><<<grid_for(total, 256), 256, 0, st>>>(a));
   SDX_LAUNCH_CHECK("depthwise");
   return SDX_OK;
@@ -184,6 +188,10 @@ int direct_conv_launch(const DirectArgs& a, cudaStream_t st) {
   if (wbytes > 96 * 1024) return set_error(SDX_ERR_NOT_SUPPORTED, "direct conv: weights exceed the smem stage");
   const int64_t total = (int64_t)a.batch * a.oh * a.ow * ((a.oc + 7) / 8);
   if (total == 0) return SDX_OK;
+  if (stem_tiled_launch(a, st)) {
+    SDX_LAUNCH_CHECK("stem_tiled");
+    return SDX_OK;
+  }
   SDX_ACT_DISPATCH(a.act, ACTC, {
     static bool attr = false;
     if (!attr) {

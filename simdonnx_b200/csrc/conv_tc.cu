@@ -50,6 +50,8 @@ constexpr int TC_THREADS = 192;
 constexpr int TC_MAX_STAGES = 8;
 constexpr uint32_t TC_A_STAGE_BYTES = TC_BM * TC_BK * 2;  // 16 KB
 constexpr int TC_SMEM_LIMIT = 227 * 1024;
+constexpr int TC_MAX_BN = 128;
+constexpr int TC_BIAS_SMEM_MAX = 4096;  // bias floats staged in shared memory
 
 struct TcArgs {
   int mode;
@@ -91,6 +93,7 @@ struct TcArgs {
   uint32_t sbuf_bytes;  // bytes of one staging buffer
   int nsbuf;            // staging buffers (1 or 2)
   uint32_t group_tx;    // bytes one residual group box delivers
+  int bias_smem;        // bias floats staged in shared memory (per accumulator column), 0 = none
   unsigned int* err;
 };
 
@@ -228,7 +231,9 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
   uint8_t* sA = smem;
   uint8_t* sB = smem + (size_t)S * TC_A_STAGE_BYTES;
   uint8_t* sStage = sB + (size_t)S * b_stage_bytes;
-  uint64_t* bars = reinterpret_cast<uint64_t*>(sStage + (size_t)a.nsbuf * a.sbuf_bytes);
+  float* sBias = reinterpret_cast<float*>(sStage + (size_t)a.nsbuf * a.sbuf_bytes);
+  uint64_t* bars = reinterpret_cast<uint64_t*>(sStage + (size_t)a.nsbuf * a.sbuf_bytes +
+                                               (((size_t)a.bias_smem * 4 + 15) & ~(size_t)15));
   uint64_t* full = bars;
   uint64_t* empty = bars + S;
   uint64_t* accf = bars + 2 * S;
@@ -265,6 +270,9 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
     tmem_alloc(smem_u32(tmem_slot), a.tmem_cols);
     tmem_relinquish();
   }
+  // per-column bias in shared memory (ConvT: expanded over its taps), read as broadcasts
+  for (int i = threadIdx.x; i < a.bias_smem; i += blockDim.x)
+    sBias[i] = i < a.N ? __ldg(a.bias + (a.convt_oc > 0 ? i % a.convt_oc : i)) : 0.0f;
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
@@ -419,33 +427,43 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
         }
       }
       const uint32_t tbase = tmem_base + ((uint32_t)(q * 32) << 16) + acc * (uint32_t)a.acc_stride;
-      for (int c = 0; c < a.BN; c += 16) {
-        float v[16];
-        __syncwarp();
-        tmem_ld_32x32b_x16(tbase + (uint32_t)c, v);
-        if (c + 16 >= a.BN) {
-          // accumulator fully read: hand it back to the MMA warp before the stores
-          tc_fence_before();
-          mbar_arrive(smem_u32(&acce[acc]));
-        }
+      // the whole accumulator row at once: all TMEM loads in flight, one wait, then the accumulator
+      // goes back to the MMA warp before any of the epilogue math
+      float v[TC_MAX_BN];
+      const float* sbias = a.bias_smem ? sBias + tcd.n0 : nullptr;
+      __syncwarp();
 #pragma unroll
-        for (int g = 0; g < 2; g++) {
-          const int tcol = c + 8 * g;
+      for (int c = 0; c < TC_MAX_BN / 16; c++)
+        if (c * 16 < a.BN) tmem_ld16_issue(tbase + (uint32_t)(c * 16), v + c * 16);
+      tmem_wait_ld();
+#pragma unroll
+      for (int c = 0; c < TC_MAX_BN / 16; c++)
+        if (c * 16 < a.BN) tmem_ld_wait16(v + c * 16);
+      tc_fence_before();
+      mbar_arrive(smem_u32(&acce[acc]));
+#pragma unroll
+      for (int j = 0; j < TC_MAX_BN / 8; j++) {
+        const int tcol = j * 8;
+        if (tcol >= a.BN) break;
+        {
           const int n = tcd.n0 + tcol;
-          float* vg = v + 8 * g;
+          float* vg = v + tcol;
           if (a.tma_out) {
             // bias (ConvT: per output channel) -> + residual (staged) -> act -> staging buffer
             if (a.bias) {
-              if (a.convt_oc > 0) {
-                for (int j = 0; j < 8; j++) vg[j] += __ldg(a.bias + (n + j) % a.convt_oc);
+              if (sbias) {
+#pragma unroll
+                for (int q2 = 0; q2 < 8; q2++) vg[q2] += sbias[tcol + q2];
+              } else if (a.convt_oc > 0) {
+                for (int q2 = 0; q2 < 8; q2++) vg[q2] += __ldg(a.bias + (n + q2) % a.convt_oc);
               } else if (n + 8 <= a.N) {
                 const float4* bp = reinterpret_cast<const float4*>(a.bias + n);
                 float4 b0 = __ldg(bp), b1 = __ldg(bp + 1);
                 vg[0] += b0.x; vg[1] += b0.y; vg[2] += b0.z; vg[3] += b0.w;
                 vg[4] += b1.x; vg[5] += b1.y; vg[6] += b1.z; vg[7] += b1.w;
               } else {
-                for (int j = 0; j < 8; j++)
-                  if (n + j < a.N) vg[j] += __ldg(a.bias + n + j);
+                for (int q2 = 0; q2 < 8; q2++)
+                  if (n + q2 < a.N) vg[q2] += __ldg(a.bias + n + q2);
               }
             }
             if (a.esz == 2) {
@@ -648,7 +666,7 @@ static int launch_tc(int dev, int grid, size_t smem, cudaStream_t stream, const 
 
 static size_t smem_bytes(const TcArgs& a) {
   return 1024 + (size_t)a.stages * (TC_A_STAGE_BYTES + 2 * (size_t)a.BN * TC_BK * 2) + (size_t)a.nsbuf * a.sbuf_bytes +
-         8 * (2 * a.stages + 9) + 16;
+         (((size_t)a.bias_smem * 4 + 15) & ~(size_t)15) + 8 * (2 * a.stages + 9) + 16;
 }
 
 int tc_launch(const TcProblem& p, cudaStream_t stream) {
@@ -805,11 +823,13 @@ int tc_launch(const TcProblem& p, cudaStream_t stream) {
     return set_error(SDX_ERR_NOT_SUPPORTED, "tc convt: channel geometry has no TMA store layout");
   }
 
+  if (p.bias && BN * n_tiles <= TC_BIAS_SMEM_MAX) a.bias_smem = BN * n_tiles;
   // ---- pipeline depth from the shared-memory budget (2 staging buffers when they fit)
   a.nsbuf = a.tma_out ? 2 : 1;
   if (!a.tma_out) a.sbuf_bytes = 0;
   for (;;) {
-    const size_t fixed = 1024 + (size_t)a.nsbuf * a.sbuf_bytes + 8 * (2 * TC_MAX_STAGES + 9) + 16;
+    const size_t fixed = 1024 + (size_t)a.nsbuf * a.sbuf_bytes + (((size_t)a.bias_smem * 4 + 15) & ~(size_t)15) +
+                         8 * (2 * TC_MAX_STAGES + 9) + 16;
     const size_t per = TC_A_STAGE_BYTES + 2 * (size_t)BN * TC_BK * 2;
     const size_t room = fixed < (size_t)TC_SMEM_LIMIT ? (size_t)TC_SMEM_LIMIT - fixed : 0;
     const int st = (int)std::min<size_t>(TC_MAX_STAGES, room / per);

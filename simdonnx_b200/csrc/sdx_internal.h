@@ -79,6 +79,8 @@ struct DwArgs {
   __half* y;
 };
 int depthwise_launch(const DwArgs& a, cudaStream_t st);
+// smem-tiled variant (tiled_kernels.cu); false when the shape is not one it handles
+bool depthwise_tiled_launch(const DwArgs& a, cudaStream_t st);
 
 struct DirectArgs {
   int batch, ih, iw, ic, oh, ow, oc, kh, kw, sh, sw, pt, pl, act;
@@ -94,6 +96,7 @@ struct DirectArgs {
   int y_ch_off;
 };
 int direct_conv_launch(const DirectArgs& a, cudaStream_t st);
+bool stem_tiled_launch(const DirectArgs& a, cudaStream_t st);
 
 struct ConvtDotArgs {
   int batch, ih, iw, ic, oc, kh, kw, act, y_f32;
