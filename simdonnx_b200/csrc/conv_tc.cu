@@ -46,7 +46,8 @@ namespace sdx {
 
 constexpr int TC_BM = 128;
 constexpr int TC_BK = 64;  // halves per 128-byte swizzled row
-constexpr int TC_THREADS = 192;
+constexpr int TC_EPI_GROUPS = 2;                        // epilogue warp groups (one per accumulator)
+constexpr int TC_THREADS = 64 + 128 * TC_EPI_GROUPS;    // producer warp, MMA warp, epilogue groups
 constexpr int TC_MAX_STAGES = 8;
 constexpr uint32_t TC_A_STAGE_BYTES = TC_BM * TC_BK * 2;  // 16 KB
 constexpr int TC_SMEM_LIMIT = 227 * 1024;
@@ -91,7 +92,7 @@ struct TcArgs {
   int swz;              // group rows are 128 B and 128B-swizzled
   uint32_t group_bytes; // bytes of one group in the staging buffer
   uint32_t sbuf_bytes;  // bytes of one staging buffer
-  int nsbuf;            // staging buffers (1 or 2)
+  int nsbuf;            // staging buffers per epilogue group (1 or 2)
   uint32_t group_tx;    // bytes one residual group box delivers
   int bias_smem;        // bias floats staged in shared memory (per accumulator column), 0 = none
   unsigned int* err;
@@ -231,17 +232,17 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
   uint8_t* sA = smem;
   uint8_t* sB = smem + (size_t)S * TC_A_STAGE_BYTES;
   uint8_t* sStage = sB + (size_t)S * b_stage_bytes;
-  float* sBias = reinterpret_cast<float*>(sStage + (size_t)a.nsbuf * a.sbuf_bytes);
-  uint64_t* bars = reinterpret_cast<uint64_t*>(sStage + (size_t)a.nsbuf * a.sbuf_bytes +
+  float* sBias = reinterpret_cast<float*>(sStage + (size_t)TC_EPI_GROUPS * a.nsbuf * a.sbuf_bytes);
+  uint64_t* bars = reinterpret_cast<uint64_t*>(sStage + (size_t)TC_EPI_GROUPS * a.nsbuf * a.sbuf_bytes +
                                                (((size_t)a.bias_smem * 4 + 15) & ~(size_t)15));
   uint64_t* full = bars;
   uint64_t* empty = bars + S;
   uint64_t* accf = bars + 2 * S;
   uint64_t* acce = bars + 2 * S + 2;
   uint64_t* drain = bars + 2 * S + 4;
-  uint64_t* resb = bars + 2 * S + 5;  // [2]
-  uint64_t* epib = bars + 2 * S + 7;  // [2] epilogue rendezvous: staging free, staging written
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 2 * S + 9);
+  uint64_t* resb = bars + 2 * S + 5;  // [group][buffer]
+  uint64_t* epib = bars + 2 * S + 9;  // [group][2] epilogue rendezvous: staging free, staging written
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 2 * S + 13);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -253,6 +254,8 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
     for (int i = 0; i < 2; i++) {
       mbar_init(smem_u32(&accf[i]), 1);
       mbar_init(smem_u32(&acce[i]), 128);
+    }
+    for (int i = 0; i < 4; i++) {
       mbar_init(smem_u32(&resb[i]), 1);
       mbar_init(smem_u32(&epib[i]), 128);
     }
@@ -363,13 +366,16 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
     }
     __syncwarp();
   } else {
-    // epilogue: warp w reads TMEM lanes 32*(w%4) .. +31 (the lane quadrant it may access)
+    // epilogue: group e (warps 2+4e .. 5+4e) drains accumulator e, i.e. every other tile of this
+    // CTA; warp w reads TMEM lanes 32*(w%4) .. +31 (the lane quadrant it may access)
+    const int e = (warp - 2) >> 2;
     const int q = warp & 3;
     const int row_in_tile = q * 32 + lane;
-    const bool elected = threadIdx.x == 64;
-    uint32_t lt = 0;
+    const bool elected = threadIdx.x == 64 + 128 * e;
     uint32_t res_phase[2] = {0, 0};
-    for (int tile = blockIdx.x; tile < total_tiles; tile += gridDim.x, lt++) {
+    uint32_t lc = 0;  // this group's tile count
+    for (int tile = blockIdx.x + e * gridDim.x; tile < total_tiles; tile += 2 * gridDim.x, lc++) {
+      const uint32_t lt = 2 * lc + (uint32_t)e;
       const uint32_t acc = lt & 1u, ar = lt >> 1;
       int ok = 0;
       if (lane == 0) ok = mbar_wait(smem_u32(&accf[acc]), ar & 1u, a.err, SDX_DEV_WAIT_ACC_FULL, abort_flag) ? 1 : 0;
@@ -403,17 +409,17 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
       }
       // column groups of this tile that start inside the tensor (a group fully past N is skipped)
       const int ng = a.convt_oc > 0 ? a.ngroups : min(a.ngroups, (a.N - tcd.n0 + a.G - 1) / max(a.G, 1));
-      const uint32_t sbi = lt % (uint32_t)a.nsbuf;
-      const uint32_t sb = smem_u32(sStage) + sbi * a.sbuf_bytes;
+      const uint32_t sbi = lc % (uint32_t)a.nsbuf;
+      const uint32_t sb = smem_u32(sStage) + ((uint32_t)e * a.nsbuf + sbi) * a.sbuf_bytes;
       if (a.tma_out) {
         // the staging buffer is free once the TMA store that last read it has finished reading
         if (elected) {
           if (a.nsbuf == 2) bulk_wait_read1();
           else bulk_wait_read0();
         }
-        if (!epi_sync(smem_u32(&epib[0]), lt & 1u, a.err, abort_flag)) break;
+        if (!epi_sync(smem_u32(&epib[2 * e]), lc & 1u, a.err, abort_flag)) break;
         if (a.tma_res) {
-          const uint32_t rb = smem_u32(&resb[sbi]);
+          const uint32_t rb = smem_u32(&resb[2 * e + sbi]);
           if (elected) {
             mbar_arrive_expect_tx(rb, (uint32_t)ng * a.group_tx);
             for (int g = 0; g < ng; g++) group_copy(a, &tmRes, sb + g * a.group_bytes, g, tcd, true, rb);
@@ -560,7 +566,7 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
       if (a.tma_out) {
         // make the generic-proxy staging writes visible to the TMA engine, then store the tile
         fence_async_smem();
-        if (!epi_sync(smem_u32(&epib[1]), lt & 1u, a.err, abort_flag)) break;
+        if (!epi_sync(smem_u32(&epib[2 * e + 1]), lc & 1u, a.err, abort_flag)) break;
         if (elected) {
           for (int g = 0; g < ng; g++) group_copy(a, &tmOut, sb + g * a.group_bytes, g, tcd, false, 0);
           bulk_commit();
@@ -665,8 +671,9 @@ static int launch_tc(int dev, int grid, size_t smem, cudaStream_t stream, const 
 }
 
 static size_t smem_bytes(const TcArgs& a) {
-  return 1024 + (size_t)a.stages * (TC_A_STAGE_BYTES + 2 * (size_t)a.BN * TC_BK * 2) + (size_t)a.nsbuf * a.sbuf_bytes +
-         (((size_t)a.bias_smem * 4 + 15) & ~(size_t)15) + 8 * (2 * a.stages + 9) + 16;
+  return 1024 + (size_t)a.stages * (TC_A_STAGE_BYTES + 2 * (size_t)a.BN * TC_BK * 2) +
+         (size_t)TC_EPI_GROUPS * a.nsbuf * a.sbuf_bytes + (((size_t)a.bias_smem * 4 + 15) & ~(size_t)15) +
+         8 * (2 * a.stages + 13) + 16;
 }
 
 int tc_launch(const TcProblem& p, cudaStream_t stream) {
@@ -828,8 +835,8 @@ int tc_launch(const TcProblem& p, cudaStream_t stream) {
   a.nsbuf = a.tma_out ? 2 : 1;
   if (!a.tma_out) a.sbuf_bytes = 0;
   for (;;) {
-    const size_t fixed = 1024 + (size_t)a.nsbuf * a.sbuf_bytes + (((size_t)a.bias_smem * 4 + 15) & ~(size_t)15) +
-                         8 * (2 * TC_MAX_STAGES + 9) + 16;
+    const size_t fixed = 1024 + (size_t)TC_EPI_GROUPS * a.nsbuf * a.sbuf_bytes +
+                         (((size_t)a.bias_smem * 4 + 15) & ~(size_t)15) + 8 * (2 * TC_MAX_STAGES + 13) + 16;
     const size_t per = TC_A_STAGE_BYTES + 2 * (size_t)BN * TC_BK * 2;
     const size_t room = fixed < (size_t)TC_SMEM_LIMIT ? (size_t)TC_SMEM_LIMIT - fixed : 0;
     const int st = (int)std::min<size_t>(TC_MAX_STAGES, room / per);

@@ -17,15 +17,20 @@ namespace sdx {
 // ------------------------------------------------------------------ depthwise
 // y[n, oy, ox, c] = act(b[c] + sum_{ky,kx} w[ky,kx,c] * s[n,c] * x[n, oy*S+ky-pt, ox*S+kx-pl, c] [+ add])
 // (Nhwc.Depthwise, src/Kernels/Nhwc.cs:496-631; constant-0 padding). Block = TH x TW outputs of one
-// image for a slab of CS channels (CS/8 channel groups of 8); thread = one channel group of
-// several outputs. SC: the squeeze-excitation scale s is applied while staging (fp32 tile).
-template <int ACT, int K, int S, bool SC>
+// image for a slab of CS channels (G = CS/8 channel groups of 8). Thread = one channel group of a
+// strip of R = 4 horizontally adjacent outputs: per kernel row it reads the strip's (R-1)*S+K input
+// vectors once and each tap's 8 weights once, and reuses them across the strip (register blocking).
+// The squeeze-excitation scale s[n, c] of the producer is folded into the staged weights
+// (sum w*(s*x) == sum (w*s)*x, one rounding either way).
+constexpr int DW_R = 4;
+
+template <int ACT, int K, int S>
 __global__ void __launch_bounds__(256) dw_tiled_kernel(DwArgs a, int CS, int TH, int TW, int tiles_x) {
   extern __shared__ float4 dsm_f4[];
   float* sw = reinterpret_cast<float*>(dsm_f4);
   const int G = CS >> 3;
   const int IWt = (TW - 1) * S + K, IHt = (TH - 1) * S + K;
-  uint8_t* stile = reinterpret_cast<uint8_t*>(sw + K * K * CS);
+  uint4* stile = reinterpret_cast<uint4*>(sw + K * K * CS);  // [IHt*IWt][G] x 8 halves
   const int n = blockIdx.z, c0 = blockIdx.y * CS;
   const int ty = blockIdx.x / tiles_x, tx = blockIdx.x - ty * tiles_x;
   const int oy0 = ty * TH, ox0 = tx * TW;
@@ -34,7 +39,9 @@ __global__ void __launch_bounds__(256) dw_tiled_kernel(DwArgs a, int CS, int TH,
 
   for (int i = tid; i < K * K * CS; i += blockDim.x) {
     const int tap = i / CS, c = i - tap * CS;
-    sw[i] = __ldg(a.w + (int64_t)tap * a.c + c0 + c);
+    float w = __ldg(a.w + (int64_t)tap * a.c + c0 + c);
+    if (a.in_scale) w *= __ldg(a.in_scale + (int64_t)n * a.c + c0 + c);
+    sw[i] = w;
   }
   const __half* xb = a.x + (int64_t)n * a.ih * a.iw * a.c + c0;
   for (int i = tid; i < IHt * IWt * G; i += blockDim.x) {
@@ -44,114 +51,102 @@ __global__ void __launch_bounds__(256) dw_tiled_kernel(DwArgs a, int CS, int TH,
     uint4 u = make_uint4(0, 0, 0, 0);
     if ((unsigned)iy < (unsigned)a.ih && (unsigned)ix < (unsigned)a.iw)
       u = __ldg(reinterpret_cast<const uint4*>(xb + ((int64_t)iy * a.iw + ix) * a.c + g * 8));
-    if constexpr (SC) {
-      const __half2* h = reinterpret_cast<const __half2*>(&u);
-      const float* sc = a.in_scale + (int64_t)n * a.c + c0 + g * 8;
-      float4 f0, f1;
-      float2 t;
-      t = __half22float2(h[0]); f0.x = t.x * __ldg(sc + 0); f0.y = t.y * __ldg(sc + 1);
-      t = __half22float2(h[1]); f0.z = t.x * __ldg(sc + 2); f0.w = t.y * __ldg(sc + 3);
-      t = __half22float2(h[2]); f1.x = t.x * __ldg(sc + 4); f1.y = t.y * __ldg(sc + 5);
-      t = __half22float2(h[3]); f1.z = t.x * __ldg(sc + 6); f1.w = t.y * __ldg(sc + 7);
-      float4* dst = reinterpret_cast<float4*>(stile) + ((int64_t)p * CS + g * 8) / 4;
-      dst[0] = f0;
-      dst[1] = f1;
-    } else {
-      reinterpret_cast<uint4*>(stile)[((int64_t)p * CS + g * 8) / 8] = u;
-    }
+    stile[i] = u;
   }
   __syncthreads();
 
-  const int cg = tid % G, pl = tid / G, lanes = blockDim.x / G;
+  const int cg = tid % G, strip = tid / G;
+  const int spr = TW / DW_R;
+  const int sy = strip / spr, sx = strip - sy * spr;
+  if (sy >= TH) return;
+  const int oy = oy0 + sy;
+  if (oy >= a.oh) return;
   const int c = c0 + cg * 8;
-  float bias[8];
+  float acc[DW_R][8];
   {
     const float4* bp = reinterpret_cast<const float4*>(a.bias + c);
     float4 b0 = __ldg(bp), b1 = __ldg(bp + 1);
-    bias[0] = b0.x; bias[1] = b0.y; bias[2] = b0.z; bias[3] = b0.w;
-    bias[4] = b1.x; bias[5] = b1.y; bias[6] = b1.z; bias[7] = b1.w;
-  }
-  const float* swc = sw + cg * 8;
-  for (int o = pl; o < TH * TW; o += lanes) {
-    const int ly = o / TW, lx = o - ly * TW;
-    const int oy = oy0 + ly, ox = ox0 + lx;
-    if (oy >= a.oh || ox >= a.ow) continue;
-    float acc[8];
 #pragma unroll
-    for (int j = 0; j < 8; j++) acc[j] = bias[j];
-#pragma unroll
-    for (int ky = 0; ky < K; ky++) {
-#pragma unroll
-      for (int kx = 0; kx < K; kx++) {
-        const int p = (ly * S + ky) * IWt + lx * S + kx;
-        float xv[8];
-        if constexpr (SC) {
-          const float4* src = reinterpret_cast<const float4*>(stile) + ((int64_t)p * CS + cg * 8) / 4;
-          float4 f0 = src[0], f1 = src[1];
-          xv[0] = f0.x; xv[1] = f0.y; xv[2] = f0.z; xv[3] = f0.w;
-          xv[4] = f1.x; xv[5] = f1.y; xv[6] = f1.z; xv[7] = f1.w;
-        } else {
-          const uint4 u = reinterpret_cast<const uint4*>(stile)[((int64_t)p * CS + cg * 8) / 8];
-          const __half2* h = reinterpret_cast<const __half2*>(&u);
-#pragma unroll
-          for (int i = 0; i < 4; i++) {
-            float2 t = __half22float2(h[i]);
-            xv[2 * i] = t.x;
-            xv[2 * i + 1] = t.y;
-          }
-        }
-        const float4* wp = reinterpret_cast<const float4*>(swc + (ky * K + kx) * CS);
-        const float4 w0 = wp[0], w1 = wp[1];
-        acc[0] = fmaf(xv[0], w0.x, acc[0]); acc[1] = fmaf(xv[1], w0.y, acc[1]);
-        acc[2] = fmaf(xv[2], w0.z, acc[2]); acc[3] = fmaf(xv[3], w0.w, acc[3]);
-        acc[4] = fmaf(xv[4], w1.x, acc[4]); acc[5] = fmaf(xv[5], w1.y, acc[5]);
-        acc[6] = fmaf(xv[6], w1.z, acc[6]); acc[7] = fmaf(xv[7], w1.w, acc[7]);
-      }
+    for (int r = 0; r < DW_R; r++) {
+      acc[r][0] = b0.x; acc[r][1] = b0.y; acc[r][2] = b0.z; acc[r][3] = b0.w;
+      acc[r][4] = b1.x; acc[r][5] = b1.y; acc[r][6] = b1.z; acc[r][7] = b1.w;
     }
-    const int64_t off = (((int64_t)n * a.oh + oy) * a.ow + ox) * a.c + c;
-    if (a.add) {
-      const uint4 r = __ldg(reinterpret_cast<const uint4*>(a.add + off));
-      const __half2* h = reinterpret_cast<const __half2*>(&r);
+  }
+  constexpr int NX = (DW_R - 1) * S + K;
+  const int lx0 = sx * DW_R * S;
+#pragma unroll
+  for (int ky = 0; ky < K; ky++) {
+    const uint4* row = stile + ((sy * S + ky) * IWt + lx0) * G + cg;
+    float xv[NX][8];
+#pragma unroll
+    for (int j = 0; j < NX; j++) {
+      const uint4 u = row[j * G];
+      const __half2* h = reinterpret_cast<const __half2*>(&u);
 #pragma unroll
       for (int i = 0; i < 4; i++) {
         float2 t = __half22float2(h[i]);
-        acc[2 * i] += t.x;
-        acc[2 * i + 1] += t.y;
+        xv[j][2 * i] = t.x;
+        xv[j][2 * i + 1] = t.y;
+      }
+    }
+#pragma unroll
+    for (int kx = 0; kx < K; kx++) {
+      const float4* wp = reinterpret_cast<const float4*>(sw + (ky * K + kx) * CS + cg * 8);
+      const float4 w0 = wp[0], w1 = wp[1];
+      const float wv[8] = {w0.x, w0.y, w0.z, w0.w, w1.x, w1.y, w1.z, w1.w};
+#pragma unroll
+      for (int r = 0; r < DW_R; r++)
+#pragma unroll
+        for (int q = 0; q < 8; q++) acc[r][q] = fmaf(xv[r * S + kx][q], wv[q], acc[r][q]);
+    }
+  }
+#pragma unroll
+  for (int r = 0; r < DW_R; r++) {
+    const int ox = ox0 + sx * DW_R + r;
+    if (ox >= a.ow) break;
+    const int64_t off = (((int64_t)n * a.oh + oy) * a.ow + ox) * a.c + c;
+    if (a.add) {
+      const uint4 ru = __ldg(reinterpret_cast<const uint4*>(a.add + off));
+      const __half2* h = reinterpret_cast<const __half2*>(&ru);
+#pragma unroll
+      for (int i = 0; i < 4; i++) {
+        float2 t = __half22float2(h[i]);
+        acc[r][2 * i] += t.x;
+        acc[r][2 * i + 1] += t.y;
       }
     }
     uint4 u;
     __half2* h = reinterpret_cast<__half2*>(&u);
 #pragma unroll
-    for (int i = 0; i < 4; i++) h[i] = __floats2half2_rn(act_t<ACT>(acc[2 * i]), act_t<ACT>(acc[2 * i + 1]));
+    for (int i = 0; i < 4; i++) h[i] = __floats2half2_rn(act_t<ACT>(acc[r][2 * i]), act_t<ACT>(acc[r][2 * i + 1]));
     *reinterpret_cast<uint4*>(a.y + off) = u;
   }
 }
 
-template <int ACT, int K, int S, bool SC>
+template <int ACT, int K, int S>
 static int dw_launch_t(const DwArgs& a, cudaStream_t st) {
   const int CS = a.c <= 64 ? a.c : 64;
-  const int TH = 8, TW = S == 1 ? 16 : 8;
+  const int G = CS / 8;
+  const int TW = 16, TH = (256 / G) / (TW / DW_R);
   const int IWt = (TW - 1) * S + K, IHt = (TH - 1) * S + K;
-  const size_t smem = sizeof(float) * K * K * CS + (size_t)IHt * IWt * CS * (SC ? 4 : 2);
+  const size_t smem = sizeof(float) * K * K * CS + (size_t)IHt * IWt * CS * 2;
   static bool attr = false;
   if (!attr) {
-    cudaFuncSetAttribute(dw_tiled_kernel<ACT, K, S, SC>, cudaFuncAttributeMaxDynamicSharedMemorySize, 160 * 1024);
+    cudaFuncSetAttribute(dw_tiled_kernel<ACT, K, S>, cudaFuncAttributeMaxDynamicSharedMemorySize, 160 * 1024);
     attr = true;
   }
   const int tiles_x = (a.ow + TW - 1) / TW, tiles_y = (a.oh + TH - 1) / TH;
   dim3 grid(tiles_x * tiles_y, a.c / CS, a.batch);
-  dw_tiled_kernel<ACT, K, S, SC><<<grid, 256, smem, st>>>(a, CS, TH, TW, tiles_x);
+  dw_tiled_kernel<ACT, K, S><<<grid, 256, smem, st>>>(a, CS, TH, TW, tiles_x);
   return SDX_OK;
 }
 
 template <int ACT>
 static bool dw_dispatch_ks(const DwArgs& a, cudaStream_t st) {
-  const bool sc = a.in_scale != nullptr;
-#define SDX_DW_CASE(KK, SS)                                                   \
-  if (a.kh == KK && a.kw == KK && a.sh == SS && a.sw == SS) {                 \
-    if (sc) dw_launch_t<ACT, KK, SS, true>(a, st);                            \
-    else dw_launch_t<ACT, KK, SS, false>(a, st);                              \
-    return true;                                                              \
+#define SDX_DW_CASE(KK, SS)                                   \
+  if (a.kh == KK && a.kw == KK && a.sh == SS && a.sw == SS) { \
+    dw_launch_t<ACT, KK, SS>(a, st);                          \
+    return true;                                              \
   }
   SDX_DW_CASE(3, 1)
   SDX_DW_CASE(3, 2)
@@ -162,8 +157,9 @@ static bool dw_dispatch_ks(const DwArgs& a, cudaStream_t st) {
 }
 
 bool depthwise_tiled_launch(const DwArgs& a, cudaStream_t st) {
-  if (a.c % 8 != 0 || (a.c > 64 && a.c % 64 != 0) || a.batch > 65535) return false;
-  if ((int64_t)((a.ow + 15) / 16) * ((a.oh + 7) / 8) > (1ll << 31) - 1) return false;
+  // channel slabs of 16, 32 or 64 (the strip layout needs 256 / (CS/8) to be a multiple of 4)
+  if (a.c % 8 != 0 || a.batch > 65535) return false;
+  if (!(a.c == 16 || a.c == 32 || a.c % 64 == 0)) return false;
   switch (a.act) {
     case ACT_HARDSWISH: return dw_dispatch_ks<ACT_HARDSWISH>(a, st);
     case ACT_RELU: return dw_dispatch_ks<ACT_RELU>(a, st);
