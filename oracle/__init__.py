@@ -160,6 +160,8 @@ def conv(x: np.ndarray, plan: ConvPlan, strides=(1, 1), pads=(0, 0, 0, 0), act="
     x = _f32(x)
     n, ih, iw, ic = x.shape
     assert ic == plan.ic
+    if plan.u is not None and tuple(strides) != (1, 1):
+        raise ValueError("Winograd plan used for a strided conv: build the ConvPlan with the conv's strides")
     oh = conv_out_size(ih, plan.kh, strides[0], pads[0], pads[2])
     ow = conv_out_size(iw, plan.kw, strides[1], pads[1], pads[3])
     y = np.empty((n, oh, ow, plan.oc), np.float32)

@@ -4,9 +4,11 @@ A random He-initialised det net with squeeze-excitation gates is bistable: its d
 either vanish (gates ~0.5 everywhere, output ~constant) or blow up (gates saturate at 0/1, and
 fp16 rounding gets amplified 10x). This script fixes one well-conditioned instance, LSUV-style:
 walking the plan in order on a seeded calibration batch (the CPU oracle, fp32), each conv's He
-weights get the scale that gives its pre-activation output RMS 1.0, and each gate's second FC the
-scale that gives its pre-gate logits RMS 1.5 (HardSigmoid(0.2, 0.5) then spreads gates over
-~[0.2, 0.8]). Biases keep their seeded values. The scales are a property of the config, like a
+weights get the scale that gives its pre-activation output RMS 1.0, each gate's second FC the scale that gives
+its pre-gate logits RMS 0.75 (HardSigmoid(0.2, 0.5) then spreads gates over ~[0.2, 0.8]) and the
+output ConvT logits RMS 1.0 (probabilities spread around 0.5 without saturating). Targets that push
+the net towards the edge of chaos (gate logits RMS 1.5, output logits 2.0) amplify fp16 storage
+rounding of the first layers about 3x by the output. Biases keep their seeded values. The scales are a property of the config, like a
 checkpoint; the product only reads the frozen table.
 
     python tests/golden/calibrate_det.py
@@ -25,7 +27,8 @@ from oracle.runner import OracleSession  # noqa: E402
 from simdonnx_b200 import configs  # noqa: E402
 
 TARGET_ACT = 1.0
-TARGET_GATE = 1.5
+TARGET_GATE = 0.75
+TARGET_OUT = 1.0
 
 
 def forward_until(P, feeds, stop_node):
@@ -83,7 +86,7 @@ def main(hw=640, batch=1):
             pre = sess._exec(n, env)
             n.p = p0
             rms = float(np.sqrt(np.mean(pre.astype(np.float64) ** 2)))
-            s = (2.0 if n.outs[0] == P.output else TARGET_ACT) / max(rms, 1e-12)
+            s = (TARGET_OUT if n.outs[0] == P.output else TARGET_ACT) / max(rms, 1e-12)
             scales[n.name] = s
             P.values[n.ins[1]].const = (P.values[n.ins[1]].const * s).astype(np.float32)
     print("DET_SCALES = {")
