@@ -196,6 +196,26 @@ typedef struct sdx_gate_desc {
 size_t sdx_channel_gate_scratch_bytes(int batch, int hw, int c);
 int sdx_channel_gate(sdx_ctx* ctx, const sdx_gate_desc* d, sdx_stream s);
 
+/* Same gate as sdx_channel_gate, but it allocates nothing: the channel-sum scratch is a fixed
+ * device array inside the library (one per device) of SDX_GATE_STATIC_MAX_SCRATCH_BYTES, and
+ * d->partial is ignored. No counterpart in the reference (its CPU gate uses stack/pooled buffers).
+ * For callers that cannot hand out device memory at call time: a host runtime that owns all device
+ * memory and gives its plugins no allocator, or a caller that must not pay cudaMalloc/cudaFree,
+ * which can wait for work already running on the device.
+ * Limits and rules:
+ *  - sdx_channel_gate_scratch_bytes(batch, hw, c) must be <= SDX_GATE_STATIC_MAX_SCRATCH_BYTES,
+ *    else SDX_ERR_NOT_SUPPORTED (nothing enqueued); e.g. c = 512 with one pixel chunk allows
+ *    2048 images.
+ *  - The first call on a device looks up the array's device address (cudaGetSymbolAddress) and
+ *    caches it; make that first call before beginning any stream capture on that device.
+ *  - All calls on one device share the one array: two calls whose kernels overlap on the GPU
+ *    (different streams, no ordering between them) race and give wrong gates. Order them on one
+ *    stream or with events.
+ *  - The array keeps the last call's partial sums; each call writes every entry it reads before
+ *    reading it, so nothing needs clearing. */
+#define SDX_GATE_STATIC_MAX_SCRATCH_BYTES (4 * 1024 * 1024)
+int sdx_channel_gate_static(sdx_ctx* ctx, const sdx_gate_desc* d, sdx_stream s);
+
 /* Per-image channel broadcast y[n, p, c] = x[n, p, c] op v[n, c] (+relu) (Ew.Channel via
  * Ops.Elementwise, src/Kernels/Ops.cs:388-420). x, y fp16; v fp32. */
 int sdx_channel_broadcast(sdx_ctx* ctx, int batch, int64_t pixels, int c, int op, int relu, sdx_dptr x,

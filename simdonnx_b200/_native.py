@@ -119,6 +119,7 @@ _SIGS = {
     "sdx_pool": (_i, [_p, ctypes.POINTER(PoolDesc), _p]),
     "sdx_channel_gate_scratch_bytes": (_sz, [_i, _i, _i]),
     "sdx_channel_gate": (_i, [_p, ctypes.POINTER(GateDesc), _p]),
+    "sdx_channel_gate_static": (_i, [_p, ctypes.POINTER(GateDesc), _p]),
     "sdx_channel_broadcast": (_i, [_p, _i, _i64, _i, _i, _i, _u64, _u64, _u64, _p]),
     "sdx_resize_nearest": (_i, [_p, ctypes.POINTER(ResizeDesc), _p]),
     "sdx_concat_channels": (_i, [_p, _i64, _i, ctypes.POINTER(_i), ctypes.POINTER(_u64), _u64, _p]),

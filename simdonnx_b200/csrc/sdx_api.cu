@@ -115,6 +115,31 @@ static inline T* P(sdx_dptr p) {
   return reinterpret_cast<T*>(p);
 }
 
+// Channel-sum scratch of sdx_channel_gate_static. It is a fixed file-scope device array (the
+// runtime places one copy on each device when the module loads), so that entry point never
+// allocates. Every entry a call reads is first written by the same call, so nothing has to be
+// cleared between calls; the array simply keeps the partial sums of the last call.
+static __device__ __align__(256) float g_gate_static_partial[SDX_GATE_STATIC_MAX_SCRATCH_BYTES / sizeof(float)];
+
+// Device address of g_gate_static_partial on `device` (the current device), looked up on the
+// first call for that device and cached. The address stays valid while the device's primary
+// context lives.
+static int gate_static_scratch(int device, float** out) {
+  constexpr int kMaxDevices = 64;
+  static std::mutex mu;
+  static float* cached[kMaxDevices] = {};
+  if (device < 0 || device >= kMaxDevices) return set_error(SDX_ERR_INVALID, "channel gate (static): device ordinal out of range");
+  std::lock_guard<std::mutex> lock(mu);
+  if (!cached[device]) {
+    void* p = nullptr;
+    CK(cudaGetSymbolAddress(&p, g_gate_static_partial), "cudaGetSymbolAddress(channel gate scratch)");
+    if (!p) return set_error(SDX_ERR_CUDA, "channel gate (static): scratch array has no device address");
+    cached[device] = static_cast<float*>(p);
+  }
+  *out = cached[device];
+  return SDX_OK;
+}
+
 extern "C" {
 
 int sdx_abi_version(void) { return SDX_ABI_VERSION; }
@@ -668,6 +693,34 @@ int sdx_channel_gate(sdx_ctx* ctx, const sdx_gate_desc* d, sdx_stream s) {
   a.b2 = P<const float>(d->b2);
   a.s = P<float>(d->s);
   a.partial = P<float>(d->partial);
+  return gate_launch(a, S(ctx, s));
+}
+
+int sdx_channel_gate_static(sdx_ctx* ctx, const sdx_gate_desc* d, sdx_stream s) {
+  USE(ctx);
+  if (!d) return set_error(SDX_ERR_INVALID, "null desc");
+  if (d->batch < 0 || d->hw < 0 || d->c < 0)
+    return set_error(SDX_ERR_INVALID, "channel gate (static): negative batch, hw or c");
+  const size_t need = gate_scratch_bytes(d->batch, d->hw, d->c);
+  if (need > (size_t)SDX_GATE_STATIC_MAX_SCRATCH_BYTES)
+    return set_error(SDX_ERR_NOT_SUPPORTED,
+                     "channel gate (static): needs %zu scratch bytes, above the fixed %d-byte array; "
+                     "use sdx_channel_gate with caller-provided scratch",
+                     need, (int)SDX_GATE_STATIC_MAX_SCRATCH_BYTES);
+  float* scratch = nullptr;
+  int rc = gate_static_scratch(ctx->device, &scratch);
+  if (rc) return rc;
+  LAUNCH_GUARD();
+  GateArgs a;
+  a.batch = d->batch; a.hw = d->hw; a.c = d->c; a.r = d->r; a.act1_relu = d->act1_relu; a.hard = d->hard;
+  a.alpha = d->alpha; a.beta = d->beta; a.offset = d->offset;
+  a.x = P<const __half>(d->x);
+  a.w1 = P<const float>(d->w1);
+  a.b1 = P<const float>(d->b1);
+  a.w2 = P<const float>(d->w2);
+  a.b2 = P<const float>(d->b2);
+  a.s = P<float>(d->s);
+  a.partial = scratch;
   return gate_launch(a, S(ctx, s));
 }
 
