@@ -1,17 +1,19 @@
 // Dense conv / pointwise conv / Gemm / stride==kernel ConvTranspose on the sm_100a tensor cores.
 //
-// One persistent, warp-specialised kernel (192 threads, one CTA per SM):
+// One persistent, warp-specialised kernel (320 threads, one CTA per SM):
 //   warp 0      TMA producer: per 64-channel k-block one A box and the two B boxes (weight terms
 //               hi, lo) into a smem ring (SWIZZLE_128B, no multicast), full/empty mbarriers;
 //   warp 1      allocates TMEM, one lane issues tcgen05.mma (M=128, N=BN, K=16 per instruction,
-//               f16 x f16 -> f32) into one of two TMEM accumulators and commits the stage back;
-//   warps 2..5  epilogue: drain the accumulator with tcgen05.ld (thread = output pixel row), apply
-//               bias -> + residual -> activation (the reference's Store16 order,
-//               src/Kernels/Nhwc.cs:376-398), write the tile into a staging buffer in shared
-//               memory and store it with TMA tensor stores (fully coalesced, asynchronous, clipped
-//               at the tensor edges); the residual tile arrives the same way by a TMA load.
-// The double-buffered accumulator lets the epilogue of tile i overlap the MMAs of tile i+1, and
-// the double-buffered staging lets the TMA store of tile i overlap the epilogue of tile i+1.
+//               f16 x f16 -> f32) into one of four TMEM accumulators and commits the stage back;
+//   warps 2..9  epilogue, two groups of four warps taking alternate tiles. Warp q of a group owns
+//               TMEM lanes (= tile rows) 32q..32q+31 and finishes them on its own: tcgen05.ld in
+//               16-column chunks (double-buffered registers), bias -> + residual -> activation (the
+//               reference's Store16 order, src/Kernels/Nhwc.cs:376-398), a swizzled staging slab
+//               in shared memory, and a TMA tensor store of its 32 rows (coalesced, asynchronous,
+//               clipped at the tensor edges). Its residual rows arrive by a TMA load issued one
+//               tile ahead. No barrier spans more than one warp.
+// Four accumulators (two when BN > 128) let the MMAs run ahead of each epilogue group, and the
+// double-buffered staging lets the TMA store of tile i overlap the epilogue of tile i+1.
 //
 // A operand ("mode"):
 //   TC_ROWS  A is a row-major [M, K] matrix (1x1 conv with the batch folded into rows,
@@ -46,12 +48,11 @@ namespace sdx {
 
 constexpr int TC_BM = 128;
 constexpr int TC_BK = 64;  // halves per 128-byte swizzled row
-constexpr int TC_EPI_GROUPS = 2;                        // epilogue warp groups (one per accumulator)
+constexpr int TC_EPI_GROUPS = 2;                        // epilogue warp groups (alternate tiles)
 constexpr int TC_THREADS = 64 + 128 * TC_EPI_GROUPS;    // producer warp, MMA warp, epilogue groups
 constexpr int TC_MAX_STAGES = 8;
 constexpr uint32_t TC_A_STAGE_BYTES = TC_BM * TC_BK * 2;  // 16 KB
 constexpr int TC_SMEM_LIMIT = 227 * 1024;
-constexpr int TC_MAX_BN = 128;
 constexpr int TC_BIAS_SMEM_MAX = 4096;  // bias floats staged in shared memory
 
 struct TcArgs {
@@ -68,6 +69,7 @@ struct TcArgs {
   int b_rows_per_tap;
   int stages;
   int acc_stride;
+  int nacc;             // TMEM accumulators: 4 when 4 x BN fits the 512 columns, else 2
   uint32_t tmem_cols;
   uint32_t a_box_bytes;
   // epilogue
@@ -89,11 +91,11 @@ struct TcArgs {
   int esz;              // output element bytes
   int G;                // columns per store group
   int ngroups;          // groups per tile
-  int swz;              // group rows are 128 B and 128B-swizzled
-  uint32_t group_bytes; // bytes of one group in the staging buffer
+  int swz;              // staging rows (G * esz bytes = 32, 64 or 128) use the TMA swizzle of that span
+  uint32_t group_bytes; // bytes of one group in the staging buffer (128 rows)
   uint32_t sbuf_bytes;  // bytes of one staging buffer
   int nsbuf;            // staging buffers per epilogue group (1 or 2)
-  uint32_t group_tx;    // bytes one residual group box delivers
+  uint32_t slab_tx;     // bytes one residual box (one group, one warp's 32 rows) delivers
   int bias_smem;        // bias floats staged in shared memory (per accumulator column), 0 = none
   unsigned int* err;
 };
@@ -123,17 +125,6 @@ __device__ __forceinline__ void bulk_wait_read0() { asm volatile("cp.async.bulk.
 __device__ __forceinline__ void bulk_wait_read1() { asm volatile("cp.async.bulk.wait_group.read 1;" ::: "memory"); }
 __device__ __forceinline__ void bulk_wait_all() { asm volatile("cp.async.bulk.wait_group 0;" ::: "memory"); }
 __device__ __forceinline__ void fence_async_smem() { asm volatile("fence.proxy.async.shared::cta;" ::: "memory"); }
-// Rendezvous of the 128 epilogue threads through an mbarrier (count 128) instead of a named
-// barrier, so a warp that leaves on the abort path cannot strand the others: their wait is bounded.
-__device__ __forceinline__ bool epi_sync(uint32_t bar, uint32_t parity, unsigned int* err, volatile int* abort_flag) {
-  mbar_arrive(bar);
-  int ok = 0;
-  if ((threadIdx.x & 31) == 0) ok = mbar_wait(bar, parity, err, SDX_DEV_WAIT_ACC_FULL, abort_flag) ? 1 : 0;
-  ok = __shfl_sync(0xffffffffu, ok, 0);
-  __syncwarp();
-  return ok != 0;
-}
-
 // ------------------------------------------------------------------ per-thread fallback helpers
 __device__ __forceinline__ void load8_res(const TcArgs& a, int64_t off, float* r) {
   if (a.res_f32) {
@@ -181,15 +172,6 @@ __device__ __forceinline__ void out_coord(const TcArgs& a, int64_t row, int n, i
   }
 }
 
-// Staging-buffer byte address of (row r, tile column tc) -- tc a multiple of 8.
-__device__ __forceinline__ uint32_t stage_addr(const TcArgs& a, uint32_t sbuf, int r, int tc, int byte_in_8) {
-  const int g = tc / a.G, cg = tc - g * a.G;
-  const uint32_t base = sbuf + (uint32_t)g * a.group_bytes;
-  const int b = cg * a.esz + byte_in_8;
-  if (a.swz) return base + (uint32_t)r * 128u + ((uint32_t)(((b >> 4) ^ (r & 7)) << 4) | (uint32_t)(b & 15));
-  return base + (uint32_t)r * (uint32_t)(a.G * a.esz) + (uint32_t)b;
-}
-
 __device__ __forceinline__ void lds16(uint32_t addr, uint4& v) {
   asm volatile("ld.shared.v4.u32 {%0, %1, %2, %3}, [%4];" : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w) : "r"(addr));
 }
@@ -202,20 +184,157 @@ struct TileCoord {
   int img, oy0, ox0, m0, n0;
 };
 
-// TMA store (or residual load) of column group g of a tile.
-__device__ __forceinline__ void group_copy(const TcArgs& a, const CUtensorMap* map, uint32_t src, int g,
-                                           const TileCoord& t, bool load, uint32_t bar) {
+// TMA store (or residual load) of column group g of warp q's 32 tile rows. Tile pixel rows
+// 32q..32q+31 form one box: BW >= 32 gives a run of 32 pixels inside one tile row, BW < 32 gives
+// 32/BW whole tile rows (tile widths are powers of two, so BW divides 32 or 32 divides BW).
+// A store whose box starts past the tensor's edge is skipped (it would write nothing); loads there
+// read the zero fill.
+__device__ __forceinline__ void warp_copy(const TcArgs& a, const CUtensorMap* map, uint32_t src, int g, int q,
+                                          const TileCoord& t, bool load, uint32_t bar) {
   const int n = t.n0 + g * a.G;
-  if (a.convt_oc > 0) {
-    const int row = a.convt_kw * a.convt_oc;
-    const int dy = n / row, c = n - dy * row;
-    tma_store_5d(map, src, c, t.ox0, dy, t.oy0, t.img);
-  } else if (a.mode == TC_CONV) {
-    if (load) tma_load_4d(src, map, bar, a.out_ch_off + n, t.ox0, t.oy0, t.img);
-    else tma_store_4d(map, src, a.out_ch_off + n, t.ox0, t.oy0, t.img);
+  if (a.mode == TC_CONV) {
+    const int p0 = q * 32;
+    const int x = t.ox0 + p0 % a.BW, y = t.oy0 + p0 / a.BW;
+    if (!load && (x >= a.OW || y >= a.OH)) return;
+    if (a.convt_oc > 0) {
+      const int row = a.convt_kw * a.convt_oc;
+      const int dy = n / row, c = n - dy * row;
+      tma_store_5d(map, src, c, x, dy, y, t.img);
+    } else if (load) {
+      tma_load_4d(src, map, bar, a.out_ch_off + n, x, y, t.img);
+    } else {
+      tma_store_4d(map, src, a.out_ch_off + n, x, y, t.img);
+    }
   } else {
-    if (load) tma_load_2d(src, map, bar, a.out_ch_off + n, t.m0);
-    else tma_store_2d(map, src, a.out_ch_off + n, t.m0);
+    if (load) tma_load_2d(src, map, bar, a.out_ch_off + n, t.m0 + q * 32);
+    else if (t.m0 + q * 32 < a.M) tma_store_2d(map, src, a.out_ch_off + n, t.m0 + q * 32);
+  }
+}
+
+// One 16-column chunk (tile columns 16c..16c+15) of one accumulator row: bias -> + residual ->
+// activation -> staging slab row `srow` (TMA store path) or global memory (fallback path).
+// (g, cg) = column group of the chunk and its first column inside the group; advanced here.
+template <int ACT>
+__device__ __forceinline__ void epi_chunk(const TcArgs& a, float (&v)[16], int c, uint32_t srow, uint32_t xr,
+                                          const float* sBias, const TileCoord& t, bool valid, int64_t pix, int& g,
+                                          int& cg) {
+  const int n = t.n0 + c * 16;
+  if (a.bias_smem) {
+    const float4* bp = reinterpret_cast<const float4*>(sBias + n);
+#pragma unroll
+    for (int i = 0; i < 4; i++) {
+      const float4 b = bp[i];
+      v[4 * i] += b.x; v[4 * i + 1] += b.y; v[4 * i + 2] += b.z; v[4 * i + 3] += b.w;
+    }
+  } else if (a.bias) {
+#pragma unroll
+    for (int j = 0; j < 16; j++)
+      if (n + j < a.N) v[j] += __ldg(a.bias + (a.convt_oc > 0 ? (n + j) % a.convt_oc : n + j));
+  }
+  if (a.tma_out) {
+    const uint32_t row = srow + (uint32_t)g * a.group_bytes;
+    const uint32_t k0 = ((uint32_t)cg * (uint32_t)a.esz) >> 4;  // first 16-byte unit of the chunk
+    if (a.esz == 2) {
+      const uint32_t ad0 = row + (((k0) ^ xr) << 4), ad1 = row + (((k0 + 1u) ^ xr) << 4);
+      if (a.tma_res) {
+        uint4 u0, u1;
+        lds16(ad0, u0);
+        lds16(ad1, u1);
+        const __half2* h0 = reinterpret_cast<const __half2*>(&u0);
+        const __half2* h1 = reinterpret_cast<const __half2*>(&u1);
+#pragma unroll
+        for (int i = 0; i < 4; i++) {
+          const float2 f0 = __half22float2(h0[i]), f1 = __half22float2(h1[i]);
+          v[2 * i] += f0.x; v[2 * i + 1] += f0.y;
+          v[8 + 2 * i] += f1.x; v[8 + 2 * i + 1] += f1.y;
+        }
+      } else if (a.res && valid && n + 16 <= a.N) {
+        float r8[8];
+        load8_res(a, pix * a.res_pix_stride + a.res_ch_off + n, r8);
+#pragma unroll
+        for (int j = 0; j < 8; j++) v[j] += r8[j];
+        load8_res(a, pix * a.res_pix_stride + a.res_ch_off + n + 8, r8);
+#pragma unroll
+        for (int j = 0; j < 8; j++) v[8 + j] += r8[j];
+      }
+      uint4 u0, u1;
+      __half2* h0 = reinterpret_cast<__half2*>(&u0);
+      __half2* h1 = reinterpret_cast<__half2*>(&u1);
+#pragma unroll
+      for (int i = 0; i < 4; i++) {
+        h0[i] = __floats2half2_rn(act_t<ACT>(v[2 * i]), act_t<ACT>(v[2 * i + 1]));
+        h1[i] = __floats2half2_rn(act_t<ACT>(v[8 + 2 * i]), act_t<ACT>(v[8 + 2 * i + 1]));
+      }
+      sts16(ad0, u0);
+      sts16(ad1, u1);
+    } else {
+#pragma unroll
+      for (int k = 0; k < 4; k++) {
+        const uint32_t ad = row + (((k0 + (uint32_t)k) ^ xr) << 4);
+        float* w = v + 4 * k;
+        if (a.tma_res) {
+          uint4 u;
+          lds16(ad, u);
+          w[0] += __uint_as_float(u.x); w[1] += __uint_as_float(u.y);
+          w[2] += __uint_as_float(u.z); w[3] += __uint_as_float(u.w);
+        } else if (a.res && valid && n + 16 <= a.N) {
+#pragma unroll
+          for (int j = 0; j < 4; j++) {
+            const int64_t ro = pix * a.res_pix_stride + a.res_ch_off + n + 4 * k + j;
+            w[j] += a.res_f32 ? static_cast<const float*>(a.res)[ro] : __half2float(static_cast<const __half*>(a.res)[ro]);
+          }
+        }
+        uint4 u;
+        u.x = __float_as_uint(act_t<ACT>(w[0])); u.y = __float_as_uint(act_t<ACT>(w[1]));
+        u.z = __float_as_uint(act_t<ACT>(w[2])); u.w = __float_as_uint(act_t<ACT>(w[3]));
+        sts16(ad, u);
+      }
+    }
+    cg += 16;
+    if (cg >= a.G) {
+      cg -= a.G;
+      g++;
+    }
+    return;
+  }
+  // ---- fallback: per-thread global stores
+  if (!valid) return;
+#pragma unroll
+  for (int j0 = 0; j0 < 16; j0 += 8) {
+    const int nn = n + j0;
+    if (nn >= a.N) continue;
+    float* vg = v + j0;
+    int64_t opix;
+    int och;
+    out_coord(a, pix, nn, opix, och);
+    if (a.vec_ok && nn + 8 <= a.N) {
+      if (a.res) {
+        float r8[8];
+        load8_res(a, opix * a.res_pix_stride + a.res_ch_off + och, r8);
+#pragma unroll
+        for (int j = 0; j < 8; j++) vg[j] += r8[j];
+      }
+#pragma unroll
+      for (int j = 0; j < 8; j++) vg[j] = act_t<ACT>(vg[j]);
+      store8(a, opix * a.out_pix_stride + a.out_ch_off + och, vg);
+    } else {
+#pragma unroll
+      for (int j = 0; j < 8; j++) {
+        if (nn + j >= a.N) continue;
+        int64_t op;
+        int oc;
+        out_coord(a, pix, nn + j, op, oc);
+        float x = vg[j];
+        if (a.res) {
+          const int64_t ro = op * a.res_pix_stride + a.res_ch_off + oc;
+          x += a.res_f32 ? static_cast<const float*>(a.res)[ro] : __half2float(static_cast<const __half*>(a.res)[ro]);
+        }
+        x = act_t<ACT>(x);
+        const int64_t oo = op * a.out_pix_stride + a.out_ch_off + oc;
+        if (a.out_f32) static_cast<float*>(a.out)[oo] = x;
+        else static_cast<__half*>(a.out)[oo] = __float2half_rn(x);
+      }
+    }
   }
 }
 
@@ -237,12 +356,11 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
                                                (((size_t)a.bias_smem * 4 + 15) & ~(size_t)15));
   uint64_t* full = bars;
   uint64_t* empty = bars + S;
-  uint64_t* accf = bars + 2 * S;
-  uint64_t* acce = bars + 2 * S + 2;
-  uint64_t* drain = bars + 2 * S + 4;
-  uint64_t* resb = bars + 2 * S + 5;  // [group][buffer]
-  uint64_t* epib = bars + 2 * S + 9;  // [group][2] epilogue rendezvous: staging free, staging written
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 2 * S + 13);
+  uint64_t* accf = bars + 2 * S;                  // [4] accumulator full (MMA commit)
+  uint64_t* acce = accf + 4;                      // [4] accumulator drained (128 epilogue threads)
+  uint64_t* drain = acce + 4;
+  uint64_t* resb = drain + 1;                     // [group][buffer][warp] residual slab landed
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(resb + TC_EPI_GROUPS * 2 * 4);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -251,14 +369,11 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
       mbar_init(smem_u32(&full[s]), 1);
       mbar_init(smem_u32(&empty[s]), 1);
     }
-    for (int i = 0; i < 2; i++) {
+    for (int i = 0; i < 4; i++) {
       mbar_init(smem_u32(&accf[i]), 1);
       mbar_init(smem_u32(&acce[i]), 128);
     }
-    for (int i = 0; i < 4; i++) {
-      mbar_init(smem_u32(&resb[i]), 1);
-      mbar_init(smem_u32(&epib[i]), 128);
-    }
+    for (int i = 0; i < TC_EPI_GROUPS * 2 * 4; i++) mbar_init(smem_u32(&resb[i]), 1);
     mbar_init(smem_u32(drain), 1);
     *abort_flag = 0;
     mbar_fence_init();
@@ -335,7 +450,7 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
       uint32_t it = 0, lt = 0;
       bool ok = true;
       for (int tile = blockIdx.x; tile < total_tiles && ok; tile += gridDim.x, lt++) {
-        const uint32_t acc = lt & 1u, ar = lt >> 1;
+        const uint32_t acc = lt & (uint32_t)(a.nacc - 1), ar = lt / (uint32_t)a.nacc;
         if (!mbar_wait(smem_u32(&acce[acc]), (ar & 1u) ^ 1u, a.err, SDX_DEV_WAIT_ACC_EMPTY, abort_flag)) break;
         tc_fence_after();
         const uint32_t d = tmem_base + acc * (uint32_t)a.acc_stride;
@@ -366,215 +481,149 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
     }
     __syncwarp();
   } else {
-    // epilogue: group e (warps 2+4e .. 5+4e) drains accumulator e, i.e. every other tile of this
-    // CTA; warp w reads TMEM lanes 32*(w%4) .. +31 (the lane quadrant it may access)
+    // epilogue: group e (warps 2+4e .. 5+4e) takes the tiles lt = e, e+2, ... of this CTA; warp q
+    // reads TMEM lanes 32q..32q+31 (the lane quadrant it may access), i.e. tile rows 32q..32q+31
     const int e = (warp - 2) >> 2;
     const int q = warp & 3;
     const int row_in_tile = q * 32 + lane;
-    const bool elected = threadIdx.x == 64 + 128 * e;
-    uint32_t res_phase[2] = {0, 0};
+    const uint32_t P = (uint32_t)(a.G * a.esz);  // staging row pitch in bytes
+    // 16-byte-unit XOR of this row under the 32/64/128-byte TMA swizzle (address bits 7.. of a
+    // 1024-aligned slab); 0 when the staging rows are not swizzled
+    const uint32_t xr = a.swz ? (((uint32_t)lane * P) >> 7) & (P / 16u - 1u) : 0u;
+    const uint32_t stage0 = smem_u32(sStage) + (uint32_t)e * a.nsbuf * a.sbuf_bytes + (uint32_t)q * 32u * P;
+    const int tile0 = blockIdx.x + e * gridDim.x, tstep = 2 * gridDim.x;
+    uint32_t res_phase = 0;    // bit b: parity of the next wait on buffer b's residual barrier
+    bool res_pending = false;  // lane 0: a residual load is in flight into buffer (lc % nsbuf)
+
+    auto coords = [&](int tile, TileCoord& t) {
+      const int m_tile = tile / a.n_tiles, n_tile = tile - m_tile * a.n_tiles;
+      t.n0 = n_tile * a.BN;
+      t.img = 0;
+      t.oy0 = 0;
+      t.ox0 = 0;
+      t.m0 = m_tile * TC_BM;
+      if (a.mode == TC_CONV) {
+        const int per_img = a.tiles_h * a.tiles_w;
+        t.img = m_tile / per_img;
+        const int r = m_tile - t.img * per_img;
+        t.oy0 = (r / a.tiles_w) * a.BH;
+        t.ox0 = (r % a.tiles_w) * a.BW;
+      }
+    };
+    // column groups of a tile that start inside the tensor (a group fully past N is skipped)
+    auto groups_of = [&](const TileCoord& t) {
+      return a.convt_oc > 0 ? a.ngroups : min(a.ngroups, (a.N - t.n0 + a.G - 1) / max(a.G, 1));
+    };
+    auto issue_res = [&](int tile, uint32_t buf) {
+      TileCoord t;
+      coords(tile, t);
+      const int ng = groups_of(t);
+      const uint32_t rb = smem_u32(&resb[(e * 2 + buf) * 4 + q]);
+      const uint32_t slab = stage0 + buf * a.sbuf_bytes;
+      mbar_arrive_expect_tx(rb, (uint32_t)ng * a.slab_tx);
+      for (int g = 0; g < ng; g++) warp_copy(a, &tmRes, slab + g * a.group_bytes, g, q, t, true, rb);
+    };
+    if (a.tma_res && lane == 0 && tile0 < total_tiles) {
+      issue_res(tile0, 0);
+      res_pending = true;
+    }
+
     uint32_t lc = 0;  // this group's tile count
-    for (int tile = blockIdx.x + e * gridDim.x; tile < total_tiles; tile += 2 * gridDim.x, lc++) {
+    for (int tile = tile0; tile < total_tiles; tile += tstep, lc++) {
       const uint32_t lt = 2 * lc + (uint32_t)e;
-      const uint32_t acc = lt & 1u, ar = lt >> 1;
+      const uint32_t acc = lt & (uint32_t)(a.nacc - 1), ar = lt / (uint32_t)a.nacc;
+      const uint32_t sbi = lc % (uint32_t)a.nsbuf;
       int ok = 0;
-      if (lane == 0) ok = mbar_wait(smem_u32(&accf[acc]), ar & 1u, a.err, SDX_DEV_WAIT_ACC_FULL, abort_flag) ? 1 : 0;
+      if (lane == 0) {
+        ok = mbar_wait(smem_u32(&accf[acc]), ar & 1u, a.err, SDX_DEV_WAIT_ACC_FULL, abort_flag) ? 1 : 0;
+        if (ok && a.tma_res) {
+          ok = mbar_wait(smem_u32(&resb[(e * 2 + sbi) * 4 + q]), (res_phase >> sbi) & 1u, a.err,
+                         SDX_DEV_WAIT_FULL, abort_flag) ? 1 : 0;
+          if (ok) {
+            res_phase ^= 1u << sbi;
+            res_pending = false;
+          }
+        }
+      }
       ok = __shfl_sync(0xffffffffu, ok, 0);
       if (!ok) break;
       __syncwarp();
       tc_fence_after();
 
-      const int m_tile = tile / a.n_tiles, n_tile = tile - m_tile * a.n_tiles;
       TileCoord tcd;
-      tcd.n0 = n_tile * a.BN;
-      tcd.img = 0;
-      tcd.oy0 = 0;
-      tcd.ox0 = 0;
-      tcd.m0 = m_tile * TC_BM;
+      coords(tile, tcd);
       bool valid;
       int64_t pix;
       if (a.mode == TC_CONV) {
-        const int per_img = a.tiles_h * a.tiles_w;
-        tcd.img = m_tile / per_img;
-        const int r = m_tile - tcd.img * per_img;
-        tcd.oy0 = (r / a.tiles_w) * a.BH;
-        tcd.ox0 = (r % a.tiles_w) * a.BW;
         const int h = row_in_tile / a.BW, w = row_in_tile - h * a.BW;
         const int oy = tcd.oy0 + h, ox = tcd.ox0 + w;
-        valid = row_in_tile < a.BH * a.BW && oy < a.OH && ox < a.OW;
+        valid = oy < a.OH && ox < a.OW;
         pix = ((int64_t)tcd.img * a.OH + oy) * a.OW + ox;
       } else {
         pix = (int64_t)tcd.m0 + row_in_tile;
         valid = pix < a.M;
       }
-      // column groups of this tile that start inside the tensor (a group fully past N is skipped)
-      const int ng = a.convt_oc > 0 ? a.ngroups : min(a.ngroups, (a.N - tcd.n0 + a.G - 1) / max(a.G, 1));
-      const uint32_t sbi = lc % (uint32_t)a.nsbuf;
-      const uint32_t sb = smem_u32(sStage) + ((uint32_t)e * a.nsbuf + sbi) * a.sbuf_bytes;
-      if (a.tma_out) {
-        // the staging buffer is free once the TMA store that last read it has finished reading
-        if (elected) {
-          if (a.nsbuf == 2) bulk_wait_read1();
-          else bulk_wait_read0();
-        }
-        if (!epi_sync(smem_u32(&epib[2 * e]), lc & 1u, a.err, abort_flag)) break;
-        if (a.tma_res) {
-          const uint32_t rb = smem_u32(&resb[2 * e + sbi]);
-          if (elected) {
-            mbar_arrive_expect_tx(rb, (uint32_t)ng * a.group_tx);
-            for (int g = 0; g < ng; g++) group_copy(a, &tmRes, sb + g * a.group_bytes, g, tcd, true, rb);
-          }
-          int rok = 0;
-          if (lane == 0) rok = mbar_wait(rb, res_phase[sbi], a.err, SDX_DEV_WAIT_FULL, abort_flag) ? 1 : 0;
-          res_phase[sbi] ^= 1u;
-          rok = __shfl_sync(0xffffffffu, rok, 0);
-          if (!rok) break;
-          __syncwarp();
-        }
-      }
+      const uint32_t slab = stage0 + sbi * a.sbuf_bytes;
+      const uint32_t srow = slab + (uint32_t)lane * P;
       const uint32_t tbase = tmem_base + ((uint32_t)(q * 32) << 16) + acc * (uint32_t)a.acc_stride;
-      // the whole accumulator row at once: all TMEM loads in flight, one wait, then the accumulator
-      // goes back to the MMA warp before any of the epilogue math
-      float v[TC_MAX_BN];
-      const float* sbias = a.bias_smem ? sBias + tcd.n0 : nullptr;
-      __syncwarp();
-#pragma unroll
-      for (int c = 0; c < TC_MAX_BN / 16; c++)
-        if (c * 16 < a.BN) tmem_ld16_issue(tbase + (uint32_t)(c * 16), v + c * 16);
-      tmem_wait_ld();
-#pragma unroll
-      for (int c = 0; c < TC_MAX_BN / 16; c++)
-        if (c * 16 < a.BN) tmem_ld_wait16(v + c * 16);
-      tc_fence_before();
-      mbar_arrive(smem_u32(&acce[acc]));
-#pragma unroll
-      for (int j = 0; j < TC_MAX_BN / 8; j++) {
-        const int tcol = j * 8;
-        if (tcol >= a.BN) break;
-        {
-          const int n = tcd.n0 + tcol;
-          float* vg = v + tcol;
-          if (a.tma_out) {
-            // bias (ConvT: per output channel) -> + residual (staged) -> act -> staging buffer
-            if (a.bias) {
-              if (sbias) {
-#pragma unroll
-                for (int q2 = 0; q2 < 8; q2++) vg[q2] += sbias[tcol + q2];
-              } else if (a.convt_oc > 0) {
-                for (int q2 = 0; q2 < 8; q2++) vg[q2] += __ldg(a.bias + (n + q2) % a.convt_oc);
-              } else if (n + 8 <= a.N) {
-                const float4* bp = reinterpret_cast<const float4*>(a.bias + n);
-                float4 b0 = __ldg(bp), b1 = __ldg(bp + 1);
-                vg[0] += b0.x; vg[1] += b0.y; vg[2] += b0.z; vg[3] += b0.w;
-                vg[4] += b1.x; vg[5] += b1.y; vg[6] += b1.z; vg[7] += b1.w;
-              } else {
-                for (int q2 = 0; q2 < 8; q2++)
-                  if (n + q2 < a.N) vg[q2] += __ldg(a.bias + n + q2);
-              }
-            }
-            if (a.esz == 2) {
-              const uint32_t ad = stage_addr(a, sb, row_in_tile, tcol, 0);
-              if (a.tma_res) {
-                uint4 u;
-                lds16(ad, u);
-                const __half2* h = reinterpret_cast<const __half2*>(&u);
-#pragma unroll
-                for (int i = 0; i < 4; i++) {
-                  float2 f = __half22float2(h[i]);
-                  vg[2 * i] += f.x;
-                  vg[2 * i + 1] += f.y;
-                }
-              } else if (a.res && valid && n + 8 <= a.N) {
-                float r8[8];
-                load8_res(a, pix * a.res_pix_stride + a.res_ch_off + n, r8);
-#pragma unroll
-                for (int j = 0; j < 8; j++) vg[j] += r8[j];
-              }
-              uint4 u;
-              __half2* h = reinterpret_cast<__half2*>(&u);
-#pragma unroll
-              for (int i = 0; i < 4; i++)
-                h[i] = __floats2half2_rn(act_t<ACT>(vg[2 * i]), act_t<ACT>(vg[2 * i + 1]));
-              sts16(ad, u);
-            } else {
-              const uint32_t a0 = stage_addr(a, sb, row_in_tile, tcol, 0);
-              const uint32_t a1 = stage_addr(a, sb, row_in_tile, tcol, 16);
-              if (a.tma_res) {
-                uint4 u0, u1;
-                lds16(a0, u0);
-                lds16(a1, u1);
-                vg[0] += __uint_as_float(u0.x); vg[1] += __uint_as_float(u0.y);
-                vg[2] += __uint_as_float(u0.z); vg[3] += __uint_as_float(u0.w);
-                vg[4] += __uint_as_float(u1.x); vg[5] += __uint_as_float(u1.y);
-                vg[6] += __uint_as_float(u1.z); vg[7] += __uint_as_float(u1.w);
-              } else if (a.res && valid && n + 8 <= a.N) {
-                float r8[8];
-                load8_res(a, pix * a.res_pix_stride + a.res_ch_off + n, r8);
-#pragma unroll
-                for (int j = 0; j < 8; j++) vg[j] += r8[j];
-              }
-              uint4 u0, u1;
-              u0.x = __float_as_uint(act_t<ACT>(vg[0])); u0.y = __float_as_uint(act_t<ACT>(vg[1]));
-              u0.z = __float_as_uint(act_t<ACT>(vg[2])); u0.w = __float_as_uint(act_t<ACT>(vg[3]));
-              u1.x = __float_as_uint(act_t<ACT>(vg[4])); u1.y = __float_as_uint(act_t<ACT>(vg[5]));
-              u1.z = __float_as_uint(act_t<ACT>(vg[6])); u1.w = __float_as_uint(act_t<ACT>(vg[7]));
-              sts16(a0, u0);
-              sts16(a1, u1);
-            }
-            continue;
-          }
-          // ---- fallback: per-thread global stores
-          if (!valid || n >= a.N) continue;
-          int64_t opix;
-          int och;
-          out_coord(a, pix, n, opix, och);
-          if (a.vec_ok && n + 8 <= a.N) {
-            if (a.bias) {
-              const float4* bp = reinterpret_cast<const float4*>(a.bias + (a.convt_oc > 0 ? och : n));
-              float4 b0 = __ldg(bp), b1 = __ldg(bp + 1);
-              vg[0] += b0.x; vg[1] += b0.y; vg[2] += b0.z; vg[3] += b0.w;
-              vg[4] += b1.x; vg[5] += b1.y; vg[6] += b1.z; vg[7] += b1.w;
-            }
-            if (a.res) {
-              float r8[8];
-              load8_res(a, opix * a.res_pix_stride + a.res_ch_off + och, r8);
-#pragma unroll
-              for (int j = 0; j < 8; j++) vg[j] += r8[j];
-            }
-#pragma unroll
-            for (int j = 0; j < 8; j++) vg[j] = act_t<ACT>(vg[j]);
-            store8(a, opix * a.out_pix_stride + a.out_ch_off + och, vg);
+      const int nch = a.BN / 16;
+      int g = 0, cg = 0;
+      // 16-column chunks through two register buffers: the load of chunk c+1 is in flight while
+      // chunk c is processed; the accumulator goes back to the MMA warp after its last load
+      float va[16], vb[16];
+      tmem_ld16_issue(tbase, va);
+      for (int c = 0; c < nch; c += 2) {
+        tmem_wait_ld();
+        tmem_ld_wait16(va);
+        if (c + 1 < nch) {
+          tmem_ld16_issue(tbase + (uint32_t)(c + 1) * 16u, vb);
+        } else {
+          tc_fence_before();
+          mbar_arrive(smem_u32(&acce[acc]));
+        }
+        epi_chunk<ACT>(a, va, c, srow, xr, sBias, tcd, valid, pix, g, cg);
+        if (c + 1 < nch) {
+          tmem_wait_ld();
+          tmem_ld_wait16(vb);
+          if (c + 2 < nch) {
+            tmem_ld16_issue(tbase + (uint32_t)(c + 2) * 16u, va);
           } else {
-            for (int j = 0; j < 8 && n + j < a.N; j++) {
-              int64_t op;
-              int oc;
-              out_coord(a, pix, n + j, op, oc);
-              float x = vg[j];
-              if (a.bias) x += a.bias[a.convt_oc > 0 ? oc : n + j];
-              if (a.res) {
-                const int64_t ro = op * a.res_pix_stride + a.res_ch_off + oc;
-                x += a.res_f32 ? static_cast<const float*>(a.res)[ro] : __half2float(static_cast<const __half*>(a.res)[ro]);
-              }
-              x = act_t<ACT>(x);
-              const int64_t oo = op * a.out_pix_stride + a.out_ch_off + oc;
-              if (a.out_f32) static_cast<float*>(a.out)[oo] = x;
-              else static_cast<__half*>(a.out)[oo] = __float2half_rn(x);
-            }
+            tc_fence_before();
+            mbar_arrive(smem_u32(&acce[acc]));
           }
+          epi_chunk<ACT>(a, vb, c + 1, srow, xr, sBias, tcd, valid, pix, g, cg);
         }
       }
       if (a.tma_out) {
-        // make the generic-proxy staging writes visible to the TMA engine, then store the tile
+        // make this warp's generic-proxy staging writes visible to the TMA engine, store its rows
         fence_async_smem();
-        if (!epi_sync(smem_u32(&epib[2 * e + 1]), lc & 1u, a.err, abort_flag)) break;
-        if (elected) {
-          for (int g = 0; g < ng; g++) group_copy(a, &tmOut, sb + g * a.group_bytes, g, tcd, false, 0);
+        __syncwarp();
+        if (lane == 0) {
+          const int ng = groups_of(tcd);
+          for (int gg = 0; gg < ng; gg++) warp_copy(a, &tmOut, slab + gg * a.group_bytes, gg, q, tcd, false, 0);
           bulk_commit();
+          // the next tile's buffer is free once the store that last read it has read it; then its
+          // residual rows can be fetched while this warp waits for the next accumulator
+          if (tile + tstep < total_tiles) {
+            if (a.nsbuf == 2) bulk_wait_read1();
+            else bulk_wait_read0();
+            if (a.tma_res) {
+              issue_res(tile + tstep, (lc + 1) % (uint32_t)a.nsbuf);
+              res_pending = true;
+            }
+          }
         }
       }
       __syncwarp();
     }
-    if (elected && a.tma_out) bulk_wait_all();
+    if (lane == 0) {
+      if (res_pending) {
+        // wind-down after an abort: the residual copy in flight must land before smem goes away
+        const uint32_t buf = lc % (uint32_t)a.nsbuf;
+        mbar_wait_drain(smem_u32(&resb[(e * 2 + buf) * 4 + q]), (res_phase >> buf) & 1u, a.err, SDX_DEV_WAIT_DRAIN);
+      }
+      if (a.tma_out) bulk_wait_all();
+    }
   }
   __syncthreads();
   if (warp == 1) {
@@ -619,16 +668,15 @@ static uint32_t pow2_cols(int cols) {
   return c;
 }
 
-// Conv output tile (BH x BW pixels, BH*BW <= 128) that wastes the fewest MMA rows.
+// Conv output tile: BW x BH = 128 pixels with BW a power of two (so each epilogue warp's 32 rows
+// form one TMA box), the one that wastes the fewest MMA rows; ties go to the wider tile.
 static void pick_pixel_tile(int OH, int OW, int* BH, int* BW) {
   double best = -1;
   int bh = 1, bw = 128;
-  const int cands[] = {128, 112, 96, 80, 64, 56, 48, 40, 32, 28, 24, 20, 16, 14, 12, 10, 8, 7, 6, 5, 4, 3, 2, 1};
-  for (int w : cands) {
-    if (w > 2 * OW && w > 8) continue;
-    int h = std::max(1, std::min(TC_BM / w, OH));
-    int tw = (OW + w - 1) / w, th = (OH + h - 1) / h;
-    double util = (double)OH * OW / ((double)tw * th * TC_BM);
+  for (int w = 128; w >= 1; w >>= 1) {
+    const int h = TC_BM / w;
+    const int tw = (OW + w - 1) / w, th = (OH + h - 1) / h;
+    const double util = (double)OH * OW / ((double)tw * th * TC_BM);
     if (util > best + 1e-9) {
       best = util;
       bh = h;
@@ -673,7 +721,7 @@ static int launch_tc(int dev, int grid, size_t smem, cudaStream_t stream, const 
 static size_t smem_bytes(const TcArgs& a) {
   return 1024 + (size_t)a.stages * (TC_A_STAGE_BYTES + 2 * (size_t)a.BN * TC_BK * 2) +
          (size_t)TC_EPI_GROUPS * a.nsbuf * a.sbuf_bytes + (((size_t)a.bias_smem * 4 + 15) & ~(size_t)15) +
-         8 * (2 * a.stages + 13) + 16;
+         8 * (2 * a.stages + 25) + 16;
 }
 
 int tc_launch(const TcProblem& p, cudaStream_t stream) {
@@ -696,8 +744,10 @@ int tc_launch(const TcProblem& p, cudaStream_t stream) {
   a.pad_t = p.pad_t;
   a.pad_l = p.pad_l;
   a.b_rows_per_tap = BN * n_tiles;
+  if (BN > 256) return set_error(SDX_ERR_INVALID, "tc: N tile above 256 columns");
   a.acc_stride = BN;
-  a.tmem_cols = pow2_cols(2 * BN);
+  a.nacc = 4 * BN <= 512 ? 4 : 2;
+  a.tmem_cols = pow2_cols(a.nacc * BN);
   a.bias = p.bias;
   a.res = p.res;
   a.res_f32 = p.res_f32;
@@ -761,9 +811,10 @@ int tc_launch(const TcProblem& p, cudaStream_t stream) {
     if (rc) return rc;
   }
 
-  // ---- epilogue: TMA store groups
+  // ---- epilogue: TMA store groups. A group is G columns (G * esz bytes = one staging row, at most
+  // 128 B); each epilogue warp stores its 32 tile rows of every group as one box.
   const int esz = a.esz;
-  const int cw = 128 / esz;  // columns in one 128-byte swizzled row
+  const int cw = 128 / esz;  // columns in one 128-byte row
   int G;
   if (convt) {
     const int row = p.convt_kw * p.convt_oc;
@@ -773,36 +824,42 @@ int tc_launch(const TcProblem& p, cudaStream_t stream) {
     G = BN * esz >= 128 ? cw : BN;
     if (BN % G != 0) G = 0;
   }
-  bool tma_out = G > 0 && (G * esz) % 16 == 0 && aligned16(p.out) && (p.out_pix_stride * esz) % 16 == 0 &&
+  // 16-column epilogue chunks must not straddle groups
+  bool tma_out = G > 0 && G % 16 == 0 && aligned16(p.out) && (p.out_pix_stride * esz) % 16 == 0 &&
                  (p.out_ch_off * esz) % 16 == 0;
   if (convt) tma_out = tma_out && p.mode == TC_CONV;
-  const int box_rows = p.mode == TC_CONV ? a.BH * a.BW : TC_BM;
   if (tma_out) {
+    const int P = G * esz;
     a.G = G;
     a.ngroups = BN / G;
-    a.swz = (G * esz == 128) ? 1 : 0;
-    a.group_bytes = (uint32_t)(TC_BM * G * esz);
+    a.swz = (P == 32 || P == 64 || P == 128) ? 1 : 0;
+    a.group_bytes = (uint32_t)(TC_BM * P);
     a.sbuf_bytes = (a.group_bytes * a.ngroups + 1023u) & ~1023u;
     const CUtensorMapDataType dt = p.out_f32 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT32 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16;
-    const CUtensorMapSwizzle sw = a.swz ? CU_TENSOR_MAP_SWIZZLE_128B : CU_TENSOR_MAP_SWIZZLE_NONE;
+    const CUtensorMapSwizzle sw = !a.swz ? CU_TENSOR_MAP_SWIZZLE_NONE
+                                  : P == 128 ? CU_TENSOR_MAP_SWIZZLE_128B
+                                  : P == 64  ? CU_TENSOR_MAP_SWIZZLE_64B
+                                             : CU_TENSOR_MAP_SWIZZLE_32B;
+    // one warp's 32 tile rows: a run of 32 pixels (BW >= 32) or 32/BW whole tile rows (BW < 32)
+    const uint32_t wbw = (uint32_t)std::min(a.BW, 32), wbh = (uint32_t)std::max(1, 32 / std::max(a.BW, 1));
     int rc;
     if (convt) {
       const uint64_t row = (uint64_t)p.convt_kw * p.convt_oc;
       uint64_t dims[5] = {row, (uint64_t)p.convt_W, (uint64_t)p.convt_kh, (uint64_t)p.convt_H, (uint64_t)p.batch};
       uint64_t strides[4] = {row * esz, row * p.convt_W * esz, row * p.convt_W * p.convt_kh * esz,
                              row * p.convt_W * p.convt_kh * p.convt_H * esz};
-      uint32_t box[5] = {(uint32_t)G, (uint32_t)a.BW, 1, (uint32_t)a.BH, 1};
+      uint32_t box[5] = {(uint32_t)G, wbw, 1, wbh, 1};
       rc = encode_map(&mOut, p.out, 5, dims, strides, box, dt, sw);
     } else if (p.mode == TC_CONV) {
       const uint64_t ps = (uint64_t)p.out_pix_stride;
       uint64_t dims[4] = {(uint64_t)(p.out_ch_off + p.N), (uint64_t)p.OW, (uint64_t)p.OH, (uint64_t)p.batch};
       uint64_t strides[3] = {ps * esz, ps * p.OW * esz, ps * p.OW * p.OH * esz};
-      uint32_t box[4] = {(uint32_t)G, (uint32_t)a.BW, (uint32_t)a.BH, 1};
+      uint32_t box[4] = {(uint32_t)G, wbw, wbh, 1};
       rc = encode_map(&mOut, p.out, 4, dims, strides, box, dt, sw);
     } else {
       uint64_t dims[2] = {(uint64_t)(p.out_ch_off + p.N), (uint64_t)p.M};
       uint64_t strides[1] = {(uint64_t)p.out_pix_stride * esz};
-      uint32_t box[2] = {(uint32_t)G, TC_BM};
+      uint32_t box[2] = {(uint32_t)G, 32};
       rc = encode_map(&mOut, p.out, 2, dims, strides, box, dt, sw);
     }
     if (rc) return rc;
@@ -813,17 +870,17 @@ int tc_launch(const TcProblem& p, cudaStream_t stream) {
         const uint64_t ps = (uint64_t)p.res_pix_stride;
         uint64_t dims[4] = {(uint64_t)(p.res_ch_off + p.N), (uint64_t)p.OW, (uint64_t)p.OH, (uint64_t)p.batch};
         uint64_t strides[3] = {ps * esz, ps * p.OW * esz, ps * p.OW * p.OH * esz};
-        uint32_t box[4] = {(uint32_t)G, (uint32_t)a.BW, (uint32_t)a.BH, 1};
+        uint32_t box[4] = {(uint32_t)G, wbw, wbh, 1};
         rc = encode_map(&mRes, p.res, 4, dims, strides, box, dt, sw);
       } else {
         uint64_t dims[2] = {(uint64_t)(p.res_ch_off + p.N), (uint64_t)p.M};
         uint64_t strides[1] = {(uint64_t)p.res_pix_stride * esz};
-        uint32_t box[2] = {(uint32_t)G, TC_BM};
+        uint32_t box[2] = {(uint32_t)G, 32};
         rc = encode_map(&mRes, p.res, 2, dims, strides, box, dt, sw);
       }
       if (rc) return rc;
       a.tma_res = 1;
-      a.group_tx = (uint32_t)(G * esz * box_rows);
+      a.slab_tx = (uint32_t)(P * 32);
     }
     a.tma_out = 1;
   } else if (convt && p.mode == TC_CONV) {
@@ -836,7 +893,7 @@ int tc_launch(const TcProblem& p, cudaStream_t stream) {
   if (!a.tma_out) a.sbuf_bytes = 0;
   for (;;) {
     const size_t fixed = 1024 + (size_t)TC_EPI_GROUPS * a.nsbuf * a.sbuf_bytes +
-                         (((size_t)a.bias_smem * 4 + 15) & ~(size_t)15) + 8 * (2 * TC_MAX_STAGES + 13) + 16;
+                         (((size_t)a.bias_smem * 4 + 15) & ~(size_t)15) + 8 * (2 * TC_MAX_STAGES + 25) + 16;
     const size_t per = TC_A_STAGE_BYTES + 2 * (size_t)BN * TC_BK * 2;
     const size_t room = fixed < (size_t)TC_SMEM_LIMIT ? (size_t)TC_SMEM_LIMIT - fixed : 0;
     const int st = (int)std::min<size_t>(TC_MAX_STAGES, room / per);
