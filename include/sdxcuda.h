@@ -236,6 +236,12 @@ int sdx_resize_nearest(sdx_ctx* ctx, const sdx_resize_desc* d, sdx_stream s);
 /* NHWC channel concat (Nhwc.ConcatInner, src/Kernels/Nhwc.Det.cs:354-370), fp16, up to 8 inputs. */
 int sdx_concat_channels(sdx_ctx* ctx, int64_t pixels, int nin, const int* counts, const sdx_dptr* ins,
                         sdx_dptr y, sdx_stream s);
+/* Channel concat of nearest-upsampled inputs: y[n, oy, ox, off_i + c] = x_i[n, oy / s_i, ox / s_i, c]
+ * (a Concat whose inputs are ResizeNearest outputs, Nhwc.ResizeNearest src/Kernels/Nhwc.Det.cs:160-200,
+ * fused with Nhwc.ConcatInner). Input i is [batch, oh / s_i, ow / s_i, counts[i]] fp16 NHWC; s_i = 1
+ * for a full-size input. Every output pixel is written whole. */
+int sdx_concat_nearest(sdx_ctx* ctx, int batch, int oh, int ow, int nin, const int* counts, const int* scales,
+                       const sdx_dptr* ins, sdx_dptr y, sdx_stream s);
 
 /* Elementwise binary on equal shapes (Ew.Binary, src/Kernels/Ew.cs:75-84), fp16, optional relu. */
 int sdx_binary(sdx_ctx* ctx, int64_t n, int op, int relu, sdx_dptr a, sdx_dptr b, sdx_dptr y, sdx_stream s);
@@ -266,7 +272,8 @@ int sdx_attention(sdx_ctx* ctx, int batch, int t, int heads, int d, float scale,
 enum sdx_op_kind {
   SDX_OP_CONV = 1, SDX_OP_GEMM = 2, SDX_OP_CONVT = 3, SDX_OP_POOL = 4, SDX_OP_CHANNEL_GATE = 5,
   SDX_OP_CHANNEL_BROADCAST = 6, SDX_OP_RESIZE_NEAREST = 7, SDX_OP_CONCAT = 8, SDX_OP_BINARY = 9, SDX_OP_ACT = 10,
-  SDX_OP_CONVERT = 11, SDX_OP_LAYERNORM = 12, SDX_OP_SOFTMAX = 13, SDX_OP_ATTENTION = 14
+  SDX_OP_CONVERT = 11, SDX_OP_LAYERNORM = 12, SDX_OP_SOFTMAX = 13, SDX_OP_ATTENTION = 14,
+  SDX_OP_CONCAT_NEAREST = 15
 };
 /* Generic argument block for the ops without a descriptor struct. */
 typedef struct sdx_misc_desc {
@@ -276,6 +283,7 @@ typedef struct sdx_misc_desc {
   float eps, scale;
   sdx_dptr a, b, x, y, w, bias;
   sdx_dptr ins[8];
+  int aux[8];  /* SDX_OP_CONCAT_NEAREST: per-input scale */
 } sdx_misc_desc;
 
 /* sizeof the descriptor struct sdx_session_add_node expects for op_kind (0 = unknown kind). */

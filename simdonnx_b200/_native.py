@@ -22,6 +22,7 @@ NHWC, NCHW = 0, 1
 
 OP_CONV, OP_GEMM, OP_CONVT, OP_POOL, OP_CHANNEL_GATE, OP_CHANNEL_BROADCAST, OP_RESIZE_NEAREST = 1, 2, 3, 4, 5, 6, 7
 OP_CONCAT, OP_BINARY, OP_ACT, OP_CONVERT, OP_LAYERNORM, OP_SOFTMAX, OP_ATTENTION = 8, 9, 10, 11, 12, 13, 14
+OP_CONCAT_NEAREST = 15
 
 FAULT_MALLOC, FAULT_LAUNCH, FAULT_GRAPH, FAULT_D2H, FAULT_SYNC = 1, 2, 3, 4, 5
 
@@ -68,13 +69,13 @@ class MiscDesc(ctypes.Structure):
         (n, _i) for n in ("batch", "c", "t", "heads", "d", "op", "act", "relu", "x_dtype", "x_layout", "y_dtype",
                           "y_layout", "nin")] + [
         ("counts", _i * 8), ("eps", _f), ("scale", _f)] + [
-        (n, _u64) for n in ("a", "b", "x", "y", "w", "bias")] + [("ins", _u64 * 8)]
+        (n, _u64) for n in ("a", "b", "x", "y", "w", "bias")] + [("ins", _u64 * 8), ("aux", _i * 8)]
 
 
 DESC_OF_OP = {OP_CONV: ConvDesc, OP_GEMM: GemmDesc, OP_CONVT: ConvtDesc, OP_POOL: PoolDesc,
               OP_CHANNEL_GATE: GateDesc, OP_RESIZE_NEAREST: ResizeDesc, OP_CHANNEL_BROADCAST: MiscDesc,
               OP_CONCAT: MiscDesc, OP_BINARY: MiscDesc, OP_ACT: MiscDesc, OP_CONVERT: MiscDesc,
-              OP_LAYERNORM: MiscDesc, OP_SOFTMAX: MiscDesc, OP_ATTENTION: MiscDesc}
+              OP_LAYERNORM: MiscDesc, OP_SOFTMAX: MiscDesc, OP_ATTENTION: MiscDesc, OP_CONCAT_NEAREST: MiscDesc}
 
 _SIGS = {
     "sdx_abi_version": (_i, []),
@@ -123,6 +124,8 @@ _SIGS = {
     "sdx_channel_broadcast": (_i, [_p, _i, _i64, _i, _i, _i, _u64, _u64, _u64, _p]),
     "sdx_resize_nearest": (_i, [_p, ctypes.POINTER(ResizeDesc), _p]),
     "sdx_concat_channels": (_i, [_p, _i64, _i, ctypes.POINTER(_i), ctypes.POINTER(_u64), _u64, _p]),
+    "sdx_concat_nearest": (_i, [_p, _i, _i, _i, _i, ctypes.POINTER(_i), ctypes.POINTER(_i), ctypes.POINTER(_u64), _u64,
+                                _p]),
     "sdx_binary": (_i, [_p, _i64, _i, _i, _u64, _u64, _u64, _p]),
     "sdx_act": (_i, [_p, _i64, _i, _u64, _u64, _p]),
     "sdx_convert": (_i, [_p, _i, _i, _i64, _i, _i, _i, _i, _u64, _u64, _p]),

@@ -222,6 +222,18 @@ def concat_channels(be: CudaBackend, xs):
     return y
 
 
+def concat_nearest(be: CudaBackend, xs, scales, out_hw):
+    """Channel concat of nearest-upsampled inputs: input i is upsampled by scales[i] to out_hw."""
+    nb = xs[0].shape[0]
+    oh, ow = out_hw
+    counts = (ctypes.c_int * len(xs))(*[t.shape[-1] for t in xs])
+    sc = (ctypes.c_int * len(xs))(*[int(s) for s in scales])
+    ins = (ctypes.c_uint64 * len(xs))(*[ptr(t) for t in xs])
+    y = torch.empty((nb, oh, ow, sum(t.shape[-1] for t in xs)), dtype=torch.float16, device=xs[0].device)
+    N.call("sdx_concat_nearest", be.ctx, nb, oh, ow, len(xs), counts, sc, ins, ptr(y), cur_stream())
+    return y
+
+
 def binary(be: CudaBackend, a, b, op="add", relu=False):
     y = torch.empty_like(a)
     N.call("sdx_binary", be.ctx, a.numel(), N.EW[op], int(relu), ptr(a), ptr(b), ptr(y), cur_stream())

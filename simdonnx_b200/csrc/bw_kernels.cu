@@ -11,6 +11,8 @@
 
 namespace sdx {
 
+static inline bool aligned8(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 7u) == 0; }
+
 static inline int grid_for(int64_t n, int block) {
   int64_t g = (n + block - 1) / block;
   return (int)std::min<int64_t>(g, (int64_t)1 << 30);
@@ -206,6 +208,76 @@ int direct_conv_launch(const DirectArgs& a, cudaStream_t st) {
 
 // ------------------------------------------------------------------ ConvT, oc < 8 (dot path)
 // ConvTDot (src/Kernels/Nhwc.Det.cs:96-131): per output element one dot product over ic + bias, act.
+// Fast form (kh*kw*oc <= 32): blocks walk input rows; a thread reads its input pixel once, in
+// 8-channel pieces, and keeps all kh*kw*oc sums in registers; weights [tap][o][ic] in shared memory
+// (staged once per block).
+constexpr int CONVT_DOT_MAX_OUT = 32;
+template <int ACT>
+__global__ void convt_dot_rows_kernel(ConvtDotArgs a) {
+  extern __shared__ float sw[];
+  const int taps = a.kh * a.kw, to = taps * a.oc;
+  const int nw = to * a.ic;
+  for (int i = threadIdx.x; i < nw; i += blockDim.x) {
+    const int c = i % a.ic, k = i / a.ic;
+    const int o = k % a.oc, tap = k / a.oc;
+    sw[i] = a.w[((int64_t)c * a.oc + o) * taps + tap];
+  }
+  float* sb = sw + nw;
+  for (int i = threadIdx.x; i < a.oc; i += blockDim.x) sb[i] = a.bias ? a.bias[i] : 0.0f;
+  __syncthreads();
+  const int ow = a.iw * a.kw, oh = a.ih * a.kh;
+  const int per_row = (a.iw + blockDim.x - 1) / blockDim.x;  // jobs (row pieces) per input row
+  const int jobs = a.batch * a.ih * per_row;
+  for (int job = blockIdx.x; job < jobs; job += gridDim.x) {
+    const int row = job / per_row;  // n * ih + y
+    const int x = (job - row * per_row) * blockDim.x + threadIdx.x;
+    if (x >= a.iw) continue;
+    const int n = row / a.ih, y = row - n * a.ih;
+    const __half* xp = a.x + ((int64_t)row * a.iw + x) * a.ic;
+    float acc[CONVT_DOT_MAX_OUT];
+#pragma unroll
+    for (int k = 0; k < CONVT_DOT_MAX_OUT; k++) acc[k] = k < to ? sb[k % a.oc] : 0.0f;
+    for (int c = 0; c < a.ic; c += 8) {
+      float xv[8];
+      h8_to_f(__ldg(reinterpret_cast<const uint4*>(xp + c)), xv);
+#pragma unroll
+      for (int k = 0; k < CONVT_DOT_MAX_OUT; k++) {
+        if (k < to) {
+          const float* wk = sw + k * a.ic + c;
+          float s = acc[k];
+#pragma unroll
+          for (int j = 0; j < 8; j++) s = fmaf(xv[j], wk[j], s);
+          acc[k] = s;
+        }
+      }
+    }
+    if (a.oc == 1 && a.kw == 2 && a.y_f32) {
+      // one output channel, two taps per output row: adjacent floats, one 8-byte store per row
+#pragma unroll
+      for (int dy = 0; dy < CONVT_DOT_MAX_OUT / 2; dy++) {
+        if (dy < a.kh) {
+          const int64_t op = ((int64_t)n * oh + y * a.kh + dy) * ow + x * 2;
+          *reinterpret_cast<float2*>(static_cast<float*>(a.y) + op) =
+              make_float2(act_t<ACT>(acc[2 * dy]), act_t<ACT>(acc[2 * dy + 1]));
+        }
+      }
+    } else {
+#pragma unroll
+      for (int k = 0; k < CONVT_DOT_MAX_OUT; k++) {
+        if (k < to) {
+          const int o = k % a.oc, tap = k / a.oc;
+          const int dy = tap / a.kw, dx = tap - dy * a.kw;
+          const int64_t op = ((int64_t)n * oh + y * a.kh + dy) * ow + x * a.kw + dx;
+          const float v = act_t<ACT>(acc[k]);
+          if (a.y_f32) static_cast<float*>(a.y)[op * a.oc + o] = v;
+          else static_cast<__half*>(a.y)[op * a.oc + o] = __float2half_rn(v);
+        }
+      }
+    }
+  }
+}
+
+// General form (any kh*kw*oc): one thread per input pixel, weights from global memory.
 template <int ACT>
 __global__ void convt_dot_kernel(ConvtDotArgs a) {
   const int taps = a.kh * a.kw;
@@ -241,7 +313,19 @@ int convt_dot_launch(const ConvtDotArgs& a, cudaStream_t st) {
   if (a.ic % 8 != 0) return set_error(SDX_ERR_NOT_SUPPORTED, "convt dot: ic must be a multiple of 8");
   const int64_t total = (int64_t)a.batch * a.ih * a.iw;
   if (total == 0) return SDX_OK;
-  SDX_ACT_DISPATCH(a.act, ACTC, convt_dot_kernel<ACTC><<<grid_for(total, 256), 256, 0, st>>>(a));
+  const int to = a.kh * a.kw * a.oc;
+  const size_t wbytes = sizeof(float) * ((size_t)to * a.ic + a.oc);
+  const int64_t rows = (int64_t)a.batch * a.ih;
+  if (to <= CONVT_DOT_MAX_OUT && wbytes <= 48 * 1024 && rows * a.iw <= INT32_MAX && aligned8(a.y)) {
+    const int block = a.iw >= 128 ? 128 : (a.iw + 31) / 32 * 32;
+    const int64_t jobs = rows * ((a.iw + block - 1) / block);
+    int dev = 0;
+    cudaGetDevice(&dev);
+    const int grid = (int)std::min<int64_t>(jobs, (int64_t)num_sms(dev) * 16);
+    SDX_ACT_DISPATCH(a.act, ACTC, convt_dot_rows_kernel<ACTC><<<grid, block, wbytes, st>>>(a));
+  } else {
+    SDX_ACT_DISPATCH(a.act, ACTC, convt_dot_kernel<ACTC><<<grid_for(total, 256), 256, 0, st>>>(a));
+  }
   SDX_LAUNCH_CHECK("convt_dot");
   return SDX_OK;
 }
@@ -410,14 +494,16 @@ __device__ __forceinline__ float ew_op(float a, float b, int op) {
 
 __global__ void broadcast_kernel(int batch, int64_t pixels, int c, int op, int relu, const __half* __restrict__ x,
                                  const float* __restrict__ v, __half* __restrict__ y) {
+  // grid: (chunk blocks of one image, images); chunk index inside an image is 32-bit
   const int cg = c >> 3;
-  const int64_t total = (int64_t)batch * pixels * cg;
-  for (int64_t idx = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; idx < total;
-       idx += (int64_t)gridDim.x * blockDim.x) {
-    const int g = (int)(idx % cg);
-    const int n = (int)(idx / cg / pixels);
+  const int n = blockIdx.y;
+  const int per_img = (int)(pixels * cg);
+  const uint4* xi = reinterpret_cast<const uint4*>(x) + (int64_t)n * per_img;
+  uint4* yi = reinterpret_cast<uint4*>(y) + (int64_t)n * per_img;
+  for (int idx = blockIdx.x * blockDim.x + threadIdx.x; idx < per_img; idx += gridDim.x * blockDim.x) {
+    const int g = idx % cg;
     float xv[8];
-    h8_to_f(__ldg(reinterpret_cast<const uint4*>(x) + idx), xv);
+    h8_to_f(__ldg(xi + idx), xv);
     const float4* vp = reinterpret_cast<const float4*>(v + (int64_t)n * c + g * 8);
     float4 v0 = __ldg(vp), v1 = __ldg(vp + 1);
     const float vv[8] = {v0.x, v0.y, v0.z, v0.w, v1.x, v1.y, v1.z, v1.w};
@@ -426,36 +512,39 @@ __global__ void broadcast_kernel(int batch, int64_t pixels, int c, int op, int r
       float s = ew_op(xv[j], vv[j], op);
       xv[j] = relu ? fmaxf(s, 0.0f) : s;
     }
-    reinterpret_cast<uint4*>(y)[idx] = f_to_h8(xv);
+    yi[idx] = f_to_h8(xv);
   }
 }
 
 int broadcast_launch(int batch, int64_t pixels, int c, int op, int relu, const __half* x, const float* v, __half* y,
                      cudaStream_t st) {
   if (c % 8 != 0) return set_error(SDX_ERR_NOT_SUPPORTED, "broadcast: channels must be a multiple of 8");
-  const int64_t total = (int64_t)batch * pixels * (c / 8);
-  if (total == 0) return SDX_OK;
-  broadcast_kernel<<<grid_for(total, 256), 256, 0, st>>>(batch, pixels, c, op, relu, x, v, y);
+  const int64_t per_img = pixels * (c / 8);
+  if (per_img == 0 || batch == 0) return SDX_OK;
+  if (per_img > INT32_MAX / 2 || batch > 65535) return set_error(SDX_ERR_NOT_SUPPORTED, "broadcast: too large");
+  const int bx = (int)std::min<int64_t>((per_img + 255) / 256, 4096);
+  broadcast_kernel<<<dim3(bx, batch), 256, 0, st>>>(batch, pixels, c, op, relu, x, v, y);
   SDX_LAUNCH_CHECK("broadcast");
   return SDX_OK;
 }
 
 // ------------------------------------------------------------------ nearest resize (+ addend)
+// One block per output row (n, oy); threads walk the row's 16-byte chunks, so the index math is
+// 32-bit and per row. src = floor(dst / scale) (src/Kernels/Nhwc.Det.cs:173, :180).
 __global__ void resize_kernel(ResizeArgs a) {
   const int cg = a.c >> 3;
-  const int64_t total = (int64_t)a.batch * a.oh * a.ow * cg;
+  const int row = blockIdx.x;  // n * oh + oy
+  const int n = row / a.oh, oy = row - n * a.oh;
   const int fy = a.oh / a.ih, fx = a.ow / a.iw;
-  for (int64_t idx = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; idx < total;
-       idx += (int64_t)gridDim.x * blockDim.x) {
-    const int g = (int)(idx % cg);
-    int64_t p = idx / cg;
-    const int ox = (int)(p % a.ow);
-    p /= a.ow;
-    const int oy = (int)(p % a.oh);
-    const int n = (int)(p / a.oh);
-    const int iy = min(oy / fy, a.ih - 1), ix = min(ox / fx, a.iw - 1);
-    uint4 u = __ldg(reinterpret_cast<const uint4*>(a.x + (((int64_t)n * a.ih + iy) * a.iw + ix) * a.c + g * 8));
-    const int64_t op = ((int64_t)n * a.oh + oy) * a.ow + ox;
+  const int iy = min(oy / fy, a.ih - 1);
+  const __half* xrow = a.x + ((int64_t)n * a.ih + iy) * a.iw * a.c;
+  const int64_t op0 = (int64_t)row * a.ow;
+  const int total = a.ow * cg;
+  for (int t = threadIdx.x; t < total; t += blockDim.x) {
+    const int ox = t / cg, g = t - ox * cg;
+    const int ix = min(ox / fx, a.iw - 1);
+    uint4 u = __ldg(reinterpret_cast<const uint4*>(xrow + (int64_t)ix * a.c + g * 8));
+    const int64_t op = op0 + ox;
     if (a.add) {
       float v[8], r[8];
       h8_to_f(u, v);
@@ -471,11 +560,52 @@ __global__ void resize_kernel(ResizeArgs a) {
 int resize_launch(const ResizeArgs& a, cudaStream_t st) {
   if (a.c % 8 || a.y_pix_stride % 8 || a.y_ch_off % 8)
     return set_error(SDX_ERR_NOT_SUPPORTED, "resize: channels / slice must be multiples of 8");
-  if (a.oh % a.ih || a.ow % a.iw) return set_error(SDX_ERR_NOT_SUPPORTED, "resize: integer scales only");
-  const int64_t total = (int64_t)a.batch * a.oh * a.ow * (a.c / 8);
-  if (total == 0) return SDX_OK;
-  resize_kernel<<<grid_for(total, 256), 256, 0, st>>>(a);
+  if (a.ih <= 0 || a.iw <= 0 || a.oh % a.ih || a.ow % a.iw)
+    return set_error(SDX_ERR_NOT_SUPPORTED, "resize: integer scales only");
+  const int64_t rows = (int64_t)a.batch * a.oh;
+  if (rows == 0 || a.ow == 0 || a.c == 0) return SDX_OK;
+  if (rows > INT32_MAX || (int64_t)a.ow * (a.c / 8) > INT32_MAX) return set_error(SDX_ERR_NOT_SUPPORTED, "resize: too large");
+  resize_kernel<<<(unsigned)rows, 256, 0, st>>>(a);
   SDX_LAUNCH_CHECK("resize_nearest");
+  return SDX_OK;
+}
+
+// Channel concat of nearest-upsampled inputs (a Concat whose inputs are ResizeNearest outputs or
+// full-size tensors, fused): every output pixel is written whole, in 16-byte chunks, so no
+// partial-sector writes reach HBM. Input i has spatial size (oh / s_i, ow / s_i).
+__global__ void concat_nearest_kernel(ConcatNearestArgs a) {
+  const int cg = a.ctot >> 3;
+  const int row = blockIdx.x;  // n * oh + oy
+  const int n = row / a.oh, oy = row - n * a.oh;
+  __half* yrow = a.y + (int64_t)row * a.ow * a.ctot;
+  const int total = a.ow * cg;
+  for (int t = threadIdx.x; t < total; t += blockDim.x) {
+    const int ox = t / cg, ch = (t - ox * cg) * 8;
+    int i = 0;
+#pragma unroll
+    for (int k = 1; k < 8; k++)
+      if (k < a.nin && ch >= a.off[k]) i = k;
+    const int sc = a.s[i];
+    const int ih = a.oh / sc, iw = a.ow / sc;
+    const __half* src = a.x[i] + (((int64_t)n * ih + oy / sc) * iw + ox / sc) * a.c[i] + (ch - a.off[i]);
+    *reinterpret_cast<uint4*>(yrow + (int64_t)t * 8) = __ldg(reinterpret_cast<const uint4*>(src));
+  }
+}
+
+int concat_nearest_launch(const ConcatNearestArgs& a, cudaStream_t st) {
+  if (a.nin <= 0 || a.nin > 8) return set_error(SDX_ERR_INVALID, "concat nearest: 1..8 inputs");
+  if (a.oh <= 0 || a.ow <= 0 || a.batch < 0) return set_error(SDX_ERR_INVALID, "concat nearest: bad output size");
+  for (int i = 0; i < a.nin; i++) {
+    if (a.c[i] <= 0 || a.c[i] % 8) return set_error(SDX_ERR_NOT_SUPPORTED, "concat nearest: channels must be multiples of 8");
+    if (a.s[i] <= 0 || a.oh % a.s[i] || a.ow % a.s[i])
+      return set_error(SDX_ERR_NOT_SUPPORTED, "concat nearest: integer scales that divide the output size only");
+    if (!a.x[i]) return set_error(SDX_ERR_INVALID, "concat nearest: null input");
+  }
+  const int64_t rows = (int64_t)a.batch * a.oh;
+  if (rows == 0) return SDX_OK;
+  if (rows > INT32_MAX || (int64_t)a.ow * (a.ctot / 8) > INT32_MAX) return set_error(SDX_ERR_NOT_SUPPORTED, "concat nearest: too large");
+  concat_nearest_kernel<<<(unsigned)rows, 256, 0, st>>>(a);
+  SDX_LAUNCH_CHECK("concat_nearest");
   return SDX_OK;
 }
 

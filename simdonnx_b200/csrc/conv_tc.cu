@@ -18,11 +18,14 @@
 // A operand ("mode"):
 //   TC_ROWS  A is a row-major [M, K] matrix (1x1 conv with the batch folded into rows,
 //            src/Kernels/Nhwc.cs:177-183; Gemm, src/Kernels/Nhwc.Avx512.cs:241-266).
-//   TC_CONV  implicit-GEMM k x k conv, stride 1: for tap (ky, kx) and channel block cb the A tile
-//            is the 4-D box {64 ch, BW, BH, 1} of the NHWC input at (ox0+kx-pl, oy0+ky-pt); the
-//            TMA zero-fills out-of-range rows/columns, which is the constant-0 padding. K is
-//            tap-major then channel, the order of the reference's packed weights
-//            (src/Kernels/Nhwc.cs:102-125).
+//   TC_CONV  implicit-GEMM k x k conv, stride 1. Halo mode (kh > 1): per column tap kx and channel
+//            block cb ONE 4-D box {64 ch, BW, BH + kh - 1, 1} of the NHWC input at
+//            (ox0+kx-pl, oy0-pt) serves all kh row taps: the A operand of tap (ky, kx) is that box
+//            from row ky*BW on (BW >= 8, so the offset is a whole 1024-byte swizzle atom). That
+//            loads each input row (BH + kh - 1) / BH times per kx instead of kh times. Otherwise
+//            (kh = 1) one box {64 ch, BW, BH, 1} per tap. The TMA zero-fills out-of-range
+//            rows/columns, which is the constant-0 padding. K is tap-major then channel, the order
+//            of the reference's packed weights (src/Kernels/Nhwc.cs:102-125).
 // B operand: packed weights [2][taps][n_tiles*BN][ICpad] fp16 (K-major): every weight w is stored as
 // the two-term sum hi + lo with hi = fp16(w), lo = fp16(w - hi), and both terms are multiplied into
 // the same TMEM accumulator (two MMAs per k-step). The activations stay one fp16 term; the weights
@@ -63,6 +66,10 @@ struct TcArgs {
   int n_tiles;
   int m_tiles;
   int kb_per_tap;
+  int halo;             // TC_CONV: one A box per (kx, channel block) holds the BH + kh - 1 input rows
+                        // of all kh row taps; the MMAs of tap (ky, kx) read it from row ky * BW on
+  int b_taps;           // weight taps per stage (kh in halo mode, else 1)
+  uint32_t a_stage_bytes;  // bytes of one A stage (1024-aligned)
   int taps, kw;
   int pad_t, pad_l;
   int OH, OW, BH, BW, tiles_h, tiles_w;
@@ -346,10 +353,11 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   const int S = a.stages;
-  const uint32_t b_half_bytes = (uint32_t)a.BN * TC_BK * 2;
+  const uint32_t b_tap_bytes = (uint32_t)a.BN * TC_BK * 2;              // one tap, one weight term
+  const uint32_t b_half_bytes = b_tap_bytes * (uint32_t)a.b_taps;        // all taps of a stage, one term
   const uint32_t b_stage_bytes = 2 * b_half_bytes;
   uint8_t* sA = smem;
-  uint8_t* sB = smem + (size_t)S * TC_A_STAGE_BYTES;
+  uint8_t* sB = smem + (size_t)S * a.a_stage_bytes;
   uint8_t* sStage = sB + (size_t)S * b_stage_bytes;
   float* sBias = reinterpret_cast<float*>(sStage + (size_t)TC_EPI_GROUPS * a.nsbuf * a.sbuf_bytes);
   uint64_t* bars = reinterpret_cast<uint64_t*>(sStage + (size_t)TC_EPI_GROUPS * a.nsbuf * a.sbuf_bytes +
@@ -397,7 +405,8 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
   const uint32_t tmem_base = *tmem_slot;
 
   const int total_tiles = a.m_tiles * a.n_tiles;
-  const int kblocks = a.taps * a.kb_per_tap;
+  // pipeline stages per tile: (tap, channel block), or (kx, channel block) in halo mode
+  const int kblocks = (a.halo ? a.kw : a.taps) * a.kb_per_tap;
 
   if (warp == 0) {
     if (lane == 0) {
@@ -424,18 +433,29 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
           }
           const uint32_t fb = smem_u32(&full[s]);
           mbar_arrive_expect_tx(fb, a.a_box_bytes + b_stage_bytes);
-          const int tap = kb / a.kb_per_tap, cb = kb - tap * a.kb_per_tap;
-          const uint32_t dA = smem_u32(sA + (size_t)s * TC_A_STAGE_BYTES);
-          if (a.mode == TC_CONV) {
-            const int ky = tap / a.kw, kx = tap - ky * a.kw;
-            tma_load_4d(dA, &tmA, fb, cb * TC_BK, ox0 + kx - a.pad_l, oy0 + ky - a.pad_t, img);
+          const int tk = kb / a.kb_per_tap, cb = kb - tk * a.kb_per_tap;  // tk: tap, or kx in halo mode
+          const uint32_t dA = smem_u32(sA + (size_t)s * a.a_stage_bytes);
+          const uint32_t dB = smem_u32(sB + (size_t)s * b_stage_bytes);
+          if (a.halo) {
+            // rows oy0 - pt .. oy0 - pt + BH + kh - 2 of input column block kx (zero fill = padding)
+            tma_load_4d(dA, &tmA, fb, cb * TC_BK, ox0 + tk - a.pad_l, oy0 - a.pad_t, img);
+            for (int ky = 0; ky < a.b_taps; ky++) {
+              const int brow = (ky * a.kw + tk) * a.b_rows_per_tap + n_tile * a.BN;
+              tma_load_2d(dB + ky * b_tap_bytes, &tmB, fb, cb * TC_BK, brow);
+              tma_load_2d(dB + b_half_bytes + ky * b_tap_bytes, &tmB, fb, cb * TC_BK,
+                          a.taps * a.b_rows_per_tap + brow);
+            }
           } else {
-            tma_load_2d(dA, &tmA, fb, cb * TC_BK, m_tile * TC_BM);
+            if (a.mode == TC_CONV) {
+              const int ky = tk / a.kw, kx = tk - ky * a.kw;
+              tma_load_4d(dA, &tmA, fb, cb * TC_BK, ox0 + kx - a.pad_l, oy0 + ky - a.pad_t, img);
+            } else {
+              tma_load_2d(dA, &tmA, fb, cb * TC_BK, m_tile * TC_BM);
+            }
+            const int brow = tk * a.b_rows_per_tap + n_tile * a.BN;
+            tma_load_2d(dB, &tmB, fb, cb * TC_BK, brow);
+            tma_load_2d(dB + b_half_bytes, &tmB, fb, cb * TC_BK, a.taps * a.b_rows_per_tap + brow);
           }
-          const int brow = tap * a.b_rows_per_tap + n_tile * a.BN;
-          tma_load_2d(smem_u32(sB + (size_t)s * b_stage_bytes), &tmB, fb, cb * TC_BK, brow);
-          tma_load_2d(smem_u32(sB + (size_t)s * b_stage_bytes + b_half_bytes), &tmB, fb, cb * TC_BK,
-                      a.taps * a.b_rows_per_tap + brow);
           issued[s] = round + 1;
         }
       }
@@ -462,13 +482,18 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
             break;
           }
           tc_fence_after();
-          const uint64_t ad = umma_desc_sw128(smem_u32(sA + (size_t)s * TC_A_STAGE_BYTES));
-          const uint64_t bd = umma_desc_sw128(smem_u32(sB + (size_t)s * b_stage_bytes));
-          const uint64_t bl = umma_desc_sw128(smem_u32(sB + (size_t)s * b_stage_bytes + b_half_bytes));
+          const uint32_t sa = smem_u32(sA + (size_t)s * a.a_stage_bytes);
+          const uint32_t sb = smem_u32(sB + (size_t)s * b_stage_bytes);
+          // tap j of the stage: A from row j * BW of the halo box (1024-aligned), B tap j
+          for (int j = 0; j < a.b_taps; j++) {
+            const uint64_t ad = umma_desc_sw128(sa + (uint32_t)j * (uint32_t)a.BW * 128u);
+            const uint64_t bd = umma_desc_sw128(sb + (uint32_t)j * b_tap_bytes);
+            const uint64_t bl = umma_desc_sw128(sb + b_half_bytes + (uint32_t)j * b_tap_bytes);
 #pragma unroll
-          for (int k = 0; k < TC_BK / 16; k++) {
-            umma_f16(d, ad + 2u * k, bd + 2u * k, idesc, (kb > 0 || k > 0) ? 1u : 0u);
-            umma_f16(d, ad + 2u * k, bl + 2u * k, idesc, 1u);
+            for (int k = 0; k < TC_BK / 16; k++) {
+              umma_f16(d, ad + 2u * k, bd + 2u * k, idesc, (kb > 0 || j > 0 || k > 0) ? 1u : 0u);
+              umma_f16(d, ad + 2u * k, bl + 2u * k, idesc, 1u);
+            }
           }
           tc_commit(smem_u32(&empty[s]));
         }
@@ -669,16 +694,19 @@ static uint32_t pow2_cols(int cols) {
 }
 
 // Conv output tile: BW x BH = 128 pixels with BW a power of two (so each epilogue warp's 32 rows
-// form one TMA box), the one that wastes the fewest MMA rows; ties go to the wider tile.
-static void pick_pixel_tile(int OH, int OW, int* BH, int* BW) {
-  double best = -1;
-  int bh = 1, bw = 128;
-  for (int w = 128; w >= 1; w >>= 1) {
+// form one TMA box) and BW >= min_w, the one that wastes the fewest MMA rows; among equals the one
+// whose input box with `halo` extra rows re-reads the least, then the wider one.
+static void pick_pixel_tile(int OH, int OW, int min_w, int halo, int* BH, int* BW) {
+  double best = -1, best_over = 0;
+  int bh = TC_BM / 128, bw = 128;
+  for (int w = 128; w >= min_w; w >>= 1) {
     const int h = TC_BM / w;
     const int tw = (OW + w - 1) / w, th = (OH + h - 1) / h;
     const double util = (double)OH * OW / ((double)tw * th * TC_BM);
-    if (util > best + 1e-9) {
+    const double over = (double)(h + halo) / h;
+    if (util > best + 1e-9 || (util > best - 1e-9 && over < best_over - 1e-9)) {
       best = util;
+      best_over = over;
       bh = h;
       bw = w;
     }
@@ -719,7 +747,7 @@ static int launch_tc(int dev, int grid, size_t smem, cudaStream_t stream, const 
 }
 
 static size_t smem_bytes(const TcArgs& a) {
-  return 1024 + (size_t)a.stages * (TC_A_STAGE_BYTES + 2 * (size_t)a.BN * TC_BK * 2) +
+  return 1024 + (size_t)a.stages * (a.a_stage_bytes + 2 * (size_t)a.b_taps * a.BN * TC_BK * 2) +
          (size_t)TC_EPI_GROUPS * a.nsbuf * a.sbuf_bytes + (((size_t)a.bias_smem * 4 + 15) & ~(size_t)15) +
          8 * (2 * a.stages + 25) + 16;
 }
@@ -777,8 +805,15 @@ int tc_launch(const TcProblem& p, cudaStream_t stream) {
   memset(&mRes, 0, sizeof(mRes));
   if (p.mode == TC_CONV) {
     if (p.C % 8 != 0) return set_error(SDX_ERR_INVALID, "tc conv: input channels must be a multiple of 8");
+    // halo mode for kh > 1: tile widths of at least 8 pixels keep the row offsets 1024-aligned;
+    // used when three stages of it (A box + kh weight taps, two terms) and the staging fit
+    const size_t halo_stage = (size_t)(TC_BM / 8 + p.kh - 1) * 8 * TC_BK * 2 + 2 * (size_t)p.kh * BN * TC_BK * 2;
+    const size_t staging_max = (size_t)TC_EPI_GROUPS * TC_BM * BN * (p.out_f32 ? 4 : 2);
+    const bool halo = p.kh > 1 && p.kh - 1 + TC_BM / 8 <= 256 && 3 * halo_stage + staging_max + 4096 <= (size_t)TC_SMEM_LIMIT;
     int BH, BW;
-    pick_pixel_tile(p.OH, p.OW, &BH, &BW);
+    pick_pixel_tile(p.OH, p.OW, halo ? 8 : 1, halo ? p.kh - 1 : 0, &BH, &BW);
+    a.halo = halo ? 1 : 0;
+    a.b_taps = halo ? p.kh : 1;
     a.BH = BH;
     a.BW = BW;
     a.OH = p.OH;
@@ -786,10 +821,12 @@ int tc_launch(const TcProblem& p, cudaStream_t stream) {
     a.tiles_h = (p.OH + BH - 1) / BH;
     a.tiles_w = (p.OW + BW - 1) / BW;
     a.m_tiles = p.batch * a.tiles_h * a.tiles_w;
-    a.a_box_bytes = (uint32_t)BH * BW * TC_BK * 2;
+    const int box_h = halo ? BH + p.kh - 1 : BH;
+    a.a_box_bytes = (uint32_t)box_h * BW * TC_BK * 2;
+    a.a_stage_bytes = std::max<uint32_t>(TC_A_STAGE_BYTES, (a.a_box_bytes + 1023u) & ~1023u);
     uint64_t dims[4] = {(uint64_t)p.C, (uint64_t)p.W, (uint64_t)p.H, (uint64_t)p.batch};
     uint64_t strides[3] = {(uint64_t)p.C * 2, (uint64_t)p.W * p.C * 2, (uint64_t)p.H * p.W * p.C * 2};
-    uint32_t box[4] = {TC_BK, (uint32_t)BW, (uint32_t)BH, 1};
+    uint32_t box[4] = {TC_BK, (uint32_t)BW, (uint32_t)box_h, 1};
     int rc = encode_map(&mA, p.a, 4, dims, strides, box);
     if (rc) return rc;
   } else {
@@ -797,6 +834,8 @@ int tc_launch(const TcProblem& p, cudaStream_t stream) {
     a.M = p.M;
     a.m_tiles = (p.M + TC_BM - 1) / TC_BM;
     a.a_box_bytes = TC_A_STAGE_BYTES;
+    a.a_stage_bytes = TC_A_STAGE_BYTES;
+    a.b_taps = 1;
     uint64_t dims[2] = {(uint64_t)p.K, (uint64_t)p.M};
     uint64_t strides[1] = {(uint64_t)p.lda * 2};
     uint32_t box[2] = {TC_BK, TC_BM};
@@ -894,7 +933,7 @@ int tc_launch(const TcProblem& p, cudaStream_t stream) {
   for (;;) {
     const size_t fixed = 1024 + (size_t)TC_EPI_GROUPS * a.nsbuf * a.sbuf_bytes +
                          (((size_t)a.bias_smem * 4 + 15) & ~(size_t)15) + 8 * (2 * TC_MAX_STAGES + 25) + 16;
-    const size_t per = TC_A_STAGE_BYTES + 2 * (size_t)BN * TC_BK * 2;
+    const size_t per = a.a_stage_bytes + 2 * (size_t)a.b_taps * BN * TC_BK * 2;
     const size_t room = fixed < (size_t)TC_SMEM_LIMIT ? (size_t)TC_SMEM_LIMIT - fixed : 0;
     const int st = (int)std::min<size_t>(TC_MAX_STAGES, room / per);
     if (st >= 2 || a.nsbuf <= 1) {

@@ -761,6 +761,27 @@ int sdx_concat_channels(sdx_ctx* ctx, int64_t pixels, int nin, const int* counts
   return SDX_OK;
 }
 
+int sdx_concat_nearest(sdx_ctx* ctx, int batch, int oh, int ow, int nin, const int* counts, const int* scales,
+                       const sdx_dptr* ins, sdx_dptr y, sdx_stream s) {
+  USE(ctx);
+  if (nin <= 0 || nin > 8 || !counts || !scales || !ins) return set_error(SDX_ERR_INVALID, "concat nearest: 1..8 inputs");
+  LAUNCH_GUARD();
+  ConcatNearestArgs a;
+  memset(&a, 0, sizeof(a));
+  a.batch = batch; a.oh = oh; a.ow = ow; a.nin = nin;
+  int off = 0;
+  for (int i = 0; i < nin; i++) {
+    a.c[i] = counts[i];
+    a.s[i] = scales[i];
+    a.off[i] = off;
+    a.x[i] = P<const __half>(ins[i]);
+    off += counts[i];
+  }
+  a.ctot = off;
+  a.y = P<__half>(y);
+  return concat_nearest_launch(a, S(ctx, s));
+}
+
 int sdx_binary(sdx_ctx* ctx, int64_t n, int op, int relu, sdx_dptr a, sdx_dptr b, sdx_dptr y, sdx_stream s) {
   USE(ctx);
   LAUNCH_GUARD();

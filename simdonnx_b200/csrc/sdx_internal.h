@@ -137,6 +137,14 @@ struct ResizeArgs {
   __half* y;
 };
 int resize_launch(const ResizeArgs& a, cudaStream_t st);
+
+struct ConcatNearestArgs {
+  int batch, oh, ow, nin, ctot;
+  int c[8], s[8], off[8];  // channels, upsampling scale and first output channel of input i
+  const __half* x[8];
+  __half* y;
+};
+int concat_nearest_launch(const ConcatNearestArgs& a, cudaStream_t st);
 int slice_copy_launch(int64_t pixels, int c, const __half* x, int64_t y_pix_stride, int y_ch_off, __half* y,
                       cudaStream_t st);
 int binary_launch(int64_t n, int op, int relu, const __half* a, const __half* b, __half* y, cudaStream_t st);

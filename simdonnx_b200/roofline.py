@@ -85,6 +85,8 @@ def node_cost(plan: ExecPlan, n) -> tuple:
         return "pool", 0, _nb(plan, n.ins[0]) + _nb(plan, out)
     if op == "Concat":
         return "concat", 0, sum(_nb(plan, v) for v in n.ins) + _nb(plan, out)
+    if op == "ConcatNearest":
+        return "concat_nearest", 0, sum(_nb(plan, v) for v in n.ins) + _nb(plan, out)
     if op == "Convert":
         return "convert", 0, _nb(plan, n.ins[0]) + _nb(plan, out)
     if op in ("LayerNorm", "Softmax", "Act"):

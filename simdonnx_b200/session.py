@@ -4,8 +4,9 @@ The reference's Vulkan backend is the template (VkGraphModel, src/Backends/Vulka
 :472-1112; VkInferenceSession, src/Backends/Vulkan/VkSession.cs:63-143, :282-337, :535-556):
   * backend-side rewrites that change no numerics class (cuda_rewrite): fp32 -> fp16 boundary
     conversion where a tensor-core conv reads a graph input; the squeeze-excitation product x*s
-    folded into the load of the depthwise convs that consume it; producers of a channel Concat
-    write straight into their slice of its output;
+    folded into the load of the depthwise convs that consume it; a channel Concat of
+    nearest-upsampled tensors becomes one ConcatNearest node that writes whole output pixels;
+    producers of any other channel Concat write straight into their slice of its output;
   * one device arena (int64 byte offsets, plan.plan_arena) + a per-model const store of packed
     weights; every node becomes one sdx_* descriptor over device pointers arena + offset;
   * the node list is validated once eagerly and captured into one CUDA graph.
@@ -66,7 +67,46 @@ def cuda_rewrite(plan: ExecPlan) -> ExecPlan:
         keep.append(n)
     P.nodes = keep
 
-    # 3. channel concat: producers write into their slice
+    # 3. channel concat of nearest-upsampled inputs -> one ConcatNearest node that writes whole
+    #    output pixels (the upsampled 24-channel slices alone would be partial-sector writes)
+    prods = {o: m for m in P.nodes for o in m.outs}
+    drop = set()
+    out_nodes = []
+    for n in P.nodes:
+        if n.op == "Concat" and P.values[n.outs[0]].dtype == "f16" and len(P.shape(n.outs[0])) == 4:
+            nb, oh, ow, _ = P.shape(n.outs[0])
+            srcs, scales, resized, ok = [], [], [], True
+            for v in n.ins:
+                vs = P.shape(v)
+                m = prods.get(v)
+                if P.values[v].dtype != "f16" or len(vs) != 4 or vs[3] % 8 != 0:
+                    ok = False
+                    break
+                if (m is not None and m.op == "ResizeNearest" and len(m.ins) == 1 and len(P.consumers(v)) == 1 and
+                        m.p.scales[0] == m.p.scales[1] and v != P.output):
+                    src = m.ins[0]
+                    ss = P.shape(src)
+                    f = m.p.scales[0]
+                    if ss[1] * f != oh or ss[2] * f != ow or P.values[src].dtype != "f16":
+                        ok = False
+                        break
+                    srcs.append(src)
+                    scales.append(f)
+                    resized.append(m)
+                elif vs[1:3] == (oh, ow):
+                    srcs.append(v)
+                    scales.append(1)
+                else:
+                    ok = False
+                    break
+            if ok and resized and len(srcs) <= 8:
+                drop.update(id(m) for m in resized)
+                out_nodes.append(Node("ConcatNearest", srcs, list(n.outs), tuple(scales), n.name))
+                continue
+        out_nodes.append(n)
+    P.nodes = [n for n in out_nodes if id(n) not in drop]
+
+    # 4. channel concat: producers write into their slice
     keep = []
     for n in P.nodes:
         if n.op == "Concat":
@@ -228,6 +268,17 @@ class CudaInferenceSession:
             d.add = self.ptr(n.ins[1]) if len(n.ins) > 1 else 0
             d.y = self.ptr(n.outs[0])
             return N.OP_RESIZE_NEAREST, d
+        if op == "ConcatNearest":
+            nb, oh, ow, _ = P.shape(n.outs[0])
+            d = N.MiscDesc()
+            d.batch, d.rows, d.n = nb, oh, ow
+            d.nin = len(n.ins)
+            for i, v in enumerate(n.ins):
+                d.counts[i] = P.shape(v)[-1]
+                d.aux[i] = int(p[i])
+                d.ins[i] = self.ptr(v)
+            d.y = self.ptr(n.outs[0])
+            return N.OP_CONCAT_NEAREST, d
         if op == "Concat":
             d = N.MiscDesc()
             first = P.shape(n.ins[0])

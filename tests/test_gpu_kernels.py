@@ -156,6 +156,7 @@ def test_gemm_residual(be):
 
 # ------------------------------------------------------------------------------------------- ConvT
 @pytest.mark.parametrize("ic,oc,h,w,act,f32", [(24, 24, 40, 40, "relu", False), (24, 1, 40, 40, "sigmoid", True),
+                                               (16, 3, 13, 300, "none", False),
                                                (64, 32, 16, 16, "none", False), (512, 256, 8, 8, "none", False)])
 def test_convt(be, ic, oc, h, w, act, f32):
     from simdonnx_b200 import backend as B
@@ -226,6 +227,17 @@ def test_channel_gate_and_broadcast(be, c, hw):
     assert_close(host(s), ref_s, "gate")
     y = B.channel_broadcast(be, dev16(x), s)
     assert_close(host(y), O.channel_broadcast(x, ref_s), "x*s")
+
+
+def test_concat_nearest(be):
+    """Upsample-and-concat in one pass == resize each input then concat (bit exact: pure copies)."""
+    from simdonnx_b200 import backend as B
+    rng = np.random.default_rng(23)
+    parts = [rnd(rng, 2, 5, 6, 24), rnd(rng, 2, 10, 12, 16), rnd(rng, 2, 20, 24, 8), rnd(rng, 2, 40, 48, 24)]
+    scales = (8, 4, 2, 1)
+    ref = O.concat_channels([O.resize_nearest(p, (s, s)) if s > 1 else p for p, s in zip(parts, scales)])
+    y = B.concat_nearest(be, [dev16(p) for p in parts], scales, (40, 48))
+    np.testing.assert_array_equal(host(y), ref.astype(np.float16).astype(np.float32))
 
 
 def test_resize_add_and_concat(be):

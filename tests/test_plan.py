@@ -52,9 +52,27 @@ def test_det_rewrites():
     fused = [n for n in P.nodes if n.op == "Conv" and getattr(n.p, "in_scale", None)]
     assert len(fused) == 8
     assert sum(n.op == "Elementwise" for n in P.nodes) == 4
-    # the FPN concat is written in place by its four producers
+    # the FPN concat of three upsampled maps and p2 becomes one ConcatNearest node (no resize nodes)
     assert not any(n.op == "Concat" for n in P.nodes)
-    assert sorted(P.values[v].alias[1] for v in ("fpn.p5u", "fpn.p4u", "fpn.p3u", "fpn.p2")) == [0, 24, 48, 72]
+    cn = [n for n in P.nodes if n.op == "ConcatNearest"]
+    assert len(cn) == 1 and cn[0].ins == ["fpn.p5", "fpn.p4", "fpn.p3", "fpn.p2"] and cn[0].p == (8, 4, 2, 1)
+    assert not any(n.op == "ResizeNearest" and n.outs[0] in ("fpn.p5u", "fpn.p4u", "fpn.p3u") for n in P.nodes)
+
+
+def test_concat_slice_aliasing_without_upsampling():
+    """A Concat of conv outputs is written in place by its producers (slice offsets 0, c0, ...)."""
+    b = configs._Builder(3)
+    P = b.P
+    x = P.add_value("x", (1, 8, 8, 16))
+    P.inputs = [x]
+    a1 = b.conv("a1", x, 16, 1)
+    a2 = b.conv("a2", x, 24, 3)
+    y = P.add_value("y", (1, 8, 8, 40))
+    P.add_node("Concat", [a1, a2], [y], None, "cat")
+    P.output = y
+    R = cuda_rewrite(P)
+    assert not any(n.op in ("Concat", "ConcatNearest") for n in R.nodes)
+    assert (R.values["a1"].alias, R.values["a2"].alias) == (("y", 0), ("y", 16))
 
 
 def test_det_shapes_follow_onnx_formulas():
