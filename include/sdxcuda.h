@@ -150,6 +150,9 @@ typedef struct sdx_conv_desc {
   int y_ch_off;      /* first output channel in that slice */
   sdx_dptr x, w, bias, add, y;  /* w: packed by sdx_pack_conv; bias fp32 [oc] or 0; add 0 = none */
   sdx_dptr in_scale; /* fp32 [batch, ic] per-image channel scale applied to x on load (SE gate), or 0 */
+  int w_terms;       /* tensor-core routes: fp16 weight terms, 1 (w) or 2 (hi + lo, ~22-bit weights);
+                        0 = default: 2 for 1x1 kernels (their MMAs hide under HBM time), 1 for larger
+                        kernels (MMA-bound; one fp16 term is the reference GPU backends' weight type) */
 } sdx_conv_desc;
 int sdx_conv2d(sdx_ctx* ctx, const sdx_conv_desc* d, sdx_stream s);
 

@@ -73,8 +73,8 @@ def launch_count() -> int:
 # ------------------------------------------------------------------------------- packing
 def conv_desc(batch, ih, iw, ic, oc, kh, kw, stride=(1, 1), pads=(0, 0, 0, 0), group=1, act="none",
               x_dtype=torch.float16, x_layout=N.NHWC, y_dtype=torch.float16, y_layout=N.NHWC,
-              add_dtype=torch.float16, add_layout=N.NHWC, pool=False, pool_relu=False, y_pix_stride=0, y_ch_off=0
-              ) -> N.ConvDesc:
+              add_dtype=torch.float16, add_layout=N.NHWC, pool=False, pool_relu=False, y_pix_stride=0, y_ch_off=0,
+              w_terms=0) -> N.ConvDesc:
     d = N.ConvDesc()
     d.batch, d.ih, d.iw, d.ic, d.oc, d.kh, d.kw = batch, ih, iw, ic, oc, kh, kw
     d.sh, d.sw = stride
@@ -88,6 +88,7 @@ def conv_desc(batch, ih, iw, ic, oc, kh, kw, stride=(1, 1), pads=(0, 0, 0, 0), g
     d.y_dtype, d.y_layout = _F[y_dtype], y_layout
     d.add_dtype, d.add_layout = _F[add_dtype], add_layout
     d.y_pix_stride, d.y_ch_off = y_pix_stride, y_ch_off
+    d.w_terms = w_terms
     return d
 
 

@@ -26,11 +26,15 @@
 //            (kh = 1) one box {64 ch, BW, BH, 1} per tap. The TMA zero-fills out-of-range
 //            rows/columns, which is the constant-0 padding. K is tap-major then channel, the order
 //            of the reference's packed weights (src/Kernels/Nhwc.cs:102-125).
-// B operand: packed weights [2][taps][n_tiles*BN][ICpad] fp16 (K-major): every weight w is stored as
-// the two-term sum hi + lo with hi = fp16(w), lo = fp16(w - hi), and both terms are multiplied into
-// the same TMEM accumulator (two MMAs per k-step). The activations stay one fp16 term; the weights
-// keep ~22 significant bits, so weight rounding no longer shifts coherent sums such as the
-// squeeze-excitation means. The path is HBM-bound, so the extra MMAs cost nothing measurable.
+// B operand: packed weights [terms][taps][n_tiles*BN][Kpad] fp16 (K-major), K padded to the channel
+// block (64, 32 or 16). With two terms every weight w is stored as hi + lo, hi = fp16(w),
+// lo = fp16(w - hi), and both are multiplied into the same TMEM accumulator (two MMAs per k-step):
+// the weights keep ~22 significant bits, so weight rounding does not shift coherent sums such as
+// squeeze-excitation means. 1x1 convs, Gemm and ConvT use two terms (their MMAs hide under HBM
+// time); k x k convs default to one (the MMA issue rate bounds them; one fp16 term is the weight
+// type of the reference's GPU backends). The activations are one fp16 term.
+// The weights sit in shared memory for the whole kernel when they fit beside the A ring, else they
+// are streamed with each A stage.
 //
 // ConvT (stride == kernel, src/Kernels/Nhwc.Det.cs:46-93): a 1x1 TC_CONV over the input pixels with
 // N = kh*kw*OC columns (tap-major); the epilogue stores column group (dy, dx*OC + o) of a BH x BW
@@ -50,11 +54,9 @@
 namespace sdx {
 
 constexpr int TC_BM = 128;
-constexpr int TC_BK = 64;  // halves per 128-byte swizzled row
 constexpr int TC_EPI_GROUPS = 2;                        // epilogue warp groups (alternate tiles)
 constexpr int TC_THREADS = 64 + 128 * TC_EPI_GROUPS;    // producer warp, MMA warp, epilogue groups
-constexpr int TC_MAX_STAGES = 8;
-constexpr uint32_t TC_A_STAGE_BYTES = TC_BM * TC_BK * 2;  // 16 KB
+constexpr int TC_MAX_STAGES = 8;  // <= 32 (ring slots are tracked in 32-bit masks)
 constexpr int TC_SMEM_LIMIT = 227 * 1024;
 constexpr int TC_BIAS_SMEM_MAX = 4096;  // bias floats staged in shared memory
 
@@ -70,6 +72,10 @@ struct TcArgs {
                         // of all kh row taps; the MMAs of tap (ky, kx) read it from row ky * BW on
   int b_taps;           // weight taps per stage (kh in halo mode, else 1)
   uint32_t a_stage_bytes;  // bytes of one A stage (1024-aligned)
+  int kblk;             // channels per k-block: 64, 32 or 16 (rows of 128/64/32 B, same-span swizzle)
+  int b_resident;       // 1: all weights are loaded into shared memory once per CTA
+  int wterms;           // fp16 weight terms: 1 (w) or 2 (hi, lo: two MMAs per k-step)
+  uint32_t b_total_bytes;  // bytes of all weights (both terms), resident mode
   int taps, kw;
   int pad_t, pad_l;
   int OH, OW, BH, BW, tiles_h, tiles_w;
@@ -218,6 +224,19 @@ __device__ __forceinline__ void warp_copy(const TcArgs& a, const CUtensorMap* ma
   }
 }
 
+// NK k-steps of 16 channels: each multiplies the A rows by the weight term (TWO: by both terms,
+// hi then lo) into the same accumulator; `first` = 0 makes the very first MMA of a tile overwrite
+// the accumulator.
+template <int NK, bool TWO>
+__device__ __forceinline__ void umma_steps(uint32_t d, uint64_t ad, uint64_t bdh, uint64_t bdl, uint32_t idesc,
+                                           uint32_t first) {
+#pragma unroll
+  for (int k = 0; k < NK; k++) {
+    umma_f16(d, ad + 2u * k, bdh + 2u * k, idesc, k == 0 ? first : 1u);
+    if (TWO) umma_f16(d, ad + 2u * k, bdl + 2u * k, idesc, 1u);
+  }
+}
+
 // One 16-column chunk (tile columns 16c..16c+15) of one accumulator row: bias -> + residual ->
 // activation -> staging slab row `srow` (TMA store path) or global memory (fallback path).
 // (g, cg) = column group of the chunk and its first column inside the group; advanced here.
@@ -353,12 +372,13 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   const int S = a.stages;
-  const uint32_t b_tap_bytes = (uint32_t)a.BN * TC_BK * 2;              // one tap, one weight term
+  const uint32_t kbytes = (uint32_t)a.kblk * 2;                          // operand row bytes
+  const uint32_t b_tap_bytes = (uint32_t)a.BN * kbytes;                  // one tap, one weight term
   const uint32_t b_half_bytes = b_tap_bytes * (uint32_t)a.b_taps;        // all taps of a stage, one term
-  const uint32_t b_stage_bytes = 2 * b_half_bytes;
+  const uint32_t b_stage_bytes = a.b_resident ? 0u : (uint32_t)a.wterms * b_half_bytes;
   uint8_t* sA = smem;
-  uint8_t* sB = smem + (size_t)S * a.a_stage_bytes;
-  uint8_t* sStage = sB + (size_t)S * b_stage_bytes;
+  uint8_t* sB = smem + (size_t)S * a.a_stage_bytes;  // resident: all weights; else S weight stages
+  uint8_t* sStage = sB + (a.b_resident ? (size_t)a.b_total_bytes : (size_t)S * b_stage_bytes);
   float* sBias = reinterpret_cast<float*>(sStage + (size_t)TC_EPI_GROUPS * a.nsbuf * a.sbuf_bytes);
   uint64_t* bars = reinterpret_cast<uint64_t*>(sStage + (size_t)TC_EPI_GROUPS * a.nsbuf * a.sbuf_bytes +
                                                (((size_t)a.bias_smem * 4 + 15) & ~(size_t)15));
@@ -368,7 +388,8 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
   uint64_t* acce = accf + 4;                      // [4] accumulator drained (128 epilogue threads)
   uint64_t* drain = acce + 4;
   uint64_t* resb = drain + 1;                     // [group][buffer][warp] residual slab landed
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(resb + TC_EPI_GROUPS * 2 * 4);
+  uint64_t* bres = resb + TC_EPI_GROUPS * 2 * 4;  // resident weights landed
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bres + 1);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -383,6 +404,7 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
     }
     for (int i = 0; i < TC_EPI_GROUPS * 2 * 4; i++) mbar_init(smem_u32(&resb[i]), 1);
     mbar_init(smem_u32(drain), 1);
+    mbar_init(smem_u32(bres), 1);
     *abort_flag = 0;
     mbar_fence_init();
   }
@@ -408,97 +430,164 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
   // pipeline stages per tile: (tap, channel block), or (kx, channel block) in halo mode
   const int kblocks = (a.halo ? a.kw : a.taps) * a.kb_per_tap;
 
+  // weight block (term, tap, channel block, n tile) in the resident layout
+  auto b_res_off = [&](int term, int tap, int cb, int nt) -> uint32_t {
+    return (uint32_t)((((term * a.taps + tap) * a.kb_per_tap + cb) * a.n_tiles + nt)) * b_tap_bytes;
+  };
+  // The producer and MMA loops run on one thread each and sit on the critical path of every
+  // stage: no integer division inside them (ring slot, phase, tap and channel block advance as
+  // counters).
   if (warp == 0) {
     if (lane == 0) {
-      uint32_t it = 0;
-      uint32_t issued[TC_MAX_STAGES];
-      for (int s = 0; s < TC_MAX_STAGES; s++) issued[s] = 0;
+      uint32_t issued_mask = 0;  // ring slots that received at least one copy
+      uint32_t last_phase = 0;   // bit s: phase of the last copy into slot s
       bool ok = true;
+      if (a.b_resident) {
+        // every weight block once, onto one barrier
+        const uint32_t bb = smem_u32(bres);
+        mbar_arrive_expect_tx(bb, a.b_total_bytes);
+        for (int term = 0; term < a.wterms; term++)
+          for (int tap = 0; tap < a.taps; tap++)
+            for (int cb = 0; cb < a.kb_per_tap; cb++)
+              for (int nt = 0; nt < a.n_tiles; nt++)
+                tma_load_2d(smem_u32(sB) + b_res_off(term, tap, cb, nt), &tmB, bb, cb * a.kblk,
+                            (term * a.taps + tap) * a.b_rows_per_tap + nt * a.BN);
+      }
+      int s = 0;
+      uint32_t phase = 0;
       for (int tile = blockIdx.x; tile < total_tiles && ok; tile += gridDim.x) {
-        const int m_tile = tile / a.n_tiles, n_tile = tile - m_tile * a.n_tiles;
+        const int m_tile = a.n_tiles == 1 ? tile : tile / a.n_tiles;
+        const int n_tile = tile - m_tile * a.n_tiles;
         int img = 0, oy0 = 0, ox0 = 0;
         if (a.mode == TC_CONV) {
           const int per_img = a.tiles_h * a.tiles_w;
           img = m_tile / per_img;
           const int r = m_tile - img * per_img;
-          oy0 = (r / a.tiles_w) * a.BH;
-          ox0 = (r % a.tiles_w) * a.BW;
+          const int ty = r / a.tiles_w;
+          oy0 = ty * a.BH;
+          ox0 = (r - ty * a.tiles_w) * a.BW;
         }
-        for (int kb = 0; kb < kblocks; kb++, it++) {
-          const int s = (int)(it % (uint32_t)S);
-          const uint32_t round = it / (uint32_t)S;
-          if (!mbar_wait(smem_u32(&empty[s]), (round & 1u) ^ 1u, a.err, SDX_DEV_WAIT_EMPTY, abort_flag)) {
+        int tk = 0, cb = 0;  // tk: tap, or kx in halo mode
+        for (int kb = 0; kb < kblocks; kb++) {
+          if (!mbar_wait(smem_u32(&empty[s]), phase ^ 1u, a.err, SDX_DEV_WAIT_EMPTY, abort_flag)) {
             ok = false;
             break;
           }
           const uint32_t fb = smem_u32(&full[s]);
           mbar_arrive_expect_tx(fb, a.a_box_bytes + b_stage_bytes);
-          const int tk = kb / a.kb_per_tap, cb = kb - tk * a.kb_per_tap;  // tk: tap, or kx in halo mode
-          const uint32_t dA = smem_u32(sA + (size_t)s * a.a_stage_bytes);
-          const uint32_t dB = smem_u32(sB + (size_t)s * b_stage_bytes);
+          const uint32_t dA = smem_u32(sA) + (uint32_t)s * a.a_stage_bytes;
+          const uint32_t dB = smem_u32(sB) + (uint32_t)s * b_stage_bytes;
           if (a.halo) {
             // rows oy0 - pt .. oy0 - pt + BH + kh - 2 of input column block kx (zero fill = padding)
-            tma_load_4d(dA, &tmA, fb, cb * TC_BK, ox0 + tk - a.pad_l, oy0 - a.pad_t, img);
-            for (int ky = 0; ky < a.b_taps; ky++) {
-              const int brow = (ky * a.kw + tk) * a.b_rows_per_tap + n_tile * a.BN;
-              tma_load_2d(dB + ky * b_tap_bytes, &tmB, fb, cb * TC_BK, brow);
-              tma_load_2d(dB + b_half_bytes + ky * b_tap_bytes, &tmB, fb, cb * TC_BK,
-                          a.taps * a.b_rows_per_tap + brow);
-            }
+            tma_load_4d(dA, &tmA, fb, cb * a.kblk, ox0 + tk - a.pad_l, oy0 - a.pad_t, img);
+          } else if (a.mode == TC_CONV) {
+            const int ky = tk / a.kw, kx = tk - ky * a.kw;
+            tma_load_4d(dA, &tmA, fb, cb * a.kblk, ox0 + kx - a.pad_l, oy0 + ky - a.pad_t, img);
           } else {
-            if (a.mode == TC_CONV) {
-              const int ky = tk / a.kw, kx = tk - ky * a.kw;
-              tma_load_4d(dA, &tmA, fb, cb * TC_BK, ox0 + kx - a.pad_l, oy0 + ky - a.pad_t, img);
-            } else {
-              tma_load_2d(dA, &tmA, fb, cb * TC_BK, m_tile * TC_BM);
-            }
-            const int brow = tk * a.b_rows_per_tap + n_tile * a.BN;
-            tma_load_2d(dB, &tmB, fb, cb * TC_BK, brow);
-            tma_load_2d(dB + b_half_bytes, &tmB, fb, cb * TC_BK, a.taps * a.b_rows_per_tap + brow);
+            tma_load_2d(dA, &tmA, fb, cb * a.kblk, m_tile * TC_BM);
           }
-          issued[s] = round + 1;
+          if (!a.b_resident) {
+            for (int j = 0; j < a.b_taps; j++) {
+              const int tap = a.halo ? j * a.kw + tk : tk;
+              const int brow = tap * a.b_rows_per_tap + n_tile * a.BN;
+              tma_load_2d(dB + j * b_tap_bytes, &tmB, fb, cb * a.kblk, brow);
+              if (a.wterms == 2)
+                tma_load_2d(dB + b_half_bytes + j * b_tap_bytes, &tmB, fb, cb * a.kblk, a.taps * a.b_rows_per_tap + brow);
+            }
+          }
+          issued_mask |= 1u << s;
+          last_phase = (last_phase & ~(1u << s)) | (phase << s);
+          if (++cb == a.kb_per_tap) {
+            cb = 0;
+            tk++;
+          }
+          if (++s == S) {
+            s = 0;
+            phase ^= 1u;
+          }
         }
       }
       // wind-down: every issued copy must land before the CTA's shared memory goes away
-      for (int s = 0; s < S; s++)
-        if (issued[s] > 0) mbar_wait_drain(smem_u32(&full[s]), (issued[s] - 1) & 1u, a.err, SDX_DEV_WAIT_DRAIN);
+      for (int q = 0; q < S; q++)
+        if (issued_mask & (1u << q))
+          mbar_wait_drain(smem_u32(&full[q]), (last_phase >> q) & 1u, a.err, SDX_DEV_WAIT_DRAIN);
+      if (a.b_resident) mbar_wait_drain(smem_u32(bres), 0, a.err, SDX_DEV_WAIT_DRAIN);
     }
     __syncwarp();
   } else if (warp == 1) {
     if (lane == 0) {
       const uint32_t idesc = umma_idesc_f16(TC_BM, a.BN);
-      uint32_t it = 0, lt = 0;
-      bool ok = true;
-      for (int tile = blockIdx.x; tile < total_tiles && ok; tile += gridDim.x, lt++) {
-        const uint32_t acc = lt & (uint32_t)(a.nacc - 1), ar = lt / (uint32_t)a.nacc;
-        if (!mbar_wait(smem_u32(&acce[acc]), (ar & 1u) ^ 1u, a.err, SDX_DEV_WAIT_ACC_EMPTY, abort_flag)) break;
+      const int nk = a.kblk / 16;  // MMA k-steps per block
+      // descriptor words: the high word (stride offset, version, swizzle) and the leading-offset
+      // bits are the same for every operand; only the start address changes
+      const uint64_t dconst = umma_desc_kmajor(0u, kbytes);
+      const uint32_t a_row_step = (uint32_t)a.BW * kbytes;  // halo: A rows of the next row tap
+      bool ok = !a.b_resident || mbar_wait(smem_u32(bres), 0, a.err, SDX_DEV_WAIT_FULL, abort_flag);
+      if (ok) tc_fence_after();
+      int s = 0;
+      uint32_t phase = 0;
+      uint32_t acc = 0, accph = 0;
+      for (int tile = blockIdx.x; tile < total_tiles && ok; tile += gridDim.x) {
+        const int n_tile = a.n_tiles == 1 ? 0 : tile % a.n_tiles;
+        if (!mbar_wait(smem_u32(&acce[acc]), accph ^ 1u, a.err, SDX_DEV_WAIT_ACC_EMPTY, abort_flag)) break;
         tc_fence_after();
         const uint32_t d = tmem_base + acc * (uint32_t)a.acc_stride;
-        for (int kb = 0; kb < kblocks; kb++, it++) {
-          const int s = (int)(it % (uint32_t)S);
-          const uint32_t round = it / (uint32_t)S;
-          if (!mbar_wait(smem_u32(&full[s]), round & 1u, a.err, SDX_DEV_WAIT_FULL, abort_flag)) {
+        int tk = 0, cb = 0;
+        uint32_t first = 0;  // 0 until the tile's first MMA (overwrite), then 1 (accumulate)
+        for (int kb = 0; kb < kblocks; kb++) {
+          if (!mbar_wait(smem_u32(&full[s]), phase, a.err, SDX_DEV_WAIT_FULL, abort_flag)) {
             ok = false;
             break;
           }
           tc_fence_after();
-          const uint32_t sa = smem_u32(sA + (size_t)s * a.a_stage_bytes);
-          const uint32_t sb = smem_u32(sB + (size_t)s * b_stage_bytes);
-          // tap j of the stage: A from row j * BW of the halo box (1024-aligned), B tap j
+          const uint32_t sa = smem_u32(sA) + (uint32_t)s * a.a_stage_bytes;
+          const uint32_t sbs = smem_u32(sB) + (uint32_t)s * b_stage_bytes;
+          // tap j of the stage: A from row j * BW of the halo box (a whole number of swizzle atoms)
           for (int j = 0; j < a.b_taps; j++) {
-            const uint64_t ad = umma_desc_sw128(sa + (uint32_t)j * (uint32_t)a.BW * 128u);
-            const uint64_t bd = umma_desc_sw128(sb + (uint32_t)j * b_tap_bytes);
-            const uint64_t bl = umma_desc_sw128(sb + b_half_bytes + (uint32_t)j * b_tap_bytes);
-#pragma unroll
-            for (int k = 0; k < TC_BK / 16; k++) {
-              umma_f16(d, ad + 2u * k, bd + 2u * k, idesc, (kb > 0 || j > 0 || k > 0) ? 1u : 0u);
-              umma_f16(d, ad + 2u * k, bl + 2u * k, idesc, 1u);
+            uint32_t bh, bl;
+            if (a.b_resident) {
+              const uint32_t off = b_res_off(0, a.halo ? j * a.kw + tk : tk, cb, n_tile);
+              bh = smem_u32(sB) + off;
+              bl = bh + (uint32_t)(a.taps * a.kb_per_tap * a.n_tiles) * b_tap_bytes;
+            } else {
+              bh = sbs + (uint32_t)j * b_tap_bytes;
+              bl = bh + b_half_bytes;
             }
+            const uint64_t ad = dconst | (uint64_t)(((sa + (uint32_t)j * a_row_step) >> 4) & 0x3FFFu);
+            const uint64_t bdh = dconst | (uint64_t)((bh >> 4) & 0x3FFFu);
+            const uint64_t bdl = dconst | (uint64_t)((bl >> 4) & 0x3FFFu);
+            // k-steps unrolled: the issue loop is this thread's critical path
+            if (a.wterms == 2) {
+              switch (nk) {
+                case 4: umma_steps<4, true>(d, ad, bdh, bdl, idesc, first); break;
+                case 2: umma_steps<2, true>(d, ad, bdh, bdl, idesc, first); break;
+                default: umma_steps<1, true>(d, ad, bdh, bdl, idesc, first); break;
+              }
+            } else {
+              switch (nk) {
+                case 4: umma_steps<4, false>(d, ad, bdh, bdl, idesc, first); break;
+                case 2: umma_steps<2, false>(d, ad, bdh, bdl, idesc, first); break;
+                default: umma_steps<1, false>(d, ad, bdh, bdl, idesc, first); break;
+              }
+            }
+            first = 1u;
           }
           tc_commit(smem_u32(&empty[s]));
+          if (++cb == a.kb_per_tap) {
+            cb = 0;
+            tk++;
+          }
+          if (++s == S) {
+            s = 0;
+            phase ^= 1u;
+          }
         }
         if (!ok) break;
         tc_commit(smem_u32(&accf[acc]));
+        if (++acc == (uint32_t)a.nacc) {
+          acc = 0;
+          accph ^= 1u;
+        }
       }
       // wind-down: all issued MMAs complete before TMEM / smem are released
       tc_commit(smem_u32(drain));
@@ -521,7 +610,8 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
     bool res_pending = false;  // lane 0: a residual load is in flight into buffer (lc % nsbuf)
 
     auto coords = [&](int tile, TileCoord& t) {
-      const int m_tile = tile / a.n_tiles, n_tile = tile - m_tile * a.n_tiles;
+      const int m_tile = a.n_tiles == 1 ? tile : tile / a.n_tiles;
+      const int n_tile = tile - m_tile * a.n_tiles;
       t.n0 = n_tile * a.BN;
       t.img = 0;
       t.oy0 = 0;
@@ -556,8 +646,8 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
     uint32_t lc = 0;  // this group's tile count
     for (int tile = tile0; tile < total_tiles; tile += tstep, lc++) {
       const uint32_t lt = 2 * lc + (uint32_t)e;
-      const uint32_t acc = lt & (uint32_t)(a.nacc - 1), ar = lt / (uint32_t)a.nacc;
-      const uint32_t sbi = lc % (uint32_t)a.nsbuf;
+      const uint32_t acc = lt & (uint32_t)(a.nacc - 1), ar = lt >> (a.nacc == 4 ? 2 : 1);
+      const uint32_t sbi = a.nsbuf == 2 ? (lc & 1u) : 0u;
       int ok = 0;
       if (lane == 0) {
         ok = mbar_wait(smem_u32(&accf[acc]), ar & 1u, a.err, SDX_DEV_WAIT_ACC_FULL, abort_flag) ? 1 : 0;
@@ -577,16 +667,20 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
 
       TileCoord tcd;
       coords(tile, tcd);
-      bool valid;
-      int64_t pix;
-      if (a.mode == TC_CONV) {
-        const int h = row_in_tile / a.BW, w = row_in_tile - h * a.BW;
-        const int oy = tcd.oy0 + h, ox = tcd.ox0 + w;
-        valid = oy < a.OH && ox < a.OW;
-        pix = ((int64_t)tcd.img * a.OH + oy) * a.OW + ox;
-      } else {
-        pix = (int64_t)tcd.m0 + row_in_tile;
-        valid = pix < a.M;
+      // output pixel of this row: only the per-thread paths (no TMA store, or a residual that TMA
+      // cannot stage) need it
+      bool valid = false;
+      int64_t pix = 0;
+      if (!a.tma_out || (a.res && !a.tma_res)) {
+        if (a.mode == TC_CONV) {
+          const int h = row_in_tile / a.BW, w = row_in_tile - h * a.BW;
+          const int oy = tcd.oy0 + h, ox = tcd.ox0 + w;
+          valid = oy < a.OH && ox < a.OW;
+          pix = ((int64_t)tcd.img * a.OH + oy) * a.OW + ox;
+        } else {
+          pix = (int64_t)tcd.m0 + row_in_tile;
+          valid = pix < a.M;
+        }
       }
       const uint32_t slab = stage0 + sbi * a.sbuf_bytes;
       const uint32_t srow = slab + (uint32_t)lane * P;
@@ -633,7 +727,7 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
             if (a.nsbuf == 2) bulk_wait_read1();
             else bulk_wait_read0();
             if (a.tma_res) {
-              issue_res(tile + tstep, (lc + 1) % (uint32_t)a.nsbuf);
+              issue_res(tile + tstep, a.nsbuf == 2 ? ((lc + 1) & 1u) : 0u);
               res_pending = true;
             }
           }
@@ -644,7 +738,7 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
     if (lane == 0) {
       if (res_pending) {
         // wind-down after an abort: the residual copy in flight must land before smem goes away
-        const uint32_t buf = lc % (uint32_t)a.nsbuf;
+        const uint32_t buf = a.nsbuf == 2 ? (lc & 1u) : 0u;
         mbar_wait_drain(smem_u32(&resb[(e * 2 + buf) * 4 + q]), (res_phase >> buf) & 1u, a.err, SDX_DEV_WAIT_DRAIN);
       }
       if (a.tma_out) bulk_wait_all();
@@ -746,10 +840,34 @@ static int launch_tc(int dev, int grid, size_t smem, cudaStream_t stream, const 
   return SDX_OK;
 }
 
+// Channel block of a K-long reduction: 64 channels (128-byte rows) when K pads to a multiple of 64,
+// else 32 or 16, so at most 15 zero channels are padded in.
+int tc_kblk(int K) {
+  const int r = (K + 15) / 16 * 16;
+  return r % 64 == 0 ? 64 : r % 32 == 0 ? 32 : 16;
+}
+
+static int tc_kpad(int K) {
+  const int kb = tc_kblk(K);
+  return (K + kb - 1) / kb * kb;
+}
+
+static CUtensorMapSwizzle swizzle_of(int row_bytes) {
+  return row_bytes == 128 ? CU_TENSOR_MAP_SWIZZLE_128B : row_bytes == 64 ? CU_TENSOR_MAP_SWIZZLE_64B
+                                                                          : CU_TENSOR_MAP_SWIZZLE_32B;
+}
+
+static size_t b_stage_bytes_of(const TcArgs& a) {
+  return a.b_resident ? 0 : (size_t)a.wterms * a.b_taps * a.BN * a.kblk * 2;
+}
+
+static size_t smem_fixed(const TcArgs& a) {
+  return 1024 + (size_t)TC_EPI_GROUPS * a.nsbuf * a.sbuf_bytes + (((size_t)a.bias_smem * 4 + 15) & ~(size_t)15) +
+         8 * (2 * TC_MAX_STAGES + 26) + 16 + (a.b_resident ? (size_t)a.b_total_bytes : 0);
+}
+
 static size_t smem_bytes(const TcArgs& a) {
-  return 1024 + (size_t)a.stages * (a.a_stage_bytes + 2 * (size_t)a.b_taps * a.BN * TC_BK * 2) +
-         (size_t)TC_EPI_GROUPS * a.nsbuf * a.sbuf_bytes + (((size_t)a.bias_smem * 4 + 15) & ~(size_t)15) +
-         8 * (2 * a.stages + 25) + 16;
+  return smem_fixed(a) + (size_t)a.stages * (a.a_stage_bytes + b_stage_bytes_of(a));
 }
 
 int tc_launch(const TcProblem& p, cudaStream_t stream) {
@@ -759,14 +877,17 @@ int tc_launch(const TcProblem& p, cudaStream_t stream) {
   int BN, n_tiles;
   if (convt) tc_plan_n_convt(p.convt_kh, p.convt_kw, p.convt_oc, &BN, &n_tiles);
   else tc_plan_n(p.N, &BN, &n_tiles);
-  const int kpad = (p.K + TC_BK - 1) / TC_BK * TC_BK;
+  const int kblk = tc_kblk(p.K), kpad = tc_kpad(p.K);
+  const int kbytes = kblk * 2;
   TcArgs a;
   memset(&a, 0, sizeof(a));
   a.mode = p.mode;
   a.N = p.N;
   a.BN = BN;
   a.n_tiles = n_tiles;
-  a.kb_per_tap = kpad / TC_BK;
+  a.kblk = kblk;
+  a.kb_per_tap = kpad / kblk;
+  a.wterms = p.wterms == 1 ? 1 : 2;
   a.taps = p.mode == TC_CONV ? p.kh * p.kw : 1;
   a.kw = p.kw;
   a.pad_t = p.pad_t;
@@ -805,13 +926,18 @@ int tc_launch(const TcProblem& p, cudaStream_t stream) {
   memset(&mRes, 0, sizeof(mRes));
   if (p.mode == TC_CONV) {
     if (p.C % 8 != 0) return set_error(SDX_ERR_INVALID, "tc conv: input channels must be a multiple of 8");
-    // halo mode for kh > 1: tile widths of at least 8 pixels keep the row offsets 1024-aligned;
-    // used when three stages of it (A box + kh weight taps, two terms) and the staging fit
-    const size_t halo_stage = (size_t)(TC_BM / 8 + p.kh - 1) * 8 * TC_BK * 2 + 2 * (size_t)p.kh * BN * TC_BK * 2;
-    const size_t staging_max = (size_t)TC_EPI_GROUPS * TC_BM * BN * (p.out_f32 ? 4 : 2);
-    const bool halo = p.kh > 1 && p.kh - 1 + TC_BM / 8 <= 256 && 3 * halo_stage + staging_max + 4096 <= (size_t)TC_SMEM_LIMIT;
+    // halo mode for kh > 1: tile widths of at least 8 pixels make the row offsets whole swizzle
+    // atoms; used when three stages of it (A box + kh weight taps, two terms) and the staging fit,
+    // or the weights fit resident beside three A boxes
     int BH, BW;
-    pick_pixel_tile(p.OH, p.OW, halo ? 8 : 1, halo ? p.kh - 1 : 0, &BH, &BW);
+    pick_pixel_tile(p.OH, p.OW, 8, p.kh - 1, &BH, &BW);
+    const size_t halo_a = (size_t)(BH + p.kh - 1) * BW * kbytes;
+    const size_t staging_max = (size_t)TC_EPI_GROUPS * TC_BM * BN * (p.out_f32 ? 4 : 2);
+    const size_t b_all = (size_t)a.wterms * p.kh * p.kw * (kpad / kblk) * n_tiles * BN * kbytes;
+    const bool halo = p.kh > 1 && BH + p.kh - 1 <= 256 &&
+                      (3 * (halo_a + (size_t)a.wterms * p.kh * BN * kbytes) + staging_max + 4096 <= (size_t)TC_SMEM_LIMIT ||
+                       b_all + 3 * halo_a + staging_max + 4096 <= (size_t)TC_SMEM_LIMIT);
+    if (!halo) pick_pixel_tile(p.OH, p.OW, 1, 0, &BH, &BW);
     a.halo = halo ? 1 : 0;
     a.b_taps = halo ? p.kh : 1;
     a.BH = BH;
@@ -822,31 +948,31 @@ int tc_launch(const TcProblem& p, cudaStream_t stream) {
     a.tiles_w = (p.OW + BW - 1) / BW;
     a.m_tiles = p.batch * a.tiles_h * a.tiles_w;
     const int box_h = halo ? BH + p.kh - 1 : BH;
-    a.a_box_bytes = (uint32_t)box_h * BW * TC_BK * 2;
-    a.a_stage_bytes = std::max<uint32_t>(TC_A_STAGE_BYTES, (a.a_box_bytes + 1023u) & ~1023u);
+    a.a_box_bytes = (uint32_t)(box_h * BW * kbytes);
+    a.a_stage_bytes = (a.a_box_bytes + 1023u) & ~1023u;
     uint64_t dims[4] = {(uint64_t)p.C, (uint64_t)p.W, (uint64_t)p.H, (uint64_t)p.batch};
     uint64_t strides[3] = {(uint64_t)p.C * 2, (uint64_t)p.W * p.C * 2, (uint64_t)p.H * p.W * p.C * 2};
-    uint32_t box[4] = {TC_BK, (uint32_t)BW, (uint32_t)box_h, 1};
-    int rc = encode_map(&mA, p.a, 4, dims, strides, box);
+    uint32_t box[4] = {(uint32_t)kblk, (uint32_t)BW, (uint32_t)box_h, 1};
+    int rc = encode_map(&mA, p.a, 4, dims, strides, box, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, swizzle_of(kbytes));
     if (rc) return rc;
   } else {
     if (p.lda % 8 != 0) return set_error(SDX_ERR_INVALID, "tc rows: A row stride must be a multiple of 8 halves");
     a.M = p.M;
     a.m_tiles = (p.M + TC_BM - 1) / TC_BM;
-    a.a_box_bytes = TC_A_STAGE_BYTES;
-    a.a_stage_bytes = TC_A_STAGE_BYTES;
+    a.a_box_bytes = (uint32_t)(TC_BM * kbytes);
+    a.a_stage_bytes = (a.a_box_bytes + 1023u) & ~1023u;
     a.b_taps = 1;
     uint64_t dims[2] = {(uint64_t)p.K, (uint64_t)p.M};
     uint64_t strides[1] = {(uint64_t)p.lda * 2};
-    uint32_t box[2] = {TC_BK, TC_BM};
-    int rc = encode_map(&mA, p.a, 2, dims, strides, box);
+    uint32_t box[2] = {(uint32_t)kblk, TC_BM};
+    int rc = encode_map(&mA, p.a, 2, dims, strides, box, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, swizzle_of(kbytes));
     if (rc) return rc;
   }
   {
-    uint64_t dims[2] = {(uint64_t)kpad, 2ull * a.taps * a.b_rows_per_tap};
+    uint64_t dims[2] = {(uint64_t)kpad, (uint64_t)a.wterms * a.taps * a.b_rows_per_tap};
     uint64_t strides[1] = {(uint64_t)kpad * 2};
-    uint32_t box[2] = {TC_BK, (uint32_t)BN};
-    int rc = encode_map(&mB, p.w, 2, dims, strides, box);
+    uint32_t box[2] = {(uint32_t)kblk, (uint32_t)BN};
+    int rc = encode_map(&mB, p.w, 2, dims, strides, box, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, swizzle_of(kbytes));
     if (rc) return rc;
   }
 
@@ -927,21 +1053,27 @@ int tc_launch(const TcProblem& p, cudaStream_t stream) {
   }
 
   if (p.bias && BN * n_tiles <= TC_BIAS_SMEM_MAX) a.bias_smem = BN * n_tiles;
-  // ---- pipeline depth from the shared-memory budget (2 staging buffers when they fit)
-  a.nsbuf = a.tma_out ? 2 : 1;
+  // ---- shared-memory plan. Preference: weights resident (loaded once per CTA) with 2 staging
+  // buffers and >= 3 A stages, resident with 1 staging buffer and >= 2 stages, then streamed
+  // weights (per stage) likewise. 8 stages at most.
   if (!a.tma_out) a.sbuf_bytes = 0;
-  for (;;) {
-    const size_t fixed = 1024 + (size_t)TC_EPI_GROUPS * a.nsbuf * a.sbuf_bytes +
-                         (((size_t)a.bias_smem * 4 + 15) & ~(size_t)15) + 8 * (2 * TC_MAX_STAGES + 25) + 16;
-    const size_t per = a.a_stage_bytes + 2 * (size_t)a.b_taps * BN * TC_BK * 2;
-    const size_t room = fixed < (size_t)TC_SMEM_LIMIT ? (size_t)TC_SMEM_LIMIT - fixed : 0;
-    const int st = (int)std::min<size_t>(TC_MAX_STAGES, room / per);
-    if (st >= 2 || a.nsbuf <= 1) {
-      a.stages = std::max(2, st);
-      break;
+  a.b_total_bytes = (uint32_t)((size_t)a.wterms * a.taps * a.kb_per_tap * n_tiles * BN * kbytes);
+  bool planned = false;
+  for (int res = 1; res >= 0 && !planned; res--) {
+    for (int nsb = a.tma_out ? 2 : 1; nsb >= 1 && !planned; nsb--) {
+      a.b_resident = res;
+      a.nsbuf = nsb;
+      const size_t fixed = smem_fixed(a);
+      const size_t per = a.a_stage_bytes + b_stage_bytes_of(a);
+      if (fixed >= (size_t)TC_SMEM_LIMIT) continue;
+      const int st = (int)std::min<size_t>(TC_MAX_STAGES, ((size_t)TC_SMEM_LIMIT - fixed) / per);
+      if (st >= (nsb == 2 ? 3 : 2)) {
+        a.stages = st;
+        planned = true;
+      }
     }
-    a.nsbuf = 1;
   }
+  if (!planned) return set_error(SDX_ERR_NOT_SUPPORTED, "tc: shared memory plan too large");
   const size_t smem = smem_bytes(a);
   if (smem > (size_t)TC_SMEM_LIMIT) return set_error(SDX_ERR_NOT_SUPPORTED, "tc: shared memory plan too large");
 
@@ -959,17 +1091,17 @@ int tc_launch(const TcProblem& p, cudaStream_t stream) {
 
 // Packs ONNX conv weights w [OC][IC][KH][KW] (fp32) into the B operand [2][taps][n_tiles*BN][ICpad]
 // fp16 (hi terms, then lo terms), zero padded.
-size_t tc_weights_halves(int N, int K, int taps) {
+size_t tc_weights_halves(int N, int K, int taps, int terms) {
   int BN, nt;
   tc_plan_n(N, &BN, &nt);
-  size_t kpad = (size_t)(K + TC_BK - 1) / TC_BK * TC_BK;
-  return 2 * (size_t)taps * BN * nt * kpad;
+  size_t kpad = (size_t)tc_kpad(K);
+  return (size_t)(terms == 1 ? 1 : 2) * taps * BN * nt * kpad;
 }
 
 size_t tc_convt_weights_halves(int IC, int OC, int KH, int KW) {
   int BN, nt;
   tc_plan_n_convt(KH, KW, OC, &BN, &nt);
-  size_t kpad = (size_t)(IC + TC_BK - 1) / TC_BK * TC_BK;
+  size_t kpad = (size_t)tc_kpad(IC);
   return 2 * (size_t)BN * nt * kpad;
 }
 
@@ -980,16 +1112,22 @@ static inline void put2(__half* out, size_t idx, size_t lo_off, float w) {
   out[idx + lo_off] = __float2half_rn(w - __half2float(h));
 }
 
-void tc_pack_conv(const float* w, int OC, int IC, int KH, int KW, __half* out) {
+// terms == 1: only the hi block (w rounded to fp16).
+void tc_pack_conv(const float* w, int OC, int IC, int KH, int KW, int terms, __half* out) {
   int BN, nt;
   tc_plan_n(OC, &BN, &nt);
-  const size_t rows = (size_t)BN * nt, kpad = (size_t)(IC + TC_BK - 1) / TC_BK * TC_BK;
+  const size_t rows = (size_t)BN * nt, kpad = (size_t)tc_kpad(IC);
   const int taps = KH * KW;
   const size_t lo = (size_t)taps * rows * kpad;
-  memset(out, 0, sizeof(__half) * 2 * lo);
+  memset(out, 0, sizeof(__half) * (terms == 1 ? 1 : 2) * lo);
   for (int o = 0; o < OC; o++)
     for (int c = 0; c < IC; c++)
-      for (int t = 0; t < taps; t++) put2(out, ((size_t)t * rows + o) * kpad + c, lo, w[((size_t)o * IC + c) * taps + t]);
+      for (int t = 0; t < taps; t++) {
+        const size_t idx = ((size_t)t * rows + o) * kpad + c;
+        const float v = w[((size_t)o * IC + c) * taps + t];
+        if (terms == 1) out[idx] = __float2half_rn(v);
+        else put2(out, idx, lo, v);
+      }
 }
 
 // ConvT weights [IC][OC][KH][KW] -> one GEMM panel whose row tap*OC + o is w[:, o, tap].
@@ -997,7 +1135,7 @@ void tc_pack_convt(const float* w, int IC, int OC, int KH, int KW, __half* out) 
   const int taps = KH * KW;
   int BN, nt;
   tc_plan_n_convt(KH, KW, OC, &BN, &nt);
-  const size_t rows = (size_t)BN * nt, kpad = (size_t)(IC + TC_BK - 1) / TC_BK * TC_BK;
+  const size_t rows = (size_t)BN * nt, kpad = (size_t)tc_kpad(IC);
   const size_t lo = rows * kpad;
   memset(out, 0, sizeof(__half) * 2 * lo);
   for (int c = 0; c < IC; c++)
@@ -1008,7 +1146,7 @@ void tc_pack_convt(const float* w, int IC, int OC, int KH, int KW, __half* out) 
 void tc_pack_gemm(const float* b, int K, int N, int trans_b, __half* out) {
   int BN, nt;
   tc_plan_n(N, &BN, &nt);
-  const size_t rows = (size_t)BN * nt, kpad = (size_t)(K + TC_BK - 1) / TC_BK * TC_BK;
+  const size_t rows = (size_t)BN * nt, kpad = (size_t)tc_kpad(K);
   const size_t lo = rows * kpad;
   memset(out, 0, sizeof(__half) * 2 * lo);
   for (int n = 0; n < N; n++)

@@ -441,14 +441,22 @@ static int conv_route(const sdx_conv_desc* d) {
   return R_INVALID;
 }
 
+// fp16 weight terms of a tensor-core conv: the caller's choice, else two for 1x1 kernels (their MMAs
+// hide under HBM time) and one for larger kernels (MMA-bound)
+static int conv_wterms(const sdx_conv_desc* d) {
+  if (d->w_terms == 1 || d->w_terms == 2) return d->w_terms;
+  return d->kh * d->kw > 1 ? 1 : 2;
+}
+
 int sdx_pack_conv(const sdx_conv_desc* d, const float* w, void* out, size_t* bytes) {
   if (!d || !bytes) return set_error(SDX_ERR_INVALID, "null argument");
+  if (d->w_terms < 0 || d->w_terms > 2) return set_error(SDX_ERR_INVALID, "conv: w_terms must be 0, 1 or 2");
   const int route = conv_route(d);
   const int taps = d->kh * d->kw;
   size_t need = 0;
   switch (route) {
     case R_TC_CONV:
-    case R_TC_ROWS: need = tc_weights_halves(d->oc, d->ic, taps) * sizeof(__half); break;
+    case R_TC_ROWS: need = tc_weights_halves(d->oc, d->ic, taps, conv_wterms(d)) * sizeof(__half); break;
     case R_DEPTHWISE: need = sizeof(float) * (size_t)taps * d->ic; break;
     case R_DIRECT: need = sizeof(float) * (size_t)taps * d->ic * d->oc; break;
     default: return set_error(SDX_ERR_NOT_SUPPORTED, "conv: no CUDA kernel for this shape/flags");
@@ -460,7 +468,7 @@ int sdx_pack_conv(const sdx_conv_desc* d, const float* w, void* out, size_t* byt
   if (*bytes < need) return set_error(SDX_ERR_INVALID, "pack buffer too small");
   if (!w) return set_error(SDX_ERR_INVALID, "null weights");
   if (route == R_TC_CONV || route == R_TC_ROWS) {
-    tc_pack_conv(w, d->oc, d->ic, d->kh, d->kw, static_cast<__half*>(out));
+    tc_pack_conv(w, d->oc, d->ic, d->kh, d->kw, conv_wterms(d), static_cast<__half*>(out));
   } else if (route == R_DEPTHWISE) {
     float* o = static_cast<float*>(out);
     for (int c = 0; c < d->ic; c++)
@@ -491,7 +499,7 @@ int sdx_pack_convt(int ic, int oc, int kh, int kw, const float* w, void* out, si
 
 int sdx_pack_gemm(int k, int n, int trans_b, const float* b, void* out, size_t* bytes) {
   if (!bytes) return set_error(SDX_ERR_INVALID, "null argument");
-  size_t need = tc_weights_halves(n, k, 1) * sizeof(__half);
+  size_t need = tc_weights_halves(n, k, 1, 2) * sizeof(__half);
   if (!out) {
     *bytes = need;
     return SDX_OK;
@@ -510,6 +518,7 @@ int sdx_conv2d(sdx_ctx* ctx, const sdx_conv_desc* d, sdx_stream s) {
   if (!d) return set_error(SDX_ERR_INVALID, "null desc");
   LAUNCH_GUARD();
   if (d->batch <= 0 || d->oh <= 0 || d->ow <= 0) return set_error(SDX_ERR_INVALID, "conv: empty shape");
+  if (d->w_terms < 0 || d->w_terms > 2) return set_error(SDX_ERR_INVALID, "conv: w_terms must be 0, 1 or 2");
   // output size must follow the ONNX formula (src/Engine/GraphCompiler.cs:1790-1794)
   const int oh = (d->ih + d->pad_t + d->pad_b - d->kh) / d->sh + 1, ow = (d->iw + d->pad_l + d->pad_r - d->kw) / d->sw + 1;
   if (oh != d->oh || ow != d->ow) return set_error(SDX_ERR_INVALID, "conv: output %dx%d, expected %dx%d", d->oh, d->ow, oh, ow);
@@ -537,6 +546,7 @@ int sdx_conv2d(sdx_ctx* ctx, const sdx_conv_desc* d, sdx_stream s) {
       p.pad_t = d->pad_t;
       p.pad_l = d->pad_l;
       p.w = P<const __half>(d->w);
+      p.wterms = conv_wterms(d);
       p.N = d->oc;
       p.bias = P<const float>(d->bias);
       p.res = P<const void>(d->add);
@@ -602,6 +612,7 @@ int sdx_gemm(sdx_ctx* ctx, const sdx_gemm_desc* d, sdx_stream s) {
   p.M = d->m;
   p.K = d->k;
   p.w = P<const __half>(d->w);
+  p.wterms = 2;
   p.N = d->n;
   p.bias = P<const float>(d->bias);
   p.res = P<const void>(d->add);
@@ -639,6 +650,7 @@ int sdx_convt(sdx_ctx* ctx, const sdx_convt_desc* d, sdx_stream s) {
     p.kh = 1;
     p.kw = 1;
     p.w = P<const __half>(d->w);
+    p.wterms = 2;
     p.N = d->kh * d->kw * d->oc;
     p.bias = P<const float>(d->bias);
     p.out = P<void>(d->y);

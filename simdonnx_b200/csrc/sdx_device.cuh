@@ -175,15 +175,15 @@ __device__ __forceinline__ void tc_commit(uint32_t bar) {
   asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(bar) : "memory");
 }
 
-// D[tmem] (+)= A[smem desc] * B[smem desc]^T, f16 inputs, f32 accumulation.
+// D[tmem] (+)= A[smem desc] * B[smem desc]^T, f16 inputs, f32 accumulation. No memory clobber: the
+// operands are ordered by the mbarrier waits (which carry one) and volatile asm keeps program order.
 __device__ __forceinline__ void umma_f16(uint32_t d_tmem, uint64_t a_desc, uint64_t b_desc, uint32_t idesc,
                                          uint32_t accumulate) {
   asm volatile(
       "{\n\t.reg .pred p;\n\t"
       "setp.ne.b32 p, %4, 0;\n\t"
       "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n\t}" ::"r"(d_tmem),
-      "l"(a_desc), "l"(b_desc), "r"(idesc), "r"(accumulate)
-      : "memory");
+      "l"(a_desc), "l"(b_desc), "r"(idesc), "r"(accumulate));
 }
 
 // Shared-memory matrix descriptor (tcgen05 format): K-major operand in the 128-byte swizzled
@@ -195,6 +195,19 @@ __device__ __forceinline__ uint64_t umma_desc_sw128(uint32_t smem_addr) {
   d |= (uint64_t)(1024u >> 4) << 32;            // stride byte offset: 8 rows x 128 B
   d |= (uint64_t)1u << 46;                      // descriptor version (sm_100)
   d |= (uint64_t)2u << 61;                      // SWIZZLE_128B
+  return d;
+}
+
+// K-major operand whose rows are `row_bytes` (32, 64 or 128) long and stored under the TMA swizzle of
+// the same span (SWIZZLE_32B / 64B / 128B): 8-row core-matrix groups 8 * row_bytes apart.
+__device__ __forceinline__ uint64_t umma_desc_kmajor(uint32_t smem_addr, uint32_t row_bytes) {
+  const uint64_t layout = row_bytes == 128u ? 2u : row_bytes == 64u ? 4u : 6u;
+  uint64_t d = 0;
+  d |= (uint64_t)((smem_addr >> 4) & 0x3FFFu);   // start address, bits [0,14)
+  d |= (uint64_t)1u << 16;                       // leading byte offset (unused for swizzled K-major)
+  d |= (uint64_t)((8u * row_bytes) >> 4) << 32;  // stride byte offset: 8 rows
+  d |= (uint64_t)1u << 46;                       // descriptor version (sm_100)
+  d |= layout << 61;                             // swizzle mode
   return d;
 }
 

@@ -45,6 +45,7 @@ struct TcProblem {
   // B: packed weights (tc_pack_*)
   const __half* w;
   int N;
+  int wterms;  // fp16 weight terms in w: 1, or 2 (hi, lo)
   // epilogue
   const float* bias;
   const void* res;
@@ -61,10 +62,10 @@ struct TcProblem {
 };
 void tc_plan_n(int N, int* BN, int* n_tiles);
 int tc_launch(const TcProblem& p, cudaStream_t stream);
-size_t tc_weights_halves(int N, int K, int taps);
+size_t tc_weights_halves(int N, int K, int taps, int terms);
 size_t tc_convt_weights_halves(int IC, int OC, int KH, int KW);
 void tc_plan_n_convt(int kh, int kw, int OC, int* BN, int* n_tiles);
-void tc_pack_conv(const float* w, int OC, int IC, int KH, int KW, __half* out);
+void tc_pack_conv(const float* w, int OC, int IC, int KH, int KW, int terms, __half* out);
 void tc_pack_convt(const float* w, int IC, int OC, int KH, int KW, __half* out);
 void tc_pack_gemm(const float* b, int K, int N, int trans_b, __half* out);
 

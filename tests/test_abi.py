@@ -49,16 +49,21 @@ def test_fault_injection_is_host_side():
 
 
 def test_pack_sizes_cpu():
-    # packing is host code: sizes follow the tile plan (N padded to 16, K to 64)
+    # packing is host code: sizes follow the tile plan (N padded to 16, K to the channel block)
     from simdonnx_b200 import backend as B
     import torch
     d = B.conv_desc(1, 8, 8, 64, 64, 3, 3, pads=(1, 1, 1, 1))
     nb = ctypes.c_size_t()
     N.call("sdx_pack_conv", ctypes.byref(d), None, None, ctypes.byref(nb))
-    assert nb.value == 2 * 9 * 64 * 64 * 2  # hi + lo fp16 terms
-    d = B.conv_desc(1, 8, 8, 96, 24, 3, 3, pads=(1, 1, 1, 1))
+    assert nb.value == 9 * 64 * 64 * 2  # k x k kernels default to one fp16 weight term
+    d.w_terms = 2
     N.call("sdx_pack_conv", ctypes.byref(d), None, None, ctypes.byref(nb))
-    assert nb.value == 2 * 9 * 32 * 128 * 2
+    assert nb.value == 2 * 9 * 64 * 64 * 2  # hi + lo fp16 terms
+    d = B.conv_desc(1, 8, 8, 96, 24, 1, 1)
+    N.call("sdx_pack_conv", ctypes.byref(d), None, None, ctypes.byref(nb))
+    assert nb.value == 2 * 32 * 96 * 2  # 1x1: two terms; 96 channels: 32-channel blocks, no K padding
+    d.w_terms = 3
+    assert N.lib().sdx_pack_conv(ctypes.byref(d), None, None, ctypes.byref(nb)) == 1
     d = B.conv_desc(1, 8, 8, 3, 16, 3, 3, stride=(2, 2), pads=(1, 1, 1, 1), x_dtype=torch.float32, x_layout=1)
     N.call("sdx_pack_conv", ctypes.byref(d), None, None, ctypes.byref(nb))
     assert nb.value == 9 * 3 * 16 * 4

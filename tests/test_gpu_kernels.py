@@ -75,8 +75,9 @@ CONV_CASES = [
 ]
 
 
+@pytest.mark.parametrize("w_terms", [0, 2])
 @pytest.mark.parametrize("ic,oc,k,s,h,w,residual,act", CONV_CASES)
-def test_conv_shapes(be, ic, oc, k, s, h, w, residual, act):
+def test_conv_shapes(be, ic, oc, k, s, h, w, residual, act, w_terms):
     from simdonnx_b200 import backend as B
     rng = np.random.default_rng(ic * 131 + oc * 7 + k)
     n, p = 2, k // 2
@@ -86,9 +87,9 @@ def test_conv_shapes(be, ic, oc, k, s, h, w, residual, act):
     oh, ow = (h + 2 * p - k) // s + 1, (w + 2 * p - k) // s + 1
     res = rnd(rng, n, oh, ow, oc) if residual else None
     ref = O.conv(x, O.ConvPlan(wt, b, winograd=False), strides=(s, s), pads=(p, p, p, p), act=act, add=res)
-    d = B.conv_desc(n, h, w, ic, oc, k, k, stride=(s, s), pads=(p, p, p, p), act=act)
+    d = B.conv_desc(n, h, w, ic, oc, k, k, stride=(s, s), pads=(p, p, p, p), act=act, w_terms=w_terms)
     y = B.conv2d(be, d, dev16(x), B.pack_conv(d, wt), bias=dev32(b), add=None if res is None else dev16(res))
-    assert_close(host(y), ref, f"conv {ic}->{oc} k{k} s{s}")
+    assert_close(host(y), ref, f"conv {ic}->{oc} k{k} s{s} terms {w_terms}")
 
 
 def test_conv_into_channel_slice(be):
