@@ -71,7 +71,9 @@ struct TcArgs {
   int halo;             // TC_CONV: one A box per (kx, channel block) holds the BH + kh - 1 input rows
                         // of all kh row taps; the MMAs of tap (ky, kx) read it from row ky * BW on
   int b_taps;           // weight taps per stage (kh in halo mode, else 1)
-  uint32_t a_stage_bytes;  // bytes of one A stage (1024-aligned)
+  uint32_t a_stage_bytes;  // bytes of one A stage: cps boxes of a_blk_bytes
+  uint32_t a_blk_bytes;    // one channel block's A box, rounded up to 1024 bytes
+  int cps;              // channel blocks per pipeline stage (divides kb_per_tap)
   int kblk;             // channels per k-block: 64, 32 or 16 (rows of 128/64/32 B, same-span swizzle)
   int b_resident;       // 1: all weights are loaded into shared memory once per CTA
   int wterms;           // fp16 weight terms: 1 (w) or 2 (hi, lo: two MMAs per k-step)
@@ -224,16 +226,42 @@ __device__ __forceinline__ void warp_copy(const TcArgs& a, const CUtensorMap* ma
   }
 }
 
-// NK k-steps of 16 channels: each multiplies the A rows by the weight term (TWO: by both terms,
-// hi then lo) into the same accumulator; `first` = 0 makes the very first MMA of a tile overwrite
-// the accumulator.
-template <int NK, bool TWO>
-__device__ __forceinline__ void umma_steps(uint32_t d, uint64_t ad, uint64_t bdh, uint64_t bdl, uint32_t idesc,
-                                           uint32_t first) {
+// The MMAs of one pipeline stage, fully unrolled (the issuing thread's scalar work between MMAs is
+// its bottleneck for small N): BT taps x NK k-steps of 16 channels, each multiplying the A rows by
+// the weight term (TWO: both terms, hi then lo). Descriptors advance by constant strides given in
+// 16-byte units: A by `a_tap` per tap, B by `b_tap` per tap and `b_lo` to the lo term.
+// `first` = 0 makes the first MMA of a tile overwrite the accumulator.
+template <int BT, int NK, bool TWO>
+__device__ __forceinline__ void umma_stage(uint32_t d, uint64_t ad, uint64_t bd, uint32_t a_tap, uint32_t b_tap,
+                                           uint32_t b_lo, uint32_t idesc, uint32_t first) {
 #pragma unroll
-  for (int k = 0; k < NK; k++) {
-    umma_f16(d, ad + 2u * k, bdh + 2u * k, idesc, k == 0 ? first : 1u);
-    if (TWO) umma_f16(d, ad + 2u * k, bdl + 2u * k, idesc, 1u);
+  for (int j = 0; j < BT; j++) {
+#pragma unroll
+    for (int k = 0; k < NK; k++) {
+      const uint64_t a = ad + (uint64_t)(j * a_tap + 2u * k), b = bd + (uint64_t)(j * b_tap + 2u * k);
+      umma_f16(d, a, b, idesc, (j == 0 && k == 0) ? first : 1u);
+      if (TWO) umma_f16(d, a, b + b_lo, idesc, 1u);
+    }
+  }
+}
+
+template <bool TWO>
+__device__ __forceinline__ void umma_stage_dispatch(int bt, int nk, uint32_t d, uint64_t ad, uint64_t bd, uint32_t a_tap,
+                                                    uint32_t b_tap, uint32_t b_lo, uint32_t idesc, uint32_t first) {
+  if (bt == 1) {
+    if (nk == 4) umma_stage<1, 4, TWO>(d, ad, bd, a_tap, b_tap, b_lo, idesc, first);
+    else if (nk == 2) umma_stage<1, 2, TWO>(d, ad, bd, a_tap, b_tap, b_lo, idesc, first);
+    else umma_stage<1, 1, TWO>(d, ad, bd, a_tap, b_tap, b_lo, idesc, first);
+  } else if (bt == 3) {
+    if (nk == 4) umma_stage<3, 4, TWO>(d, ad, bd, a_tap, b_tap, b_lo, idesc, first);
+    else if (nk == 2) umma_stage<3, 2, TWO>(d, ad, bd, a_tap, b_tap, b_lo, idesc, first);
+    else umma_stage<3, 1, TWO>(d, ad, bd, a_tap, b_tap, b_lo, idesc, first);
+  } else {
+    for (int j = 0; j < bt; j++) {
+      if (nk == 4) umma_stage<1, 4, TWO>(d, ad + (uint64_t)(j * a_tap), bd + (uint64_t)(j * b_tap), 0, 0, b_lo, idesc, j == 0 ? first : 1u);
+      else if (nk == 2) umma_stage<1, 2, TWO>(d, ad + (uint64_t)(j * a_tap), bd + (uint64_t)(j * b_tap), 0, 0, b_lo, idesc, j == 0 ? first : 1u);
+      else umma_stage<1, 1, TWO>(d, ad + (uint64_t)(j * a_tap), bd + (uint64_t)(j * b_tap), 0, 0, b_lo, idesc, j == 0 ? first : 1u);
+    }
   }
 }
 
@@ -374,7 +402,8 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
   const int S = a.stages;
   const uint32_t kbytes = (uint32_t)a.kblk * 2;                          // operand row bytes
   const uint32_t b_tap_bytes = (uint32_t)a.BN * kbytes;                  // one tap, one weight term
-  const uint32_t b_half_bytes = b_tap_bytes * (uint32_t)a.b_taps;        // all taps of a stage, one term
+  const uint32_t b_cb_bytes = b_tap_bytes * (uint32_t)a.b_taps;          // one channel block: its taps, one term
+  const uint32_t b_half_bytes = b_cb_bytes * (uint32_t)a.cps;            // one term of a stage
   const uint32_t b_stage_bytes = a.b_resident ? 0u : (uint32_t)a.wterms * b_half_bytes;
   uint8_t* sA = smem;
   uint8_t* sB = smem + (size_t)S * a.a_stage_bytes;  // resident: all weights; else S weight stages
@@ -428,7 +457,8 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
 
   const int total_tiles = a.m_tiles * a.n_tiles;
   // pipeline stages per tile: (tap, channel block), or (kx, channel block) in halo mode
-  const int kblocks = (a.halo ? a.kw : a.taps) * a.kb_per_tap;
+  const int groups = a.kb_per_tap / a.cps;  // channel-block groups per tap
+  const int kblocks = (a.halo ? a.kw : a.taps) * groups;
 
   // weight block (term, tap, channel block, n tile) in the resident layout
   auto b_res_off = [&](int term, int tap, int cb, int nt) -> uint32_t {
@@ -467,38 +497,43 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
           oy0 = ty * a.BH;
           ox0 = (r - ty * a.tiles_w) * a.BW;
         }
-        int tk = 0, cb = 0;  // tk: tap, or kx in halo mode
+        int tk = 0, cg = 0;  // tk: tap, or kx in halo mode; cg: channel-block group
         for (int kb = 0; kb < kblocks; kb++) {
           if (!mbar_wait(smem_u32(&empty[s]), phase ^ 1u, a.err, SDX_DEV_WAIT_EMPTY, abort_flag)) {
             ok = false;
             break;
           }
           const uint32_t fb = smem_u32(&full[s]);
-          mbar_arrive_expect_tx(fb, a.a_box_bytes + b_stage_bytes);
-          const uint32_t dA = smem_u32(sA) + (uint32_t)s * a.a_stage_bytes;
-          const uint32_t dB = smem_u32(sB) + (uint32_t)s * b_stage_bytes;
-          if (a.halo) {
-            // rows oy0 - pt .. oy0 - pt + BH + kh - 2 of input column block kx (zero fill = padding)
-            tma_load_4d(dA, &tmA, fb, cb * a.kblk, ox0 + tk - a.pad_l, oy0 - a.pad_t, img);
-          } else if (a.mode == TC_CONV) {
-            const int ky = tk / a.kw, kx = tk - ky * a.kw;
-            tma_load_4d(dA, &tmA, fb, cb * a.kblk, ox0 + kx - a.pad_l, oy0 + ky - a.pad_t, img);
-          } else {
-            tma_load_2d(dA, &tmA, fb, cb * a.kblk, m_tile * TC_BM);
-          }
-          if (!a.b_resident) {
-            for (int j = 0; j < a.b_taps; j++) {
-              const int tap = a.halo ? j * a.kw + tk : tk;
-              const int brow = tap * a.b_rows_per_tap + n_tile * a.BN;
-              tma_load_2d(dB + j * b_tap_bytes, &tmB, fb, cb * a.kblk, brow);
-              if (a.wterms == 2)
-                tma_load_2d(dB + b_half_bytes + j * b_tap_bytes, &tmB, fb, cb * a.kblk, a.taps * a.b_rows_per_tap + brow);
+          mbar_arrive_expect_tx(fb, (uint32_t)a.cps * a.a_box_bytes + b_stage_bytes);
+          const uint32_t dA0 = smem_u32(sA) + (uint32_t)s * a.a_stage_bytes;
+          const uint32_t dB0 = smem_u32(sB) + (uint32_t)s * b_stage_bytes;
+          for (int ci = 0; ci < a.cps; ci++) {
+            const int cb = cg * a.cps + ci;
+            const uint32_t dA = dA0 + (uint32_t)ci * a.a_blk_bytes;
+            if (a.halo) {
+              // rows oy0 - pt .. oy0 - pt + BH + kh - 2 of input column block kx (zero fill = padding)
+              tma_load_4d(dA, &tmA, fb, cb * a.kblk, ox0 + tk - a.pad_l, oy0 - a.pad_t, img);
+            } else if (a.mode == TC_CONV) {
+              const int ky = tk / a.kw, kx = tk - ky * a.kw;
+              tma_load_4d(dA, &tmA, fb, cb * a.kblk, ox0 + kx - a.pad_l, oy0 + ky - a.pad_t, img);
+            } else {
+              tma_load_2d(dA, &tmA, fb, cb * a.kblk, m_tile * TC_BM);
+            }
+            if (!a.b_resident) {
+              const uint32_t dB = dB0 + (uint32_t)ci * b_cb_bytes;
+              for (int j = 0; j < a.b_taps; j++) {
+                const int tap = a.halo ? j * a.kw + tk : tk;
+                const int brow = tap * a.b_rows_per_tap + n_tile * a.BN;
+                tma_load_2d(dB + j * b_tap_bytes, &tmB, fb, cb * a.kblk, brow);
+                if (a.wterms == 2)
+                  tma_load_2d(dB + b_half_bytes + j * b_tap_bytes, &tmB, fb, cb * a.kblk, a.taps * a.b_rows_per_tap + brow);
+              }
             }
           }
           issued_mask |= 1u << s;
           last_phase = (last_phase & ~(1u << s)) | (phase << s);
-          if (++cb == a.kb_per_tap) {
-            cb = 0;
+          if (++cg == groups) {
+            cg = 0;
             tk++;
           }
           if (++s == S) {
@@ -521,7 +556,14 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
       // descriptor words: the high word (stride offset, version, swizzle) and the leading-offset
       // bits are the same for every operand; only the start address changes
       const uint64_t dconst = umma_desc_kmajor(0u, kbytes);
-      const uint32_t a_row_step = (uint32_t)a.BW * kbytes;  // halo: A rows of the next row tap
+      const uint32_t sB_addr = smem_u32(sB);
+      // strides in 16-byte descriptor units: A rows of the next row tap (halo), the next tap's
+      // weights (resident: kw taps on in the [tap][cb][n_tile] layout; streamed: the next block),
+      // and the lo weight term
+      const uint32_t a_tap16 = ((uint32_t)a.BW * kbytes) >> 4;
+      const uint32_t b_tap16 = a.b_resident ? (b_res_off(0, a.kw, 0, 0) >> 4) : (b_tap_bytes >> 4);
+      const uint32_t b_cb = a.b_resident ? b_res_off(0, 0, 1, 0) : b_cb_bytes;  // next channel block
+      const uint32_t b_lo16 = (a.b_resident ? b_res_off(1, 0, 0, 0) : b_half_bytes) >> 4;
       bool ok = !a.b_resident || mbar_wait(smem_u32(bres), 0, a.err, SDX_DEV_WAIT_FULL, abort_flag);
       if (ok) tc_fence_after();
       int s = 0;
@@ -532,7 +574,7 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
         if (!mbar_wait(smem_u32(&acce[acc]), accph ^ 1u, a.err, SDX_DEV_WAIT_ACC_EMPTY, abort_flag)) break;
         tc_fence_after();
         const uint32_t d = tmem_base + acc * (uint32_t)a.acc_stride;
-        int tk = 0, cb = 0;
+        int tk = 0, cg = 0;
         uint32_t first = 0;  // 0 until the tile's first MMA (overwrite), then 1 (accumulate)
         for (int kb = 0; kb < kblocks; kb++) {
           if (!mbar_wait(smem_u32(&full[s]), phase, a.err, SDX_DEV_WAIT_FULL, abort_flag)) {
@@ -540,41 +582,20 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
             break;
           }
           tc_fence_after();
-          const uint32_t sa = smem_u32(sA) + (uint32_t)s * a.a_stage_bytes;
-          const uint32_t sbs = smem_u32(sB) + (uint32_t)s * b_stage_bytes;
-          // tap j of the stage: A from row j * BW of the halo box (a whole number of swizzle atoms)
-          for (int j = 0; j < a.b_taps; j++) {
-            uint32_t bh, bl;
-            if (a.b_resident) {
-              const uint32_t off = b_res_off(0, a.halo ? j * a.kw + tk : tk, cb, n_tile);
-              bh = smem_u32(sB) + off;
-              bl = bh + (uint32_t)(a.taps * a.kb_per_tap * a.n_tiles) * b_tap_bytes;
-            } else {
-              bh = sbs + (uint32_t)j * b_tap_bytes;
-              bl = bh + b_half_bytes;
-            }
-            const uint64_t ad = dconst | (uint64_t)(((sa + (uint32_t)j * a_row_step) >> 4) & 0x3FFFu);
-            const uint64_t bdh = dconst | (uint64_t)((bh >> 4) & 0x3FFFu);
-            const uint64_t bdl = dconst | (uint64_t)((bl >> 4) & 0x3FFFu);
-            // k-steps unrolled: the issue loop is this thread's critical path
-            if (a.wterms == 2) {
-              switch (nk) {
-                case 4: umma_steps<4, true>(d, ad, bdh, bdl, idesc, first); break;
-                case 2: umma_steps<2, true>(d, ad, bdh, bdl, idesc, first); break;
-                default: umma_steps<1, true>(d, ad, bdh, bdl, idesc, first); break;
-              }
-            } else {
-              switch (nk) {
-                case 4: umma_steps<4, false>(d, ad, bdh, bdl, idesc, first); break;
-                case 2: umma_steps<2, false>(d, ad, bdh, bdl, idesc, first); break;
-                default: umma_steps<1, false>(d, ad, bdh, bdl, idesc, first); break;
-              }
-            }
+          // per channel block: descriptors of its first tap; the other taps are constant strides away
+          uint32_t sa = smem_u32(sA) + (uint32_t)s * a.a_stage_bytes;
+          uint32_t b0 = a.b_resident ? sB_addr + b_res_off(0, tk, cg * a.cps, n_tile)
+                                     : sB_addr + (uint32_t)s * b_stage_bytes;
+          for (int ci = 0; ci < a.cps; ci++, sa += a.a_blk_bytes, b0 += b_cb) {
+            const uint64_t ad = dconst | (uint64_t)((sa >> 4) & 0x3FFFu);
+            const uint64_t bd = dconst | (uint64_t)((b0 >> 4) & 0x3FFFu);
+            if (a.wterms == 2) umma_stage_dispatch<true>(a.b_taps, nk, d, ad, bd, a_tap16, b_tap16, b_lo16, idesc, first);
+            else umma_stage_dispatch<false>(a.b_taps, nk, d, ad, bd, a_tap16, b_tap16, b_lo16, idesc, first);
             first = 1u;
           }
           tc_commit(smem_u32(&empty[s]));
-          if (++cb == a.kb_per_tap) {
-            cb = 0;
+          if (++cg == groups) {
+            cg = 0;
             tk++;
           }
           if (++s == S) {
@@ -858,7 +879,7 @@ static CUtensorMapSwizzle swizzle_of(int row_bytes) {
 }
 
 static size_t b_stage_bytes_of(const TcArgs& a) {
-  return a.b_resident ? 0 : (size_t)a.wterms * a.b_taps * a.BN * a.kblk * 2;
+  return a.b_resident ? 0 : (size_t)a.wterms * a.cps * a.b_taps * a.BN * a.kblk * 2;
 }
 
 static size_t smem_fixed(const TcArgs& a) {
@@ -949,7 +970,7 @@ int tc_launch(const TcProblem& p, cudaStream_t stream) {
     a.m_tiles = p.batch * a.tiles_h * a.tiles_w;
     const int box_h = halo ? BH + p.kh - 1 : BH;
     a.a_box_bytes = (uint32_t)(box_h * BW * kbytes);
-    a.a_stage_bytes = (a.a_box_bytes + 1023u) & ~1023u;
+    a.a_blk_bytes = (a.a_box_bytes + 1023u) & ~1023u;
     uint64_t dims[4] = {(uint64_t)p.C, (uint64_t)p.W, (uint64_t)p.H, (uint64_t)p.batch};
     uint64_t strides[3] = {(uint64_t)p.C * 2, (uint64_t)p.W * p.C * 2, (uint64_t)p.H * p.W * p.C * 2};
     uint32_t box[4] = {(uint32_t)kblk, (uint32_t)BW, (uint32_t)box_h, 1};
@@ -960,7 +981,7 @@ int tc_launch(const TcProblem& p, cudaStream_t stream) {
     a.M = p.M;
     a.m_tiles = (p.M + TC_BM - 1) / TC_BM;
     a.a_box_bytes = (uint32_t)(TC_BM * kbytes);
-    a.a_stage_bytes = (a.a_box_bytes + 1023u) & ~1023u;
+    a.a_blk_bytes = (a.a_box_bytes + 1023u) & ~1023u;
     a.b_taps = 1;
     uint64_t dims[2] = {(uint64_t)p.K, (uint64_t)p.M};
     uint64_t strides[1] = {(uint64_t)p.lda * 2};
@@ -1058,18 +1079,27 @@ int tc_launch(const TcProblem& p, cudaStream_t stream) {
   // weights (per stage) likewise. 8 stages at most.
   if (!a.tma_out) a.sbuf_bytes = 0;
   a.b_total_bytes = (uint32_t)((size_t)a.wterms * a.taps * a.kb_per_tap * n_tiles * BN * kbytes);
+  // stages of cps channel blocks each (fewer, larger stages amortise the per-stage waits and
+  // commits of the two issuing threads): the largest cps with >= 3 stages, else cps = 1 with >= 2
   bool planned = false;
   for (int res = 1; res >= 0 && !planned; res--) {
-    for (int nsb = a.tma_out ? 2 : 1; nsb >= 1 && !planned; nsb--) {
-      a.b_resident = res;
-      a.nsbuf = nsb;
-      const size_t fixed = smem_fixed(a);
-      const size_t per = a.a_stage_bytes + b_stage_bytes_of(a);
-      if (fixed >= (size_t)TC_SMEM_LIMIT) continue;
-      const int st = (int)std::min<size_t>(TC_MAX_STAGES, ((size_t)TC_SMEM_LIMIT - fixed) / per);
-      if (st >= (nsb == 2 ? 3 : 2)) {
-        a.stages = st;
-        planned = true;
+    for (int pass = 0; pass < 2 && !planned; pass++) {
+      for (int cps = pass == 0 ? a.kb_per_tap : 1; cps >= 1 && !planned; cps--) {
+        if (a.kb_per_tap % cps) continue;
+        for (int nsb = a.tma_out ? 2 : 1; nsb >= 1 && !planned; nsb--) {
+          a.b_resident = res;
+          a.nsbuf = nsb;
+          a.cps = cps;
+          a.a_stage_bytes = (uint32_t)cps * a.a_blk_bytes;
+          const size_t fixed = smem_fixed(a);
+          const size_t per = a.a_stage_bytes + b_stage_bytes_of(a);
+          if (fixed >= (size_t)TC_SMEM_LIMIT) continue;
+          const int st = (int)std::min<size_t>(TC_MAX_STAGES, ((size_t)TC_SMEM_LIMIT - fixed) / per);
+          if (st >= (pass == 0 ? 3 : (nsb == 2 ? 3 : 2))) {
+            a.stages = st;
+            planned = true;
+          }
+        }
       }
     }
   }
