@@ -574,6 +574,7 @@ int sdx_conv2d(sdx_ctx* ctx, const sdx_conv_desc* d, sdx_stream s) {
       a.in_scale = P<const float>(d->in_scale);
       a.add = P<const __half>(d->add);
       a.y = P<__half>(d->y);
+      a.err = ctx->err_word;
       if (!a.bias) return set_error(SDX_ERR_INVALID, "depthwise: bias required (zeros when absent)");
       return depthwise_launch(a, st);
     }

@@ -78,6 +78,7 @@ struct DwArgs {
   const float* in_scale;  // [batch, c] or null
   const __half* add;
   __half* y;
+  unsigned int* err;      // device error word (bounded waits of the TMA-fed kernel)
 };
 int depthwise_launch(const DwArgs& a, cudaStream_t st);
 // smem-tiled variant (tiled_kernels.cu); false when the shape is not one it handles

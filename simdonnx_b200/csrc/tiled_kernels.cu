@@ -141,11 +141,210 @@ static int dw_launch_t(const DwArgs& a, cudaStream_t st) {
   return SDX_OK;
 }
 
+// ---- persistent, TMA-fed form. Each CTA walks a contiguous range of tiles (image, channel slab,
+// tile row, tile column); thread 0 prefetches the next tile's input box (+ halo, zero fill = padding)
+// with one TMA load into the other of two buffers while all threads compute the current one, so
+// loads overlap compute and need no per-element index math. Weights (times the image's SE scale)
+// are restaged only when the image or slab changes. All waits are bounded; a failed wait ends the
+// CTA through a block-uniform vote after draining its copies in flight.
+template <int ACT, int K, int S>
+__global__ void __launch_bounds__(256) dw_tma_kernel(const __grid_constant__ CUtensorMap tmX, DwArgs a, int CS, int TH,
+                                                     int TW, int tiles_x, int tiles_per_img, int slabs, int total) {
+  extern __shared__ uint8_t dsm_raw[];
+  uint8_t* dsm = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(dsm_raw) + 127) & ~uintptr_t(127));
+  const int G = CS >> 3;
+  const int IWt = (TW - 1) * S + K, IHt = (TH - 1) * S + K;
+  const uint32_t tile_bytes = (uint32_t)IHt * IWt * CS * 2;
+  const uint32_t buf_bytes = (tile_bytes + 127u) & ~127u;
+  const uint4* bufs = reinterpret_cast<const uint4*>(dsm);
+  float* sw = reinterpret_cast<float*>(dsm + 2 * buf_bytes);                       // [K*K][CS]
+  uint64_t* full = reinterpret_cast<uint64_t*>(dsm + 2 * buf_bytes + ((K * K * CS * 4 + 15) & ~15));
+  __shared__ int abort_flag;
+  const int tid = threadIdx.x;
+  const int per = (total + gridDim.x - 1) / gridDim.x;
+  const int t0 = blockIdx.x * per, t1 = min(total, t0 + per);
+  if (t0 >= t1) return;
+  auto decode = [&](int t, int& n, int& slab, int& oy0, int& ox0) {
+    n = t / (slabs * tiles_per_img);
+    const int r = t - n * slabs * tiles_per_img;
+    slab = r / tiles_per_img;
+    const int q = r - slab * tiles_per_img;
+    const int ty = q / tiles_x;
+    oy0 = ty * TH;
+    ox0 = (q - ty * tiles_x) * TW;
+  };
+  auto issue = [&](int t, int b) {
+    int n, slab, oy0, ox0;
+    decode(t, n, slab, oy0, ox0);
+    const uint32_t bar = smem_u32(&full[b]);
+    mbar_arrive_expect_tx(bar, tile_bytes);
+    tma_load_4d(smem_u32(dsm + b * buf_bytes), &tmX, bar, slab * CS, ox0 * S - a.pl, oy0 * S - a.pt, n);
+  };
+  uint32_t issued[2] = {0, 0};  // thread 0: copies issued into each buffer
+  if (tid == 0) {
+    abort_flag = 0;
+    mbar_init(smem_u32(&full[0]), 1);
+    mbar_init(smem_u32(&full[1]), 1);
+    mbar_fence_init();
+    tma_prefetch_desc(&tmX);
+  }
+  __syncthreads();
+  if (tid == 0) {
+    issue(t0, 0);
+    issued[0] = 1;
+  }
+  const int cg = tid % G, strip = tid / G;
+  const int spr = TW / DW_R;
+  const int sy = strip / spr, sx = strip - sy * spr;
+  constexpr int NX = (DW_R - 1) * S + K;
+  int key = -1;
+  int i = 0;
+  for (int t = t0; t < t1; t++, i++) {
+    const int b = i & 1;
+    if (tid == 0 && t + 1 < t1) {
+      // buffer b^1 was last read by tile i-1, which every thread finished before the barrier that
+      // ended that iteration
+      issue(t + 1, b ^ 1);
+      issued[b ^ 1]++;
+    }
+    int n, slab, oy0, ox0;
+    decode(t, n, slab, oy0, ox0);
+    const int c0 = slab * CS;
+    if (n * slabs + slab != key) {
+      key = n * slabs + slab;
+      for (int j = tid; j < K * K * CS; j += blockDim.x) {
+        const int tap = j / CS, c = j - tap * CS;
+        float w = __ldg(a.w + (int64_t)tap * a.c + c0 + c);
+        if (a.in_scale) w *= __ldg(a.in_scale + (int64_t)n * a.c + c0 + c);
+        sw[j] = w;
+      }
+      __syncthreads();
+    }
+    const bool ok = mbar_wait(smem_u32(&full[b]), (uint32_t)(i >> 1) & 1u, a.err, SDX_DEV_WAIT_FULL, &abort_flag);
+    if (__syncthreads_or(!ok)) break;
+    const uint4* stile = bufs + (size_t)b * (buf_bytes / 16);
+    const int oy = oy0 + sy;
+    if (sy < TH && oy < a.oh) {
+      const int c = c0 + cg * 8;
+      float acc[DW_R][8];
+      {
+        const float4* bp = reinterpret_cast<const float4*>(a.bias + c);
+        const float4 b0 = __ldg(bp), b1 = __ldg(bp + 1);
+#pragma unroll
+        for (int r = 0; r < DW_R; r++) {
+          acc[r][0] = b0.x; acc[r][1] = b0.y; acc[r][2] = b0.z; acc[r][3] = b0.w;
+          acc[r][4] = b1.x; acc[r][5] = b1.y; acc[r][6] = b1.z; acc[r][7] = b1.w;
+        }
+      }
+      const int lx0 = sx * DW_R * S;
+#pragma unroll
+      for (int ky = 0; ky < K; ky++) {
+        // this kernel row's weights stay in registers; input vectors stream through once each
+        float wr[K][8];
+#pragma unroll
+        for (int kx = 0; kx < K; kx++) {
+          const float4* wp = reinterpret_cast<const float4*>(sw + (ky * K + kx) * CS + cg * 8);
+          const float4 w0 = wp[0], w1 = wp[1];
+          wr[kx][0] = w0.x; wr[kx][1] = w0.y; wr[kx][2] = w0.z; wr[kx][3] = w0.w;
+          wr[kx][4] = w1.x; wr[kx][5] = w1.y; wr[kx][6] = w1.z; wr[kx][7] = w1.w;
+        }
+        const uint4* row = stile + ((sy * S + ky) * IWt + lx0) * G + cg;
+#pragma unroll
+        for (int j = 0; j < NX; j++) {
+          const uint4 u = row[j * G];
+          const __half2* h = reinterpret_cast<const __half2*>(&u);
+          float xv[8];
+#pragma unroll
+          for (int q = 0; q < 4; q++) {
+            const float2 f = __half22float2(h[q]);
+            xv[2 * q] = f.x;
+            xv[2 * q + 1] = f.y;
+          }
+#pragma unroll
+          for (int r = 0; r < DW_R; r++) {
+            const int kx = j - r * S;
+            if (kx >= 0 && kx < K) {
+#pragma unroll
+              for (int q = 0; q < 8; q++) acc[r][q] = fmaf(xv[q], wr[kx][q], acc[r][q]);
+            }
+          }
+        }
+      }
+#pragma unroll
+      for (int r = 0; r < DW_R; r++) {
+        const int ox = ox0 + sx * DW_R + r;
+        if (ox >= a.ow) break;
+        const int64_t off = (((int64_t)n * a.oh + oy) * a.ow + ox) * a.c + c;
+        if (a.add) {
+          const uint4 ru = __ldg(reinterpret_cast<const uint4*>(a.add + off));
+          const __half2* h = reinterpret_cast<const __half2*>(&ru);
+#pragma unroll
+          for (int q = 0; q < 4; q++) {
+            const float2 f = __half22float2(h[q]);
+            acc[r][2 * q] += f.x;
+            acc[r][2 * q + 1] += f.y;
+          }
+        }
+        uint4 u;
+        __half2* h = reinterpret_cast<__half2*>(&u);
+#pragma unroll
+        for (int q = 0; q < 4; q++) h[q] = __floats2half2_rn(act_t<ACT>(acc[r][2 * q]), act_t<ACT>(acc[r][2 * q + 1]));
+        *reinterpret_cast<uint4*>(a.y + off) = u;
+      }
+    }
+    __syncthreads();
+  }
+  // wind-down (only after an abort can a copy still be in flight): drain every issued copy
+  if (tid == 0) {
+    for (int b = 0; b < 2; b++)
+      if (issued[b] > 0) mbar_wait_drain(smem_u32(&full[b]), (issued[b] - 1) & 1u, a.err, SDX_DEV_WAIT_DRAIN);
+  }
+}
+
+template <int ACT, int K, int S>
+static bool dw_tma_launch_t(const DwArgs& a, cudaStream_t st) {
+  if ((reinterpret_cast<uintptr_t>(a.x) & 15u) || (a.c * 2) % 16) return false;
+  const int CS = a.c <= 64 ? a.c : 64;
+  const int G = CS / 8;
+  const int TW = 16, TH = (256 / G) / (TW / DW_R);
+  const int IWt = (TW - 1) * S + K, IHt = (TH - 1) * S + K;
+  if (IWt > 256 || IHt > 256) return false;
+  const size_t tile_bytes = (size_t)IHt * IWt * CS * 2;
+  const size_t smem = 128 + 2 * ((tile_bytes + 127) & ~(size_t)127) + ((K * K * CS * 4 + 15) & ~15) + 16;
+  if (smem > 200 * 1024) return false;
+  PFN_encodeTiled enc = get_encode_tiled();
+  if (!enc) return false;
+  CUtensorMap map;
+  const cuuint64_t dims[4] = {(cuuint64_t)a.c, (cuuint64_t)a.iw, (cuuint64_t)a.ih, (cuuint64_t)a.batch};
+  const cuuint64_t strides[3] = {(cuuint64_t)a.c * 2, (cuuint64_t)a.iw * a.c * 2, (cuuint64_t)a.ih * a.iw * a.c * 2};
+  const cuuint32_t box[4] = {(cuuint32_t)CS, (cuuint32_t)IWt, (cuuint32_t)IHt, 1};
+  const cuuint32_t estr[4] = {1, 1, 1, 1};
+  if (enc(&map, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 4, const_cast<__half*>(a.x), dims, strides, box, estr,
+          CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+          CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) != CUDA_SUCCESS)
+    return false;
+  static bool attr = false;
+  if (!attr) {
+    cudaFuncSetAttribute(dw_tma_kernel<ACT, K, S>, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024);
+    attr = true;
+  }
+  const int tiles_x = (a.ow + TW - 1) / TW, tiles_y = (a.oh + TH - 1) / TH;
+  const int slabs = a.c / CS;
+  const int64_t total = (int64_t)a.batch * slabs * tiles_x * tiles_y;
+  if (total <= 0 || total > INT32_MAX) return false;
+  int dev = 0, per_sm = 1;
+  cudaGetDevice(&dev);
+  cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, dw_tma_kernel<ACT, K, S>, 256, smem);
+  const int grid = (int)std::min<int64_t>(total, (int64_t)num_sms(dev) * std::max(1, per_sm));
+  dw_tma_kernel<ACT, K, S><<<grid, 256, smem, st>>>(map, a, CS, TH, TW, tiles_x, tiles_x * tiles_y, slabs, (int)total);
+  return true;
+}
+
 template <int ACT>
 static bool dw_dispatch_ks(const DwArgs& a, cudaStream_t st) {
 #define SDX_DW_CASE(KK, SS)                                   \
   if (a.kh == KK && a.kw == KK && a.sh == SS && a.sw == SS) { \
-    dw_launch_t<ACT, KK, SS>(a, st);                          \
+    if (!dw_tma_launch_t<ACT, KK, SS>(a, st)) dw_launch_t<ACT, KK, SS>(a, st); \
     return true;                                              \
   }
   SDX_DW_CASE(3, 1)
