@@ -595,6 +595,7 @@ int sdx_conv2d(sdx_ctx* ctx, const sdx_conv_desc* d, sdx_stream s) {
       a.y_nchw = d->y_layout == SDX_NCHW;
       a.y_pix_stride = ystride;
       a.y_ch_off = d->y_ch_off;
+      a.err = ctx->err_word;
       return direct_conv_launch(a, st);
     }
     default: return set_error(SDX_ERR_NOT_SUPPORTED, "conv: no CUDA kernel for this shape/flags");

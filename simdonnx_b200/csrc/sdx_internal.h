@@ -96,6 +96,7 @@ struct DirectArgs {
   int y_f32, y_nchw;
   int64_t y_pix_stride;
   int y_ch_off;
+  unsigned int* err;  // device error word (bounded waits of the TMA-fed stem)
 };
 int direct_conv_launch(const DirectArgs& a, cudaStream_t st);
 bool stem_tiled_launch(const DirectArgs& a, cudaStream_t st);

@@ -440,7 +440,179 @@ static void stem_launch_t(const DirectArgs& a, cudaStream_t st) {
   stem_tiled_kernel<ACT, K, S><<<grid, 256, smem, st>>>(a, TH, TW, tiles_x);
 }
 
+// ---- persistent, TMA-fed stem for the graph-input conv: fp32 NCHW input, IC = 3, OC = 16, 3x3,
+// stride 2 (the det model's first conv; the NCHW -> NHWC relayout and fp16 rounding of its output
+// happen on the way out). Each CTA walks a contiguous range of 16 x 64 output tiles; thread 0
+// prefetches the next tile's three input planes (+ halo, zero fill = padding) with one TMA load while
+// all threads compute the current tile. Thread = 4 horizontally adjacent outputs x 16 channels:
+// per input row it reads 9 floats once, per tap the 16 weights once (shared-memory broadcasts).
+// The TMA box starts 3 columns left of the window (pad 1 + 3 = 4 floats) so its x coordinate stays
+// 16-byte aligned; buffers are 1024-byte aligned.
+constexpr int STEM_TH = 16, STEM_TW = 64, STEM_R = 4;
+constexpr int STEM_IH = (STEM_TH - 1) * 2 + 3;           // 33 input rows
+constexpr int STEM_IW = ((STEM_TW - 1) * 2 + 3 + 3 + 3) / 4 * 4;  // 132 columns (3 of alignment)
+
+template <int ACT>
+__global__ void __launch_bounds__(256) stem_tma_kernel(const __grid_constant__ CUtensorMap tmX, DirectArgs a,
+                                                       int tiles_x, int tiles_per_img, int total) {
+  constexpr int IC = 3, OC = 16, K = 3;
+  constexpr uint32_t kTileBytes = IC * STEM_IH * STEM_IW * 4;
+  constexpr uint32_t kBufBytes = (kTileBytes + 1023u) & ~1023u;  // TMA destinations 1024-aligned
+  extern __shared__ uint8_t ssm_raw[];
+  uint8_t* ssm = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(ssm_raw) + 1023) & ~uintptr_t(1023));
+  float* bufs = reinterpret_cast<float*>(ssm);                                   // [2][IC][IH][IW]
+  float* sw = reinterpret_cast<float*>(ssm + 2 * kBufBytes);                     // [K*K][IC][OC]
+  float* sb = sw + K * K * IC * OC;                                              // [OC]
+  uint64_t* full = reinterpret_cast<uint64_t*>(sb + OC);
+  __shared__ int abort_flag;
+  const int tid = threadIdx.x;
+  const int per = (total + gridDim.x - 1) / gridDim.x;
+  const int t0 = blockIdx.x * per, t1 = min(total, t0 + per);
+  if (t0 >= t1) return;
+  auto decode = [&](int t, int& n, int& oy0, int& ox0) {
+    n = t / tiles_per_img;
+    const int q = t - n * tiles_per_img;
+    const int ty = q / tiles_x;
+    oy0 = ty * STEM_TH;
+    ox0 = (q - ty * tiles_x) * STEM_TW;
+  };
+  auto issue = [&](int t, int b) {
+    int n, oy0, ox0;
+    decode(t, n, oy0, ox0);
+    const uint32_t bar = smem_u32(&full[b]);
+    mbar_arrive_expect_tx(bar, kTileBytes);
+    tma_load_4d(smem_u32(bufs + b * (kBufBytes / 4)), &tmX, bar, ox0 * 2 - a.pl - 3, oy0 * 2 - a.pt, 0, n);
+  };
+  uint32_t issued[2] = {0, 0};
+  for (int i = tid; i < K * K * IC * OC; i += blockDim.x) sw[i] = __ldg(a.w + i);
+  for (int i = tid; i < OC; i += blockDim.x) sb[i] = a.bias ? __ldg(a.bias + i) : 0.0f;
+  if (tid == 0) {
+    abort_flag = 0;
+    mbar_init(smem_u32(&full[0]), 1);
+    mbar_init(smem_u32(&full[1]), 1);
+    mbar_fence_init();
+    tma_prefetch_desc(&tmX);
+  }
+  __syncthreads();
+  if (tid == 0) {
+    issue(t0, 0);
+    issued[0] = 1;
+  }
+  const int ly = tid / (STEM_TW / STEM_R), lx = (tid - ly * (STEM_TW / STEM_R)) * STEM_R;
+  int i = 0;
+  for (int t = t0; t < t1; t++, i++) {
+    const int b = i & 1;
+    if (tid == 0 && t + 1 < t1) {
+      issue(t + 1, b ^ 1);
+      issued[b ^ 1]++;
+    }
+    int n, oy0, ox0;
+    decode(t, n, oy0, ox0);
+    const bool ok = mbar_wait(smem_u32(&full[b]), (uint32_t)(i >> 1) & 1u, a.err, SDX_DEV_WAIT_FULL, &abort_flag);
+    if (__syncthreads_or(!ok)) break;
+    const float* tile = bufs + b * (kBufBytes / 4);
+    const int oy = oy0 + ly;
+    if (oy < a.oh) {
+      float acc[STEM_R][OC];
+#pragma unroll
+      for (int r = 0; r < STEM_R; r++)
+#pragma unroll
+        for (int o = 0; o < OC; o++) acc[r][o] = sb[o];
+#pragma unroll
+      for (int c = 0; c < IC; c++) {
+#pragma unroll
+        for (int ky = 0; ky < K; ky++) {
+          // window columns 2*lx .. 2*lx + 8 of this input row (+3: the alignment offset)
+          const float* row = tile + (c * STEM_IH + ly * 2 + ky) * STEM_IW + lx * 2 + 3;
+          float xv[(STEM_R - 1) * 2 + K];
+#pragma unroll
+          for (int j = 0; j < (STEM_R - 1) * 2 + K; j++) xv[j] = row[j];
+#pragma unroll
+          for (int kx = 0; kx < K; kx++) {
+            const float4* wp = reinterpret_cast<const float4*>(sw + ((ky * K + kx) * IC + c) * OC);
+            float wv[OC];
+#pragma unroll
+            for (int q = 0; q < OC / 4; q++) {
+              const float4 w4 = wp[q];
+              wv[4 * q] = w4.x; wv[4 * q + 1] = w4.y; wv[4 * q + 2] = w4.z; wv[4 * q + 3] = w4.w;
+            }
+#pragma unroll
+            for (int r = 0; r < STEM_R; r++)
+#pragma unroll
+              for (int o = 0; o < OC; o++) acc[r][o] = fmaf(xv[r * 2 + kx], wv[o], acc[r][o]);
+          }
+        }
+      }
+#pragma unroll
+      for (int r = 0; r < STEM_R; r++) {
+        const int ox = ox0 + lx + r;
+        if (ox >= a.ow) break;
+        __half* yp = static_cast<__half*>(a.y) + (((int64_t)n * a.oh + oy) * a.ow + ox) * a.y_pix_stride + a.y_ch_off;
+#pragma unroll
+        for (int h8 = 0; h8 < OC / 8; h8++) {
+          uint4 u;
+          __half2* h = reinterpret_cast<__half2*>(&u);
+#pragma unroll
+          for (int q = 0; q < 4; q++)
+            h[q] = __floats2half2_rn(act_t<ACT>(acc[r][h8 * 8 + 2 * q]), act_t<ACT>(acc[r][h8 * 8 + 2 * q + 1]));
+          reinterpret_cast<uint4*>(yp)[h8] = u;
+        }
+      }
+    }
+    __syncthreads();
+  }
+  if (tid == 0) {
+    for (int b = 0; b < 2; b++)
+      if (issued[b] > 0) mbar_wait_drain(smem_u32(&full[b]), (issued[b] - 1) & 1u, a.err, SDX_DEV_WAIT_DRAIN);
+  }
+}
+
+template <int ACT>
+static bool stem_tma_launch_t(const DirectArgs& a, cudaStream_t st) {
+  PFN_encodeTiled enc = get_encode_tiled();
+  if (!enc) return false;
+  CUtensorMap map;
+  const cuuint64_t dims[4] = {(cuuint64_t)a.iw, (cuuint64_t)a.ih, 3, (cuuint64_t)a.batch};
+  const cuuint64_t strides[3] = {(cuuint64_t)a.iw * 4, (cuuint64_t)a.ih * a.iw * 4, (cuuint64_t)3 * a.ih * a.iw * 4};
+  const cuuint32_t box[4] = {(cuuint32_t)STEM_IW, (cuuint32_t)STEM_IH, 3, 1};
+  const cuuint32_t estr[4] = {1, 1, 1, 1};
+  if (enc(&map, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 4, const_cast<void*>(a.x), dims, strides, box, estr,
+          CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+          CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) != CUDA_SUCCESS)
+    return false;
+  const size_t buf = ((size_t)3 * STEM_IH * STEM_IW * 4 + 1023) & ~(size_t)1023;
+  const size_t smem = 1024 + 2 * buf + sizeof(float) * (9 * 3 * 16 + 16) + 16;
+  static bool attr = false;
+  if (!attr) {
+    cudaFuncSetAttribute(stem_tma_kernel<ACT>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+    attr = true;
+  }
+  const int tiles_x = (a.ow + STEM_TW - 1) / STEM_TW, tiles_y = (a.oh + STEM_TH - 1) / STEM_TH;
+  const int64_t total = (int64_t)a.batch * tiles_x * tiles_y;
+  if (total <= 0 || total > INT32_MAX) return false;
+  int dev = 0, per_sm = 1;
+  cudaGetDevice(&dev);
+  cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, stem_tma_kernel<ACT>, 256, smem);
+  const int grid = (int)std::min<int64_t>(total, (int64_t)num_sms(dev) * std::max(1, per_sm));
+  stem_tma_kernel<ACT><<<grid, 256, smem, st>>>(map, a, tiles_x, tiles_x * tiles_y, (int)total);
+  return true;
+}
+
 bool stem_tiled_launch(const DirectArgs& a, cudaStream_t st) {
+  // the det stem: fp32 NCHW graph input, 3 -> 16 channels, 3x3 stride 2 (TMA-fed form)
+  if (a.ic == 3 && a.oc == 16 && a.kh == 3 && a.kw == 3 && a.sh == 2 && a.sw == 2 && a.x_f32 && a.x_nchw && !a.add &&
+      !a.y_f32 && !a.y_nchw && a.y_pix_stride % 8 == 0 && a.y_ch_off % 8 == 0 && a.pl == 1 &&
+      (reinterpret_cast<uintptr_t>(a.x) & 15u) == 0 && (a.iw * 4) % 16 == 0 &&
+      (reinterpret_cast<uintptr_t>(a.y) & 15u) == 0) {
+    bool done = false;
+    switch (a.act) {
+      case ACT_HARDSWISH: done = stem_tma_launch_t<ACT_HARDSWISH>(a, st); break;
+      case ACT_RELU: done = stem_tma_launch_t<ACT_RELU>(a, st); break;
+      case ACT_NONE: done = stem_tma_launch_t<ACT_NONE>(a, st); break;
+      default: break;
+    }
+    if (done) return true;
+  }
   if (a.ic > 4 || a.oc % 8 != 0 || a.oc > 64 || a.add || a.y_f32 || a.y_nchw || a.kh != 3 || a.kw != 3 ||
       a.sh != a.sw || (a.sh != 1 && a.sh != 2) || a.batch > 65535 || (a.y_pix_stride % 8) || (a.y_ch_off % 8))
     return false;
