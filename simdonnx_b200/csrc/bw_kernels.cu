@@ -208,14 +208,16 @@ int direct_conv_launch(const DirectArgs& a, cudaStream_t st) {
 
 // ------------------------------------------------------------------ ConvT, oc < 8 (dot path)
 // ConvTDot (src/Kernels/Nhwc.Det.cs:96-131): per output element one dot product over ic + bias, act.
-// Fast form (kh*kw*oc <= 32): blocks walk input rows; a thread reads its input pixel once, in
+// Fast form (kh*kw*oc in {4, 8, 12, 16}): blocks walk input rows; a thread reads its input pixel once, in
 // 8-channel pieces, and keeps all kh*kw*oc sums in registers; weights [tap][o][ic] in shared memory
 // (staged once per block).
-constexpr int CONVT_DOT_MAX_OUT = 32;
-template <int ACT>
+// TO = kh*kw*oc is a template constant: the per-output loops then hold exactly TO accumulators
+// (predicated-off copies of a wider unrolled loop would still issue).
+template <int ACT, int TO>
 __global__ void convt_dot_rows_kernel(ConvtDotArgs a) {
   extern __shared__ float sw[];
-  const int taps = a.kh * a.kw, to = taps * a.oc;
+  const int taps = a.kh * a.kw;
+  constexpr int to = TO;
   const int nw = to * a.ic;
   for (int i = threadIdx.x; i < nw; i += blockDim.x) {
     const int c = i % a.ic, k = i / a.ic;
@@ -234,27 +236,26 @@ __global__ void convt_dot_rows_kernel(ConvtDotArgs a) {
     if (x >= a.iw) continue;
     const int n = row / a.ih, y = row - n * a.ih;
     const __half* xp = a.x + ((int64_t)row * a.iw + x) * a.ic;
-    float acc[CONVT_DOT_MAX_OUT];
+    float acc[TO];
 #pragma unroll
-    for (int k = 0; k < CONVT_DOT_MAX_OUT; k++) acc[k] = k < to ? sb[k % a.oc] : 0.0f;
+    for (int k = 0; k < TO; k++) acc[k] = sb[k % a.oc];
     for (int c = 0; c < a.ic; c += 8) {
       float xv[8];
       h8_to_f(__ldg(reinterpret_cast<const uint4*>(xp + c)), xv);
 #pragma unroll
-      for (int k = 0; k < CONVT_DOT_MAX_OUT; k++) {
-        if (k < to) {
-          const float* wk = sw + k * a.ic + c;
-          float s = acc[k];
-#pragma unroll
-          for (int j = 0; j < 8; j++) s = fmaf(xv[j], wk[j], s);
-          acc[k] = s;
-        }
+      for (int k = 0; k < TO; k++) {
+        const float4* wk = reinterpret_cast<const float4*>(sw + k * a.ic + c);
+        const float4 w0 = wk[0], w1 = wk[1];
+        float s = acc[k];
+        s = fmaf(xv[0], w0.x, s); s = fmaf(xv[1], w0.y, s); s = fmaf(xv[2], w0.z, s); s = fmaf(xv[3], w0.w, s);
+        s = fmaf(xv[4], w1.x, s); s = fmaf(xv[5], w1.y, s); s = fmaf(xv[6], w1.z, s); s = fmaf(xv[7], w1.w, s);
+        acc[k] = s;
       }
     }
     if (a.oc == 1 && a.kw == 2 && a.y_f32) {
       // one output channel, two taps per output row: adjacent floats, one 8-byte store per row
 #pragma unroll
-      for (int dy = 0; dy < CONVT_DOT_MAX_OUT / 2; dy++) {
+      for (int dy = 0; dy < TO / 2; dy++) {
         if (dy < a.kh) {
           const int64_t op = ((int64_t)n * oh + y * a.kh + dy) * ow + x * 2;
           *reinterpret_cast<float2*>(static_cast<float*>(a.y) + op) =
@@ -263,8 +264,8 @@ __global__ void convt_dot_rows_kernel(ConvtDotArgs a) {
       }
     } else {
 #pragma unroll
-      for (int k = 0; k < CONVT_DOT_MAX_OUT; k++) {
-        if (k < to) {
+      for (int k = 0; k < TO; k++) {
+        {
           const int o = k % a.oc, tap = k / a.oc;
           const int dy = tap / a.kw, dx = tap - dy * a.kw;
           const int64_t op = ((int64_t)n * oh + y * a.kh + dy) * ow + x * a.kw + dx;
@@ -316,13 +317,17 @@ int convt_dot_launch(const ConvtDotArgs& a, cudaStream_t st) {
   const int to = a.kh * a.kw * a.oc;
   const size_t wbytes = sizeof(float) * ((size_t)to * a.ic + a.oc);
   const int64_t rows = (int64_t)a.batch * a.ih;
-  if (to <= CONVT_DOT_MAX_OUT && wbytes <= 48 * 1024 && rows * a.iw <= INT32_MAX && aligned8(a.y)) {
+  if ((to == 4 || to == 8 || to == 12 || to == 16) && wbytes <= 48 * 1024 && rows * a.iw <= INT32_MAX &&
+      aligned8(a.y)) {
     const int block = a.iw >= 128 ? 128 : (a.iw + 31) / 32 * 32;
     const int64_t jobs = rows * ((a.iw + block - 1) / block);
     int dev = 0;
     cudaGetDevice(&dev);
     const int grid = (int)std::min<int64_t>(jobs, (int64_t)num_sms(dev) * 16);
-    SDX_ACT_DISPATCH(a.act, ACTC, convt_dot_rows_kernel<ACTC><<<grid, block, wbytes, st>>>(a));
+#define SDX_CT_TO(TOV) \
+  if (to == TOV) SDX_ACT_DISPATCH(a.act, ACTC, convt_dot_rows_kernel<ACTC, TOV><<<grid, block, wbytes, st>>>(a));
+    SDX_CT_TO(4) SDX_CT_TO(8) SDX_CT_TO(12) SDX_CT_TO(16)
+#undef SDX_CT_TO
   } else {
     SDX_ACT_DISPATCH(a.act, ACTC, convt_dot_kernel<ACTC><<<grid_for(total, 256), 256, 0, st>>>(a));
   }
