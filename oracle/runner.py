@@ -50,6 +50,10 @@ class OracleSession:
         for n in P.nodes:
             out = self._exec(n, env)
             for o, val in zip(n.outs, out if isinstance(out, tuple) else (out,)):
+                # the plan's shapes are authoritative ([N, 1, W, C] and [N, W, C] name the same rows)
+                v = P.values[o]
+                if v.layout != "nchw" and val.shape != v.shape and val.size == int(np.prod(v.shape)):
+                    val = val.reshape(v.shape)
                 env[o] = val
         return env if self.keep_all else {P.output: env[P.output]}
 
@@ -66,7 +70,7 @@ class OracleSession:
         if op == "Conv":
             x = self._nhwc(n.ins[0], env)
             kp = self._conv_plan(n)
-            add = env[p.add] if p.add else None
+            add = self._nhwc(p.add, env) if p.add else None
             if p.pool is not None:
                 return O.conv_pool(x, kp, pads=p.pads, act=p.act, pool_relu=p.pool.fuse_relu)
             return O.conv(x, kp, strides=p.strides, pads=p.pads, act=p.act, add=add)

@@ -84,3 +84,38 @@ def test_det_graph_replay_equals_eager():
     g = CudaInferenceSession(plan, use_graph=True).run(feeds)
     e = CudaInferenceSession(plan, use_graph=False).run(feeds)
     assert np.array_equal(g, e)
+
+
+def test_rec_n1_output():
+    """C3 recognition model (rectangular depthwise strides, AvgPool, LayerNorm, fused attention,
+    Gemm residual epilogues, 6625-wide fp32 logits) against the oracle running the same plan."""
+    from simdonnx_b200 import configs
+    plan = configs.build_rec(batch=1)
+    sess, feeds, ref, got = _run_both(plan)
+    assert_close(got, ref[plan.output], "rec logits")
+    sess.close()
+
+
+def test_rec_batch_images_match_single_runs_bitwise():
+    from simdonnx_b200 import configs
+    from simdonnx_b200.session import CudaInferenceSession
+    big = configs.build_rec(batch=4)
+    feeds = {k: f() for k, f in big.feeds.items()}
+    sb = CudaInferenceSession(big)
+    out = sb.run(feeds)
+    one = configs.build_rec(batch=1)
+    s1 = CudaInferenceSession(one)
+    o1 = s1.run({one.input: feeds[big.input][2:3]})
+    assert np.array_equal(o1[0], out[2])
+    sb.close()
+    s1.close()
+
+
+def test_unet_n1_output():
+    """C4 UNet at its full 512x512 size: tcgen05 3x3 convs, max pools, ConvT 2x2 decoders, skip
+    concats and the final 1x1 conv with the fp32 NCHW input as residual."""
+    from simdonnx_b200 import configs
+    plan = configs.build_unet(batch=1)
+    sess, feeds, ref, got = _run_both(plan)
+    assert_close(got, ref[plan.output], "unet output")
+    sess.close()
