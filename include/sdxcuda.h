@@ -301,6 +301,15 @@ int sdx_session_stream(sdx_session* s, sdx_stream* stream);
 int sdx_session_enqueue(sdx_session* s);
 /* End-to-end run: host input -> device, graph, device -> host output, wait (timeout_ms as sdx_stream_sync). */
 int sdx_session_run(sdx_session* s, const void* host_in, void* host_out, int timeout_ms);
+/* Pipelined end-to-end runs (the Submit / Wait split of VkInferenceSession, src/Backends/Vulkan/
+ * VkSession.cs:543-556, with the host copies inside): submit enqueues host -> device copy of host_in, the graph and the device ->
+ * host copy into host_out, and returns at once. Two device staging slots per direction and two copy
+ * streams let the input copy of batch i+1 and the output copy of batch i-1 run while batch i
+ * computes. host_in / host_out should be pinned (sdx_host_alloc_pinned) and must stay valid and
+ * unmodified until sdx_session_wait returns; with more than two submissions in flight, alternate
+ * at least two host buffer pairs. sdx_session_wait blocks until every submission finished. */
+int sdx_session_submit(sdx_session* s, const void* host_in, void* host_out);
+int sdx_session_wait(sdx_session* s, int timeout_ms);
 int sdx_session_node_count(sdx_session* s, int* count);
 /* Runs node `index` alone, eagerly, on the session stream (per-node timing, like the reference's
  * VkInferenceSession.DebugProfile, src/Backends/Vulkan/VkSession.cs:413-492). */

@@ -140,6 +140,8 @@ _SIGS = {
     "sdx_session_build": (_i, [_p, _i]),
     "sdx_session_stream": (_i, [_p, ctypes.POINTER(_p)]),
     "sdx_session_enqueue": (_i, [_p]),
+    "sdx_session_submit": (_i, [_p, _p, _p]),
+    "sdx_session_wait": (_i, [_p, _i]),
     "sdx_session_run": (_i, [_p, _p, _p, _i]),
     "sdx_session_node_count": (_i, [_p, ctypes.POINTER(_i)]),
     "sdx_session_enqueue_node": (_i, [_p, _i]),

@@ -27,7 +27,55 @@ struct sdx_session {
   size_t in_bytes, out_bytes;
   cudaGraphExec_t graph;
   int built;
+  // pipelined submit/wait: two device staging slots per direction and two copy streams, so the
+  // host->device copy of batch i+1 and the device->host copy of batch i-1 overlap the compute of i
+  struct Pipe {
+    bool ready = false;
+    cudaStream_t h2d = nullptr, d2h = nullptr;
+    void* stage_in[2] = {nullptr, nullptr};
+    void* stage_out[2] = {nullptr, nullptr};
+    cudaEvent_t in_landed[2] = {}, in_free[2] = {}, out_ready[2] = {}, out_free[2] = {};
+    unsigned long long submitted = 0;
+  } pipe;
 };
+
+static void pipe_release(sdx_session* s) {
+  sdx_session::Pipe& p = s->pipe;
+  if (p.h2d) cudaStreamSynchronize(p.h2d);
+  if (p.d2h) cudaStreamSynchronize(p.d2h);
+  for (int i = 0; i < 2; i++) {
+    if (p.stage_in[i]) cudaFree(p.stage_in[i]);
+    if (p.stage_out[i]) cudaFree(p.stage_out[i]);
+    if (p.in_landed[i]) cudaEventDestroy(p.in_landed[i]);
+    if (p.in_free[i]) cudaEventDestroy(p.in_free[i]);
+    if (p.out_ready[i]) cudaEventDestroy(p.out_ready[i]);
+    if (p.out_free[i]) cudaEventDestroy(p.out_free[i]);
+  }
+  if (p.h2d) cudaStreamDestroy(p.h2d);
+  if (p.d2h) cudaStreamDestroy(p.d2h);
+  p = sdx_session::Pipe();
+}
+
+static int pipe_setup(sdx_session* s) {
+  sdx_session::Pipe& p = s->pipe;
+  if (p.ready) return SDX_OK;
+  cudaError_t e = cudaStreamCreateWithFlags(&p.h2d, cudaStreamNonBlocking);
+  if (e == cudaSuccess) e = cudaStreamCreateWithFlags(&p.d2h, cudaStreamNonBlocking);
+  for (int i = 0; i < 2 && e == cudaSuccess; i++) {
+    if (s->in_bytes) e = cudaMalloc(&p.stage_in[i], s->in_bytes);
+    if (e == cudaSuccess && s->out_bytes) e = cudaMalloc(&p.stage_out[i], s->out_bytes);
+    if (e == cudaSuccess) e = cudaEventCreateWithFlags(&p.in_landed[i], cudaEventDisableTiming);
+    if (e == cudaSuccess) e = cudaEventCreateWithFlags(&p.in_free[i], cudaEventDisableTiming);
+    if (e == cudaSuccess) e = cudaEventCreateWithFlags(&p.out_ready[i], cudaEventDisableTiming);
+    if (e == cudaSuccess) e = cudaEventCreateWithFlags(&p.out_free[i], cudaEventDisableTiming);
+  }
+  if (e != cudaSuccess) {
+    pipe_release(s);
+    return set_cuda_error(e, "session pipeline setup");
+  }
+  p.ready = true;
+  return SDX_OK;
+}
 
 static size_t desc_size(int kind) {
   switch (kind) {
@@ -226,9 +274,65 @@ int sdx_session_enqueue_node(sdx_session* s, int index) {
   return run_node(s, s->nodes[(size_t)index]);
 }
 
+int sdx_session_submit(sdx_session* s, const void* host_in, void* host_out) {
+  if (!s || !s->built) return set_error(SDX_ERR_INVALID, "session not built");
+  if (s->ctx->poisoned) return set_error(SDX_ERR_POISONED, "context saw a device error; close and reopen it");
+  cudaSetDevice(s->ctx->device);
+  int rc = pipe_setup(s);
+  if (rc) return rc;
+  sdx_session::Pipe& p = s->pipe;
+  const int slot = (int)(p.submitted & 1u);
+  const bool reuse = p.submitted >= 2;  // the slot's events were recorded by submission i-2
+#define PCK(call, what)                                         \
+  do {                                                          \
+    cudaError_t e_ = (call);                                    \
+    if (e_ != cudaSuccess) return set_cuda_error(e_, what);     \
+  } while (0)
+  if (host_in && s->in_bytes) {
+    // the staging slot is free once submission i-2 copied it into the arena
+    if (reuse) PCK(cudaStreamWaitEvent(p.h2d, p.in_free[slot], 0), "wait input slot");
+    rc = sdx_memcpy_htod_async(s->ctx, reinterpret_cast<sdx_dptr>(p.stage_in[slot]), host_in, s->in_bytes, p.h2d);
+    if (rc) return rc;
+    PCK(cudaEventRecord(p.in_landed[slot], p.h2d), "record input landed");
+    PCK(cudaStreamWaitEvent(s->stream, p.in_landed[slot], 0), "wait input landed");
+    PCK(cudaMemcpyAsync(reinterpret_cast<void*>(s->in), p.stage_in[slot], s->in_bytes, cudaMemcpyDeviceToDevice,
+                        s->stream), "input into the arena");
+    PCK(cudaEventRecord(p.in_free[slot], s->stream), "record input slot free");
+  }
+  rc = sdx_session_enqueue(s);
+  if (rc) return rc;
+  if (host_out && s->out_bytes) {
+    if (reuse) PCK(cudaStreamWaitEvent(s->stream, p.out_free[slot], 0), "wait output slot");
+    PCK(cudaMemcpyAsync(p.stage_out[slot], reinterpret_cast<void*>(s->out), s->out_bytes, cudaMemcpyDeviceToDevice,
+                        s->stream), "output out of the arena");
+    PCK(cudaEventRecord(p.out_ready[slot], s->stream), "record output ready");
+    PCK(cudaStreamWaitEvent(p.d2h, p.out_ready[slot], 0), "wait output ready");
+    rc = sdx_memcpy_dtoh_async(s->ctx, host_out, reinterpret_cast<sdx_dptr>(p.stage_out[slot]), s->out_bytes, p.d2h);
+    if (rc) return rc;
+    PCK(cudaEventRecord(p.out_free[slot], p.d2h), "record output slot free");
+  }
+#undef PCK
+  p.submitted++;
+  return SDX_OK;
+}
+
+int sdx_session_wait(sdx_session* s, int timeout_ms) {
+  if (!s) return set_error(SDX_ERR_INVALID, "null session");
+  cudaSetDevice(s->ctx->device);
+  int rc = sdx_stream_sync(s->ctx, s->stream, timeout_ms);
+  if (rc) return rc;
+  if (s->pipe.ready) {
+    rc = sdx_stream_sync(s->ctx, s->pipe.d2h, timeout_ms);
+    if (rc) return rc;
+    rc = sdx_stream_sync(s->ctx, s->pipe.h2d, timeout_ms);
+  }
+  return rc;
+}
+
 int sdx_session_destroy(sdx_session* s) {
   if (!s) return SDX_OK;
   cudaSetDevice(s->ctx->device);
+  pipe_release(s);
   cudaStreamSynchronize(s->stream);
   if (s->graph) cudaGraphExecDestroy(s->graph);
   if (s->arena) cudaFree(s->arena);

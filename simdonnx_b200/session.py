@@ -399,16 +399,29 @@ class CudaInferenceSession:
             off = self.plan.offsets[name] - self.in_off
             buf[off:off + a.nbytes] = a.view(np.uint8).ravel()
 
-    def run(self, feeds: dict | None = None, timeout_ms: int = 0) -> np.ndarray:
-        """End-to-end: pinned host input -> device, graph, device -> pinned host output, wait."""
+    def run(self, feeds: dict | None = None, timeout_ms: int = 0, copy: bool = True) -> np.ndarray:
+        """End-to-end: pinned host input -> device, graph, device -> pinned host output, wait.
+        copy=False returns a view of the pinned output buffer (valid until the next run)."""
         pin_in, pin_out = self.pinned_io()
         if feeds is not None:
             self.stage_inputs(feeds)
         N.call("sdx_session_run", self.h, ctypes.c_void_p(pin_in.data_ptr()), ctypes.c_void_p(pin_out.data_ptr()),
                timeout_ms)
+        return self._output_view(pin_out, copy)
+
+    def _output_view(self, pin_out, copy: bool) -> np.ndarray:
         ov = self.plan.values[self.plan.output]
         dt = np.float16 if ov.dtype == "f16" else np.float32
-        return pin_out.numpy().view(dt).reshape(ov.shape).astype(np.float32)
+        y = pin_out.numpy().view(dt).reshape(ov.shape)
+        return y.astype(np.float32) if (copy or dt != np.float32) else y
+
+    def submit(self, pin_in: torch.Tensor, pin_out: torch.Tensor) -> None:
+        """Pipelined end-to-end run (sdx_session_submit): returns at once; the pinned buffers must
+        stay untouched until wait()."""
+        N.call("sdx_session_submit", self.h, ctypes.c_void_p(pin_in.data_ptr()), ctypes.c_void_p(pin_out.data_ptr()))
+
+    def wait(self, timeout_ms: int = 0) -> None:
+        N.call("sdx_session_wait", self.h, timeout_ms)
 
     def close(self) -> None:
         if getattr(self, "h", None):
