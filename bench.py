@@ -262,38 +262,54 @@ def main() -> None:
              "hbm_gbs": tot["bytes"] / step_s / 1e9, "hbm_frac": tot["bytes"] / step_s / 1e9 / hbm}
 
     # ---- end to end through the C-ABI run call (pinned host I/O inside each step)
-    e2e = None
-    if not args.no_e2e:
-        # (a) pipelined: K sdx_session_submit calls over two pinned host buffer pairs, then one wait;
-        #     each step copies its fp32 input host -> device and its fp32 output device -> host
-        sess.stage_inputs(feeds)
-        pin_in, pin_out = sess.pinned_io()
+    def e2e_measure(es, efeeds):
+        """(pipelined, serial) seconds for K steps through the C ABI with pinned host buffers."""
+        es.stage_inputs(efeeds)
+        pin_in, pin_out = es.pinned_io()
         pairs = [(pin_in, pin_out), (pin_in.clone().pin_memory(), torch.empty_like(pin_out).pin_memory())]
-        sess.submit(*pairs[0])
-        sess.wait(120000)
+        es.submit(*pairs[0])
+        es.wait(120000)
         barrier()
         t0 = time.perf_counter()
         for i in range(args.steps):
-            sess.submit(*pairs[i % 2])
-        sess.wait(120000)
+            es.submit(*pairs[i % 2])
+        es.wait(120000)
         el = time.perf_counter() - t0
-        # (b) serial: K synchronous sdx_session_run calls (copy in, compute, copy out, wait)
         barrier()
         t1 = time.perf_counter()
         for _ in range(args.steps):
-            sess.run(timeout_ms=120000, copy=False)
+            es.run(timeout_ms=120000, copy=False)
         el_serial = time.perf_counter() - t1
         barrier()
         if world > 1:
             t = torch.tensor([el, el_serial], device="cuda")
             dist.all_reduce(t, op=dist.ReduceOp.MAX)
             el, el_serial = float(t[0].item()), float(t[1].item())
-        e2e = {"value": images / el, "unit": "images/s", "h2d_bytes_per_step": sess.in_bytes,
-               "d2h_bytes_per_step": sess.out_bytes,
-               "timing": "host wall clock from the first of K pipelined sdx_session_submit calls to "
+        return el, el_serial
+
+    e2e = None
+    if not args.no_e2e:
+        # (1) fp32 tensor input (the plan measured above)
+        el_t, el_ts = e2e_measure(sess, feeds)
+        tensor_e2e = {"value": images / el_t, "unit": "images/s", "h2d_bytes_per_step": sess.in_bytes,
+                      "d2h_bytes_per_step": sess.out_bytes, "serial_value": images / el_ts}
+        sess_bytes = (sess.in_bytes, sess.out_bytes)
+        sess.close()
+        # (2) image-session input: u8 RGB pixels, normalized on the device (sdx_image_to_tensor)
+        iplan = configs.build_det(batch=args.batch, hw=HW, image_input=True)
+        ifeeds = {k: f() for k, f in iplan.feeds.items()}
+        isess = CudaInferenceSession(iplan, device=local)
+        el_i, el_is = e2e_measure(isess, ifeeds)
+        e2e = {"value": images / el_i, "unit": "images/s", "h2d_bytes_per_step": isess.in_bytes,
+               "d2h_bytes_per_step": isess.out_bytes, "input": "u8 RGB images [N,640,640,3], normalized on the device",
+               "timing": "host wall clock from the first of K pipelined sdx_session_submit calls (pinned host "
+                         "buffers: H2D of the step's images, D2H of its fp32 probability map) to "
                          "sdx_session_wait, max over ranks",
-               "serial_value": images / el_serial,
-               "serial_timing": "host wall clock around K synchronous sdx_session_run calls"}
+               "serial_value": images / el_is,
+               "serial_timing": "host wall clock around K synchronous sdx_session_run calls",
+               "fp32_tensor_input": tensor_e2e}
+        isess.close()
+        del sess_bytes
 
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
@@ -315,7 +331,8 @@ def main() -> None:
             "launches_per_step": launches_per_step, "clocks": clk,
         }
         print(json.dumps(line), flush=True)
-    sess.close()
+    if args.no_e2e:
+        sess.close()
     if world > 1:
         dist.barrier()
         dist.destroy_process_group()

@@ -239,6 +239,20 @@ int sdx_resize_nearest(sdx_ctx* ctx, const sdx_resize_desc* d, sdx_stream s);
 /* NHWC channel concat (Nhwc.ConcatInner, src/Kernels/Nhwc.Det.cs:354-370), fp16, up to 8 inputs. */
 int sdx_concat_channels(sdx_ctx* ctx, int64_t pixels, int nin, const int* counts, const sdx_dptr* ins,
                         sdx_dptr y, sdx_stream s);
+/* Image-session preprocessing (the reference's Vulkan image session, src/Backends/Vulkan/
+ * VkImageSession.cs; shader src/Backends/Vulkan/Shaders/img2nhwc.comp:4-37): interleaved u8 pixels
+ * (bpp 3 or 4, row stride `stride` bytes, images `image_bytes` apart; 0 = packed) mapped through
+ * lut[c * 256 + byte] (fp32 [3][256], tensor channel c; swap_rb = 1 takes channel 0 from byte 2),
+ * replicate padding around the image placed at (pad_t, pad_l) of the [oh, ow] tensor. Output fp32
+ * NCHW [batch, 3, oh, ow] (y_nhwc_f16 = 0) or fp16 NHWC [batch, oh, ow, 3]. */
+typedef struct sdx_image_desc {
+  int batch, ih, iw, bpp, swap_rb;
+  int oh, ow, pad_t, pad_l, y_nhwc_f16;
+  int64_t stride, image_bytes;
+  sdx_dptr src, lut, y;
+} sdx_image_desc;
+int sdx_image_to_tensor(sdx_ctx* ctx, const sdx_image_desc* d, sdx_stream s);
+
 /* Channel concat of nearest-upsampled inputs: y[n, oy, ox, off_i + c] = x_i[n, oy / s_i, ox / s_i, c]
  * (a Concat whose inputs are ResizeNearest outputs, Nhwc.ResizeNearest src/Kernels/Nhwc.Det.cs:160-200,
  * fused with Nhwc.ConcatInner). Input i is [batch, oh / s_i, ow / s_i, counts[i]] fp16 NHWC; s_i = 1
@@ -276,7 +290,7 @@ enum sdx_op_kind {
   SDX_OP_CONV = 1, SDX_OP_GEMM = 2, SDX_OP_CONVT = 3, SDX_OP_POOL = 4, SDX_OP_CHANNEL_GATE = 5,
   SDX_OP_CHANNEL_BROADCAST = 6, SDX_OP_RESIZE_NEAREST = 7, SDX_OP_CONCAT = 8, SDX_OP_BINARY = 9, SDX_OP_ACT = 10,
   SDX_OP_CONVERT = 11, SDX_OP_LAYERNORM = 12, SDX_OP_SOFTMAX = 13, SDX_OP_ATTENTION = 14,
-  SDX_OP_CONCAT_NEAREST = 15
+  SDX_OP_CONCAT_NEAREST = 15, SDX_OP_IMAGE = 16
 };
 /* Generic argument block for the ops without a descriptor struct. */
 typedef struct sdx_misc_desc {

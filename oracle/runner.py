@@ -44,7 +44,7 @@ class OracleSession:
             if v.is_const:
                 env[name] = v.const
         for name in (P.inputs or [P.input]):
-            a = np.ascontiguousarray(feeds[name], np.float32)
+            a = np.ascontiguousarray(feeds[name], np.uint8 if P.values[name].dtype == "u8" else np.float32)
             assert a.shape == P.values[name].shape, (name, a.shape)
             env[name] = a
         for n in P.nodes:
@@ -126,4 +126,17 @@ class OracleSession:
             return np.ascontiguousarray(y.transpose(0, 2, 1, 3)).reshape(nb, t, p.heads * p.head_dim)
         if op == "Act":
             return O.act(env[n.ins[0]], p)
+        if op == "ImageToTensor":
+            # img2nhwc.comp (src/Backends/Vulkan/Shaders/img2nhwc.comp:24-37): replicate padding,
+            # byte -> lut[c][byte], channel 0 from byte 2 when swapped; here fp32 NCHW
+            img = env[n.ins[0]]
+            lut = P.values[p.lut].const.reshape(3, 256)
+            out = P.values[n.outs[0]]
+            nb, _, oh, ow = out.shape
+            ih, iw = img.shape[1], img.shape[2]
+            sy = np.clip(np.arange(oh) - p.pads[0], 0, ih - 1)
+            sx = np.clip(np.arange(ow) - p.pads[1], 0, iw - 1)
+            px = img[:, sy][:, :, sx]
+            order = (2, 1, 0) if p.swap_rb else (0, 1, 2)
+            return np.stack([lut[c][px[..., order[c]]] for c in range(3)], axis=1).astype(np.float32)
         raise NotImplementedError(op)

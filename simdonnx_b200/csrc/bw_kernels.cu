@@ -533,6 +533,52 @@ int broadcast_launch(int batch, int64_t pixels, int c, int op, int relu, const _
   return SDX_OK;
 }
 
+// ------------------------------------------------------------------ image -> tensor
+// Image-session preprocessing (img2nhwc.comp of the reference's Vulkan image session,
+// src/Backends/Vulkan/Shaders/img2nhwc.comp:4-37): interleaved u8 pixels (3 or 4 bytes, optional
+// R/B swap) mapped through a per-channel table lut[c][byte], replicate padding around an image
+// placed at (pt, pl) in the tensor; here written as fp32 NCHW planes (the graph input of the det
+// and UNet plans) or fp16 NHWC. One block per output row; the table sits in shared memory.
+__global__ void image_kernel(ImageArgs a) {
+  __shared__ float lut[3 * 256];
+  for (int i = threadIdx.x; i < 3 * 256; i += blockDim.x) lut[i] = __ldg(a.lut + i);
+  __syncthreads();
+  const int row = blockIdx.x;  // n * oh + oy
+  const int n = row / a.oh, oy = row - n * a.oh;
+  const int sy = min(max(oy - a.pt, 0), a.ih - 1);
+  const uint8_t* srow = a.src + (int64_t)n * a.img_bytes + (int64_t)sy * a.stride;
+  const int ob = a.swap ? 2 : 0;
+  for (int ox = threadIdx.x; ox < a.ow; ox += blockDim.x) {
+    const int sx = min(max(ox - a.pl, 0), a.iw - 1);
+    const uint8_t* px = srow + (int64_t)sx * a.bpp;
+    const float v0 = lut[px[ob]], v1 = lut[256 + px[1]], v2 = lut[512 + px[2 - ob]];
+    if (a.y_nhwc_f16) {
+      __half* y = static_cast<__half*>(a.y) + ((int64_t)row * a.ow + ox) * 3;
+      y[0] = __float2half_rn(v0);
+      y[1] = __float2half_rn(v1);
+      y[2] = __float2half_rn(v2);
+    } else {
+      float* y = static_cast<float*>(a.y);
+      const int64_t plane = (int64_t)a.oh * a.ow, o = (int64_t)n * 3 * plane + (int64_t)oy * a.ow + ox;
+      y[o] = v0;
+      y[o + plane] = v1;
+      y[o + 2 * plane] = v2;
+    }
+  }
+}
+
+int image_launch(const ImageArgs& a, cudaStream_t st) {
+  if (a.bpp != 3 && a.bpp != 4) return set_error(SDX_ERR_INVALID, "image: 3 or 4 bytes per pixel");
+  if (a.ih <= 0 || a.iw <= 0 || a.oh <= 0 || a.ow <= 0 || a.batch <= 0) return set_error(SDX_ERR_INVALID, "image: empty");
+  if (a.stride < (int64_t)a.iw * a.bpp || a.img_bytes < a.stride * a.ih) return set_error(SDX_ERR_INVALID, "image: stride");
+  if (!a.src || !a.lut || !a.y) return set_error(SDX_ERR_INVALID, "image: null pointer");
+  const int64_t rows = (int64_t)a.batch * a.oh;
+  if (rows > INT32_MAX) return set_error(SDX_ERR_NOT_SUPPORTED, "image: too large");
+  image_kernel<<<(unsigned)rows, 256, 0, st>>>(a);
+  SDX_LAUNCH_CHECK("image");
+  return SDX_OK;
+}
+
 // ------------------------------------------------------------------ nearest resize (+ addend)
 // One block per output row (n, oy); threads walk the row's 16-byte chunks, so the index math is
 // 32-bit and per row. src = floor(dst / scale) (src/Kernels/Nhwc.Det.cs:173, :180).

@@ -775,6 +775,21 @@ int sdx_concat_channels(sdx_ctx* ctx, int64_t pixels, int nin, const int* counts
   return SDX_OK;
 }
 
+int sdx_image_to_tensor(sdx_ctx* ctx, const sdx_image_desc* d, sdx_stream s) {
+  USE(ctx);
+  if (!d) return set_error(SDX_ERR_INVALID, "null desc");
+  LAUNCH_GUARD();
+  ImageArgs a;
+  a.batch = d->batch; a.ih = d->ih; a.iw = d->iw; a.bpp = d->bpp; a.swap = d->swap_rb;
+  a.oh = d->oh; a.ow = d->ow; a.pt = d->pad_t; a.pl = d->pad_l; a.y_nhwc_f16 = d->y_nhwc_f16;
+  a.stride = d->stride > 0 ? d->stride : (int64_t)d->iw * d->bpp;
+  a.img_bytes = d->image_bytes > 0 ? d->image_bytes : a.stride * d->ih;
+  a.src = P<const uint8_t>(d->src);
+  a.lut = P<const float>(d->lut);
+  a.y = P<void>(d->y);
+  return image_launch(a, S(ctx, s));
+}
+
 int sdx_concat_nearest(sdx_ctx* ctx, int batch, int oh, int ow, int nin, const int* counts, const int* scales,
                        const sdx_dptr* ins, sdx_dptr y, sdx_stream s) {
   USE(ctx);

@@ -141,6 +141,15 @@ struct ResizeArgs {
 };
 int resize_launch(const ResizeArgs& a, cudaStream_t st);
 
+struct ImageArgs {
+  int batch, ih, iw, bpp, swap, oh, ow, pt, pl, y_nhwc_f16;
+  int64_t stride, img_bytes;  // source row stride and per-image stride, bytes
+  const uint8_t* src;
+  const float* lut;           // [3][256]
+  void* y;
+};
+int image_launch(const ImageArgs& a, cudaStream_t st);
+
 struct ConcatNearestArgs {
   int batch, oh, ow, nin, ctot;
   int c[8], s[8], off[8];  // channels, upsampling scale and first output channel of input i

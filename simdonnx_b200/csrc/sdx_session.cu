@@ -94,6 +94,7 @@ static size_t desc_size(int kind) {
     case SDX_OP_SOFTMAX:
     case SDX_OP_ATTENTION:
     case SDX_OP_CONCAT_NEAREST: return sizeof(sdx_misc_desc);
+    case SDX_OP_IMAGE: return sizeof(sdx_image_desc);
     default: return 0;
   }
 }
@@ -112,6 +113,7 @@ static int run_node(sdx_session* s, const sdx_session::Node& n) {
     case SDX_OP_RESIZE_NEAREST: return sdx_resize_nearest(c, static_cast<const sdx_resize_desc*>(d), st);
     case SDX_OP_CHANNEL_BROADCAST: return sdx_channel_broadcast(c, m->batch, m->pixels, m->c, m->op, m->relu, m->x, m->b, m->y, st);
     case SDX_OP_CONCAT: return sdx_concat_channels(c, m->pixels, m->nin, m->counts, m->ins, m->y, st);
+    case SDX_OP_IMAGE: return sdx_image_to_tensor(c, static_cast<const sdx_image_desc*>(d), st);
     case SDX_OP_CONCAT_NEAREST:
       return sdx_concat_nearest(c, m->batch, (int)m->rows, (int)m->n, m->nin, m->counts, m->aux, m->ins, m->y, st);
     case SDX_OP_BINARY: return sdx_binary(c, m->n, m->op, m->relu, m->a, m->b, m->y, st);

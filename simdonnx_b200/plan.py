@@ -89,6 +89,15 @@ class AttentionP:
 
 
 @dataclass
+class ImageP:
+    """Image-session preprocessing (VkImageSession / img2nhwc.comp): u8 pixels -> lut -> tensor."""
+    lut: str                     # const fp32 [3, 256]
+    bpp: int = 3
+    swap_rb: bool = False
+    pads: tuple = (0, 0)         # image position (top, left) inside the tensor; replicate padding
+
+
+@dataclass
 class Value:
     name: str
     shape: tuple
@@ -103,7 +112,7 @@ class Value:
 
     @property
     def nbytes(self) -> int:
-        return int(np.prod(self.shape)) * (2 if self.dtype == "f16" else 4)
+        return int(np.prod(self.shape)) * {"f16": 2, "u8": 1}.get(self.dtype, 4)
 
 
 @dataclass

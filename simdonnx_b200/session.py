@@ -268,6 +268,19 @@ class CudaInferenceSession:
             d.add = self.ptr(n.ins[1]) if len(n.ins) > 1 else 0
             d.y = self.ptr(n.outs[0])
             return N.OP_RESIZE_NEAREST, d
+        if op == "ImageToTensor":
+            img, yv = P.values[n.ins[0]], P.values[n.outs[0]]
+            nb, ih, iw, bpp = img.shape
+            d = N.ImageDesc()
+            d.batch, d.ih, d.iw, d.bpp, d.swap_rb = nb, ih, iw, bpp, int(p.swap_rb)
+            if yv.layout == "nchw":
+                d.oh, d.ow, d.y_nhwc_f16 = yv.shape[2], yv.shape[3], 0
+            else:
+                d.oh, d.ow, d.y_nhwc_f16 = yv.shape[1], yv.shape[2], 1
+            d.pad_t, d.pad_l = p.pads
+            d.stride, d.image_bytes = iw * bpp, ih * iw * bpp
+            d.src, d.lut, d.y = self.ptr(n.ins[0]), self._f32(p.lut), self.ptr(n.outs[0])
+            return N.OP_IMAGE, d
         if op == "ConcatNearest":
             nb, oh, ow, _ = P.shape(n.outs[0])
             d = N.MiscDesc()
@@ -362,9 +375,10 @@ class CudaInferenceSession:
     def write_inputs(self, feeds: dict) -> None:
         """Copy host inputs into the arena (synchronous)."""
         for name in self.plan.inputs:
-            a = np.ascontiguousarray(feeds[name], np.float32)
+            dt = self.plan.values[name].dtype
+            a = np.ascontiguousarray(feeds[name], np.uint8 if dt == "u8" else np.float32)
             t = torch.from_numpy(a).to(self.device)
-            if self.plan.values[name].dtype == "f16":
+            if dt == "f16":
                 t = t.half()
             torch.cuda.synchronize(self.device)
             N.call("sdx_memcpy_dtod_async", self.be.ctx, self.ptr(name), B.ptr(t), t.numel() * t.element_size(),
@@ -393,8 +407,9 @@ class CudaInferenceSession:
         pin_in, _ = self.pinned_io()
         buf = pin_in.numpy()
         for name in self.plan.inputs:
-            a = np.ascontiguousarray(feeds[name], np.float32)
-            if self.plan.values[name].dtype == "f16":
+            dt = self.plan.values[name].dtype
+            a = np.ascontiguousarray(feeds[name], np.uint8 if dt == "u8" else np.float32)
+            if dt == "f16":
                 a = a.astype(np.float16)
             off = self.plan.offsets[name] - self.in_off
             buf[off:off + a.nbytes] = a.view(np.uint8).ravel()

@@ -57,5 +57,9 @@ class Rng:
     def uniform(self, name: str, shape, lo=0.0, hi=1.0):
         return uniform(name_seed(self.seed, name), shape, lo, hi)
 
+    def bytes(self, name: str, shape) -> np.ndarray:
+        """Seeded uniform u8 values (synthetic image pixels)."""
+        return (splitmix64(name_seed(self.seed, name), int(np.prod(shape))) >> np.uint64(56)).astype(np.uint8).reshape(shape)
+
     def normal(self, name: str, shape, std=1.0, mean=0.0):
         return normal(name_seed(self.seed, name), shape, std, mean)

@@ -143,3 +143,13 @@ def test_pipelined_submit_matches_run():
         got = sess._output_view(po, True)
         assert np.array_equal(got, want[i]), f"batch {i}"
     sess.close()
+
+
+def test_det_image_input_n1():
+    """Image-session input: u8 pixels normalized on the device (sdx_image_to_tensor) feeding the det
+    model; against the oracle running the same plan."""
+    from simdonnx_b200 import configs
+    plan = configs.build_det(batch=1, image_input=True)
+    sess, feeds, ref, got = _run_both(plan)
+    assert_close(got, ref[plan.output], "det (image input) output")
+    sess.close()

@@ -90,3 +90,28 @@ def test_seeded_inputs_are_batch_prefix_stable():
     xb = b.feeds[b.input]()
     assert np.array_equal(xa[0], xb[0])
     assert xb.min() >= 0 and xb.max() < 1
+
+
+def test_image_front_semantics_on_oracle():
+    """The image front (u8 pixels -> lut -> fp32 NCHW) matches a direct restatement of the
+    reference shader: replicate padding, per-channel table, optional R/B swap."""
+    import numpy as np
+    from oracle.runner import OracleSession
+    from simdonnx_b200.plan import ExecPlan, ImageP
+    P = ExecPlan()
+    img = P.add_value("img", (2, 5, 7, 4), "u8", "nhwc")
+    lut = P.add_const("lut", (np.arange(768, dtype=np.float32).reshape(3, 256) * 0.01))
+    y = P.add_value("y", (2, 3, 9, 11), "f32", "nchw")
+    P.add_node("ImageToTensor", [img], [y], ImageP(lut, bpp=4, swap_rb=True, pads=(1, 2)), "image")
+    P.inputs, P.input, P.output = [img], img, y
+    rng = np.random.default_rng(3)
+    pix = rng.integers(0, 256, (2, 5, 7, 4), dtype=np.uint8)
+    got = OracleSession(P).run({img: pix})[y]
+    table = P.values[lut].const
+    for n in range(2):
+        for c in range(3):
+            for oy in range(9):
+                for ox in range(11):
+                    sy, sx = min(max(oy - 1, 0), 4), min(max(ox - 2, 0), 6)
+                    byte = pix[n, sy, sx, 2 - c]  # swapped: channel 0 from byte 2
+                    assert got[n, c, oy, ox] == table[c, byte]
