@@ -100,16 +100,32 @@ __device__ __forceinline__ bool mbar_try_wait(uint32_t bar, uint32_t parity) {
   return done != 0;
 }
 
+// try_wait with a suspend-time hint: the waiting thread is suspended (not spinning, so it takes no
+// issue slots from the warps that share its scheduler) until the phase completes or about
+// `hint_ns` passes.
+__device__ __forceinline__ bool mbar_try_wait_sleep(uint32_t bar, uint32_t parity, uint32_t hint_ns) {
+  uint32_t done;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2, %3;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}"
+      : "=r"(done)
+      : "r"(bar), "r"(parity), "r"(hint_ns)
+      : "memory");
+  return done != 0;
+}
+
 // Waits until the phase of `bar` with parity `parity` has completed. Bounded: returns false (after
 // recording `code` and raising *abort_flag) when SDX_WAIT_NS passes, or at once when another role
-// of the CTA has already raised *abort_flag.
+// of the CTA has already raised *abort_flag. After the first probe the thread sleeps in the barrier
+// (suspend hint) between checks of the abort flag and the clock.
 __device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity, unsigned int* err, unsigned int code,
                                           volatile int* abort_flag) {
   if (mbar_try_wait(bar, parity)) return true;
   uint64_t t0 = global_timer_ns();
   for (uint32_t it = 1;; ++it) {
-    if (mbar_try_wait(bar, parity)) return true;
-    if ((it & 255u) == 0) {
+    if (mbar_try_wait_sleep(bar, parity, 20000u)) return true;
+    if ((it & 15u) == 0) {
       if (*abort_flag) return false;
       if (global_timer_ns() - t0 > SDX_WAIT_NS) {
         record_error(err, code);
