@@ -21,7 +21,7 @@ import torch
 
 from . import _native as N
 from . import backend as B
-from .plan import ExecPlan, Node
+from .plan import ExecPlan, Node, conv_out
 
 _DT = {"f16": N.F16, "f32": N.F32}
 _LAY = {"nhwc": N.NHWC, "nchw": N.NCHW, "raw": N.NHWC}
@@ -37,6 +37,27 @@ def cuda_rewrite(plan: ExecPlan) -> ExecPlan:
     P.values = {k: copy.copy(v) for k, v in plan.values.items()}
     P.nodes = [Node(n.op, list(n.ins), list(n.outs), copy.copy(n.p), n.name) for n in plan.nodes]
     P.inputs = list(plan.inputs or [plan.input])
+
+    # 0. conv + fused 2x2/2 max pool (ConvP.Pool, src/Engine/ExecPlan.cs:63-64) -> conv into an arena
+    #    value, then MaxPool (+relu): max of fp16-rounded values == fp16 rounding of the max, so the
+    #    result equals the fused kernel's
+    out_nodes = []
+    for n in P.nodes:
+        if n.op == "Conv" and n.p.pool is not None:
+            pool = n.p.pool
+            yv = P.values[n.outs[0]]
+            nb, ih, iw, _ = _nhwc_shape(P.values[n.ins[0]])
+            oc = yv.shape[3]
+            k, st, pd = n.p.kernel, n.p.strides, n.p.pads
+            ch, cw = conv_out(ih, k[0], st[0], pd[0], pd[2]), conv_out(iw, k[1], st[1], pd[1], pd[3])
+            full = P.add_value(n.outs[0] + ".prepool", (nb, ch, cw, oc), yv.dtype, "nhwc")
+            conv = Node("Conv", list(n.ins), [full], copy.copy(n.p), n.name)
+            conv.p.pool = None
+            out_nodes.append(conv)
+            out_nodes.append(Node("MaxPool", [full], list(n.outs), pool, n.name + ".pool"))
+            continue
+        out_nodes.append(n)
+    P.nodes = out_nodes
 
     # 1. fp32 NHWC graph input read by a tensor-core conv -> explicit conversion to fp16
     out_nodes = []

@@ -153,3 +153,20 @@ def test_det_image_input_n1():
     sess, feeds, ref, got = _run_both(plan)
     assert_close(got, ref[plan.output], "det (image input) output")
     sess.close()
+
+
+@pytest.mark.parametrize("ic,oc,act,pool_relu", [(16, 32, "relu", False), (3, 16, "none", True), (64, 64, "hardswish", False)])
+def test_conv_pool_node(ic, oc, act, pool_relu):
+    """A6: conv + fused 2x2/2 max pool against the oracle's ConvPool (Nhwc.ConvPool)."""
+    from simdonnx_b200 import configs
+    from simdonnx_b200.plan import PoolP
+    b = configs._Builder(ic + oc)
+    P = b.P
+    x = P.add_value("x", (2, 37, 30, ic), "f32", "nhwc")
+    P.inputs, P.input = [x], x
+    y = b.conv("cp", x, oc, 3, act=act, pool=PoolP((2, 2), (2, 2), fuse_relu=pool_relu))
+    P.output = y
+    P.feeds = {x: lambda: b.rng.uniform("x", (2, 37, 30, ic), -1, 1)}
+    sess, feeds, ref, got = _run_both(P)
+    assert_close(got, ref[P.output], f"conv+pool {ic}->{oc}")
+    sess.close()

@@ -115,3 +115,19 @@ def test_image_front_semantics_on_oracle():
                     sy, sx = min(max(oy - 1, 0), 4), min(max(ox - 2, 0), 6)
                     byte = pix[n, sy, sx, 2 - c]  # swapped: channel 0 from byte 2
                     assert got[n, c, oy, ox] == table[c, byte]
+
+
+def test_conv_pool_split_for_cuda():
+    """ConvP.Pool (fused 2x2/2 max pool) runs on CUDA as conv -> MaxPool (+relu) over an arena value."""
+    from simdonnx_b200.plan import PoolP
+    b = configs._Builder(5)
+    P = b.P
+    x = P.add_value("x", (1, 17, 22, 16))
+    P.inputs, P.input = [x], x
+    y = b.conv("cp", x, 32, 3, act="relu", pool=PoolP((2, 2), (2, 2), fuse_relu=True))
+    P.output = y
+    R = cuda_rewrite(P)
+    ops = [(n.op, n.outs[0]) for n in R.nodes]
+    assert ops == [("Conv", "cp.prepool"), ("MaxPool", "cp")]
+    assert R.shape("cp.prepool") == (1, 17, 22, 32) and R.shape("cp") == (1, 8, 11, 32)
+    assert R.nodes[1].p.fuse_relu
