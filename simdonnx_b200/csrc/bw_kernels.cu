@@ -400,15 +400,15 @@ int pool_launch(const PoolArgs& a, cudaStream_t st) {
 // Stage 1: per (image, pixel chunk) channel sums into scratch; stage 2: one CTA per image reduces
 // the chunks, forms the means, runs FC1 (+relu) and FC2 and the (hard) sigmoid gate
 // (Nhwc.ChannelGate, src/Kernels/Nhwc.Det.cs:287-314).
-// Pixel chunks per image depend on the image size only, so an image's gate (and everything after
-// it) is bit-identical whatever batch it runs in.
-static int gate_chunks(int batch, int hw) {
-  (void)batch;
-  return std::min(64, std::max(1, (hw + 2047) / 2048));
+// Pixel chunks per image (about 64 KB of input each, at most 64) depend on the image's size only,
+// so an image's gate (and everything after it) is bit-identical whatever batch it runs in.
+static int gate_chunks(int hw, int c) {
+  const int64_t bytes = (int64_t)hw * c * 2;
+  return (int)std::min<int64_t>(64, std::max<int64_t>(1, std::min<int64_t>(hw, (bytes + 65535) / 65536)));
 }
 
 size_t gate_scratch_bytes(int batch, int hw, int c) {
-  return sizeof(float) * (size_t)batch * gate_chunks(batch, hw) * c;
+  return sizeof(float) * (size_t)batch * gate_chunks(hw, c) * c;
 }
 
 __global__ void gap_partial_kernel(const __half* __restrict__ x, int hw, int c, int chunks, float* __restrict__ partial) {
@@ -473,7 +473,7 @@ __global__ void gate_fc_kernel(GateArgs a, int chunks) {
 int gate_launch(const GateArgs& a, cudaStream_t st) {
   if (a.c % 8 != 0 || a.c > 4096) return set_error(SDX_ERR_NOT_SUPPORTED, "channel gate: c must be a multiple of 8, <= 4096");
   if (!a.partial) return set_error(SDX_ERR_INVALID, "channel gate: scratch buffer missing");
-  const int chunks = gate_chunks(a.batch, a.hw);
+  const int chunks = gate_chunks(a.hw, a.c);
   const int cg = a.c / 8;
   int block = std::max(cg, std::min(256, (256 / cg) * cg));
   if (block > 1024) return set_error(SDX_ERR_NOT_SUPPORTED, "channel gate: too many channels");
