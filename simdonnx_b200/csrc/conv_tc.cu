@@ -81,6 +81,8 @@ struct TcArgs {
   int taps, kw;
   int pad_t, pad_l;
   int OH, OW, BH, BW, tiles_h, tiles_w;
+  int BWs;              // tile step along x (BW, or BW - 2 in kx-in-N mode: the halo columns overlap)
+  int kxn;              // 3x3 conv with the column taps as GEMM columns (kx * 32 + oc)
   int b_rows_per_tap;
   int stages;
   int acc_stride;
@@ -495,7 +497,7 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
           const int r = m_tile - img * per_img;
           const int ty = r / a.tiles_w;
           oy0 = ty * a.BH;
-          ox0 = (r - ty * a.tiles_w) * a.BW;
+          ox0 = (r - ty * a.tiles_w) * a.BWs;
         }
         int tk = 0, cg = 0;  // tk: tap, or kx in halo mode; cg: channel-block group
         for (int kb = 0; kb < kblocks; kb++) {
@@ -643,7 +645,7 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
         t.img = m_tile / per_img;
         const int r = m_tile - t.img * per_img;
         t.oy0 = (r / a.tiles_w) * a.BH;
-        t.ox0 = (r % a.tiles_w) * a.BW;
+        t.ox0 = (r % a.tiles_w) * a.BWs;
       }
     };
     // column groups of a tile that start inside the tensor (a group fully past N is skipped)
@@ -706,6 +708,78 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
       const uint32_t slab = stage0 + sbi * a.sbuf_bytes;
       const uint32_t srow = slab + (uint32_t)lane * P;
       const uint32_t tbase = tmem_base + ((uint32_t)(q * 32) << 16) + acc * (uint32_t)a.acc_stride;
+      if (a.kxn) {
+        // kx-in-N: columns kx * 32 + oc; row x of the tile is input column ox0 - 1 + x, and the
+        // output at that column is D[x - 1][kx 0] + D[x][kx 1] + D[x + 1][kx 2] (neighbouring
+        // lanes: the 32 rows of a warp are consecutive columns of one or two tile rows)
+        float sum[32];
+#pragma unroll
+        for (int i = 0; i < 32; i++) sum[i] = 0.0f;
+#pragma unroll
+        for (int kx = 0; kx < 3; kx++) {
+          float v[32];
+          tmem_ld16_issue(tbase + (uint32_t)(kx * 32), v);
+          tmem_ld16_issue(tbase + (uint32_t)(kx * 32 + 16), v + 16);
+          tmem_wait_ld();
+          tmem_ld_wait16(v);
+          tmem_ld_wait16(v + 16);
+          if (kx == 2) {
+            tc_fence_before();
+            mbar_arrive(smem_u32(&acce[acc]));
+          }
+#pragma unroll
+          for (int i = 0; i < 32; i++) {
+            float u = v[i];
+            if (kx == 0) u = __shfl_up_sync(0xffffffffu, u, 1);
+            if (kx == 2) u = __shfl_down_sync(0xffffffffu, u, 1);
+            sum[i] += u;
+          }
+        }
+        const int h = row_in_tile / a.BW, x = row_in_tile - h * a.BW;
+        const int oy = tcd.oy0 + h, ox = tcd.ox0 - 1 + x;
+        if (x >= 1 && x <= a.BW - 2 && oy < a.OH && ox < a.OW) {
+          const int64_t px = ((int64_t)tcd.img * a.OH + oy) * a.OW + ox;
+#pragma unroll
+          for (int o0 = 0; o0 < 32; o0 += 8) {
+            if (o0 >= a.N) break;
+            float r8[8];
+#pragma unroll
+            for (int j = 0; j < 8; j++) {
+              const int o = o0 + j;
+              r8[j] = sum[o0 + j] + (a.bias_smem ? sBias[o] : (a.bias && o < a.N ? __ldg(a.bias + o) : 0.0f));
+            }
+            if (a.vec_ok && o0 + 8 <= a.N) {
+              if (a.res) {
+                float q8[8];
+                load8_res(a, px * a.res_pix_stride + a.res_ch_off + o0, q8);
+#pragma unroll
+                for (int j = 0; j < 8; j++) r8[j] += q8[j];
+              }
+#pragma unroll
+              for (int j = 0; j < 8; j++) r8[j] = act_t<ACT>(r8[j]);
+              store8(a, px * a.out_pix_stride + a.out_ch_off + o0, r8);
+            } else {
+#pragma unroll
+              for (int j = 0; j < 8; j++) {
+                const int o = o0 + j;
+                if (o >= a.N) continue;
+                float y = r8[j];
+                if (a.res) {
+                  const int64_t ro = px * a.res_pix_stride + a.res_ch_off + o;
+                  y += a.res_f32 ? static_cast<const float*>(a.res)[ro]
+                                 : __half2float(static_cast<const __half*>(a.res)[ro]);
+                }
+                y = act_t<ACT>(y);
+                const int64_t oo = px * a.out_pix_stride + a.out_ch_off + o;
+                if (a.out_f32) static_cast<float*>(a.out)[oo] = y;
+                else static_cast<__half*>(a.out)[oo] = __float2half_rn(y);
+              }
+            }
+          }
+        }
+        __syncwarp();
+        continue;
+      }
       const int nch = a.BN / 16;
       int g = 0, cg = 0;
       // 16-column chunks through two register buffers: the load of chunk c+1 is in flight while
@@ -897,6 +971,7 @@ int tc_launch(const TcProblem& p, cudaStream_t stream) {
   const bool convt = p.convt_oc > 0;
   int BN, n_tiles;
   if (convt) tc_plan_n_convt(p.convt_kh, p.convt_kw, p.convt_oc, &BN, &n_tiles);
+  else if (p.kxn) BN = 96, n_tiles = 1;
   else tc_plan_n(p.N, &BN, &n_tiles);
   const int kblk = tc_kblk(p.K), kpad = tc_kpad(p.K);
   const int kbytes = kblk * 2;
@@ -945,7 +1020,38 @@ int tc_launch(const TcProblem& p, cudaStream_t stream) {
   CUtensorMap mA, mB, mOut, mRes;
   memset(&mOut, 0, sizeof(mOut));
   memset(&mRes, 0, sizeof(mRes));
-  if (p.mode == TC_CONV) {
+  if (p.mode == TC_CONV && p.kxn) {
+    // kx-in-N: a virtual conv with the 3 row taps as pipeline taps (halo mode, one column block)
+    // and N = 3 x 32 columns (kx, oc); the A box is BW = BWs + 2 input columns wide, starting one
+    // column left of the tile, so row x of the tile holds input column ox0 - 1 + x
+    if (p.C % 8 != 0) return set_error(SDX_ERR_INVALID, "tc conv: input channels must be a multiple of 8");
+    const int BW = (p.OW + 13) / 14 * 14 <= (p.OW + 29) / 30 * 30 ? 16 : 32;  // less column waste
+    const int BH = TC_BM / BW;
+    a.kxn = 1;
+    a.halo = 1;
+    a.taps = 3;
+    a.kw = 1;
+    a.b_taps = 3;
+    a.b_rows_per_tap = BN * n_tiles;
+    a.BH = BH;
+    a.BW = BW;
+    a.BWs = BW - 2;
+    a.OH = p.OH;
+    a.OW = p.OW;
+    a.tiles_h = (p.OH + BH - 1) / BH;
+    a.tiles_w = (p.OW + a.BWs - 1) / a.BWs;
+    a.m_tiles = p.batch * a.tiles_h * a.tiles_w;
+    a.pad_t = 1;
+    a.pad_l = 1;
+    const int box_h = BH + 2;
+    a.a_box_bytes = (uint32_t)(box_h * BW * kbytes);
+    a.a_blk_bytes = (a.a_box_bytes + 1023u) & ~1023u;
+    uint64_t dims[4] = {(uint64_t)p.C, (uint64_t)p.W, (uint64_t)p.H, (uint64_t)p.batch};
+    uint64_t strides[3] = {(uint64_t)p.C * 2, (uint64_t)p.W * p.C * 2, (uint64_t)p.H * p.W * p.C * 2};
+    uint32_t box[4] = {(uint32_t)kblk, (uint32_t)BW, (uint32_t)box_h, 1};
+    int rc = encode_map(&mA, p.a, 4, dims, strides, box, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, swizzle_of(kbytes));
+    if (rc) return rc;
+  } else if (p.mode == TC_CONV) {
     if (p.C % 8 != 0) return set_error(SDX_ERR_INVALID, "tc conv: input channels must be a multiple of 8");
     // halo mode for kh > 1: tile widths of at least 8 pixels make the row offsets whole swizzle
     // atoms; used when three stages of it (A box + kh weight taps, two terms) and the staging fit,
@@ -963,6 +1069,7 @@ int tc_launch(const TcProblem& p, cudaStream_t stream) {
     a.b_taps = halo ? p.kh : 1;
     a.BH = BH;
     a.BW = BW;
+    a.BWs = BW;
     a.OH = p.OH;
     a.OW = p.OW;
     a.tiles_h = (p.OH + BH - 1) / BH;
@@ -1014,6 +1121,7 @@ int tc_launch(const TcProblem& p, cudaStream_t stream) {
   bool tma_out = G > 0 && G % 16 == 0 && aligned16(p.out) && (p.out_pix_stride * esz) % 16 == 0 &&
                  (p.out_ch_off * esz) % 16 == 0;
   if (convt) tma_out = tma_out && p.mode == TC_CONV;
+  if (p.kxn) tma_out = false;  // the kx-in-N epilogue stores per thread
   if (tma_out) {
     const int P = G * esz;
     a.G = G;
@@ -1158,6 +1266,29 @@ void tc_pack_conv(const float* w, int OC, int IC, int KH, int KW, int terms, __h
         if (terms == 1) out[idx] = __float2half_rn(v);
         else put2(out, idx, lo, v);
       }
+}
+
+bool tc_conv_kxn(int kh, int kw, int sh, int sw, int pt, int pl, int pb, int pr, int oc) {
+  return kh == 3 && kw == 3 && sh == 1 && sw == 1 && pt == 1 && pl == 1 && pb == 1 && pr == 1 && oc >= 8 && oc <= 32;
+}
+
+size_t tc_kxn_weights_halves(int K, int terms) {
+  return (size_t)(terms == 1 ? 1 : 2) * 3 * 96 * (size_t)tc_kpad(K);
+}
+
+// kx-in-N weights: [terms][ky][kx * 32 + o][Kpad], rows o >= OC zero.
+void tc_pack_conv_kxn(const float* w, int OC, int IC, int terms, __half* out) {
+  const size_t kpad = (size_t)tc_kpad(IC), lo = (size_t)3 * 96 * kpad;
+  memset(out, 0, sizeof(__half) * (terms == 1 ? 1 : 2) * lo);
+  for (int o = 0; o < OC; o++)
+    for (int c = 0; c < IC; c++)
+      for (int ky = 0; ky < 3; ky++)
+        for (int kx = 0; kx < 3; kx++) {
+          const size_t idx = ((size_t)ky * 96 + kx * 32 + o) * kpad + c;
+          const float v = w[((size_t)o * IC + c) * 9 + ky * 3 + kx];
+          if (terms == 1) out[idx] = __float2half_rn(v);
+          else put2(out, idx, lo, v);
+        }
 }
 
 // ConvT weights [IC][OC][KH][KW] -> one GEMM panel whose row tap*OC + o is w[:, o, tap].

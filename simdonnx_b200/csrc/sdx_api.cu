@@ -443,6 +443,10 @@ static int conv_route(const sdx_conv_desc* d) {
 
 // fp16 weight terms of a tensor-core conv: the caller's choice, else two for 1x1 kernels (their MMAs
 // hide under HBM time) and one for larger kernels (MMA-bound)
+static bool conv_kxn(const sdx_conv_desc* d) {
+  return tc_conv_kxn(d->kh, d->kw, d->sh, d->sw, d->pad_t, d->pad_l, d->pad_b, d->pad_r, d->oc);
+}
+
 static int conv_wterms(const sdx_conv_desc* d) {
   if (d->w_terms == 1 || d->w_terms == 2) return d->w_terms;
   return d->kh * d->kw > 1 ? 1 : 2;
@@ -456,7 +460,11 @@ int sdx_pack_conv(const sdx_conv_desc* d, const float* w, void* out, size_t* byt
   size_t need = 0;
   switch (route) {
     case R_TC_CONV:
-    case R_TC_ROWS: need = tc_weights_halves(d->oc, d->ic, taps, conv_wterms(d)) * sizeof(__half); break;
+    case R_TC_ROWS:
+      need = (route == R_TC_CONV && conv_kxn(d) ? tc_kxn_weights_halves(d->ic, conv_wterms(d))
+                                                : tc_weights_halves(d->oc, d->ic, taps, conv_wterms(d))) *
+             sizeof(__half);
+      break;
     case R_DEPTHWISE: need = sizeof(float) * (size_t)taps * d->ic; break;
     case R_DIRECT: need = sizeof(float) * (size_t)taps * d->ic * d->oc; break;
     default: return set_error(SDX_ERR_NOT_SUPPORTED, "conv: no CUDA kernel for this shape/flags");
@@ -468,7 +476,8 @@ int sdx_pack_conv(const sdx_conv_desc* d, const float* w, void* out, size_t* byt
   if (*bytes < need) return set_error(SDX_ERR_INVALID, "pack buffer too small");
   if (!w) return set_error(SDX_ERR_INVALID, "null weights");
   if (route == R_TC_CONV || route == R_TC_ROWS) {
-    tc_pack_conv(w, d->oc, d->ic, d->kh, d->kw, conv_wterms(d), static_cast<__half*>(out));
+    if (route == R_TC_CONV && conv_kxn(d)) tc_pack_conv_kxn(w, d->oc, d->ic, conv_wterms(d), static_cast<__half*>(out));
+    else tc_pack_conv(w, d->oc, d->ic, d->kh, d->kw, conv_wterms(d), static_cast<__half*>(out));
   } else if (route == R_DEPTHWISE) {
     float* o = static_cast<float*>(out);
     for (int c = 0; c < d->ic; c++)
@@ -547,6 +556,7 @@ int sdx_conv2d(sdx_ctx* ctx, const sdx_conv_desc* d, sdx_stream s) {
       p.pad_l = d->pad_l;
       p.w = P<const __half>(d->w);
       p.wterms = conv_wterms(d);
+      p.kxn = route == R_TC_CONV && conv_kxn(d) ? 1 : 0;
       p.N = d->oc;
       p.bias = P<const float>(d->bias);
       p.res = P<const void>(d->add);
