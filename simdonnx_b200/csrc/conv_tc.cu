@@ -114,6 +114,7 @@ struct TcArgs {
   int nsbuf;            // staging buffers per epilogue group (1 or 2)
   uint32_t slab_tx;     // bytes one residual box (one group, one warp's 32 rows) delivers
   int bias_smem;        // bias floats staged in shared memory (per accumulator column), 0 = none
+  int log2G;            // log2 of G (fast epilogue: G is 16, 32 or 64)
   unsigned int* err;
 };
 
@@ -394,7 +395,48 @@ __device__ __forceinline__ void epi_chunk(const TcArgs& a, float (&v)[16], int c
   }
 }
 
+// Fast form of epi_chunk (kernel template EPI = 1): fp16 output through swizzled staging and TMA
+// stores, the bias (zeros when absent) in shared memory, the residual (if any) TMA-staged. The code
+// is straight-line, so the sixteen columns interleave; `sb` is the tile's bias (sBias + n0).
 template <int ACT>
+__device__ __forceinline__ void epi_chunk_fast(const TcArgs& a, float (&v)[16], int c, uint32_t srow, uint32_t xr,
+                                               const float* sb) {
+  const int col = c * 16;
+  const uint32_t row = srow + (uint32_t)(col >> a.log2G) * a.group_bytes;
+  const uint32_t k0 = ((uint32_t)(col & (a.G - 1)) * 2u) >> 4;
+  const uint32_t ad0 = row + ((k0 ^ xr) << 4), ad1 = row + (((k0 + 1u) ^ xr) << 4);
+  const float4* bp = reinterpret_cast<const float4*>(sb + col);
+#pragma unroll
+  for (int i = 0; i < 4; i++) {
+    const float4 b = bp[i];
+    v[4 * i] += b.x; v[4 * i + 1] += b.y; v[4 * i + 2] += b.z; v[4 * i + 3] += b.w;
+  }
+  if (a.tma_res) {
+    uint4 u0, u1;
+    lds16(ad0, u0);
+    lds16(ad1, u1);
+    const __half2* h0 = reinterpret_cast<const __half2*>(&u0);
+    const __half2* h1 = reinterpret_cast<const __half2*>(&u1);
+#pragma unroll
+    for (int i = 0; i < 4; i++) {
+      const float2 f0 = __half22float2(h0[i]), f1 = __half22float2(h1[i]);
+      v[2 * i] += f0.x; v[2 * i + 1] += f0.y;
+      v[8 + 2 * i] += f1.x; v[8 + 2 * i + 1] += f1.y;
+    }
+  }
+  uint4 u0, u1;
+  __half2* h0 = reinterpret_cast<__half2*>(&u0);
+  __half2* h1 = reinterpret_cast<__half2*>(&u1);
+#pragma unroll
+  for (int i = 0; i < 4; i++) {
+    h0[i] = __floats2half2_rn(act_t<ACT>(v[2 * i]), act_t<ACT>(v[2 * i + 1]));
+    h1[i] = __floats2half2_rn(act_t<ACT>(v[8 + 2 * i]), act_t<ACT>(v[8 + 2 * i + 1]));
+  }
+  sts16(ad0, u0);
+  sts16(ad1, u1);
+}
+
+template <int ACT, int EPI>
 __global__ void __launch_bounds__(TC_THREADS, 1)
     conv_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
                    const __grid_constant__ CUtensorMap tmOut, const __grid_constant__ CUtensorMap tmRes,
@@ -451,7 +493,7 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
   }
   // per-column bias in shared memory (ConvT: expanded over its taps), read as broadcasts
   for (int i = threadIdx.x; i < a.bias_smem; i += blockDim.x)
-    sBias[i] = i < a.N ? __ldg(a.bias + (a.convt_oc > 0 ? i % a.convt_oc : i)) : 0.0f;
+    sBias[i] = (a.bias && i < a.N) ? __ldg(a.bias + (a.convt_oc > 0 ? i % a.convt_oc : i)) : 0.0f;
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
@@ -795,7 +837,8 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
           tc_fence_before();
           mbar_arrive(smem_u32(&acce[acc]));
         }
-        epi_chunk<ACT>(a, va, c, srow, xr, sBias, tcd, valid, pix, g, cg);
+        if (EPI) epi_chunk_fast<ACT>(a, va, c, srow, xr, sBias + tcd.n0);
+        else epi_chunk<ACT>(a, va, c, srow, xr, sBias, tcd, valid, pix, g, cg);
         if (c + 1 < nch) {
           tmem_wait_ld();
           tmem_ld_wait16(vb);
@@ -805,7 +848,8 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
             tc_fence_before();
             mbar_arrive(smem_u32(&acce[acc]));
           }
-          epi_chunk<ACT>(a, vb, c + 1, srow, xr, sBias, tcd, valid, pix, g, cg);
+          if (EPI) epi_chunk_fast<ACT>(a, vb, c + 1, srow, xr, sBias + tcd.n0);
+          else epi_chunk<ACT>(a, vb, c + 1, srow, xr, sBias, tcd, valid, pix, g, cg);
         }
       }
       if (a.tma_out) {
@@ -920,16 +964,17 @@ static int encode_map(CUtensorMap* map, const void* base, int rank, const uint64
 
 static bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
 
-template <int ACT>
+template <int ACT, int EPI>
 static int launch_tc(int dev, int grid, size_t smem, cudaStream_t stream, const CUtensorMap& mA, const CUtensorMap& mB,
                      const CUtensorMap& mOut, const CUtensorMap& mRes, const TcArgs& a) {
   static bool attr_set[64] = {false};
   if (dev >= 0 && dev < 64 && !attr_set[dev]) {
-    cudaError_t e = cudaFuncSetAttribute(conv_tc_kernel<ACT>, cudaFuncAttributeMaxDynamicSharedMemorySize, TC_SMEM_LIMIT);
+    cudaError_t e = cudaFuncSetAttribute(conv_tc_kernel<ACT, EPI>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                         TC_SMEM_LIMIT);
     if (e != cudaSuccess) return set_cuda_error(e, "cudaFuncSetAttribute(conv_tc)");
     attr_set[dev] = true;
   }
-  conv_tc_kernel<ACT><<<grid, TC_THREADS, smem, stream>>>(mA, mB, mOut, mRes, a);
+  conv_tc_kernel<ACT, EPI><<<grid, TC_THREADS, smem, stream>>>(mA, mB, mOut, mRes, a);
   cudaError_t e = cudaGetLastError();
   if (e != cudaSuccess) return set_cuda_error(e, "conv_tc launch");
   return SDX_OK;
@@ -1182,6 +1227,14 @@ int tc_launch(const TcProblem& p, cudaStream_t stream) {
   }
 
   if (p.bias && BN * n_tiles <= TC_BIAS_SMEM_MAX) a.bias_smem = BN * n_tiles;
+  // fast epilogue: fp16 out by TMA through 32/64/128-byte swizzled rows, bias in smem (zeros when
+  // there is none), residual TMA-staged or absent
+  const bool fast = a.tma_out && a.esz == 2 && a.swz && !p.kxn && (!p.res || a.tma_res) &&
+                    BN * n_tiles <= TC_BIAS_SMEM_MAX && (a.G == 16 || a.G == 32 || a.G == 64);
+  if (fast) {
+    a.bias_smem = BN * n_tiles;
+    a.log2G = a.G == 16 ? 4 : a.G == 32 ? 5 : 6;
+  }
   // ---- shared-memory plan. Preference: weights resident (loaded once per CTA) with 2 staging
   // buffers and >= 3 A stages, resident with 1 staging buffer and >= 2 stages, then streamed
   // weights (per stage) likewise. 8 stages at most.
@@ -1221,7 +1274,11 @@ int tc_launch(const TcProblem& p, cudaStream_t stream) {
   cudaGetDevice(&dev);
   const int grid = std::min(total, num_sms(dev));
   int rc = SDX_OK;
-  SDX_ACT_DISPATCH(a.act, ACTC, rc = launch_tc<ACTC>(dev, grid, smem, stream, mA, mB, mOut, mRes, a));
+  if (fast) {
+    SDX_ACT_DISPATCH(a.act, ACTC, rc = (launch_tc<ACTC, 1>(dev, grid, smem, stream, mA, mB, mOut, mRes, a)));
+  } else {
+    SDX_ACT_DISPATCH(a.act, ACTC, rc = (launch_tc<ACTC, 0>(dev, grid, smem, stream, mA, mB, mOut, mRes, a)));
+  }
   if (rc) return rc;
   count_launch();
   return SDX_OK;
