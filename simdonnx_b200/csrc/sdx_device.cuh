@@ -29,7 +29,7 @@ __device__ __forceinline__ float act_t(float v) {
   if constexpr (ACT == ACT_RELU) return fmaxf(v, 0.0f);
   else if constexpr (ACT == ACT_SIGMOID) return 1.0f / (1.0f + expf(-v));
   else if constexpr (ACT == ACT_GELU) return 0.5f * v * (1.0f + erff(v * 0.70710678118654752f));
-  else if constexpr (ACT == ACT_HARDSWISH) return v * fminf(fmaxf(fmaf(v, 1.0f / 6.0f, 0.5f), 0.0f), 1.0f);
+  else if constexpr (ACT == ACT_HARDSWISH) return v * __saturatef(fmaf(v, 1.0f / 6.0f, 0.5f));  // clamp to [0, 1]
   else if constexpr (ACT == ACT_SWISH) return v / (1.0f + expf(-v));
   else return v;
 }
@@ -50,7 +50,7 @@ __device__ __forceinline__ float act_apply(float v, int act) {
     case ACT_RELU: return fmaxf(v, 0.0f);
     case ACT_SIGMOID: return 1.0f / (1.0f + expf(-v));
     case ACT_GELU: return 0.5f * v * (1.0f + erff(v * 0.70710678118654752f));
-    case ACT_HARDSWISH: return v * fminf(fmaxf(fmaf(v, 1.0f / 6.0f, 0.5f), 0.0f), 1.0f);
+    case ACT_HARDSWISH: return v * __saturatef(fmaf(v, 1.0f / 6.0f, 0.5f));
     case ACT_SWISH: return v / (1.0f + expf(-v));
     default: return v;
   }

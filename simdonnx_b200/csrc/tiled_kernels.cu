@@ -8,6 +8,7 @@
 #include <cuda_runtime.h>
 
 #include <algorithm>
+#include <type_traits>
 
 #include "sdx_device.cuh"
 #include "sdx_internal.h"
@@ -340,12 +341,311 @@ static bool dw_tma_launch_t(const DwArgs& a, cudaStream_t st) {
   return true;
 }
 
+// ---- stride-1 sliding-window form. A thread owns CPT channels (1 or 2) of a strip of RX output
+// columns and walks down the tile's rows: each input row is read from shared memory once (RX + K - 1
+// pixels), turned into fp32 once, and applied to the K output rows it touches, whose accumulators
+// sit in a ring of K register rows. An output row is finished, activated and stored as soon as its
+// last input row has been applied. The weights of the thread's channels (times the image's SE scale)
+// stay in fp32 registers. The slab width CS, the strip and the tile width are compile-time, so every
+// shared-memory offset inside a row is an immediate; the tile height TH is one less than a multiple
+// of K, so the row walk splits into a prologue (K - 1 rows), whole groups of K rows and a tail (K - 1
+// rows) in which every ring slot and every kernel-row bound is compile-time.
+// A warp reads whole pixel runs of the [IHt][IWt][CS] tile; with RX = 5 the strips that share a
+// warp start 40 or 80 words apart, so the reads are conflict-free.
+// Register budget (two 256-thread CTAs per SM, <= 128 each): K = 3 with CPT = 2, K = 5 with CPT = 1.
+template <int CPT>
+__device__ __forceinline__ void dw_load_px(const uint8_t* p, float (&v)[CPT]) {
+  if constexpr (CPT == 2) {
+    const float2 f = __half22float2(*reinterpret_cast<const __half2*>(p));
+    v[0] = f.x;
+    v[1] = f.y;
+  } else {
+    v[0] = __half2float(*reinterpret_cast<const __half*>(p));
+  }
+}
+
+// Compile-time loop: f(std::integral_constant<int, I>) for I = I0 .. N-1.
+template <int I0, int N, class F>
+__device__ __forceinline__ void static_for(F&& f) {
+  if constexpr (I0 < N) {
+    f(std::integral_constant<int, I0>{});
+    static_for<I0 + 1, N>(f);
+  }
+}
+
+// Applies input row `rowp` (kernel rows KY0..KY1) to the ring: kernel row ky feeds ring slot
+// (SL0 - ky) mod K.
+template <int K, int RX, int CPT, int PXB, int KY0, int KY1, int SL0>
+__device__ __forceinline__ void dw_row(const uint8_t* rowp, float (&acc)[K][RX][CPT], const float (&w)[K][K][CPT]) {
+  float xf[RX + K - 1][CPT];
+#pragma unroll
+  for (int j = 0; j < RX + K - 1; j++) dw_load_px<CPT>(rowp + j * PXB, xf[j]);
+#pragma unroll
+  for (int ky = KY0; ky <= KY1; ky++) {
+    const int sl = ((SL0 - ky) % K + K) % K;
+#pragma unroll
+    for (int r = 0; r < RX; r++)
+#pragma unroll
+      for (int kx = 0; kx < K; kx++)
+#pragma unroll
+        for (int q = 0; q < CPT; q++) acc[sl][r][q] = fmaf(xf[r + kx][q], w[ky][kx][q], acc[sl][r][q]);
+  }
+}
+
+// Finishes output row `oy` from ring slot SL: bias is already in; + residual, activation, store;
+// then the slot restarts at the bias.
+template <int ACT, int K, int RX, int CPT, int SL>
+__device__ __forceinline__ void dw_store_row(const DwArgs& a, float (&acc)[K][RX][CPT], const float (&bias)[CPT], int oy,
+                                             int64_t base, int ncols) {
+  if (oy < a.oh) {
+    if (ncols >= RX) {
+#pragma unroll
+      for (int r = 0; r < RX; r++) {
+        float v[CPT];
+#pragma unroll
+        for (int q = 0; q < CPT; q++) v[q] = acc[SL][r][q];
+        if (a.add) {
+          float ad[CPT];
+          dw_load_px<CPT>(reinterpret_cast<const uint8_t*>(a.add + base + (int64_t)r * a.c), ad);
+#pragma unroll
+          for (int q = 0; q < CPT; q++) v[q] += ad[q];
+        }
+        if constexpr (CPT == 2)
+          *reinterpret_cast<__half2*>(a.y + base + (int64_t)r * a.c) =
+              __floats2half2_rn(act_t<ACT>(v[0]), act_t<ACT>(v[1]));
+        else
+          a.y[base + (int64_t)r * a.c] = __float2half_rn(act_t<ACT>(v[0]));
+      }
+    } else {
+#pragma unroll
+      for (int r = 0; r < RX; r++) {
+        if (r < ncols) {
+          float v[CPT];
+#pragma unroll
+          for (int q = 0; q < CPT; q++) v[q] = acc[SL][r][q];
+          if (a.add) {
+            float ad[CPT];
+            dw_load_px<CPT>(reinterpret_cast<const uint8_t*>(a.add + base + (int64_t)r * a.c), ad);
+#pragma unroll
+            for (int q = 0; q < CPT; q++) v[q] += ad[q];
+          }
+          if constexpr (CPT == 2)
+            *reinterpret_cast<__half2*>(a.y + base + (int64_t)r * a.c) =
+                __floats2half2_rn(act_t<ACT>(v[0]), act_t<ACT>(v[1]));
+          else
+            a.y[base + (int64_t)r * a.c] = __float2half_rn(act_t<ACT>(v[0]));
+        }
+      }
+    }
+  }
+#pragma unroll
+  for (int r = 0; r < RX; r++)
+#pragma unroll
+    for (int q = 0; q < CPT; q++) acc[SL][r][q] = bias[q];
+}
+
+template <int ACT, int K, int RX, int CPT, int CS>
+__global__ void __launch_bounds__(256, 2) dw_slide_kernel(const __grid_constant__ CUtensorMap tmX, DwArgs a, int TH,
+                                                          int tiles_x, int tiles_y, int slabs, int total) {
+  constexpr int TPP = CS / CPT;          // threads per pixel
+  constexpr int TW = RX * (256 / TPP);   // tile width: one strip per thread group
+  constexpr int IWt = TW + K - 1;
+  constexpr int PXB = CS * 2;            // bytes per pixel in the tile
+  constexpr int ROWB = IWt * PXB;        // bytes per tile row
+  extern __shared__ uint8_t dsm_raw[];
+  uint8_t* dsm = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(dsm_raw) + 127) & ~uintptr_t(127));
+  const int IHt = TH + K - 1;
+  const uint32_t tile_bytes = (uint32_t)IHt * ROWB;
+  const uint32_t buf_bytes = (tile_bytes + 127u) & ~127u;
+  uint64_t* full = reinterpret_cast<uint64_t*>(dsm + 2 * buf_bytes);
+  __shared__ int abort_flag;
+  const int tid = threadIdx.x;
+  const int per = (total + gridDim.x - 1) / gridDim.x;
+  const int t0 = blockIdx.x * per, t1 = min(total, t0 + per);
+  if (t0 >= t1) return;
+  const int tiles_per_img = tiles_x * tiles_y;
+  auto decode = [&](int t, int& n, int& slab, int& oy0, int& ox0) {
+    n = t / (slabs * tiles_per_img);
+    const int r = t - n * slabs * tiles_per_img;
+    slab = r / tiles_per_img;
+    const int q = r - slab * tiles_per_img;
+    const int ty = q / tiles_x;
+    oy0 = ty * TH;
+    ox0 = (q - ty * tiles_x) * TW;
+  };
+  auto issue = [&](int t, int b) {
+    int n, slab, oy0, ox0;
+    decode(t, n, slab, oy0, ox0);
+    const uint32_t bar = smem_u32(&full[b]);
+    mbar_arrive_expect_tx(bar, tile_bytes);
+    tma_load_4d(smem_u32(dsm + b * buf_bytes), &tmX, bar, slab * CS, ox0 - a.pl, oy0 - a.pt, n);
+  };
+  uint32_t issued[2] = {0, 0};
+  if (tid == 0) {
+    abort_flag = 0;
+    mbar_init(smem_u32(&full[0]), 1);
+    mbar_init(smem_u32(&full[1]), 1);
+    mbar_fence_init();
+    tma_prefetch_desc(&tmX);
+  }
+  __syncthreads();
+  if (tid == 0) {
+    issue(t0, 0);
+    issued[0] = 1;
+  }
+  const int cp = tid % TPP, strip = tid / TPP;
+  const int lx0 = strip * RX;  // first output column of the strip inside the tile
+  int key = -1;
+  float w[K][K][CPT];
+  float bias[CPT];
+  int i = 0;
+  for (int t = t0; t < t1; t++, i++) {
+    const int b = i & 1;
+    if (tid == 0 && t + 1 < t1) {
+      // buffer b^1 was last read by tile i-1, finished by every thread before the closing barrier
+      issue(t + 1, b ^ 1);
+      issued[b ^ 1]++;
+    }
+    int n, slab, oy0, ox0;
+    decode(t, n, slab, oy0, ox0);
+    const int c = slab * CS + CPT * cp;
+    if (n * slabs + slab != key) {
+      key = n * slabs + slab;
+#pragma unroll
+      for (int q = 0; q < CPT; q++) {
+        const float sc = a.in_scale ? __ldg(a.in_scale + (int64_t)n * a.c + c + q) : 1.0f;
+#pragma unroll
+        for (int ky = 0; ky < K; ky++)
+#pragma unroll
+          for (int kx = 0; kx < K; kx++) w[ky][kx][q] = __ldg(a.w + (int64_t)(ky * K + kx) * a.c + c + q) * sc;
+        bias[q] = __ldg(a.bias + c + q);
+      }
+    }
+    const bool ok = mbar_wait(smem_u32(&full[b]), (uint32_t)(i >> 1) & 1u, a.err, SDX_DEV_WAIT_FULL, &abort_flag);
+    if (__syncthreads_or(!ok)) break;
+    const uint8_t* sp = dsm + (size_t)b * buf_bytes + (lx0 * CS + CPT * cp) * 2;
+    float acc[K][RX][CPT];
+#pragma unroll
+    for (int sl = 0; sl < K; sl++)
+#pragma unroll
+      for (int r = 0; r < RX; r++)
+#pragma unroll
+        for (int q = 0; q < CPT; q++) acc[sl][r][q] = bias[q];
+    const int ncols = min(RX, a.ow - (ox0 + lx0));  // <= 0: strip past the right edge, nothing stored
+    const int64_t row_step = (int64_t)a.ow * a.c;
+    int64_t base = (((int64_t)n * a.oh + oy0) * a.ow + ox0 + lx0) * a.c + c;  // output row oy0
+    // prologue: input rows 0 .. K-2 feed kernel rows 0 .. iy (output row iy - ky, slot iy - ky)
+    static_for<0, K - 1>([&](auto ic) {
+      constexpr int iy = decltype(ic)::value;
+      dw_row<K, RX, CPT, PXB, 0, iy, iy>(sp + iy * ROWB, acc, w);
+    });
+    // steady state: groups of K input rows; input row K-1 + g*K + u feeds every kernel row and
+    // finishes output row g*K + u (slot u)
+    const int groups = (TH - K + 1) / K;
+    const uint8_t* gp = sp + (K - 1) * ROWB;
+    int oy = oy0;
+    for (int g = 0; g < groups; g++) {
+      static_for<0, K>([&](auto ic) {
+        constexpr int u = decltype(ic)::value;
+        dw_row<K, RX, CPT, PXB, 0, K - 1, K - 1 + u>(gp + u * ROWB, acc, w);
+        dw_store_row<ACT, K, RX, CPT, u>(a, acc, bias, oy + u, base + u * row_step, ncols);
+      });
+      gp += K * ROWB;
+      oy += K;
+      base += K * row_step;
+    }
+    // tail: input row TH + e (e = 0 .. K-2, TH = -1 mod K) feeds kernel rows e+1 .. K-1 and
+    // finishes output row TH - K + 1 + e (slot e)
+    static_for<0, K - 1>([&](auto ic) {
+      constexpr int e = decltype(ic)::value;
+      dw_row<K, RX, CPT, PXB, e + 1, K - 1, K - 1 + e>(gp + e * ROWB, acc, w);
+      dw_store_row<ACT, K, RX, CPT, e>(a, acc, bias, oy + e, base + e * row_step, ncols);
+    });
+    __syncthreads();
+  }
+  // wind-down (only after an abort can a copy still be in flight): drain every issued copy
+  if (tid == 0) {
+    for (int b = 0; b < 2; b++)
+      if (issued[b] > 0) mbar_wait_drain(smem_u32(&full[b]), (issued[b] - 1) & 1u, a.err, SDX_DEV_WAIT_DRAIN);
+  }
+}
+
+constexpr int DW_SLIDE_RX = 5;
+
+// Sliding-window launch for stride-1 layers with 16, 32 or a multiple of 64 channels, K in {3, 5}:
+// a tile is 256 / TPP strips of RX columns wide and TH rows high, TH = K*m - 1 chosen so that two
+// CTAs (each double-buffered) fit on an SM and the rows loaded per column band
+// (tiles x (TH + K - 1)) are fewest.
+template <int ACT, int K, int CS>
+static bool dw_slide_launch_cs(const DwArgs& a, cudaStream_t st) {
+  constexpr int RX = DW_SLIDE_RX, CPT = K <= 3 ? 2 : 1;
+  constexpr int TPP = CS / CPT, TW = RX * (256 / TPP), IWt = TW + K - 1;
+  static_assert(IWt <= 256, "TMA box width");
+  const size_t row_bytes = (size_t)IWt * CS * 2;
+  const size_t buf_cap = 54 * 1024;  // two CTAs per SM, two buffers each
+  const int ih_max = (int)std::min<size_t>(buf_cap / row_bytes, 256);
+  int TH = 0, best = INT32_MAX;
+  for (int th = K - 1; th + K - 1 <= ih_max; th += K) {
+    const int rows = (a.oh + th - 1) / th * (th + K - 1);
+    if (rows <= best) {
+      best = rows;
+      TH = th;
+    }
+  }
+  if (TH < K - 1 || TH == 0) return false;
+  const int IHt = TH + K - 1;
+  const size_t tile_bytes = (size_t)IHt * row_bytes;
+  const size_t smem = 128 + 2 * ((tile_bytes + 127) & ~(size_t)127) + 16;
+  PFN_encodeTiled enc = get_encode_tiled();
+  if (!enc) return false;
+  CUtensorMap map;
+  const cuuint64_t dims[4] = {(cuuint64_t)a.c, (cuuint64_t)a.iw, (cuuint64_t)a.ih, (cuuint64_t)a.batch};
+  const cuuint64_t strides[3] = {(cuuint64_t)a.c * 2, (cuuint64_t)a.iw * a.c * 2, (cuuint64_t)a.ih * a.iw * a.c * 2};
+  const cuuint32_t box[4] = {(cuuint32_t)CS, (cuuint32_t)IWt, (cuuint32_t)IHt, 1};
+  const cuuint32_t estr[4] = {1, 1, 1, 1};
+  if (enc(&map, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 4, const_cast<__half*>(a.x), dims, strides, box, estr,
+          CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+          CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) != CUDA_SUCCESS)
+    return false;
+  static bool attr = false;
+  if (!attr) {
+    cudaFuncSetAttribute(dw_slide_kernel<ACT, K, RX, CPT, CS>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                         120 * 1024);
+    attr = true;
+  }
+  const int tiles_x = (a.ow + TW - 1) / TW, tiles_y = (a.oh + TH - 1) / TH;
+  const int slabs = a.c / CS;
+  const int64_t total = (int64_t)a.batch * slabs * tiles_x * tiles_y;
+  if (total <= 0 || total > INT32_MAX) return false;
+  int dev = 0, per_sm = 1;
+  cudaGetDevice(&dev);
+  cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, dw_slide_kernel<ACT, K, RX, CPT, CS>, 256, smem);
+  const int grid = (int)std::min<int64_t>(total, (int64_t)num_sms(dev) * std::max(1, per_sm));
+  dw_slide_kernel<ACT, K, RX, CPT, CS><<<grid, 256, smem, st>>>(map, a, TH, tiles_x, tiles_y, slabs, (int)total);
+  return true;
+}
+
+template <int ACT, int K>
+static bool dw_slide_launch_t(const DwArgs& a, cudaStream_t st) {
+  if constexpr (K != 3 && K != 5) {
+    return false;
+  } else {
+    if ((reinterpret_cast<uintptr_t>(a.x) & 15u) || (reinterpret_cast<uintptr_t>(a.y) & 3u)) return false;
+    if (a.add && (reinterpret_cast<uintptr_t>(a.add) & 3u)) return false;
+    if (a.c == 16) return dw_slide_launch_cs<ACT, K, 16>(a, st);
+    if (a.c == 32) return dw_slide_launch_cs<ACT, K, 32>(a, st);
+    if (a.c % 64 == 0) return dw_slide_launch_cs<ACT, K, 64>(a, st);
+    return false;
+  }
+}
+
 // Strip length: 8 outputs per thread for stride-1 layers on maps of at least 64 x 64 (fewer
 // shared-memory reads per output; measured 1.13-1.26x faster there), else 4 (taller tiles of the
 // 8-output form waste rows on small maps, and stride 2 needs the registers).
 template <int ACT, int K, int S>
 static bool dw_tma_pick(const DwArgs& a, cudaStream_t st) {
   if constexpr (S == 1) {
+    if (dw_slide_launch_t<ACT, K>(a, st)) return true;
     if (a.oh >= 64 && a.ow >= 64) return dw_tma_launch_t<ACT, K, S, 8>(a, st);
   }
   return dw_tma_launch_t<ACT, K, S, 4>(a, st);

@@ -174,7 +174,9 @@ def test_convt(be, ic, oc, h, w, act, f32):
 
 # ------------------------------------------------------------------------------------------- bandwidth ops
 @pytest.mark.parametrize("c,k,s,h,w", [(16, 3, 1, 40, 40), (32, 3, 2, 40, 40), (128, 5, 1, 20, 20),
-                                       (256, 5, 2, 21, 19)])
+                                       (256, 5, 2, 21, 19), (64, 3, 1, 37, 45), (256, 5, 1, 40, 40),
+                                       (64, 5, 1, 23, 93), (16, 3, 1, 30, 170), (32, 5, 1, 17, 85),
+                                       (192, 3, 1, 9, 7), (16, 5, 1, 24, 90)])
 def test_depthwise(be, c, k, s, h, w):
     from simdonnx_b200 import backend as B
     rng = np.random.default_rng(c + k)
@@ -186,6 +188,24 @@ def test_depthwise(be, c, k, s, h, w):
     d = B.conv_desc(2, h, w, c, c, k, k, stride=(s, s), pads=(p, p, p, p), group=c, act="hardswish")
     y = B.conv2d(be, d, dev16(x), B.pack_conv(d, wt), bias=dev32(b))
     assert_close(host(y), ref, "depthwise")
+
+
+@pytest.mark.parametrize("c,k", [(64, 5), (16, 3)])
+def test_depthwise_residual_and_scale(be, c, k):
+    """Sliding-window depthwise with the SE scale on its load and a residual add before the act."""
+    from simdonnx_b200 import backend as B
+    rng = np.random.default_rng(5 + c)
+    h, w = 29, 51
+    x = rnd(rng, 2, h, w, c)
+    r = rnd(rng, 2, h, w, c)
+    sc = rng.uniform(0, 1, size=(2, c)).astype(np.float32)
+    wt = rnd(rng, c, 1, k, k, scale=0.3)
+    b = rnd(rng, c)
+    p = k // 2
+    ref = O.conv(O.channel_broadcast(x, sc), O.ConvPlan(wt, b, group=c), pads=(p, p, p, p), act="hardswish", add=r)
+    d = B.conv_desc(2, h, w, c, c, k, k, pads=(p, p, p, p), group=c, act="hardswish")
+    y = B.conv2d(be, d, dev16(x), B.pack_conv(d, wt), bias=dev32(b), add=dev16(r), in_scale=dev32(sc))
+    assert_close(host(y), ref, "dw+scale+residual")
 
 
 def test_depthwise_with_input_scale(be):
