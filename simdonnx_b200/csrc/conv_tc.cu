@@ -750,6 +750,56 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
       const uint32_t slab = stage0 + sbi * a.sbuf_bytes;
       const uint32_t srow = slab + (uint32_t)lane * P;
       const uint32_t tbase = tmem_base + ((uint32_t)(q * 32) << 16) + acc * (uint32_t)a.acc_stride;
+      if (EPI == 2) {
+        // kx-in-N, straight-line form (fp16 out, 16-byte rows, no residual, bias or zeros in smem):
+        // per 16 output channels, the three taps' columns are loaded with one wait, combined across
+        // neighbouring lanes (rows x-1, x, x+1), biased, activated and stored as two 16-byte words
+        const int x = row_in_tile & (a.BW - 1), h = row_in_tile >> (a.BW == 16 ? 4 : 5);
+        const int oy = tcd.oy0 + h, ox = tcd.ox0 - 1 + x;
+        const bool st_ok = x >= 1 && x <= a.BW - 2 && oy < a.OH && ox < a.OW;
+        __half* outp = static_cast<__half*>(a.out) +
+                       ((((int64_t)tcd.img * a.OH + oy) * a.OW + ox) * a.out_pix_stride + a.out_ch_off);
+        const int halves = a.N > 16 ? 2 : 1;
+#pragma unroll
+        for (int hf = 0; hf < 2; hf++) {
+          if (hf < halves) {
+            float v0[16], v1[16], v2[16];
+            tmem_ld16_issue(tbase + (uint32_t)(hf * 16), v0);
+            tmem_ld16_issue(tbase + (uint32_t)(32 + hf * 16), v1);
+            tmem_ld16_issue(tbase + (uint32_t)(64 + hf * 16), v2);
+            tmem_wait_ld();
+            tmem_ld_wait16(v0);
+            tmem_ld_wait16(v1);
+            tmem_ld_wait16(v2);
+            if (hf == halves - 1) {
+              tc_fence_before();
+              mbar_arrive(smem_u32(&acce[acc]));
+            }
+            const float4* bp = reinterpret_cast<const float4*>(sBias + hf * 16);
+            uint4 w2[2];
+            __half2* hp = reinterpret_cast<__half2*>(w2);
+#pragma unroll
+            for (int i = 0; i < 16; i += 4) {
+              const float4 b = bp[i / 4];
+              const float bb[4] = {b.x, b.y, b.z, b.w};
+              float y[4];
+#pragma unroll
+              for (int j = 0; j < 4; j++)
+                y[j] = act_t<ACT>(__shfl_up_sync(0xffffffffu, v0[i + j], 1) + v1[i + j] +
+                                  __shfl_down_sync(0xffffffffu, v2[i + j], 1) + bb[j]);
+              hp[i / 2] = __floats2half2_rn(y[0], y[1]);
+              hp[i / 2 + 1] = __floats2half2_rn(y[2], y[3]);
+            }
+            if (st_ok) {
+              uint4* op = reinterpret_cast<uint4*>(outp + hf * 16);
+              op[0] = w2[0];
+              if (hf * 16 + 8 < a.N) op[1] = w2[1];
+            }
+          }
+        }
+        __syncwarp();
+        continue;
+      }
       if (a.kxn) {
         // kx-in-N: columns kx * 32 + oc; row x of the tile is input column ox0 - 1 + x, and the
         // output at that column is D[x - 1][kx 0] + D[x][kx 1] + D[x + 1][kx 2] (neighbouring
@@ -837,7 +887,7 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
           tc_fence_before();
           mbar_arrive(smem_u32(&acce[acc]));
         }
-        if (EPI) epi_chunk_fast<ACT>(a, va, c, srow, xr, sBias + tcd.n0);
+        if (EPI == 1) epi_chunk_fast<ACT>(a, va, c, srow, xr, sBias + tcd.n0);
         else epi_chunk<ACT>(a, va, c, srow, xr, sBias, tcd, valid, pix, g, cg);
         if (c + 1 < nch) {
           tmem_wait_ld();
@@ -848,7 +898,7 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
             tc_fence_before();
             mbar_arrive(smem_u32(&acce[acc]));
           }
-          if (EPI) epi_chunk_fast<ACT>(a, vb, c + 1, srow, xr, sBias + tcd.n0);
+          if (EPI == 1) epi_chunk_fast<ACT>(a, vb, c + 1, srow, xr, sBias + tcd.n0);
           else epi_chunk<ACT>(a, vb, c + 1, srow, xr, sBias, tcd, valid, pix, g, cg);
         }
       }
@@ -1235,6 +1285,10 @@ int tc_launch(const TcProblem& p, cudaStream_t stream) {
     a.bias_smem = BN * n_tiles;
     a.log2G = a.G == 16 ? 4 : a.G == 32 ? 5 : 6;
   }
+  // straight-line kx-in-N epilogue: fp16 out with 16-byte rows, no residual, N a multiple of 8
+  const bool kxn_fast = p.kxn && !p.out_f32 && a.vec_ok && !p.res && p.N % 8 == 0 && p.N <= 32 &&
+                        BN * n_tiles <= TC_BIAS_SMEM_MAX;
+  if (kxn_fast) a.bias_smem = BN * n_tiles;
   // ---- shared-memory plan. Preference: weights resident (loaded once per CTA) with 2 staging
   // buffers and >= 3 A stages, resident with 1 staging buffer and >= 2 stages, then streamed
   // weights (per stage) likewise. 8 stages at most.
@@ -1276,6 +1330,8 @@ int tc_launch(const TcProblem& p, cudaStream_t stream) {
   int rc = SDX_OK;
   if (fast) {
     SDX_ACT_DISPATCH(a.act, ACTC, rc = (launch_tc<ACTC, 1>(dev, grid, smem, stream, mA, mB, mOut, mRes, a)));
+  } else if (kxn_fast) {
+    SDX_ACT_DISPATCH(a.act, ACTC, rc = (launch_tc<ACTC, 2>(dev, grid, smem, stream, mA, mB, mOut, mRes, a)));
   } else {
     SDX_ACT_DISPATCH(a.act, ACTC, rc = (launch_tc<ACTC, 0>(dev, grid, smem, stream, mA, mB, mOut, mRes, a)));
   }
