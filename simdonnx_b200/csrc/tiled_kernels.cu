@@ -625,6 +625,215 @@ static bool dw_slide_launch_cs(const DwArgs& a, cudaStream_t st) {
   return true;
 }
 
+// ---- stride-2 sliding-window form: the same strips and ring, with input row iy feeding output
+// rows (iy - ky) / 2 for the kernel rows ky of iy's parity. The ring holds R = ceil(K / 2) output
+// rows; the row walk is unrolled by 2R so that every slot is compile-time (the tile's first input
+// row is a multiple of 2R); rows outside the tile are skipped by warp-uniform range checks.
+template <int ACT, int K, int RX, int CPT, int CS>
+__global__ void __launch_bounds__(256, 2) dw_slide2_kernel(const __grid_constant__ CUtensorMap tmX, DwArgs a, int TH,
+                                                           int tiles_x, int tiles_y, int slabs, int total) {
+  constexpr int R = (K + 1) / 2;         // ring rows
+  constexpr int P = 2 * R;               // unroll period of the input-row walk
+  constexpr int NX = 2 * RX + K - 2;     // input pixels per strip row
+  constexpr int TPP = CS / CPT;
+  constexpr int TW = RX * (256 / TPP);
+  constexpr int IWt = 2 * TW + K - 2;
+  constexpr int PXB = CS * 2;
+  constexpr int ROWB = IWt * PXB;
+  extern __shared__ uint8_t dsm_raw[];
+  uint8_t* dsm = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(dsm_raw) + 127) & ~uintptr_t(127));
+  const int IHt = 2 * TH + K - 2;
+  const uint32_t tile_bytes = (uint32_t)IHt * ROWB;
+  const uint32_t buf_bytes = (tile_bytes + 127u) & ~127u;
+  uint64_t* full = reinterpret_cast<uint64_t*>(dsm + 2 * buf_bytes);
+  __shared__ int abort_flag;
+  const int tid = threadIdx.x;
+  const int per = (total + gridDim.x - 1) / gridDim.x;
+  const int t0 = blockIdx.x * per, t1 = min(total, t0 + per);
+  if (t0 >= t1) return;
+  const int tiles_per_img = tiles_x * tiles_y;
+  auto decode = [&](int t, int& n, int& slab, int& oy0, int& ox0) {
+    n = t / (slabs * tiles_per_img);
+    const int r = t - n * slabs * tiles_per_img;
+    slab = r / tiles_per_img;
+    const int q = r - slab * tiles_per_img;
+    const int ty = q / tiles_x;
+    oy0 = ty * TH;
+    ox0 = (q - ty * tiles_x) * TW;
+  };
+  auto issue = [&](int t, int b) {
+    int n, slab, oy0, ox0;
+    decode(t, n, slab, oy0, ox0);
+    const uint32_t bar = smem_u32(&full[b]);
+    mbar_arrive_expect_tx(bar, tile_bytes);
+    tma_load_4d(smem_u32(dsm + b * buf_bytes), &tmX, bar, slab * CS, 2 * ox0 - a.pl, 2 * oy0 - a.pt, n);
+  };
+  uint32_t issued[2] = {0, 0};
+  if (tid == 0) {
+    abort_flag = 0;
+    mbar_init(smem_u32(&full[0]), 1);
+    mbar_init(smem_u32(&full[1]), 1);
+    mbar_fence_init();
+    tma_prefetch_desc(&tmX);
+  }
+  __syncthreads();
+  if (tid == 0) {
+    issue(t0, 0);
+    issued[0] = 1;
+  }
+  const int cp = tid % TPP, strip = tid / TPP;
+  const int lx0 = strip * RX;
+  int key = -1;
+  float w[K][K][CPT];
+  float bias[CPT];
+  int i = 0;
+  for (int t = t0; t < t1; t++, i++) {
+    const int b = i & 1;
+    if (tid == 0 && t + 1 < t1) {
+      issue(t + 1, b ^ 1);
+      issued[b ^ 1]++;
+    }
+    int n, slab, oy0, ox0;
+    decode(t, n, slab, oy0, ox0);
+    const int c = slab * CS + CPT * cp;
+    if (n * slabs + slab != key) {
+      key = n * slabs + slab;
+#pragma unroll
+      for (int q = 0; q < CPT; q++) {
+        const float sc = a.in_scale ? __ldg(a.in_scale + (int64_t)n * a.c + c + q) : 1.0f;
+#pragma unroll
+        for (int ky = 0; ky < K; ky++)
+#pragma unroll
+          for (int kx = 0; kx < K; kx++) w[ky][kx][q] = __ldg(a.w + (int64_t)(ky * K + kx) * a.c + c + q) * sc;
+        bias[q] = __ldg(a.bias + c + q);
+      }
+    }
+    const bool ok = mbar_wait(smem_u32(&full[b]), (uint32_t)(i >> 1) & 1u, a.err, SDX_DEV_WAIT_FULL, &abort_flag);
+    if (__syncthreads_or(!ok)) break;
+    const uint8_t* sp = dsm + (size_t)b * buf_bytes + (2 * lx0 * CS + CPT * cp) * 2;
+    float acc[R][RX][CPT];
+#pragma unroll
+    for (int sl = 0; sl < R; sl++)
+#pragma unroll
+      for (int r = 0; r < RX; r++)
+#pragma unroll
+        for (int q = 0; q < CPT; q++) acc[sl][r][q] = bias[q];
+    const int ncols = min(RX, a.ow - (ox0 + lx0));
+    const int64_t row_step = (int64_t)a.ow * a.c;
+    const int64_t base0 = (((int64_t)n * a.oh + oy0) * a.ow + ox0 + lx0) * a.c + c;
+    for (int iy0 = 0; iy0 < IHt; iy0 += P) {
+      static_for<0, P>([&](auto ic) {
+        constexpr int u = decltype(ic)::value;
+        const int iy = iy0 + u;
+        if (iy < IHt) {
+          float xf[NX][CPT];
+          const uint8_t* rowp = sp + (size_t)iy * ROWB;
+#pragma unroll
+          for (int j = 0; j < NX; j++) dw_load_px<CPT>(rowp + j * PXB, xf[j]);
+          static_for<0, K>([&](auto kc) {
+            constexpr int ky = decltype(kc)::value;
+            if constexpr (((u - ky) & 1) == 0) {
+              const int o = (iy - ky) / 2;  // iy - ky is even here
+              if (iy >= ky && o < TH) {
+                constexpr int sl = (((u - ky) / 2) % R + R) % R;
+#pragma unroll
+                for (int r = 0; r < RX; r++)
+#pragma unroll
+                  for (int kx = 0; kx < K; kx++)
+#pragma unroll
+                    for (int q = 0; q < CPT; q++)
+                      acc[sl][r][q] = fmaf(xf[2 * r + kx][q], w[ky][kx][q], acc[sl][r][q]);
+              }
+            }
+          });
+          if constexpr (((u - (K - 1)) & 1) == 0) {
+            // output row (iy - K + 1) / 2 has had its last input row
+            if (iy >= K - 1) {
+              const int o = (iy - (K - 1)) / 2;
+              if (o < TH) {
+                constexpr int sl = (((u - (K - 1)) / 2) % R + R) % R;
+                dw_store_row<ACT, R, RX, CPT, sl>(a, acc, bias, oy0 + o, base0 + o * row_step, ncols);
+              }
+            }
+          }
+        }
+      });
+    }
+    __syncthreads();
+  }
+  if (tid == 0) {
+    for (int b = 0; b < 2; b++)
+      if (issued[b] > 0) mbar_wait_drain(smem_u32(&full[b]), (issued[b] - 1) & 1u, a.err, SDX_DEV_WAIT_DRAIN);
+  }
+}
+
+template <int ACT, int K, int CS>
+static bool dw_slide2_launch_cs(const DwArgs& a, cudaStream_t st) {
+  constexpr int RX = DW_SLIDE_RX, CPT = K <= 3 ? 2 : 1;
+  constexpr int TPP = CS / CPT, TW = RX * (256 / TPP), IWt = 2 * TW + K - 2;
+  if constexpr (IWt > 256) {
+    return false;
+  } else {
+    const size_t row_bytes = (size_t)IWt * CS * 2;
+    const size_t buf_cap = 54 * 1024;
+    const int ih_max = (int)std::min<size_t>(buf_cap / row_bytes, 256);
+    const int th_max = (ih_max - (K - 2)) / 2;
+    if (th_max < 1) return false;
+    int TH = th_max, best = INT32_MAX;
+    for (int th = th_max; th >= 1; th--) {
+      const int rows = (a.oh + th - 1) / th * (2 * th + K - 2);
+      if (rows < best) {
+        best = rows;
+        TH = th;
+      }
+    }
+    const int IHt = 2 * TH + K - 2;
+    const size_t tile_bytes = (size_t)IHt * row_bytes;
+    const size_t smem = 128 + 2 * ((tile_bytes + 127) & ~(size_t)127) + 16;
+    PFN_encodeTiled enc = get_encode_tiled();
+    if (!enc) return false;
+    CUtensorMap map;
+    const cuuint64_t dims[4] = {(cuuint64_t)a.c, (cuuint64_t)a.iw, (cuuint64_t)a.ih, (cuuint64_t)a.batch};
+    const cuuint64_t strides[3] = {(cuuint64_t)a.c * 2, (cuuint64_t)a.iw * a.c * 2,
+                                   (cuuint64_t)a.ih * a.iw * a.c * 2};
+    const cuuint32_t box[4] = {(cuuint32_t)CS, (cuuint32_t)IWt, (cuuint32_t)IHt, 1};
+    const cuuint32_t estr[4] = {1, 1, 1, 1};
+    if (enc(&map, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 4, const_cast<__half*>(a.x), dims, strides, box, estr,
+            CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+            CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) != CUDA_SUCCESS)
+      return false;
+    static bool attr = false;
+    if (!attr) {
+      cudaFuncSetAttribute(dw_slide2_kernel<ACT, K, RX, CPT, CS>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                           120 * 1024);
+      attr = true;
+    }
+    const int tiles_x = (a.ow + TW - 1) / TW, tiles_y = (a.oh + TH - 1) / TH;
+    const int slabs = a.c / CS;
+    const int64_t total = (int64_t)a.batch * slabs * tiles_x * tiles_y;
+    if (total <= 0 || total > INT32_MAX) return false;
+    int dev = 0, per_sm = 1;
+    cudaGetDevice(&dev);
+    cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, dw_slide2_kernel<ACT, K, RX, CPT, CS>, 256, smem);
+    const int grid = (int)std::min<int64_t>(total, (int64_t)num_sms(dev) * std::max(1, per_sm));
+    dw_slide2_kernel<ACT, K, RX, CPT, CS><<<grid, 256, smem, st>>>(map, a, TH, tiles_x, tiles_y, slabs, (int)total);
+    return true;
+  }
+}
+
+template <int ACT, int K>
+static bool dw_slide2_launch_t(const DwArgs& a, cudaStream_t st) {
+  if constexpr (K != 3 && K != 5) {
+    return false;
+  } else {
+    if ((reinterpret_cast<uintptr_t>(a.x) & 15u) || (reinterpret_cast<uintptr_t>(a.y) & 3u)) return false;
+    if (a.add && (reinterpret_cast<uintptr_t>(a.add) & 3u)) return false;
+    if (a.c == 32) return dw_slide2_launch_cs<ACT, K, 32>(a, st);
+    if (a.c % 64 == 0) return dw_slide2_launch_cs<ACT, K, 64>(a, st);
+    return false;
+  }
+}
+
 template <int ACT, int K>
 static bool dw_slide_launch_t(const DwArgs& a, cudaStream_t st) {
   if constexpr (K != 3 && K != 5) {
@@ -647,6 +856,8 @@ static bool dw_tma_pick(const DwArgs& a, cudaStream_t st) {
   if constexpr (S == 1) {
     if (dw_slide_launch_t<ACT, K>(a, st)) return true;
     if (a.oh >= 64 && a.ow >= 64) return dw_tma_launch_t<ACT, K, S, 8>(a, st);
+  } else if constexpr (S == 2) {
+    if (dw_slide2_launch_t<ACT, K>(a, st)) return true;
   }
   return dw_tma_launch_t<ACT, K, S, 4>(a, st);
 }

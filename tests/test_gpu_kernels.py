@@ -176,7 +176,8 @@ def test_convt(be, ic, oc, h, w, act, f32):
 @pytest.mark.parametrize("c,k,s,h,w", [(16, 3, 1, 40, 40), (32, 3, 2, 40, 40), (128, 5, 1, 20, 20),
                                        (256, 5, 2, 21, 19), (64, 3, 1, 37, 45), (256, 5, 1, 40, 40),
                                        (64, 5, 1, 23, 93), (16, 3, 1, 30, 170), (32, 5, 1, 17, 85),
-                                       (192, 3, 1, 9, 7), (16, 5, 1, 24, 90)])
+                                       (192, 3, 1, 9, 7), (16, 5, 1, 24, 90), (64, 3, 2, 37, 45),
+                                       (128, 5, 2, 40, 40), (32, 5, 2, 30, 61), (128, 3, 2, 80, 80)])
 def test_depthwise(be, c, k, s, h, w):
     from simdonnx_b200 import backend as B
     rng = np.random.default_rng(c + k)
