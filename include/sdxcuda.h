@@ -189,7 +189,7 @@ int sdx_pool(sdx_ctx* ctx, const sdx_pool_desc* d, sdx_stream s);
 /* Squeeze-excitation gate (ChannelGateP, src/Engine/ExecPlan.cs:151-158; Nhwc.ChannelGate,
  * src/Kernels/Nhwc.Det.cs:287-314): s[n, c] = gate(b2 + W2 . act1(b1 + W1 . mean_hw x[n])) + offset.
  * x fp16 NHWC; w1 fp32 [r][c], w2 fp32 [c][r]; s fp32 [batch, c]. `partial` is device scratch of
- * sdx_channel_gate_scratch_bytes() bytes (per-block channel sums). */
+ * sdx_channel_gate_scratch_bytes() bytes (per-block channel sums and the hidden layer); r <= c. */
 typedef struct sdx_gate_desc {
   int batch, hw, c, r;
   int act1_relu, hard;
@@ -208,7 +208,7 @@ int sdx_channel_gate(sdx_ctx* ctx, const sdx_gate_desc* d, sdx_stream s);
  * Limits and rules:
  *  - sdx_channel_gate_scratch_bytes(batch, hw, c) must be <= SDX_GATE_STATIC_MAX_SCRATCH_BYTES,
  *    else SDX_ERR_NOT_SUPPORTED (nothing enqueued); e.g. c = 512 with one pixel chunk allows
- *    2048 images.
+ *    1024 images.
  *  - The first call on a device looks up the array's device address (cudaGetSymbolAddress) and
  *    caches it; make that first call before beginning any stream capture on that device.
  *  - All calls on one device share the one array: two calls whose kernels overlap on the GPU

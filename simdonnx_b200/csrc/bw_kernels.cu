@@ -407,8 +407,9 @@ static int gate_chunks(int hw, int c) {
   return (int)std::min<int64_t>(64, std::max<int64_t>(1, std::min<int64_t>(hw, (bytes + 65535) / 65536)));
 }
 
+// Scratch: per-chunk channel sums [batch][chunks][c], then the hidden layer [batch][r <= c].
 size_t gate_scratch_bytes(int batch, int hw, int c) {
-  return sizeof(float) * (size_t)batch * gate_chunks(hw, c) * c;
+  return sizeof(float) * (size_t)batch * (gate_chunks(hw, c) + 1) * c;
 }
 
 __global__ void gap_partial_kernel(const __half* __restrict__ x, int hw, int c, int chunks, float* __restrict__ partial) {
@@ -421,7 +422,21 @@ __global__ void gap_partial_kernel(const __half* __restrict__ x, int hw, int c, 
   float acc[8] = {0, 0, 0, 0, 0, 0, 0, 0};
   if (lp < lanes_p) {
     const __half* base = x + (int64_t)n * hw * c + g * 8;
-    for (int p = p0 + lp; p < p1; p += lanes_p) {
+    int p = p0 + lp;
+    // four independent 16-byte loads in flight per thread, then the remainder
+    for (; p + 3 * lanes_p < p1; p += 4 * lanes_p) {
+      uint4 u[4];
+#pragma unroll
+      for (int k = 0; k < 4; k++) u[k] = __ldg(reinterpret_cast<const uint4*>(base + (int64_t)(p + k * lanes_p) * c));
+#pragma unroll
+      for (int k = 0; k < 4; k++) {
+        float v[8];
+        h8_to_f(u[k], v);
+#pragma unroll
+        for (int j = 0; j < 8; j++) acc[j] += v[j];
+      }
+    }
+    for (; p < p1; p += lanes_p) {
       float v[8];
       h8_to_f(__ldg(reinterpret_cast<const uint4*>(base + (int64_t)p * c)), v);
 #pragma unroll
@@ -439,39 +454,95 @@ __global__ void gap_partial_kernel(const __half* __restrict__ x, int hw, int c, 
   }
 }
 
-__global__ void gate_fc_kernel(GateArgs a, int chunks) {
-  extern __shared__ float sm[];
-  float* mean = sm;         // [c]
-  float* hid = sm + a.c;    // [r]
-  const int n = blockIdx.x;
+// FC stages, GATE_IMG images per CTA: every weight row is read once per CTA (coalesced, one warp
+// per row of W1 [r][c] and of W2 [c][r]) and applied to all of the CTA's images; the rows are spread
+// over a second grid dimension (GATE_RJ hidden units / GATE_CJ output channels per CTA). Each
+// image's sums run in the same order whatever images share its CTA, so the gate of an image does
+// not depend on the batch it runs in. The hidden layer goes through scratch (after the partials).
+constexpr int GATE_IMG = 8, GATE_RJ = 32, GATE_CJ = 64;
+
+// Warp sum of v[0..GATE_IMG-1]; lane 0 holds the totals.
+__device__ __forceinline__ void warp_sum_img(float (&v)[GATE_IMG]) {
+#pragma unroll
+  for (int i = 0; i < GATE_IMG; i++)
+#pragma unroll
+    for (int off = 16; off; off >>= 1) v[i] += __shfl_xor_sync(0xffffffffu, v[i], off);
+}
+
+__global__ void gate_fc1_kernel(GateArgs a, int chunks, float* __restrict__ hid) {
+  extern __shared__ float mean[];  // [GATE_IMG][c]
+  const int n0 = blockIdx.x * GATE_IMG;
+  const int nimg = min(GATE_IMG, a.batch - n0);
   const float inv = 1.0f / (float)a.hw;
-  for (int ch = threadIdx.x; ch < a.c; ch += blockDim.x) {
+  for (int idx = threadIdx.x; idx < GATE_IMG * a.c; idx += blockDim.x) {
+    const int i = idx / a.c, ch = idx - i * a.c;
     float s = 0.0f;
-    for (int k = 0; k < chunks; k++) s += a.partial[((int64_t)n * chunks + k) * a.c + ch];
-    mean[ch] = s * inv;
+    if (i < nimg)
+      for (int k = 0; k < chunks; k++) s += a.partial[((int64_t)(n0 + i) * chunks + k) * a.c + ch];
+    mean[idx] = s * inv;
   }
   __syncthreads();
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, nw = blockDim.x >> 5;
-  for (int j = warp; j < a.r; j += nw) {
-    float s = 0.0f;
-    for (int k = lane; k < a.c; k += 32) s = fmaf(a.w1[(int64_t)j * a.c + k], mean[k], s);
-    for (int off = 16; off; off >>= 1) s += __shfl_xor_sync(0xffffffffu, s, off);
+  const int j1 = min(a.r, (int)(blockIdx.y + 1) * GATE_RJ);
+  for (int j = blockIdx.y * GATE_RJ + warp; j < j1; j += nw) {
+    float s[GATE_IMG];
+#pragma unroll
+    for (int i = 0; i < GATE_IMG; i++) s[i] = 0.0f;
+    const float* wr = a.w1 + (int64_t)j * a.c;
+    for (int k = lane; k < a.c; k += 32) {
+      const float w = __ldg(wr + k);
+#pragma unroll
+      for (int i = 0; i < GATE_IMG; i++) s[i] = fmaf(w, mean[i * a.c + k], s[i]);
+    }
+    warp_sum_img(s);
     if (lane == 0) {
-      s += a.b1 ? a.b1[j] : 0.0f;
-      hid[j] = a.act1_relu ? fmaxf(s, 0.0f) : s;
+      const float b = a.b1 ? a.b1[j] : 0.0f;
+#pragma unroll
+      for (int i = 0; i < GATE_IMG; i++) {
+        const float h = s[i] + b;
+        if (i < nimg) hid[(int64_t)(n0 + i) * a.r + j] = a.act1_relu ? fmaxf(h, 0.0f) : h;
+      }
     }
   }
+}
+
+__global__ void gate_fc2_kernel(GateArgs a, const float* __restrict__ hid) {
+  extern __shared__ float hs[];  // [GATE_IMG][r]
+  const int n0 = blockIdx.x * GATE_IMG;
+  const int nimg = min(GATE_IMG, a.batch - n0);
+  for (int idx = threadIdx.x; idx < GATE_IMG * a.r; idx += blockDim.x) {
+    const int i = idx / a.r;
+    hs[idx] = i < nimg ? hid[(int64_t)n0 * a.r + idx] : 0.0f;
+  }
   __syncthreads();
-  for (int ch = threadIdx.x; ch < a.c; ch += blockDim.x) {
-    float z = a.b2 ? a.b2[ch] : 0.0f;
-    for (int j = 0; j < a.r; j++) z = fmaf(a.w2[(int64_t)ch * a.r + j], hid[j], z);
-    float g = a.hard ? fminf(fmaxf(z * a.alpha + a.beta, 0.0f), 1.0f) : 1.0f / (1.0f + expf(-z));
-    a.s[(int64_t)n * a.c + ch] = g + a.offset;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, nw = blockDim.x >> 5;
+  const int c1 = min(a.c, (int)(blockIdx.y + 1) * GATE_CJ);
+  for (int ch = blockIdx.y * GATE_CJ + warp; ch < c1; ch += nw) {
+    float z[GATE_IMG];
+#pragma unroll
+    for (int i = 0; i < GATE_IMG; i++) z[i] = 0.0f;
+    const float* wr = a.w2 + (int64_t)ch * a.r;
+    for (int j = lane; j < a.r; j += 32) {
+      const float w = __ldg(wr + j);
+#pragma unroll
+      for (int i = 0; i < GATE_IMG; i++) z[i] = fmaf(w, hs[i * a.r + j], z[i]);
+    }
+    warp_sum_img(z);
+    if (lane == 0) {
+      const float b = a.b2 ? a.b2[ch] : 0.0f;
+#pragma unroll
+      for (int i = 0; i < GATE_IMG; i++) {
+        const float zz = z[i] + b;
+        const float g = a.hard ? __saturatef(zz * a.alpha + a.beta) : 1.0f / (1.0f + expf(-zz));
+        if (i < nimg) a.s[(int64_t)(n0 + i) * a.c + ch] = g + a.offset;
+      }
+    }
   }
 }
 
 int gate_launch(const GateArgs& a, cudaStream_t st) {
   if (a.c % 8 != 0 || a.c > 4096) return set_error(SDX_ERR_NOT_SUPPORTED, "channel gate: c must be a multiple of 8, <= 4096");
+  if (a.r < 1 || a.r > a.c) return set_error(SDX_ERR_NOT_SUPPORTED, "channel gate: hidden width must be in 1..c");
   if (!a.partial) return set_error(SDX_ERR_INVALID, "channel gate: scratch buffer missing");
   const int chunks = gate_chunks(a.hw, a.c);
   const int cg = a.c / 8;
@@ -480,10 +551,24 @@ int gate_launch(const GateArgs& a, cudaStream_t st) {
   const int lanes_p = block / cg;
   const size_t red = sizeof(float) * lanes_p * a.c;
   if (red > 48 * 1024) return set_error(SDX_ERR_NOT_SUPPORTED, "channel gate: reduction stage too large");
+  const size_t fc1_smem = sizeof(float) * GATE_IMG * a.c, fc2_smem = sizeof(float) * GATE_IMG * a.r;
+  if (fc1_smem > 160 * 1024) return set_error(SDX_ERR_NOT_SUPPORTED, "channel gate: too many channels for the FC stage");
+  static bool attr = false;
+  if (!attr) {
+    cudaError_t e = cudaFuncSetAttribute(gate_fc1_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, 160 * 1024);
+    if (e == cudaSuccess)
+      e = cudaFuncSetAttribute(gate_fc2_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, 160 * 1024);
+    if (e != cudaSuccess) return set_cuda_error(e, "cudaFuncSetAttribute(gate_fc)");
+    attr = true;
+  }
+  float* hid = a.partial + (size_t)a.batch * chunks * a.c;  // [batch][r], r <= c
   gap_partial_kernel<<<dim3(chunks, a.batch), block, red, st>>>(a.x, a.hw, a.c, chunks, a.partial);
   SDX_LAUNCH_CHECK("gap_partial");
-  gate_fc_kernel<<<a.batch, 256, sizeof(float) * (a.c + a.r), st>>>(a, chunks);
-  SDX_LAUNCH_CHECK("gate_fc");
+  const int gx = (a.batch + GATE_IMG - 1) / GATE_IMG;
+  gate_fc1_kernel<<<dim3(gx, (a.r + GATE_RJ - 1) / GATE_RJ), 256, fc1_smem, st>>>(a, chunks, hid);
+  SDX_LAUNCH_CHECK("gate_fc1");
+  gate_fc2_kernel<<<dim3(gx, (a.c + GATE_CJ - 1) / GATE_CJ), 256, fc2_smem, st>>>(a, hid);
+  SDX_LAUNCH_CHECK("gate_fc2");
   return SDX_OK;
 }
 

@@ -119,29 +119,46 @@ struct TcArgs {
 };
 
 // ------------------------------------------------------------------ TMA store / bulk-group helpers
-__device__ __forceinline__ void tma_store_2d(const CUtensorMap* map, uint32_t src, int c0, int c1) {
-  asm volatile("cp.async.bulk.tensor.2d.global.shared::cta.bulk_group [%0, {%2, %3}], [%1];" ::"l"(
+// Predicated on `p` (the warp's elected lane, elect_leader()): called by the whole converged warp,
+// executed by one lane. Bulk groups belong to the issuing thread, so one warp always uses the same
+// elected lane (the lowest, as the warp is converged) for its stores, commits and waits.
+__device__ __forceinline__ void tma_store_2d(uint32_t p, const CUtensorMap* map, uint32_t src, int c0, int c1) {
+  asm volatile("{\n\t.reg .pred q;\n\tsetp.ne.b32 q, %4, 0;\n\t"
+               "@q cp.async.bulk.tensor.2d.global.shared::cta.bulk_group [%0, {%2, %3}], [%1];\n\t}" ::"l"(
                    reinterpret_cast<uint64_t>(map)),
-               "r"(src), "r"(c0), "r"(c1)
+               "r"(src), "r"(c0), "r"(c1), "r"(p)
                : "memory");
 }
-__device__ __forceinline__ void tma_store_4d(const CUtensorMap* map, uint32_t src, int c0, int c1, int c2, int c3) {
-  asm volatile("cp.async.bulk.tensor.4d.global.shared::cta.bulk_group [%0, {%2, %3, %4, %5}], [%1];" ::"l"(
+__device__ __forceinline__ void tma_store_4d(uint32_t p, const CUtensorMap* map, uint32_t src, int c0, int c1, int c2,
+                                             int c3) {
+  asm volatile("{\n\t.reg .pred q;\n\tsetp.ne.b32 q, %6, 0;\n\t"
+               "@q cp.async.bulk.tensor.4d.global.shared::cta.bulk_group [%0, {%2, %3, %4, %5}], [%1];\n\t}" ::"l"(
                    reinterpret_cast<uint64_t>(map)),
-               "r"(src), "r"(c0), "r"(c1), "r"(c2), "r"(c3)
+               "r"(src), "r"(c0), "r"(c1), "r"(c2), "r"(c3), "r"(p)
                : "memory");
 }
-__device__ __forceinline__ void tma_store_5d(const CUtensorMap* map, uint32_t src, int c0, int c1, int c2, int c3,
-                                             int c4) {
-  asm volatile("cp.async.bulk.tensor.5d.global.shared::cta.bulk_group [%0, {%2, %3, %4, %5, %6}], [%1];" ::"l"(
+__device__ __forceinline__ void tma_store_5d(uint32_t p, const CUtensorMap* map, uint32_t src, int c0, int c1, int c2,
+                                             int c3, int c4) {
+  asm volatile("{\n\t.reg .pred q;\n\tsetp.ne.b32 q, %7, 0;\n\t"
+               "@q cp.async.bulk.tensor.5d.global.shared::cta.bulk_group [%0, {%2, %3, %4, %5, %6}], [%1];\n\t}" ::"l"(
                    reinterpret_cast<uint64_t>(map)),
-               "r"(src), "r"(c0), "r"(c1), "r"(c2), "r"(c3), "r"(c4)
+               "r"(src), "r"(c0), "r"(c1), "r"(c2), "r"(c3), "r"(c4), "r"(p)
                : "memory");
 }
-__device__ __forceinline__ void bulk_commit() { asm volatile("cp.async.bulk.commit_group;" ::: "memory"); }
-__device__ __forceinline__ void bulk_wait_read0() { asm volatile("cp.async.bulk.wait_group.read 0;" ::: "memory"); }
-__device__ __forceinline__ void bulk_wait_read1() { asm volatile("cp.async.bulk.wait_group.read 1;" ::: "memory"); }
-__device__ __forceinline__ void bulk_wait_all() { asm volatile("cp.async.bulk.wait_group 0;" ::: "memory"); }
+__device__ __forceinline__ void bulk_commit(uint32_t p) {
+  asm volatile("{\n\t.reg .pred q;\n\tsetp.ne.b32 q, %0, 0;\n\t@q cp.async.bulk.commit_group;\n\t}" ::"r"(p) : "memory");
+}
+__device__ __forceinline__ void bulk_wait_read0(uint32_t p) {
+  asm volatile("{\n\t.reg .pred q;\n\tsetp.ne.b32 q, %0, 0;\n\t@q cp.async.bulk.wait_group.read 0;\n\t}" ::"r"(p)
+               : "memory");
+}
+__device__ __forceinline__ void bulk_wait_read1(uint32_t p) {
+  asm volatile("{\n\t.reg .pred q;\n\tsetp.ne.b32 q, %0, 0;\n\t@q cp.async.bulk.wait_group.read 1;\n\t}" ::"r"(p)
+               : "memory");
+}
+__device__ __forceinline__ void bulk_wait_all(uint32_t p) {
+  asm volatile("{\n\t.reg .pred q;\n\tsetp.ne.b32 q, %0, 0;\n\t@q cp.async.bulk.wait_group 0;\n\t}" ::"r"(p) : "memory");
+}
 __device__ __forceinline__ void fence_async_smem() { asm volatile("fence.proxy.async.shared::cta;" ::: "memory"); }
 // ------------------------------------------------------------------ per-thread fallback helpers
 __device__ __forceinline__ void load8_res(const TcArgs& a, int64_t off, float* r) {
@@ -198,6 +215,12 @@ __device__ __forceinline__ void sts16(uint32_t addr, const uint4& v) {
                : "memory");
 }
 
+// Bounded mbarrier wait by every lane of a converged warp; the result is made warp-uniform.
+__device__ __forceinline__ bool mbar_wait_warp(uint32_t bar, uint32_t parity, unsigned int* err, unsigned int code,
+                                               volatile int* abort_flag) {
+  return __all_sync(0xffffffffu, mbar_wait(bar, parity, err, code, abort_flag));
+}
+
 struct TileCoord {
   int img, oy0, ox0, m0, n0;
 };
@@ -207,8 +230,8 @@ struct TileCoord {
 // 32/BW whole tile rows (tile widths are powers of two, so BW divides 32 or 32 divides BW).
 // A store whose box starts past the tensor's edge is skipped (it would write nothing); loads there
 // read the zero fill.
-__device__ __forceinline__ void warp_copy(const TcArgs& a, const CUtensorMap* map, uint32_t src, int g, int q,
-                                          const TileCoord& t, bool load, uint32_t bar) {
+__device__ __forceinline__ void warp_copy(uint32_t p, const TcArgs& a, const CUtensorMap* map, uint32_t src, int g,
+                                          int q, const TileCoord& t, bool load, uint32_t bar) {
   const int n = t.n0 + g * a.G;
   if (a.mode == TC_CONV) {
     const int p0 = q * 32;
@@ -217,15 +240,15 @@ __device__ __forceinline__ void warp_copy(const TcArgs& a, const CUtensorMap* ma
     if (a.convt_oc > 0) {
       const int row = a.convt_kw * a.convt_oc;
       const int dy = n / row, c = n - dy * row;
-      tma_store_5d(map, src, c, x, dy, y, t.img);
+      tma_store_5d(p, map, src, c, x, dy, y, t.img);
     } else if (load) {
-      tma_load_4d(src, map, bar, a.out_ch_off + n, x, y, t.img);
+      tma_load_4d_p(p, src, map, bar, a.out_ch_off + n, x, y, t.img);
     } else {
-      tma_store_4d(map, src, a.out_ch_off + n, x, y, t.img);
+      tma_store_4d(p, map, src, a.out_ch_off + n, x, y, t.img);
     }
   } else {
-    if (load) tma_load_2d(src, map, bar, a.out_ch_off + n, t.m0 + q * 32);
-    else if (t.m0 + q * 32 < a.M) tma_store_2d(map, src, a.out_ch_off + n, t.m0 + q * 32);
+    if (load) tma_load_2d_p(p, src, map, bar, a.out_ch_off + n, t.m0 + q * 32);
+    else if (t.m0 + q * 32 < a.M) tma_store_2d(p, map, src, a.out_ch_off + n, t.m0 + q * 32);
   }
 }
 
@@ -235,35 +258,35 @@ __device__ __forceinline__ void warp_copy(const TcArgs& a, const CUtensorMap* ma
 // 16-byte units: A by `a_tap` per tap, B by `b_tap` per tap and `b_lo` to the lo term.
 // `first` = 0 makes the first MMA of a tile overwrite the accumulator.
 template <int BT, int NK, bool TWO>
-__device__ __forceinline__ void umma_stage(uint32_t d, uint64_t ad, uint64_t bd, uint32_t a_tap, uint32_t b_tap,
+__device__ __forceinline__ void umma_stage(uint32_t p, uint32_t d, uint64_t ad, uint64_t bd, uint32_t a_tap, uint32_t b_tap,
                                            uint32_t b_lo, uint32_t idesc, uint32_t first) {
 #pragma unroll
   for (int j = 0; j < BT; j++) {
 #pragma unroll
     for (int k = 0; k < NK; k++) {
       const uint64_t a = ad + (uint64_t)(j * a_tap + 2u * k), b = bd + (uint64_t)(j * b_tap + 2u * k);
-      umma_f16(d, a, b, idesc, (j == 0 && k == 0) ? first : 1u);
-      if (TWO) umma_f16(d, a, b + b_lo, idesc, 1u);
+      umma_f16_p(p, d, a, b, idesc, (j == 0 && k == 0) ? first : 1u);
+      if (TWO) umma_f16_p(p, d, a, b + b_lo, idesc, 1u);
     }
   }
 }
 
 template <bool TWO>
-__device__ __forceinline__ void umma_stage_dispatch(int bt, int nk, uint32_t d, uint64_t ad, uint64_t bd, uint32_t a_tap,
+__device__ __forceinline__ void umma_stage_dispatch(uint32_t p, int bt, int nk, uint32_t d, uint64_t ad, uint64_t bd, uint32_t a_tap,
                                                     uint32_t b_tap, uint32_t b_lo, uint32_t idesc, uint32_t first) {
   if (bt == 1) {
-    if (nk == 4) umma_stage<1, 4, TWO>(d, ad, bd, a_tap, b_tap, b_lo, idesc, first);
-    else if (nk == 2) umma_stage<1, 2, TWO>(d, ad, bd, a_tap, b_tap, b_lo, idesc, first);
-    else umma_stage<1, 1, TWO>(d, ad, bd, a_tap, b_tap, b_lo, idesc, first);
+    if (nk == 4) umma_stage<1, 4, TWO>(p, d, ad, bd, a_tap, b_tap, b_lo, idesc, first);
+    else if (nk == 2) umma_stage<1, 2, TWO>(p, d, ad, bd, a_tap, b_tap, b_lo, idesc, first);
+    else umma_stage<1, 1, TWO>(p, d, ad, bd, a_tap, b_tap, b_lo, idesc, first);
   } else if (bt == 3) {
-    if (nk == 4) umma_stage<3, 4, TWO>(d, ad, bd, a_tap, b_tap, b_lo, idesc, first);
-    else if (nk == 2) umma_stage<3, 2, TWO>(d, ad, bd, a_tap, b_tap, b_lo, idesc, first);
-    else umma_stage<3, 1, TWO>(d, ad, bd, a_tap, b_tap, b_lo, idesc, first);
+    if (nk == 4) umma_stage<3, 4, TWO>(p, d, ad, bd, a_tap, b_tap, b_lo, idesc, first);
+    else if (nk == 2) umma_stage<3, 2, TWO>(p, d, ad, bd, a_tap, b_tap, b_lo, idesc, first);
+    else umma_stage<3, 1, TWO>(p, d, ad, bd, a_tap, b_tap, b_lo, idesc, first);
   } else {
     for (int j = 0; j < bt; j++) {
-      if (nk == 4) umma_stage<1, 4, TWO>(d, ad + (uint64_t)(j * a_tap), bd + (uint64_t)(j * b_tap), 0, 0, b_lo, idesc, j == 0 ? first : 1u);
-      else if (nk == 2) umma_stage<1, 2, TWO>(d, ad + (uint64_t)(j * a_tap), bd + (uint64_t)(j * b_tap), 0, 0, b_lo, idesc, j == 0 ? first : 1u);
-      else umma_stage<1, 1, TWO>(d, ad + (uint64_t)(j * a_tap), bd + (uint64_t)(j * b_tap), 0, 0, b_lo, idesc, j == 0 ? first : 1u);
+      if (nk == 4) umma_stage<1, 4, TWO>(p, d, ad + (uint64_t)(j * a_tap), bd + (uint64_t)(j * b_tap), 0, 0, b_lo, idesc, j == 0 ? first : 1u);
+      else if (nk == 2) umma_stage<1, 2, TWO>(p, d, ad + (uint64_t)(j * a_tap), bd + (uint64_t)(j * b_tap), 0, 0, b_lo, idesc, j == 0 ? first : 1u);
+      else umma_stage<1, 1, TWO>(p, d, ad + (uint64_t)(j * a_tap), bd + (uint64_t)(j * b_tap), 0, 0, b_lo, idesc, j == 0 ? first : 1u);
     }
   }
 }
@@ -508,23 +531,24 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
   auto b_res_off = [&](int term, int tap, int cb, int nt) -> uint32_t {
     return (uint32_t)((((term * a.taps + tap) * a.kb_per_tap + cb) * a.n_tiles + nt)) * b_tap_bytes;
   };
-  // The producer and MMA loops run on one thread each and sit on the critical path of every
-  // stage: no integer division inside them (ring slot, phase, tap and channel block advance as
-  // counters).
+  // The producer and MMA loops sit on the critical path of every stage: no integer division inside
+  // them (ring slot, phase, tap and channel block advance as counters). Each runs on a whole warp
+  // (warp-uniform values, uniform registers) and issues its copies / MMAs from the elected lane.
   if (warp == 0) {
-    if (lane == 0) {
+    const uint32_t ld = elect_leader();
+    {
       uint32_t issued_mask = 0;  // ring slots that received at least one copy
       uint32_t last_phase = 0;   // bit s: phase of the last copy into slot s
       bool ok = true;
       if (a.b_resident) {
         // every weight block once, onto one barrier
         const uint32_t bb = smem_u32(bres);
-        mbar_arrive_expect_tx(bb, a.b_total_bytes);
+        mbar_arrive_expect_tx_p(ld, bb, a.b_total_bytes);
         for (int term = 0; term < a.wterms; term++)
           for (int tap = 0; tap < a.taps; tap++)
             for (int cb = 0; cb < a.kb_per_tap; cb++)
               for (int nt = 0; nt < a.n_tiles; nt++)
-                tma_load_2d(smem_u32(sB) + b_res_off(term, tap, cb, nt), &tmB, bb, cb * a.kblk,
+                tma_load_2d_p(ld, smem_u32(sB) + b_res_off(term, tap, cb, nt), &tmB, bb, cb * a.kblk,
                             (term * a.taps + tap) * a.b_rows_per_tap + nt * a.BN);
       }
       int s = 0;
@@ -543,12 +567,12 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
         }
         int tk = 0, cg = 0;  // tk: tap, or kx in halo mode; cg: channel-block group
         for (int kb = 0; kb < kblocks; kb++) {
-          if (!mbar_wait(smem_u32(&empty[s]), phase ^ 1u, a.err, SDX_DEV_WAIT_EMPTY, abort_flag)) {
+          if (!mbar_wait_warp(smem_u32(&empty[s]), phase ^ 1u, a.err, SDX_DEV_WAIT_EMPTY, abort_flag)) {
             ok = false;
             break;
           }
           const uint32_t fb = smem_u32(&full[s]);
-          mbar_arrive_expect_tx(fb, (uint32_t)a.cps * a.a_box_bytes + b_stage_bytes);
+          mbar_arrive_expect_tx_p(ld, fb, (uint32_t)a.cps * a.a_box_bytes + b_stage_bytes);
           const uint32_t dA0 = smem_u32(sA) + (uint32_t)s * a.a_stage_bytes;
           const uint32_t dB0 = smem_u32(sB) + (uint32_t)s * b_stage_bytes;
           for (int ci = 0; ci < a.cps; ci++) {
@@ -556,21 +580,21 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
             const uint32_t dA = dA0 + (uint32_t)ci * a.a_blk_bytes;
             if (a.halo) {
               // rows oy0 - pt .. oy0 - pt + BH + kh - 2 of input column block kx (zero fill = padding)
-              tma_load_4d(dA, &tmA, fb, cb * a.kblk, ox0 + tk - a.pad_l, oy0 - a.pad_t, img);
+              tma_load_4d_p(ld, dA, &tmA, fb, cb * a.kblk, ox0 + tk - a.pad_l, oy0 - a.pad_t, img);
             } else if (a.mode == TC_CONV) {
               const int ky = tk / a.kw, kx = tk - ky * a.kw;
-              tma_load_4d(dA, &tmA, fb, cb * a.kblk, ox0 + kx - a.pad_l, oy0 + ky - a.pad_t, img);
+              tma_load_4d_p(ld, dA, &tmA, fb, cb * a.kblk, ox0 + kx - a.pad_l, oy0 + ky - a.pad_t, img);
             } else {
-              tma_load_2d(dA, &tmA, fb, cb * a.kblk, m_tile * TC_BM);
+              tma_load_2d_p(ld, dA, &tmA, fb, cb * a.kblk, m_tile * TC_BM);
             }
             if (!a.b_resident) {
               const uint32_t dB = dB0 + (uint32_t)ci * b_cb_bytes;
               for (int j = 0; j < a.b_taps; j++) {
                 const int tap = a.halo ? j * a.kw + tk : tk;
                 const int brow = tap * a.b_rows_per_tap + n_tile * a.BN;
-                tma_load_2d(dB + j * b_tap_bytes, &tmB, fb, cb * a.kblk, brow);
+                tma_load_2d_p(ld, dB + j * b_tap_bytes, &tmB, fb, cb * a.kblk, brow);
                 if (a.wterms == 2)
-                  tma_load_2d(dB + b_half_bytes + j * b_tap_bytes, &tmB, fb, cb * a.kblk, a.taps * a.b_rows_per_tap + brow);
+                  tma_load_2d_p(ld, dB + b_half_bytes + j * b_tap_bytes, &tmB, fb, cb * a.kblk, a.taps * a.b_rows_per_tap + brow);
               }
             }
           }
@@ -594,7 +618,8 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
     }
     __syncwarp();
   } else if (warp == 1) {
-    if (lane == 0) {
+    const uint32_t ld = elect_leader();
+    {
       const uint32_t idesc = umma_idesc_f16(TC_BM, a.BN);
       const int nk = a.kblk / 16;  // MMA k-steps per block
       // descriptor words: the high word (stride offset, version, swizzle) and the leading-offset
@@ -608,20 +633,20 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
       const uint32_t b_tap16 = a.b_resident ? (b_res_off(0, a.kw, 0, 0) >> 4) : (b_tap_bytes >> 4);
       const uint32_t b_cb = a.b_resident ? b_res_off(0, 0, 1, 0) : b_cb_bytes;  // next channel block
       const uint32_t b_lo16 = (a.b_resident ? b_res_off(1, 0, 0, 0) : b_half_bytes) >> 4;
-      bool ok = !a.b_resident || mbar_wait(smem_u32(bres), 0, a.err, SDX_DEV_WAIT_FULL, abort_flag);
+      bool ok = !a.b_resident || mbar_wait_warp(smem_u32(bres), 0, a.err, SDX_DEV_WAIT_FULL, abort_flag);
       if (ok) tc_fence_after();
       int s = 0;
       uint32_t phase = 0;
       uint32_t acc = 0, accph = 0;
       for (int tile = blockIdx.x; tile < total_tiles && ok; tile += gridDim.x) {
         const int n_tile = a.n_tiles == 1 ? 0 : tile % a.n_tiles;
-        if (!mbar_wait(smem_u32(&acce[acc]), accph ^ 1u, a.err, SDX_DEV_WAIT_ACC_EMPTY, abort_flag)) break;
+        if (!mbar_wait_warp(smem_u32(&acce[acc]), accph ^ 1u, a.err, SDX_DEV_WAIT_ACC_EMPTY, abort_flag)) break;
         tc_fence_after();
         const uint32_t d = tmem_base + acc * (uint32_t)a.acc_stride;
         int tk = 0, cg = 0;
         uint32_t first = 0;  // 0 until the tile's first MMA (overwrite), then 1 (accumulate)
         for (int kb = 0; kb < kblocks; kb++) {
-          if (!mbar_wait(smem_u32(&full[s]), phase, a.err, SDX_DEV_WAIT_FULL, abort_flag)) {
+          if (!mbar_wait_warp(smem_u32(&full[s]), phase, a.err, SDX_DEV_WAIT_FULL, abort_flag)) {
             ok = false;
             break;
           }
@@ -633,11 +658,11 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
           for (int ci = 0; ci < a.cps; ci++, sa += a.a_blk_bytes, b0 += b_cb) {
             const uint64_t ad = dconst | (uint64_t)((sa >> 4) & 0x3FFFu);
             const uint64_t bd = dconst | (uint64_t)((b0 >> 4) & 0x3FFFu);
-            if (a.wterms == 2) umma_stage_dispatch<true>(a.b_taps, nk, d, ad, bd, a_tap16, b_tap16, b_lo16, idesc, first);
-            else umma_stage_dispatch<false>(a.b_taps, nk, d, ad, bd, a_tap16, b_tap16, b_lo16, idesc, first);
+            if (a.wterms == 2) umma_stage_dispatch<true>(ld, a.b_taps, nk, d, ad, bd, a_tap16, b_tap16, b_lo16, idesc, first);
+            else umma_stage_dispatch<false>(ld, a.b_taps, nk, d, ad, bd, a_tap16, b_tap16, b_lo16, idesc, first);
             first = 1u;
           }
-          tc_commit(smem_u32(&empty[s]));
+          tc_commit_p(ld, smem_u32(&empty[s]));
           if (++cg == groups) {
             cg = 0;
             tk++;
@@ -648,14 +673,14 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
           }
         }
         if (!ok) break;
-        tc_commit(smem_u32(&accf[acc]));
+        tc_commit_p(ld, smem_u32(&accf[acc]));
         if (++acc == (uint32_t)a.nacc) {
           acc = 0;
           accph ^= 1u;
         }
       }
       // wind-down: all issued MMAs complete before TMEM / smem are released
-      tc_commit(smem_u32(drain));
+      tc_commit_p(ld, smem_u32(drain));
       mbar_wait_drain(smem_u32(drain), 0, a.err, SDX_DEV_WAIT_DRAIN);
     }
     __syncwarp();
@@ -672,7 +697,8 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
     const uint32_t stage0 = smem_u32(sStage) + (uint32_t)e * a.nsbuf * a.sbuf_bytes + (uint32_t)q * 32u * P;
     const int tile0 = blockIdx.x + e * gridDim.x, tstep = 2 * gridDim.x;
     uint32_t res_phase = 0;    // bit b: parity of the next wait on buffer b's residual barrier
-    bool res_pending = false;  // lane 0: a residual load is in flight into buffer (lc % nsbuf)
+    bool res_pending = false;  // a residual load is in flight into buffer (lc % nsbuf)
+    const uint32_t eld = elect_leader();  // this warp's issuing lane for TMA copies and bulk groups
 
     auto coords = [&](int tile, TileCoord& t) {
       const int m_tile = a.n_tiles == 1 ? tile : tile / a.n_tiles;
@@ -700,10 +726,10 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
       const int ng = groups_of(t);
       const uint32_t rb = smem_u32(&resb[(e * 2 + buf) * 4 + q]);
       const uint32_t slab = stage0 + buf * a.sbuf_bytes;
-      mbar_arrive_expect_tx(rb, (uint32_t)ng * a.slab_tx);
-      for (int g = 0; g < ng; g++) warp_copy(a, &tmRes, slab + g * a.group_bytes, g, q, t, true, rb);
+      mbar_arrive_expect_tx_p(eld, rb, (uint32_t)ng * a.slab_tx);
+      for (int g = 0; g < ng; g++) warp_copy(eld, a, &tmRes, slab + g * a.group_bytes, g, q, t, true, rb);
     };
-    if (a.tma_res && lane == 0 && tile0 < total_tiles) {
+    if (a.tma_res && tile0 < total_tiles) {
       issue_res(tile0, 0);
       res_pending = true;
     }
@@ -713,19 +739,15 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
       const uint32_t lt = 2 * lc + (uint32_t)e;
       const uint32_t acc = lt & (uint32_t)(a.nacc - 1), ar = lt >> (a.nacc == 4 ? 2 : 1);
       const uint32_t sbi = a.nsbuf == 2 ? (lc & 1u) : 0u;
-      int ok = 0;
-      if (lane == 0) {
-        ok = mbar_wait(smem_u32(&accf[acc]), ar & 1u, a.err, SDX_DEV_WAIT_ACC_FULL, abort_flag) ? 1 : 0;
-        if (ok && a.tma_res) {
-          ok = mbar_wait(smem_u32(&resb[(e * 2 + sbi) * 4 + q]), (res_phase >> sbi) & 1u, a.err,
-                         SDX_DEV_WAIT_FULL, abort_flag) ? 1 : 0;
-          if (ok) {
-            res_phase ^= 1u << sbi;
-            res_pending = false;
-          }
+      bool ok = mbar_wait_warp(smem_u32(&accf[acc]), ar & 1u, a.err, SDX_DEV_WAIT_ACC_FULL, abort_flag);
+      if (ok && a.tma_res) {
+        ok = mbar_wait_warp(smem_u32(&resb[(e * 2 + sbi) * 4 + q]), (res_phase >> sbi) & 1u, a.err, SDX_DEV_WAIT_FULL,
+                            abort_flag);
+        if (ok) {
+          res_phase ^= 1u << sbi;
+          res_pending = false;
         }
       }
-      ok = __shfl_sync(0xffffffffu, ok, 0);
       if (!ok) break;
       __syncwarp();
       tc_fence_after();
@@ -906,15 +928,15 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
         // make this warp's generic-proxy staging writes visible to the TMA engine, store its rows
         fence_async_smem();
         __syncwarp();
-        if (lane == 0) {
+        {
           const int ng = groups_of(tcd);
-          for (int gg = 0; gg < ng; gg++) warp_copy(a, &tmOut, slab + gg * a.group_bytes, gg, q, tcd, false, 0);
-          bulk_commit();
+          for (int gg = 0; gg < ng; gg++) warp_copy(eld, a, &tmOut, slab + gg * a.group_bytes, gg, q, tcd, false, 0);
+          bulk_commit(eld);
           // the next tile's buffer is free once the store that last read it has read it; then its
           // residual rows can be fetched while this warp waits for the next accumulator
           if (tile + tstep < total_tiles) {
-            if (a.nsbuf == 2) bulk_wait_read1();
-            else bulk_wait_read0();
+            if (a.nsbuf == 2) bulk_wait_read1(eld);
+            else bulk_wait_read0(eld);
             if (a.tma_res) {
               issue_res(tile + tstep, a.nsbuf == 2 ? ((lc + 1) & 1u) : 0u);
               res_pending = true;
@@ -924,13 +946,13 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
       }
       __syncwarp();
     }
-    if (lane == 0) {
+    {
       if (res_pending) {
         // wind-down after an abort: the residual copy in flight must land before smem goes away
         const uint32_t buf = a.nsbuf == 2 ? (lc & 1u) : 0u;
         mbar_wait_drain(smem_u32(&resb[(e * 2 + buf) * 4 + q]), (res_phase >> buf) & 1u, a.err, SDX_DEV_WAIT_DRAIN);
       }
-      if (a.tma_out) bulk_wait_all();
+      if (a.tma_out) bulk_wait_all(eld);
     }
   }
   __syncthreads();

@@ -251,6 +251,21 @@ def test_channel_gate_and_broadcast(be, c, hw):
     assert_close(host(y), O.channel_broadcast(x, ref_s), "x*s")
 
 
+def test_channel_gate_batch_invariant(be):
+    """An image's gate is bit-identical whichever batch (and FC block of images) it runs in."""
+    from simdonnx_b200 import backend as B
+    rng = np.random.default_rng(41)
+    c, r, hw = 256, 64, 40
+    x = rnd(rng, 9, hw, hw, c)
+    w1, b1, w2, b2 = rnd(rng, r, c), rnd(rng, r), rnd(rng, c, r), rnd(rng, c)
+    args = (dev32(w1), dev32(b1), dev32(w2), dev32(b2))
+    s9 = host(B.channel_gate(be, dev16(x), *args, alpha=0.2, beta=0.5))
+    s1 = host(B.channel_gate(be, dev16(x[5:6]), *args, alpha=0.2, beta=0.5))
+    np.testing.assert_array_equal(s9[5:6], s1)
+    ref_s = O.channel_gate(x, w1, b1, w2, b2, act1_relu=True, hard=True, alpha=0.2, beta=0.5)
+    assert_close(s9, ref_s, "gate b9")
+
+
 def test_concat_nearest(be):
     """Upsample-and-concat in one pass == resize each input then concat (bit exact: pure copies)."""
     from simdonnx_b200 import backend as B

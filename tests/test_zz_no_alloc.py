@@ -87,7 +87,7 @@ def test_static_gate_matches_scratch_gate_twice(ctx, b, hw, c):
 
 
 def test_static_gate_rejects_oversized_scratch(ctx):
-    # c = 4096 with 64 pixel chunks per image needs 1 MiB per image: 5 images exceed 4 MiB
+    # c = 4096 with 64 pixel chunks per image needs over 1 MiB per image: 5 images exceed 4 MiB
     need = int(N.lib().sdx_channel_gate_scratch_bytes(5, 512 * 512, 4096))
     assert need > MAX_BYTES
     s = torch.empty((5, 4096), dtype=torch.float32, device="cuda")
