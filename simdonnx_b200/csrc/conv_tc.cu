@@ -291,6 +291,52 @@ __device__ __forceinline__ void umma_stage_dispatch(uint32_t p, int bt, int nk, 
   }
 }
 
+// MMA issue loop for tiles that are one pipeline stage (kernel taps 1, weights resident, every
+// channel block of the tile in one stage): per tile two waits, CPS x NK (x2 with TWO) MMAs and two
+// commits, no runtime loop or dispatch between them (each costs the issuing warp far more than
+// the MMA itself); ring slot, phases and the N tile advance without branches.
+struct MmaSingle {
+  uint32_t d0, acc_stride, sA, a_stage_bytes, a_blk16, b_cb16, b_nt16, b_lo16, idesc;
+  uint64_t dconst, bd0;
+  int S, nacc, n_tiles, nt_step, nt0;
+};
+template <int NK, bool TWO, int CPS>
+__device__ __noinline__ void mma_single_loop(uint32_t ld, const MmaSingle m, int tile0, int total_tiles, int tstep,
+                                             uint64_t* full, uint64_t* empty, uint64_t* accf, uint64_t* acce,
+                                             unsigned int* err, volatile int* abort_flag) {
+  int s = 0, nt = m.nt0;
+  uint32_t phase = 0, acc = 0, accph = 0;
+  for (int tile = tile0; tile < total_tiles; tile += tstep) {
+    if (!mbar_wait_warp(smem_u32(&acce[acc]), accph ^ 1u, err, SDX_DEV_WAIT_ACC_EMPTY, abort_flag)) break;
+    if (!mbar_wait_warp(smem_u32(&full[s]), phase, err, SDX_DEV_WAIT_FULL, abort_flag)) break;
+    tc_fence_after();
+    const uint32_t d = m.d0 + acc * m.acc_stride;
+    const uint64_t ad = m.dconst | (uint64_t)(((m.sA + (uint32_t)s * m.a_stage_bytes) >> 4) & 0x3FFFu);
+    const uint64_t bd = m.bd0 + (uint64_t)((uint32_t)nt * m.b_nt16);
+#pragma unroll
+    for (int ci = 0; ci < CPS; ci++)
+      umma_stage<1, NK, TWO>(ld, d, ad + (uint64_t)(ci * m.a_blk16), bd + (uint64_t)(ci * m.b_cb16), 0u, 0u, m.b_lo16,
+                             m.idesc, ci == 0 ? 0u : 1u);
+    tc_commit_p(ld, smem_u32(&empty[s]));
+    tc_commit_p(ld, smem_u32(&accf[acc]));
+    s = s + 1 == m.S ? 0 : s + 1;
+    phase ^= s == 0 ? 1u : 0u;
+    acc = acc + 1 == (uint32_t)m.nacc ? 0u : acc + 1;
+    accph ^= acc == 0 ? 1u : 0u;
+    nt += m.nt_step;
+    nt = nt >= m.n_tiles ? nt - m.n_tiles : nt;
+  }
+}
+template <int NK, bool TWO>
+__device__ __forceinline__ void mma_single_cps(int cps, uint32_t ld, const MmaSingle& m, int tile0, int total_tiles,
+                                               int tstep, uint64_t* full, uint64_t* empty, uint64_t* accf,
+                                               uint64_t* acce, unsigned int* err, volatile int* abort_flag) {
+  if (cps == 1) mma_single_loop<NK, TWO, 1>(ld, m, tile0, total_tiles, tstep, full, empty, accf, acce, err, abort_flag);
+  else if (cps == 2) mma_single_loop<NK, TWO, 2>(ld, m, tile0, total_tiles, tstep, full, empty, accf, acce, err, abort_flag);
+  else if (cps == 3) mma_single_loop<NK, TWO, 3>(ld, m, tile0, total_tiles, tstep, full, empty, accf, acce, err, abort_flag);
+  else mma_single_loop<NK, TWO, 4>(ld, m, tile0, total_tiles, tstep, full, empty, accf, acce, err, abort_flag);
+}
+
 // One 16-column chunk (tile columns 16c..16c+15) of one accumulator row: bias -> + residual ->
 // activation -> staging slab row `srow` (TMA store path) or global memory (fallback path).
 // (g, cg) = column group of the chunk and its first column inside the group; advanced here.
@@ -638,6 +684,37 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
       int s = 0;
       uint32_t phase = 0;
       uint32_t acc = 0, accph = 0;
+      const bool single = kblocks == 1 && a.b_resident && a.b_taps == 1 && a.cps <= 4 && (nk == 1 || nk == 2 || nk == 4);
+      if (ok && single) {
+        MmaSingle m;
+        m.d0 = tmem_base;
+        m.acc_stride = (uint32_t)a.acc_stride;
+        m.sA = smem_u32(sA);
+        m.a_stage_bytes = a.a_stage_bytes;
+        m.a_blk16 = a.a_blk_bytes >> 4;
+        m.b_cb16 = b_cb >> 4;
+        m.b_nt16 = b_res_off(0, 0, 0, 1) >> 4;
+        m.b_lo16 = b_lo16;
+        m.idesc = idesc;
+        m.dconst = dconst;
+        m.bd0 = dconst | (uint64_t)((sB_addr >> 4) & 0x3FFFu);
+        m.S = S;
+        m.nacc = a.nacc;
+        m.n_tiles = a.n_tiles;
+        m.nt_step = (int)(gridDim.x % (unsigned)a.n_tiles);
+        m.nt0 = (int)(blockIdx.x % (unsigned)a.n_tiles);
+        const int tt = a.m_tiles * a.n_tiles;
+        if (a.wterms == 2) {
+          if (nk == 1) mma_single_cps<1, true>(a.cps, ld, m, blockIdx.x, tt, gridDim.x, full, empty, accf, acce, a.err, abort_flag);
+          else if (nk == 2) mma_single_cps<2, true>(a.cps, ld, m, blockIdx.x, tt, gridDim.x, full, empty, accf, acce, a.err, abort_flag);
+          else mma_single_cps<4, true>(a.cps, ld, m, blockIdx.x, tt, gridDim.x, full, empty, accf, acce, a.err, abort_flag);
+        } else {
+          if (nk == 1) mma_single_cps<1, false>(a.cps, ld, m, blockIdx.x, tt, gridDim.x, full, empty, accf, acce, a.err, abort_flag);
+          else if (nk == 2) mma_single_cps<2, false>(a.cps, ld, m, blockIdx.x, tt, gridDim.x, full, empty, accf, acce, a.err, abort_flag);
+          else mma_single_cps<4, false>(a.cps, ld, m, blockIdx.x, tt, gridDim.x, full, empty, accf, acce, a.err, abort_flag);
+        }
+        ok = false;  // the loop above ran every tile
+      }
       for (int tile = blockIdx.x; tile < total_tiles && ok; tile += gridDim.x) {
         const int n_tile = a.n_tiles == 1 ? 0 : tile % a.n_tiles;
         if (!mbar_wait_warp(smem_u32(&acce[acc]), accph ^ 1u, a.err, SDX_DEV_WAIT_ACC_EMPTY, abort_flag)) break;

@@ -174,14 +174,17 @@ __global__ void __launch_bounds__(256) dw_tma_kernel(const __grid_constant__ CUt
     oy0 = ty * TH;
     ox0 = (q - ty * tiles_x) * TW;
   };
+  // warp 0 issues the tile copies warp-uniformly from its elected lane
+  uint32_t ld0 = 0;
+  if (tid < 32) ld0 = elect_leader();
   auto issue = [&](int t, int b) {
     int n, slab, oy0, ox0;
     decode(t, n, slab, oy0, ox0);
     const uint32_t bar = smem_u32(&full[b]);
-    mbar_arrive_expect_tx(bar, tile_bytes);
-    tma_load_4d(smem_u32(dsm + b * buf_bytes), &tmX, bar, slab * CS, ox0 * S - a.pl, oy0 * S - a.pt, n);
+    mbar_arrive_expect_tx_p(ld0, bar, tile_bytes);
+    tma_load_4d_p(ld0, smem_u32(dsm + b * buf_bytes), &tmX, bar, slab * CS, ox0 * S - a.pl, oy0 * S - a.pt, n);
   };
-  uint32_t issued[2] = {0, 0};  // thread 0: copies issued into each buffer
+  uint32_t issued[2] = {0, 0};  // warp 0: copies issued into each buffer
   if (tid == 0) {
     abort_flag = 0;
     mbar_init(smem_u32(&full[0]), 1);
@@ -190,7 +193,7 @@ __global__ void __launch_bounds__(256) dw_tma_kernel(const __grid_constant__ CUt
     tma_prefetch_desc(&tmX);
   }
   __syncthreads();
-  if (tid == 0) {
+  if (tid < 32) {
     issue(t0, 0);
     issued[0] = 1;
   }
@@ -202,7 +205,7 @@ __global__ void __launch_bounds__(256) dw_tma_kernel(const __grid_constant__ CUt
   int i = 0;
   for (int t = t0; t < t1; t++, i++) {
     const int b = i & 1;
-    if (tid == 0 && t + 1 < t1) {
+    if (tid < 32 && t + 1 < t1) {
       // buffer b^1 was last read by tile i-1, which every thread finished before the barrier that
       // ended that iteration
       issue(t + 1, b ^ 1);
@@ -296,7 +299,7 @@ __global__ void __launch_bounds__(256) dw_tma_kernel(const __grid_constant__ CUt
     __syncthreads();
   }
   // wind-down (only after an abort can a copy still be in flight): drain every issued copy
-  if (tid == 0) {
+  if (tid < 32) {
     for (int b = 0; b < 2; b++)
       if (issued[b] > 0) mbar_wait_drain(smem_u32(&full[b]), (issued[b] - 1) & 1u, a.err, SDX_DEV_WAIT_DRAIN);
   }
@@ -473,12 +476,15 @@ __global__ void __launch_bounds__(256, 2) dw_slide_kernel(const __grid_constant_
     oy0 = ty * TH;
     ox0 = (q - ty * tiles_x) * TW;
   };
+  // warp 0 issues the tile copies warp-uniformly from its elected lane
+  uint32_t ld0 = 0;
+  if (tid < 32) ld0 = elect_leader();
   auto issue = [&](int t, int b) {
     int n, slab, oy0, ox0;
     decode(t, n, slab, oy0, ox0);
     const uint32_t bar = smem_u32(&full[b]);
-    mbar_arrive_expect_tx(bar, tile_bytes);
-    tma_load_4d(smem_u32(dsm + b * buf_bytes), &tmX, bar, slab * CS, ox0 - a.pl, oy0 - a.pt, n);
+    mbar_arrive_expect_tx_p(ld0, bar, tile_bytes);
+    tma_load_4d_p(ld0, smem_u32(dsm + b * buf_bytes), &tmX, bar, slab * CS, ox0 - a.pl, oy0 - a.pt, n);
   };
   uint32_t issued[2] = {0, 0};
   if (tid == 0) {
@@ -489,7 +495,7 @@ __global__ void __launch_bounds__(256, 2) dw_slide_kernel(const __grid_constant_
     tma_prefetch_desc(&tmX);
   }
   __syncthreads();
-  if (tid == 0) {
+  if (tid < 32) {
     issue(t0, 0);
     issued[0] = 1;
   }
@@ -501,7 +507,7 @@ __global__ void __launch_bounds__(256, 2) dw_slide_kernel(const __grid_constant_
   int i = 0;
   for (int t = t0; t < t1; t++, i++) {
     const int b = i & 1;
-    if (tid == 0 && t + 1 < t1) {
+    if (tid < 32 && t + 1 < t1) {
       // buffer b^1 was last read by tile i-1, finished by every thread before the closing barrier
       issue(t + 1, b ^ 1);
       issued[b ^ 1]++;
@@ -564,7 +570,7 @@ __global__ void __launch_bounds__(256, 2) dw_slide_kernel(const __grid_constant_
     __syncthreads();
   }
   // wind-down (only after an abort can a copy still be in flight): drain every issued copy
-  if (tid == 0) {
+  if (tid < 32) {
     for (int b = 0; b < 2; b++)
       if (issued[b] > 0) mbar_wait_drain(smem_u32(&full[b]), (issued[b] - 1) & 1u, a.err, SDX_DEV_WAIT_DRAIN);
   }
@@ -661,12 +667,15 @@ __global__ void __launch_bounds__(256, 2) dw_slide2_kernel(const __grid_constant
     oy0 = ty * TH;
     ox0 = (q - ty * tiles_x) * TW;
   };
+  // warp 0 issues the tile copies warp-uniformly from its elected lane
+  uint32_t ld0 = 0;
+  if (tid < 32) ld0 = elect_leader();
   auto issue = [&](int t, int b) {
     int n, slab, oy0, ox0;
     decode(t, n, slab, oy0, ox0);
     const uint32_t bar = smem_u32(&full[b]);
-    mbar_arrive_expect_tx(bar, tile_bytes);
-    tma_load_4d(smem_u32(dsm + b * buf_bytes), &tmX, bar, slab * CS, 2 * ox0 - a.pl, 2 * oy0 - a.pt, n);
+    mbar_arrive_expect_tx_p(ld0, bar, tile_bytes);
+    tma_load_4d_p(ld0, smem_u32(dsm + b * buf_bytes), &tmX, bar, slab * CS, 2 * ox0 - a.pl, 2 * oy0 - a.pt, n);
   };
   uint32_t issued[2] = {0, 0};
   if (tid == 0) {
@@ -677,7 +686,7 @@ __global__ void __launch_bounds__(256, 2) dw_slide2_kernel(const __grid_constant
     tma_prefetch_desc(&tmX);
   }
   __syncthreads();
-  if (tid == 0) {
+  if (tid < 32) {
     issue(t0, 0);
     issued[0] = 1;
   }
@@ -689,7 +698,7 @@ __global__ void __launch_bounds__(256, 2) dw_slide2_kernel(const __grid_constant
   int i = 0;
   for (int t = t0; t < t1; t++, i++) {
     const int b = i & 1;
-    if (tid == 0 && t + 1 < t1) {
+    if (tid < 32 && t + 1 < t1) {
       issue(t + 1, b ^ 1);
       issued[b ^ 1]++;
     }
@@ -761,7 +770,7 @@ __global__ void __launch_bounds__(256, 2) dw_slide2_kernel(const __grid_constant
     }
     __syncthreads();
   }
-  if (tid == 0) {
+  if (tid < 32) {
     for (int b = 0; b < 2; b++)
       if (issued[b] > 0) mbar_wait_drain(smem_u32(&full[b]), (issued[b] - 1) & 1u, a.err, SDX_DEV_WAIT_DRAIN);
   }
@@ -998,12 +1007,15 @@ __global__ void __launch_bounds__(256) stem_tma_kernel(const __grid_constant__ C
     oy0 = ty * STEM_TH;
     ox0 = (q - ty * tiles_x) * STEM_TW;
   };
+  // warp 0 issues the tile copies warp-uniformly from its elected lane
+  uint32_t ld0 = 0;
+  if (tid < 32) ld0 = elect_leader();
   auto issue = [&](int t, int b) {
     int n, oy0, ox0;
     decode(t, n, oy0, ox0);
     const uint32_t bar = smem_u32(&full[b]);
-    mbar_arrive_expect_tx(bar, kTileBytes);
-    tma_load_4d(smem_u32(bufs + b * (kBufBytes / 4)), &tmX, bar, ox0 * 2 - a.pl - 3, oy0 * 2 - a.pt, 0, n);
+    mbar_arrive_expect_tx_p(ld0, bar, kTileBytes);
+    tma_load_4d_p(ld0, smem_u32(bufs + b * (kBufBytes / 4)), &tmX, bar, ox0 * 2 - a.pl - 3, oy0 * 2 - a.pt, 0, n);
   };
   uint32_t issued[2] = {0, 0};
   for (int i = tid; i < K * K * IC * OC; i += blockDim.x) sw[i] = __ldg(a.w + i);
@@ -1016,7 +1028,7 @@ __global__ void __launch_bounds__(256) stem_tma_kernel(const __grid_constant__ C
     tma_prefetch_desc(&tmX);
   }
   __syncthreads();
-  if (tid == 0) {
+  if (tid < 32) {
     issue(t0, 0);
     issued[0] = 1;
   }
@@ -1024,7 +1036,7 @@ __global__ void __launch_bounds__(256) stem_tma_kernel(const __grid_constant__ C
   int i = 0;
   for (int t = t0; t < t1; t++, i++) {
     const int b = i & 1;
-    if (tid == 0 && t + 1 < t1) {
+    if (tid < 32 && t + 1 < t1) {
       issue(t + 1, b ^ 1);
       issued[b ^ 1]++;
     }
@@ -1083,7 +1095,7 @@ __global__ void __launch_bounds__(256) stem_tma_kernel(const __grid_constant__ C
     }
     __syncthreads();
   }
-  if (tid == 0) {
+  if (tid < 32) {
     for (int b = 0; b < 2; b++)
       if (issued[b] > 0) mbar_wait_drain(smem_u32(&full[b]), (issued[b] - 1) & 1u, a.err, SDX_DEV_WAIT_DRAIN);
   }
