@@ -54,8 +54,10 @@
 namespace sdx {
 
 constexpr int TC_BM = 128;
-constexpr int TC_EPI_GROUPS = 2;                        // epilogue warp groups (alternate tiles)
-constexpr int TC_THREADS = 64 + 128 * TC_EPI_GROUPS;    // producer warp, MMA warp, epilogue groups
+// Epilogue warp groups (kernel template G): 2, or 4 for tiles of at most 64 columns (more warps
+// hide the per-tile latency of thin tiles); a CTA is the producer warp, the MMA warp and G groups.
+constexpr int TC_EPI_GROUPS_MAX = 4;
+constexpr int tc_threads(int groups) { return 64 + 128 * groups; }
 constexpr int TC_MAX_STAGES = 8;  // <= 32 (ring slots are tracked in 32-bit masks)
 constexpr int TC_SMEM_LIMIT = 227 * 1024;
 constexpr int TC_BIAS_SMEM_MAX = 4096;  // bias floats staged in shared memory
@@ -87,6 +89,7 @@ struct TcArgs {
   int stages;
   int acc_stride;
   int nacc;             // TMEM accumulators: 4 when 4 x BN fits the 512 columns, else 2
+  int egroups;          // epilogue warp groups (the kernel's G): 2 or 4
   uint32_t tmem_cols;
   uint32_t a_box_bytes;
   // epilogue
@@ -505,8 +508,8 @@ __device__ __forceinline__ void epi_chunk_fast(const TcArgs& a, float (&v)[16], 
   sts16(ad1, u1);
 }
 
-template <int ACT, int EPI>
-__global__ void __launch_bounds__(TC_THREADS, 1)
+template <int ACT, int EPI, int G>
+__global__ void __launch_bounds__(tc_threads(G), 1)
     conv_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
                    const __grid_constant__ CUtensorMap tmOut, const __grid_constant__ CUtensorMap tmRes,
                    const TcArgs a) {
@@ -521,8 +524,8 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
   uint8_t* sA = smem;
   uint8_t* sB = smem + (size_t)S * a.a_stage_bytes;  // resident: all weights; else S weight stages
   uint8_t* sStage = sB + (a.b_resident ? (size_t)a.b_total_bytes : (size_t)S * b_stage_bytes);
-  float* sBias = reinterpret_cast<float*>(sStage + (size_t)TC_EPI_GROUPS * a.nsbuf * a.sbuf_bytes);
-  uint64_t* bars = reinterpret_cast<uint64_t*>(sStage + (size_t)TC_EPI_GROUPS * a.nsbuf * a.sbuf_bytes +
+  float* sBias = reinterpret_cast<float*>(sStage + (size_t)G * a.nsbuf * a.sbuf_bytes);
+  uint64_t* bars = reinterpret_cast<uint64_t*>(sStage + (size_t)G * a.nsbuf * a.sbuf_bytes +
                                                (((size_t)a.bias_smem * 4 + 15) & ~(size_t)15));
   uint64_t* full = bars;
   uint64_t* empty = bars + S;
@@ -530,7 +533,7 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
   uint64_t* acce = accf + 4;                      // [4] accumulator drained (128 epilogue threads)
   uint64_t* drain = acce + 4;
   uint64_t* resb = drain + 1;                     // [group][buffer][warp] residual slab landed
-  uint64_t* bres = resb + TC_EPI_GROUPS * 2 * 4;  // resident weights landed
+  uint64_t* bres = resb + G * 2 * 4;  // resident weights landed
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bres + 1);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
 
@@ -544,7 +547,7 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
       mbar_init(smem_u32(&accf[i]), 1);
       mbar_init(smem_u32(&acce[i]), 128);
     }
-    for (int i = 0; i < TC_EPI_GROUPS * 2 * 4; i++) mbar_init(smem_u32(&resb[i]), 1);
+    for (int i = 0; i < G * 2 * 4; i++) mbar_init(smem_u32(&resb[i]), 1);
     mbar_init(smem_u32(drain), 1);
     mbar_init(smem_u32(bres), 1);
     *abort_flag = 0;
@@ -762,7 +765,7 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
     }
     __syncwarp();
   } else {
-    // epilogue: group e (warps 2+4e .. 5+4e) takes the tiles lt = e, e+2, ... of this CTA; warp q
+    // epilogue: group e (warps 2+4e .. 5+4e) takes the tiles lt = e, e+G, ... of this CTA (G groups); warp q
     // reads TMEM lanes 32q..32q+31 (the lane quadrant it may access), i.e. tile rows 32q..32q+31
     const int e = (warp - 2) >> 2;
     const int q = warp & 3;
@@ -772,7 +775,7 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
     // 1024-aligned slab); 0 when the staging rows are not swizzled
     const uint32_t xr = a.swz ? (((uint32_t)lane * P) >> 7) & (P / 16u - 1u) : 0u;
     const uint32_t stage0 = smem_u32(sStage) + (uint32_t)e * a.nsbuf * a.sbuf_bytes + (uint32_t)q * 32u * P;
-    const int tile0 = blockIdx.x + e * gridDim.x, tstep = 2 * gridDim.x;
+    const int tile0 = blockIdx.x + e * gridDim.x, tstep = G * gridDim.x;
     uint32_t res_phase = 0;    // bit b: parity of the next wait on buffer b's residual barrier
     bool res_pending = false;  // a residual load is in flight into buffer (lc % nsbuf)
     const uint32_t eld = elect_leader();  // this warp's issuing lane for TMA copies and bulk groups
@@ -813,7 +816,7 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
 
     uint32_t lc = 0;  // this group's tile count
     for (int tile = tile0; tile < total_tiles; tile += tstep, lc++) {
-      const uint32_t lt = 2 * lc + (uint32_t)e;
+      const uint32_t lt = G * lc + (uint32_t)e;
       const uint32_t acc = lt & (uint32_t)(a.nacc - 1), ar = lt >> (a.nacc == 4 ? 2 : 1);
       const uint32_t sbi = a.nsbuf == 2 ? (lc & 1u) : 0u;
       bool ok = mbar_wait_warp(smem_u32(&accf[acc]), ar & 1u, a.err, SDX_DEV_WAIT_ACC_FULL, abort_flag);
@@ -1113,17 +1116,17 @@ static int encode_map(CUtensorMap* map, const void* base, int rank, const uint64
 
 static bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
 
-template <int ACT, int EPI>
+template <int ACT, int EPI, int G>
 static int launch_tc(int dev, int grid, size_t smem, cudaStream_t stream, const CUtensorMap& mA, const CUtensorMap& mB,
                      const CUtensorMap& mOut, const CUtensorMap& mRes, const TcArgs& a) {
   static bool attr_set[64] = {false};
   if (dev >= 0 && dev < 64 && !attr_set[dev]) {
-    cudaError_t e = cudaFuncSetAttribute(conv_tc_kernel<ACT, EPI>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+    cudaError_t e = cudaFuncSetAttribute(conv_tc_kernel<ACT, EPI, G>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                          TC_SMEM_LIMIT);
     if (e != cudaSuccess) return set_cuda_error(e, "cudaFuncSetAttribute(conv_tc)");
     attr_set[dev] = true;
   }
-  conv_tc_kernel<ACT, EPI><<<grid, TC_THREADS, smem, stream>>>(mA, mB, mOut, mRes, a);
+  conv_tc_kernel<ACT, EPI, G><<<grid, tc_threads(G), smem, stream>>>(mA, mB, mOut, mRes, a);
   cudaError_t e = cudaGetLastError();
   if (e != cudaSuccess) return set_cuda_error(e, "conv_tc launch");
   return SDX_OK;
@@ -1151,8 +1154,8 @@ static size_t b_stage_bytes_of(const TcArgs& a) {
 }
 
 static size_t smem_fixed(const TcArgs& a) {
-  return 1024 + (size_t)TC_EPI_GROUPS * a.nsbuf * a.sbuf_bytes + (((size_t)a.bias_smem * 4 + 15) & ~(size_t)15) +
-         8 * (2 * TC_MAX_STAGES + 26) + 16 + (a.b_resident ? (size_t)a.b_total_bytes : 0);
+  return 1024 + (size_t)a.egroups * a.nsbuf * a.sbuf_bytes + (((size_t)a.bias_smem * 4 + 15) & ~(size_t)15) +
+         8 * (2 * TC_MAX_STAGES + 10 + 8 * TC_EPI_GROUPS_MAX) + 16 + (a.b_resident ? (size_t)a.b_total_bytes : 0);
 }
 
 static size_t smem_bytes(const TcArgs& a) {
@@ -1253,7 +1256,7 @@ int tc_launch(const TcProblem& p, cudaStream_t stream) {
     int BH, BW;
     pick_pixel_tile(p.OH, p.OW, 8, p.kh - 1, &BH, &BW);
     const size_t halo_a = (size_t)(BH + p.kh - 1) * BW * kbytes;
-    const size_t staging_max = (size_t)TC_EPI_GROUPS * TC_BM * BN * (p.out_f32 ? 4 : 2);
+    const size_t staging_max = (size_t)2 * TC_BM * BN * (p.out_f32 ? 4 : 2);
     const size_t b_all = (size_t)a.wterms * p.kh * p.kw * (kpad / kblk) * n_tiles * BN * kbytes;
     const bool halo = p.kh > 1 && BH + p.kh - 1 <= 256 &&
                       (3 * (halo_a + (size_t)a.wterms * p.kh * BN * kbytes) + staging_max + 4096 <= (size_t)TC_SMEM_LIMIT ||
@@ -1396,6 +1399,11 @@ int tc_launch(const TcProblem& p, cudaStream_t stream) {
   // stages of cps channel blocks each (fewer, larger stages amortise the per-stage waits and
   // commits of the two issuing threads): the largest cps with >= 3 stages, else cps = 1 with >= 2
   bool planned = false;
+  // four epilogue groups for thin tiles, and for the per-thread epilogue (ConvT scatter and other
+  // general cases) up to 128 columns; two when the staging of four would crowd out the A stages
+  const bool eg4 = !p.kxn && 4 * BN <= 512 && (BN <= 64 || (!fast && !kxn_fast));
+  for (int eg = eg4 ? 4 : 2; eg >= 2 && !planned; eg -= 2) {
+  a.egroups = eg;
   for (int res = 1; res >= 0 && !planned; res--) {
     for (int pass = 0; pass < 2 && !planned; pass++) {
       for (int cps = pass == 0 ? a.kb_per_tap : 1; cps >= 1 && !planned; cps--) {
@@ -1417,6 +1425,7 @@ int tc_launch(const TcProblem& p, cudaStream_t stream) {
       }
     }
   }
+  }
   if (!planned) return set_error(SDX_ERR_NOT_SUPPORTED, "tc: shared memory plan too large");
   const size_t smem = smem_bytes(a);
   if (smem > (size_t)TC_SMEM_LIMIT) return set_error(SDX_ERR_NOT_SUPPORTED, "tc: shared memory plan too large");
@@ -1427,12 +1436,16 @@ int tc_launch(const TcProblem& p, cudaStream_t stream) {
   cudaGetDevice(&dev);
   const int grid = std::min(total, num_sms(dev));
   int rc = SDX_OK;
-  if (fast) {
-    SDX_ACT_DISPATCH(a.act, ACTC, rc = (launch_tc<ACTC, 1>(dev, grid, smem, stream, mA, mB, mOut, mRes, a)));
-  } else if (kxn_fast) {
-    SDX_ACT_DISPATCH(a.act, ACTC, rc = (launch_tc<ACTC, 2>(dev, grid, smem, stream, mA, mB, mOut, mRes, a)));
+  if (fast && a.egroups == 4) {
+    SDX_ACT_DISPATCH(a.act, ACTC, rc = (launch_tc<ACTC, 1, 4>(dev, grid, smem, stream, mA, mB, mOut, mRes, a)));
+  } else if (fast) {
+    SDX_ACT_DISPATCH(a.act, ACTC, rc = (launch_tc<ACTC, 1, 2>(dev, grid, smem, stream, mA, mB, mOut, mRes, a)));
+  } else if (kxn_fast && a.egroups == 2) {
+    SDX_ACT_DISPATCH(a.act, ACTC, rc = (launch_tc<ACTC, 2, 2>(dev, grid, smem, stream, mA, mB, mOut, mRes, a)));
+  } else if (a.egroups == 4) {
+    SDX_ACT_DISPATCH(a.act, ACTC, rc = (launch_tc<ACTC, 0, 4>(dev, grid, smem, stream, mA, mB, mOut, mRes, a)));
   } else {
-    SDX_ACT_DISPATCH(a.act, ACTC, rc = (launch_tc<ACTC, 0>(dev, grid, smem, stream, mA, mB, mOut, mRes, a)));
+    SDX_ACT_DISPATCH(a.act, ACTC, rc = (launch_tc<ACTC, 0, 2>(dev, grid, smem, stream, mA, mB, mOut, mRes, a)));
   }
   if (rc) return rc;
   count_launch();
