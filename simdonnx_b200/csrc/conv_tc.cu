@@ -976,6 +976,20 @@ __global__ void __launch_bounds__(tc_threads(G), 1)
       }
       const int nch = a.BN / 16;
       int g = 0, cg = 0;
+      if (EPI == 1 && nch <= 2) {
+        // thin tiles: both chunks' TMEM loads in flight under one wait, the accumulator handed
+        // back before any arithmetic
+        float v0[16], v1[16];
+        tmem_ld16_issue(tbase, v0);
+        if (nch == 2) tmem_ld16_issue(tbase + 16u, v1);
+        tmem_wait_ld();
+        tmem_ld_wait16(v0);
+        if (nch == 2) tmem_ld_wait16(v1);
+        tc_fence_before();
+        mbar_arrive(smem_u32(&acce[acc]));
+        epi_chunk_fast<ACT>(a, v0, 0, srow, xr, sBias + tcd.n0);
+        if (nch == 2) epi_chunk_fast<ACT>(a, v1, 1, srow, xr, sBias + tcd.n0);
+      } else {
       // 16-column chunks through two register buffers: the load of chunk c+1 is in flight while
       // chunk c is processed; the accumulator goes back to the MMA warp after its last load
       float va[16], vb[16];
@@ -1003,6 +1017,7 @@ __global__ void __launch_bounds__(tc_threads(G), 1)
           if (EPI == 1) epi_chunk_fast<ACT>(a, vb, c + 1, srow, xr, sBias + tcd.n0);
           else epi_chunk<ACT>(a, vb, c + 1, srow, xr, sBias, tcd, valid, pix, g, cg);
         }
+      }
       }
       if (a.tma_out) {
         // make this warp's generic-proxy staging writes visible to the TMA engine, store its rows
