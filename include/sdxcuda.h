@@ -253,6 +253,18 @@ typedef struct sdx_image_desc {
 } sdx_image_desc;
 int sdx_image_to_tensor(sdx_ctx* ctx, const sdx_image_desc* d, sdx_stream s);
 
+/* The image-session preprocessing fused into the first conv of the graph: the conv `conv` reads the
+ * tensor that `image` describes (conv.ih/iw = image.oh/ow, 3 channels; conv.x and image.y are not
+ * used), so the fp32 tensor is never materialised. No reference counterpart (VkImageSession runs
+ * img2nhwc.comp as its own pass); results equal sdx_image_to_tensor followed by sdx_conv2d.
+ * SDX_ERR_NOT_SUPPORTED when the conv is not a shape the fused kernel handles (today the 3 -> 16,
+ * 3x3 stride-2 stem with fp16 NHWC output); the caller then runs the two calls. */
+typedef struct sdx_image_conv_desc {
+  sdx_image_desc image;
+  sdx_conv_desc conv;
+} sdx_image_conv_desc;
+int sdx_image_conv(sdx_ctx* ctx, const sdx_image_conv_desc* d, sdx_stream s);
+
 /* Channel concat of nearest-upsampled inputs: y[n, oy, ox, off_i + c] = x_i[n, oy / s_i, ox / s_i, c]
  * (a Concat whose inputs are ResizeNearest outputs, Nhwc.ResizeNearest src/Kernels/Nhwc.Det.cs:160-200,
  * fused with Nhwc.ConcatInner). Input i is [batch, oh / s_i, ow / s_i, counts[i]] fp16 NHWC; s_i = 1
@@ -290,7 +302,7 @@ enum sdx_op_kind {
   SDX_OP_CONV = 1, SDX_OP_GEMM = 2, SDX_OP_CONVT = 3, SDX_OP_POOL = 4, SDX_OP_CHANNEL_GATE = 5,
   SDX_OP_CHANNEL_BROADCAST = 6, SDX_OP_RESIZE_NEAREST = 7, SDX_OP_CONCAT = 8, SDX_OP_BINARY = 9, SDX_OP_ACT = 10,
   SDX_OP_CONVERT = 11, SDX_OP_LAYERNORM = 12, SDX_OP_SOFTMAX = 13, SDX_OP_ATTENTION = 14,
-  SDX_OP_CONCAT_NEAREST = 15, SDX_OP_IMAGE = 16
+  SDX_OP_CONCAT_NEAREST = 15, SDX_OP_IMAGE = 16, SDX_OP_IMAGE_CONV = 17
 };
 /* Generic argument block for the ops without a descriptor struct. */
 typedef struct sdx_misc_desc {

@@ -24,6 +24,7 @@ OP_CONV, OP_GEMM, OP_CONVT, OP_POOL, OP_CHANNEL_GATE, OP_CHANNEL_BROADCAST, OP_R
 OP_CONCAT, OP_BINARY, OP_ACT, OP_CONVERT, OP_LAYERNORM, OP_SOFTMAX, OP_ATTENTION = 8, 9, 10, 11, 12, 13, 14
 OP_CONCAT_NEAREST = 15
 OP_IMAGE = 16
+OP_IMAGE_CONV = 17
 
 FAULT_MALLOC, FAULT_LAUNCH, FAULT_GRAPH, FAULT_D2H, FAULT_SYNC = 1, 2, 3, 4, 5
 
@@ -78,11 +79,15 @@ class ImageDesc(ctypes.Structure):
         ("stride", _i64), ("image_bytes", _i64), ("src", _u64), ("lut", _u64), ("y", _u64)]
 
 
+class ImageConvDesc(ctypes.Structure):
+    _fields_ = [("image", ImageDesc), ("conv", ConvDesc)]
+
+
 DESC_OF_OP = {OP_CONV: ConvDesc, OP_GEMM: GemmDesc, OP_CONVT: ConvtDesc, OP_POOL: PoolDesc,
               OP_CHANNEL_GATE: GateDesc, OP_RESIZE_NEAREST: ResizeDesc, OP_CHANNEL_BROADCAST: MiscDesc,
               OP_CONCAT: MiscDesc, OP_BINARY: MiscDesc, OP_ACT: MiscDesc, OP_CONVERT: MiscDesc,
               OP_LAYERNORM: MiscDesc, OP_SOFTMAX: MiscDesc, OP_ATTENTION: MiscDesc, OP_CONCAT_NEAREST: MiscDesc,
-              OP_IMAGE: ImageDesc}
+              OP_IMAGE: ImageDesc, OP_IMAGE_CONV: ImageConvDesc}
 
 _SIGS = {
     "sdx_abi_version": (_i, []),
@@ -132,6 +137,7 @@ _SIGS = {
     "sdx_resize_nearest": (_i, [_p, ctypes.POINTER(ResizeDesc), _p]),
     "sdx_concat_channels": (_i, [_p, _i64, _i, ctypes.POINTER(_i), ctypes.POINTER(_u64), _u64, _p]),
     "sdx_image_to_tensor": (_i, [_p, ctypes.POINTER(ImageDesc), _p]),
+    "sdx_image_conv": (_i, [_p, ctypes.POINTER(ImageConvDesc), _p]),
     "sdx_concat_nearest": (_i, [_p, _i, _i, _i, _i, ctypes.POINTER(_i), ctypes.POINTER(_i), ctypes.POINTER(_u64), _u64,
                                 _p]),
     "sdx_binary": (_i, [_p, _i64, _i, _i, _u64, _u64, _u64, _p]),

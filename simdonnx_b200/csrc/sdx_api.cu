@@ -800,6 +800,55 @@ int sdx_image_to_tensor(sdx_ctx* ctx, const sdx_image_desc* d, sdx_stream s) {
   return image_launch(a, S(ctx, s));
 }
 
+int sdx_image_conv(sdx_ctx* ctx, const sdx_image_conv_desc* dd, sdx_stream s) {
+  USE(ctx);
+  if (!dd) return set_error(SDX_ERR_INVALID, "null desc");
+  LAUNCH_GUARD();
+  const sdx_image_desc* d = &dd->image;
+  const sdx_conv_desc* c = &dd->conv;
+  ImageArgs im;
+  im.batch = d->batch; im.ih = d->ih; im.iw = d->iw; im.bpp = d->bpp; im.swap = d->swap_rb;
+  im.oh = d->oh; im.ow = d->ow; im.pt = d->pad_t; im.pl = d->pad_l; im.y_nhwc_f16 = 0;
+  im.stride = d->stride > 0 ? d->stride : (int64_t)d->iw * d->bpp;
+  im.img_bytes = d->image_bytes > 0 ? d->image_bytes : im.stride * d->ih;
+  im.src = P<const uint8_t>(d->src);
+  im.lut = P<const float>(d->lut);
+  im.y = nullptr;
+  if (im.bpp != 3 && im.bpp != 4) return set_error(SDX_ERR_INVALID, "image conv: 3 or 4 bytes per pixel");
+  if (im.ih <= 0 || im.iw <= 0 || im.batch <= 0) return set_error(SDX_ERR_INVALID, "image conv: empty image");
+  if (im.stride < (int64_t)im.iw * im.bpp || im.img_bytes < im.stride * im.ih)
+    return set_error(SDX_ERR_INVALID, "image conv: stride");
+  if (!im.src || !im.lut) return set_error(SDX_ERR_INVALID, "image conv: null pointer");
+  if (c->batch != d->batch || c->ih != d->oh || c->iw != d->ow || c->ic != 3 || c->group != 1)
+    return set_error(SDX_ERR_INVALID, "image conv: the conv must read the image tensor (batch, 3 x oh x ow)");
+  const int oh = (c->ih + c->pad_t + c->pad_b - c->kh) / c->sh + 1, ow = (c->iw + c->pad_l + c->pad_r - c->kw) / c->sw + 1;
+  if (oh != c->oh || ow != c->ow) return set_error(SDX_ERR_INVALID, "image conv: output %dx%d, expected %dx%d", c->oh, c->ow, oh, ow);
+  DirectArgs a;
+  memset(&a, 0, sizeof(a));
+  a.batch = c->batch; a.ih = c->ih; a.iw = c->iw; a.ic = c->ic; a.oh = c->oh; a.ow = c->ow; a.oc = c->oc;
+  a.kh = c->kh; a.kw = c->kw; a.sh = c->sh; a.sw = c->sw; a.pt = c->pad_t; a.pl = c->pad_l; a.act = c->act;
+  a.x = nullptr;
+  a.x_f32 = 1;
+  a.x_nchw = 1;
+  a.w = P<const float>(c->w);
+  a.bias = P<const float>(c->bias);
+  a.add = P<const void>(c->add);
+  a.y = P<void>(c->y);
+  a.y_f32 = c->y_dtype == SDX_F32;
+  a.y_nchw = c->y_layout == SDX_NCHW;
+  a.y_pix_stride = c->y_pix_stride > 0 ? c->y_pix_stride : c->oc;
+  a.y_ch_off = c->y_ch_off;
+  a.err = ctx->err_word;
+  if (!a.w || !a.y) return set_error(SDX_ERR_INVALID, "image conv: null pointer");
+  if (c->pool || c->pad_mode != 0) return set_error(SDX_ERR_NOT_SUPPORTED, "image conv: pooled or non-zero-padded conv");
+  if (!stem_image_launch(im, a, S(ctx, s)))
+    return set_error(SDX_ERR_NOT_SUPPORTED, "image conv: no fused kernel for this conv (run image_to_tensor + conv2d)");
+  const cudaError_t e = cudaGetLastError();
+  if (e != cudaSuccess) return set_cuda_error(e, "stem_image launch");
+  count_launch();
+  return SDX_OK;
+}
+
 int sdx_concat_nearest(sdx_ctx* ctx, int batch, int oh, int ow, int nin, const int* counts, const int* scales,
                        const sdx_dptr* ins, sdx_dptr y, sdx_stream s) {
   USE(ctx);

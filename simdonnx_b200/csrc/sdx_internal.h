@@ -155,6 +155,9 @@ struct ImageArgs {
   void* y;
 };
 int image_launch(const ImageArgs& a, cudaStream_t st);
+// image normalisation fused into the det stem conv (tiled_kernels.cu); false when the conv is not
+// that shape (the caller then runs the two nodes separately)
+bool stem_image_launch(const ImageArgs& im, const DirectArgs& a, cudaStream_t st);
 
 struct ConcatNearestArgs {
   int batch, oh, ow, nin, ctot;

@@ -983,6 +983,63 @@ constexpr int STEM_TH = 16, STEM_TW = 64, STEM_R = 4;
 constexpr int STEM_IH = (STEM_TH - 1) * 2 + 3;           // 33 input rows
 constexpr int STEM_IW = ((STEM_TW - 1) * 2 + 3 + 3 + 3) / 4 * 4;  // 132 columns (3 of alignment)
 
+// One 16 x 64 stem output tile from the planar fp32 input tile in shared memory ([3][33][132], the
+// window of output column 0 starting at column 3): thread = 4 horizontally adjacent outputs x 16
+// channels of output row oy0 + ly, columns ox0 + lx .. ox0 + lx + 3.
+template <int ACT>
+__device__ __forceinline__ void stem_tile_compute(const DirectArgs& a, const float* tile, const float* sw, const float* sb,
+                                                  int n, int oy0, int ly, int ox0, int lx) {
+  constexpr int IC = 3, OC = 16, K = 3;
+  const int oy = oy0 + ly;
+  if (oy < a.oh) {
+    float acc[STEM_R][OC];
+#pragma unroll
+    for (int r = 0; r < STEM_R; r++)
+#pragma unroll
+      for (int o = 0; o < OC; o++) acc[r][o] = sb[o];
+#pragma unroll
+    for (int c = 0; c < IC; c++) {
+#pragma unroll
+      for (int ky = 0; ky < K; ky++) {
+        // window columns 2*lx .. 2*lx + 8 of this input row (+3: the alignment offset)
+        const float* row = tile + (c * STEM_IH + ly * 2 + ky) * STEM_IW + lx * 2 + 3;
+        float xv[(STEM_R - 1) * 2 + K];
+#pragma unroll
+        for (int j = 0; j < (STEM_R - 1) * 2 + K; j++) xv[j] = row[j];
+#pragma unroll
+        for (int kx = 0; kx < K; kx++) {
+          const float4* wp = reinterpret_cast<const float4*>(sw + ((ky * K + kx) * IC + c) * OC);
+          float wv[OC];
+#pragma unroll
+          for (int q = 0; q < OC / 4; q++) {
+            const float4 w4 = wp[q];
+            wv[4 * q] = w4.x; wv[4 * q + 1] = w4.y; wv[4 * q + 2] = w4.z; wv[4 * q + 3] = w4.w;
+          }
+#pragma unroll
+          for (int r = 0; r < STEM_R; r++)
+#pragma unroll
+            for (int o = 0; o < OC; o++) acc[r][o] = fmaf(xv[r * 2 + kx], wv[o], acc[r][o]);
+        }
+      }
+    }
+#pragma unroll
+    for (int r = 0; r < STEM_R; r++) {
+      const int ox = ox0 + lx + r;
+      if (ox >= a.ow) break;
+      __half* yp = static_cast<__half*>(a.y) + (((int64_t)n * a.oh + oy) * a.ow + ox) * a.y_pix_stride + a.y_ch_off;
+#pragma unroll
+      for (int h8 = 0; h8 < OC / 8; h8++) {
+        uint4 u;
+        __half2* h = reinterpret_cast<__half2*>(&u);
+#pragma unroll
+        for (int q = 0; q < 4; q++)
+          h[q] = __floats2half2_rn(act_t<ACT>(acc[r][h8 * 8 + 2 * q]), act_t<ACT>(acc[r][h8 * 8 + 2 * q + 1]));
+        reinterpret_cast<uint4*>(yp)[h8] = u;
+      }
+    }
+  }
+}
+
 template <int ACT>
 __global__ void __launch_bounds__(256) stem_tma_kernel(const __grid_constant__ CUtensorMap tmX, DirectArgs a,
                                                        int tiles_x, int tiles_per_img, int total) {
@@ -1045,54 +1102,7 @@ __global__ void __launch_bounds__(256) stem_tma_kernel(const __grid_constant__ C
     const bool ok = mbar_wait(smem_u32(&full[b]), (uint32_t)(i >> 1) & 1u, a.err, SDX_DEV_WAIT_FULL, &abort_flag);
     if (__syncthreads_or(!ok)) break;
     const float* tile = bufs + b * (kBufBytes / 4);
-    const int oy = oy0 + ly;
-    if (oy < a.oh) {
-      float acc[STEM_R][OC];
-#pragma unroll
-      for (int r = 0; r < STEM_R; r++)
-#pragma unroll
-        for (int o = 0; o < OC; o++) acc[r][o] = sb[o];
-#pragma unroll
-      for (int c = 0; c < IC; c++) {
-#pragma unroll
-        for (int ky = 0; ky < K; ky++) {
-          // window columns 2*lx .. 2*lx + 8 of this input row (+3: the alignment offset)
-          const float* row = tile + (c * STEM_IH + ly * 2 + ky) * STEM_IW + lx * 2 + 3;
-          float xv[(STEM_R - 1) * 2 + K];
-#pragma unroll
-          for (int j = 0; j < (STEM_R - 1) * 2 + K; j++) xv[j] = row[j];
-#pragma unroll
-          for (int kx = 0; kx < K; kx++) {
-            const float4* wp = reinterpret_cast<const float4*>(sw + ((ky * K + kx) * IC + c) * OC);
-            float wv[OC];
-#pragma unroll
-            for (int q = 0; q < OC / 4; q++) {
-              const float4 w4 = wp[q];
-              wv[4 * q] = w4.x; wv[4 * q + 1] = w4.y; wv[4 * q + 2] = w4.z; wv[4 * q + 3] = w4.w;
-            }
-#pragma unroll
-            for (int r = 0; r < STEM_R; r++)
-#pragma unroll
-              for (int o = 0; o < OC; o++) acc[r][o] = fmaf(xv[r * 2 + kx], wv[o], acc[r][o]);
-          }
-        }
-      }
-#pragma unroll
-      for (int r = 0; r < STEM_R; r++) {
-        const int ox = ox0 + lx + r;
-        if (ox >= a.ow) break;
-        __half* yp = static_cast<__half*>(a.y) + (((int64_t)n * a.oh + oy) * a.ow + ox) * a.y_pix_stride + a.y_ch_off;
-#pragma unroll
-        for (int h8 = 0; h8 < OC / 8; h8++) {
-          uint4 u;
-          __half2* h = reinterpret_cast<__half2*>(&u);
-#pragma unroll
-          for (int q = 0; q < 4; q++)
-            h[q] = __floats2half2_rn(act_t<ACT>(acc[r][h8 * 8 + 2 * q]), act_t<ACT>(acc[r][h8 * 8 + 2 * q + 1]));
-          reinterpret_cast<uint4*>(yp)[h8] = u;
-        }
-      }
-    }
+    stem_tile_compute<ACT>(a, tile, sw, sb, n, oy0, ly, ox0, lx);
     __syncthreads();
   }
   if (tid < 32) {
@@ -1130,6 +1140,85 @@ static bool stem_tma_launch_t(const DirectArgs& a, cudaStream_t st) {
   const int grid = (int)std::min<int64_t>(total, (int64_t)num_sms(dev) * std::max(1, per_sm));
   stem_tma_kernel<ACT><<<grid, 256, smem, st>>>(map, a, tiles_x, tiles_x * tiles_y, (int)total);
   return true;
+}
+
+// ---- the det stem fed straight from u8 images (image session): the ImageToTensor normalisation
+// (lut, optional R/B swap, replicate placement of the image inside the tensor) runs while the tile
+// is filled, so the fp32 NCHW tensor is never written or read. One CTA per 16 x 64 output tile;
+// the fill reads 3 bytes per input pixel (plain loads: rows of 3-byte pixels do not meet TMA's
+// 16-byte rules) and writes the same planar fp32 tile as the TMA-fed stem, whose compute follows.
+template <int ACT>
+__global__ void __launch_bounds__(256) stem_image_kernel(ImageArgs im, DirectArgs a, int tiles_x, int tiles_per_img) {
+  constexpr int IC = 3, OC = 16, K = 3;
+  constexpr int NCOL = (STEM_TW - 1) * 2 + K;  // 129 input columns of a tile
+  extern __shared__ float fsm[];
+  float* tile = fsm;                              // [IC][STEM_IH][STEM_IW]
+  float* sw = tile + IC * STEM_IH * STEM_IW;      // [K*K][IC][OC]
+  float* sb = sw + K * K * IC * OC;               // [OC]
+  float* lut = sb + OC;                           // [3][256]
+  const int tid = threadIdx.x;
+  const int t = blockIdx.x;
+  const int n = t / tiles_per_img;
+  const int q = t - n * tiles_per_img;
+  const int ty = q / tiles_x;
+  const int oy0 = ty * STEM_TH, ox0 = (q - ty * tiles_x) * STEM_TW;
+  for (int i = tid; i < K * K * IC * OC; i += blockDim.x) sw[i] = __ldg(a.w + i);
+  for (int i = tid; i < OC; i += blockDim.x) sb[i] = a.bias ? __ldg(a.bias + i) : 0.0f;
+  for (int i = tid; i < 3 * 256; i += blockDim.x) lut[i] = __ldg(im.lut + i);
+  __syncthreads();
+  // tensor row y = oy0*2 - pt + r, column x = ox0*2 - pl + col (conv zero padding outside the
+  // tensor); the tensor pixel is image pixel (clamp(y - image top), clamp(x - image left))
+  const uint8_t* img = im.src + (int64_t)n * im.img_bytes;
+  const int ob = im.swap ? 2 : 0;
+  for (int i = tid; i < STEM_IH * NCOL; i += blockDim.x) {
+    const int r = i / NCOL, col = i - r * NCOL;
+    const int y = oy0 * 2 - a.pt + r, x = ox0 * 2 - a.pl + col;
+    float v0 = 0.0f, v1 = 0.0f, v2 = 0.0f;
+    if ((unsigned)y < (unsigned)a.ih && (unsigned)x < (unsigned)a.iw) {
+      const int sy = min(max(y - im.pt, 0), im.ih - 1), sx = min(max(x - im.pl, 0), im.iw - 1);
+      const uint8_t* px = img + (int64_t)sy * im.stride + (int64_t)sx * im.bpp;
+      v0 = lut[px[ob]];
+      v1 = lut[256 + px[1]];
+      v2 = lut[512 + px[2 - ob]];
+    }
+    float* d = tile + r * STEM_IW + col + 3;
+    d[0] = v0;
+    d[STEM_IH * STEM_IW] = v1;
+    d[2 * STEM_IH * STEM_IW] = v2;
+  }
+  __syncthreads();
+  const int ly = tid / (STEM_TW / STEM_R), lx = (tid - ly * (STEM_TW / STEM_R)) * STEM_R;
+  stem_tile_compute<ACT>(a, tile, sw, sb, n, oy0, ly, ox0, lx);
+}
+
+template <int ACT>
+static void stem_image_launch_t(const ImageArgs& im, const DirectArgs& a, cudaStream_t st) {
+  const size_t smem = sizeof(float) * ((size_t)3 * STEM_IH * STEM_IW + 9 * 3 * 16 + 16 + 3 * 256);
+  static bool attr = false;
+  if (!attr) {
+    cudaFuncSetAttribute(stem_image_kernel<ACT>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+    attr = true;
+  }
+  const int tiles_x = (a.ow + STEM_TW - 1) / STEM_TW, tiles_y = (a.oh + STEM_TH - 1) / STEM_TH;
+  stem_image_kernel<ACT><<<a.batch * tiles_x * tiles_y, 256, smem, st>>>(im, a, tiles_x, tiles_x * tiles_y);
+}
+
+bool stem_image_launch(const ImageArgs& im, const DirectArgs& a, cudaStream_t st) {
+  // the det stem shape on an image-session input: 3 -> 16 channels, 3x3 stride 2, fp16 NHWC out
+  if (!(a.ic == 3 && a.oc == 16 && a.kh == 3 && a.kw == 3 && a.sh == 2 && a.sw == 2 && !a.add && !a.y_f32 &&
+        !a.y_nchw && a.y_pix_stride % 8 == 0 && a.y_ch_off % 8 == 0 &&
+        (reinterpret_cast<uintptr_t>(a.y) & 15u) == 0))
+    return false;
+  if (im.bpp != 3 && im.bpp != 4) return false;
+  if (a.ih != im.oh || a.iw != im.ow) return false;  // the conv reads the image session's tensor
+  const int64_t tiles = (int64_t)a.batch * ((a.ow + STEM_TW - 1) / STEM_TW) * ((a.oh + STEM_TH - 1) / STEM_TH);
+  if (tiles <= 0 || tiles > INT32_MAX) return false;
+  switch (a.act) {
+    case ACT_HARDSWISH: stem_image_launch_t<ACT_HARDSWISH>(im, a, st); return true;
+    case ACT_RELU: stem_image_launch_t<ACT_RELU>(im, a, st); return true;
+    case ACT_NONE: stem_image_launch_t<ACT_NONE>(im, a, st); return true;
+    default: return false;
+  }
 }
 
 bool stem_tiled_launch(const DirectArgs& a, cudaStream_t st) {

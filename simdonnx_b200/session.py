@@ -6,7 +6,8 @@ The reference's Vulkan backend is the template (VkGraphModel, src/Backends/Vulka
     conversion where a tensor-core conv reads a graph input; the squeeze-excitation product x*s
     folded into the load of the depthwise convs that consume it; a channel Concat of
     nearest-upsampled tensors becomes one ConcatNearest node that writes whole output pixels;
-    producers of any other channel Concat write straight into their slice of its output;
+    producers of any other channel Concat write straight into their slice of its output; the image
+    session's u8 -> fp32 normalisation is fused into the stem conv that reads it (ImageConv);
   * one device arena (int64 byte offsets, plan.plan_arena) + a per-model const store of packed
     weights; every node becomes one sdx_* descriptor over device pointers arena + offset;
   * the node list is validated once eagerly and captured into one CUDA graph.
@@ -146,6 +147,27 @@ def cuda_rewrite(plan: ExecPlan) -> ExecPlan:
                 continue
         keep.append(n)
     P.nodes = keep
+
+    # 5. image-session normalisation + the stem conv that alone reads its fp32 tensor -> ImageConv
+    #    (the tensor is never written); the shape is the fused kernel's (sdx_image_conv)
+    out_nodes = []
+    drop = set()
+    prods = {o: m for m in P.nodes for o in m.outs}
+    for n in P.nodes:
+        if n.op == "Conv" and not n.p.add and n.p.pool is None and n.p.group == 1:
+            m = prods.get(n.ins[0])
+            xv, yv = P.values[n.ins[0]], P.values[n.outs[0]]
+            if (m is not None and m.op == "ImageToTensor" and len(P.consumers(n.ins[0])) == 1 and
+                    xv.layout == "nchw" and xv.dtype == "f32" and n.ins[0] not in P.inputs and
+                    n.p.kernel == (3, 3) and n.p.strides == (2, 2) and xv.shape[1] == 3 and
+                    P.values[n.ins[1]].const.shape[0] == 16 and yv.dtype == "f16" and yv.layout == "nhwc" and
+                    not yv.alias and P.values[m.ins[0]].shape[3] in (3, 4)):
+                drop.add(id(m))
+                out_nodes.append(Node("ImageConv", [m.ins[0]] + list(n.ins[1:]), list(n.outs),
+                                      (m.p, n.p, xv.shape[2], xv.shape[3]), n.name))
+                continue
+        out_nodes.append(n)
+    P.nodes = [n for n in out_nodes if id(n) not in drop]
     return P
 
 
@@ -302,6 +324,25 @@ class CudaInferenceSession:
             d.stride, d.image_bytes = iw * bpp, ih * iw * bpp
             d.src, d.lut, d.y = self.ptr(n.ins[0]), self._f32(p.lut), self.ptr(n.outs[0])
             return N.OP_IMAGE, d
+        if op == "ImageConv":
+            ip, cp, th, tw = p
+            img = P.values[n.ins[0]]
+            nb, ih, iw, bpp = img.shape
+            W = P.values[n.ins[1]].const
+            d = N.ImageConvDesc()
+            im = d.image
+            im.batch, im.ih, im.iw, im.bpp, im.swap_rb = nb, ih, iw, bpp, int(ip.swap_rb)
+            im.oh, im.ow, im.y_nhwc_f16 = th, tw, 0
+            im.pad_t, im.pad_l = ip.pads
+            im.stride, im.image_bytes = iw * bpp, ih * iw * bpp
+            im.src, im.lut, im.y = self.ptr(n.ins[0]), self._f32(ip.lut), 0
+            cd = B.conv_desc(nb, th, tw, 3, W.shape[0], cp.kernel[0], cp.kernel[1], stride=cp.strides, pads=cp.pads,
+                             act=cp.act, x_dtype=torch.float32, x_layout=N.NCHW)
+            wt = self._const_dev(("convw", n.name), lambda: B.pack_conv(cd, W, self.device))
+            cd.x, cd.w, cd.y = 0, B.ptr(wt), self.ptr(n.outs[0])
+            cd.bias = self._f32(cp.bias) if cp.bias else 0
+            d.conv = cd
+            return N.OP_IMAGE_CONV, d
         if op == "ConcatNearest":
             nb, oh, ow, _ = P.shape(n.outs[0])
             d = N.MiscDesc()

@@ -331,3 +331,48 @@ def test_bounded_wait_reports_and_recovers(be):
     be.clear_device_error()
     test_resize_add_and_concat(be)
     assert be.device_error() == 0
+
+
+# ------------------------------------------------------------------------------------------- image session
+def _image_tensor_ref(img, lut, oh, ow, pads, swap):
+    """ImageToTensor as the oracle runner computes it (replicate padding, lut, optional R/B swap)."""
+    ih, iw = img.shape[1], img.shape[2]
+    sy = np.clip(np.arange(oh) - pads[0], 0, ih - 1)
+    sx = np.clip(np.arange(ow) - pads[1], 0, iw - 1)
+    px = img[:, sy][:, :, sx]
+    order = (2, 1, 0) if swap else (0, 1, 2)
+    return np.stack([lut[c][px[..., order[c]]] for c in range(3)], axis=1).astype(np.float32)
+
+
+@pytest.mark.parametrize("bpp,swap,ih,iw,oh,ow,pads", [(3, False, 64, 96, 64, 96, (0, 0)),
+                                                       (4, True, 30, 41, 37, 53, (3, 5)),
+                                                       (3, True, 70, 33, 70, 33, (0, 0))])
+def test_image_conv_fused_stem(be, bpp, swap, ih, iw, oh, ow, pads):
+    """u8 images -> lut -> the 3->16 3x3 s2 stem in one kernel == image_to_tensor then the conv."""
+    import ctypes
+    from simdonnx_b200 import backend as B, _native as N
+    rng = np.random.default_rng(ih * iw + bpp)
+    nb = 2
+    img = rng.integers(0, 256, size=(nb, ih, iw, bpp), dtype=np.uint8)
+    lut = rng.uniform(-2, 2, size=(3, 256)).astype(np.float32)
+    wt = rnd(rng, 16, 3, 3, 3, scale=0.3)
+    b = rnd(rng, 16)
+    x = _image_tensor_ref(img, lut, oh, ow, pads, swap)          # NCHW fp32
+    ref = O.conv(np.ascontiguousarray(x.transpose(0, 2, 3, 1)), O.ConvPlan(wt, b), strides=(2, 2), pads=(1, 1, 1, 1),
+                 act="hardswish")
+    cd = B.conv_desc(nb, oh, ow, 3, 16, 3, 3, stride=(2, 2), pads=(1, 1, 1, 1), act="hardswish",
+                     x_dtype=torch.float32, x_layout=N.NCHW)
+    wp = B.pack_conv(cd, wt)
+    y = torch.empty((nb, cd.oh, cd.ow, 16), dtype=torch.float16, device="cuda")
+    src, lut_d, bias_d = torch.from_numpy(img).cuda(), dev32(lut), dev32(b)
+    d = N.ImageConvDesc()
+    im = d.image
+    im.batch, im.ih, im.iw, im.bpp, im.swap_rb = nb, ih, iw, bpp, int(swap)
+    im.oh, im.ow, im.pad_t, im.pad_l, im.y_nhwc_f16 = oh, ow, pads[0], pads[1], 0
+    im.stride, im.image_bytes = iw * bpp, ih * iw * bpp
+    im.src, im.lut, im.y = B.ptr(src), B.ptr(lut_d), 0
+    cd.x, cd.w, cd.bias, cd.y = 0, B.ptr(wp), B.ptr(bias_d), B.ptr(y)
+    d.conv = cd
+    N.call("sdx_image_conv", be.ctx, ctypes.byref(d), B.cur_stream())
+    assert_close(host(y), ref, "image conv")
+    assert be.device_error() == 0
