@@ -177,6 +177,19 @@ typedef struct sdx_convt_desc {
 } sdx_convt_desc;
 int sdx_convt(sdx_ctx* ctx, const sdx_convt_desc* d, sdx_stream s);
 
+/* Two chained ConvTranspose nodes, the second reading only the first's output (the det head's
+ * ConvT 2x2 -> ConvT 2x2): `first` as in sdx_convt (oc 8, 16 or 24, 2x2, packed by sdx_pack_convt; its y
+ * is not written), then a 2x2 stride-2 ConvT to one channel with raw fp32 weights w2
+ * [first.oc][1][2][2], bias2 [1] and act2, written to y [batch, 4 * ih, 4 * iw, 1] (y_dtype).
+ * No reference counterpart (ConvTranspose nodes run one by one there); equals sdx_convt twice with
+ * the intermediate kept in fp32. SDX_ERR_NOT_SUPPORTED for other shapes. */
+typedef struct sdx_convt_chain_desc {
+  sdx_convt_desc first;
+  int oc2, kh2, kw2, act2, y_dtype;
+  sdx_dptr w2, bias2, y;
+} sdx_convt_chain_desc;
+int sdx_convt_chain(sdx_ctx* ctx, const sdx_convt_chain_desc* d, sdx_stream s);
+
 /* Max / average pool (PoolP, src/Engine/ExecPlan.cs:67-74; Nhwc.MaxPool src/Kernels/Nhwc.cs:730-770,
  * Nhwc.AvgPool src/Kernels/Ops.Seq.cs:180-225). fp16 NHWC. */
 typedef struct sdx_pool_desc {
@@ -302,7 +315,7 @@ enum sdx_op_kind {
   SDX_OP_CONV = 1, SDX_OP_GEMM = 2, SDX_OP_CONVT = 3, SDX_OP_POOL = 4, SDX_OP_CHANNEL_GATE = 5,
   SDX_OP_CHANNEL_BROADCAST = 6, SDX_OP_RESIZE_NEAREST = 7, SDX_OP_CONCAT = 8, SDX_OP_BINARY = 9, SDX_OP_ACT = 10,
   SDX_OP_CONVERT = 11, SDX_OP_LAYERNORM = 12, SDX_OP_SOFTMAX = 13, SDX_OP_ATTENTION = 14,
-  SDX_OP_CONCAT_NEAREST = 15, SDX_OP_IMAGE = 16, SDX_OP_IMAGE_CONV = 17
+  SDX_OP_CONCAT_NEAREST = 15, SDX_OP_IMAGE = 16, SDX_OP_IMAGE_CONV = 17, SDX_OP_CONVT_CHAIN = 18
 };
 /* Generic argument block for the ops without a descriptor struct. */
 typedef struct sdx_misc_desc {

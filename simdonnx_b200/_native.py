@@ -25,6 +25,7 @@ OP_CONCAT, OP_BINARY, OP_ACT, OP_CONVERT, OP_LAYERNORM, OP_SOFTMAX, OP_ATTENTION
 OP_CONCAT_NEAREST = 15
 OP_IMAGE = 16
 OP_IMAGE_CONV = 17
+OP_CONVT_CHAIN = 18
 
 FAULT_MALLOC, FAULT_LAUNCH, FAULT_GRAPH, FAULT_D2H, FAULT_SYNC = 1, 2, 3, 4, 5
 
@@ -79,6 +80,11 @@ class ImageDesc(ctypes.Structure):
         ("stride", _i64), ("image_bytes", _i64), ("src", _u64), ("lut", _u64), ("y", _u64)]
 
 
+class ConvtChainDesc(ctypes.Structure):
+    _fields_ = [("first", ConvtDesc)] + [(n, _i) for n in ("oc2", "kh2", "kw2", "act2", "y_dtype")] + [
+        (n, _u64) for n in ("w2", "bias2", "y")]
+
+
 class ImageConvDesc(ctypes.Structure):
     _fields_ = [("image", ImageDesc), ("conv", ConvDesc)]
 
@@ -87,7 +93,7 @@ DESC_OF_OP = {OP_CONV: ConvDesc, OP_GEMM: GemmDesc, OP_CONVT: ConvtDesc, OP_POOL
               OP_CHANNEL_GATE: GateDesc, OP_RESIZE_NEAREST: ResizeDesc, OP_CHANNEL_BROADCAST: MiscDesc,
               OP_CONCAT: MiscDesc, OP_BINARY: MiscDesc, OP_ACT: MiscDesc, OP_CONVERT: MiscDesc,
               OP_LAYERNORM: MiscDesc, OP_SOFTMAX: MiscDesc, OP_ATTENTION: MiscDesc, OP_CONCAT_NEAREST: MiscDesc,
-              OP_IMAGE: ImageDesc, OP_IMAGE_CONV: ImageConvDesc}
+              OP_IMAGE: ImageDesc, OP_IMAGE_CONV: ImageConvDesc, OP_CONVT_CHAIN: ConvtChainDesc}
 
 _SIGS = {
     "sdx_abi_version": (_i, []),
@@ -138,6 +144,7 @@ _SIGS = {
     "sdx_concat_channels": (_i, [_p, _i64, _i, ctypes.POINTER(_i), ctypes.POINTER(_u64), _u64, _p]),
     "sdx_image_to_tensor": (_i, [_p, ctypes.POINTER(ImageDesc), _p]),
     "sdx_image_conv": (_i, [_p, ctypes.POINTER(ImageConvDesc), _p]),
+    "sdx_convt_chain": (_i, [_p, ctypes.POINTER(ConvtChainDesc), _p]),
     "sdx_concat_nearest": (_i, [_p, _i, _i, _i, _i, ctypes.POINTER(_i), ctypes.POINTER(_i), ctypes.POINTER(_u64), _u64,
                                 _p]),
     "sdx_binary": (_i, [_p, _i64, _i, _i, _u64, _u64, _u64, _p]),

@@ -118,6 +118,11 @@ struct TcArgs {
   uint32_t slab_tx;     // bytes one residual box (one group, one warp's 32 rows) delivers
   int bias_smem;        // bias floats staged in shared memory (per accumulator column), 0 = none
   int log2G;            // log2 of G (fast epilogue: G is 16, 32 or 64)
+  // ConvT chain epilogue (EPI = 4): the second ConvT's weights follow the bias in smem
+  int chain_act2, chain_y_f32;
+  void* chain_y;
+  const float* chain_w2;
+  const float* chain_b2;
   unsigned int* err;
 };
 
@@ -508,6 +513,62 @@ __device__ __forceinline__ void epi_chunk_fast(const TcArgs& a, float (&v)[16], 
   sts16(ad1, u1);
 }
 
+// ConvT chain epilogue for one accumulator row = input pixel (y, x): the 4 x OC1 columns (tap1, c)
+// of the first 2x2 ConvT come out of TMEM under one wait; each channel c (+ bias, activation) of
+// each tap1 feeds the second 2x2 ConvT (one output channel), so the row yields the 4 x 4 output
+// block at (4y, 4x): 16 independent FMA chains over c, stored as four 16-byte rows (fp32) or 8-byte
+// rows (fp16). smem: sBias[c] = first bias, then the second ConvT's raw weights [c][tap2] and bias.
+template <int ACT, int OC1>  // OC1 in {8, 16, 24}: 4 x OC1 columns = whole 16-column TMEM loads
+__device__ __forceinline__ void chain_row(const TcArgs& a, uint32_t tbase, const float* sBias, uint64_t* acce_bar,
+                                          int img, int y, int x, bool ok) {
+  float v[4 * OC1];
+#pragma unroll
+  for (int j = 0; j < 4 * OC1 / 16; j++) tmem_ld16_issue(tbase + (uint32_t)(16 * j), v + 16 * j);
+  tmem_wait_ld();
+#pragma unroll
+  for (int j = 0; j < 4 * OC1 / 16; j++) tmem_ld_wait16(v + 16 * j);
+  tc_fence_before();
+  mbar_arrive(smem_u32(acce_bar));
+  const float4* w2 = reinterpret_cast<const float4*>(sBias + a.BN);
+  const float b2 = sBias[a.BN + 4 * OC1];
+  float blk[16];
+#pragma unroll
+  for (int i = 0; i < 16; i++) blk[i] = b2;
+#pragma unroll
+  for (int c = 0; c < OC1; c++) {
+    const float4 w = w2[c];
+    const float bb = sBias[c];
+#pragma unroll
+    for (int t1 = 0; t1 < 4; t1++) {
+      const float h = act_t<ACT>(v[t1 * OC1 + c] + bb);
+      const int r0 = 2 * (t1 >> 1), c0 = 2 * (t1 & 1);
+      blk[r0 * 4 + c0] = fmaf(h, w.x, blk[r0 * 4 + c0]);
+      blk[r0 * 4 + c0 + 1] = fmaf(h, w.y, blk[r0 * 4 + c0 + 1]);
+      blk[(r0 + 1) * 4 + c0] = fmaf(h, w.z, blk[(r0 + 1) * 4 + c0]);
+      blk[(r0 + 1) * 4 + c0 + 1] = fmaf(h, w.w, blk[(r0 + 1) * 4 + c0 + 1]);
+    }
+  }
+  if (!ok) return;
+#pragma unroll
+  for (int i = 0; i < 16; i++) blk[i] = act_apply(blk[i], a.chain_act2);
+  const int64_t W4 = (int64_t)a.OW * 4;
+  const int64_t base = ((int64_t)img * a.OH * 4 + (int64_t)y * 4) * W4 + (int64_t)x * 4;
+#pragma unroll
+  for (int r = 0; r < 4; r++) {
+    if (a.chain_y_f32) {
+      *reinterpret_cast<float4*>(static_cast<float*>(a.chain_y) + base + r * W4) =
+          make_float4(blk[4 * r], blk[4 * r + 1], blk[4 * r + 2], blk[4 * r + 3]);
+    } else {
+      __half2 h0 = __floats2half2_rn(blk[4 * r], blk[4 * r + 1]);
+      __half2 h1 = __floats2half2_rn(blk[4 * r + 2], blk[4 * r + 3]);
+      uint2 u;
+      u.x = *reinterpret_cast<uint32_t*>(&h0);
+      u.y = *reinterpret_cast<uint32_t*>(&h1);
+      *reinterpret_cast<uint2*>(static_cast<__half*>(a.chain_y) + base + r * W4) = u;
+    }
+  }
+}
+
 template <int ACT, int EPI, int G>
 __global__ void __launch_bounds__(tc_threads(G), 1)
     conv_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
@@ -564,8 +625,14 @@ __global__ void __launch_bounds__(tc_threads(G), 1)
     tmem_relinquish();
   }
   // per-column bias in shared memory (ConvT: expanded over its taps), read as broadcasts
-  for (int i = threadIdx.x; i < a.bias_smem; i += blockDim.x)
+  for (int i = threadIdx.x; i < (EPI == 4 ? a.BN : a.bias_smem); i += blockDim.x)
     sBias[i] = (a.bias && i < a.N) ? __ldg(a.bias + (a.convt_oc > 0 ? i % a.convt_oc : i)) : 0.0f;
+  if (EPI == 4) {
+    // second ConvT: raw weights [c][tap2] (float4 per channel), then its bias
+    const int oc1 = a.convt_oc;
+    for (int i = threadIdx.x; i <= 4 * oc1; i += blockDim.x)
+      sBias[a.BN + i] = i < 4 * oc1 ? __ldg(a.chain_w2 + i) : __ldg(a.chain_b2);
+  }
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
@@ -852,6 +919,15 @@ __global__ void __launch_bounds__(tc_threads(G), 1)
       const uint32_t slab = stage0 + sbi * a.sbuf_bytes;
       const uint32_t srow = slab + (uint32_t)lane * P;
       const uint32_t tbase = tmem_base + ((uint32_t)(q * 32) << 16) + acc * (uint32_t)a.acc_stride;
+      if (EPI == 4) {
+        const int y = tcd.oy0 + row_in_tile / a.BW, x = tcd.ox0 + row_in_tile % a.BW;
+        const bool ok_px = y < a.OH && x < a.OW;
+        if (a.convt_oc == 24) chain_row<ACT, 24>(a, tbase, sBias, acce + acc, tcd.img, y, x, ok_px);
+        else if (a.convt_oc == 16) chain_row<ACT, 16>(a, tbase, sBias, acce + acc, tcd.img, y, x, ok_px);
+        else chain_row<ACT, 8>(a, tbase, sBias, acce + acc, tcd.img, y, x, ok_px);
+        __syncwarp();
+        continue;
+      }
       if (EPI == 2) {
         // kx-in-N, straight-line form (fp16 out, 16-byte rows, no residual, bias or zeros in smem):
         // per 16 output channels, the three taps' columns are loaded with one wait, combined across
@@ -1221,6 +1297,18 @@ int tc_launch(const TcProblem& p, cudaStream_t stream) {
   a.convt_oc = p.convt_oc;
   a.convt_H = p.convt_H;
   a.convt_W = p.convt_W;
+  const bool chain = p.chain_w2 != nullptr;
+  if (chain) {
+    if (!convt || p.mode != TC_CONV || p.convt_kh != 2 || p.convt_kw != 2 ||
+        (p.convt_oc != 8 && p.convt_oc != 16 && p.convt_oc != 24) || BN != 4 * p.convt_oc ||
+        n_tiles != 1 || !p.chain_b2 || !p.chain_y)
+      return set_error(SDX_ERR_NOT_SUPPORTED, "tc convt chain: first ConvT must be 2x2 with 8, 16 or 24 outputs");
+    a.chain_w2 = p.chain_w2;
+    a.chain_b2 = p.chain_b2;
+    a.chain_act2 = p.chain_act2;
+    a.chain_y = p.chain_y;
+    a.chain_y_f32 = p.chain_y_f32;
+  }
   a.esz = p.out_f32 ? 4 : 2;
   bool vec = (p.out_pix_stride % 8 == 0) && (p.out_ch_off % 8 == 0) && aligned16(p.out) && (p.N % 8 == 0);
   if (convt) vec = vec && p.convt_oc % 8 == 0;
@@ -1332,7 +1420,7 @@ int tc_launch(const TcProblem& p, cudaStream_t stream) {
   // 16-column epilogue chunks must not straddle groups
   bool tma_out = G > 0 && G % 16 == 0 && aligned16(p.out) && (p.out_pix_stride * esz) % 16 == 0 &&
                  (p.out_ch_off * esz) % 16 == 0;
-  if (convt) tma_out = tma_out && p.mode == TC_CONV;
+  if (convt) tma_out = tma_out && p.mode == TC_CONV && !chain;
   if (p.kxn) tma_out = false;  // the kx-in-N epilogue stores per thread
   if (tma_out) {
     const int P = G * esz;
@@ -1389,7 +1477,7 @@ int tc_launch(const TcProblem& p, cudaStream_t stream) {
       a.slab_tx = (uint32_t)(P * 32);
     }
     a.tma_out = 1;
-  } else if (convt && p.mode == TC_CONV) {
+  } else if (convt && p.mode == TC_CONV && !chain) {
     return set_error(SDX_ERR_NOT_SUPPORTED, "tc convt: channel geometry has no TMA store layout");
   }
 
@@ -1416,7 +1504,8 @@ int tc_launch(const TcProblem& p, cudaStream_t stream) {
   bool planned = false;
   // four epilogue groups for thin tiles, and for the per-thread epilogue (ConvT scatter and other
   // general cases) up to 128 columns; two when the staging of four would crowd out the A stages
-  const bool eg4 = !p.kxn && 4 * BN <= 512 && (BN <= 64 || (!fast && !kxn_fast));
+  if (chain) a.bias_smem = BN + 4 * p.convt_oc + 4;  // first bias, second ConvT's weights and bias
+  const bool eg4 = !p.kxn && !chain && 4 * BN <= 512 && (BN <= 64 || (!fast && !kxn_fast));
   for (int eg = eg4 ? 4 : 2; eg >= 2 && !planned; eg -= 2) {
   a.egroups = eg;
   for (int res = 1; res >= 0 && !planned; res--) {
@@ -1451,7 +1540,9 @@ int tc_launch(const TcProblem& p, cudaStream_t stream) {
   cudaGetDevice(&dev);
   const int grid = std::min(total, num_sms(dev));
   int rc = SDX_OK;
-  if (fast && a.egroups == 4) {
+  if (chain) {
+    SDX_ACT_DISPATCH(a.act, ACTC, rc = (launch_tc<ACTC, 4, 2>(dev, grid, smem, stream, mA, mB, mOut, mRes, a)));
+  } else if (fast && a.egroups == 4) {
     SDX_ACT_DISPATCH(a.act, ACTC, rc = (launch_tc<ACTC, 1, 4>(dev, grid, smem, stream, mA, mB, mOut, mRes, a)));
   } else if (fast) {
     SDX_ACT_DISPATCH(a.act, ACTC, rc = (launch_tc<ACTC, 1, 2>(dev, grid, smem, stream, mA, mB, mOut, mRes, a)));

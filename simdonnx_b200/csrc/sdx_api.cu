@@ -688,6 +688,53 @@ int sdx_convt(sdx_ctx* ctx, const sdx_convt_desc* d, sdx_stream s) {
   return convt_dot_launch(a, S(ctx, s));
 }
 
+int sdx_convt_chain(sdx_ctx* ctx, const sdx_convt_chain_desc* dd, sdx_stream s) {
+  USE(ctx);
+  if (!dd) return set_error(SDX_ERR_INVALID, "null desc");
+  LAUNCH_GUARD();
+  const sdx_convt_desc* d = &dd->first;
+  if ((d->oc != 8 && d->oc != 16 && d->oc != 24) || d->kh != 2 || d->kw != 2 || dd->oc2 != 1 || dd->kh2 != 2 ||
+      dd->kw2 != 2)
+    return set_error(SDX_ERR_NOT_SUPPORTED, "convt chain: 2x2 ConvT (8, 16 or 24 outputs) then 2x2 ConvT to one channel");
+  if (d->ic % 8 != 0) return set_error(SDX_ERR_NOT_SUPPORTED, "convt chain: ic must be a multiple of 8");
+  if (!dd->w2 || !dd->bias2 || !dd->y || !d->x || !d->w) return set_error(SDX_ERR_INVALID, "convt chain: null pointer");
+  TcProblem p;
+  memset(&p, 0, sizeof(p));
+  p.mode = TC_CONV;
+  p.a = P<const __half>(d->x);
+  p.lda = d->ic;
+  p.M = d->batch * d->ih * d->iw;
+  p.K = d->ic;
+  p.batch = d->batch;
+  p.H = d->ih;
+  p.W = d->iw;
+  p.C = d->ic;
+  p.OH = d->ih;
+  p.OW = d->iw;
+  p.kh = 1;
+  p.kw = 1;
+  p.w = P<const __half>(d->w);
+  p.wterms = 2;
+  p.N = d->kh * d->kw * d->oc;
+  p.bias = P<const float>(d->bias);
+  p.out = nullptr;
+  p.out_f32 = 0;
+  p.out_pix_stride = d->oc;
+  p.act = d->act;
+  p.convt_kh = d->kh;
+  p.convt_kw = d->kw;
+  p.convt_oc = d->oc;
+  p.convt_H = d->ih;
+  p.convt_W = d->iw;
+  p.chain_w2 = P<const float>(dd->w2);
+  p.chain_b2 = P<const float>(dd->bias2);
+  p.chain_act2 = dd->act2;
+  p.chain_y = P<void>(dd->y);
+  p.chain_y_f32 = dd->y_dtype == SDX_F32;
+  p.err = ctx->err_word;
+  return tc_launch(p, S(ctx, s));
+}
+
 int sdx_pool(sdx_ctx* ctx, const sdx_pool_desc* d, sdx_stream s) {
   USE(ctx);
   if (!d) return set_error(SDX_ERR_INVALID, "null desc");

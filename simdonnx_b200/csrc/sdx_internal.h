@@ -59,6 +59,13 @@ struct TcProblem {
   int act;
   int convt_kh, convt_kw, convt_oc, convt_H, convt_W;
   int kxn;  // 3x3 conv with its column taps as GEMM columns (tc_conv_kxn)
+  // ConvT chain: a second 2x2 stride-2 ConvT with one output channel applied in the epilogue to the
+  // first one's (activated, fp32) output, which is never stored; `out` is unused then
+  const float* chain_w2;  // raw fp32 [convt_oc][1][2][2]
+  const float* chain_b2;  // [1]
+  int chain_act2;
+  void* chain_y;          // [batch, 4 * convt_H, 4 * convt_W, 1]
+  int chain_y_f32;
   unsigned int* err;
 };
 void tc_plan_n(int N, int* BN, int* n_tiles);

@@ -96,6 +96,7 @@ static size_t desc_size(int kind) {
     case SDX_OP_CONCAT_NEAREST: return sizeof(sdx_misc_desc);
     case SDX_OP_IMAGE: return sizeof(sdx_image_desc);
     case SDX_OP_IMAGE_CONV: return sizeof(sdx_image_conv_desc);
+    case SDX_OP_CONVT_CHAIN: return sizeof(sdx_convt_chain_desc);
     default: return 0;
   }
 }
@@ -116,6 +117,7 @@ static int run_node(sdx_session* s, const sdx_session::Node& n) {
     case SDX_OP_CONCAT: return sdx_concat_channels(c, m->pixels, m->nin, m->counts, m->ins, m->y, st);
     case SDX_OP_IMAGE: return sdx_image_to_tensor(c, static_cast<const sdx_image_desc*>(d), st);
     case SDX_OP_IMAGE_CONV: return sdx_image_conv(c, static_cast<const sdx_image_conv_desc*>(d), st);
+    case SDX_OP_CONVT_CHAIN: return sdx_convt_chain(c, static_cast<const sdx_convt_chain_desc*>(d), st);
     case SDX_OP_CONCAT_NEAREST:
       return sdx_concat_nearest(c, m->batch, (int)m->rows, (int)m->n, m->nin, m->counts, m->aux, m->ins, m->y, st);
     case SDX_OP_BINARY: return sdx_binary(c, m->n, m->op, m->relu, m->a, m->b, m->y, st);

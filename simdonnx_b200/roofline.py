@@ -66,6 +66,20 @@ def node_cost(plan: ExecPlan, n) -> tuple:
         flops = 2 * nb * ih * iw * ic * oc * kh * kw
         byt = _nb(plan, n.ins[0]) + W.size * (2 if oc >= 8 else 4) + 4 * oc + _nb(plan, out)
         return cls, flops, byt
+    if op == "ConvTChain":
+        # two ConvTs with the intermediate kept on chip: traffic = input, weights, final output
+        nb, ih, iw, ic = plan.values[n.ins[0]].shape
+        W1, W2 = plan.values[n.ins[1]].const, plan.values[n.ins[2]].const
+        _, oc1, kh, kw = W1.shape
+        flops = 2 * nb * ih * iw * ic * oc1 * kh * kw + 2 * nb * ih * kh * iw * kw * oc1 * W2[0].size
+        byt = _nb(plan, n.ins[0]) + W1.size * 2 + W2.size * 4 + 4 * oc1 + _nb(plan, out)
+        return "convt_chain", flops, byt
+    if op == "ImageConv":
+        # u8 image normalisation fused into the stem conv: traffic = image bytes, weights, output
+        W = plan.values[n.ins[1]].const
+        nb, oh, ow, oc = plan.values[out].shape
+        flops = 2 * nb * oh * ow * oc * W.shape[1] * W.shape[2] * W.shape[3]
+        return "stem_image", flops, _nb(plan, n.ins[0]) + W.size * 4 + _nb(plan, out)
     if op == "Gemm":
         a = n.ins[0]
         Wb = plan.values[n.ins[1]].const

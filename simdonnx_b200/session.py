@@ -148,7 +148,29 @@ def cuda_rewrite(plan: ExecPlan) -> ExecPlan:
         keep.append(n)
     P.nodes = keep
 
-    # 5. image-session normalisation + the stem conv that alone reads its fp32 tensor -> ImageConv
+    # 5. ConvTranspose 2x2 (8, 16 or 24 outputs) whose output only a 2x2 ConvTranspose to one channel reads
+    #    -> one ConvTChain node (the intermediate stays in registers, fp32)
+    out_nodes = []
+    drop = set()
+    prods = {o: m for m in P.nodes for o in m.outs}
+    for n in P.nodes:
+        if n.op == "ConvTranspose":
+            m = prods.get(n.ins[0])
+            if m is not None and m.op == "ConvTranspose" and len(P.consumers(n.ins[0])) == 1 and n.ins[0] != P.output:
+                W1, W2 = P.values[m.ins[1]].const, P.values[n.ins[1]].const
+                ic1, oc1, kh1, kw1 = W1.shape
+                ic2, oc2, kh2, kw2 = W2.shape
+                xv = P.values[m.ins[0]]
+                if (oc1 in (8, 16, 24) and (kh1, kw1) == (2, 2) and (kh2, kw2) == (2, 2) and oc2 == 1 and ic2 == oc1 and
+                        ic1 % 8 == 0 and xv.dtype == "f16" and len(xv.shape) == 4):
+                    drop.add(id(m))
+                    out_nodes.append(Node("ConvTChain", [m.ins[0], m.ins[1], n.ins[1]], list(n.outs), (m.p, n.p),
+                                          n.name))
+                    continue
+        out_nodes.append(n)
+    P.nodes = [n for n in out_nodes if id(n) not in drop]
+
+    # 6. image-session normalisation + the stem conv that alone reads its fp32 tensor -> ImageConv
     #    (the tensor is never written); the shape is the fused kernel's (sdx_image_conv)
     out_nodes = []
     drop = set()
@@ -324,6 +346,26 @@ class CudaInferenceSession:
             d.stride, d.image_bytes = iw * bpp, ih * iw * bpp
             d.src, d.lut, d.y = self.ptr(n.ins[0]), self._f32(p.lut), self.ptr(n.outs[0])
             return N.OP_IMAGE, d
+        if op == "ConvTChain":
+            p1, p2 = p
+            xv, yv = P.values[n.ins[0]], P.values[n.outs[0]]
+            nb, ih, iw, ic = xv.shape
+            W1, W2 = P.values[n.ins[1]].const, P.values[n.ins[2]].const
+            _, oc1, kh, kw = W1.shape
+            d = N.ConvtChainDesc()
+            f = d.first
+            f.batch, f.ih, f.iw, f.ic, f.oc, f.kh, f.kw = nb, ih, iw, ic, oc1, kh, kw
+            f.act, f.y_dtype = N.ACT[p1.act], N.F16
+            w1 = self._const_dev(("convtw", n.name + ".1"), lambda: B.pack_convt(W1, self.device))
+            w2 = self._const_dev(("convtw", n.name + ".2"), lambda: torch.from_numpy(W2).to(self.device))
+            f.x, f.w, f.bias, f.y = self.ptr(n.ins[0]), B.ptr(w1), self._f32(p1.bias), 0
+            d.oc2, d.kh2, d.kw2, d.act2, d.y_dtype = 1, 2, 2, N.ACT[p2.act], _DT[yv.dtype]
+            d.w2 = B.ptr(w2)
+            d.bias2 = self._f32(p2.bias) if p2.bias else self._zeros(1)
+            d.y = self.ptr(n.outs[0])
+            if not p1.bias:
+                f.bias = self._zeros(kh * kw * oc1)
+            return N.OP_CONVT_CHAIN, d
         if op == "ImageConv":
             ip, cp, th, tw = p
             img = P.values[n.ins[0]]

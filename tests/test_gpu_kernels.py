@@ -376,3 +376,33 @@ def test_image_conv_fused_stem(be, bpp, swap, ih, iw, oh, ow, pads):
     N.call("sdx_image_conv", be.ctx, ctypes.byref(d), B.cur_stream())
     assert_close(host(y), ref, "image conv")
     assert be.device_error() == 0
+
+
+@pytest.mark.parametrize("ic,oc1,h,w,act1,f32", [(24, 24, 20, 30, "relu", True), (16, 8, 9, 17, "none", False),
+                                                 (32, 16, 13, 64, "relu", True)])
+def test_convt_chain(be, ic, oc1, h, w, act1, f32):
+    """ConvT 2x2 (ic -> oc1, act1) then ConvT 2x2 (oc1 -> 1, sigmoid) in one kernel == the two ConvTs
+    one after the other (the intermediate kept in fp32)."""
+    import ctypes
+    from simdonnx_b200 import backend as B, _native as N
+    rng = np.random.default_rng(ic * 7 + oc1)
+    nb = 2
+    x = rnd(rng, nb, h, w, ic)
+    w1 = rnd(rng, ic, oc1, 2, 2, scale=1 / np.sqrt(ic))
+    b1 = rnd(rng, oc1)
+    w2 = rnd(rng, oc1, 1, 2, 2, scale=1 / np.sqrt(oc1))
+    b2 = rnd(rng, 1)
+    ref = O.convt(O.convt(x, w1, b1, act=act1), w2, b2, act="sigmoid")
+    y = torch.empty((nb, 4 * h, 4 * w, 1), dtype=torch.float32 if f32 else torch.float16, device="cuda")
+    xd, w1p, b1d, w2d, b2d = dev16(x), B.pack_convt(w1), dev32(b1), dev32(w2), dev32(b2)
+    d = N.ConvtChainDesc()
+    f = d.first
+    f.batch, f.ih, f.iw, f.ic, f.oc, f.kh, f.kw = nb, h, w, ic, oc1, 2, 2
+    f.act, f.y_dtype = N.ACT[act1], N.F16
+    f.x, f.w, f.bias, f.y = B.ptr(xd), B.ptr(w1p), B.ptr(b1d), 0
+    d.oc2, d.kh2, d.kw2, d.act2 = 1, 2, 2, N.ACT["sigmoid"]
+    d.y_dtype = N.F32 if f32 else N.F16
+    d.w2, d.bias2, d.y = B.ptr(w2d), B.ptr(b2d), B.ptr(y)
+    N.call("sdx_convt_chain", be.ctx, ctypes.byref(d), B.cur_stream())
+    assert_close(host(y), ref, f"convt chain {ic}->{oc1}->1")
+    assert be.device_error() == 0
