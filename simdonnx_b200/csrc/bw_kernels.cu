@@ -459,7 +459,7 @@ __global__ void gap_partial_kernel(const __half* __restrict__ x, int hw, int c, 
 // over a second grid dimension (GATE_RJ hidden units / GATE_CJ output channels per CTA). Each
 // image's sums run in the same order whatever images share its CTA, so the gate of an image does
 // not depend on the batch it runs in. The hidden layer goes through scratch (after the partials).
-constexpr int GATE_IMG = 8, GATE_RJ = 32, GATE_CJ = 64;
+constexpr int GATE_IMG = 8, GATE_RJ = 8, GATE_CJ = 32;
 
 // Warp sum of v[0..GATE_IMG-1]; lane 0 holds the totals.
 __device__ __forceinline__ void warp_sum_img(float (&v)[GATE_IMG]) {

@@ -549,8 +549,14 @@ __device__ __forceinline__ void chain_row(const TcArgs& a, uint32_t tbase, const
     }
   }
   if (!ok) return;
+  if (a.chain_act2 == ACT_SIGMOID) {
+    // the det probability map: hardware exp and reciprocal (a few ulp) instead of the IEEE forms
 #pragma unroll
-  for (int i = 0; i < 16; i++) blk[i] = act_apply(blk[i], a.chain_act2);
+    for (int i = 0; i < 16; i++) blk[i] = __frcp_rn(1.0f + __expf(-blk[i]));
+  } else {
+#pragma unroll
+    for (int i = 0; i < 16; i++) blk[i] = act_apply(blk[i], a.chain_act2);
+  }
   const int64_t W4 = (int64_t)a.OW * 4;
   const int64_t base = ((int64_t)img * a.OH * 4 + (int64_t)y * 4) * W4 + (int64_t)x * 4;
 #pragma unroll
