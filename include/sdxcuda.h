@@ -153,6 +153,9 @@ typedef struct sdx_conv_desc {
   int w_terms;       /* tensor-core routes: fp16 weight terms, 1 (w) or 2 (hi + lo, ~22-bit weights);
                         0 = default: 2 for 1x1 kernels (their MMAs hide under HBM time), 1 for larger
                         kernels (MMA-bound; one fp16 term is the reference GPU backends' weight type) */
+  int add_up;        /* 0 or 1: the residual as given; 2: `add` is [batch, oh/2, ow/2, oc] fp16 NHWC, read
+                        nearest-upsampled (an FPN top-down ResizeNearest(x, add = this conv) fused into
+                        the conv: y = act(conv + up2(add))); tensor-core routes, oh and ow even */
 } sdx_conv_desc;
 int sdx_conv2d(sdx_ctx* ctx, const sdx_conv_desc* d, sdx_stream s);
 

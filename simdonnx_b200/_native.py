@@ -37,7 +37,8 @@ class ConvDesc(ctypes.Structure):
                                   "pad_l", "pad_b", "pad_r", "group", "act", "pool", "pool_relu", "x_dtype",
                                   "x_layout", "y_dtype", "add_dtype", "add_layout", "y_layout", "pad_mode")] + [
         ("pad_value", _f), ("y_pix_stride", _i64), ("y_ch_off", _i),
-        ("x", _u64), ("w", _u64), ("bias", _u64), ("add", _u64), ("y", _u64), ("in_scale", _u64), ("w_terms", _i)]
+        ("x", _u64), ("w", _u64), ("bias", _u64), ("add", _u64), ("y", _u64), ("in_scale", _u64), ("w_terms", _i),
+        ("add_up", _i)]
 
 
 class GemmDesc(ctypes.Structure):

@@ -98,6 +98,7 @@ struct TcArgs {
   int res_f32;
   int64_t res_pix_stride;
   int res_ch_off;
+  int res_up;           // 2: residual on the half-size grid, read nearest-upsampled (per thread)
   void* out;
   int out_f32;
   int64_t out_pix_stride;
@@ -168,6 +169,11 @@ __device__ __forceinline__ void bulk_wait_all(uint32_t p) {
   asm volatile("{\n\t.reg .pred q;\n\tsetp.ne.b32 q, %0, 0;\n\t@q cp.async.bulk.wait_group 0;\n\t}" ::"r"(p) : "memory");
 }
 __device__ __forceinline__ void fence_async_smem() { asm volatile("fence.proxy.async.shared::cta;" ::: "memory"); }
+__device__ __forceinline__ void cp_async16(uint32_t dst, const void* src) {
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(dst), "l"(src) : "memory");
+}
+__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
+__device__ __forceinline__ void cp_async_wait_all() { asm volatile("cp.async.wait_group 0;" ::: "memory"); }
 // ------------------------------------------------------------------ per-thread fallback helpers
 __device__ __forceinline__ void load8_res(const TcArgs& a, int64_t off, float* r) {
   if (a.res_f32) {
@@ -477,7 +483,7 @@ __device__ __forceinline__ void epi_chunk(const TcArgs& a, float (&v)[16], int c
 // is straight-line, so the sixteen columns interleave; `sb` is the tile's bias (sBias + n0).
 template <int ACT>
 __device__ __forceinline__ void epi_chunk_fast(const TcArgs& a, float (&v)[16], int c, uint32_t srow, uint32_t xr,
-                                               const float* sb) {
+                                               const float* sb, bool res_smem) {
   const int col = c * 16;
   const uint32_t row = srow + (uint32_t)(col >> a.log2G) * a.group_bytes;
   const uint32_t k0 = ((uint32_t)(col & (a.G - 1)) * 2u) >> 4;
@@ -488,7 +494,7 @@ __device__ __forceinline__ void epi_chunk_fast(const TcArgs& a, float (&v)[16], 
     const float4 b = bp[i];
     v[4 * i] += b.x; v[4 * i + 1] += b.y; v[4 * i + 2] += b.z; v[4 * i + 3] += b.w;
   }
-  if (a.tma_res) {
+  if (res_smem) {
     uint4 u0, u1;
     lds16(ad0, u0);
     lds16(ad1, u1);
@@ -892,6 +898,44 @@ __global__ void __launch_bounds__(tc_threads(G), 1)
       const uint32_t lt = G * lc + (uint32_t)e;
       const uint32_t acc = lt & (uint32_t)(a.nacc - 1), ar = lt >> (a.nacc == 4 ? 2 : 1);
       const uint32_t sbi = a.nsbuf == 2 ? (lc & 1u) : 0u;
+      TileCoord tcd;
+      coords(tile, tcd);
+      const uint32_t slab = stage0 + sbi * a.sbuf_bytes;
+      const uint32_t srow = slab + (uint32_t)lane * P;
+      // fast epilogue, residual without a TMA map (e.g. the nearest-upsampled FPN tensor): each
+      // thread copies its row's residual into its staging row (cp.async, the staging swizzle) before
+      // waiting for the accumulator, so the loads overlap the wait; the chunks read it from smem
+      bool res_smem = a.tma_res != 0;
+      if (EPI == 1 && a.res && !a.tma_res) {
+        int64_t rpix = -1;
+        if (a.mode == TC_CONV) {
+          const int oy = tcd.oy0 + row_in_tile / a.BW, ox = tcd.ox0 + row_in_tile % a.BW;
+          if (oy < a.OH && ox < a.OW)
+            rpix = a.res_up ? ((int64_t)tcd.img * (a.OH >> 1) + (oy >> 1)) * (a.OW >> 1) + (ox >> 1)
+                            : ((int64_t)tcd.img * a.OH + oy) * a.OW + ox;
+        } else {
+          const int64_t pix = (int64_t)tcd.m0 + row_in_tile;
+          if (pix < a.M) {
+            if (a.res_up) {
+              const int64_t hw = (int64_t)a.OH * a.OW, img = pix / hw, rem = pix - img * hw;
+              const int y = (int)(rem / a.OW), x = (int)(rem - (int64_t)y * a.OW);
+              rpix = (img * (a.OH >> 1) + (y >> 1)) * (a.OW >> 1) + (x >> 1);
+            } else {
+              rpix = pix;
+            }
+          }
+        }
+        if (rpix >= 0) {
+          const __half* src = static_cast<const __half*>(a.res) + (rpix * a.res_pix_stride + a.res_ch_off + tcd.n0);
+          const int units = min(a.BN, a.N - tcd.n0) >> 3;  // 16-byte units inside the tensor
+          for (int u = 0; u < units; u++) {
+            const uint32_t g = (uint32_t)(u >> (a.log2G - 3)), k = (uint32_t)(u & ((a.G >> 3) - 1));
+            cp_async16(srow + g * a.group_bytes + ((k ^ xr) << 4), src + u * 8);
+          }
+        }
+        cp_async_commit();
+        res_smem = true;
+      }
       bool ok = mbar_wait_warp(smem_u32(&accf[acc]), ar & 1u, a.err, SDX_DEV_WAIT_ACC_FULL, abort_flag);
       if (ok && a.tma_res) {
         ok = mbar_wait_warp(smem_u32(&resb[(e * 2 + sbi) * 4 + q]), (res_phase >> sbi) & 1u, a.err, SDX_DEV_WAIT_FULL,
@@ -901,12 +945,11 @@ __global__ void __launch_bounds__(tc_threads(G), 1)
           res_pending = false;
         }
       }
+      if (EPI == 1 && a.res && !a.tma_res) cp_async_wait_all();
       if (!ok) break;
       __syncwarp();
       tc_fence_after();
 
-      TileCoord tcd;
-      coords(tile, tcd);
       // output pixel of this row: only the per-thread paths (no TMA store, or a residual that TMA
       // cannot stage) need it
       bool valid = false;
@@ -922,8 +965,6 @@ __global__ void __launch_bounds__(tc_threads(G), 1)
           valid = pix < a.M;
         }
       }
-      const uint32_t slab = stage0 + sbi * a.sbuf_bytes;
-      const uint32_t srow = slab + (uint32_t)lane * P;
       const uint32_t tbase = tmem_base + ((uint32_t)(q * 32) << 16) + acc * (uint32_t)a.acc_stride;
       if (EPI == 4) {
         const int y = tcd.oy0 + row_in_tile / a.BW, x = tcd.ox0 + row_in_tile % a.BW;
@@ -1069,8 +1110,8 @@ __global__ void __launch_bounds__(tc_threads(G), 1)
         if (nch == 2) tmem_ld_wait16(v1);
         tc_fence_before();
         mbar_arrive(smem_u32(&acce[acc]));
-        epi_chunk_fast<ACT>(a, v0, 0, srow, xr, sBias + tcd.n0);
-        if (nch == 2) epi_chunk_fast<ACT>(a, v1, 1, srow, xr, sBias + tcd.n0);
+        epi_chunk_fast<ACT>(a, v0, 0, srow, xr, sBias + tcd.n0, res_smem);
+        if (nch == 2) epi_chunk_fast<ACT>(a, v1, 1, srow, xr, sBias + tcd.n0, res_smem);
       } else {
       // 16-column chunks through two register buffers: the load of chunk c+1 is in flight while
       // chunk c is processed; the accumulator goes back to the MMA warp after its last load
@@ -1085,7 +1126,7 @@ __global__ void __launch_bounds__(tc_threads(G), 1)
           tc_fence_before();
           mbar_arrive(smem_u32(&acce[acc]));
         }
-        if (EPI == 1) epi_chunk_fast<ACT>(a, va, c, srow, xr, sBias + tcd.n0);
+        if (EPI == 1) epi_chunk_fast<ACT>(a, va, c, srow, xr, sBias + tcd.n0, res_smem);
         else epi_chunk<ACT>(a, va, c, srow, xr, sBias, tcd, valid, pix, g, cg);
         if (c + 1 < nch) {
           tmem_wait_ld();
@@ -1096,7 +1137,7 @@ __global__ void __launch_bounds__(tc_threads(G), 1)
             tc_fence_before();
             mbar_arrive(smem_u32(&acce[acc]));
           }
-          if (EPI == 1) epi_chunk_fast<ACT>(a, vb, c + 1, srow, xr, sBias + tcd.n0);
+          if (EPI == 1) epi_chunk_fast<ACT>(a, vb, c + 1, srow, xr, sBias + tcd.n0, res_smem);
           else epi_chunk<ACT>(a, vb, c + 1, srow, xr, sBias, tcd, valid, pix, g, cg);
         }
       }
@@ -1292,6 +1333,7 @@ int tc_launch(const TcProblem& p, cudaStream_t stream) {
   a.res_f32 = p.res_f32;
   a.res_pix_stride = p.res_pix_stride;
   a.res_ch_off = p.res_ch_off;
+  a.res_up = p.res_up;
   a.out = p.out;
   a.out_f32 = p.out_f32;
   a.out_pix_stride = p.out_pix_stride;
@@ -1392,6 +1434,8 @@ int tc_launch(const TcProblem& p, cudaStream_t stream) {
   } else {
     if (p.lda % 8 != 0) return set_error(SDX_ERR_INVALID, "tc rows: A row stride must be a multiple of 8 halves");
     a.M = p.M;
+    a.OH = p.OH;  // pixel grid of the rows (upsampled residual)
+    a.OW = p.OW;
     a.m_tiles = (p.M + TC_BM - 1) / TC_BM;
     a.a_box_bytes = (uint32_t)(TC_BM * kbytes);
     a.a_blk_bytes = (a.a_box_bytes + 1023u) & ~1023u;
@@ -1464,7 +1508,7 @@ int tc_launch(const TcProblem& p, cudaStream_t stream) {
     }
     if (rc) return rc;
     // residual by TMA when it has the output's type, layout and channel geometry
-    if (p.res && !convt && p.res_f32 == p.out_f32 && p.res_pix_stride == p.out_pix_stride &&
+    if (p.res && !convt && !p.res_up && p.res_f32 == p.out_f32 && p.res_pix_stride == p.out_pix_stride &&
         p.res_ch_off == p.out_ch_off && aligned16(p.res)) {
       if (p.mode == TC_CONV) {
         const uint64_t ps = (uint64_t)p.res_pix_stride;
@@ -1490,7 +1534,10 @@ int tc_launch(const TcProblem& p, cudaStream_t stream) {
   if (p.bias && BN * n_tiles <= TC_BIAS_SMEM_MAX) a.bias_smem = BN * n_tiles;
   // fast epilogue: fp16 out by TMA through 32/64/128-byte swizzled rows, bias in smem (zeros when
   // there is none), residual TMA-staged or absent
-  const bool fast = a.tma_out && a.esz == 2 && a.swz && !p.kxn && (!p.res || a.tma_res) &&
+  // residual read per thread in the fast epilogue: fp16, 16-byte aligned rows (N is a multiple of 8)
+  const bool res_thread = p.res && !p.res_f32 && !convt && aligned16(p.res) && p.res_pix_stride % 8 == 0 &&
+                          p.res_ch_off % 8 == 0 && p.N % 8 == 0;
+  const bool fast = a.tma_out && a.esz == 2 && a.swz && !p.kxn && (!p.res || a.tma_res || res_thread) &&
                     BN * n_tiles <= TC_BIAS_SMEM_MAX && (a.G == 16 || a.G == 32 || a.G == 64);
   if (fast) {
     a.bias_smem = BN * n_tiles;
@@ -1510,6 +1557,8 @@ int tc_launch(const TcProblem& p, cudaStream_t stream) {
   bool planned = false;
   // four epilogue groups for thin tiles, and for the per-thread epilogue (ConvT scatter and other
   // general cases) up to 128 columns; two when the staging of four would crowd out the A stages
+  if (p.res_up && !fast)
+    return set_error(SDX_ERR_NOT_SUPPORTED, "tc: upsampled residual needs the fp16 TMA-store epilogue");
   if (chain) a.bias_smem = BN + 4 * p.convt_oc + 4;  // first bias, second ConvT's weights and bias
   const bool eg4 = !p.kxn && !chain && 4 * BN <= 512 && (BN <= 64 || (!fast && !kxn_fast));
   for (int eg = eg4 ? 4 : 2; eg >= 2 && !planned; eg -= 2) {

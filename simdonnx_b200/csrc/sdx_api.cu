@@ -532,6 +532,8 @@ int sdx_conv2d(sdx_ctx* ctx, const sdx_conv_desc* d, sdx_stream s) {
   const int oh = (d->ih + d->pad_t + d->pad_b - d->kh) / d->sh + 1, ow = (d->iw + d->pad_l + d->pad_r - d->kw) / d->sw + 1;
   if (oh != d->oh || ow != d->ow) return set_error(SDX_ERR_INVALID, "conv: output %dx%d, expected %dx%d", d->oh, d->ow, oh, ow);
   const int route = conv_route(d);
+  if (d->add_up == 2 && route != R_TC_CONV && route != R_TC_ROWS)
+    return set_error(SDX_ERR_NOT_SUPPORTED, "conv: upsampled residual only on the tensor-core routes");
   const int64_t ystride = d->y_pix_stride > 0 ? d->y_pix_stride : d->oc;
   cudaStream_t st = S(ctx, s);
   switch (route) {
@@ -562,6 +564,13 @@ int sdx_conv2d(sdx_ctx* ctx, const sdx_conv_desc* d, sdx_stream s) {
       p.res = P<const void>(d->add);
       p.res_f32 = d->add_dtype == SDX_F32;
       p.res_pix_stride = d->oc;
+      if (d->add_up == 2) {
+        if (!d->add || d->add_dtype != SDX_F16 || (d->oh & 1) || (d->ow & 1) || d->pool)
+          return set_error(SDX_ERR_NOT_SUPPORTED, "conv: upsampled residual needs fp16 add, even oh/ow, no pool");
+        p.res_up = 2;
+      } else if (d->add_up != 0 && d->add_up != 1) {
+        return set_error(SDX_ERR_INVALID, "conv: add_up must be 0, 1 or 2");
+      }
       p.res_ch_off = 0;
       p.out = P<void>(d->y);
       p.out_f32 = d->y_dtype == SDX_F32;

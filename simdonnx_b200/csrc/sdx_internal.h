@@ -52,6 +52,7 @@ struct TcProblem {
   int res_f32;
   int64_t res_pix_stride;
   int res_ch_off;
+  int res_up;  // 2: the residual is the nearest 2x downsample grid [batch, OH/2, OW/2, N] (read upsampled)
   void* out;
   int out_f32;
   int64_t out_pix_stride;

@@ -148,7 +148,34 @@ def cuda_rewrite(plan: ExecPlan) -> ExecPlan:
         keep.append(n)
     P.nodes = keep
 
-    # 5. ConvTranspose 2x2 (8, 16 or 24 outputs) whose output only a 2x2 ConvTranspose to one channel reads
+    # 5. FPN top-down add: ResizeNearest(x, scale 2, add = a conv's output that nothing else reads) ->
+    #    the conv with x as a nearest-upsampled residual (sdx_conv_desc.add_up = 2), placed where the
+    #    resize was; the conv's activation must be none (the add comes before it); add_relu -> relu
+    prods = {o: m for m in P.nodes for o in m.outs}
+    fused = {}
+    for n in P.nodes:
+        if n.op == "ResizeNearest" and len(n.ins) == 2 and tuple(n.p.scales) == (2, 2):
+            x, a = n.ins
+            m = prods.get(a)
+            if m is None or m.op != "Conv" or len(P.consumers(a)) != 1 or a == P.output:
+                continue
+            xv, av = P.values[x], P.values[a]
+            if (m.p.add or m.p.pool is not None or m.p.act != "none" or m.p.group != 1 or av.alias or
+                    m.p.strides != (1, 1) or av.dtype != "f16" or xv.dtype != "f16" or av.layout != "nhwc" or
+                    P.values[m.ins[0]].dtype != "f16" or len(av.shape) != 4 or av.shape[1] % 2 or av.shape[2] % 2 or
+                    xv.shape != (av.shape[0], av.shape[1] // 2, av.shape[2] // 2, av.shape[3]) or
+                    P.values[n.outs[0]].alias or av.shape[3] % 8):
+                continue
+            c = Node("Conv", list(m.ins), list(n.outs), copy.copy(m.p), m.name)
+            c.p.add = x
+            c.p.add_up = 2
+            c.p.act = "relu" if n.p.add_relu else "none"
+            fused[id(n)] = c
+            fused[id(m)] = None
+    if fused:
+        P.nodes = [fused.get(id(n), n) for n in P.nodes if fused.get(id(n), n) is not None]
+
+    # 6. ConvTranspose 2x2 (8, 16 or 24 outputs) whose output only a 2x2 ConvTranspose to one channel reads
     #    -> one ConvTChain node (the intermediate stays in registers, fp32)
     out_nodes = []
     drop = set()
@@ -170,7 +197,7 @@ def cuda_rewrite(plan: ExecPlan) -> ExecPlan:
         out_nodes.append(n)
     P.nodes = [n for n in out_nodes if id(n) not in drop]
 
-    # 6. image-session normalisation + the stem conv that alone reads its fp32 tensor -> ImageConv
+    # 7. image-session normalisation + the stem conv that alone reads its fp32 tensor -> ImageConv
     #    (the tensor is never written); the shape is the fused kernel's (sdx_image_conv)
     out_nodes = []
     drop = set()
@@ -277,6 +304,7 @@ class CudaInferenceSession:
             d.w = B.ptr(wt)
             d.bias = self._f32(p.bias) if p.bias else (self._zeros(oc) if p.group > 1 else 0)
             d.add = self.ptr(p.add) if p.add else 0
+            d.add_up = getattr(p, "add_up", 0)
             d.y = self.ptr(n.outs[0])
             scale = getattr(p, "in_scale", None)
             d.in_scale = self.ptr(scale) if scale else 0

@@ -406,3 +406,22 @@ def test_convt_chain(be, ic, oc1, h, w, act1, f32):
     N.call("sdx_convt_chain", be.ctx, ctypes.byref(d), B.cur_stream())
     assert_close(host(y), ref, f"convt chain {ic}->{oc1}->1")
     assert be.device_error() == 0
+
+
+@pytest.mark.parametrize("ic,oc,k,h,w", [(64, 96, 1, 20, 24), (32, 64, 3, 16, 22), (256, 96, 1, 40, 40)])
+def test_conv_upsampled_residual(be, ic, oc, k, h, w):
+    """FPN top-down add fused into the lateral conv: y = conv(x) + nearest_up2(r), r on the half grid."""
+    from simdonnx_b200 import backend as B
+    rng = np.random.default_rng(ic + oc + k)
+    nb = 2
+    x = rnd(rng, nb, h, w, ic)
+    r = rnd(rng, nb, h // 2, w // 2, oc)
+    wt = rnd(rng, oc, ic, k, k, scale=1 / np.sqrt(ic * k * k))
+    b = rnd(rng, oc)
+    p = k // 2
+    ref = O.resize_nearest(r, (2, 2), add=O.conv(x, O.ConvPlan(wt, b), pads=(p, p, p, p)))
+    d = B.conv_desc(nb, h, w, ic, oc, k, k, pads=(p, p, p, p))
+    d.add_up = 2
+    y = B.conv2d(be, d, dev16(x), B.pack_conv(d, wt), bias=dev32(b), add=dev16(r))
+    assert_close(host(y), ref, f"conv {k}x{k} + up2 residual")
+    assert be.device_error() == 0
