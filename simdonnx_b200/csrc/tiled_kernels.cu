@@ -983,65 +983,76 @@ constexpr int STEM_TH = 16, STEM_TW = 64, STEM_R = 4;
 constexpr int STEM_IH = (STEM_TH - 1) * 2 + 3;           // 33 input rows
 constexpr int STEM_IW = ((STEM_TW - 1) * 2 + 3 + 3 + 3) / 4 * 4;  // 132 columns (3 of alignment)
 
-// One 16 x 64 stem output tile from the planar fp32 input tile in shared memory ([3][33][132], the
-// window of output column 0 starting at column 3): thread = 4 horizontally adjacent outputs x 16
-// channels of output row oy0 + ly, columns ox0 + lx .. ox0 + lx + 3.
+// One 16 x 64 stem output tile from the planar fp32 input tile in shared memory ([3][33][132];
+// output column j's window starts at column 2j + 3). A warp covers 32 consecutive output columns of
+// 4 output rows: thread = one column x 4 rows x 16 channels. Per (input channel, kernel row, output
+// row) it reads its 3 window values with two 8-byte loads at even columns (2j + 2, 2j + 4), so a
+// warp's load is 256 contiguous bytes (conflict-free; one thread per 4 adjacent outputs read with
+// an 8-word stride, 4- to 8-way bank conflicts); the 16 weights of a tap are shared-memory
+// broadcasts.
 template <int ACT>
 __device__ __forceinline__ void stem_tile_compute(const DirectArgs& a, const float* tile, const float* sw, const float* sb,
-                                                  int n, int oy0, int ly, int ox0, int lx) {
-  constexpr int IC = 3, OC = 16, K = 3;
-  const int oy = oy0 + ly;
-  if (oy < a.oh) {
-    float acc[STEM_R][OC];
+                                                  int n, int oy0, int ox0, int tid) {
+  constexpr int IC = 3, OC = 16, K = 3, RY = 4;
+  const int warp = tid >> 5, lane = tid & 31;
+  const int j = (warp & 1) * 32 + lane;  // output column inside the tile
+  const int r0 = (warp >> 1) * RY;       // first output row inside the tile
+  float acc[RY][OC];
 #pragma unroll
-    for (int r = 0; r < STEM_R; r++)
+  for (int r = 0; r < RY; r++)
 #pragma unroll
-      for (int o = 0; o < OC; o++) acc[r][o] = sb[o];
+    for (int o = 0; o < OC; o++) acc[r][o] = sb[o];
 #pragma unroll
-    for (int c = 0; c < IC; c++) {
+  for (int c = 0; c < IC; c++) {
 #pragma unroll
-      for (int ky = 0; ky < K; ky++) {
-        // window columns 2*lx .. 2*lx + 8 of this input row (+3: the alignment offset)
-        const float* row = tile + (c * STEM_IH + ly * 2 + ky) * STEM_IW + lx * 2 + 3;
-        float xv[(STEM_R - 1) * 2 + K];
+    for (int ky = 0; ky < K; ky++) {
+      float xv[RY][K];
 #pragma unroll
-        for (int j = 0; j < (STEM_R - 1) * 2 + K; j++) xv[j] = row[j];
+      for (int r = 0; r < RY; r++) {
+        const float* rp = tile + (c * STEM_IH + 2 * (r0 + r) + ky) * STEM_IW + 2 * j + 2;
+        const float2 p0 = *reinterpret_cast<const float2*>(rp);
+        const float2 p1 = *reinterpret_cast<const float2*>(rp + 2);
+        xv[r][0] = p0.y;
+        xv[r][1] = p1.x;
+        xv[r][2] = p1.y;
+      }
 #pragma unroll
-        for (int kx = 0; kx < K; kx++) {
-          const float4* wp = reinterpret_cast<const float4*>(sw + ((ky * K + kx) * IC + c) * OC);
-          float wv[OC];
+      for (int kx = 0; kx < K; kx++) {
+        const float4* wp = reinterpret_cast<const float4*>(sw + ((ky * K + kx) * IC + c) * OC);
+        float wv[OC];
 #pragma unroll
-          for (int q = 0; q < OC / 4; q++) {
-            const float4 w4 = wp[q];
-            wv[4 * q] = w4.x; wv[4 * q + 1] = w4.y; wv[4 * q + 2] = w4.z; wv[4 * q + 3] = w4.w;
-          }
-#pragma unroll
-          for (int r = 0; r < STEM_R; r++)
-#pragma unroll
-            for (int o = 0; o < OC; o++) acc[r][o] = fmaf(xv[r * 2 + kx], wv[o], acc[r][o]);
+        for (int q = 0; q < OC / 4; q++) {
+          const float4 w4 = wp[q];
+          wv[4 * q] = w4.x; wv[4 * q + 1] = w4.y; wv[4 * q + 2] = w4.z; wv[4 * q + 3] = w4.w;
         }
+#pragma unroll
+        for (int r = 0; r < RY; r++)
+#pragma unroll
+          for (int o = 0; o < OC; o++) acc[r][o] = fmaf(xv[r][kx], wv[o], acc[r][o]);
       }
     }
+  }
+  const int ox = ox0 + j;
+  if (ox >= a.ow) return;
 #pragma unroll
-    for (int r = 0; r < STEM_R; r++) {
-      const int ox = ox0 + lx + r;
-      if (ox >= a.ow) break;
-      __half* yp = static_cast<__half*>(a.y) + (((int64_t)n * a.oh + oy) * a.ow + ox) * a.y_pix_stride + a.y_ch_off;
+  for (int r = 0; r < RY; r++) {
+    const int oy = oy0 + r0 + r;
+    if (oy >= a.oh) break;
+    __half* yp = static_cast<__half*>(a.y) + (((int64_t)n * a.oh + oy) * a.ow + ox) * a.y_pix_stride + a.y_ch_off;
 #pragma unroll
-      for (int h8 = 0; h8 < OC / 8; h8++) {
-        uint4 u;
-        __half2* h = reinterpret_cast<__half2*>(&u);
+    for (int h8 = 0; h8 < OC / 8; h8++) {
+      uint4 u;
+      __half2* h = reinterpret_cast<__half2*>(&u);
 #pragma unroll
-        for (int q = 0; q < 4; q++)
-          h[q] = __floats2half2_rn(act_t<ACT>(acc[r][h8 * 8 + 2 * q]), act_t<ACT>(acc[r][h8 * 8 + 2 * q + 1]));
-        reinterpret_cast<uint4*>(yp)[h8] = u;
-      }
+      for (int q = 0; q < 4; q++)
+        h[q] = __floats2half2_rn(act_t<ACT>(acc[r][h8 * 8 + 2 * q]), act_t<ACT>(acc[r][h8 * 8 + 2 * q + 1]));
+      reinterpret_cast<uint4*>(yp)[h8] = u;
     }
   }
 }
 
 template <int ACT>
-__global__ void __launch_bounds__(256) stem_tma_kernel(const __grid_constant__ CUtensorMap tmX, DirectArgs a,
+__global__ void __launch_bounds__(256, 2) stem_tma_kernel(const __grid_constant__ CUtensorMap tmX, DirectArgs a,
                                                        int tiles_x, int tiles_per_img, int total) {
   constexpr int IC = 3, OC = 16, K = 3;
   constexpr uint32_t kTileBytes = IC * STEM_IH * STEM_IW * 4;
@@ -1089,7 +1100,6 @@ __global__ void __launch_bounds__(256) stem_tma_kernel(const __grid_constant__ C
     issue(t0, 0);
     issued[0] = 1;
   }
-  const int ly = tid / (STEM_TW / STEM_R), lx = (tid - ly * (STEM_TW / STEM_R)) * STEM_R;
   int i = 0;
   for (int t = t0; t < t1; t++, i++) {
     const int b = i & 1;
@@ -1102,7 +1112,7 @@ __global__ void __launch_bounds__(256) stem_tma_kernel(const __grid_constant__ C
     const bool ok = mbar_wait(smem_u32(&full[b]), (uint32_t)(i >> 1) & 1u, a.err, SDX_DEV_WAIT_FULL, &abort_flag);
     if (__syncthreads_or(!ok)) break;
     const float* tile = bufs + b * (kBufBytes / 4);
-    stem_tile_compute<ACT>(a, tile, sw, sb, n, oy0, ly, ox0, lx);
+    stem_tile_compute<ACT>(a, tile, sw, sb, n, oy0, ox0, tid);
     __syncthreads();
   }
   if (tid < 32) {
@@ -1148,7 +1158,7 @@ static bool stem_tma_launch_t(const DirectArgs& a, cudaStream_t st) {
 // the fill reads 3 bytes per input pixel (plain loads: rows of 3-byte pixels do not meet TMA's
 // 16-byte rules) and writes the same planar fp32 tile as the TMA-fed stem, whose compute follows.
 template <int ACT>
-__global__ void __launch_bounds__(256) stem_image_kernel(ImageArgs im, DirectArgs a, int tiles_x, int tiles_per_img) {
+__global__ void __launch_bounds__(256, 2) stem_image_kernel(ImageArgs im, DirectArgs a, int tiles_x, int tiles_per_img) {
   constexpr int IC = 3, OC = 16, K = 3;
   constexpr int NCOL = (STEM_TW - 1) * 2 + K;  // 129 input columns of a tile
   extern __shared__ float fsm[];
@@ -1187,8 +1197,7 @@ __global__ void __launch_bounds__(256) stem_image_kernel(ImageArgs im, DirectArg
     d[2 * STEM_IH * STEM_IW] = v2;
   }
   __syncthreads();
-  const int ly = tid / (STEM_TW / STEM_R), lx = (tid - ly * (STEM_TW / STEM_R)) * STEM_R;
-  stem_tile_compute<ACT>(a, tile, sw, sb, n, oy0, ly, ox0, lx);
+  stem_tile_compute<ACT>(a, tile, sw, sb, n, oy0, ox0, tid);
 }
 
 template <int ACT>
