@@ -524,34 +524,40 @@ __device__ __forceinline__ void epi_chunk_fast(const TcArgs& a, float (&v)[16], 
 // each tap1 feeds the second 2x2 ConvT (one output channel), so the row yields the 4 x 4 output
 // block at (4y, 4x): 16 independent FMA chains over c, stored as four 16-byte rows (fp32) or 8-byte
 // rows (fp16). smem: sBias[c] = first bias, then the second ConvT's raw weights [c][tap2] and bias.
-template <int ACT, int OC1>  // OC1 in {8, 16, 24}: 4 x OC1 columns = whole 16-column TMEM loads
+template <int ACT, int OC1>  // OC1 in {8, 16, 24}: 2 x OC1 columns = whole 16-column TMEM loads
 __device__ __forceinline__ void chain_row(const TcArgs& a, uint32_t tbase, const float* sBias, uint64_t* acce_bar,
                                           int img, int y, int x, bool ok) {
-  float v[4 * OC1];
-#pragma unroll
-  for (int j = 0; j < 4 * OC1 / 16; j++) tmem_ld16_issue(tbase + (uint32_t)(16 * j), v + 16 * j);
-  tmem_wait_ld();
-#pragma unroll
-  for (int j = 0; j < 4 * OC1 / 16; j++) tmem_ld_wait16(v + 16 * j);
-  tc_fence_before();
-  mbar_arrive(smem_u32(acce_bar));
   const float4* w2 = reinterpret_cast<const float4*>(sBias + a.BN);
   const float b2 = sBias[a.BN + 4 * OC1];
   float blk[16];
 #pragma unroll
   for (int i = 0; i < 16; i++) blk[i] = b2;
+  // two halves of two taps each (48 registers of accumulator at a time, so four epilogue groups fit)
 #pragma unroll
-  for (int c = 0; c < OC1; c++) {
-    const float4 w = w2[c];
-    const float bb = sBias[c];
+  for (int hf = 0; hf < 2; hf++) {
+    float v[2 * OC1];
 #pragma unroll
-    for (int t1 = 0; t1 < 4; t1++) {
-      const float h = act_t<ACT>(v[t1 * OC1 + c] + bb);
-      const int r0 = 2 * (t1 >> 1), c0 = 2 * (t1 & 1);
-      blk[r0 * 4 + c0] = fmaf(h, w.x, blk[r0 * 4 + c0]);
-      blk[r0 * 4 + c0 + 1] = fmaf(h, w.y, blk[r0 * 4 + c0 + 1]);
-      blk[(r0 + 1) * 4 + c0] = fmaf(h, w.z, blk[(r0 + 1) * 4 + c0]);
-      blk[(r0 + 1) * 4 + c0 + 1] = fmaf(h, w.w, blk[(r0 + 1) * 4 + c0 + 1]);
+    for (int j = 0; j < 2 * OC1 / 16; j++) tmem_ld16_issue(tbase + (uint32_t)(hf * 2 * OC1 + 16 * j), v + 16 * j);
+    tmem_wait_ld();
+#pragma unroll
+    for (int j = 0; j < 2 * OC1 / 16; j++) tmem_ld_wait16(v + 16 * j);
+    if (hf == 1) {
+      tc_fence_before();
+      mbar_arrive(smem_u32(acce_bar));
+    }
+#pragma unroll
+    for (int c = 0; c < OC1; c++) {
+      const float4 w = w2[c];
+      const float bb = sBias[c];
+#pragma unroll
+      for (int dx1 = 0; dx1 < 2; dx1++) {
+        const float h = act_t<ACT>(v[dx1 * OC1 + c] + bb);
+        const int r0 = 2 * hf, c0 = 2 * dx1;  // tap1 = (hf, dx1)
+        blk[r0 * 4 + c0] = fmaf(h, w.x, blk[r0 * 4 + c0]);
+        blk[r0 * 4 + c0 + 1] = fmaf(h, w.y, blk[r0 * 4 + c0 + 1]);
+        blk[(r0 + 1) * 4 + c0] = fmaf(h, w.z, blk[(r0 + 1) * 4 + c0]);
+        blk[(r0 + 1) * 4 + c0 + 1] = fmaf(h, w.w, blk[(r0 + 1) * 4 + c0 + 1]);
+      }
     }
   }
   if (!ok) return;
@@ -1560,7 +1566,7 @@ int tc_launch(const TcProblem& p, cudaStream_t stream) {
   if (p.res_up && !fast)
     return set_error(SDX_ERR_NOT_SUPPORTED, "tc: upsampled residual needs the fp16 TMA-store epilogue");
   if (chain) a.bias_smem = BN + 4 * p.convt_oc + 4;  // first bias, second ConvT's weights and bias
-  const bool eg4 = !p.kxn && !chain && 4 * BN <= 512 && (BN <= 64 || (!fast && !kxn_fast));
+  const bool eg4 = !p.kxn && 4 * BN <= 512 && (BN <= 64 || chain || (!fast && !kxn_fast));
   for (int eg = eg4 ? 4 : 2; eg >= 2 && !planned; eg -= 2) {
   a.egroups = eg;
   for (int res = 1; res >= 0 && !planned; res--) {
@@ -1595,7 +1601,9 @@ int tc_launch(const TcProblem& p, cudaStream_t stream) {
   cudaGetDevice(&dev);
   const int grid = std::min(total, num_sms(dev));
   int rc = SDX_OK;
-  if (chain) {
+  if (chain && a.egroups == 4) {
+    SDX_ACT_DISPATCH(a.act, ACTC, rc = (launch_tc<ACTC, 4, 4>(dev, grid, smem, stream, mA, mB, mOut, mRes, a)));
+  } else if (chain) {
     SDX_ACT_DISPATCH(a.act, ACTC, rc = (launch_tc<ACTC, 4, 2>(dev, grid, smem, stream, mA, mB, mOut, mRes, a)));
   } else if (fast && a.egroups == 4) {
     SDX_ACT_DISPATCH(a.act, ACTC, rc = (launch_tc<ACTC, 1, 4>(dev, grid, smem, stream, mA, mB, mOut, mRes, a)));
