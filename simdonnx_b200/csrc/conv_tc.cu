@@ -310,11 +310,11 @@ __device__ __forceinline__ void umma_stage_dispatch(uint32_t p, int bt, int nk, 
 // commits, no runtime loop or dispatch between them (each costs the issuing warp far more than
 // the MMA itself); ring slot, phases and the N tile advance without branches.
 struct MmaSingle {
-  uint32_t d0, acc_stride, sA, a_stage_bytes, a_blk16, b_cb16, b_nt16, b_lo16, idesc;
+  uint32_t d0, acc_stride, sA, a_stage_bytes, a_blk16, b_cb16, b_nt16, b_lo16, idesc, a_tap16, b_tap16;
   uint64_t dconst, bd0;
   int S, nacc, n_tiles, nt_step, nt0;
 };
-template <int NK, bool TWO, int CPS>
+template <int BT, int NK, bool TWO, int CPS>
 __device__ __noinline__ void mma_single_loop(uint32_t ld, const MmaSingle m, int tile0, int total_tiles, int tstep,
                                              uint64_t* full, uint64_t* empty, uint64_t* accf, uint64_t* acce,
                                              unsigned int* err, volatile int* abort_flag) {
@@ -329,8 +329,8 @@ __device__ __noinline__ void mma_single_loop(uint32_t ld, const MmaSingle m, int
     const uint64_t bd = m.bd0 + (uint64_t)((uint32_t)nt * m.b_nt16);
 #pragma unroll
     for (int ci = 0; ci < CPS; ci++)
-      umma_stage<1, NK, TWO>(ld, d, ad + (uint64_t)(ci * m.a_blk16), bd + (uint64_t)(ci * m.b_cb16), 0u, 0u, m.b_lo16,
-                             m.idesc, ci == 0 ? 0u : 1u);
+      umma_stage<BT, NK, TWO>(ld, d, ad + (uint64_t)(ci * m.a_blk16), bd + (uint64_t)(ci * m.b_cb16), m.a_tap16,
+                              m.b_tap16, m.b_lo16, m.idesc, ci == 0 ? 0u : 1u);
     tc_commit_p(ld, smem_u32(&empty[s]));
     tc_commit_p(ld, smem_u32(&accf[acc]));
     s = s + 1 == m.S ? 0 : s + 1;
@@ -341,14 +341,14 @@ __device__ __noinline__ void mma_single_loop(uint32_t ld, const MmaSingle m, int
     nt = nt >= m.n_tiles ? nt - m.n_tiles : nt;
   }
 }
-template <int NK, bool TWO>
+template <int BT, int NK, bool TWO>
 __device__ __forceinline__ void mma_single_cps(int cps, uint32_t ld, const MmaSingle& m, int tile0, int total_tiles,
                                                int tstep, uint64_t* full, uint64_t* empty, uint64_t* accf,
                                                uint64_t* acce, unsigned int* err, volatile int* abort_flag) {
-  if (cps == 1) mma_single_loop<NK, TWO, 1>(ld, m, tile0, total_tiles, tstep, full, empty, accf, acce, err, abort_flag);
-  else if (cps == 2) mma_single_loop<NK, TWO, 2>(ld, m, tile0, total_tiles, tstep, full, empty, accf, acce, err, abort_flag);
-  else if (cps == 3) mma_single_loop<NK, TWO, 3>(ld, m, tile0, total_tiles, tstep, full, empty, accf, acce, err, abort_flag);
-  else mma_single_loop<NK, TWO, 4>(ld, m, tile0, total_tiles, tstep, full, empty, accf, acce, err, abort_flag);
+  if (cps == 1) mma_single_loop<BT, NK, TWO, 1>(ld, m, tile0, total_tiles, tstep, full, empty, accf, acce, err, abort_flag);
+  else if (cps == 2) mma_single_loop<BT, NK, TWO, 2>(ld, m, tile0, total_tiles, tstep, full, empty, accf, acce, err, abort_flag);
+  else if (cps == 3) mma_single_loop<BT, NK, TWO, 3>(ld, m, tile0, total_tiles, tstep, full, empty, accf, acce, err, abort_flag);
+  else mma_single_loop<BT, NK, TWO, 4>(ld, m, tile0, total_tiles, tstep, full, empty, accf, acce, err, abort_flag);
 }
 
 // One 16-column chunk (tile columns 16c..16c+15) of one accumulator row: bias -> + residual ->
@@ -772,7 +772,9 @@ __global__ void __launch_bounds__(tc_threads(G), 1)
       int s = 0;
       uint32_t phase = 0;
       uint32_t acc = 0, accph = 0;
-      const bool single = kblocks == 1 && a.b_resident && a.b_taps == 1 && a.cps <= 4 && (nk == 1 || nk == 2 || nk == 4);
+      // one-tap tiles (pointwise), and the kx-in-N 3x3 convs (three row taps, one weight term)
+      const bool single = kblocks == 1 && a.b_resident && (a.b_taps == 1 || (a.b_taps == 3 && a.wterms == 1)) &&
+                          a.cps <= 4 && (nk == 1 || nk == 2 || nk == 4);
       if (ok && single) {
         MmaSingle m;
         m.d0 = tmem_base;
@@ -783,6 +785,8 @@ __global__ void __launch_bounds__(tc_threads(G), 1)
         m.b_cb16 = b_cb >> 4;
         m.b_nt16 = b_res_off(0, 0, 0, 1) >> 4;
         m.b_lo16 = b_lo16;
+        m.a_tap16 = a_tap16;
+        m.b_tap16 = b_tap16;
         m.idesc = idesc;
         m.dconst = dconst;
         m.bd0 = dconst | (uint64_t)((sB_addr >> 4) & 0x3FFFu);
@@ -792,14 +796,18 @@ __global__ void __launch_bounds__(tc_threads(G), 1)
         m.nt_step = (int)(gridDim.x % (unsigned)a.n_tiles);
         m.nt0 = (int)(blockIdx.x % (unsigned)a.n_tiles);
         const int tt = a.m_tiles * a.n_tiles;
-        if (a.wterms == 2) {
-          if (nk == 1) mma_single_cps<1, true>(a.cps, ld, m, blockIdx.x, tt, gridDim.x, full, empty, accf, acce, a.err, abort_flag);
-          else if (nk == 2) mma_single_cps<2, true>(a.cps, ld, m, blockIdx.x, tt, gridDim.x, full, empty, accf, acce, a.err, abort_flag);
-          else mma_single_cps<4, true>(a.cps, ld, m, blockIdx.x, tt, gridDim.x, full, empty, accf, acce, a.err, abort_flag);
+        if (a.b_taps == 3) {
+          if (nk == 1) mma_single_cps<3, 1, false>(a.cps, ld, m, blockIdx.x, tt, gridDim.x, full, empty, accf, acce, a.err, abort_flag);
+          else if (nk == 2) mma_single_cps<3, 2, false>(a.cps, ld, m, blockIdx.x, tt, gridDim.x, full, empty, accf, acce, a.err, abort_flag);
+          else mma_single_cps<3, 4, false>(a.cps, ld, m, blockIdx.x, tt, gridDim.x, full, empty, accf, acce, a.err, abort_flag);
+        } else if (a.wterms == 2) {
+          if (nk == 1) mma_single_cps<1, 1, true>(a.cps, ld, m, blockIdx.x, tt, gridDim.x, full, empty, accf, acce, a.err, abort_flag);
+          else if (nk == 2) mma_single_cps<1, 2, true>(a.cps, ld, m, blockIdx.x, tt, gridDim.x, full, empty, accf, acce, a.err, abort_flag);
+          else mma_single_cps<1, 4, true>(a.cps, ld, m, blockIdx.x, tt, gridDim.x, full, empty, accf, acce, a.err, abort_flag);
         } else {
-          if (nk == 1) mma_single_cps<1, false>(a.cps, ld, m, blockIdx.x, tt, gridDim.x, full, empty, accf, acce, a.err, abort_flag);
-          else if (nk == 2) mma_single_cps<2, false>(a.cps, ld, m, blockIdx.x, tt, gridDim.x, full, empty, accf, acce, a.err, abort_flag);
-          else mma_single_cps<4, false>(a.cps, ld, m, blockIdx.x, tt, gridDim.x, full, empty, accf, acce, a.err, abort_flag);
+          if (nk == 1) mma_single_cps<1, 1, false>(a.cps, ld, m, blockIdx.x, tt, gridDim.x, full, empty, accf, acce, a.err, abort_flag);
+          else if (nk == 2) mma_single_cps<1, 2, false>(a.cps, ld, m, blockIdx.x, tt, gridDim.x, full, empty, accf, acce, a.err, abort_flag);
+          else mma_single_cps<1, 4, false>(a.cps, ld, m, blockIdx.x, tt, gridDim.x, full, empty, accf, acce, a.err, abort_flag);
         }
         ok = false;  // the loop above ran every tile
       }
