@@ -309,6 +309,57 @@ __device__ __forceinline__ void umma_stage_dispatch(uint32_t p, int bt, int nk, 
 // channel block of the tile in one stage): per tile two waits, CPS x NK (x2 with TWO) MMAs and two
 // commits, no runtime loop or dispatch between them (each costs the issuing warp far more than
 // the MMA itself); ring slot, phases and the N tile advance without branches.
+// Producer loop for the same single-stage tiles: per tile one empty wait, one expect_tx and CPS
+// A copies (2-D row boxes, or the 4-D pixel box at (ox0 - pad_l, oy0 - pad_t)), without per-stage
+// dispatch. Ring slots that received a copy and their last phase are reported for the wind-down.
+struct ProdSingle {
+  uint32_t sA, a_stage_bytes, a_blk_bytes, stage_tx;
+  int S, n_tiles, tiles_h, tiles_w, BH, BWs, kblk, pad_l, pad_t;
+};
+template <int CONV, int CPS>
+__device__ __noinline__ void producer_single_loop(uint32_t ld, const ProdSingle p, const CUtensorMap* tmA, int tile0,
+                                                  int total_tiles, int tstep, uint64_t* full, uint64_t* empty,
+                                                  unsigned int* err, volatile int* abort_flag, uint32_t& issued_mask,
+                                                  uint32_t& last_phase) {
+  int s = 0;
+  uint32_t phase = 0;
+  for (int tile = tile0; tile < total_tiles; tile += tstep) {
+    const int m_tile = p.n_tiles == 1 ? tile : tile / p.n_tiles;
+    if (!mbar_wait_warp(smem_u32(&empty[s]), phase ^ 1u, err, SDX_DEV_WAIT_EMPTY, abort_flag)) break;
+    const uint32_t fb = smem_u32(&full[s]);
+    mbar_arrive_expect_tx_p(ld, fb, p.stage_tx);
+    const uint32_t dA0 = p.sA + (uint32_t)s * p.a_stage_bytes;
+    if (CONV) {
+      const int per_img = p.tiles_h * p.tiles_w;
+      const int img = m_tile / per_img;
+      const int r = m_tile - img * per_img;
+      const int ty = r / p.tiles_w;
+      const int oy0 = ty * p.BH, ox0 = (r - ty * p.tiles_w) * p.BWs;
+#pragma unroll
+      for (int ci = 0; ci < CPS; ci++)
+        tma_load_4d_p(ld, dA0 + (uint32_t)ci * p.a_blk_bytes, tmA, fb, ci * p.kblk, ox0 - p.pad_l, oy0 - p.pad_t, img);
+    } else {
+#pragma unroll
+      for (int ci = 0; ci < CPS; ci++)
+        tma_load_2d_p(ld, dA0 + (uint32_t)ci * p.a_blk_bytes, tmA, fb, ci * p.kblk, m_tile * TC_BM);
+    }
+    issued_mask |= 1u << s;
+    last_phase = (last_phase & ~(1u << s)) | (phase << s);
+    s = s + 1 == p.S ? 0 : s + 1;
+    phase ^= s == 0 ? 1u : 0u;
+  }
+}
+template <int CONV>
+__device__ __forceinline__ void producer_single_cps(int cps, uint32_t ld, const ProdSingle& p, const CUtensorMap* tmA,
+                                                    int tile0, int total_tiles, int tstep, uint64_t* full,
+                                                    uint64_t* empty, unsigned int* err, volatile int* abort_flag,
+                                                    uint32_t& issued_mask, uint32_t& last_phase) {
+  if (cps == 1) producer_single_loop<CONV, 1>(ld, p, tmA, tile0, total_tiles, tstep, full, empty, err, abort_flag, issued_mask, last_phase);
+  else if (cps == 2) producer_single_loop<CONV, 2>(ld, p, tmA, tile0, total_tiles, tstep, full, empty, err, abort_flag, issued_mask, last_phase);
+  else if (cps == 3) producer_single_loop<CONV, 3>(ld, p, tmA, tile0, total_tiles, tstep, full, empty, err, abort_flag, issued_mask, last_phase);
+  else producer_single_loop<CONV, 4>(ld, p, tmA, tile0, total_tiles, tstep, full, empty, err, abort_flag, issued_mask, last_phase);
+}
+
 struct MmaSingle {
   uint32_t d0, acc_stride, sA, a_stage_bytes, a_blk16, b_cb16, b_nt16, b_lo16, idesc, a_tap16, b_tap16;
   uint64_t dconst, bd0;
@@ -687,6 +738,32 @@ __global__ void __launch_bounds__(tc_threads(G), 1)
       }
       int s = 0;
       uint32_t phase = 0;
+      // single-stage tiles with resident weights (pointwise, kx-in-N 3x3, ConvT): the dispatch-free
+      // loop; a 4-D box at (ox0 - pad_l, oy0 - pad_t) covers halo mode with one column tap and the
+      // one-tap conv mode alike
+      if (kblocks == 1 && a.b_resident && a.cps <= 4 && (a.mode != TC_CONV || a.halo || a.taps == 1)) {
+        ProdSingle ps;
+        ps.sA = smem_u32(sA);
+        ps.a_stage_bytes = a.a_stage_bytes;
+        ps.a_blk_bytes = a.a_blk_bytes;
+        ps.stage_tx = (uint32_t)a.cps * a.a_box_bytes;
+        ps.S = S;
+        ps.n_tiles = a.n_tiles;
+        ps.tiles_h = a.tiles_h;
+        ps.tiles_w = a.tiles_w;
+        ps.BH = a.BH;
+        ps.BWs = a.BWs;
+        ps.kblk = a.kblk;
+        ps.pad_l = a.pad_l;
+        ps.pad_t = a.pad_t;
+        if (a.mode == TC_CONV)
+          producer_single_cps<1>(a.cps, ld, ps, &tmA, blockIdx.x, total_tiles, gridDim.x, full, empty, a.err, abort_flag,
+                                 issued_mask, last_phase);
+        else
+          producer_single_cps<0>(a.cps, ld, ps, &tmA, blockIdx.x, total_tiles, gridDim.x, full, empty, a.err, abort_flag,
+                                 issued_mask, last_phase);
+        ok = false;  // every tile issued above
+      }
       for (int tile = blockIdx.x; tile < total_tiles && ok; tile += gridDim.x) {
         const int m_tile = a.n_tiles == 1 ? tile : tile / a.n_tiles;
         const int n_tile = tile - m_tile * a.n_tiles;
