@@ -1008,9 +1008,11 @@ __global__ void __launch_bounds__(tc_threads(G), 1)
           const int64_t pix = (int64_t)tcd.m0 + row_in_tile;
           if (pix < a.M) {
             if (a.res_up) {
-              const int64_t hw = (int64_t)a.OH * a.OW, img = pix / hw, rem = pix - img * hw;
-              const int y = (int)(rem / a.OW), x = (int)(rem - (int64_t)y * a.OW);
-              rpix = (img * (a.OH >> 1) + (y >> 1)) * (a.OW >> 1) + (x >> 1);
+              // 32-bit index math (a.M < 2^31 rows): 64-bit divisions cost the epilogue per tile
+              const uint32_t hw = (uint32_t)a.OH * (uint32_t)a.OW, p32 = (uint32_t)pix;
+              const uint32_t img = p32 / hw, rem = p32 - img * hw;
+              const uint32_t y = rem / (uint32_t)a.OW, x = rem - y * (uint32_t)a.OW;
+              rpix = ((int64_t)img * (a.OH >> 1) + (y >> 1)) * (a.OW >> 1) + (x >> 1);
             } else {
               rpix = pix;
             }
