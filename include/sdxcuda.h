@@ -156,6 +156,10 @@ typedef struct sdx_conv_desc {
   int add_up;        /* 0 or 1: the residual as given; 2: `add` is [batch, oh/2, ow/2, oc] fp16 NHWC, read
                         nearest-upsampled (an FPN top-down ResizeNearest(x, add = this conv) fused into
                         the conv: y = act(conv + up2(add))); tensor-core routes, oh and ow even */
+  sdx_dptr gap_sums; /* fp32 [batch * oh * ow / 32, oc]: channel sums of y over each run of 32 pixels
+                        (the global average pool of a following SE gate, fused: pass it as that gate's
+                        `sums`), or 0. 1x1 tensor-core route with the fp16 TMA-store epilogue
+                        (y fp16, oc % 16 == 0, 16-byte aligned rows); (batch * oh * ow) % 32 == 0 */
 } sdx_conv_desc;
 int sdx_conv2d(sdx_ctx* ctx, const sdx_conv_desc* d, sdx_stream s);
 
@@ -211,6 +215,8 @@ typedef struct sdx_gate_desc {
   int act1_relu, hard;
   float alpha, beta, offset;
   sdx_dptr x, w1, b1, w2, b2, s, partial;
+  sdx_dptr sums;     /* fp32 [batch, hw / 32, c]: 32-pixel channel sums of x written by the producing
+                        conv (sdx_conv_desc.gap_sums), or 0. When set, x is not read; hw % 32 == 0 */
 } sdx_gate_desc;
 size_t sdx_channel_gate_scratch_bytes(int batch, int hw, int c);
 int sdx_channel_gate(sdx_ctx* ctx, const sdx_gate_desc* d, sdx_stream s);

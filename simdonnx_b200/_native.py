@@ -38,7 +38,7 @@ class ConvDesc(ctypes.Structure):
                                   "x_layout", "y_dtype", "add_dtype", "add_layout", "y_layout", "pad_mode")] + [
         ("pad_value", _f), ("y_pix_stride", _i64), ("y_ch_off", _i),
         ("x", _u64), ("w", _u64), ("bias", _u64), ("add", _u64), ("y", _u64), ("in_scale", _u64), ("w_terms", _i),
-        ("add_up", _i)]
+        ("add_up", _i), ("gap_sums", _u64)]
 
 
 class GemmDesc(ctypes.Structure):
@@ -60,7 +60,7 @@ class PoolDesc(ctypes.Structure):
 class GateDesc(ctypes.Structure):
     _fields_ = [(n, _i) for n in ("batch", "hw", "c", "r", "act1_relu", "hard")] + [
         ("alpha", _f), ("beta", _f), ("offset", _f)] + [
-        (n, _u64) for n in ("x", "w1", "b1", "w2", "b2", "s", "partial")]
+        (n, _u64) for n in ("x", "w1", "b1", "w2", "b2", "s", "partial", "sums")]
 
 
 class ResizeDesc(ctypes.Structure):

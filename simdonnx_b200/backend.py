@@ -180,7 +180,8 @@ def pool(be: CudaBackend, x, k, s, pads=(0, 0, 0, 0), is_avg=False, relu=False, 
     return y
 
 
-def channel_gate(be: CudaBackend, x, w1, b1, w2, b2, act1_relu=True, hard=True, alpha=0.2, beta=0.5, offset=0.0):
+def channel_gate(be: CudaBackend, x, w1, b1, w2, b2, act1_relu=True, hard=True, alpha=0.2, beta=0.5, offset=0.0,
+                 sums=None):
     b, h, w, c = x.shape
     r = w1.shape[0]
     s = torch.empty((b, c), dtype=torch.float32, device=x.device)
@@ -189,6 +190,7 @@ def channel_gate(be: CudaBackend, x, w1, b1, w2, b2, act1_relu=True, hard=True, 
     d.batch, d.hw, d.c, d.r, d.act1_relu, d.hard = b, h * w, c, r, int(act1_relu), int(hard)
     d.alpha, d.beta, d.offset = alpha, beta, offset
     d.x, d.w1, d.b1, d.w2, d.b2, d.s, d.partial = ptr(x), ptr(w1), ptr(b1), ptr(w2), ptr(b2), ptr(s), ptr(scratch)
+    d.sums = ptr(sums)  # a conv's 32-pixel channel sums of x (then x is not read)
     N.call("sdx_channel_gate", be.ctx, ctypes.byref(d), cur_stream())
     return s
 

@@ -407,38 +407,53 @@ static int gate_chunks(int hw, int c) {
   return (int)std::min<int64_t>(64, std::max<int64_t>(1, std::min<int64_t>(hw, (bytes + 65535) / 65536)));
 }
 
+// Chunks over the [batch][hw / 32][c] fp32 32-pixel sums a conv wrote (about 32 KB each); never
+// more than gate_chunks(hw, c), so the same scratch serves both forms. Also batch-independent.
+static int gate_sum_chunks(int hw, int c) {
+  const int rows = hw / 32;
+  const int64_t bytes = (int64_t)rows * c * 4;
+  return (int)std::min<int64_t>(gate_chunks(hw, c),
+                                std::max<int64_t>(1, std::min<int64_t>(rows, (bytes + 32767) / 32768)));
+}
+
 // Scratch: per-chunk channel sums [batch][chunks][c], then the hidden layer [batch][r <= c].
 size_t gate_scratch_bytes(int batch, int hw, int c) {
   return sizeof(float) * (size_t)batch * (gate_chunks(hw, c) + 1) * c;
 }
 
-__global__ void gap_partial_kernel(const __half* __restrict__ x, int hw, int c, int chunks, float* __restrict__ partial) {
+// eight consecutive channels of one row as fp32
+__device__ __forceinline__ void ld8f(const __half* p, float (&v)[8]) { h8_to_f(__ldg(reinterpret_cast<const uint4*>(p)), v); }
+__device__ __forceinline__ void ld8f(const float* p, float (&v)[8]) {
+  const float4 a = __ldg(reinterpret_cast<const float4*>(p)), b = __ldg(reinterpret_cast<const float4*>(p) + 1);
+  v[0] = a.x; v[1] = a.y; v[2] = a.z; v[3] = a.w; v[4] = b.x; v[5] = b.y; v[6] = b.z; v[7] = b.w;
+}
+
+// Channel sums of rows [p0, p1) of image n's `rows` x c tile: fp16 pixels, or fp32 32-pixel sums.
+template <typename T>
+__global__ void gap_partial_kernel(const T* __restrict__ x, int rows, int c, int chunks, float* __restrict__ partial) {
   extern __shared__ float red[];
   const int n = blockIdx.y, chunk = blockIdx.x;
   const int cg = c >> 3;
   const int lanes_p = blockDim.x / cg;  // pixel lanes (blockDim is a multiple of cg)
   const int g = threadIdx.x % cg, lp = threadIdx.x / cg;
-  const int p0 = (int)((int64_t)chunk * hw / chunks), p1 = (int)((int64_t)(chunk + 1) * hw / chunks);
+  const int p0 = (int)((int64_t)chunk * rows / chunks), p1 = (int)((int64_t)(chunk + 1) * rows / chunks);
   float acc[8] = {0, 0, 0, 0, 0, 0, 0, 0};
   if (lp < lanes_p) {
-    const __half* base = x + (int64_t)n * hw * c + g * 8;
+    const T* base = x + (int64_t)n * rows * c + g * 8;
     int p = p0 + lp;
-    // four independent 16-byte loads in flight per thread, then the remainder
+    // four independent row loads in flight per thread, then the remainder
     for (; p + 3 * lanes_p < p1; p += 4 * lanes_p) {
-      uint4 u[4];
+      float v[4][8];
 #pragma unroll
-      for (int k = 0; k < 4; k++) u[k] = __ldg(reinterpret_cast<const uint4*>(base + (int64_t)(p + k * lanes_p) * c));
+      for (int k = 0; k < 4; k++) ld8f(base + (int64_t)(p + k * lanes_p) * c, v[k]);
 #pragma unroll
-      for (int k = 0; k < 4; k++) {
-        float v[8];
-        h8_to_f(u[k], v);
+      for (int k = 0; k < 4; k++)
 #pragma unroll
-        for (int j = 0; j < 8; j++) acc[j] += v[j];
-      }
+        for (int j = 0; j < 8; j++) acc[j] += v[k][j];
     }
     for (; p < p1; p += lanes_p) {
       float v[8];
-      h8_to_f(__ldg(reinterpret_cast<const uint4*>(base + (int64_t)p * c)), v);
+      ld8f(base + (int64_t)p * c, v);
 #pragma unroll
       for (int j = 0; j < 8; j++) acc[j] += v[j];
     }
@@ -544,7 +559,10 @@ int gate_launch(const GateArgs& a, cudaStream_t st) {
   if (a.c % 8 != 0 || a.c > 4096) return set_error(SDX_ERR_NOT_SUPPORTED, "channel gate: c must be a multiple of 8, <= 4096");
   if (a.r < 1 || a.r > a.c) return set_error(SDX_ERR_NOT_SUPPORTED, "channel gate: hidden width must be in 1..c");
   if (!a.partial) return set_error(SDX_ERR_INVALID, "channel gate: scratch buffer missing");
-  const int chunks = gate_chunks(a.hw, a.c);
+  if (a.sums && a.hw % 32 != 0) return set_error(SDX_ERR_NOT_SUPPORTED, "channel gate: 32-pixel sums need hw % 32 == 0");
+  if (a.sums && (reinterpret_cast<uintptr_t>(a.sums) & 15))
+    return set_error(SDX_ERR_INVALID, "channel gate: sums must be 16-byte aligned");
+  const int chunks = a.sums ? gate_sum_chunks(a.hw, a.c) : gate_chunks(a.hw, a.c);
   const int cg = a.c / 8;
   int block = std::max(cg, std::min(256, (256 / cg) * cg));
   if (block > 1024) return set_error(SDX_ERR_NOT_SUPPORTED, "channel gate: too many channels");
@@ -562,7 +580,8 @@ int gate_launch(const GateArgs& a, cudaStream_t st) {
     attr = true;
   }
   float* hid = a.partial + (size_t)a.batch * chunks * a.c;  // [batch][r], r <= c
-  gap_partial_kernel<<<dim3(chunks, a.batch), block, red, st>>>(a.x, a.hw, a.c, chunks, a.partial);
+  if (a.sums) gap_partial_kernel<float><<<dim3(chunks, a.batch), block, red, st>>>(a.sums, a.hw / 32, a.c, chunks, a.partial);
+  else gap_partial_kernel<__half><<<dim3(chunks, a.batch), block, red, st>>>(a.x, a.hw, a.c, chunks, a.partial);
   SDX_LAUNCH_CHECK("gap_partial");
   const int gx = (a.batch + GATE_IMG - 1) / GATE_IMG;
   gate_fc1_kernel<<<dim3(gx, (a.r + GATE_RJ - 1) / GATE_RJ), 256, fc1_smem, st>>>(a, chunks, hid);

@@ -124,6 +124,9 @@ struct TcArgs {
   void* chain_y;
   const float* chain_w2;
   const float* chain_b2;
+  // channel sums of the activated output over each run of 32 rows (a warp's rows; rows mode, M a
+  // multiple of 32): fp32 [M / 32][N], or null
+  float* gap;
   unsigned int* err;
 };
 
@@ -529,6 +532,69 @@ __device__ __forceinline__ void epi_chunk(const TcArgs& a, float (&v)[16], int c
   }
 }
 
+// Two-float packed add (sm_100 f32x2 pipe: one instruction for both lanes of the pair).
+__device__ __forceinline__ float2 add_f32x2(float2 a, float2 b) {
+  uint64_t x, y, d;
+  asm("mov.b64 %0, {%1, %2};" : "=l"(x) : "f"(a.x), "f"(a.y));
+  asm("mov.b64 %0, {%1, %2};" : "=l"(y) : "f"(b.x), "f"(b.y));
+  asm("add.rn.f32x2 %0, %1, %2;" : "=l"(d) : "l"(x), "l"(y));
+  float2 r;
+  asm("mov.b64 {%0, %1}, %2;" : "=f"(r.x), "=f"(r.y) : "l"(d));
+  return r;
+}
+
+// Channel sums of one warp's 32 staged output rows (fp16, the fast epilogue's swizzled staging: BN
+// columns in groups of G = min(BN, 64), row pitch P = 2G bytes) into gp[0 .. nlim). Lane l sums the
+// column pair j = l % NP over rows l / NP + R * i (NP = min(BN / 2, 32) pairs side by side, R = 32 /
+// NP rows per step), 4-byte loads; the swizzle term of those rows is a compile-time function of i, so
+// each load is one instruction off a per-lane base. Lanes that share a pair then combine (offsets
+// NP .. 16). BN = 128: two pairs per lane (one per 64-column group).
+template <int BN>
+__device__ __forceinline__ void gap_warp_rows(uint32_t slab, uint32_t group_bytes, int lane, float* gp, int nlim) {
+  constexpr int G = BN < 64 ? BN : 64;
+  constexpr int P = 2 * G;
+  constexpr int XM = P / 16 - 1;  // swizzle mask of the 16-byte unit index
+  constexpr int NP = BN / 2 < 32 ? BN / 2 : 32;
+  constexpr int R = 32 / NP;
+  constexpr int NG = BN / 2 / NP;  // pairs per lane: 1, or 2 for BN = 128
+  constexpr int IT = 32 / R;       // row steps
+  const int j = lane % NP, r0 = lane / NP;
+  const uint32_t byte = (uint32_t)(2 * j * 2) % (uint32_t)P;  // pair's byte offset inside its group row
+  const uint32_t k = byte >> 4, inner = byte & 15u;
+  // per-lane address of row r0 for each swizzle term c (the term of row r0 + R * i is c = ((r0 + R * i)
+  // * P >> 7) & XM; with r0 < R it depends on i only)
+  uint32_t base[XM + 1];
+#pragma unroll
+  for (int c = 0; c <= XM; c++) base[c] = slab + (uint32_t)r0 * P + (((k ^ (uint32_t)c) << 4) | inner);
+  float2 acc[NG];
+#pragma unroll
+  for (int g = 0; g < NG; g++) acc[g] = make_float2(0.0f, 0.0f);
+#pragma unroll
+  for (int i = 0; i < IT; i++) {
+    const int c = (((R * i) * P) >> 7) & XM;
+#pragma unroll
+    for (int g = 0; g < NG; g++) {
+      uint32_t w;
+      asm volatile("ld.shared.b32 %0, [%1];" : "=r"(w) : "r"(base[c] + (uint32_t)g * group_bytes + (uint32_t)(R * i * P)));
+      acc[g] = add_f32x2(acc[g], __half22float2(*reinterpret_cast<const __half2*>(&w)));
+    }
+  }
+#pragma unroll
+  for (int off = NP; off < 32; off *= 2)
+#pragma unroll
+    for (int g = 0; g < NG; g++) {
+      acc[g].x += __shfl_xor_sync(0xffffffffu, acc[g].x, off);
+      acc[g].y += __shfl_xor_sync(0xffffffffu, acc[g].y, off);
+    }
+  if (r0 == 0) {
+#pragma unroll
+    for (int g = 0; g < NG; g++) {
+      const int col = 2 * (j + g * NP);
+      if (col < nlim) *reinterpret_cast<float2*>(gp + col) = acc[g];
+    }
+  }
+}
+
 // Fast form of epi_chunk (kernel template EPI = 1): fp16 output through swizzled staging and TMA
 // stores, the bias (zeros when absent) in shared memory, the residual (if any) TMA-staged. The code
 // is straight-line, so the sixteen columns interleave; `sb` is the tile's bias (sBias + n0).
@@ -558,13 +624,15 @@ __device__ __forceinline__ void epi_chunk_fast(const TcArgs& a, float (&v)[16], 
       v[8 + 2 * i] += f1.x; v[8 + 2 * i + 1] += f1.y;
     }
   }
+#pragma unroll
+  for (int i = 0; i < 16; i++) v[i] = act_t<ACT>(v[i]);
   uint4 u0, u1;
   __half2* h0 = reinterpret_cast<__half2*>(&u0);
   __half2* h1 = reinterpret_cast<__half2*>(&u1);
 #pragma unroll
   for (int i = 0; i < 4; i++) {
-    h0[i] = __floats2half2_rn(act_t<ACT>(v[2 * i]), act_t<ACT>(v[2 * i + 1]));
-    h1[i] = __floats2half2_rn(act_t<ACT>(v[8 + 2 * i]), act_t<ACT>(v[8 + 2 * i + 1]));
+    h0[i] = __floats2half2_rn(v[2 * i], v[2 * i + 1]);
+    h1[i] = __floats2half2_rn(v[8 + 2 * i], v[8 + 2 * i + 1]);
   }
   sts16(ad0, u0);
   sts16(ad1, u1);
@@ -1192,6 +1260,16 @@ __global__ void __launch_bounds__(tc_threads(G), 1)
       }
       const int nch = a.BN / 16;
       int g = 0, cg = 0;
+      // channel sums of this warp's 32 rows (rows mode): its row of a.gap, warp-uniform
+      float* gp = nullptr;
+      int nlim = 0;
+      if (EPI == 1 && a.gap) {
+        const int64_t r0 = (int64_t)tcd.m0 + q * 32;
+        if (r0 < a.M) {
+          gp = a.gap + (r0 >> 5) * a.N + tcd.n0;
+          nlim = a.N - tcd.n0;
+        }
+      }
       if (EPI == 1 && nch <= 2) {
         // thin tiles: both chunks' TMEM loads in flight under one wait, the accumulator handed
         // back before any arithmetic
@@ -1243,6 +1321,13 @@ __global__ void __launch_bounds__(tc_threads(G), 1)
           const int ng = groups_of(tcd);
           for (int gg = 0; gg < ng; gg++) warp_copy(eld, a, &tmOut, slab + gg * a.group_bytes, gg, q, tcd, false, 0);
           bulk_commit(eld);
+          // channel sums of the staged rows (read alongside the store's own reads of them)
+          if (EPI == 1 && gp) {
+            if (a.BN == 16) gap_warp_rows<16>(slab, a.group_bytes, lane, gp, nlim);
+            else if (a.BN == 32) gap_warp_rows<32>(slab, a.group_bytes, lane, gp, nlim);
+            else if (a.BN == 64) gap_warp_rows<64>(slab, a.group_bytes, lane, gp, nlim);
+            else gap_warp_rows<128>(slab, a.group_bytes, lane, gp, nlim);
+          }
           // the next tile's buffer is free once the store that last read it has read it; then its
           // residual rows can be fetched while this warp waits for the next accumulator
           if (tile + tstep < total_tiles) {
@@ -1427,6 +1512,7 @@ int tc_launch(const TcProblem& p, cudaStream_t stream) {
   a.res_pix_stride = p.res_pix_stride;
   a.res_ch_off = p.res_ch_off;
   a.res_up = p.res_up;
+  a.gap = p.gap;
   a.out = p.out;
   a.out_f32 = p.out_f32;
   a.out_pix_stride = p.out_pix_stride;
@@ -1652,6 +1738,12 @@ int tc_launch(const TcProblem& p, cudaStream_t stream) {
   // general cases) up to 128 columns; two when the staging of four would crowd out the A stages
   if (p.res_up && !fast)
     return set_error(SDX_ERR_NOT_SUPPORTED, "tc: upsampled residual needs the fp16 TMA-store epilogue");
+  if (p.gap && (!fast || p.mode == TC_CONV || convt || p.M % 32 != 0 || p.N % 16 != 0 ||
+                (BN != 16 && BN != 32 && BN != 64 && BN != 128) || a.G != (BN < 64 ? BN : 64) ||
+                (reinterpret_cast<uintptr_t>(p.gap) & 7)))
+    return set_error(SDX_ERR_NOT_SUPPORTED,
+                     "tc: fused channel sums need a 1x1 conv with the fp16 TMA-store epilogue, rows % 32 == 0, "
+                     "oc % 16 == 0 and an 8-byte aligned sums buffer");
   if (chain) a.bias_smem = BN + 4 * p.convt_oc + 4;  // first bias, second ConvT's weights and bias
   const bool eg4 = !p.kxn && 4 * BN <= 512 && (BN <= 64 || chain || (!fast && !kxn_fast));
   for (int eg = eg4 ? 4 : 2; eg >= 2 && !planned; eg -= 2) {

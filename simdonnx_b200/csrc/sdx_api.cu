@@ -534,6 +534,8 @@ int sdx_conv2d(sdx_ctx* ctx, const sdx_conv_desc* d, sdx_stream s) {
   const int route = conv_route(d);
   if (d->add_up == 2 && route != R_TC_CONV && route != R_TC_ROWS)
     return set_error(SDX_ERR_NOT_SUPPORTED, "conv: upsampled residual only on the tensor-core routes");
+  if (d->gap_sums && route != R_TC_ROWS)
+    return set_error(SDX_ERR_NOT_SUPPORTED, "conv: fused channel sums only on the 1x1 tensor-core route");
   const int64_t ystride = d->y_pix_stride > 0 ? d->y_pix_stride : d->oc;
   cudaStream_t st = S(ctx, s);
   switch (route) {
@@ -577,6 +579,7 @@ int sdx_conv2d(sdx_ctx* ctx, const sdx_conv_desc* d, sdx_stream s) {
       p.out_pix_stride = ystride;
       p.out_ch_off = d->y_ch_off;
       p.act = d->act;
+      p.gap = P<float>(d->gap_sums);
       p.err = ctx->err_word;
       return tc_launch(p, st);
     }
@@ -773,6 +776,7 @@ int sdx_channel_gate(sdx_ctx* ctx, const sdx_gate_desc* d, sdx_stream s) {
   a.b2 = P<const float>(d->b2);
   a.s = P<float>(d->s);
   a.partial = P<float>(d->partial);
+  a.sums = P<const float>(d->sums);
   return gate_launch(a, S(ctx, s));
 }
 
@@ -801,6 +805,7 @@ int sdx_channel_gate_static(sdx_ctx* ctx, const sdx_gate_desc* d, sdx_stream s) 
   a.b2 = P<const float>(d->b2);
   a.s = P<float>(d->s);
   a.partial = scratch;
+  a.sums = P<const float>(d->sums);
   return gate_launch(a, S(ctx, s));
 }
 

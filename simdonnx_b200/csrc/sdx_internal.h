@@ -53,6 +53,7 @@ struct TcProblem {
   int64_t res_pix_stride;
   int res_ch_off;
   int res_up;  // 2: the residual is the nearest 2x downsample grid [batch, OH/2, OW/2, N] (read upsampled)
+  float* gap;  // fp32 [M / 32][N]: channel sums of the activated output over each 32-row run, or null
   void* out;
   int out_f32;
   int64_t out_pix_stride;
@@ -138,6 +139,7 @@ struct GateArgs {
   const float *w1, *b1, *w2, *b2;
   float* s;
   float* partial;
+  const float* sums;  // fp32 [batch][hw / 32][c] 32-pixel channel sums (a conv's fused output), or null
 };
 size_t gate_scratch_bytes(int batch, int hw, int c);
 int gate_launch(const GateArgs& a, cudaStream_t st);

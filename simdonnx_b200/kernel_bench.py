@@ -29,6 +29,7 @@ def main():
     ap.add_argument("--k", type=int, default=3)
     ap.add_argument("--stride", type=int, default=1)
     ap.add_argument("--act", default="hardswish")
+    ap.add_argument("--gap", action="store_true", help="pw: also write the 32-pixel channel sums (SE pooling)")
     ap.add_argument("--iters", type=int, default=20)
     ap.add_argument("--warmup", type=int, default=3)
     a = ap.parse_args()
@@ -55,11 +56,17 @@ def main():
         w = (rng.standard_normal((co, ci // group, k, k)) * 0.1).astype(np.float32)
         wp = B.pack_conv(d, w)
         bias = torch.zeros(co, device=dev)
+        sums = None
+        if a.gap:
+            sums = torch.empty((n * d.oh * d.ow // 32, co), dtype=torch.float32, device=dev)
+            d.gap_sums = B.ptr(sums)
         y = B.conv2d(be, d, x, wp, bias=bias)
         run = lambda: B.conv2d(be, d, x, wp, bias=bias, y=y)
         flops = 2 * n * d.oh * d.ow * co * (ci // group) * k * k
         wbytes = w.size * (4 if a.op in ("dw", "stem") else 2)
         byts = x.numel() * x.element_size() + wbytes + 4 * co + y.numel() * y.element_size()
+        if sums is not None:
+            byts += sums.numel() * 4
         shape = dict(n=n, h=hw, w=hw, cin=ci, cout=co, k=k, stride=s, oh=d.oh, ow=d.ow)
     elif a.op == "convt":
         x = torch.randn((n, hw, hw, ci), device=dev).half()

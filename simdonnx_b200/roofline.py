@@ -57,6 +57,8 @@ def node_cost(plan: ExecPlan, n) -> tuple:
         sc = getattr(p, "in_scale", None)
         if sc:
             byt += _nb(plan, sc)
+        if len(n.outs) > 1:  # fused 32-pixel channel sums for the SE gate
+            byt += _nb(plan, n.outs[1])
         return cls, flops, byt
     if op == "ConvTranspose":
         nb, ih, iw, ic = plan.values[n.ins[0]].shape
@@ -88,7 +90,9 @@ def node_cost(plan: ExecPlan, n) -> tuple:
         byt = _nb(plan, a) + Wb.size * 2 + (4 * nn if p.bias else 0) + _nb(plan, p.add) + _nb(plan, out)
         return "gemm_tc", 2 * m * nn * k, byt
     if op == "ChannelGate":
-        byt = _nb(plan, n.ins[0]) + plan.values[n.ins[1]].const.size * 4 + plan.values[n.ins[2]].const.size * 4
+        # reads the producing conv's 32-pixel channel sums when it wrote them, else the tensor
+        src = n.ins[3] if len(n.ins) > 3 else n.ins[0]
+        byt = _nb(plan, src) + plan.values[n.ins[1]].const.size * 4 + plan.values[n.ins[2]].const.size * 4
         return "channel_gate", 0, byt + _nb(plan, out)
     if op == "Elementwise":
         cls = "broadcast" if plan.values[n.ins[0]].shape != plan.values[n.ins[1]].shape else "binary"

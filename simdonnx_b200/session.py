@@ -217,6 +217,34 @@ def cuda_rewrite(plan: ExecPlan) -> ExecPlan:
                 continue
         out_nodes.append(n)
     P.nodes = [n for n in out_nodes if id(n) not in drop]
+
+    # 8. SE gate whose input is the output of a 1x1 tensor-core conv (fp16 TMA-store epilogue) -> the
+    #    conv also writes the 32-pixel channel sums of its output (sdx_conv_desc.gap_sums, fp32
+    #    [nb * h * w / 32, c]) and the gate reduces those instead of re-reading the tensor
+    prods = {o: m for m in P.nodes for o in m.outs}
+    for n in P.nodes:
+        if n.op != "ChannelGate" or len(n.ins) != 3:
+            continue
+        m = prods.get(n.ins[0])
+        if m is None or m.op != "Conv" or len(m.outs) != 1:
+            continue
+        xv, yv = P.values[m.ins[0]], P.values[m.outs[0]]
+        W = P.values[m.ins[1]].const
+        addv = P.values[m.p.add] if m.p.add else None
+        if not (m.p.group == 1 and m.p.pool is None and tuple(m.p.kernel) == (1, 1) and
+                tuple(m.p.strides) == (1, 1) and not any(m.p.pads) and getattr(m.p, "in_scale", None) is None and
+                xv.dtype == "f16" and xv.layout == "nhwc" and len(xv.shape) == 4 and xv.shape[3] % 8 == 0 and
+                yv.dtype == "f16" and yv.layout == "nhwc" and W.shape[0] % 16 == 0 and
+                (addv is None or (addv.dtype == "f16" and addv.layout == "nhwc" and not addv.alias))):
+            continue
+        if yv.alias and (P.shape(yv.alias[0])[3] % 8 or yv.alias[1] % 8):
+            continue
+        nb, h, w, c = yv.shape
+        if (h * w) % 32 or c != W.shape[0]:
+            continue
+        sums = P.add_value(m.outs[0] + ".gapsums", (nb * h * w // 32, c), "f32", "raw")
+        m.outs.append(sums)
+        n.ins.append(sums)
     return P
 
 
@@ -306,6 +334,7 @@ class CudaInferenceSession:
             d.add = self.ptr(p.add) if p.add else 0
             d.add_up = getattr(p, "add_up", 0)
             d.y = self.ptr(n.outs[0])
+            d.gap_sums = self.ptr(n.outs[1]) if len(n.outs) > 1 else 0
             scale = getattr(p, "in_scale", None)
             d.in_scale = self.ptr(scale) if scale else 0
             return N.OP_CONV, d
@@ -334,6 +363,7 @@ class CudaInferenceSession:
             d.x, d.w1, d.w2 = self.ptr(n.ins[0]), self._f32(n.ins[1]), self._f32(n.ins[2])
             d.b1, d.b2 = self._f32(p.b1), self._f32(p.b2)
             d.s, d.partial = self.ptr(n.outs[0]), self.scratch
+            d.sums = self.ptr(n.ins[3]) if len(n.ins) > 3 else 0
             return N.OP_CHANNEL_GATE, d
         if op == "Elementwise":
             a, b = n.ins

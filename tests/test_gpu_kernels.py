@@ -425,3 +425,35 @@ def test_conv_upsampled_residual(be, ic, oc, k, h, w):
     y = B.conv2d(be, d, dev16(x), B.pack_conv(d, wt), bias=dev32(b), add=dev16(r))
     assert_close(host(y), ref, f"conv {k}x{k} + up2 residual")
     assert be.device_error() == 0
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("ic,oc,h,w,act", [(16, 32, 32, 40, "hardswish"), (64, 128, 16, 16, "relu"),
+                                           (128, 256, 8, 12, "none")])
+def test_conv_channel_sums_feed_gate(be, ic, oc, h, w, act):
+    """SE pooling fused into a 1x1 conv: the conv also writes fp32 channel sums of each 32-pixel run of
+    its output, and the gate reading them equals the oracle gate over the reference output."""
+    from simdonnx_b200 import _native as N, backend as B
+    rng = np.random.default_rng(ic + oc + h)
+    nb = 3
+    x = rnd(rng, nb, h, w, ic)
+    wt = rnd(rng, oc, ic, 1, 1, scale=1 / np.sqrt(ic))
+    b = rnd(rng, oc)
+    ref = O.conv(x, O.ConvPlan(wt, b), act=act)
+    d = B.conv_desc(nb, h, w, ic, oc, 1, 1, act=act)
+    sums = torch.full((nb * h * w // 32, oc), float("nan"), dtype=torch.float32, device="cuda")
+    d.gap_sums = B.ptr(sums)
+    y = B.conv2d(be, d, dev16(x), B.pack_conv(d, wt), bias=dev32(b))
+    assert_close(host(y), ref, f"1x1 conv {ic}->{oc} with sums")
+    assert_close(host(sums), ref.reshape(-1, 32, oc).sum(axis=1), "32-pixel channel sums")
+    r = oc // 4
+    w1, b1, w2, b2 = rnd(rng, r, oc), rnd(rng, r), rnd(rng, oc, r), rnd(rng, oc)
+    ref_s = O.channel_gate(ref, w1, b1, w2, b2, act1_relu=True, hard=True, alpha=0.2, beta=0.5)
+    s = B.channel_gate(be, y, dev32(w1), dev32(b1), dev32(w2), dev32(b2), alpha=0.2, beta=0.5, sums=sums)
+    assert_close(host(s), ref_s, "gate from the conv's sums")
+    assert be.device_error() == 0
+    # shapes the fused sums do not cover are refused before anything is enqueued
+    d3 = B.conv_desc(nb, 3, 5, ic, oc, 1, 1, act=act)
+    d3.gap_sums = B.ptr(sums)
+    with pytest.raises(N.SdxError):
+        B.conv2d(be, d3, dev16(rnd(rng, nb, 3, 5, ic)), B.pack_conv(d3, wt), bias=dev32(b))
