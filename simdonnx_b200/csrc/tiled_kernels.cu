@@ -355,7 +355,9 @@ static bool dw_tma_launch_t(const DwArgs& a, cudaStream_t st) {
 // rows) in which every ring slot and every kernel-row bound is compile-time.
 // A warp reads whole pixel runs of the [IHt][IWt][CS] tile; with RX = 5 the strips that share a
 // warp start 40 or 80 words apart, so the reads are conflict-free.
-// Register budget (two 256-thread CTAs per SM, <= 128 each): K = 3 with CPT = 2, K = 5 with CPT = 1.
+// Register budget (two 256-thread CTAs per SM, <= 128 each): a channel pair per thread (CPT = 2,
+// one packed f32x2 FMA per tap) for K = 3 and K = 5 (K = 5 takes all 128: 50 accumulators, 50
+// weights, 18 inputs).
 template <int CPT>
 __device__ __forceinline__ void dw_load_px(const uint8_t* p, float (&v)[CPT]) {
   if constexpr (CPT == 2) {
@@ -364,6 +366,27 @@ __device__ __forceinline__ void dw_load_px(const uint8_t* p, float (&v)[CPT]) {
     v[1] = f.y;
   } else {
     v[0] = __half2float(*reinterpret_cast<const __half*>(p));
+  }
+}
+
+// acc += x * w on a channel pair with one packed f32x2 FMA (sm_100): each lane is the same
+// single-rounding fmaf, so results equal the scalar form bit for bit.
+__device__ __forceinline__ void ffma2(float& a0, float& a1, float x0, float x1, float w0, float w1) {
+  asm("{\n\t.reg .b64 ra, rx, rw;\n\t"
+      "mov.b64 ra, {%0, %1};\n\tmov.b64 rx, {%2, %3};\n\tmov.b64 rw, {%4, %5};\n\t"
+      "fma.rn.f32x2 ra, rx, rw, ra;\n\tmov.b64 {%0, %1}, ra;\n\t}"
+      : "+f"(a0), "+f"(a1)
+      : "f"(x0), "f"(x1), "f"(w0), "f"(w1));
+}
+
+// acc[q] += x[q] * w[q] over the CPT channels of a thread (packed for channel pairs)
+template <int CPT>
+__device__ __forceinline__ void fma_px(float (&acc)[CPT], const float (&x)[CPT], const float (&w)[CPT]) {
+  if constexpr (CPT == 2) {
+    ffma2(acc[0], acc[1], x[0], x[1], w[0], w[1]);
+  } else {
+#pragma unroll
+    for (int q = 0; q < CPT; q++) acc[q] = fmaf(x[q], w[q], acc[q]);
   }
 }
 
@@ -389,9 +412,7 @@ __device__ __forceinline__ void dw_row(const uint8_t* rowp, float (&acc)[K][RX][
 #pragma unroll
     for (int r = 0; r < RX; r++)
 #pragma unroll
-      for (int kx = 0; kx < K; kx++)
-#pragma unroll
-        for (int q = 0; q < CPT; q++) acc[sl][r][q] = fmaf(xf[r + kx][q], w[ky][kx][q], acc[sl][r][q]);
+      for (int kx = 0; kx < K; kx++) fma_px<CPT>(acc[sl][r], xf[r + kx], w[ky][kx]);
   }
 }
 
@@ -584,7 +605,7 @@ constexpr int DW_SLIDE_RX = 5;
 // (tiles x (TH + K - 1)) are fewest.
 template <int ACT, int K, int CS>
 static bool dw_slide_launch_cs(const DwArgs& a, cudaStream_t st) {
-  constexpr int RX = DW_SLIDE_RX, CPT = K <= 3 ? 2 : 1;
+  constexpr int RX = DW_SLIDE_RX, CPT = 2;
   constexpr int TPP = CS / CPT, TW = RX * (256 / TPP), IWt = TW + K - 1;
   static_assert(IWt <= 256, "TMA box width");
   const size_t row_bytes = (size_t)IWt * CS * 2;
@@ -748,10 +769,7 @@ __global__ void __launch_bounds__(256, 2) dw_slide2_kernel(const __grid_constant
 #pragma unroll
                 for (int r = 0; r < RX; r++)
 #pragma unroll
-                  for (int kx = 0; kx < K; kx++)
-#pragma unroll
-                    for (int q = 0; q < CPT; q++)
-                      acc[sl][r][q] = fmaf(xf[2 * r + kx][q], w[ky][kx][q], acc[sl][r][q]);
+                  for (int kx = 0; kx < K; kx++) fma_px<CPT>(acc[sl][r], xf[2 * r + kx], w[ky][kx]);
               }
             }
           });

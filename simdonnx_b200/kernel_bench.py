@@ -5,7 +5,7 @@ GB/s and TFLOP/s against the algorithmic work. Small enough to run under ncu.
     python -m simdonnx_b200.kernel_bench --op pw --batch 64 --hw 80 --cin 64 --cout 128 --iters 20
 ops: pw (1x1 conv, tensor cores), conv3 (3x3 s1, tensor cores), dw (depthwise), stem (3x3 s2 from
 fp32 NCHW), convt (2x2 s2 ConvTranspose), gate (squeeze-excitation gate), copy (torch copy, the
-HBM reference point)
+HBM reference point), fill (write-only reference), expand (1:2 read:write reference, torch cat)
 """
 from __future__ import annotations
 
@@ -85,6 +85,19 @@ def main():
         b1, b2 = torch.zeros(r, device=dev), torch.zeros(ci, device=dev)
         run = lambda: B.channel_gate(be, x, w1, b1, w2, b2)
         byts = x.numel() * 2
+        shape = dict(n=n, h=hw, w=hw, c=ci)
+    elif a.op == "fill":
+        # write-only reference: bytes / time of a plain fill of the output-sized tensor
+        y = torch.empty((n, hw, hw, co), device=dev).half()
+        run = lambda: y.fill_(1.0)
+        byts = y.numel() * 2
+        shape = dict(n=n, h=hw, w=hw, c=co)
+    elif a.op == "expand":
+        # 1:2 read:write reference (the pointwise conv's traffic shape): y = cat(x, x) on channels
+        x = torch.randn((n, hw, hw, ci), device=dev).half()
+        y = torch.empty((n, hw, hw, 2 * ci), device=dev).half()
+        run = lambda: torch.cat([x, x], dim=-1, out=y)
+        byts = x.numel() * 2 + y.numel() * 2
         shape = dict(n=n, h=hw, w=hw, c=ci)
     elif a.op == "copy":
         x = torch.randn((n, hw, hw, ci), device=dev).half()
