@@ -159,7 +159,8 @@ typedef struct sdx_conv_desc {
   sdx_dptr gap_sums; /* fp32 [batch * oh * ow / 32, oc]: channel sums of y over each run of 32 pixels
                         (the global average pool of a following SE gate, fused: pass it as that gate's
                         `sums`), or 0. 1x1 tensor-core route with the fp16 TMA-store epilogue
-                        (y fp16, oc % 16 == 0, 16-byte aligned rows); (batch * oh * ow) % 32 == 0 */
+                        (y fp16, oc 16, 32, 64 or a multiple of 128, 16-byte aligned rows);
+                        (batch * oh * ow) % 32 == 0 */
 } sdx_conv_desc;
 int sdx_conv2d(sdx_ctx* ctx, const sdx_conv_desc* d, sdx_stream s);
 

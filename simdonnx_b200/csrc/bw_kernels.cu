@@ -555,6 +555,92 @@ __global__ void gate_fc2_kernel(GateArgs a, const float* __restrict__ hid) {
   }
 }
 
+// Whole gate of one image in one CTA, from the producing conv's 32-pixel sums: column sums of the
+// image's hw / 32 rows (fixed lane and row order, so batch-independent), the mean, FC1 (+relu) and
+// FC2 with the gate, one warp per output row of each FC. smem: [lanes][c] reduction, mean[c], hid[r].
+__global__ void __launch_bounds__(256) gate_sums_kernel(GateArgs a) {
+  extern __shared__ float gsm[];
+  const int n = blockIdx.x, c = a.c, rows = a.hw >> 5;
+  const int cg = c >> 3, lanes_p = blockDim.x / cg;
+  float* red = gsm;                      // [lanes_p][c]
+  float* mean = red + lanes_p * c;       // [c]
+  float* hid = mean + c;                 // [r]
+  const int g = threadIdx.x % cg, lp = threadIdx.x / cg;
+  if (lp < lanes_p) {
+    float acc[8] = {0, 0, 0, 0, 0, 0, 0, 0};
+    const float* base = a.sums + (int64_t)n * rows * c + g * 8;
+    int p = lp;
+    for (; p + 3 * lanes_p < rows; p += 4 * lanes_p) {
+      float v[4][8];
+#pragma unroll
+      for (int k = 0; k < 4; k++) ld8f(base + (int64_t)(p + k * lanes_p) * c, v[k]);
+#pragma unroll
+      for (int k = 0; k < 4; k++)
+#pragma unroll
+        for (int j = 0; j < 8; j++) acc[j] += v[k][j];
+    }
+    for (; p < rows; p += lanes_p) {
+      float v[8];
+      ld8f(base + (int64_t)p * c, v);
+#pragma unroll
+      for (int j = 0; j < 8; j++) acc[j] += v[j];
+    }
+#pragma unroll
+    for (int j = 0; j < 8; j++) red[lp * c + g * 8 + j] = acc[j];
+  }
+  __syncthreads();
+  const float inv = 1.0f / (float)a.hw;
+  for (int ch = threadIdx.x; ch < c; ch += blockDim.x) {
+    float sum = 0.0f;
+    for (int l = 0; l < lanes_p; l++) sum += red[l * c + ch];
+    mean[ch] = sum * inv;
+  }
+  __syncthreads();
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, nw = blockDim.x >> 5;
+  // FC1, four hidden units per warp pass (their weight rows' loads in flight together)
+  for (int j0 = warp * 4; j0 < a.r; j0 += nw * 4) {
+    float sum[4] = {0.0f, 0.0f, 0.0f, 0.0f};
+#pragma unroll 2
+    for (int k = lane; k < c; k += 32) {
+      const float m = mean[k];
+#pragma unroll
+      for (int u = 0; u < 4; u++)
+        if (j0 + u < a.r) sum[u] = fmaf(__ldg(a.w1 + (int64_t)(j0 + u) * c + k), m, sum[u]);
+    }
+#pragma unroll
+    for (int u = 0; u < 4; u++) {
+#pragma unroll
+      for (int off = 16; off; off >>= 1) sum[u] += __shfl_xor_sync(0xffffffffu, sum[u], off);
+      if (lane == 0 && j0 + u < a.r) {
+        const float h = sum[u] + (a.b1 ? a.b1[j0 + u] : 0.0f);
+        hid[j0 + u] = a.act1_relu ? fmaxf(h, 0.0f) : h;
+      }
+    }
+  }
+  __syncthreads();
+  // FC2 and the gate, four channels per warp pass
+  for (int c0 = warp * 4; c0 < c; c0 += nw * 4) {
+    float z[4] = {0.0f, 0.0f, 0.0f, 0.0f};
+#pragma unroll 2
+    for (int j = lane; j < a.r; j += 32) {
+      const float h = hid[j];
+#pragma unroll
+      for (int u = 0; u < 4; u++)
+        if (c0 + u < c) z[u] = fmaf(__ldg(a.w2 + (int64_t)(c0 + u) * a.r + j), h, z[u]);
+    }
+#pragma unroll
+    for (int u = 0; u < 4; u++) {
+#pragma unroll
+      for (int off = 16; off; off >>= 1) z[u] += __shfl_xor_sync(0xffffffffu, z[u], off);
+      if (lane == 0 && c0 + u < c) {
+        const float zz = z[u] + (a.b2 ? a.b2[c0 + u] : 0.0f);
+        const float gv = a.hard ? __saturatef(zz * a.alpha + a.beta) : 1.0f / (1.0f + expf(-zz));
+        a.s[(int64_t)n * c + c0 + u] = gv + a.offset;
+      }
+    }
+  }
+}
+
 int gate_launch(const GateArgs& a, cudaStream_t st) {
   if (a.c % 8 != 0 || a.c > 4096) return set_error(SDX_ERR_NOT_SUPPORTED, "channel gate: c must be a multiple of 8, <= 4096");
   if (a.r < 1 || a.r > a.c) return set_error(SDX_ERR_NOT_SUPPORTED, "channel gate: hidden width must be in 1..c");
@@ -562,6 +648,16 @@ int gate_launch(const GateArgs& a, cudaStream_t st) {
   if (a.sums && a.hw % 32 != 0) return set_error(SDX_ERR_NOT_SUPPORTED, "channel gate: 32-pixel sums need hw % 32 == 0");
   if (a.sums && (reinterpret_cast<uintptr_t>(a.sums) & 15))
     return set_error(SDX_ERR_INVALID, "channel gate: sums must be 16-byte aligned");
+  if (a.sums && a.c <= 2048) {
+    // one CTA per image: the 32-pixel sums are small enough to reduce where the FCs run
+    const int lanes = 256 / (a.c / 8);
+    const size_t smem = sizeof(float) * ((size_t)std::max(1, lanes) * a.c + a.c + a.r);
+    if (lanes >= 1 && smem <= 48 * 1024) {
+      if (a.batch > 0) gate_sums_kernel<<<a.batch, 256, smem, st>>>(a);
+      SDX_LAUNCH_CHECK("gate_sums");
+      return SDX_OK;
+    }
+  }
   const int chunks = a.sums ? gate_sum_chunks(a.hw, a.c) : gate_chunks(a.hw, a.c);
   const int cg = a.c / 8;
   int block = std::max(cg, std::min(256, (256 / cg) * cg));

@@ -1361,15 +1361,13 @@ __global__ void __launch_bounds__(tc_threads(G), 1)
 // ------------------------------------------------------------------------------------------
 // host side
 // ------------------------------------------------------------------------------------------
-// N tile: the whole N when it is at most 64 columns, else 128-column tiles.
+// N tile: ceil(N / 128) tiles of equal width, each rounded up to 16 columns (96 -> one 96-column
+// tile, 192 -> two of 96), so that no MMA column or epilogue chunk is spent past N when N is not a
+// power of two.
 void tc_plan_n(int N, int* BN, int* n_tiles) {
-  if (N <= 64) {
-    *BN = (N + 15) / 16 * 16;
-    *n_tiles = 1;
-  } else {
-    *BN = 128;
-    *n_tiles = (N + 127) / 128;
-  }
+  const int nt = (N + 127) / 128;
+  *n_tiles = nt;
+  *BN = ((N + nt - 1) / nt + 15) / 16 * 16;
 }
 
 // ConvT columns (dy, dx, o), tap-major: one tile holds whole dy rows (kw*OC <= 64) or 128-column
@@ -1383,8 +1381,12 @@ void tc_plan_n_convt(int kh, int kw, int OC, int* BN, int* n_tiles) {
   } else if (row % 128 == 0) {
     *BN = 128;
     *n_tiles = N / 128;
+  } else if (N <= 64) {
+    *BN = (N + 15) / 16 * 16;
+    *n_tiles = 1;
   } else {
-    tc_plan_n(N, BN, n_tiles);
+    *BN = 128;
+    *n_tiles = (N + 127) / 128;
   }
 }
 
@@ -1643,8 +1645,9 @@ int tc_launch(const TcProblem& p, cudaStream_t stream) {
     G = std::min(cw, row);
     if (row % G != 0 || BN % G != 0) G = 0;
   } else {
+    // the widest store group (at most one 128-byte row) that divides the tile
     G = BN * esz >= 128 ? cw : BN;
-    if (BN % G != 0) G = 0;
+    while (G > 0 && BN % G != 0) G = G % 2 == 0 && G / 2 >= 16 / esz * 2 ? G / 2 : 0;
   }
   // 16-column epilogue chunks must not straddle groups
   bool tma_out = G > 0 && G % 16 == 0 && aligned16(p.out) && (p.out_pix_stride * esz) % 16 == 0 &&
@@ -1743,7 +1746,7 @@ int tc_launch(const TcProblem& p, cudaStream_t stream) {
                 (reinterpret_cast<uintptr_t>(p.gap) & 7)))
     return set_error(SDX_ERR_NOT_SUPPORTED,
                      "tc: fused channel sums need a 1x1 conv with the fp16 TMA-store epilogue, rows % 32 == 0, "
-                     "oc % 16 == 0 and an 8-byte aligned sums buffer");
+                     "oc 16, 32, 64 or a multiple of 128 and an 8-byte aligned sums buffer");
   if (chain) a.bias_smem = BN + 4 * p.convt_oc + 4;  // first bias, second ConvT's weights and bias
   const bool eg4 = !p.kxn && 4 * BN <= 512 && (BN <= 64 || chain || (!fast && !kxn_fast));
   for (int eg = eg4 ? 4 : 2; eg >= 2 && !planned; eg -= 2) {

@@ -234,7 +234,7 @@ def cuda_rewrite(plan: ExecPlan) -> ExecPlan:
         if not (m.p.group == 1 and m.p.pool is None and tuple(m.p.kernel) == (1, 1) and
                 tuple(m.p.strides) == (1, 1) and not any(m.p.pads) and getattr(m.p, "in_scale", None) is None and
                 xv.dtype == "f16" and xv.layout == "nhwc" and len(xv.shape) == 4 and xv.shape[3] % 8 == 0 and
-                yv.dtype == "f16" and yv.layout == "nhwc" and W.shape[0] % 16 == 0 and
+                yv.dtype == "f16" and yv.layout == "nhwc" and (W.shape[0] in (16, 32, 64) or W.shape[0] % 128 == 0) and
                 (addv is None or (addv.dtype == "f16" and addv.layout == "nhwc" and not addv.alias))):
             continue
         if yv.alias and (P.shape(yv.alias[0])[3] % 8 or yv.alias[1] % 8):
