@@ -532,6 +532,15 @@ __device__ __forceinline__ void epi_chunk(const TcArgs& a, float (&v)[16], int c
   }
 }
 
+// (a0, a1) += h * (w0, w1) as one packed f32x2 FMA (sm_100); each lane is the single-rounding fmaf.
+__device__ __forceinline__ void ffma2_pair(float& a0, float& a1, float h, float w0, float w1) {
+  asm("{\n\t.reg .b64 ra, rh, rw;\n\t"
+      "mov.b64 ra, {%0, %1};\n\tmov.b64 rh, {%2, %2};\n\tmov.b64 rw, {%3, %4};\n\t"
+      "fma.rn.f32x2 ra, rh, rw, ra;\n\tmov.b64 {%0, %1}, ra;\n\t}"
+      : "+f"(a0), "+f"(a1)
+      : "f"(h), "f"(w0), "f"(w1));
+}
+
 // Two-float packed add (sm_100 f32x2 pipe: one instruction for both lanes of the pair).
 __device__ __forceinline__ float2 add_f32x2(float2 a, float2 b) {
   uint64_t x, y, d;
@@ -672,10 +681,8 @@ __device__ __forceinline__ void chain_row(const TcArgs& a, uint32_t tbase, const
       for (int dx1 = 0; dx1 < 2; dx1++) {
         const float h = act_t<ACT>(v[dx1 * OC1 + c] + bb);
         const int r0 = 2 * hf, c0 = 2 * dx1;  // tap1 = (hf, dx1)
-        blk[r0 * 4 + c0] = fmaf(h, w.x, blk[r0 * 4 + c0]);
-        blk[r0 * 4 + c0 + 1] = fmaf(h, w.y, blk[r0 * 4 + c0 + 1]);
-        blk[(r0 + 1) * 4 + c0] = fmaf(h, w.z, blk[(r0 + 1) * 4 + c0]);
-        blk[(r0 + 1) * 4 + c0 + 1] = fmaf(h, w.w, blk[(r0 + 1) * 4 + c0 + 1]);
+        ffma2_pair(blk[r0 * 4 + c0], blk[r0 * 4 + c0 + 1], h, w.x, w.y);
+        ffma2_pair(blk[(r0 + 1) * 4 + c0], blk[(r0 + 1) * 4 + c0 + 1], h, w.z, w.w);
       }
     }
   }
