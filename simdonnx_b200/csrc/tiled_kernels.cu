@@ -1069,6 +1069,253 @@ __device__ __forceinline__ void stem_tile_compute(const DirectArgs& a, const flo
   }
 }
 
+// ---- tensor-core form of the det stem, warp-specialised like the tensor-core conv: warp 0 streams
+// the fp32 input tiles (TMA, two buffers), warps 2-5 build im2col rows of 128-pixel M blocks into a
+// ring of shared-memory slots, warp 1 issues the MMAs of each block into a ring of TMEM
+// accumulators, warps 6-9 drain them (bias, activation, fp16 NHWC stores). Every hand-off is an
+// mbarrier, so building, MMAs, draining and loading overlap. A row = one output pixel, K = 27 taps
+// (k = (ky*3 + kx)*3 + c, padded to 32) of fp16-rounded inputs in 64-byte rows under the 64-byte
+// swizzle; B = the 16 filters as fp16 hi and lo terms (the same layout), fp32 accumulation.
+constexpr int STEM_TC_TH = 8;
+constexpr int STEM_TC_IH = 2 * STEM_TC_TH + 1;                   // 17 input rows
+constexpr int STEM_TC_NBUF = 5;                                   // input tiles in flight or in use
+constexpr int STEM_TC_NB = STEM_TC_TH * STEM_TW / 128;           // 4 M blocks per tile
+constexpr int STEM_TC_NA = 4;                                     // im2col slots
+constexpr int STEM_TC_NACC = 4;                                   // TMEM accumulators (16 columns each)
+constexpr uint32_t STEM_TC_A_BYTES = 128u * 64u;                  // one block's im2col rows
+constexpr uint32_t STEM_TC_B_BYTES = 16u * 64u;                   // the filters
+constexpr uint32_t STEM_TC_TMEM_COLS = 64u;
+constexpr int STEM_TC_THREADS = 320;                              // 10 warps
+
+// Builds the filter rows as fp16 hi and lo terms (w = hi + lo to ~22 bits; one term leaves a
+// weight error common to every pixel, which the det network amplifies past the parity bound): row n,
+// column k = tap * 3 + c, swizzled like the A rows; the lo term STEM_TC_B_BYTES after the hi term.
+__device__ __forceinline__ void stem_tc_weights(const float* sw, uint32_t b0, int tid, int nthreads) {
+  for (int e = tid; e < 16 * 32; e += nthreads) {
+    const int n = e >> 5, k = e & 31;
+    const float w = k < 27 ? sw[k * 16 + n] : 0.0f;
+    const __half h = __float2half_rn(w);
+    const __half l = __float2half_rn(w - __half2float(h));
+    const uint32_t off = (uint32_t)n * 64u + ((((uint32_t)k >> 3) ^ (((uint32_t)n >> 1) & 3u)) << 4) + ((uint32_t)k & 7u) * 2u;
+    asm volatile("st.shared.b16 [%0], %1;" ::"r"(b0 + off), "h"(__half_as_ushort(h)) : "memory");
+    asm volatile("st.shared.b16 [%0], %1;" ::"r"(b0 + STEM_TC_B_BYTES + off), "h"(__half_as_ushort(l)) : "memory");
+  }
+}
+
+// im2col row `row` (0 .. 127) of block `blk` of the staged tile ([3][IH][STEM_IW] fp32, column
+// 2j + 3 + kx under tap kx) into the slot at `slot`.
+__device__ __forceinline__ void stem_tc_row(const float* tile, uint32_t slot, int blk, int row) {
+  const int p = blk * 128 + row;
+  const int r = p >> 6, j = p & 63;
+  float xs[32];
+#pragma unroll
+  for (int c = 0; c < 3; c++)
+#pragma unroll
+    for (int ky = 0; ky < 3; ky++) {
+      const float* rp = tile + (c * STEM_TC_IH + 2 * r + ky) * STEM_IW + 2 * j + 2;
+      const float2 p0 = *reinterpret_cast<const float2*>(rp);
+      const float2 p1 = *reinterpret_cast<const float2*>(rp + 2);
+      xs[(ky * 3 + 0) * 3 + c] = p0.y;
+      xs[(ky * 3 + 1) * 3 + c] = p1.x;
+      xs[(ky * 3 + 2) * 3 + c] = p1.y;
+    }
+#pragma unroll
+  for (int k = 27; k < 32; k++) xs[k] = 0.0f;
+  const uint32_t base = slot + (uint32_t)row * 64u;
+  const uint32_t xr = ((uint32_t)row >> 1) & 3u;
+#pragma unroll
+  for (int u = 0; u < 4; u++) {
+    uint4 q;
+    __half2* h = reinterpret_cast<__half2*>(&q);
+#pragma unroll
+    for (int i = 0; i < 4; i++) h[i] = __floats2half2_rn(xs[8 * u + 2 * i], xs[8 * u + 2 * i + 1]);
+    asm volatile("st.shared.v4.b32 [%0], {%1, %2, %3, %4};" ::"r"(base + (((uint32_t)u ^ xr) << 4)), "r"(q.x),
+                 "r"(q.y), "r"(q.z), "r"(q.w)
+                 : "memory");
+  }
+}
+
+template <int ACT>
+__global__ void __launch_bounds__(STEM_TC_THREADS, 1) stem_tc_kernel(const __grid_constant__ CUtensorMap tmX,
+                                                                    DirectArgs a, int tiles_x, int tiles_per_img,
+                                                                    int total) {
+  constexpr int IC = 3, OC = 16, K = 3;
+  constexpr uint32_t kTileBytes = IC * STEM_TC_IH * STEM_IW * 4;
+  constexpr uint32_t kBufBytes = (kTileBytes + 1023u) & ~1023u;  // TMA destinations 1024-aligned
+  extern __shared__ uint8_t ssm_raw[];
+  uint8_t* ssm = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(ssm_raw) + 1023) & ~uintptr_t(1023));
+  float* bufs = reinterpret_cast<float*>(ssm);                                  // [NBUF][IC][IH][IW]
+  uint8_t* sA = ssm + STEM_TC_NBUF * kBufBytes;                                 // [NA][128][64 B]
+  uint8_t* sB = sA + STEM_TC_NA * STEM_TC_A_BYTES;                              // [2 terms][16][64 B]
+  float* sw = reinterpret_cast<float*>(sB + 2 * STEM_TC_B_BYTES);               // [K*K][IC][OC]
+  float* sb = sw + K * K * IC * OC;                                             // [OC]
+  uint64_t* tfull = reinterpret_cast<uint64_t*>(sb + OC);                       // [NBUF] tile landed
+  uint64_t* tempty = tfull + STEM_TC_NBUF;                                      // [NBUF] tile consumed (128)
+  uint64_t* afull = tempty + STEM_TC_NBUF;                                      // [NA] rows built (128)
+  uint64_t* aempty = afull + STEM_TC_NA;                                        // [NA] rows read (commit)
+  uint64_t* accf = aempty + STEM_TC_NA;                                         // [NACC] MMAs done (commit)
+  uint64_t* acce = accf + STEM_TC_NACC;                                         // [NACC] drained (128)
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(acce + STEM_TC_NACC);
+  __shared__ int abort_flag;
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const int per = (total + gridDim.x - 1) / gridDim.x;
+  const int t0 = blockIdx.x * per, t1 = min(total, t0 + per);
+  if (t0 >= t1) return;
+  const int ntiles = t1 - t0;
+  auto decode = [&](int t, int& n, int& oy0, int& ox0) {
+    n = t / tiles_per_img;
+    const int q = t - n * tiles_per_img;
+    const int ty = q / tiles_x;
+    oy0 = ty * STEM_TC_TH;
+    ox0 = (q - ty * tiles_x) * STEM_TW;
+  };
+  for (int i = tid; i < K * K * IC * OC; i += blockDim.x) sw[i] = __ldg(a.w + i);
+  for (int i = tid; i < OC; i += blockDim.x) sb[i] = a.bias ? __ldg(a.bias + i) : 0.0f;
+  if (tid == 0) {
+    abort_flag = 0;
+    for (int i = 0; i < STEM_TC_NBUF; i++) {
+      mbar_init(smem_u32(&tfull[i]), 1);
+      mbar_init(smem_u32(&tempty[i]), 128);
+    }
+    for (int i = 0; i < STEM_TC_NA; i++) {
+      mbar_init(smem_u32(&afull[i]), 128);
+      mbar_init(smem_u32(&aempty[i]), 1);
+    }
+    for (int i = 0; i < STEM_TC_NACC; i++) {
+      mbar_init(smem_u32(&accf[i]), 1);
+      mbar_init(smem_u32(&acce[i]), 128);
+    }
+    mbar_fence_init();
+    tma_prefetch_desc(&tmX);
+  }
+  if (warp == 1) {
+    tmem_alloc(smem_u32(tmem_slot), STEM_TC_TMEM_COLS);
+    tmem_relinquish();
+  }
+  __syncthreads();
+  stem_tc_weights(sw, smem_u32(sB), tid, blockDim.x);
+  fence_async_smem_cta();  // the filter rows are read by the tensor cores (async proxy)
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+  const uint32_t ld = elect_leader();  // warp-uniform issue from the elected lane (warps 0 and 1)
+  const int nblk = ntiles * STEM_TC_NB;
+  uint32_t issued[STEM_TC_NBUF] = {};  // warp 0: copies per buffer
+  int mma_done = 0;             // warp 1: blocks whose MMAs were committed
+
+  if (warp == 0) {
+    // ---- input tiles
+    for (int i = 0; i < ntiles; i++) {
+      const int b = i % STEM_TC_NBUF, use = i / STEM_TC_NBUF;
+      if (use > 0 && !mbar_wait(smem_u32(&tempty[b]), (uint32_t)(use - 1) & 1u, a.err, SDX_DEV_WAIT_EMPTY,
+                                &abort_flag))
+        break;
+      int n, oy0, ox0;
+      decode(t0 + i, n, oy0, ox0);
+      const uint32_t bar = smem_u32(&tfull[b]);
+      mbar_arrive_expect_tx_p(ld, bar, kTileBytes);
+      tma_load_4d_p(ld, smem_u32(bufs + b * (kBufBytes / 4)), &tmX, bar, ox0 * 2 - a.pl - 3, oy0 * 2 - a.pt, 0, n);
+      issued[b]++;
+    }
+  } else if (warp == 1) {
+    // ---- MMAs: two k-steps per block into accumulator g % NACC
+    constexpr uint32_t idesc = umma_idesc_f16(128, 16);
+    const uint64_t bd = umma_desc_kmajor(smem_u32(sB), 64);
+    for (int g = 0; g < nblk; g++) {
+      const int sl = g % STEM_TC_NA, ac = g % STEM_TC_NACC;
+      bool ok = mbar_wait(smem_u32(&afull[sl]), (uint32_t)(g / STEM_TC_NA) & 1u, a.err, SDX_DEV_WAIT_FULL, &abort_flag);
+      if (ok && g >= STEM_TC_NACC)
+        ok = mbar_wait(smem_u32(&acce[ac]), (uint32_t)(g / STEM_TC_NACC - 1) & 1u, a.err, SDX_DEV_WAIT_ACC_EMPTY,
+                       &abort_flag);
+      if (!__all_sync(0xffffffffu, ok)) break;
+      tc_fence_after();
+      const uint64_t ad = umma_desc_kmajor(smem_u32(sA) + (uint32_t)sl * STEM_TC_A_BYTES, 64);
+      const uint32_t d = tmem + (uint32_t)(16 * ac);
+      const uint64_t bl = bd + (STEM_TC_B_BYTES >> 4);  // the lo term
+      umma_f16_p(ld, d, ad, bd, idesc, 0u);
+      umma_f16_p(ld, d, ad, bl, idesc, 1u);
+      umma_f16_p(ld, d, ad + 2u, bd + 2u, idesc, 1u);
+      umma_f16_p(ld, d, ad + 2u, bl + 2u, idesc, 1u);
+      tc_commit_p(ld, smem_u32(&aempty[sl]));
+      tc_commit_p(ld, smem_u32(&accf[ac]));
+      mma_done = g + 1;
+    }
+  } else if (warp >= 2 && warp < 6) {
+    // ---- im2col rows: thread = one row of every block
+    const int row = tid - 64;
+    for (int i = 0; i < ntiles; i++) {
+      const int b = i % STEM_TC_NBUF;
+      bool ok = mbar_wait(smem_u32(&tfull[b]), (uint32_t)(i / STEM_TC_NBUF) & 1u, a.err, SDX_DEV_WAIT_FULL,
+                          &abort_flag);
+      if (!ok) break;
+      const float* tile = bufs + b * (kBufBytes / 4);
+      for (int blk = 0; blk < STEM_TC_NB && ok; blk++) {
+        const int g = i * STEM_TC_NB + blk, sl = g % STEM_TC_NA;
+        if (g >= STEM_TC_NA)
+          ok = mbar_wait(smem_u32(&aempty[sl]), (uint32_t)(g / STEM_TC_NA - 1) & 1u, a.err, SDX_DEV_WAIT_EMPTY,
+                         &abort_flag);
+        if (!ok) break;
+        stem_tc_row(tile, smem_u32(sA) + (uint32_t)sl * STEM_TC_A_BYTES, blk, row);
+        fence_async_smem_cta();
+        mbar_arrive(smem_u32(&afull[sl]));
+      }
+      if (!ok) break;
+      mbar_arrive(smem_u32(&tempty[b]));
+    }
+  } else if (warp >= 6 && warp < 10) {
+    // ---- drain: warp w reads TMEM lanes 32 (w % 4) .. of each accumulator
+    const int q = warp & 3;
+    for (int g = 0; g < nblk; g++) {
+      const int ac = g % STEM_TC_NACC;
+      const bool ok = __all_sync(0xffffffffu, mbar_wait(smem_u32(&accf[ac]), (uint32_t)(g / STEM_TC_NACC) & 1u, a.err,
+                                                        SDX_DEV_WAIT_ACC_FULL, &abort_flag));
+      if (!ok) break;
+      tc_fence_after();
+      float v[16];
+      tmem_ld16_issue(tmem + ((uint32_t)(q * 32) << 16) + (uint32_t)(16 * ac), v);
+      tmem_wait_ld();
+      tmem_ld_wait16(v);
+      tc_fence_before();
+      mbar_arrive(smem_u32(&acce[ac]));
+      const int i = g / STEM_TC_NB, blk = g - i * STEM_TC_NB;
+      int n, oy0, ox0;
+      decode(t0 + i, n, oy0, ox0);
+      const int p = blk * 128 + q * 32 + lane;
+      const int oy = oy0 + (p >> 6), ox = ox0 + (p & 63);
+      if (oy < a.oh && ox < a.ow) {
+        __half* yp = static_cast<__half*>(a.y) + (((int64_t)n * a.oh + oy) * a.ow + ox) * a.y_pix_stride + a.y_ch_off;
+#pragma unroll
+        for (int h8 = 0; h8 < 2; h8++) {
+          uint4 u;
+          __half2* hh = reinterpret_cast<__half2*>(&u);
+#pragma unroll
+          for (int k = 0; k < 4; k++) {
+            const int o = h8 * 8 + 2 * k;
+            hh[k] = __floats2half2_rn(act_t<ACT>(v[o] + sb[o]), act_t<ACT>(v[o + 1] + sb[o + 1]));
+          }
+          reinterpret_cast<uint4*>(yp)[h8] = u;
+        }
+      }
+    }
+  }
+  // wind-down: copies in flight must land and committed MMAs finish before smem and TMEM go away
+  if (warp == 0) {
+    for (int b = 0; b < STEM_TC_NBUF; b++)
+      if (issued[b] > 0) mbar_wait_drain(smem_u32(&tfull[b]), (issued[b] - 1) & 1u, a.err, SDX_DEV_WAIT_DRAIN);
+  }
+  if (warp == 1 && mma_done > 0) {
+    const int g = mma_done - 1;
+    mbar_wait_drain(smem_u32(&accf[g % STEM_TC_NACC]), (uint32_t)(g / STEM_TC_NACC) & 1u, a.err, SDX_DEV_WAIT_DRAIN);
+  }
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc(tmem, STEM_TC_TMEM_COLS);
+  }
+}
+
 template <int ACT>
 __global__ void __launch_bounds__(256, 2) stem_tma_kernel(const __grid_constant__ CUtensorMap tmX, DirectArgs a,
                                                        int tiles_x, int tiles_per_img, int total) {
@@ -1170,6 +1417,47 @@ static bool stem_tma_launch_t(const DirectArgs& a, cudaStream_t st) {
   return true;
 }
 
+// Shared memory of stem_tc_kernel and its launch: one persistent CTA per SM over contiguous tile
+// ranges.
+template <int ACT>
+static bool stem_tc_run(const CUtensorMap& map, const DirectArgs& a, cudaStream_t st) {
+  const size_t buf = ((size_t)3 * STEM_TC_IH * STEM_IW * 4 + 1023) & ~(size_t)1023;
+  const size_t smem = 1024 + STEM_TC_NBUF * buf + (size_t)STEM_TC_NA * STEM_TC_A_BYTES + 2 * STEM_TC_B_BYTES +
+                      sizeof(float) * (9 * 3 * 16 + 16) +
+                      sizeof(uint64_t) * (2 * STEM_TC_NBUF + 2 * STEM_TC_NA + 2 * STEM_TC_NACC) + 16;
+  static bool attr = false;
+  if (!attr) {
+    if (cudaFuncSetAttribute(stem_tc_kernel<ACT>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem) !=
+        cudaSuccess)
+      return false;
+    attr = true;
+  }
+  const int tiles_x = (a.ow + STEM_TW - 1) / STEM_TW, tiles_y = (a.oh + STEM_TC_TH - 1) / STEM_TC_TH;
+  const int64_t total = (int64_t)a.batch * tiles_x * tiles_y;
+  if (total <= 0 || total > INT32_MAX) return false;
+  int dev = 0;
+  cudaGetDevice(&dev);
+  const int grid = (int)std::min<int64_t>(total, (int64_t)num_sms(dev));  // one CTA per SM
+  stem_tc_kernel<ACT><<<grid, STEM_TC_THREADS, smem, st>>>(map, a, tiles_x, tiles_x * tiles_y, (int)total);
+  return true;
+}
+
+template <int ACT>
+static bool stem_tc_launch_t(const DirectArgs& a, cudaStream_t st) {
+  PFN_encodeTiled enc = get_encode_tiled();
+  if (!enc) return false;
+  CUtensorMap map;
+  const cuuint64_t dims[4] = {(cuuint64_t)a.iw, (cuuint64_t)a.ih, 3, (cuuint64_t)a.batch};
+  const cuuint64_t strides[3] = {(cuuint64_t)a.iw * 4, (cuuint64_t)a.ih * a.iw * 4, (cuuint64_t)3 * a.ih * a.iw * 4};
+  const cuuint32_t box[4] = {(cuuint32_t)STEM_IW, (cuuint32_t)STEM_TC_IH, 3, 1};
+  const cuuint32_t estr[4] = {1, 1, 1, 1};
+  if (enc(&map, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 4, const_cast<void*>(a.x), dims, strides, box, estr,
+          CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+          CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) != CUDA_SUCCESS)
+    return false;
+  return stem_tc_run<ACT>(map, a, st);
+}
+
 // ---- the det stem fed straight from u8 images (image session): the ImageToTensor normalisation
 // (lut, optional R/B swap, replicate placement of the image inside the tensor) runs while the tile
 // is filled, so the fp32 NCHW tensor is never written or read. One CTA per 16 x 64 output tile;
@@ -1256,9 +1544,9 @@ bool stem_tiled_launch(const DirectArgs& a, cudaStream_t st) {
       (reinterpret_cast<uintptr_t>(a.y) & 15u) == 0) {
     bool done = false;
     switch (a.act) {
-      case ACT_HARDSWISH: done = stem_tma_launch_t<ACT_HARDSWISH>(a, st); break;
-      case ACT_RELU: done = stem_tma_launch_t<ACT_RELU>(a, st); break;
-      case ACT_NONE: done = stem_tma_launch_t<ACT_NONE>(a, st); break;
+      case ACT_HARDSWISH: done = stem_tc_launch_t<ACT_HARDSWISH>(a, st) || stem_tma_launch_t<ACT_HARDSWISH>(a, st); break;
+      case ACT_RELU: done = stem_tc_launch_t<ACT_RELU>(a, st) || stem_tma_launch_t<ACT_RELU>(a, st); break;
+      case ACT_NONE: done = stem_tc_launch_t<ACT_NONE>(a, st) || stem_tma_launch_t<ACT_NONE>(a, st); break;
       default: break;
     }
     if (done) return true;

@@ -108,16 +108,18 @@ def test_conv_into_channel_slice(be):
     assert np.all(got[..., :48] == 0) and np.all(got[..., 72:] == 0)
 
 
-def test_stem_nchw_fp32_input(be):
-    """Graph-input stem: fp32 NCHW input read directly (boundary relayout fused), 3x3 s2, HardSwish."""
+@pytest.mark.parametrize("nb,ih,iw,act", [(2, 64, 48, "hardswish"), (3, 200, 260, "relu"), (1, 640, 640, "none")])
+def test_stem_nchw_fp32_input(be, nb, ih, iw, act):
+    """Graph-input stem: fp32 NCHW input read directly (boundary relayout fused), 3x3 s2; partial and
+    many-tile grids (the tensor-core form builds im2col rows per 128 output pixels)."""
     from simdonnx_b200 import backend as B
-    rng = np.random.default_rng(9)
-    x = rng.uniform(0, 1, size=(2, 3, 64, 48)).astype(np.float32)
+    rng = np.random.default_rng(9 + ih)
+    x = rng.uniform(0, 1, size=(nb, 3, ih, iw)).astype(np.float32)
     wt = rnd(rng, 16, 3, 3, 3, scale=0.5)
     b = rnd(rng, 16)
     ref = O.conv(np.ascontiguousarray(x.transpose(0, 2, 3, 1)), O.ConvPlan(wt, b), strides=(2, 2),
-                 pads=(1, 1, 1, 1), act="hardswish")
-    d = B.conv_desc(2, 64, 48, 3, 16, 3, 3, stride=(2, 2), pads=(1, 1, 1, 1), act="hardswish",
+                 pads=(1, 1, 1, 1), act=act)
+    d = B.conv_desc(nb, ih, iw, 3, 16, 3, 3, stride=(2, 2), pads=(1, 1, 1, 1), act=act,
                     x_dtype=torch.float32, x_layout=1)
     y = B.conv2d(be, d, dev32(x), B.pack_conv(d, wt), bias=dev32(b))
     assert_close(host(y), ref, "stem")
