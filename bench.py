@@ -147,6 +147,93 @@ def run_reference(args, rank: int) -> None:
     print(json.dumps(line), flush=True)
 
 
+def node_times(sess, N, roofline, torch, passes: int = 3):
+    """Per-node device times of a session: `passes` eager runs of its node list on the session
+    stream with a CUDA event between nodes; the median per node. Returns (rows, launches per pass)."""
+    n_nodes = sess.node_count()
+    stream = sess.stream
+    samples = [[] for _ in range(n_nodes)]
+    launches = 0
+    for _ in range(passes):
+        evs = [torch.cuda.Event(enable_timing=True) for _ in range(n_nodes + 1)]
+        before = int(N.lib().sdx_launch_count())
+        with torch.cuda.stream(stream):
+            evs[0].record(stream)
+            for i in range(n_nodes):
+                N.call("sdx_session_enqueue_node", sess.h, i)
+                evs[i + 1].record(stream)
+        evs[-1].synchronize()
+        launches = int(N.lib().sdx_launch_count()) - before
+        for i in range(n_nodes):
+            samples[i].append(evs[i].elapsed_time(evs[i + 1]))
+    rows = []
+    for i, node in enumerate(sess.plan.nodes):
+        cls, fl, by = roofline.node_cost(sess.plan, node)
+        t = statistics.median(samples[i])
+        rows.append({"node": node.name, "op": node.op, "kernel": cls, "ms": t, "bytes": by, "flops": fl,
+                     "gbs": by / t / 1e6 if t > 0 else None, "tflops": fl / t / 1e9 if t > 0 else None,
+                     "out": list(sess.plan.values[node.outs[0]].shape)})
+    return rows, launches
+
+
+def measure_extras(args, local, N, configs, roofline, torch, CudaInferenceSession) -> dict:
+    """Side measurements on this GPU (not the headline): the tensor-bound half of the hot path
+    (C4 UNet at N=16: images/s and, per 3x3 conv, TFLOP/s against the sustained bf16 peak), the
+    single fused node C1 (N=8) and C3 rec at N=64. Device-resident, CUDA events, K graph replays."""
+    dev = torch.device("cuda", local)
+    tc_peak = peaks_sustained()
+    hbm, _, _ = peaks()
+    out = {}
+    for key, build, batch in (("unet_c4", configs.build_unet, 16), ("c1", configs.build_c1, 8),
+                              ("rec_c3", configs.build_rec, 64)):
+        plan = build(batch=batch)
+        s = CudaInferenceSession(plan, device=local)
+        if plan.feeds_dev:
+            s.write_inputs({k: f(dev) for k, f in plan.feeds_dev.items()})
+        else:
+            s.write_inputs({k: f() for k, f in plan.feeds.items()})
+        for _ in range(args.warmup):
+            s.enqueue()
+        torch.cuda.synchronize()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record(s.stream)
+        for _ in range(args.steps):
+            s.enqueue()
+        e1.record(s.stream)
+        e1.synchronize()
+        ms = e0.elapsed_time(e1) / args.steps
+        rows, _ = node_times(s, N, roofline, torch)
+        tot = roofline.plan_totals(s.plan)
+        rec = {"batch": batch, "ms_per_step": ms, "images_per_s": batch / (ms / 1e3),
+               "whole_step_tflops": tot["flops"] / ms / 1e9, "whole_step_gbs": tot["bytes"] / ms / 1e6}
+        if key == "unet_c4":
+            convs = [r for r in rows if r["op"] == "Conv" and r["kernel"] == "conv_tc"]
+            tc_ms = sum(r["ms"] for r in convs)
+            tc_fl = sum(r["flops"] for r in convs)
+            rec["conv3x3_tc"] = {"launches": len(convs), "ms": tc_ms, "tflops": tc_fl / tc_ms / 1e9,
+                                 "frac_of_sustained_bf16": tc_fl / tc_ms / 1e9 / tc_peak,
+                                 "peak_tflops_sustained": tc_peak}
+            rec["per_conv"] = [{"node": r["node"], "out": r["out"], "ms": round(r["ms"], 4),
+                                "tflops": round(r["tflops"], 1),
+                                "frac_of_sustained_bf16": round(r["tflops"] / tc_peak, 3)} for r in convs]
+        else:
+            rec["node_ms_sum"] = sum(r["ms"] for r in rows)
+            rec["gbs"] = tot["bytes"] / ms / 1e6
+            rec["hbm_frac"] = tot["bytes"] / ms / 1e6 / hbm
+        out[key] = rec
+        s.close()
+    return out
+
+
+def peaks_sustained() -> float:
+    path = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    if os.path.exists(path):
+        with open(path) as f:
+            d = json.load(f)
+        return d.get("bf16_tflops_sustained", d["bf16_tflops"])
+    return 1400.0
+
+
 def main() -> None:
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -158,6 +245,8 @@ def main() -> None:
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--node-times", default="", help="write per-node timings (JSON) to this path")
+    ap.add_argument("--repeats", type=int, default=5, help="extra K-step timed regions (spread only)")
+    ap.add_argument("--no-extras", action="store_true", help="skip the UNet / C1 / rec side measurements")
     args = ap.parse_args()
     args.warmup = max(args.warmup, 3)
 
@@ -183,9 +272,11 @@ def main() -> None:
         dist.init_process_group("nccl", timeout=timedelta(seconds=180), device_id=torch.device("cuda", local))
 
     plan = configs.build_det(batch=args.batch, hw=HW)
-    feeds = {k: f() for k, f in plan.feeds.items()}
+    dev = torch.device("cuda", local)
+    # the seeded SplitMix64 input made on the device (bit-identical to synth.uniform, seconds not minutes)
+    feeds_dev = {k: f(dev) for k, f in plan.feeds_dev.items()}
     sess = CudaInferenceSession(plan, device=local)
-    sess.write_inputs(feeds)
+    sess.write_inputs(feeds_dev)
     stream = sess.stream
     launches0 = int(N.lib().sdx_launch_count())
 
@@ -216,28 +307,36 @@ def main() -> None:
     images = args.batch * world * args.steps
     value = images / (ms / 1e3)
 
-    # ---- per-node timing pass (eager, same stream): kernel classes and the dominant one
-    n_nodes = sess.node_count()
-    evs = [torch.cuda.Event(enable_timing=True) for _ in range(n_nodes + 1)]
-    before = int(N.lib().sdx_launch_count())
-    with torch.cuda.stream(stream):
-        evs[0].record(stream)
-        for i in range(n_nodes):
-            N.call("sdx_session_enqueue_node", sess.h, i)
-            evs[i + 1].record(stream)
-    evs[-1].synchronize()
-    launches_per_step = int(N.lib().sdx_launch_count()) - before
+    # ---- repeats of the same K-step region (spread of the device-resident figure inside this run)
+    rep_ms = []
+    for _ in range(args.repeats):
+        barrier()
+        r0, r1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        r0.record(stream)
+        for _ in range(args.steps):
+            sess.enqueue()
+        r1.record(stream)
+        r1.synchronize()
+        t = r0.elapsed_time(r1)
+        if world > 1:
+            tt = torch.tensor([t], device="cuda")
+            dist.all_reduce(tt, op=dist.ReduceOp.MAX)
+            t = float(tt.item())
+        rep_ms.append(t)
+    repeats = None
+    if rep_ms:
+        rv = sorted(images / (t / 1e3) for t in rep_ms)
+        repeats = {"n": len(rv), "steps_each": args.steps, "images_per_s_min": rv[0],
+                   "images_per_s_median": statistics.median(rv), "images_per_s_max": rv[-1]}
+
+    # ---- per-node timing passes (eager, same stream): kernel classes and the dominant one
+    per_node, launches_per_step = node_times(sess, N, roofline, torch)
     classes = {}
-    per_node = []
-    for i, node in enumerate(sess.plan.nodes):
-        cls, fl, by = roofline.node_cost(sess.plan, node)
-        t = evs[i].elapsed_time(evs[i + 1])
-        per_node.append({"node": node.name, "op": node.op, "kernel": cls, "ms": t, "bytes": by, "flops": fl,
-                         "gbs": by / t / 1e6 if t > 0 else None, "out": list(sess.plan.values[node.outs[0]].shape)})
-        c = classes.setdefault(cls, {"ms": 0.0, "flops": 0, "bytes": 0, "launches": 0})
-        c["ms"] += t
-        c["flops"] += fl
-        c["bytes"] += by
+    for r in per_node:
+        c = classes.setdefault(r["kernel"], {"ms": 0.0, "flops": 0, "bytes": 0, "launches": 0})
+        c["ms"] += r["ms"]
+        c["flops"] += r["flops"]
+        c["bytes"] += r["bytes"]
         c["launches"] += 1
     if args.node_times and rank == 0:
         with open(args.node_times, "w") as f:
@@ -259,6 +358,9 @@ def main() -> None:
                  "timing": "per-node CUDA events on the session stream, eager pass after the timed region"})
     tot = roofline.plan_totals(sess.plan)
     step_s = ms / 1e3 / args.steps
+    extras = None
+    if world == 1 and not args.no_extras:
+        extras = measure_extras(args, local, N, configs, roofline, torch, CudaInferenceSession)
     whole = {"algorithmic_bytes_per_step": tot["bytes"], "algorithmic_flops_per_step": tot["flops"],
              "hbm_gbs": tot["bytes"] / step_s / 1e9, "hbm_frac": tot["bytes"] / step_s / 1e9 / hbm}
 
@@ -291,6 +393,7 @@ def main() -> None:
     e2e = None
     if not args.no_e2e:
         # (1) fp32 tensor input (the plan measured above)
+        feeds = {k: t.cpu().numpy() for k, t in feeds_dev.items()}
         el_t, el_ts = e2e_measure(sess, feeds)
         tensor_e2e = {"value": images / el_t, "unit": "images/s", "h2d_bytes_per_step": sess.in_bytes,
                       "d2h_bytes_per_step": sess.out_bytes, "serial_value": images / el_ts}
@@ -298,7 +401,7 @@ def main() -> None:
         sess.close()
         # (2) image-session input: u8 RGB pixels, normalized on the device (sdx_image_to_tensor)
         iplan = configs.build_det(batch=args.batch, hw=HW, image_input=True)
-        ifeeds = {k: f() for k, f in iplan.feeds.items()}
+        ifeeds = {k: f(dev).cpu().numpy() for k, f in iplan.feeds_dev.items()}
         isess = CudaInferenceSession(iplan, device=local)
         el_i, el_is = e2e_measure(isess, ifeeds)
         e2e = {"value": images / el_i, "unit": "images/s", "h2d_bytes_per_step": isess.in_bytes,
@@ -307,8 +410,7 @@ def main() -> None:
                          "buffers: H2D of the step's images, D2H of its fp32 probability map) to "
                          "sdx_session_wait, max over ranks",
                "serial_value": images / el_is,
-               "serial_timing": "host wall clock around K synchronous sdx_session_run calls",
-               "fp32_tensor_input": tensor_e2e}
+               "serial_timing": "host wall clock around K synchronous sdx_session_run calls"}
         isess.close()
         del sess_bytes
 
@@ -328,7 +430,8 @@ def main() -> None:
             "roofline": roof, "whole_step": whole,
             "kernel_classes": {k: {"ms": round(v["ms"], 4), "launches": v["launches"]} for k, v in
                                sorted(classes.items(), key=lambda kv: -kv[1]["ms"])},
-            "cpu_baseline": cpu, "e2e": e2e, "gpu_launches": launches_per_step * args.steps,
+            "cpu_baseline": cpu, "e2e": e2e, "e2e_fp32_input": tensor_e2e if e2e else None,
+            "repeats": repeats, "extras": extras, "gpu_launches": launches_per_step * args.steps,
             "launches_per_step": launches_per_step, "clocks": clk,
         }
         print(json.dumps(line), flush=True)

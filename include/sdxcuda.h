@@ -233,7 +233,9 @@ int sdx_channel_gate(sdx_ctx* ctx, const sdx_gate_desc* d, sdx_stream s);
  *    else SDX_ERR_NOT_SUPPORTED (nothing enqueued); e.g. c = 512 with one pixel chunk allows
  *    1024 images.
  *  - The first call on a device looks up the array's device address (cudaGetSymbolAddress) and
- *    caches it; make that first call before beginning any stream capture on that device.
+ *    caches it; make that first call before beginning any stream capture on that device. The
+ *    cached address belongs to the device's primary context: after cudaDeviceReset (or anything
+ *    else that destroys that context) do not call this entry point again in the same process.
  *  - All calls on one device share the one array: two calls whose kernels overlap on the GPU
  *    (different streams, no ordering between them) race and give wrong gates. Order them on one
  *    stream or with events.

@@ -195,11 +195,10 @@ int direct_conv_launch(const DirectArgs& a, cudaStream_t st) {
     return SDX_OK;
   }
   SDX_ACT_DISPATCH(a.act, ACTC, {
-    static bool attr = false;
-    if (!attr) {
-      cudaFuncSetAttribute(direct_conv_kernel<ACTC>, cudaFuncAttributeMaxDynamicSharedMemorySize, 96 * 1024);
-      attr = true;
-    }
+    static SmemAttr attr{};
+    const int rc = raise_smem_limit(attr, (const void*)direct_conv_kernel<ACTC>, 96 * 1024,
+                                    "cudaFuncSetAttribute(direct_conv)");
+    if (rc) return rc;
     direct_conv_kernel<ACTC><<<grid_for(total, 256), 256, wbytes, st>>>(a);
   });
   SDX_LAUNCH_CHECK("direct_conv");
@@ -667,14 +666,11 @@ int gate_launch(const GateArgs& a, cudaStream_t st) {
   if (red > 48 * 1024) return set_error(SDX_ERR_NOT_SUPPORTED, "channel gate: reduction stage too large");
   const size_t fc1_smem = sizeof(float) * GATE_IMG * a.c, fc2_smem = sizeof(float) * GATE_IMG * a.r;
   if (fc1_smem > 160 * 1024) return set_error(SDX_ERR_NOT_SUPPORTED, "channel gate: too many channels for the FC stage");
-  static bool attr = false;
-  if (!attr) {
-    cudaError_t e = cudaFuncSetAttribute(gate_fc1_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, 160 * 1024);
-    if (e == cudaSuccess)
-      e = cudaFuncSetAttribute(gate_fc2_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, 160 * 1024);
-    if (e != cudaSuccess) return set_cuda_error(e, "cudaFuncSetAttribute(gate_fc)");
-    attr = true;
-  }
+  static SmemAttr attr1{}, attr2{};
+  int rc = raise_smem_limit(attr1, (const void*)gate_fc1_kernel, 160 * 1024, "cudaFuncSetAttribute(gate_fc1)");
+  if (rc == SDX_OK)
+    rc = raise_smem_limit(attr2, (const void*)gate_fc2_kernel, 160 * 1024, "cudaFuncSetAttribute(gate_fc2)");
+  if (rc) return rc;
   float* hid = a.partial + (size_t)a.batch * chunks * a.c;  // [batch][r], r <= c
   if (a.sums) gap_partial_kernel<float><<<dim3(chunks, a.batch), block, red, st>>>(a.sums, a.hw / 32, a.c, chunks, a.partial);
   else gap_partial_kernel<__half><<<dim3(chunks, a.batch), block, red, st>>>(a.x, a.hw, a.c, chunks, a.partial);
@@ -1073,11 +1069,9 @@ int attention_launch(int batch, int t, int heads, int d, float scale, const __ha
   const size_t smem = sizeof(float) * ((size_t)3 * t * d + (size_t)t * t);
   if (smem > 160 * 1024) return set_error(SDX_ERR_NOT_SUPPORTED, "attention: sequence too long for the smem kernel");
   if (batch * heads == 0) return SDX_OK;
-  static bool attr = false;
-  if (!attr) {
-    cudaFuncSetAttribute(attention_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, 160 * 1024);
-    attr = true;
-  }
+  static SmemAttr attr{};
+  const int rc = raise_smem_limit(attr, (const void*)attention_kernel, 160 * 1024, "cudaFuncSetAttribute(attention)");
+  if (rc) return rc;
   attention_kernel<<<batch * heads, 128, smem, st>>>(t, heads, d, scale, qkv, y);
   SDX_LAUNCH_CHECK("attention");
   return SDX_OK;

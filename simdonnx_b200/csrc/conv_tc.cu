@@ -1444,13 +1444,10 @@ static bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 
 template <int ACT, int EPI, int G>
 static int launch_tc(int dev, int grid, size_t smem, cudaStream_t stream, const CUtensorMap& mA, const CUtensorMap& mB,
                      const CUtensorMap& mOut, const CUtensorMap& mRes, const TcArgs& a) {
-  static bool attr_set[64] = {false};
-  if (dev >= 0 && dev < 64 && !attr_set[dev]) {
-    cudaError_t e = cudaFuncSetAttribute(conv_tc_kernel<ACT, EPI, G>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                         TC_SMEM_LIMIT);
-    if (e != cudaSuccess) return set_cuda_error(e, "cudaFuncSetAttribute(conv_tc)");
-    attr_set[dev] = true;
-  }
+  static SmemAttr attr{};
+  const int rc = raise_smem_limit(attr, (const void*)conv_tc_kernel<ACT, EPI, G>, TC_SMEM_LIMIT,
+                                  "cudaFuncSetAttribute(conv_tc)");
+  if (rc) return rc;
   conv_tc_kernel<ACT, EPI, G><<<grid, tc_threads(G), smem, stream>>>(mA, mB, mOut, mRes, a);
   cudaError_t e = cudaGetLastError();
   if (e != cudaSuccess) return set_cuda_error(e, "conv_tc launch");

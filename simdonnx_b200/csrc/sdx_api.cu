@@ -55,12 +55,30 @@ PFN_encodeTiled get_encode_tiled() {
 }
 
 int num_sms(int device) {
-  static int cache[64] = {0};
-  if (device >= 0 && device < 64 && cache[device]) return cache[device];
+  static std::atomic<int> cache[SDX_MAX_DEVICES];
+  const bool slot = device >= 0 && device < SDX_MAX_DEVICES;
+  if (slot) {
+    const int c = cache[device].load(std::memory_order_relaxed);
+    if (c) return c;
+  }
   int n = 148;
   cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, device);
-  if (device >= 0 && device < 64) cache[device] = n;
+  if (slot) cache[device].store(n, std::memory_order_relaxed);
   return n;
+}
+
+int raise_smem_limit(SmemAttr& rec, const void* fn, int bytes, const char* what) {
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return set_cuda_error(e, what);
+  if (dev < 0 || dev >= SDX_MAX_DEVICES) return set_error(SDX_ERR_INVALID, "%s: device ordinal %d out of range", what, dev);
+  if (rec.bytes[dev].load(std::memory_order_acquire) >= bytes) return SDX_OK;
+  e = cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes);
+  if (e != cudaSuccess) return set_cuda_error(e, what);
+  int cur = rec.bytes[dev].load(std::memory_order_relaxed);
+  while (cur < bytes && !rec.bytes[dev].compare_exchange_weak(cur, bytes, std::memory_order_release)) {
+  }
+  return SDX_OK;
 }
 
 // ---- host-side fault injection (tests only; never touches the GPU)

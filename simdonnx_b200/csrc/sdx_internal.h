@@ -6,6 +6,8 @@
 #include <stddef.h>
 #include <stdint.h>
 
+#include <atomic>
+
 #include "sdx_status.h"
 
 struct sdx_ctx {
@@ -29,6 +31,19 @@ typedef CUresult (*PFN_encodeTiled)(CUtensorMap*, CUtensorMapDataType, cuuint32_
 PFN_encodeTiled get_encode_tiled();
 int num_sms(int device);
 void count_launch();
+
+// Per-kernel, per-device record of the dynamic shared-memory limit already raised with
+// cudaFuncSetAttribute (the attribute belongs to the kernel on the CURRENT device: a process that
+// drives several GPUs must raise it on each). Zero-initialised as a function-local static.
+constexpr int SDX_MAX_DEVICES = 64;
+struct SmemAttr {
+  std::atomic<int> bytes[SDX_MAX_DEVICES];
+};
+// Raises `fn`'s dynamic shared-memory limit to at least `bytes` on the current device, once per
+// device (thread-safe: concurrent first calls both set the same value, which is idempotent). The
+// record is updated only after the call succeeded, so a failure (e.g. inside a stream capture) is
+// retried by the next launch. Returns SDX_OK or an SDX_ERR_CUDA status naming `what`.
+int raise_smem_limit(SmemAttr& rec, const void* fn, int bytes, const char* what);
 // fault injection: true when the call of `kind` must fail now (see sdx_fault_inject)
 bool inject_fire(int kind);
 enum { FAULT_MALLOC = 1, FAULT_LAUNCH = 2, FAULT_GRAPH = 3, FAULT_D2H = 4, FAULT_SYNC = 5 };

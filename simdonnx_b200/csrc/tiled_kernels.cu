@@ -125,21 +125,19 @@ __global__ void __launch_bounds__(256) dw_tiled_kernel(DwArgs a, int CS, int TH,
 }
 
 template <int ACT, int K, int S>
-static int dw_launch_t(const DwArgs& a, cudaStream_t st) {
+static bool dw_launch_t(const DwArgs& a, cudaStream_t st) {
   const int CS = a.c <= 64 ? a.c : 64;
   const int G = CS / 8;
   const int TW = 16, TH = (256 / G) / (TW / DW_R);
   const int IWt = (TW - 1) * S + K, IHt = (TH - 1) * S + K;
   const size_t smem = sizeof(float) * K * K * CS + (size_t)IHt * IWt * CS * 2;
-  static bool attr = false;
-  if (!attr) {
-    cudaFuncSetAttribute(dw_tiled_kernel<ACT, K, S>, cudaFuncAttributeMaxDynamicSharedMemorySize, 160 * 1024);
-    attr = true;
-  }
+  static SmemAttr attr{};
+  if (raise_smem_limit(attr, (const void*)dw_tiled_kernel<ACT, K, S>, 160 * 1024, "cudaFuncSetAttribute(dw_tiled)"))
+    return false;
   const int tiles_x = (a.ow + TW - 1) / TW, tiles_y = (a.oh + TH - 1) / TH;
   dim3 grid(tiles_x * tiles_y, a.c / CS, a.batch);
   dw_tiled_kernel<ACT, K, S><<<grid, 256, smem, st>>>(a, CS, TH, TW, tiles_x);
-  return SDX_OK;
+  return true;
 }
 
 // ---- persistent, TMA-fed form. Each CTA walks a contiguous range of tiles (image, channel slab,
@@ -327,11 +325,9 @@ static bool dw_tma_launch_t(const DwArgs& a, cudaStream_t st) {
           CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
           CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) != CUDA_SUCCESS)
     return false;
-  static bool attr = false;
-  if (!attr) {
-    cudaFuncSetAttribute(dw_tma_kernel<ACT, K, S, R>, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024);
-    attr = true;
-  }
+  static SmemAttr attr{};
+  if (raise_smem_limit(attr, (const void*)dw_tma_kernel<ACT, K, S, R>, 200 * 1024, "cudaFuncSetAttribute(dw_tma)"))
+    return false;
   const int tiles_x = (a.ow + TW - 1) / TW, tiles_y = (a.oh + TH - 1) / TH;
   const int slabs = a.c / CS;
   const int64_t total = (int64_t)a.batch * slabs * tiles_x * tiles_y;
@@ -634,12 +630,10 @@ static bool dw_slide_launch_cs(const DwArgs& a, cudaStream_t st) {
           CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
           CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) != CUDA_SUCCESS)
     return false;
-  static bool attr = false;
-  if (!attr) {
-    cudaFuncSetAttribute(dw_slide_kernel<ACT, K, RX, CPT, CS>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                         120 * 1024);
-    attr = true;
-  }
+  static SmemAttr attr{};
+  if (raise_smem_limit(attr, (const void*)dw_slide_kernel<ACT, K, RX, CPT, CS>, 120 * 1024,
+                       "cudaFuncSetAttribute(dw_slide)"))
+    return false;
   const int tiles_x = (a.ow + TW - 1) / TW, tiles_y = (a.oh + TH - 1) / TH;
   const int slabs = a.c / CS;
   const int64_t total = (int64_t)a.batch * slabs * tiles_x * tiles_y;
@@ -829,12 +823,10 @@ static bool dw_slide2_launch_cs(const DwArgs& a, cudaStream_t st) {
             CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
             CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) != CUDA_SUCCESS)
       return false;
-    static bool attr = false;
-    if (!attr) {
-      cudaFuncSetAttribute(dw_slide2_kernel<ACT, K, RX, CPT, CS>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                           120 * 1024);
-      attr = true;
-    }
+    static SmemAttr attr{};
+    if (raise_smem_limit(attr, (const void*)dw_slide2_kernel<ACT, K, RX, CPT, CS>, 120 * 1024,
+                         "cudaFuncSetAttribute(dw_slide2)"))
+      return false;
     const int tiles_x = (a.ow + TW - 1) / TW, tiles_y = (a.oh + TH - 1) / TH;
     const int slabs = a.c / CS;
     const int64_t total = (int64_t)a.batch * slabs * tiles_x * tiles_y;
@@ -893,8 +885,7 @@ template <int ACT>
 static bool dw_dispatch_ks(const DwArgs& a, cudaStream_t st) {
 #define SDX_DW_CASE(KK, SS)                                   \
   if (a.kh == KK && a.kw == KK && a.sh == SS && a.sw == SS) { \
-    if (!dw_tma_pick<ACT, KK, SS>(a, st)) dw_launch_t<ACT, KK, SS>(a, st); \
-    return true;                                              \
+    return dw_tma_pick<ACT, KK, SS>(a, st) || dw_launch_t<ACT, KK, SS>(a, st); \
   }
   SDX_DW_CASE(3, 1)
   SDX_DW_CASE(3, 2)
@@ -975,18 +966,17 @@ __global__ void __launch_bounds__(256) stem_tiled_kernel(DirectArgs a, int TH, i
 }
 
 template <int ACT, int K, int S>
-static void stem_launch_t(const DirectArgs& a, cudaStream_t st) {
+static bool stem_launch_t(const DirectArgs& a, cudaStream_t st) {
   const int TH = 8, TW = 32;
   const int IWt = (TW - 1) * S + K, IHt = (TH - 1) * S + K;
   const size_t smem = sizeof(float) * ((size_t)K * K * a.ic * a.oc + (size_t)a.ic * IHt * IWt);
-  static bool attr = false;
-  if (!attr) {
-    cudaFuncSetAttribute(stem_tiled_kernel<ACT, K, S>, cudaFuncAttributeMaxDynamicSharedMemorySize, 96 * 1024);
-    attr = true;
-  }
+  static SmemAttr attr{};
+  if (raise_smem_limit(attr, (const void*)stem_tiled_kernel<ACT, K, S>, 96 * 1024, "cudaFuncSetAttribute(stem_tiled)"))
+    return false;
   const int tiles_x = (a.ow + TW - 1) / TW, tiles_y = (a.oh + TH - 1) / TH;
   dim3 grid(tiles_x * tiles_y, a.batch);
   stem_tiled_kernel<ACT, K, S><<<grid, 256, smem, st>>>(a, TH, TW, tiles_x);
+  return true;
 }
 
 // ---- persistent, TMA-fed stem for the graph-input conv: fp32 NCHW input, IC = 3, OC = 16, 3x3,
@@ -1401,11 +1391,9 @@ static bool stem_tma_launch_t(const DirectArgs& a, cudaStream_t st) {
     return false;
   const size_t buf = ((size_t)3 * STEM_IH * STEM_IW * 4 + 1023) & ~(size_t)1023;
   const size_t smem = 1024 + 2 * buf + sizeof(float) * (9 * 3 * 16 + 16) + 16;
-  static bool attr = false;
-  if (!attr) {
-    cudaFuncSetAttribute(stem_tma_kernel<ACT>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
-    attr = true;
-  }
+  static SmemAttr attr{};
+  if (raise_smem_limit(attr, (const void*)stem_tma_kernel<ACT>, (int)smem, "cudaFuncSetAttribute(stem_tma)"))
+    return false;
   const int tiles_x = (a.ow + STEM_TW - 1) / STEM_TW, tiles_y = (a.oh + STEM_TH - 1) / STEM_TH;
   const int64_t total = (int64_t)a.batch * tiles_x * tiles_y;
   if (total <= 0 || total > INT32_MAX) return false;
@@ -1425,13 +1413,9 @@ static bool stem_tc_run(const CUtensorMap& map, const DirectArgs& a, cudaStream_
   const size_t smem = 1024 + STEM_TC_NBUF * buf + (size_t)STEM_TC_NA * STEM_TC_A_BYTES + 2 * STEM_TC_B_BYTES +
                       sizeof(float) * (9 * 3 * 16 + 16) +
                       sizeof(uint64_t) * (2 * STEM_TC_NBUF + 2 * STEM_TC_NA + 2 * STEM_TC_NACC) + 16;
-  static bool attr = false;
-  if (!attr) {
-    if (cudaFuncSetAttribute(stem_tc_kernel<ACT>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem) !=
-        cudaSuccess)
-      return false;
-    attr = true;
-  }
+  static SmemAttr attr{};
+  if (raise_smem_limit(attr, (const void*)stem_tc_kernel<ACT>, (int)smem, "cudaFuncSetAttribute(stem_tc)"))
+    return false;
   const int tiles_x = (a.ow + STEM_TW - 1) / STEM_TW, tiles_y = (a.oh + STEM_TC_TH - 1) / STEM_TC_TH;
   const int64_t total = (int64_t)a.batch * tiles_x * tiles_y;
   if (total <= 0 || total > INT32_MAX) return false;
@@ -1507,15 +1491,14 @@ __global__ void __launch_bounds__(256, 2) stem_image_kernel(ImageArgs im, Direct
 }
 
 template <int ACT>
-static void stem_image_launch_t(const ImageArgs& im, const DirectArgs& a, cudaStream_t st) {
+static bool stem_image_launch_t(const ImageArgs& im, const DirectArgs& a, cudaStream_t st) {
   const size_t smem = sizeof(float) * ((size_t)3 * STEM_IH * STEM_IW + 9 * 3 * 16 + 16 + 3 * 256);
-  static bool attr = false;
-  if (!attr) {
-    cudaFuncSetAttribute(stem_image_kernel<ACT>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
-    attr = true;
-  }
+  static SmemAttr attr{};
+  if (raise_smem_limit(attr, (const void*)stem_image_kernel<ACT>, (int)smem, "cudaFuncSetAttribute(stem_image)"))
+    return false;
   const int tiles_x = (a.ow + STEM_TW - 1) / STEM_TW, tiles_y = (a.oh + STEM_TH - 1) / STEM_TH;
   stem_image_kernel<ACT><<<a.batch * tiles_x * tiles_y, 256, smem, st>>>(im, a, tiles_x, tiles_x * tiles_y);
+  return true;
 }
 
 bool stem_image_launch(const ImageArgs& im, const DirectArgs& a, cudaStream_t st) {
@@ -1529,9 +1512,9 @@ bool stem_image_launch(const ImageArgs& im, const DirectArgs& a, cudaStream_t st
   const int64_t tiles = (int64_t)a.batch * ((a.ow + STEM_TW - 1) / STEM_TW) * ((a.oh + STEM_TH - 1) / STEM_TH);
   if (tiles <= 0 || tiles > INT32_MAX) return false;
   switch (a.act) {
-    case ACT_HARDSWISH: stem_image_launch_t<ACT_HARDSWISH>(im, a, st); return true;
-    case ACT_RELU: stem_image_launch_t<ACT_RELU>(im, a, st); return true;
-    case ACT_NONE: stem_image_launch_t<ACT_NONE>(im, a, st); return true;
+    case ACT_HARDSWISH: return stem_image_launch_t<ACT_HARDSWISH>(im, a, st);
+    case ACT_RELU: return stem_image_launch_t<ACT_RELU>(im, a, st);
+    case ACT_NONE: return stem_image_launch_t<ACT_NONE>(im, a, st);
     default: return false;
   }
 }
@@ -1559,9 +1542,7 @@ bool stem_tiled_launch(const DirectArgs& a, cudaStream_t st) {
   switch (a.act) {
 #define SDX_STEM_CASE(ACTC)                                               \
   case ACTC:                                                              \
-    if (a.sh == 1) stem_launch_t<ACTC, 3, 1>(a, st);                      \
-    else stem_launch_t<ACTC, 3, 2>(a, st);                                \
-    return true;
+    return a.sh == 1 ? stem_launch_t<ACTC, 3, 1>(a, st) : stem_launch_t<ACTC, 3, 2>(a, st);
     SDX_STEM_CASE(ACT_HARDSWISH)
     SDX_STEM_CASE(ACT_RELU)
     SDX_STEM_CASE(ACT_NONE)

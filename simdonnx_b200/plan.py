@@ -132,6 +132,8 @@ class ExecPlan:
     output: str = ""
     inputs: list = field(default_factory=list)     # every graph input, back to back at the arena start
     feeds: dict = field(default_factory=dict)      # input name -> callable making its seeded data
+    feeds_dev: dict = field(default_factory=dict)  # input name -> callable(device): the same data as a
+                                                   # torch tensor made on that device (large batches)
     offsets: dict = field(default_factory=dict)   # value -> arena byte offset (int64)
     arena_bytes: int = 0
 

@@ -535,13 +535,23 @@ class CudaInferenceSession:
         N.call("sdx_session_enqueue", self.h)
 
     def write_inputs(self, feeds: dict) -> None:
-        """Copy host inputs into the arena (synchronous)."""
+        """Copy inputs into the arena (synchronous): numpy arrays from the host, or torch tensors
+        already on this device (plan.feeds_dev)."""
         for name in self.plan.inputs:
             dt = self.plan.values[name].dtype
-            a = np.ascontiguousarray(feeds[name], np.uint8 if dt == "u8" else np.float32)
-            t = torch.from_numpy(a).to(self.device)
-            if dt == "f16":
-                t = t.half()
+            f = feeds[name]
+            if isinstance(f, torch.Tensor):
+                t = f.to(self.device).contiguous()
+                want = {"u8": torch.uint8, "f16": torch.float16}.get(dt, torch.float32)
+                if t.dtype != want:
+                    t = t.to(want)
+                if tuple(t.shape) != tuple(self.plan.values[name].shape):
+                    raise ValueError(f"input {name}: shape {tuple(t.shape)}, plan {self.plan.values[name].shape}")
+            else:
+                a = np.ascontiguousarray(f, np.uint8 if dt == "u8" else np.float32)
+                t = torch.from_numpy(a).to(self.device)
+                if dt == "f16":
+                    t = t.half()
             torch.cuda.synchronize(self.device)
             N.call("sdx_memcpy_dtod_async", self.be.ctx, self.ptr(name), B.ptr(t), t.numel() * t.element_size(),
                    ctypes.c_void_p(self.stream_ptr))

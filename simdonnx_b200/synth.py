@@ -48,6 +48,48 @@ def normal(seed: int, shape, std: float = 1.0, mean: float = 0.0) -> np.ndarray:
     return (mean + std * z[:n]).astype(np.float32).reshape(shape)
 
 
+def _i64(c: int) -> int:
+    """A uint64 constant as the int64 with the same bits."""
+    return c - (1 << 64) if c >= 1 << 63 else c
+
+
+def _splitmix64_torch(seed: int, start: int, n: int, device):
+    """SplitMix64 outputs start+1 .. start+n as int64 tensors holding the uint64 bits (two's-complement
+    products and masked shifts give the same bits as the uint64 arithmetic of splitmix64)."""
+    import torch
+    i = torch.arange(start + 1, start + n + 1, dtype=torch.int64, device=device)
+    z = i * _i64(0x9E3779B97F4A7C15) + _i64(seed & 0xFFFFFFFFFFFFFFFF)
+    z = (z ^ ((z >> 30) & ((1 << 34) - 1))) * _i64(0xBF58476D1CE4E5B9)
+    z = (z ^ ((z >> 27) & ((1 << 37) - 1))) * _i64(0x94D049BB133111EB)
+    return z ^ ((z >> 31) & ((1 << 33) - 1))
+
+
+def uniform_torch(seed: int, shape, device, lo: float = 0.0, hi: float = 1.0, chunk: int = 1 << 26):
+    """uniform() computed with torch on `device` (bit-identical values; seconds instead of minutes for
+    the det N=256 input). Generated in chunks of `chunk` elements to bound the int64 temporaries."""
+    import torch
+    n = int(np.prod(shape))
+    out = torch.empty(n, dtype=torch.float32, device=device)
+    for s in range(0, n, chunk):
+        m = min(chunk, n - s)
+        z = _splitmix64_torch(seed, s, m, device)
+        u = ((z >> 11) & ((1 << 53) - 1)).to(torch.float64) * (1.0 / 9007199254740992.0)
+        out[s:s + m] = (lo + (hi - lo) * u).to(torch.float32)
+    return out.reshape(shape)
+
+
+def bytes_torch(seed: int, shape, device, chunk: int = 1 << 26):
+    """Rng.bytes() computed with torch on `device` (bit-identical)."""
+    import torch
+    n = int(np.prod(shape))
+    out = torch.empty(n, dtype=torch.uint8, device=device)
+    for s in range(0, n, chunk):
+        m = min(chunk, n - s)
+        z = _splitmix64_torch(seed, s, m, device)
+        out[s:s + m] = ((z >> 56) & 0xFF).to(torch.uint8)
+    return out.reshape(shape)
+
+
 class Rng:
     """Named-tensor generator: Rng(seed).normal('conv1.w', shape, std)."""
 
@@ -63,3 +105,9 @@ class Rng:
 
     def normal(self, name: str, shape, std=1.0, mean=0.0):
         return normal(name_seed(self.seed, name), shape, std, mean)
+
+    def uniform_torch(self, name: str, shape, device, lo=0.0, hi=1.0):
+        return uniform_torch(name_seed(self.seed, name), shape, device, lo, hi)
+
+    def bytes_torch(self, name: str, shape, device):
+        return bytes_torch(name_seed(self.seed, name), shape, device)

@@ -131,3 +131,18 @@ def test_conv_pool_split_for_cuda():
     assert ops == [("Conv", "cp.prepool"), ("MaxPool", "cp")]
     assert R.shape("cp.prepool") == (1, 17, 22, 32) and R.shape("cp") == (1, 8, 11, 32)
     assert R.nodes[1].p.fuse_relu
+
+
+def test_device_feed_generator_matches_host_generator():
+    """plan.feeds_dev (torch SplitMix64, used by bench.py for the N=256 input) produces exactly the
+    values of plan.feeds (numpy SplitMix64): same bits, on small shapes and across chunk edges."""
+    import torch
+    from simdonnx_b200 import synth
+    r = synth.Rng(2)
+    assert np.array_equal(r.uniform("input", (2, 3, 40, 24)), r.uniform_torch("input", (2, 3, 40, 24), "cpu").numpy())
+    assert np.array_equal(r.bytes("image", (2, 17, 9, 3)), r.bytes_torch("image", (2, 17, 9, 3), "cpu").numpy())
+    assert np.array_equal(synth.uniform(99, (1001,), -1.0, 2.0),
+                          synth.uniform_torch(99, (1001,), "cpu", -1.0, 2.0, chunk=64).numpy())
+    p = configs.build_det(batch=1, hw=64)
+    (k, f), = p.feeds.items()
+    assert np.array_equal(f(), p.feeds_dev[k](torch.device("cpu")).numpy())

@@ -52,25 +52,34 @@ def _inputs(seed, b, hw, c):
     return x, w1, b1, w2, b2
 
 
-def _gate_with_scratch(ctx, args):
+def _run(ctx, fn, d, stream):
+    """Calls `fn` on the context's own stream (stream None) or on a torch stream, then waits."""
+    torch.cuda.synchronize()  # inputs were written on torch's default stream
+    if stream is None:
+        N.call(fn, ctx, ctypes.byref(d), None)
+        N.call("sdx_stream_sync", ctx, None, 10000)
+    else:
+        N.call(fn, ctx, ctypes.byref(d), ctypes.c_void_p(stream.cuda_stream))
+        stream.synchronize()
+
+
+def _gate_with_scratch(ctx, args, sums=None, stream=None):
     x = args[0]
     b, h, w, c = x.shape
     s = torch.empty((b, c), dtype=torch.float32, device="cuda")
     scratch = torch.empty(int(N.lib().sdx_channel_gate_scratch_bytes(b, h * w, c)), dtype=torch.uint8, device="cuda")
     d = _desc(*args, s, scratch)
-    torch.cuda.synchronize()  # inputs were written on torch's stream; the gate runs on the context's
-    N.call("sdx_channel_gate", ctx, ctypes.byref(d), None)
-    N.call("sdx_stream_sync", ctx, None, 10000)
+    d.sums = _ptr(sums)
+    _run(ctx, "sdx_channel_gate", d, stream)
     return s.cpu().numpy()
 
 
-def _gate_static(ctx, args):
+def _gate_static(ctx, args, sums=None, stream=None):
     x = args[0]
     s = torch.full((x.shape[0], x.shape[-1]), float("nan"), dtype=torch.float32, device="cuda")
     d = _desc(*args, s)
-    torch.cuda.synchronize()
-    N.call("sdx_channel_gate_static", ctx, ctypes.byref(d), None)
-    N.call("sdx_stream_sync", ctx, None, 10000)
+    d.sums = _ptr(sums)
+    _run(ctx, "sdx_channel_gate_static", d, stream)
     return s.cpu().numpy()
 
 
@@ -99,3 +108,28 @@ def test_static_gate_rejects_oversized_scratch(ctx):
     assert rc == 8, rc  # SDX_ERR_NOT_SUPPORTED
     assert "scratch" in N.last_error()
     assert int(N.lib().sdx_launch_count()) == before
+
+
+def test_static_gate_from_conv_sums_wide(ctx):
+    """The scratch array on the other path: a gate that reads a conv's fp32 32-pixel channel sums
+    with c = 4096 (above 2048 channels those sums are reduced per chunk into the scratch array)."""
+    b, hw, c = 2, 16, 4096  # 16 x 16 pixels: 8 runs of 32 per image
+    args = _inputs(77, b, hw, c)
+    x = args[0]
+    sums = x.float().reshape(b, hw * hw // 32, 32, c).sum(dim=2).contiguous()
+    assert int(N.lib().sdx_channel_gate_scratch_bytes(b, hw * hw, c)) <= MAX_BYTES
+    ref = _gate_with_scratch(ctx, args, sums)
+    for _ in range(2):
+        got = _gate_static(ctx, args, sums)
+        assert np.isfinite(got).all()
+        np.testing.assert_allclose(got, ref, rtol=1e-6, atol=1e-6)
+
+
+def test_static_gate_on_caller_stream(ctx):
+    """Both gates enqueued on a torch stream handle passed through the C ABI (not the context's own)."""
+    args = _inputs(5, 3, 40, 128)
+    st = torch.cuda.Stream()
+    ref = _gate_with_scratch(ctx, args, stream=st)
+    for _ in range(2):
+        got = _gate_static(ctx, args, stream=st)
+        np.testing.assert_allclose(got, ref, rtol=1e-6, atol=1e-6)
