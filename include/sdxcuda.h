@@ -111,7 +111,10 @@ int sdx_selftest_bounded_wait(sdx_ctx* ctx, int wait_ms, sdx_stream s);
  * Call with out == NULL to get the size in bytes in *bytes.
  * ====================================================================================== */
 /* ConvP weights w [oc][ic/group][kh][kw] for the kernel sdx_conv2d routes `d` to (Nhwc.Pack,
- * src/Kernels/Nhwc.cs:102-125). */
+ * src/Kernels/Nhwc.cs:102-125). The layout depends on the shape and layout fields of `d` (batch and
+ * spatial sizes, channels, kernel, strides, pads, dtypes, layouts, y_pix_stride / y_ch_off, add_up,
+ * w_terms), not on its pointers: pack with the descriptor that sdx_conv2d will get (thin 1x1 convs
+ * over whole fp16 tensors are packed for pixel folding, which depends on batch * ih * iw). */
 struct sdx_conv_desc;
 int sdx_pack_conv(const struct sdx_conv_desc* d, const float* w, void* out, size_t* bytes);
 /* ConvTP weights w [ic][oc][kh][kw] (Nhwc.PackConvT, src/Kernels/Nhwc.Det.cs:26-44). */

@@ -1,0 +1,99 @@
+// Tile-level arguments of the tcgen05 conv / GEMM kernel (conv_tc_kernel.cuh) shared by the host
+// planner (conv_tc.cu) and the per-activation kernel instantiation units (conv_tc_inst_*.cu).
+#pragma once
+#include <cuda.h>
+#include <cuda_runtime.h>
+#include <stddef.h>
+#include <stdint.h>
+
+namespace sdx {
+
+constexpr int TC_BM = 128;
+// Epilogue warp groups (kernel template G): 2, or 4 for tiles of at most 64 columns (more warps
+// hide the per-tile latency of thin tiles); a CTA is the producer warp, the MMA warp and G groups.
+constexpr int TC_EPI_GROUPS_MAX = 4;
+constexpr int tc_threads(int groups) { return 64 + 128 * groups; }
+constexpr int TC_MAX_STAGES = 8;  // <= 32 (ring slots are tracked in 32-bit masks)
+constexpr int TC_SMEM_LIMIT = 227 * 1024;
+constexpr int TC_BIAS_SMEM_MAX = 4096;  // bias floats staged in shared memory
+
+struct TcArgs {
+  int mode;
+  int M;
+  int N;
+  int BN;
+  int n_tiles;
+  int m_tiles;
+  int kb_per_tap;
+  int halo;             // TC_CONV: one A box per (kx, channel block) holds the BH + kh - 1 input rows
+                        // of all kh row taps; the MMAs of tap (ky, kx) read it from row ky * BW on
+  int b_taps;           // weight taps per stage (kh in halo mode, else 1)
+  uint32_t a_stage_bytes;  // bytes of one A stage: cps boxes of a_blk_bytes
+  uint32_t a_blk_bytes;    // one channel block's A box, rounded up to 1024 bytes
+  int cps;              // channel blocks per pipeline stage (divides kb_per_tap)
+  int kblk;             // channels per k-block: 64, 32 or 16 (rows of 128/64/32 B, same-span swizzle)
+  int b_resident;       // 1: all weights are loaded into shared memory once per CTA
+  int wterms;           // fp16 weight terms: 1 (w) or 2 (hi, lo: two MMAs per k-step)
+  uint32_t b_total_bytes;  // bytes of all weights (both terms), resident mode
+  int taps, kw;
+  int pad_t, pad_l;
+  int OH, OW, BH, BW, tiles_h, tiles_w;
+  int BWs;              // tile step along x (BW, or BW - 2 in kx-in-N mode: the halo columns overlap)
+  int kxn;              // 3x3 conv with the column taps as GEMM columns (kx * 32 + oc)
+  int b_rows_per_tap;
+  int stages;
+  int acc_stride;
+  int nacc;             // TMEM accumulators: 4 when 4 x BN fits the 512 columns, else 2
+  int egroups;          // epilogue warp groups (the kernel's G): 2 or 4
+  uint32_t tmem_cols;
+  uint32_t a_box_bytes;
+  // epilogue
+  const float* bias;
+  const void* res;
+  int res_f32;
+  int64_t res_pix_stride;
+  int res_ch_off;
+  int res_up;           // 2: residual on the half-size grid, read nearest-upsampled (per thread)
+  void* out;
+  int out_f32;
+  int64_t out_pix_stride;
+  int out_ch_off;
+  int act;
+  int vec_ok;
+  int convt_kh, convt_kw, convt_oc, convt_H, convt_W;
+  // TMA store epilogue
+  int tma_out;          // 1: staging buffer + TMA stores; 0: per-thread stores (fallback)
+  int tma_res;          // 1: residual tile by TMA load into the staging buffer
+  int esz;              // output element bytes
+  int G;                // columns per store group
+  int ngroups;          // groups per tile
+  int swz;              // staging rows (G * esz bytes = 32, 64 or 128) use the TMA swizzle of that span
+  uint32_t group_bytes; // bytes of one group in the staging buffer (128 rows)
+  uint32_t sbuf_bytes;  // bytes of one staging buffer
+  int nsbuf;            // staging buffers per epilogue group (1 or 2)
+  uint32_t slab_tx;     // bytes one residual box (one group, one warp's 32 rows) delivers
+  int bias_smem;        // bias floats staged in shared memory (per accumulator column), 0 = none
+  int log2G;            // log2 of G (fast epilogue: G is 16, 32 or 64)
+  // ConvT chain epilogue (EPI = 4): the second ConvT's weights follow the bias in smem
+  int chain_act2, chain_y_f32;
+  void* chain_y;
+  const float* chain_w2;
+  const float* chain_b2;
+  // channel sums of the activated output over each run of 32 rows (a warp's rows; rows mode, M a
+  // multiple of 32): fp32 [M / 32][N], or null
+  float* gap;
+  // pixel folding (rows mode): each GEMM row holds `fold` consecutive pixels (A = [M, fold * K]
+  // over the same memory, block-diagonal weights, N = fold * OC columns); the bias repeats every
+  // bias_mod columns and the channel sums are per 32 pixels, i.e. per 32 / fold rows: [M * fold / 32][OC]
+  int fold;
+  int bias_mod;
+  unsigned int* err;
+};
+
+// Launches conv_tc_kernel<ACT, EPI, G>; one explicit instantiation per (ACT, EPI, G) the planner
+// uses, spread over conv_tc_inst_*.cu so that the kernels compile in parallel.
+template <int ACT, int EPI, int G>
+int launch_tc(int dev, int grid, size_t smem, cudaStream_t stream, const CUtensorMap& mA, const CUtensorMap& mB,
+              const CUtensorMap& mOut, const CUtensorMap& mRes, const TcArgs& a);
+
+}  // namespace sdx

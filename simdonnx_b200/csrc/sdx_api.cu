@@ -465,6 +465,17 @@ static bool conv_kxn(const sdx_conv_desc* d) {
   return tc_conv_kxn(d->kh, d->kw, d->sh, d->sw, d->pad_t, d->pad_l, d->pad_b, d->pad_r, d->oc);
 }
 
+// Pixel folding factor of a 1x1 tensor-core conv (tc_fold_factor): only for a dense fp16 NHWC
+// output and an fp16 residual read at full resolution. Depends on the shape and these layout
+// fields only (not on pointers), so sdx_pack_conv and sdx_conv2d agree for one descriptor.
+static int conv_fold(const sdx_conv_desc* d) {
+  if (conv_route(d) != R_TC_ROWS) return 1;
+  const int64_t ystride = d->y_pix_stride > 0 ? d->y_pix_stride : d->oc;
+  if (d->y_dtype != SDX_F16 || ystride != d->oc || d->y_ch_off != 0 || d->add_dtype != SDX_F16 || d->add_up == 2)
+    return 1;
+  return tc_fold_factor((int64_t)d->batch * d->ih * d->iw, d->ic, d->oc);
+}
+
 static int conv_wterms(const sdx_conv_desc* d) {
   if (d->w_terms == 1 || d->w_terms == 2) return d->w_terms;
   return d->kh * d->kw > 1 ? 1 : 2;
@@ -480,6 +491,7 @@ int sdx_pack_conv(const sdx_conv_desc* d, const float* w, void* out, size_t* byt
     case R_TC_CONV:
     case R_TC_ROWS:
       need = (route == R_TC_CONV && conv_kxn(d) ? tc_kxn_weights_halves(d->ic, conv_wterms(d))
+              : conv_fold(d) > 1                ? tc_fold_weights_halves(d->ic, d->oc, conv_fold(d), conv_wterms(d))
                                                 : tc_weights_halves(d->oc, d->ic, taps, conv_wterms(d))) *
              sizeof(__half);
       break;
@@ -495,6 +507,7 @@ int sdx_pack_conv(const sdx_conv_desc* d, const float* w, void* out, size_t* byt
   if (!w) return set_error(SDX_ERR_INVALID, "null weights");
   if (route == R_TC_CONV || route == R_TC_ROWS) {
     if (route == R_TC_CONV && conv_kxn(d)) tc_pack_conv_kxn(w, d->oc, d->ic, conv_wterms(d), static_cast<__half*>(out));
+    else if (conv_fold(d) > 1) tc_pack_conv_fold(w, d->oc, d->ic, conv_fold(d), conv_wterms(d), static_cast<__half*>(out));
     else tc_pack_conv(w, d->oc, d->ic, d->kh, d->kw, conv_wterms(d), static_cast<__half*>(out));
   } else if (route == R_DEPTHWISE) {
     float* o = static_cast<float*>(out);
@@ -599,6 +612,20 @@ int sdx_conv2d(sdx_ctx* ctx, const sdx_conv_desc* d, sdx_stream s) {
       p.act = d->act;
       p.gap = P<float>(d->gap_sums);
       p.err = ctx->err_word;
+      if (route == R_TC_ROWS) {
+        const int f = conv_fold(d);
+        if (f > 1) {
+          // f consecutive pixels per GEMM row over the same memory (block-diagonal weights)
+          p.fold = f;
+          p.bias_mod = d->oc;
+          p.M /= f;
+          p.K *= f;
+          p.lda *= f;
+          p.N *= f;
+          p.res_pix_stride *= f;
+          p.out_pix_stride *= f;
+        }
+      }
       return tc_launch(p, st);
     }
     case R_DEPTHWISE: {

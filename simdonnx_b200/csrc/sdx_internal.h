@@ -69,6 +69,11 @@ struct TcProblem {
   int res_ch_off;
   int res_up;  // 2: the residual is the nearest 2x downsample grid [batch, OH/2, OW/2, N] (read upsampled)
   float* gap;  // fp32 [M / 32][N]: channel sums of the activated output over each 32-row run, or null
+  // pixel folding of a 1x1 conv (rows mode): M, K, N, lda, strides are those of the folded GEMM
+  // (fold pixels per row, block-diagonal weights from tc_pack_conv_fold); bias_mod = OC, the
+  // bias repeats every OC columns; gap (if any) is still [pixels / 32][OC]
+  int fold;
+  int bias_mod;
   void* out;
   int out_f32;
   int64_t out_pix_stride;
@@ -96,6 +101,13 @@ void tc_pack_conv_kxn(const float* w, int OC, int IC, int terms, __half* out);
 size_t tc_convt_weights_halves(int IC, int OC, int KH, int KW);
 void tc_plan_n_convt(int kh, int kw, int OC, int* BN, int* n_tiles);
 void tc_pack_conv(const float* w, int OC, int IC, int KH, int KW, int terms, __half* out);
+// Pixel folding factor of a 1x1 conv over `pixels` rows (1, 2 or 4): F consecutive pixels per GEMM
+// row when OC * F <= 128 and IC * F <= 128 (thin convs: F times the pixels per tile for the same
+// per-tile cost). The caller checks the layout conditions (dense fp16 output and residual).
+int tc_fold_factor(int64_t pixels, int IC, int OC);
+size_t tc_fold_weights_halves(int IC, int OC, int fold, int terms);
+// Block-diagonal B operand of the folded GEMM: row j*OC + o, column j*IC + c = w[o][c]
+void tc_pack_conv_fold(const float* w, int OC, int IC, int fold, int terms, __half* out);
 void tc_pack_convt(const float* w, int IC, int OC, int KH, int KW, __half* out);
 void tc_pack_gemm(const float* b, int K, int N, int trans_b, __half* out);
 

@@ -327,12 +327,12 @@ class CudaInferenceSession:
                             add_layout=_LAY[addv.layout] if addv else N.NHWC,
                             pool=p.pool is not None, pool_relu=bool(p.pool and p.pool.fuse_relu),
                             y_pix_stride=P.shape(yslice[0])[3] if yslice else 0, y_ch_off=yslice[1] if yslice else 0)
+            d.add_up = getattr(p, "add_up", 0)  # a layout field: set before packing (the fold depends on it)
             wt = self._const_dev(("convw", n.name), lambda: B.pack_conv(d, W, self.device))
             d.x = self.ptr(n.ins[0])
             d.w = B.ptr(wt)
             d.bias = self._f32(p.bias) if p.bias else (self._zeros(oc) if p.group > 1 else 0)
             d.add = self.ptr(p.add) if p.add else 0
-            d.add_up = getattr(p, "add_up", 0)
             d.y = self.ptr(n.outs[0])
             d.gap_sums = self.ptr(n.outs[1]) if len(n.outs) > 1 else 0
             scale = getattr(p, "in_scale", None)

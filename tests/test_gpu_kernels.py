@@ -459,3 +459,45 @@ def test_conv_channel_sums_feed_gate(be, ic, oc, h, w, act):
     d3.gap_sums = B.ptr(sums)
     with pytest.raises(N.SdxError):
         B.conv2d(be, d3, dev16(rnd(rng, nb, 3, 5, ic)), B.pack_conv(d3, wt), bias=dev32(b))
+
+
+# thin 1x1 convs run pixel-folded (F consecutive pixels per GEMM row, block-diagonal weights)
+FOLD_CASES = [
+    # ic, oc, h, w, residual, act, expected fold
+    (16, 32, 16, 24, False, "hardswish", 4),   # det b1.pw shape class
+    (32, 64, 16, 16, True, "relu", 2),         # det b2.pw
+    (64, 64, 8, 16, False, "none", 2),         # det b3.pw
+    (8, 32, 32, 32, True, "gelu", 4),
+    (16, 32, 10, 10, False, "hardswish", 1),   # 200 pixels: no fold (not whole 32-row runs)
+]
+
+
+@pytest.mark.parametrize("ic,oc,h,w,residual,act,fold", FOLD_CASES)
+def test_pointwise_pixel_folded(be, ic, oc, h, w, residual, act, fold):
+    """1x1 convs with oc * F = 128 run F pixels per GEMM row: against the oracle, with the fused
+    32-pixel channel sums (per pixel run, not per folded row) and an fp16 residual."""
+    from simdonnx_b200 import backend as B
+    rng = np.random.default_rng(ic * 7 + oc + h)
+    nb = 2
+    x = rnd(rng, nb, h, w, ic)
+    wt = rnd(rng, oc, ic, 1, 1, scale=1 / np.sqrt(ic))
+    b = rnd(rng, oc)
+    res = rnd(rng, nb, h, w, oc) if residual else None
+    ref = O.conv(x, O.ConvPlan(wt, b), act=act, add=res)
+    d = B.conv_desc(nb, h, w, ic, oc, 1, 1, act=act)
+    packed = B.pack_conv(d, wt)
+    if fold > 1:
+        # F copies of the weights on the block diagonal: 2 fp16 terms x 128 rows x F * ic columns
+        assert packed.numel() == 2 * 2 * 128 * ic * fold, packed.numel()
+    sums = None
+    if (nb * h * w) % 32 == 0:
+        sums = torch.full((nb * h * w // 32, oc), float("nan"), dtype=torch.float32, device="cuda")
+        d.gap_sums = B.ptr(sums)
+    y = B.conv2d(be, d, dev16(x), packed, bias=dev32(b), add=None if res is None else dev16(res))
+    got = host(y)
+    assert_close(got, ref, f"1x1 {ic}->{oc} fold {fold}")
+    if sums is not None:
+        # the sums are of the stored fp16 output, per run of 32 pixels
+        want = got.astype(np.float64).reshape(-1, 32, oc).sum(axis=1)
+        np.testing.assert_allclose(host(sums), want, rtol=2e-5, atol=2e-4)
+    assert be.device_error() == 0
