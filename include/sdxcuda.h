@@ -154,8 +154,10 @@ typedef struct sdx_conv_desc {
   sdx_dptr x, w, bias, add, y;  /* w: packed by sdx_pack_conv; bias fp32 [oc] or 0; add 0 = none */
   sdx_dptr in_scale; /* fp32 [batch, ic] per-image channel scale applied to x on load (SE gate), or 0 */
   int w_terms;       /* tensor-core routes: fp16 weight terms, 1 (w) or 2 (hi + lo, ~22-bit weights);
-                        0 = default: 2 for 1x1 kernels (their MMAs hide under HBM time), 1 for larger
-                        kernels (MMA-bound; one fp16 term is the reference GPU backends' weight type) */
+                        0 = default: 2 for 1x1 kernels with ic < 128 (early narrow layers, whose weight
+                        rounding every later layer amplifies), 1 for 1x1 kernels with ic >= 128 and for
+                        larger kernels (their MMAs' operand traffic bounds them; one fp16 term is the
+                        reference GPU backends' weight type) */
   int add_up;        /* 0 or 1: the residual as given; 2: `add` is [batch, oh/2, ow/2, oc] fp16 NHWC, read
                         nearest-upsampled (an FPN top-down ResizeNearest(x, add = this conv) fused into
                         the conv: y = act(conv + up2(add))); tensor-core routes, oh and ow even */

@@ -130,6 +130,14 @@ int tc_launch(const TcProblem& p, cudaStream_t stream) {
   if (convt) tc_plan_n_convt(p.convt_kh, p.convt_kw, p.convt_oc, &BN, &n_tiles);
   else if (p.kxn) BN = 96, n_tiles = 1;
   else tc_plan_n(p.N, &BN, &n_tiles);
+  // 128 output columns of a short reduction (pointwise convs): two 64-column tiles, whose fast
+  // epilogue runs four warp groups instead of two; the packed weights are the same 128 rows, and
+  // the two tiles of one row block run on neighbouring CTAs, so A's second read hits L2
+  if (p.mode == TC_ROWS && !convt && BN == 128 && n_tiles == 1 && p.N == 128 && p.K <= 128 && !p.out_f32 &&
+      p.fold <= 1) {
+    BN = 64;
+    n_tiles = 2;
+  }
   const int kblk = tc_kblk(p.K), kpad = tc_kpad(p.K);
   const int kbytes = kblk * 2;
   TcArgs a;
@@ -159,8 +167,9 @@ int tc_launch(const TcProblem& p, cudaStream_t stream) {
   a.gap = p.gap;
   a.fold = p.fold > 1 ? p.fold : 1;
   a.bias_mod = p.bias_mod;
-  if (a.fold > 1 && (p.mode != TC_ROWS || convt || p.N != 128 || p.bias_mod * a.fold != p.N))
-    return set_error(SDX_ERR_INVALID, "tc: pixel folding needs rows mode and 128 folded columns");
+  if (a.fold > 1 && (p.mode != TC_ROWS || convt || p.N != 64 || p.bias_mod * a.fold != p.N || BN != 64 ||
+                     n_tiles != 1))
+    return set_error(SDX_ERR_INVALID, "tc: pixel folding needs rows mode and 64 folded columns");
   a.out = p.out;
   a.out_f32 = p.out_f32;
   a.out_pix_stride = p.out_pix_stride;
@@ -387,7 +396,7 @@ int tc_launch(const TcProblem& p, cudaStream_t stream) {
   // general cases) up to 128 columns; two when the staging of four would crowd out the A stages
   if (p.res_up && !fast)
     return set_error(SDX_ERR_NOT_SUPPORTED, "tc: upsampled residual needs the fp16 TMA-store epilogue");
-  if (p.gap && a.fold > 1 && (!fast || BN != 128 || n_tiles != 1 || a.G != 64 || p.M % 32 != 0))
+  if (p.gap && a.fold > 1 && (!fast || BN != 64 || n_tiles != 1 || a.G != 64 || p.M % 32 != 0))
     return set_error(SDX_ERR_NOT_SUPPORTED, "tc: folded channel sums need one 128-column tile, fast epilogue");
   if (p.gap && a.fold == 1 && (!fast || p.mode == TC_CONV || convt || p.M % 32 != 0 || p.N % 16 != 0 ||
                 (BN != 16 && BN != 32 && BN != 64 && BN != 128) || a.G != (BN < 64 ? BN : 64) ||
@@ -529,9 +538,10 @@ void tc_pack_convt(const float* w, int IC, int OC, int KH, int KW, __half* out) 
 }
 
 int tc_fold_factor(int64_t pixels, int IC, int OC) {
-  // pixels % (32 * f): the folded rows come in whole 32-row runs (fused channel sums per 32 pixels)
+  // folded to 64-column tiles (the width whose fast epilogue runs four warp groups); pixels %
+  // (32 * f): the folded rows come in whole 32-row runs (fused channel sums per 32 pixels)
   for (int f = 4; f >= 2; f /= 2)
-    if (OC * f == 128 && IC * f <= 128 && pixels % (32 * f) == 0) return f;
+    if (OC * f == 64 && IC * f <= 128 && pixels % (32 * f) == 0) return f;
   return 1;
 }
 

@@ -540,14 +540,14 @@ __device__ __forceinline__ void gap_warp_rows(uint32_t slab, uint32_t group_byte
 }
 
 // Channel sums of one warp's 32 staged rows of a pixel-folded tile (F pixels of OC channels per
-// row, F * OC = 128 columns in two 64-column groups of 128-byte swizzled rows): per run of 32
+// row, F * OC = 64 * NG columns in NG 64-column groups of 128-byte swizzled rows): per run of 32
 // pixels (32 / F rows) and channel, into gp[run * OC + channel] for the warp's F runs. Lane j sums
-// the column pair j of both groups over every row (64 4-byte loads; the swizzle term of row r is
-// r & 7, one base address per term), per run; the pairs that hold the same channel in other pixel
-// slots (the other group, and for OC = 32 lane j ^ 16) are then added.
-template <int F, int OC>
+// the column pair j of every group over every row (4-byte loads; the swizzle term of row r is
+// r & 7, one base address per term), per run; the lanes whose pairs hold the same channel in other
+// pixel slots (j ^ OC/2, ...) then combine by shuffles, and lanes 0 .. OC/2 - 1 store.
+template <int F, int OC, int NG>
 __device__ __forceinline__ void gap_warp_rows_fold(uint32_t slab, uint32_t group_bytes, int lane, float* gp) {
-  static_assert(F * OC == 128, "folded tile is 128 columns");
+  static_assert(F * OC == 64 * NG && OC % 16 == 0 && OC <= 64, "folded tile of whole 64-column groups");
   constexpr int RPR = 32 / F;  // rows per 32-pixel run
   const uint32_t byte = (uint32_t)lane * 4u;  // the pair's byte offset in its 128-byte group row
   const uint32_t k = byte >> 4, inner = byte & 15u;
@@ -558,7 +558,7 @@ __device__ __forceinline__ void gap_warp_rows_fold(uint32_t slab, uint32_t group
 #pragma unroll
   for (int r = 0; r < F; r++) acc[r] = make_float2(0.0f, 0.0f);
 #pragma unroll
-  for (int g = 0; g < 2; g++) {
+  for (int g = 0; g < NG; g++) {
 #pragma unroll
     for (int row = 0; row < 32; row++) {
       uint32_t w;
@@ -566,13 +566,13 @@ __device__ __forceinline__ void gap_warp_rows_fold(uint32_t slab, uint32_t group
       acc[row / RPR] = add_f32x2(acc[row / RPR], __half22float2(*reinterpret_cast<const __half2*>(&w)));
     }
   }
-  if (OC == 32) {
+#pragma unroll
+  for (int off = OC / 2; off < 32; off *= 2)
 #pragma unroll
     for (int r = 0; r < F; r++) {
-      acc[r].x += __shfl_xor_sync(0xffffffffu, acc[r].x, 16);
-      acc[r].y += __shfl_xor_sync(0xffffffffu, acc[r].y, 16);
+      acc[r].x += __shfl_xor_sync(0xffffffffu, acc[r].x, off);
+      acc[r].y += __shfl_xor_sync(0xffffffffu, acc[r].y, off);
     }
-  }
   if (lane < OC / 2) {
 #pragma unroll
     for (int r = 0; r < F; r++) *reinterpret_cast<float2*>(gp + r * OC + 2 * lane) = acc[r];
@@ -1327,8 +1327,8 @@ __global__ void __launch_bounds__(tc_threads(G), 1)
           bulk_commit(eld);
           // channel sums of the staged rows (read alongside the store's own reads of them)
           if (EPI == 1 && gp && a.fold > 1) {
-            if (a.fold == 4) gap_warp_rows_fold<4, 32>(slab, a.group_bytes, lane, gp);
-            else gap_warp_rows_fold<2, 64>(slab, a.group_bytes, lane, gp);
+            if (a.fold == 4) gap_warp_rows_fold<4, 16, 1>(slab, a.group_bytes, lane, gp);
+            else gap_warp_rows_fold<2, 32, 1>(slab, a.group_bytes, lane, gp);
           } else if (EPI == 1 && gp) {
             if (a.BN == 16) gap_warp_rows<16>(slab, a.group_bytes, lane, gp, nlim);
             else if (a.BN == 32) gap_warp_rows<32>(slab, a.group_bytes, lane, gp, nlim);

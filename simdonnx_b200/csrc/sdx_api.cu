@@ -459,8 +459,6 @@ static int conv_route(const sdx_conv_desc* d) {
   return R_INVALID;
 }
 
-// fp16 weight terms of a tensor-core conv: the caller's choice, else two for 1x1 kernels (their MMAs
-// hide under HBM time) and one for larger kernels (MMA-bound)
 static bool conv_kxn(const sdx_conv_desc* d) {
   return tc_conv_kxn(d->kh, d->kw, d->sh, d->sw, d->pad_t, d->pad_l, d->pad_b, d->pad_r, d->oc);
 }
@@ -476,9 +474,16 @@ static int conv_fold(const sdx_conv_desc* d) {
   return tc_fold_factor((int64_t)d->batch * d->ih * d->iw, d->ic, d->oc);
 }
 
+// fp16 weight terms of a tensor-core conv: the caller's choice, else one for k x k kernels (their thin
+// MMAs bound them) and for 1x1 kernels with at least 128 input channels, two (hi + lo) for narrower
+// 1x1 kernels. The narrow 1x1 convs sit early in the det/rec trunks, where a weight rounding error
+// is shared by every pixel and amplified by every later layer (the squeeze-excitation means shift
+// coherently); in the wide ones it averages over the reduction, and their second term doubles the
+// MMAs' shared-memory operand traffic, which bounds them.
 static int conv_wterms(const sdx_conv_desc* d) {
   if (d->w_terms == 1 || d->w_terms == 2) return d->w_terms;
-  return d->kh * d->kw > 1 ? 1 : 2;
+  if (d->kh * d->kw > 1) return 1;
+  return d->ic >= 128 ? 1 : 2;
 }
 
 int sdx_pack_conv(const sdx_conv_desc* d, const float* w, void* out, size_t* bytes) {

@@ -463,11 +463,12 @@ def test_conv_channel_sums_feed_gate(be, ic, oc, h, w, act):
 
 # thin 1x1 convs run pixel-folded (F consecutive pixels per GEMM row, block-diagonal weights)
 FOLD_CASES = [
-    # ic, oc, h, w, residual, act, expected fold
-    (16, 32, 16, 24, False, "hardswish", 4),   # det b1.pw shape class
-    (32, 64, 16, 16, True, "relu", 2),         # det b2.pw
-    (64, 64, 8, 16, False, "none", 2),         # det b3.pw
-    (8, 32, 32, 32, True, "gelu", 4),
+    # ic, oc, h, w, residual, act, expected fold (oc * fold = 64 columns)
+    (16, 32, 16, 24, False, "hardswish", 2),   # det b1.pw shape class
+    (8, 32, 32, 32, True, "gelu", 2),
+    (16, 16, 16, 16, True, "relu", 4),
+    (8, 16, 8, 32, False, "hardswish", 4),
+    (32, 64, 16, 16, True, "relu", 1),         # det b2.pw: 64 columns already
     (16, 32, 10, 10, False, "hardswish", 1),   # 200 pixels: no fold (not whole 32-row runs)
 ]
 
@@ -487,8 +488,8 @@ def test_pointwise_pixel_folded(be, ic, oc, h, w, residual, act, fold):
     d = B.conv_desc(nb, h, w, ic, oc, 1, 1, act=act)
     packed = B.pack_conv(d, wt)
     if fold > 1:
-        # F copies of the weights on the block diagonal: 2 fp16 terms x 128 rows x F * ic columns
-        assert packed.numel() == 2 * 2 * 128 * ic * fold, packed.numel()
+        # F copies of the weights on the block diagonal: 2 fp16 terms x 64 rows x F * ic columns
+        assert packed.numel() == 2 * 2 * 64 * ic * fold, packed.numel()
     sums = None
     if (nb * h * w) % 32 == 0:
         sums = torch.full((nb * h * w // 32, oc), float("nan"), dtype=torch.float32, device="cuda")
