@@ -181,6 +181,22 @@ typedef struct sdx_gemm_desc {
 } sdx_gemm_desc;
 int sdx_gemm(sdx_ctx* ctx, const sdx_gemm_desc* d, sdx_stream s);
 
+/* Fused CTC projection + argmax (CtcProjection.ArgMax, src/Decoding/CtcProjection.cs:47-55;
+ * MatMul.TryArgMax, src/Decoding/Kernels/MatMul.ArgMax.cs:29-70): for each of the m rows of the Gemm
+ * `gemm` (a [m, k] fp16 x packed B [k, n] + bias; act none, no residual; y unused), the index of the
+ * largest logit (ties keep the first) into indices (int32 [m]) and its softmax probability over the
+ * row into probs (fp32 [m]); the [m, n] logits are never stored. The tensor-core epilogue folds each
+ * 128-column tile into (max, index, online denominator) as UpdateArgMax does; a second kernel merges
+ * the tiles in column order. scratch: sdx_gemm_argmax_scratch_bytes(m, n) bytes of device memory.
+ * A non-finite logit records SDX_DEV_NONFINITE (0x201) in the device error word and writes index -1
+ * (the reference throws InvalidDataException); sdx_stream_sync then returns SDX_ERR_DEVICE. */
+typedef struct sdx_gemm_argmax_desc {
+  sdx_gemm_desc gemm;
+  sdx_dptr indices, probs, scratch;
+} sdx_gemm_argmax_desc;
+size_t sdx_gemm_argmax_scratch_bytes(int m, int n);
+int sdx_gemm_argmax(sdx_ctx* ctx, const sdx_gemm_argmax_desc* d, sdx_stream s);
+
 /* ConvTranspose node, stride == kernel, no pad (ConvTP, src/Engine/ExecPlan.cs:108-114;
  * Nhwc.ConvTranspose / ConvTDot, src/Kernels/Nhwc.Det.cs:51-131). x fp16 NHWC, y [b, ih*kh, iw*kw, oc]. */
 typedef struct sdx_convt_desc {
@@ -306,6 +322,72 @@ int sdx_concat_nearest(sdx_ctx* ctx, int batch, int oh, int ow, int nin, const i
 int sdx_binary(sdx_ctx* ctx, int64_t n, int op, int relu, sdx_dptr a, sdx_dptr b, sdx_dptr y, sdx_stream s);
 /* Activation node (Act.Apply, src/Kernels/Act.cs:70-81), fp16. */
 int sdx_act(sdx_ctx* ctx, int64_t n, int act, sdx_dptr x, sdx_dptr y, sdx_stream s);
+
+/* Elementwise binary with numpy broadcasting (Ops.Elementwise, src/Kernels/Ops.cs:388-441):
+ * y = act(a op b) over out_shape; a_shape / b_shape are right-aligned to `rank` (leading 1s for a
+ * lower-rank operand) and each dim is 1 or the output's. act: the EwP activation (relu fused in the
+ * reference; the others applied after, the same elementwise result). Storage per operand fp16 or
+ * fp32 (sdx_dtype), arithmetic fp32; y contiguous. */
+#define SDX_BCAST_MAX_RANK 6
+typedef struct sdx_bcast_desc {
+  int rank;
+  int64_t out_shape[SDX_BCAST_MAX_RANK], a_shape[SDX_BCAST_MAX_RANK], b_shape[SDX_BCAST_MAX_RANK];
+  int op, act;
+  int a_dtype, b_dtype, y_dtype;
+  sdx_dptr a, b, y;
+} sdx_bcast_desc;
+int sdx_binary_bcast(sdx_ctx* ctx, const sdx_bcast_desc* d, sdx_stream s);
+
+/* SafeDiv fused op: y = clamp(a / max(b, eps), lo, hi) over n same-shape elements, fp32 arithmetic
+ * (SafeDivOp, src/Engine/Fusions/SafeDivOp.cs:14-34; FusedKernels.SafeDiv, src/Kernels/FusedKernels.cs:32-55). */
+typedef struct sdx_safediv_desc {
+  int64_t n;
+  float eps, lo, hi;
+  int dtype;  /* storage of a, b and y (sdx_dtype) */
+  sdx_dptr a, b, y;
+} sdx_safediv_desc;
+int sdx_safe_div(sdx_ctx* ctx, const sdx_safediv_desc* d, sdx_stream s);
+
+/* ChannelShift fused op, NHWC (ChannelShiftOp / ShiftP, src/Engine/Fusions/ChannelShiftOp.cs:9-66;
+ * FusedKernels.ChannelShift, src/Kernels/FusedKernels.cs:196-221): channel group g = [end[g-1], end[g])
+ * reads y[n, y, x, ch] = x[n, y + off[g], x, ch] (axis 2) or x[n, y, x + off[g], ch] (axis 3), zero
+ * outside the image; channels from the last end on are copied. Up to 8 groups. */
+typedef struct sdx_shift_desc {
+  int batch, h, w, c;
+  int axis;  /* 2: shift along H, 3: along W (the logical NCHW axis) */
+  int ngroups;
+  int group_ends[8], offsets[8];
+  int dtype;
+  sdx_dptr x, y;
+} sdx_shift_desc;
+int sdx_channel_shift(sdx_ctx* ctx, const sdx_shift_desc* d, sdx_stream s);
+
+/* UpHead fused network tail, NHWC (UpHeadOp / UpHeadP, src/Engine/Fusions/UpHeadOp.cs:9-30;
+ * FusedKernels.UpHead, src/Kernels/FusedKernels.cs:71-193): y[n, oy, ox, o] = act(bias[o] +
+ * sum_c w[o, c] * s[c]), s = [relu](bilinear resize of x by (scale_h, scale_w)) + [relu](skip), the
+ * full-resolution resize / add tensors never stored. x [batch, ih, iw, c], skip and y at [oh, ow];
+ * w fp32 [oc][c] (the 1x1 conv's weights), bias fp32 [oc] or 0; oc <= 8, c % 4 == 0, c <= 128;
+ * act none, relu or sigmoid. The reference's recomputed-skip variant (UpHeadP.SkipConv) has no CUDA
+ * kernel: run the skip conv, then this. */
+typedef struct sdx_uphead_desc {
+  int batch, ih, iw, c, oh, ow, oc;
+  float scale_h, scale_w;
+  int resize_relu, skip_relu, act;
+  int x_dtype, skip_dtype, y_dtype;
+  sdx_dptr x, skip, w, bias, y;
+} sdx_uphead_desc;
+int sdx_uphead(sdx_ctx* ctx, const sdx_uphead_desc* d, sdx_stream s);
+
+/* Batched MatMul of two activations (ExecOp.MatMul, Ops.MatMul src/Kernels/Ops.Seq.cs:90-113):
+ * a [.., m, k] x b [.., k, n] -> y [batch dims, m, n] with numpy broadcast over the batch dims (shapes
+ * right-aligned to `rank` >= 2, leading 1s). fp32 accumulation in ascending k. */
+typedef struct sdx_matmul_desc {
+  int rank;
+  int64_t a_shape[SDX_BCAST_MAX_RANK], b_shape[SDX_BCAST_MAX_RANK];
+  int a_dtype, b_dtype, y_dtype;
+  sdx_dptr a, b, y;
+} sdx_matmul_desc;
+int sdx_matmul(sdx_ctx* ctx, const sdx_matmul_desc* d, sdx_stream s);
 /* Storage conversion / boundary relayout: fp32 <-> fp16, NCHW <-> NHWC (VkSession f32to16 / f16to32
  * staging, src/Backends/Vulkan/VkSession.cs:286-310). */
 int sdx_convert(sdx_ctx* ctx, int batch, int c, int64_t hw, int x_dtype, int x_layout, int y_dtype, int y_layout,
@@ -332,7 +414,9 @@ enum sdx_op_kind {
   SDX_OP_CONV = 1, SDX_OP_GEMM = 2, SDX_OP_CONVT = 3, SDX_OP_POOL = 4, SDX_OP_CHANNEL_GATE = 5,
   SDX_OP_CHANNEL_BROADCAST = 6, SDX_OP_RESIZE_NEAREST = 7, SDX_OP_CONCAT = 8, SDX_OP_BINARY = 9, SDX_OP_ACT = 10,
   SDX_OP_CONVERT = 11, SDX_OP_LAYERNORM = 12, SDX_OP_SOFTMAX = 13, SDX_OP_ATTENTION = 14,
-  SDX_OP_CONCAT_NEAREST = 15, SDX_OP_IMAGE = 16, SDX_OP_IMAGE_CONV = 17, SDX_OP_CONVT_CHAIN = 18
+  SDX_OP_CONCAT_NEAREST = 15, SDX_OP_IMAGE = 16, SDX_OP_IMAGE_CONV = 17, SDX_OP_CONVT_CHAIN = 18,
+  SDX_OP_BINARY_BCAST = 19, SDX_OP_SAFE_DIV = 20, SDX_OP_CHANNEL_SHIFT = 21, SDX_OP_UPHEAD = 22,
+  SDX_OP_MATMUL = 23, SDX_OP_GEMM_ARGMAX = 24
 };
 /* Generic argument block for the ops without a descriptor struct. */
 typedef struct sdx_misc_desc {

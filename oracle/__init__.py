@@ -344,3 +344,123 @@ def softmax(x) -> np.ndarray:
     y = np.empty_like(x)
     lib().orc_softmax(_p(x), _p(y), x.size // c, c)
     return y
+
+
+# ---------------------------------------------------------------------------------------------
+# Elementwise with numpy broadcast, the built-in fused ops, batched MatMul and the fused CTC head,
+# restated in numpy (fp32 storage and arithmetic; IEEE per element like the reference's scalar and
+# Vector<float> code).
+# ---------------------------------------------------------------------------------------------
+def binary_bcast(a, b, op="add", act_kind="none") -> np.ndarray:
+    """Ops.Elementwise (src/Kernels/Ops.cs:388-441): numpy broadcasting of a and b, one IEEE fp32
+    op per element (Ew.Binary / Ew.Scalar / Ew.Channel / Strided.Binary all compute a op b), relu
+    fused, any other activation applied after (Activation)."""
+    a, b = _f32(a), _f32(b)
+    f = {"add": np.add, "sub": np.subtract, "mul": np.multiply, "div": np.divide}[op]
+    with np.errstate(divide="ignore", invalid="ignore", over="ignore"):
+        y = f(a, b, dtype=np.float32).astype(np.float32)
+    return y if act_kind == "none" else act(np.ascontiguousarray(y), act_kind)
+
+
+def safe_div(a, b, eps, lo, hi) -> np.ndarray:
+    """FusedKernels.SafeDiv (src/Kernels/FusedKernels.cs:32-55): clamp(a / max(b, eps), lo, hi)."""
+    a, b = _f32(a), _f32(b)
+    with np.errstate(divide="ignore", invalid="ignore", over="ignore"):
+        q = a / np.maximum(b, np.float32(eps))
+    return np.minimum(np.maximum(q, np.float32(lo)), np.float32(hi)).astype(np.float32)
+
+
+def channel_shift(x, axis, group_ends, offsets) -> np.ndarray:
+    """FusedKernels.ChannelShift (src/Kernels/FusedKernels.cs:196-221), NHWC x [n, h, w, c]: channel
+    group g = [end[g-1], end[g]) reads in[y + off[g], x] (axis 2) or in[y, x + off[g]] (axis 3),
+    zero outside; channels from the last end on are copied."""
+    x = _f32(x)
+    n, h, w, c = x.shape
+    y = x.copy()
+    g0 = 0
+    for g1, off in zip(group_ends, offsets):
+        src = np.zeros((n, h, w, g1 - g0), np.float32)
+        if axis == 2:
+            lo, hi = max(0, -off), min(h, h - off)
+            if lo < hi:
+                src[:, lo:hi] = x[:, lo + off:hi + off, :, g0:g1]
+        else:
+            lo, hi = max(0, -off), min(w, w - off)
+            if lo < hi:
+                src[:, :, lo:hi] = x[:, :, lo + off:hi + off, g0:g1]
+        y[..., g0:g1] = src
+        g0 = g1
+    return y
+
+
+def _resize_axis(out_len, in_len, scale):
+    """Nhwc.ResizeAxis (src/Kernels/Nhwc.cs:773-783) in fp32."""
+    o = np.arange(out_len, dtype=np.float32)
+    f = ((o + np.float32(0.5)) / np.float32(scale) - np.float32(0.5)).astype(np.float32)
+    fl = np.floor(f)
+    i0 = np.clip(fl.astype(np.int64), 0, in_len - 1)
+    i1 = np.clip(fl.astype(np.int64) + 1, 0, in_len - 1)
+    return i0, i1, (f - fl).astype(np.float32)
+
+
+def uphead(x, skip, w, bias, scale_h, scale_w, resize_relu=False, skip_relu=False, act_kind="none") -> np.ndarray:
+    """FusedKernels.UpHead (src/Kernels/FusedKernels.cs:71-193), NHWC: s = [relu](bilinear(x)) +
+    [relu](skip) with ResizePixel's separate fp32 multiply and add (src/Kernels/Nhwc.cs:788-815),
+    then y[o] = act(bias[o] + sum_c w[o, c] s[c]) with one fused multiply-add per channel, ascending
+    (the AVX tiers' FMA chain; fp64 product and sum rounded once to fp32)."""
+    x, skip, w = _f32(x), _f32(skip), _f32(w)
+    n, ih, iw, c = x.shape
+    oh, ow = skip.shape[1], skip.shape[2]
+    y0, y1, wy = _resize_axis(oh, ih, scale_h)
+    x0, x1, wx = _resize_axis(ow, iw, scale_w)
+    a = x[:, y0][:, :, x0]
+    b_ = x[:, y0][:, :, x1]
+    e = x[:, y1][:, :, x0]
+    f = x[:, y1][:, :, x1]
+    wxb = wx[None, None, :, None]
+    wyb = wy[None, :, None, None]
+    top = (a + ((b_ - a) * wxb).astype(np.float32)).astype(np.float32)
+    bot = (e + ((f - e) * wxb).astype(np.float32)).astype(np.float32)
+    v = (top + ((bot - top) * wyb).astype(np.float32)).astype(np.float32)
+    if resize_relu:
+        v = np.maximum(v, 0)
+    sk = np.maximum(skip, 0) if skip_relu else skip
+    s = (v + sk).astype(np.float32)
+    oc = w.shape[0]
+    acc = np.broadcast_to(np.zeros(oc, np.float32) if bias is None else _f32(bias), (n, oh, ow, oc)).copy()
+    for ch in range(c):
+        acc = (s[..., ch:ch + 1].astype(np.float64) * w[:, ch].astype(np.float64) + acc.astype(np.float64)).astype(np.float32)
+    return acc if act_kind == "none" else act(np.ascontiguousarray(acc), act_kind)
+
+
+def matmul_bcast(a, b) -> np.ndarray:
+    """Ops.MatMul (src/Kernels/Ops.Seq.cs:90-113): a [.., m, k] x b [.., k, n] with numpy broadcast
+    over the batch dims; each batch is the oracle's GemmKN-order matmul."""
+    a, b = _f32(a), _f32(b)
+    bs = np.broadcast_shapes(a.shape[:-2], b.shape[:-2])
+    ab = np.broadcast_to(a, bs + a.shape[-2:]).reshape((-1,) + a.shape[-2:])
+    bb = np.broadcast_to(b, bs + b.shape[-2:]).reshape((-1,) + b.shape[-2:])
+    out = np.stack([matmul(np.ascontiguousarray(ab[i]), np.ascontiguousarray(bb[i])) for i in range(ab.shape[0])])
+    return out.reshape(bs + (a.shape[-2], b.shape[-1]))
+
+
+def ctc_argmax(logits) -> tuple:
+    """MatMul.TryArgMax's per-row result (src/Decoding/Kernels/MatMul.ArgMax.cs:29-70, UpdateArgMax
+    :246-268) from the row's logits, columns in order: index of the first maximum and the online
+    softmax denominator s (a new maximum rescales s by exp(old - new) and adds 1, any other value
+    adds exp(value - max)); probability min(1, 1 / s). Vectorised over rows, sequential over columns."""
+    z = _f32(logits)
+    z = z.reshape(-1, z.shape[-1])
+    rows = z.shape[0]
+    m = np.full(rows, -np.inf, np.float32)
+    s = np.zeros(rows, np.float32)
+    best = np.zeros(rows, np.int64)
+    with np.errstate(over="ignore", invalid="ignore"):
+        for col in range(z.shape[1]):
+            v = z[:, col]
+            up = v > m
+            s = np.where(up, (s * np.exp(m - v, dtype=np.float32) + np.float32(1)).astype(np.float32),
+                         (s + np.exp(v - m, dtype=np.float32)).astype(np.float32))
+            best = np.where(up, col, best)
+            m = np.where(up, v, m)
+    return best, np.minimum(np.float32(1), np.float32(1) / s).astype(np.float32)

@@ -12,8 +12,59 @@ import numpy as np
 import oracle as O
 
 
+def fold_batchnorm(plan):
+    """The reference's load-time BatchNorm handling, restated (independently of the product's
+    rewrite): OnnxRewrites.FoldConvBatchNorm (src/Onnx/OnnxRewrites.cs:71-111) folds a BatchNorm
+    into the Conv it alone reads (no activation, pool or residual in between; conv output not a
+    graph output): scale = gamma / sqrt(var + eps), w *= scale, b = (b - mean) * scale + beta, fp32.
+    Every other BatchNorm stays and runs as x * s + t (GraphCompiler.EmitBatchNorm,
+    src/Engine/GraphCompiler.cs:1896-1922)."""
+    import copy
+    if not any(n.op == "BatchNorm" for n in plan.nodes):
+        return plan
+    P = copy.copy(plan)
+    P.values = dict(plan.values)
+    nodes = [copy.copy(n) for n in plan.nodes]
+    for n in nodes:
+        n.ins, n.outs, n.p = list(n.ins), list(n.outs), copy.copy(n.p)
+    prod = {o: m for m in nodes for o in m.outs}
+    uses = {}
+    for m in nodes:
+        for v in m.ins:
+            uses[v] = uses.get(v, 0) + 1
+        for attr in ("bias", "add", "b1", "b2", "in_scale"):
+            v = getattr(m.p, attr, None)
+            if isinstance(v, str):
+                uses[v] = uses.get(v, 0) + 1
+    keep = []
+    for n in nodes:
+        if n.op == "BatchNorm":
+            c = prod.get(n.ins[0])
+            if (c is not None and c.op == "Conv" and uses.get(n.ins[0], 0) == 1 and n.ins[0] != P.output and
+                    c.p.pool is None and not c.p.add and c.p.act == "none"):
+                g, be = P.values[n.p.gamma].const, P.values[n.p.beta].const
+                mu, var = P.values[n.p.mean].const, P.values[n.p.var].const
+                scale = (g / np.sqrt(var + np.float32(n.p.eps), dtype=np.float32)).astype(np.float32)
+                w = P.values[c.ins[1]].const
+                b0 = P.values[c.p.bias].const if c.p.bias else np.zeros(w.shape[0], np.float32)
+                wn, bn_ = "oracle.bnfold." + c.name + ".w", "oracle.bnfold." + c.name + ".b"
+                P.values[wn] = copy.copy(P.values[c.ins[1]])
+                P.values[wn].const = (w * scale.reshape(-1, 1, 1, 1)).astype(np.float32)
+                P.values[bn_] = copy.copy(P.values[c.ins[1]])
+                P.values[bn_].const = ((b0 - mu) * scale + be).astype(np.float32)
+                P.values[bn_].shape = (w.shape[0],)
+                c.ins[1] = wn
+                c.p.bias = bn_
+                c.outs[0] = n.outs[0]
+                continue
+        keep.append(n)
+    P.nodes = keep
+    return P
+
+
 class OracleSession:
     def __init__(self, plan, keep_all: bool = False):
+        plan = fold_batchnorm(plan)
         self.plan = plan
         self.keep_all = keep_all
         self._packs = {}
@@ -91,10 +142,30 @@ class OracleSession:
             elif b.ndim == 2 and a.ndim == 4 and b.shape == (a.shape[0], a.shape[3]):
                 y = O.channel_broadcast(a, b, p.op, relu=relu)
             else:
-                raise NotImplementedError(f"broadcast {a.shape} {b.shape}")
+                # numpy broadcast (Ops.Elementwise's general case)
+                return O.binary_bcast(a, b, p.op, p.act)
             if p.act not in ("none", "relu"):
                 y = O.act(y, p.act)
             return y
+        if op == "BatchNorm":
+            # not folded: x * s + t (GraphCompiler.EmitBatchNorm), two fp32 elementwise passes
+            g, be = P.values[p.gamma].const, P.values[p.beta].const
+            mu, var = P.values[p.mean].const, P.values[p.var].const
+            s = (g / np.sqrt(var + np.float32(p.eps), dtype=np.float32)).astype(np.float32)
+            t = (be - mu * s).astype(np.float32)
+            return O.binary_bcast(O.binary_bcast(env[n.ins[0]], s, "mul"), t, "add")
+        if op == "SafeDiv":
+            return O.safe_div(env[n.ins[0]], env[n.ins[1]], p.eps, p.lo, p.hi)
+        if op == "ChannelShift":
+            return O.channel_shift(env[n.ins[0]], p.axis, p.group_ends, p.offsets)
+        if op == "UpHead":
+            oc = P.values[n.outs[0]].shape[3]
+            w = P.values[n.ins[2]].const.reshape(oc, -1)
+            b = P.values[p.bias].const if p.bias else None
+            return O.uphead(env[n.ins[0]], env[n.ins[1]], w, b, p.scales[0], p.scales[1], p.resize_relu, p.skip_relu,
+                            p.act)
+        if op == "MatMul":
+            return O.matmul_bcast(env[n.ins[0]], env[n.ins[1]])
         if op == "ResizeNearest":
             add = env[n.ins[1]] if len(n.ins) > 1 else None
             return O.resize_nearest(env[n.ins[0]], p.scales, add=add, add_relu=p.add_relu)
@@ -104,6 +175,13 @@ class OracleSession:
             return O.maxpool(env[n.ins[0]], p.kernel, p.strides, p.pads, relu=p.fuse_relu)
         if op == "AvgPool":
             return O.avgpool(env[n.ins[0]], p.kernel, p.strides, p.pads, p.count_include_pad)
+        if op == "Gemm" and getattr(p, "ctc", False):
+            # CtcProjection.ArgMax: the projection, then the per-row UpdateArgMax walk; packed as the
+            # plan's [2, rows] int32 value (indices, then probabilities' fp32 bits)
+            a = env[n.ins[0]]
+            logits = O.gemm(a.reshape(-1, a.shape[-1]), self._gemm_plan(n))
+            idx, prob = O.ctc_argmax(logits)
+            return np.stack([idx.astype(np.int32), prob.astype(np.float32).view(np.int32)])
         if op == "Gemm":
             y = O.gemm(env[n.ins[0]], self._gemm_plan(n), act=p.act)
             if p.add:

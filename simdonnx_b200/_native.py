@@ -26,6 +26,8 @@ OP_CONCAT_NEAREST = 15
 OP_IMAGE = 16
 OP_IMAGE_CONV = 17
 OP_CONVT_CHAIN = 18
+OP_BINARY_BCAST, OP_SAFE_DIV, OP_CHANNEL_SHIFT, OP_UPHEAD, OP_MATMUL, OP_GEMM_ARGMAX = 19, 20, 21, 22, 23, 24
+BCAST_MAX_RANK = 6
 
 FAULT_MALLOC, FAULT_LAUNCH, FAULT_GRAPH, FAULT_D2H, FAULT_SYNC = 1, 2, 3, 4, 5
 
@@ -90,11 +92,43 @@ class ImageConvDesc(ctypes.Structure):
     _fields_ = [("image", ImageDesc), ("conv", ConvDesc)]
 
 
+class BcastDesc(ctypes.Structure):
+    _fields_ = [("rank", _i), ("out_shape", _i64 * BCAST_MAX_RANK), ("a_shape", _i64 * BCAST_MAX_RANK),
+                ("b_shape", _i64 * BCAST_MAX_RANK)] + [(n, _i) for n in ("op", "act", "a_dtype", "b_dtype", "y_dtype")] + [
+        (n, _u64) for n in ("a", "b", "y")]
+
+
+class SafeDivDesc(ctypes.Structure):
+    _fields_ = [("n", _i64), ("eps", _f), ("lo", _f), ("hi", _f), ("dtype", _i)] + [(n, _u64) for n in ("a", "b", "y")]
+
+
+class ShiftDesc(ctypes.Structure):
+    _fields_ = [(n, _i) for n in ("batch", "h", "w", "c", "axis", "ngroups")] + [
+        ("group_ends", _i * 8), ("offsets", _i * 8), ("dtype", _i), ("x", _u64), ("y", _u64)]
+
+
+class UpHeadDesc(ctypes.Structure):
+    _fields_ = [(n, _i) for n in ("batch", "ih", "iw", "c", "oh", "ow", "oc")] + [("scale_h", _f), ("scale_w", _f)] + [
+        (n, _i) for n in ("resize_relu", "skip_relu", "act", "x_dtype", "skip_dtype", "y_dtype")] + [
+        (n, _u64) for n in ("x", "skip", "w", "bias", "y")]
+
+
+class MatMulDesc(ctypes.Structure):
+    _fields_ = [("rank", _i), ("a_shape", _i64 * BCAST_MAX_RANK), ("b_shape", _i64 * BCAST_MAX_RANK)] + [
+        (n, _i) for n in ("a_dtype", "b_dtype", "y_dtype")] + [(n, _u64) for n in ("a", "b", "y")]
+
+
+class GemmArgmaxDesc(ctypes.Structure):
+    _fields_ = [("gemm", GemmDesc), ("indices", _u64), ("probs", _u64), ("scratch", _u64)]
+
+
 DESC_OF_OP = {OP_CONV: ConvDesc, OP_GEMM: GemmDesc, OP_CONVT: ConvtDesc, OP_POOL: PoolDesc,
               OP_CHANNEL_GATE: GateDesc, OP_RESIZE_NEAREST: ResizeDesc, OP_CHANNEL_BROADCAST: MiscDesc,
               OP_CONCAT: MiscDesc, OP_BINARY: MiscDesc, OP_ACT: MiscDesc, OP_CONVERT: MiscDesc,
               OP_LAYERNORM: MiscDesc, OP_SOFTMAX: MiscDesc, OP_ATTENTION: MiscDesc, OP_CONCAT_NEAREST: MiscDesc,
-              OP_IMAGE: ImageDesc, OP_IMAGE_CONV: ImageConvDesc, OP_CONVT_CHAIN: ConvtChainDesc}
+              OP_IMAGE: ImageDesc, OP_IMAGE_CONV: ImageConvDesc, OP_CONVT_CHAIN: ConvtChainDesc,
+              OP_BINARY_BCAST: BcastDesc, OP_SAFE_DIV: SafeDivDesc, OP_CHANNEL_SHIFT: ShiftDesc, OP_UPHEAD: UpHeadDesc,
+              OP_MATMUL: MatMulDesc, OP_GEMM_ARGMAX: GemmArgmaxDesc}
 
 _SIGS = {
     "sdx_abi_version": (_i, []),
@@ -154,6 +188,13 @@ _SIGS = {
     "sdx_layernorm": (_i, [_p, _i64, _i, _f, _u64, _u64, _u64, _u64, _p]),
     "sdx_softmax": (_i, [_p, _i64, _i, _i, _u64, _u64, _p]),
     "sdx_attention": (_i, [_p, _i, _i, _i, _i, _f, _u64, _u64, _p]),
+    "sdx_binary_bcast": (_i, [_p, ctypes.POINTER(BcastDesc), _p]),
+    "sdx_safe_div": (_i, [_p, ctypes.POINTER(SafeDivDesc), _p]),
+    "sdx_channel_shift": (_i, [_p, ctypes.POINTER(ShiftDesc), _p]),
+    "sdx_uphead": (_i, [_p, ctypes.POINTER(UpHeadDesc), _p]),
+    "sdx_matmul": (_i, [_p, ctypes.POINTER(MatMulDesc), _p]),
+    "sdx_gemm_argmax_scratch_bytes": (_sz, [_i, _i]),
+    "sdx_gemm_argmax": (_i, [_p, ctypes.POINTER(GemmArgmaxDesc), _p]),
     "sdx_desc_size": (_sz, [_i]),
     "sdx_session_create": (_i, [_p, _sz, ctypes.POINTER(_p)]),
     "sdx_session_arena": (_i, [_p, ctypes.POINTER(_u64), ctypes.POINTER(_sz)]),

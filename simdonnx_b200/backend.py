@@ -275,3 +275,98 @@ def attention(be: CudaBackend, qkv, batch, t, heads, d, scale):
     y = torch.empty((batch, t, heads * d), dtype=torch.float16, device=qkv.device)
     N.call("sdx_attention", be.ctx, batch, t, heads, d, scale, ptr(qkv), ptr(y), cur_stream())
     return y
+
+
+def _dt(t: torch.Tensor) -> int:
+    return N.F32 if t.dtype == torch.float32 else N.F16
+
+
+def binary_bcast(be: CudaBackend, a, b, op="add", act="none", y_dtype=torch.float16):
+    """y = act(a op b) with numpy broadcasting (sdx_binary_bcast)."""
+    shape = torch.broadcast_shapes(a.shape, b.shape)
+    r = max(1, len(shape))
+    if r > N.BCAST_MAX_RANK:
+        raise ValueError("rank above 6")
+    y = torch.empty(shape, dtype=y_dtype, device=a.device)
+    d = N.BcastDesc()
+    d.rank = r
+    full = lambda s: [1] * (r - len(s)) + list(s) if len(s) else [1] * r
+    for i, (o, x, z) in enumerate(zip(full(shape), full(a.shape), full(b.shape))):
+        d.out_shape[i], d.a_shape[i], d.b_shape[i] = o, x, z
+    d.op, d.act = N.EW[op], N.ACT[act]
+    d.a_dtype, d.b_dtype, d.y_dtype = _dt(a), _dt(b), _dt(y)
+    d.a, d.b, d.y = ptr(a.contiguous()), ptr(b.contiguous()), ptr(y)
+    N.call("sdx_binary_bcast", be.ctx, ctypes.byref(d), cur_stream())
+    return y
+
+
+def safe_div(be: CudaBackend, a, b, eps, lo, hi):
+    y = torch.empty_like(a)
+    d = N.SafeDivDesc()
+    d.n, d.eps, d.lo, d.hi, d.dtype = a.numel(), eps, lo, hi, _dt(a)
+    d.a, d.b, d.y = ptr(a), ptr(b), ptr(y)
+    N.call("sdx_safe_div", be.ctx, ctypes.byref(d), cur_stream())
+    return y
+
+
+def channel_shift(be: CudaBackend, x, axis, group_ends, offsets):
+    b, h, w, c = x.shape
+    y = torch.empty_like(x)
+    d = N.ShiftDesc()
+    d.batch, d.h, d.w, d.c, d.axis, d.ngroups = b, h, w, c, axis, len(group_ends)
+    for i, (e, o) in enumerate(zip(group_ends, offsets)):
+        d.group_ends[i], d.offsets[i] = e, o
+    d.dtype, d.x, d.y = _dt(x), ptr(x), ptr(y)
+    N.call("sdx_channel_shift", be.ctx, ctypes.byref(d), cur_stream())
+    return y
+
+
+def uphead(be: CudaBackend, x, skip, w, bias, scale_h, scale_w, resize_relu=False, skip_relu=False, act="none",
+           y_dtype=torch.float16):
+    """w: fp32 [oc, c] (the 1x1 conv weights), bias fp32 [oc] or None; x, skip NHWC."""
+    b, ih, iw, c = x.shape
+    _, oh, ow, _ = skip.shape
+    oc = w.shape[0]
+    y = torch.empty((b, oh, ow, oc), dtype=y_dtype, device=x.device)
+    d = N.UpHeadDesc()
+    d.batch, d.ih, d.iw, d.c, d.oh, d.ow, d.oc = b, ih, iw, c, oh, ow, oc
+    d.scale_h, d.scale_w = scale_h, scale_w
+    d.resize_relu, d.skip_relu, d.act = int(resize_relu), int(skip_relu), N.ACT[act]
+    d.x_dtype, d.skip_dtype, d.y_dtype = _dt(x), _dt(skip), _dt(y)
+    d.x, d.skip, d.w, d.bias, d.y = ptr(x), ptr(skip), ptr(w), ptr(bias), ptr(y)
+    N.call("sdx_uphead", be.ctx, ctypes.byref(d), cur_stream())
+    return y
+
+
+def matmul(be: CudaBackend, a, b, y_dtype=torch.float16):
+    """a [.., m, k] x b [.., k, n] with batch broadcast (sdx_matmul)."""
+    r = max(a.dim(), b.dim())
+    bs = torch.broadcast_shapes(a.shape[:-2], b.shape[:-2])
+    y = torch.empty(tuple(bs) + (a.shape[-2], b.shape[-1]), dtype=y_dtype, device=a.device)
+    d = N.MatMulDesc()
+    d.rank = r
+    fa = [1] * (r - a.dim()) + list(a.shape)
+    fb = [1] * (r - b.dim()) + list(b.shape)
+    for i in range(r):
+        d.a_shape[i], d.b_shape[i] = fa[i], fb[i]
+    d.a_dtype, d.b_dtype, d.y_dtype = _dt(a), _dt(b), _dt(y)
+    d.a, d.b, d.y = ptr(a), ptr(b), ptr(y)
+    N.call("sdx_matmul", be.ctx, ctypes.byref(d), cur_stream())
+    return y
+
+
+def gemm_argmax(be: CudaBackend, a, w_packed, n, bias=None):
+    """The fused CTC head: per row of a [m, k] (fp16) x packed B [k, n] + bias, (index of the first
+    maximum, its softmax probability); the logits are never stored (sdx_gemm_argmax)."""
+    m, k = a.shape[0], a.shape[-1]
+    idx = torch.empty(m, dtype=torch.int32, device=a.device)
+    prob = torch.empty(m, dtype=torch.float32, device=a.device)
+    scratch = torch.empty(int(N.lib().sdx_gemm_argmax_scratch_bytes(m, n)), dtype=torch.uint8, device=a.device)
+    d = N.GemmArgmaxDesc()
+    g = d.gemm
+    g.m, g.k, g.n, g.lda = m, k, n, a.stride(0)
+    g.act, g.y_dtype, g.add_dtype = N.ACT["none"], N.F32, N.F16
+    g.a, g.w, g.bias = ptr(a), ptr(w_packed), ptr(bias)
+    d.indices, d.probs, d.scratch = ptr(idx), ptr(prob), ptr(scratch)
+    N.call("sdx_gemm_argmax", be.ctx, ctypes.byref(d), cur_stream())
+    return idx, prob

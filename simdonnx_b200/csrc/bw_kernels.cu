@@ -185,9 +185,87 @@ __global__ void direct_conv_kernel(DirectArgs a) {
   }
 }
 
+// Conv + fused 2x2 stride-2 max pool (Nhwc.ConvPool / PoolBand, src/Kernels/Nhwc.cs:666-727; the
+// GPU plans fuse it for small stems, src/Engine/GraphCompiler.cs:883-904): thread = one pooled pixel
+// x 8 output channels; it computes the four conv outputs of its 2x2 window (each bias-initialised,
+// taps then input channels ascending, one FMA per term, activation), takes their max in the
+// reference's order max(max(max(s0, s1), s2), s3) and applies the optional relu. The full-size
+// conv output is never stored.
+template <int ACT>
+__global__ void conv_pool_direct_kernel(DirectArgs a) {
+  extern __shared__ float sw[];
+  const int wn = a.kh * a.kw * a.ic * a.oc;
+  for (int i = threadIdx.x; i < wn; i += blockDim.x) sw[i] = a.w[i];
+  __syncthreads();
+  const int ph = a.oh / 2, pw = a.ow / 2;
+  const int og = (a.oc + 7) / 8;
+  const int64_t total = (int64_t)a.batch * ph * pw * og;
+  for (int64_t idx = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; idx < total;
+       idx += (int64_t)gridDim.x * blockDim.x) {
+    int64_t p = idx;
+    const int px = (int)(p % pw);
+    p /= pw;
+    const int py = (int)(p % ph);
+    p /= ph;
+    const int n = (int)(p % a.batch);
+    const int g = (int)(p / a.batch);
+    const int o0 = g * 8;
+    const int no = min(8, a.oc - o0);
+    float best[8];
+#pragma unroll
+    for (int q = 0; q < 4; q++) {
+      const int oy = 2 * py + (q >> 1), ox = 2 * px + (q & 1);
+      float acc[8];
+#pragma unroll
+      for (int j = 0; j < 8; j++) acc[j] = (j < no && a.bias) ? a.bias[o0 + j] : 0.0f;
+      for (int ky = 0; ky < a.kh; ky++) {
+        const int iy = oy * a.sh + ky - a.pt;
+        if ((unsigned)iy >= (unsigned)a.ih) continue;
+        for (int kx = 0; kx < a.kw; kx++) {
+          const int ix = ox * a.sw + kx - a.pl;
+          if ((unsigned)ix >= (unsigned)a.iw) continue;
+          const float* wt = sw + ((ky * a.kw + kx) * a.ic) * a.oc + o0;
+          for (int c = 0; c < a.ic; c++) {
+            const float xv = load_x(a, n, c, iy, ix);
+            const float* wc = wt + c * a.oc;
+#pragma unroll
+            for (int j = 0; j < 8; j++)
+              if (j < no) acc[j] = fmaf(xv, wc[j], acc[j]);
+          }
+        }
+      }
+#pragma unroll
+      for (int j = 0; j < 8; j++) {
+        const float v = act_t<ACT>(acc[j]);
+        best[j] = q == 0 ? v : fmaxf(best[j], v);
+      }
+    }
+    const int64_t yo = (((int64_t)n * ph + py) * pw + px) * a.y_pix_stride + a.y_ch_off + o0;
+    for (int j = 0; j < no; j++) {
+      const float v = a.pool_relu ? fmaxf(best[j], 0.0f) : best[j];
+      if (a.y_f32) static_cast<float*>(a.y)[yo + j] = v;
+      else static_cast<__half*>(a.y)[yo + j] = __float2half_rn(v);
+    }
+  }
+}
+
 int direct_conv_launch(const DirectArgs& a, cudaStream_t st) {
   const size_t wbytes = sizeof(float) * a.kh * a.kw * a.ic * a.oc;
   if (wbytes > 96 * 1024) return set_error(SDX_ERR_NOT_SUPPORTED, "direct conv: weights exceed the smem stage");
+  if (a.pool) {
+    if (a.add || a.y_nchw) return set_error(SDX_ERR_NOT_SUPPORTED, "conv + pool: no residual, NHWC output");
+    const int64_t ptotal = (int64_t)a.batch * (a.oh / 2) * (a.ow / 2) * ((a.oc + 7) / 8);
+    if (ptotal == 0) return SDX_OK;
+    SDX_ACT_DISPATCH(a.act, ACTC, {
+      static SmemAttr attr{};
+      const int rc = raise_smem_limit(attr, (const void*)conv_pool_direct_kernel<ACTC>, 96 * 1024,
+                                      "cudaFuncSetAttribute(conv_pool_direct)");
+      if (rc) return rc;
+      conv_pool_direct_kernel<ACTC><<<grid_for(ptotal, 256), 256, wbytes, st>>>(a);
+    });
+    SDX_LAUNCH_CHECK("conv_pool_direct");
+    return SDX_OK;
+  }
   const int64_t total = (int64_t)a.batch * a.oh * a.ow * ((a.oc + 7) / 8);
   if (total == 0) return SDX_OK;
   if (stem_tiled_launch(a, st)) {

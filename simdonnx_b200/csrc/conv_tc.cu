@@ -165,6 +165,15 @@ int tc_launch(const TcProblem& p, cudaStream_t stream) {
   a.res_ch_off = p.res_ch_off;
   a.res_up = p.res_up;
   a.gap = p.gap;
+  const bool argmax = p.arg_m != nullptr;
+  if (argmax && (p.mode != TC_ROWS || convt || p.fold > 1 || p.gap || p.res || p.act != ACT_NONE || !p.arg_i ||
+                 !p.arg_s))
+    return set_error(SDX_ERR_INVALID, "tc: the fused CTC head is a plain rows-mode GEMM (no residual, act, sums)");
+  a.arg_m = p.arg_m;
+  a.arg_i = p.arg_i;
+  a.arg_s = p.arg_s;
+  a.arg_ld = p.arg_ld;
+  if (argmax && p.arg_ld < p.M) return set_error(SDX_ERR_INVALID, "tc: argmax state stride below M");
   a.fold = p.fold > 1 ? p.fold : 1;
   a.bias_mod = p.bias_mod;
   if (a.fold > 1 && (p.mode != TC_ROWS || convt || p.N != 64 || p.bias_mod * a.fold != p.N || BN != 64 ||
@@ -309,6 +318,7 @@ int tc_launch(const TcProblem& p, cudaStream_t stream) {
                  (p.out_ch_off * esz) % 16 == 0;
   if (convt) tma_out = tma_out && p.mode == TC_CONV && !chain;
   if (p.kxn) tma_out = false;  // the kx-in-N epilogue stores per thread
+  if (argmax) tma_out = false;  // the fused CTC head stores no tensor
   if (tma_out) {
     const int P = G * esz;
     a.G = G;
@@ -440,7 +450,10 @@ int tc_launch(const TcProblem& p, cudaStream_t stream) {
   cudaGetDevice(&dev);
   const int grid = std::min(total, num_sms(dev));
   int rc = SDX_OK;
-  if (chain && a.egroups == 4) {
+  if (argmax) {
+    rc = a.egroups == 4 ? launch_tc<ACT_NONE, 5, 4>(dev, grid, smem, stream, mA, mB, mOut, mRes, a)
+                        : launch_tc<ACT_NONE, 5, 2>(dev, grid, smem, stream, mA, mB, mOut, mRes, a);
+  } else if (chain && a.egroups == 4) {
     SDX_ACT_DISPATCH(a.act, ACTC, rc = (launch_tc<ACTC, 4, 4>(dev, grid, smem, stream, mA, mB, mOut, mRes, a)));
   } else if (chain) {
     SDX_ACT_DISPATCH(a.act, ACTC, rc = (launch_tc<ACTC, 4, 2>(dev, grid, smem, stream, mA, mB, mOut, mRes, a)));

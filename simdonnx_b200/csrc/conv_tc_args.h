@@ -87,6 +87,12 @@ struct TcArgs {
   // bias_mod columns and the channel sums are per 32 pixels, i.e. per 32 / fold rows: [M * fold / 32][OC]
   int fold;
   int bias_mod;
+  // fused CTC head (kernel template EPI = 5): per row and N tile, the running (max, first index of
+  // the max, online softmax denominator) over the tile's columns, stored [n_tile][M]; no output
+  float* arg_m;
+  int* arg_i;
+  float* arg_s;
+  int arg_ld;  // entries between two N tiles' states (>= M)
   unsigned int* err;
 };
 

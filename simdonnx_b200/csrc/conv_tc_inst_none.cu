@@ -17,4 +17,9 @@ template int launch_tc<ACT_NONE, 0, 4>(int, int, size_t, cudaStream_t, const CUt
                                     const CUtensorMap&, const CUtensorMap&, const TcArgs&);
 template int launch_tc<ACT_NONE, 0, 2>(int, int, size_t, cudaStream_t, const CUtensorMap&, const CUtensorMap&,
                                     const CUtensorMap&, const CUtensorMap&, const TcArgs&);
+// the fused CTC head (EPI = 5) has no activation
+template int launch_tc<ACT_NONE, 5, 4>(int, int, size_t, cudaStream_t, const CUtensorMap&, const CUtensorMap&,
+                                    const CUtensorMap&, const CUtensorMap&, const TcArgs&);
+template int launch_tc<ACT_NONE, 5, 2>(int, int, size_t, cudaStream_t, const CUtensorMap&, const CUtensorMap&,
+                                    const CUtensorMap&, const CUtensorMap&, const TcArgs&);
 }  // namespace sdx

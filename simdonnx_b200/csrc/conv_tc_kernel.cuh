@@ -1135,6 +1135,51 @@ __global__ void __launch_bounds__(tc_threads(G), 1)
         __syncwarp();
         continue;
       }
+      if (EPI == 5) {
+        // fused CTC head: this row's logits over the tile's columns, bias added, folded column by
+        // column into (max, first index of the max, online softmax denominator) exactly as the
+        // reference's UpdateArgMax does (a new maximum rescales the denominator by exp(old - new) and
+        // adds 1; any other value adds exp(value - max)); the logits are never stored
+        const int64_t row = (int64_t)tcd.m0 + row_in_tile;
+        float m = -INFINITY, s = 0.0f;
+        int best = 0;
+        bool bad = false;
+        const int nch = a.BN / 16;
+        for (int c = 0; c < nch; c++) {
+          float v[16];
+          tmem_ld16_issue(tbase + (uint32_t)(c * 16), v);
+          tmem_wait_ld();
+          tmem_ld_wait16(v);
+          if (c == nch - 1) {
+            tc_fence_before();
+            mbar_arrive(smem_u32(&acce[acc]));
+          }
+#pragma unroll
+          for (int j = 0; j < 16; j++) {
+            const int col = tcd.n0 + c * 16 + j;
+            if (col < a.N) {
+              const float x = v[j] + (a.bias ? __ldg(a.bias + col) : 0.0f);
+              bad |= !isfinite(x);
+              if (x > m) {
+                s = s * expf(m - x) + 1.0f;
+                m = x;
+                best = col;
+              } else {
+                s += expf(x - m);
+              }
+            }
+          }
+        }
+        if (row < a.M) {
+          const int64_t o = (int64_t)(tcd.n0 / a.BN) * a.arg_ld + row;
+          a.arg_m[o] = m;
+          a.arg_i[o] = best;
+          a.arg_s[o] = s;
+        }
+        if (bad) record_error(a.err, SDX_DEV_NONFINITE);
+        __syncwarp();
+        continue;
+      }
       if (EPI == 2) {
         // kx-in-N, straight-line form (fp16 out, 16-byte rows, no residual, bias or zeros in smem):
         // per 16 output channels, the three taps' columns are loaded with one wait, combined across

@@ -456,6 +456,12 @@ static int conv_route(const sdx_conv_desc* d) {
     return R_TC_CONV;
   }
   if (d->pool == 0 && d->in_scale == 0) return R_DIRECT;
+  // conv + fused 2x2/2 max pool: the small stem convs the reference's GPU plans fuse
+  // (GraphCompiler.GpuSmallConv, src/Engine/GraphCompiler.cs:28-32, :897-898): ic < 8, oc a multiple of
+  // 8 up to 128, at most 4096 weights, unit strides; NHWC output (the pooled tensor)
+  if (d->pool == 1 && d->in_scale == 0 && d->ic < 8 && d->oc % 8 == 0 && d->oc <= 128 &&
+      (int64_t)d->oc * d->ic * d->kh * d->kw <= 4096 && unit && d->y_layout == SDX_NHWC && d->add == 0)
+    return R_DIRECT;
   return R_INVALID;
 }
 
@@ -652,6 +658,9 @@ int sdx_conv2d(sdx_ctx* ctx, const sdx_conv_desc* d, sdx_stream s) {
     }
     case R_DIRECT: {
       DirectArgs a;
+      memset(&a, 0, sizeof(a));
+      a.pool = d->pool;
+      a.pool_relu = d->pool_relu;
       a.batch = d->batch; a.ih = d->ih; a.iw = d->iw; a.ic = d->ic; a.oh = d->oh; a.ow = d->ow; a.oc = d->oc;
       a.kh = d->kh; a.kw = d->kw; a.sh = d->sh; a.sw = d->sw; a.pt = d->pad_t; a.pl = d->pad_l; a.act = d->act;
       a.x = P<const void>(d->x);
@@ -698,6 +707,55 @@ int sdx_gemm(sdx_ctx* ctx, const sdx_gemm_desc* d, sdx_stream s) {
   p.act = d->act;
   p.err = ctx->err_word;
   return tc_launch(p, S(ctx, s));
+}
+
+// Scratch of the fused CTC head: per row and 128-column tile the (max, index, denominator) state,
+// [n_tiles][m] each, every array 256-byte aligned.
+static size_t argmax_part_bytes(int m) { return ((size_t)m * 4 + 255) / 256 * 256; }
+
+size_t sdx_gemm_argmax_scratch_bytes(int m, int n) {
+  if (m <= 0 || n <= 0) return 0;
+  int BN, nt;
+  tc_plan_n(n, &BN, &nt);
+  return 3 * (size_t)nt * argmax_part_bytes(m);
+}
+
+int sdx_gemm_argmax(sdx_ctx* ctx, const sdx_gemm_argmax_desc* dd, sdx_stream s) {
+  USE(ctx);
+  if (!dd) return set_error(SDX_ERR_INVALID, "null desc");
+  const sdx_gemm_desc* d = &dd->gemm;
+  if (d->m <= 0 || d->n <= 0 || d->k <= 0) return set_error(SDX_ERR_INVALID, "gemm argmax: empty problem");
+  if (!dd->indices || !dd->probs || !dd->scratch) return set_error(SDX_ERR_INVALID, "gemm argmax: null output or scratch");
+  if (d->add || d->act != SDX_ACT_NONE)
+    return set_error(SDX_ERR_NOT_SUPPORTED, "gemm argmax: the CTC projection has no residual or activation");
+  if (dd->scratch & 255) return set_error(SDX_ERR_INVALID, "gemm argmax: scratch must be 256-byte aligned");
+  LAUNCH_GUARD();
+  int BN, nt;
+  tc_plan_n(d->n, &BN, &nt);
+  const size_t part = (size_t)nt * argmax_part_bytes(d->m);
+  TcProblem p;
+  memset(&p, 0, sizeof(p));
+  p.mode = TC_ROWS;
+  p.a = P<const __half>(d->a);
+  p.lda = d->lda > 0 ? d->lda : d->k;
+  p.M = d->m;
+  p.K = d->k;
+  p.w = P<const __half>(d->w);
+  p.wterms = 2;
+  p.N = d->n;
+  p.bias = P<const float>(d->bias);
+  p.act = SDX_ACT_NONE;
+  p.out_pix_stride = d->n;
+  p.arg_m = P<float>(dd->scratch);
+  p.arg_i = P<int>(dd->scratch + part);
+  p.arg_s = P<float>(dd->scratch + 2 * part);
+  p.arg_ld = (int)(argmax_part_bytes(d->m) / 4);  // tile t's states start at t * arg_ld (256-byte rows)
+  p.err = ctx->err_word;
+  cudaStream_t st = S(ctx, s);
+  int rc = tc_launch(p, st);
+  if (rc) return rc;
+  return ctc_argmax_merge_launch(p.arg_m, p.arg_i, p.arg_s, d->m, p.arg_ld, nt, P<int>(dd->indices),
+                                 P<float>(dd->probs), ctx->err_word, st);
 }
 
 int sdx_convt(sdx_ctx* ctx, const sdx_convt_desc* d, sdx_stream s) {
@@ -1019,6 +1077,141 @@ int sdx_attention(sdx_ctx* ctx, int batch, int t, int heads, int d, float scale,
   USE(ctx);
   LAUNCH_GUARD();
   return attention_launch(batch, t, heads, d, scale, P<const __half>(qkv), P<__half>(y), S(ctx, s));
+}
+
+static bool dtype_ok(int t) { return t == SDX_F16 || t == SDX_F32; }
+
+int sdx_binary_bcast(sdx_ctx* ctx, const sdx_bcast_desc* d, sdx_stream s) {
+  USE(ctx);
+  if (!d) return set_error(SDX_ERR_INVALID, "null desc");
+  if (d->rank < 1 || d->rank > SDX_BCAST_MAX_RANK) return set_error(SDX_ERR_INVALID, "bcast: rank must be 1..6");
+  if (d->op < 0 || d->op > 3 || d->act < 0 || d->act > 5) return set_error(SDX_ERR_INVALID, "bcast: bad op or act");
+  if (!dtype_ok(d->a_dtype) || !dtype_ok(d->b_dtype) || !dtype_ok(d->y_dtype))
+    return set_error(SDX_ERR_INVALID, "bcast: bad dtype");
+  if (!d->a || !d->b || !d->y) return set_error(SDX_ERR_INVALID, "bcast: null pointer");
+  BcastArgs p;
+  memset(&p, 0, sizeof(p));
+  p.rank = d->rank;
+  int64_t sa = 1, sb = 1, n = 1;
+  for (int i = d->rank - 1; i >= 0; i--) {
+    const int64_t o = d->out_shape[i], ea = d->a_shape[i], eb = d->b_shape[i];
+    if (o < 0 || (ea != o && ea != 1) || (eb != o && eb != 1))
+      return set_error(SDX_ERR_INVALID, "bcast: dim %d: %lld vs %lld / %lld do not broadcast", i, (long long)o,
+                       (long long)ea, (long long)eb);
+    p.shape[i] = o;
+    p.sa[i] = ea == 1 ? 0 : sa;
+    p.sb[i] = eb == 1 ? 0 : sb;
+    sa *= ea;
+    sb *= eb;
+    n *= o;
+  }
+  p.n = n;
+  p.op = d->op;
+  p.act = d->act;
+  p.a_f32 = d->a_dtype == SDX_F32;
+  p.b_f32 = d->b_dtype == SDX_F32;
+  p.y_f32 = d->y_dtype == SDX_F32;
+  p.a = P<const void>(d->a);
+  p.b = P<const void>(d->b);
+  p.y = P<void>(d->y);
+  LAUNCH_GUARD();
+  return bcast_binary_launch(p, S(ctx, s));
+}
+
+int sdx_safe_div(sdx_ctx* ctx, const sdx_safediv_desc* d, sdx_stream s) {
+  USE(ctx);
+  if (!d) return set_error(SDX_ERR_INVALID, "null desc");
+  if (d->n < 0 || !dtype_ok(d->dtype)) return set_error(SDX_ERR_INVALID, "safediv: bad size or dtype");
+  if (!(d->eps > 0.0f)) return set_error(SDX_ERR_INVALID, "safediv: eps must be > 0");
+  if (d->n && (!d->a || !d->b || !d->y)) return set_error(SDX_ERR_INVALID, "safediv: null pointer");
+  LAUNCH_GUARD();
+  return safediv_launch(d->n, d->eps, d->lo, d->hi, d->dtype == SDX_F32, P<const void>(d->a), P<const void>(d->b),
+                        P<void>(d->y), S(ctx, s));
+}
+
+int sdx_channel_shift(sdx_ctx* ctx, const sdx_shift_desc* d, sdx_stream s) {
+  USE(ctx);
+  if (!d) return set_error(SDX_ERR_INVALID, "null desc");
+  if (d->batch < 0 || d->h < 0 || d->w < 0 || d->c < 0 || (d->axis != 2 && d->axis != 3) || d->ngroups < 0 ||
+      d->ngroups > 8 || !dtype_ok(d->dtype))
+    return set_error(SDX_ERR_INVALID, "channel shift: bad shape, axis (2 or 3) or group count (<= 8)");
+  ShiftArgs a;
+  memset(&a, 0, sizeof(a));
+  a.batch = d->batch; a.h = d->h; a.w = d->w; a.c = d->c; a.axis = d->axis; a.ng = d->ngroups;
+  int prev = 0;
+  for (int g = 0; g < d->ngroups; g++) {
+    if (d->group_ends[g] < prev || d->group_ends[g] > d->c)
+      return set_error(SDX_ERR_INVALID, "channel shift: group ends must ascend within c");
+    a.ends[g] = prev = d->group_ends[g];
+    a.offs[g] = d->offsets[g];
+  }
+  a.f32 = d->dtype == SDX_F32;
+  a.x = P<const void>(d->x);
+  a.y = P<void>(d->y);
+  LAUNCH_GUARD();
+  return channel_shift_launch(a, S(ctx, s));
+}
+
+int sdx_uphead(sdx_ctx* ctx, const sdx_uphead_desc* d, sdx_stream s) {
+  USE(ctx);
+  if (!d) return set_error(SDX_ERR_INVALID, "null desc");
+  if (d->batch < 0 || d->ih <= 0 || d->iw <= 0 || d->oh < 0 || d->ow < 0 || !(d->scale_h > 0) || !(d->scale_w > 0) ||
+      !dtype_ok(d->x_dtype) || !dtype_ok(d->skip_dtype) || !dtype_ok(d->y_dtype))
+    return set_error(SDX_ERR_INVALID, "uphead: bad shape, scale or dtype");
+  if (!d->x || !d->skip || !d->w || !d->y) return set_error(SDX_ERR_INVALID, "uphead: null pointer");
+  UpHeadArgs a;
+  memset(&a, 0, sizeof(a));
+  a.batch = d->batch; a.ih = d->ih; a.iw = d->iw; a.c = d->c; a.oh = d->oh; a.ow = d->ow; a.oc = d->oc;
+  a.sy = d->scale_h; a.sx = d->scale_w;
+  a.resize_relu = d->resize_relu; a.skip_relu = d->skip_relu; a.act = d->act;
+  a.x_f32 = d->x_dtype == SDX_F32; a.skip_f32 = d->skip_dtype == SDX_F32; a.y_f32 = d->y_dtype == SDX_F32;
+  a.x = P<const void>(d->x);
+  a.skip = P<const void>(d->skip);
+  a.w = P<const float>(d->w);
+  a.bias = P<const float>(d->bias);
+  a.y = P<void>(d->y);
+  LAUNCH_GUARD();
+  return uphead_launch(a, S(ctx, s));
+}
+
+int sdx_matmul(sdx_ctx* ctx, const sdx_matmul_desc* d, sdx_stream s) {
+  USE(ctx);
+  if (!d) return set_error(SDX_ERR_INVALID, "null desc");
+  if (d->rank < 2 || d->rank > SDX_BCAST_MAX_RANK || !dtype_ok(d->a_dtype) || !dtype_ok(d->b_dtype) ||
+      !dtype_ok(d->y_dtype))
+    return set_error(SDX_ERR_INVALID, "matmul: rank must be 2..6; bad dtype");
+  const int r = d->rank;
+  const int64_t m = d->a_shape[r - 2], k = d->a_shape[r - 1], n = d->b_shape[r - 1];
+  if (d->b_shape[r - 2] != k) return set_error(SDX_ERR_INVALID, "matmul: K mismatch");
+  if (m > INT32_MAX || k > INT32_MAX || n > INT32_MAX) return set_error(SDX_ERR_NOT_SUPPORTED, "matmul: dims too large");
+  MatMulArgs p;
+  memset(&p, 0, sizeof(p));
+  p.m = (int)m;
+  p.k = (int)k;
+  p.n = (int)n;
+  p.batch_rank = r - 2;
+  int64_t batch = 1, as = m * k, bs = k * n;
+  for (int i = r - 3; i >= 0; i--) {
+    const int64_t ea = d->a_shape[i], eb = d->b_shape[i], o = ea == 1 ? eb : ea;
+    if ((ea != o && ea != 1) || (eb != o && eb != 1) || o < 0)
+      return set_error(SDX_ERR_INVALID, "matmul: batch dim %d does not broadcast", i);
+    p.bshape[i] = o;
+    p.a_bstride[i] = ea == 1 ? 0 : as;
+    p.b_bstride[i] = eb == 1 ? 0 : bs;
+    as *= ea;
+    bs *= eb;
+    batch *= o;
+  }
+  if (batch > INT32_MAX) return set_error(SDX_ERR_NOT_SUPPORTED, "matmul: batch too large");
+  p.batch = (int)batch;
+  p.a_f32 = d->a_dtype == SDX_F32;
+  p.b_f32 = d->b_dtype == SDX_F32;
+  p.y_f32 = d->y_dtype == SDX_F32;
+  p.a = P<const void>(d->a);
+  p.b = P<const void>(d->b);
+  p.y = P<void>(d->y);
+  LAUNCH_GUARD();
+  return batched_matmul_launch(p, S(ctx, s));
 }
 
 }  // extern "C"

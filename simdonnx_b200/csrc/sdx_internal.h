@@ -74,6 +74,12 @@ struct TcProblem {
   // bias repeats every OC columns; gap (if any) is still [pixels / 32][OC]
   int fold;
   int bias_mod;
+  // fused CTC head (rows mode, no output tensor): per row and N tile the argmax state over the
+  // tile's columns of act(bias + A x B) ([n_tiles][M] each; merged by ctc_argmax_merge_launch)
+  float* arg_m;
+  int* arg_i;
+  float* arg_s;
+  int arg_ld;  // entries between two N tiles' states (>= M)
   void* out;
   int out_f32;
   int64_t out_pix_stride;
@@ -139,6 +145,9 @@ struct DirectArgs {
   int64_t y_pix_stride;
   int y_ch_off;
   unsigned int* err;  // device error word (bounded waits of the TMA-fed stem)
+  // fused 2x2 stride-2 max pool (ConvP.Pool): y is [batch, oh / 2, ow / 2, oc] NHWC (odd last
+  // rows / columns of the conv output dropped), relu after the max when pool_relu
+  int pool, pool_relu;
 };
 int direct_conv_launch(const DirectArgs& a, cudaStream_t st);
 bool stem_tiled_launch(const DirectArgs& a, cudaStream_t st);
@@ -214,5 +223,53 @@ int layernorm_launch(int64_t rows, int c, float eps, const __half* x, const floa
 int softmax_launch(int64_t rows, int c, int y_f32, const __half* x, void* y, cudaStream_t st);
 int attention_launch(int batch, int t, int heads, int d, float scale, const __half* qkv, __half* y, cudaStream_t st);
 int bounded_wait_selftest_launch(unsigned int* err, int wait_ms, cudaStream_t st);
+
+// ---- ext_kernels.cu: broadcast elementwise, fused ops, batched MatMul, CTC argmax merge
+constexpr int BCAST_RANK_MAX = 6;
+struct BcastArgs {
+  int rank;                              // output rank (1 .. BCAST_RANK_MAX)
+  int64_t shape[BCAST_RANK_MAX];     // output shape (contiguous output)
+  int64_t sa[BCAST_RANK_MAX], sb[BCAST_RANK_MAX];  // element strides, 0 on broadcast dims
+  int64_t n;                             // output elements
+  int op, act, a_f32, b_f32, y_f32;
+  const void* a;
+  const void* b;
+  void* y;
+};
+int bcast_binary_launch(const BcastArgs& p, cudaStream_t st);
+int safediv_launch(int64_t n, float eps, float lo, float hi, int f32, const void* a, const void* b, void* y,
+                   cudaStream_t st);
+struct ShiftArgs {
+  int batch, h, w, c, axis, ng;
+  int ends[8], offs[8];
+  int f32;
+  const void* x;
+  void* y;
+};
+int channel_shift_launch(const ShiftArgs& a, cudaStream_t st);
+struct UpHeadArgs {
+  int batch, ih, iw, c, oh, ow, oc;
+  float sy, sx;  // resize scales (output / input) of H and W
+  int resize_relu, skip_relu, act;
+  int x_f32, skip_f32, y_f32;
+  const void* x;
+  const void* skip;
+  const float* w;     // [oc][c]
+  const float* bias;  // [oc] or null
+  void* y;
+};
+int uphead_launch(const UpHeadArgs& a, cudaStream_t st);
+struct MatMulArgs {
+  int batch, m, k, n;
+  int batch_rank;                               // output batch dims (<= 6)
+  int64_t bshape[6], a_bstride[6], b_bstride[6];  // batch shape and per-operand element strides (0 = broadcast)
+  int a_f32, b_f32, y_f32;
+  const void* a;
+  const void* b;
+  void* y;
+};
+int batched_matmul_launch(const MatMulArgs& p, cudaStream_t st);
+int ctc_argmax_merge_launch(const float* pm, const int* pi, const float* ps, int rows, int ld, int tiles,
+                            int* indices, float* probs, unsigned int* err, cudaStream_t st);
 
 }  // namespace sdx

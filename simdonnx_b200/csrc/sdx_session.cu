@@ -97,6 +97,12 @@ static size_t desc_size(int kind) {
     case SDX_OP_IMAGE: return sizeof(sdx_image_desc);
     case SDX_OP_IMAGE_CONV: return sizeof(sdx_image_conv_desc);
     case SDX_OP_CONVT_CHAIN: return sizeof(sdx_convt_chain_desc);
+    case SDX_OP_BINARY_BCAST: return sizeof(sdx_bcast_desc);
+    case SDX_OP_SAFE_DIV: return sizeof(sdx_safediv_desc);
+    case SDX_OP_CHANNEL_SHIFT: return sizeof(sdx_shift_desc);
+    case SDX_OP_UPHEAD: return sizeof(sdx_uphead_desc);
+    case SDX_OP_MATMUL: return sizeof(sdx_matmul_desc);
+    case SDX_OP_GEMM_ARGMAX: return sizeof(sdx_gemm_argmax_desc);
     default: return 0;
   }
 }
@@ -127,6 +133,12 @@ static int run_node(sdx_session* s, const sdx_session::Node& n) {
     case SDX_OP_LAYERNORM: return sdx_layernorm(c, m->rows, m->c, m->eps, m->x, m->w, m->bias, m->y, st);
     case SDX_OP_SOFTMAX: return sdx_softmax(c, m->rows, m->c, m->y_dtype, m->x, m->y, st);
     case SDX_OP_ATTENTION: return sdx_attention(c, m->batch, m->t, m->heads, m->d, m->scale, m->x, m->y, st);
+    case SDX_OP_BINARY_BCAST: return sdx_binary_bcast(c, static_cast<const sdx_bcast_desc*>(d), st);
+    case SDX_OP_SAFE_DIV: return sdx_safe_div(c, static_cast<const sdx_safediv_desc*>(d), st);
+    case SDX_OP_CHANNEL_SHIFT: return sdx_channel_shift(c, static_cast<const sdx_shift_desc*>(d), st);
+    case SDX_OP_UPHEAD: return sdx_uphead(c, static_cast<const sdx_uphead_desc*>(d), st);
+    case SDX_OP_MATMUL: return sdx_matmul(c, static_cast<const sdx_matmul_desc*>(d), st);
+    case SDX_OP_GEMM_ARGMAX: return sdx_gemm_argmax(c, static_cast<const sdx_gemm_argmax_desc*>(d), st);
     default: return set_error(SDX_ERR_INVALID, "unknown op kind %d", n.kind);
   }
 }

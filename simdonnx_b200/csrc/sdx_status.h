@@ -18,3 +18,4 @@
 #define SDX_DEV_WAIT_ACC_EMPTY 0x104u  // MMA issuer timed out waiting for the epilogue
 #define SDX_DEV_WAIT_DRAIN 0x105u      // wind-down wait for in-flight copies / MMAs timed out
 #define SDX_DEV_TEST_WAIT 0x1F0u       // the self-test wait kernel timed out (expected in its test)
+#define SDX_DEV_NONFINITE 0x201u       // the fused CTC head saw a non-finite logit (the reference throws)

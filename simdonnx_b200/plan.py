@@ -51,6 +51,8 @@ class GemmP:
     bias: str | None = None
     act: str = "none"
     add: str | None = None       # residual folded into the Gemm epilogue (GPU plans)
+    ctc: bool = False            # CTC head (CtcProjection.ArgMax): output i32 [2, rows] = per row the
+                                 # index of the first maximum, then its softmax probability (fp32 bits)
 
 
 @dataclass
@@ -98,6 +100,46 @@ class ImageP:
 
 
 @dataclass
+class BatchNormP:
+    """Inference BatchNormalization before the load-time rewrite (OnnxRewrites.FoldConvBatchNorm,
+    src/Onnx/OnnxRewrites.cs:71-111, or GraphCompiler.EmitBatchNorm, src/Engine/GraphCompiler.cs:1896-1922):
+    names of the fp32 [C] constants and epsilon."""
+    gamma: str
+    beta: str
+    mean: str
+    var: str
+    eps: float = 1e-5
+
+
+@dataclass
+class SafeDivP:
+    """SafeDivOp (src/Engine/Fusions/SafeDivOp.cs:9-13): out = clamp(a / max(b, eps), lo, hi)."""
+    eps: float
+    lo: float
+    hi: float
+
+
+@dataclass
+class ShiftP:
+    """ChannelShiftOp (src/Engine/Fusions/ChannelShiftOp.cs:9-14): per channel group a zero-filled
+    shift along H (axis 2) or W (axis 3)."""
+    axis: int
+    group_ends: tuple
+    offsets: tuple
+
+
+@dataclass
+class UpHeadP:
+    """UpHeadOp (src/Engine/Fusions/UpHeadOp.cs:16-30): bilinear resize of ins[0] by scales (h, w),
+    [relu], + [relu](ins[1]), 1x1 conv ins[2] ([oc, c, 1, 1]) + bias, act."""
+    scales: tuple
+    resize_relu: bool = False
+    skip_relu: bool = False
+    act: str = "none"
+    bias: str | None = None
+
+
+@dataclass
 class Value:
     name: str
     shape: tuple
@@ -112,7 +154,7 @@ class Value:
 
     @property
     def nbytes(self) -> int:
-        return int(np.prod(self.shape)) * {"f16": 2, "u8": 1}.get(self.dtype, 4)
+        return int(np.prod(self.shape)) * {"f16": 2, "u8": 1}.get(self.dtype, 4)  # f32, i32: 4
 
 
 @dataclass
@@ -224,7 +266,7 @@ class ExecPlan:
 def _param_refs(p) -> list:
     """Value ids read through op params (ExecNode.ParamRefs, src/Engine/ExecPlan.cs:246-262)."""
     refs = []
-    for attr in ("bias", "add", "b1", "b2", "in_scale"):
+    for attr in ("bias", "add", "b1", "b2", "in_scale", "gamma", "beta", "mean", "var"):
         v = getattr(p, attr, None)
         if isinstance(v, str):
             refs.append(v)

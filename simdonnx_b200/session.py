@@ -23,8 +23,10 @@ import torch
 from . import _native as N
 from . import backend as B
 from .plan import ExecPlan, Node, conv_out
+from .rewrites import fold_conv_batchnorm, lower_batchnorm
 
 _DT = {"f16": N.F16, "f32": N.F32}
+_NP = {"f16": np.float16, "f32": np.float32, "i32": np.int32, "u8": np.uint8}
 _LAY = {"nhwc": N.NHWC, "nchw": N.NCHW, "raw": N.NHWC}
 
 
@@ -33,7 +35,20 @@ def _nhwc_shape(v):
     return (s[0], s[2], s[3], s[1]) if v.layout == "nchw" else s
 
 
+def _small_stem_pool(P: ExecPlan, n) -> bool:
+    """Conv + 2x2/2 max pool that the fused small-stem kernel takes (GraphCompiler.GpuSmallConv,
+    src/Engine/GraphCompiler.cs:28-32, with the pool fused only for such convs, :897-898)."""
+    xv = P.values[n.ins[0]]
+    ic = _nhwc_shape(xv)[3]
+    W = P.values[n.ins[1]].const
+    oc = W.shape[0]
+    return (n.p.group == 1 and ic < 8 and oc % 8 == 0 and oc <= 128 and oc * ic * W.shape[2] * W.shape[3] <= 4096 and
+            tuple(n.p.strides) == (1, 1) and not n.p.add and P.values[n.outs[0]].layout == "nhwc")
+
+
 def cuda_rewrite(plan: ExecPlan) -> ExecPlan:
+    # the reference's load-time BatchNorm rewrites come first (FoldConvBatchNorm, EmitBatchNorm)
+    plan = lower_batchnorm(fold_conv_batchnorm(plan))
     P = copy.copy(plan)
     P.values = {k: copy.copy(v) for k, v in plan.values.items()}
     P.nodes = [Node(n.op, list(n.ins), list(n.outs), copy.copy(n.p), n.name) for n in plan.nodes]
@@ -41,10 +56,11 @@ def cuda_rewrite(plan: ExecPlan) -> ExecPlan:
 
     # 0. conv + fused 2x2/2 max pool (ConvP.Pool, src/Engine/ExecPlan.cs:63-64) -> conv into an arena
     #    value, then MaxPool (+relu): max of fp16-rounded values == fp16 rounding of the max, so the
-    #    result equals the fused kernel's
+    #    result equals the fused kernel's. Small stems keep the pool in their epilogue (the fused
+    #    direct kernel); the wider convs that reach here go through the tensor cores.
     out_nodes = []
     for n in P.nodes:
-        if n.op == "Conv" and n.p.pool is not None:
+        if n.op == "Conv" and n.p.pool is not None and not _small_stem_pool(P, n):
             pool = n.p.pool
             yv = P.values[n.outs[0]]
             nb, ih, iw, _ = _nhwc_shape(P.values[n.ins[0]])
@@ -263,6 +279,11 @@ class CudaInferenceSession:
             if n.op == "ChannelGate":
                 nn, h, w, c = P.shape(n.ins[0])
                 self._scratch_bytes = max(self._scratch_bytes, int(N.lib().sdx_channel_gate_scratch_bytes(nn, h * w, c)))
+            if n.op == "Gemm" and getattr(n.p, "ctc", False):
+                Wb = P.values[n.ins[1]].const
+                k, nn = (Wb.shape[1], Wb.shape[0]) if n.p.trans_b else Wb.shape
+                m = int(np.prod(P.shape(n.ins[0]))) // k
+                self._scratch_bytes = max(self._scratch_bytes, int(N.lib().sdx_gemm_argmax_scratch_bytes(m, nn)))
         total = P.arena_bytes + self._scratch_bytes + 256
         h = ctypes.c_void_p()
         with torch.cuda.device(device):
@@ -367,16 +388,80 @@ class CudaInferenceSession:
             return N.OP_CHANNEL_GATE, d
         if op == "Elementwise":
             a, b = n.ins
+            sa, sb = P.shape(a), P.shape(b)
+            va, vb, vy = P.values[a], P.values[b], P.values[n.outs[0]]
+            f16 = va.dtype == "f16" and vb.dtype == "f16" and vy.dtype == "f16"
             d = N.MiscDesc()
             d.op, d.relu = N.EW[p.op], int(p.act == "relu")
-            if P.shape(a) == P.shape(b):
-                d.n = int(np.prod(P.shape(a)))
+            if sa == sb and f16 and p.act in ("none", "relu") and int(np.prod(sa)) % 8 == 0:
+                d.n = int(np.prod(sa))
                 d.a, d.b, d.y = self.ptr(a), self.ptr(b), self.ptr(n.outs[0])
                 return N.OP_BINARY, d
-            nb, c = P.shape(a)[0], P.shape(a)[-1]
-            d.batch, d.c, d.pixels = nb, c, int(np.prod(P.shape(a))) // (nb * c)
-            d.x, d.b, d.y = self.ptr(a), self.ptr(b), self.ptr(n.outs[0])
-            return N.OP_CHANNEL_BROADCAST, d
+            if (len(sa) == 4 and sb == (sa[0], sa[3]) and va.dtype == "f16" and vy.dtype == "f16" and vb.dtype == "f32"
+                    and p.act in ("none", "relu") and not vb.is_const):
+                nb, c = sa[0], sa[-1]
+                d.batch, d.c, d.pixels = nb, c, int(np.prod(sa)) // (nb * c)
+                d.x, d.b, d.y = self.ptr(a), self.ptr(b), self.ptr(n.outs[0])
+                return N.OP_CHANNEL_BROADCAST, d
+            # numpy broadcast (Ops.Elementwise's general case); the plan's [N, C] gate vector is
+            # [N, 1, 1, C] against an NHWC tensor
+            if len(sb) == 2 and len(sa) == 4 and sb == (sa[0], sa[3]):
+                sb = (sa[0], 1, 1, sa[3])
+            if len(sa) == 2 and len(sb) == 4 and sa == (sb[0], sb[3]):
+                sa = (sb[0], 1, 1, sb[3])
+            out = np.broadcast_shapes(sa, sb)
+            r = len(out)
+            full = lambda s: [1] * (r - len(s)) + list(s)
+            bd = N.BcastDesc()
+            bd.rank = r
+            for i, (o, x, z) in enumerate(zip(out, full(sa), full(sb))):
+                bd.out_shape[i], bd.a_shape[i], bd.b_shape[i] = o, x, z
+            bd.op, bd.act = N.EW[p.op], N.ACT[p.act]
+            bd.a_dtype, bd.b_dtype, bd.y_dtype = _DT[va.dtype], _DT[vb.dtype], _DT[vy.dtype]
+            bd.a = self._f32(a) if va.is_const else self.ptr(a)
+            bd.b = self._f32(b) if vb.is_const else self.ptr(b)
+            bd.y = self.ptr(n.outs[0])
+            return N.OP_BINARY_BCAST, bd
+        if op == "SafeDiv":
+            va = P.values[n.ins[0]]
+            d = N.SafeDivDesc()
+            d.n, d.eps, d.lo, d.hi, d.dtype = int(np.prod(va.shape)), p.eps, p.lo, p.hi, _DT[va.dtype]
+            d.a, d.b, d.y = self.ptr(n.ins[0]), self.ptr(n.ins[1]), self.ptr(n.outs[0])
+            return N.OP_SAFE_DIV, d
+        if op == "ChannelShift":
+            nb, h, w, c = P.shape(n.ins[0])
+            d = N.ShiftDesc()
+            d.batch, d.h, d.w, d.c, d.axis, d.ngroups = nb, h, w, c, p.axis, len(p.group_ends)
+            for i, (e, o) in enumerate(zip(p.group_ends, p.offsets)):
+                d.group_ends[i], d.offsets[i] = e, o
+            d.dtype, d.x, d.y = _DT[P.values[n.ins[0]].dtype], self.ptr(n.ins[0]), self.ptr(n.outs[0])
+            return N.OP_CHANNEL_SHIFT, d
+        if op == "UpHead":
+            x, skip, wv = n.ins
+            nb, ih, iw, c = P.shape(x)
+            _, oh, ow, oc = P.shape(n.outs[0])
+            W = P.values[wv].const.reshape(oc, c)
+            d = N.UpHeadDesc()
+            d.batch, d.ih, d.iw, d.c, d.oh, d.ow, d.oc = nb, ih, iw, c, oh, ow, oc
+            d.scale_h, d.scale_w = p.scales
+            d.resize_relu, d.skip_relu, d.act = int(p.resize_relu), int(p.skip_relu), N.ACT[p.act]
+            d.x_dtype, d.skip_dtype = _DT[P.values[x].dtype], _DT[P.values[skip].dtype]
+            d.y_dtype = _DT[P.values[n.outs[0]].dtype]
+            wt = self._const_dev(("uphead", n.name), lambda: torch.from_numpy(np.ascontiguousarray(W)).to(self.device))
+            d.x, d.skip, d.w, d.bias, d.y = self.ptr(x), self.ptr(skip), B.ptr(wt), self._f32(p.bias), self.ptr(n.outs[0])
+            return N.OP_UPHEAD, d
+        if op == "MatMul":
+            a, b = n.ins
+            sa, sb = P.shape(a), P.shape(b)
+            r = max(len(sa), len(sb))
+            d = N.MatMulDesc()
+            d.rank = r
+            for i, (x, z) in enumerate(zip([1] * (r - len(sa)) + list(sa), [1] * (r - len(sb)) + list(sb))):
+                d.a_shape[i], d.b_shape[i] = x, z
+            d.a_dtype, d.b_dtype = _DT[P.values[a].dtype], _DT[P.values[b].dtype]
+            d.y_dtype = _DT[P.values[n.outs[0]].dtype]
+            d.a, d.b, d.y = self.ptr(a), self.ptr(b), self.ptr(n.outs[0])
+            return N.OP_MATMUL, d
         if op == "ResizeNearest":
             x = n.ins[0]
             nb, ih, iw, c = P.shape(x)
@@ -475,6 +560,22 @@ class CudaInferenceSession:
             d.is_avg, d.relu, d.count_include_pad = int(op == "AvgPool"), int(p.fuse_relu), int(p.count_include_pad)
             d.x, d.y = self.ptr(n.ins[0]), self.ptr(n.outs[0])
             return N.OP_POOL, d
+        if op == "Gemm" and getattr(p, "ctc", False):
+            # CTC head: indices (int32 [rows]) then probabilities (fp32 [rows]) in the output value
+            a = n.ins[0]
+            Wb = P.values[n.ins[1]].const
+            k, nn = (Wb.shape[1], Wb.shape[0]) if p.trans_b else Wb.shape
+            m = int(np.prod(P.shape(a))) // k
+            d = N.GemmArgmaxDesc()
+            g = d.gemm
+            g.m, g.k, g.n, g.lda = m, k, nn, k
+            g.act, g.y_dtype, g.add_dtype = N.ACT["none"], N.F32, N.F16
+            wt = self._const_dev(("gemmw", n.name), lambda: B.pack_gemm(Wb, p.trans_b, self.device))
+            g.a, g.w, g.bias = self.ptr(a), B.ptr(wt), self._f32(p.bias)
+            d.indices = self.ptr(n.outs[0])
+            d.probs = self.ptr(n.outs[0]) + 4 * m
+            d.scratch = self.scratch
+            return N.OP_GEMM_ARGMAX, d
         if op == "Gemm":
             a = n.ins[0]
             Wb = P.values[n.ins[1]].const
@@ -560,13 +661,13 @@ class CudaInferenceSession:
     def read(self, name: str) -> np.ndarray:
         """A value's arena contents as fp32 (dense values only)."""
         v = self.plan.values[name]
-        dt = np.float16 if v.dtype == "f16" else np.float32
+        dt = _NP[v.dtype]
         out = np.empty(v.shape, dt)
         N.call("sdx_stream_sync", self.be.ctx, ctypes.c_void_p(self.stream_ptr), 0)
         N.call("sdx_memcpy_dtoh_async", self.be.ctx, out.ctypes.data_as(ctypes.c_void_p), self.ptr(name), out.nbytes,
                ctypes.c_void_p(self.stream_ptr))
         N.call("sdx_stream_sync", self.be.ctx, ctypes.c_void_p(self.stream_ptr), 0)
-        return out.astype(np.float32)
+        return out if v.dtype == "i32" else out.astype(np.float32)
 
     def pinned_io(self):
         """Pinned host staging buffers (input region, output) for end-to-end runs."""
@@ -598,8 +699,10 @@ class CudaInferenceSession:
 
     def _output_view(self, pin_out, copy: bool) -> np.ndarray:
         ov = self.plan.values[self.plan.output]
-        dt = np.float16 if ov.dtype == "f16" else np.float32
+        dt = _NP[ov.dtype]
         y = pin_out.numpy().view(dt).reshape(ov.shape)
+        if ov.dtype == "i32":
+            return y.copy() if copy else y
         return y.astype(np.float32) if (copy or dt != np.float32) else y
 
     def submit(self, pin_in: torch.Tensor, pin_out: torch.Tensor) -> None:

@@ -170,3 +170,58 @@ def test_conv_pool_node(ic, oc, act, pool_relu):
     sess, feeds, ref, got = _run_both(P)
     assert_close(got, ref[P.output], f"conv+pool {ic}->{oc}")
     sess.close()
+
+
+def test_c1_batchnorm_folded_at_load():
+    """C1 written with an un-folded BatchNorm: the backend folds it into the conv at load
+    (FoldConvBatchNorm) and the result matches the oracle, which folds independently."""
+    from simdonnx_b200 import configs
+    plan = configs.build_c1(batch=2, bn=True)
+    sess, feeds, ref, got = _run_both(plan)
+    assert not any(n.op == "BatchNorm" for n in sess.plan.nodes)
+    assert_close(got, ref[plan.output], "C1 + BatchNorm")
+    sess.close()
+
+
+def test_fused_ops_tail_graph():
+    """Conv + fused pool (small stem), standalone BatchNorm (affine), conv + folded BatchNorm,
+    ChannelShift, broadcast multiply by a constant vector, Sigmoid, SafeDiv, MaxPool and UpHead in
+    one session graph, against the oracle running the same plan."""
+    from simdonnx_b200 import configs
+    plan = configs.build_fused_tail(batch=2)
+    sess, feeds, ref, got = _run_both(plan)
+    ops = [n.op for n in sess.plan.nodes]
+    assert "UpHead" in ops and "SafeDiv" in ops and "ChannelShift" in ops and "MaxPool" in ops
+    assert sess.plan.nodes[0].p.pool is not None  # the stem kept its pool (one fused kernel)
+    assert_close(got, ref[plan.output], "fused tail")
+    sess.close()
+
+
+def test_matmul_graph():
+    from simdonnx_b200 import configs
+    plan = configs.build_matmul(batch=3)
+    sess, feeds, ref, got = _run_both(plan)
+    assert_close(got, ref[plan.output], "matmul graph")
+    sess.close()
+
+
+@pytest.mark.parametrize("batch", [1, 16])
+def test_rec_ctc_head(batch):
+    """C3 with the fused CTC head: per time step the class index and its probability, against the
+    oracle's Gemm + UpdateArgMax walk (indices compared where the oracle's top-2 logit margin is
+    clear of the fp16 storage error, probabilities within the parity bar)."""
+    from oracle.runner import OracleSession
+    from simdonnx_b200 import configs
+    plan = configs.build_rec(batch=batch, ctc=True)
+    sess, feeds, ref, got = _run_both(plan)
+    got_i, got_p = got[0], got[1].view(np.float32)
+    want = ref[plan.output]
+    want_i, want_p = want[0], want[1].view(np.float32)
+    logits = OracleSession(configs.build_rec(batch=batch)).run(feeds)[configs.build_rec(batch=batch).output]
+    z = logits.reshape(-1, logits.shape[-1])
+    top2 = np.sort(z, axis=1)[:, -2:]
+    clear = (top2[:, 1] - top2[:, 0]) > 2e-2 * np.abs(z).max()
+    np.testing.assert_array_equal(got_i[clear], want_i[clear])
+    assert (got_i == want_i).mean() > 0.9
+    assert_close(got_p, want_p, "ctc probabilities")
+    sess.close()

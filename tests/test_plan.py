@@ -146,3 +146,42 @@ def test_device_feed_generator_matches_host_generator():
     p = configs.build_det(batch=1, hw=64)
     (k, f), = p.feeds.items()
     assert np.array_equal(f(), p.feeds_dev[k](torch.device("cpu")).numpy())
+
+
+def test_batchnorm_fold_matches_reference_math():
+    """The load-time BatchNorm fold (rewrites.fold_conv_batchnorm, FoldConvBatchNorm) and the oracle's
+    own restatement give the same folded weights bit for bit, and the folded conv matches conv -> BN
+    evaluated in fp64 on the oracle's reference conv."""
+    import oracle as O
+    from oracle.runner import OracleSession, fold_batchnorm
+    from simdonnx_b200.rewrites import fold_conv_batchnorm
+    plan = configs.build_c1(batch=1, hw=12, c=16, bn=True)
+    ours, theirs = fold_conv_batchnorm(plan), fold_batchnorm(plan)
+    cw = [n for n in ours.nodes if n.op == "Conv"][0]
+    tw = [n for n in theirs.nodes if n.op == "Conv"][0]
+    assert not any(n.op == "BatchNorm" for n in ours.nodes)
+    assert np.array_equal(ours.values[cw.ins[1]].const, theirs.values[tw.ins[1]].const)
+    assert np.array_equal(ours.values[cw.p.bias].const, theirs.values[tw.p.bias].const)
+    feeds = {k: f() for k, f in plan.feeds.items()}
+    got = OracleSession(plan).run(feeds)[plan.output]
+    bn = [n for n in plan.nodes if n.op == "BatchNorm"][0].p
+    V = lambda k: plan.values[k].const.astype(np.float64)
+    conv = O.conv_ref64(feeds[plan.input], plan.values["c1.w"].const, None, pads=(1, 1, 1, 1)).astype(np.float64)
+    want = (conv - V(bn.mean)) / np.sqrt(V(bn.var) + bn.eps) * V(bn.gamma) + V(bn.beta)
+    want = np.maximum(want + feeds["c1.res"], 0)
+    assert np.abs(got - want).max() <= 1e-5 * np.abs(want).max()
+
+
+def test_unfoldable_batchnorm_lowers_to_the_affine_pair():
+    """A BatchNorm after a pool (no conv to fold into) becomes x * s + t (EmitBatchNorm); the
+    lowered plan computes the same values as the oracle's BatchNorm node, bit for bit."""
+    from oracle.runner import OracleSession
+    from simdonnx_b200.rewrites import fold_conv_batchnorm, lower_batchnorm
+    plan = configs.build_fused_tail(batch=1, hw=32)
+    low = lower_batchnorm(fold_conv_batchnorm(plan))
+    ops = [n.op for n in low.nodes]
+    assert "BatchNorm" not in ops and ops.count("Elementwise") == 3  # bn0 -> mul + add; the gain
+    feeds = {k: f() for k, f in plan.feeds.items()}
+    a = OracleSession(plan).run(feeds)[plan.output]
+    b = OracleSession(low).run(feeds)[low.output]
+    assert np.array_equal(a, b)
