@@ -179,13 +179,16 @@ def node_times(sess, N, roofline, torch, passes: int = 3):
 def measure_extras(args, local, N, configs, roofline, torch, CudaInferenceSession) -> dict:
     """Side measurements on this GPU (not the headline): the tensor-bound half of the hot path
     (C4 UNet at N=16: images/s and, per 3x3 conv, TFLOP/s against the sustained bf16 peak), the
-    single fused node C1 (N=8) and C3 rec at N=64. Device-resident, CUDA events, K graph replays."""
+    single fused node C1 (N=8) and C3 rec at N=64, with fp32 logits and with the fused CTC head
+    (per-step index and probability; the [N*40, 6625] logits never stored). Device-resident, CUDA
+    events, K graph replays."""
     dev = torch.device("cuda", local)
     tc_peak = peaks_sustained()
     hbm, _, _ = peaks()
     out = {}
     for key, build, batch in (("unet_c4", configs.build_unet, 16), ("c1", configs.build_c1, 8),
-                              ("rec_c3", configs.build_rec, 64)):
+                              ("rec_c3", configs.build_rec, 64),
+                              ("rec_c3_ctc_head", lambda batch: configs.build_rec(batch=batch, ctc=True), 64)):
         plan = build(batch=batch)
         s = CudaInferenceSession(plan, device=local)
         if plan.feeds_dev:

@@ -84,6 +84,13 @@ def node_cost(plan: ExecPlan, n) -> tuple:
         nb, oh, ow, oc = plan.values[out].shape
         flops = 2 * nb * oh * ow * oc * W.shape[1] * W.shape[2] * W.shape[3]
         return "stem_image", flops, _nb(plan, n.ins[0]) + W.size * 4 + _nb(plan, out)
+    if op == "Gemm" and getattr(p, "ctc", False):
+        # fused CTC head: the logits stay on chip; traffic = features, weights, bias, [2, rows] result
+        a = n.ins[0]
+        Wb = plan.values[n.ins[1]].const
+        k, nn = (Wb.shape[1], Wb.shape[0]) if p.trans_b else Wb.shape
+        m = int(np.prod(plan.values[a].shape)) // k
+        return "ctc_head", 2 * m * nn * k, _nb(plan, a) + Wb.size * 2 + 4 * nn + _nb(plan, out)
     if op == "Gemm":
         a = n.ins[0]
         Wb = plan.values[n.ins[1]].const
@@ -111,6 +118,18 @@ def node_cost(plan: ExecPlan, n) -> tuple:
         return "convert", 0, _nb(plan, n.ins[0]) + _nb(plan, out)
     if op in ("LayerNorm", "Softmax", "Act"):
         return op.lower(), 0, _nb(plan, n.ins[0]) + _nb(plan, out)
+    if op in ("SafeDiv", "ChannelShift"):
+        return op.lower(), 0, sum(_nb(plan, v) for v in n.ins) + _nb(plan, out)
+    if op == "UpHead":
+        nb, oh, ow, oc = plan.values[out].shape
+        c = plan.values[n.ins[0]].shape[3]
+        return "uphead", 2 * nb * oh * ow * oc * c, (_nb(plan, n.ins[0]) + _nb(plan, n.ins[1]) + 4 * oc * c +
+                                                     _nb(plan, out))
+    if op == "MatMul":
+        sa, sb = plan.values[n.ins[0]].shape, plan.values[n.ins[1]].shape
+        so = plan.values[out].shape
+        batch = int(np.prod(so[:-2])) if len(so) > 2 else 1
+        return "matmul", 2 * batch * sa[-2] * sa[-1] * sb[-1], _nb(plan, n.ins[0]) + _nb(plan, n.ins[1]) + _nb(plan, out)
     if op == "Attention":
         nb, t, _ = plan.values[n.ins[0]].shape
         flops = 4 * nb * p.heads * t * t * p.head_dim
