@@ -398,7 +398,15 @@ int tc_launch(const TcProblem& p, cudaStream_t stream) {
   // buffers and >= 3 A stages, resident with 1 staging buffer and >= 2 stages, then streamed
   // weights (per stage) likewise. 8 stages at most.
   if (!a.tma_out) a.sbuf_bytes = 0;
-  a.b_total_bytes = (uint32_t)((size_t)a.wterms * a.taps * a.kb_per_tap * n_tiles * BN * kbytes);
+  // every CTA keeps a single N tile when the grid (one CTA per SM, or one per tile) is a multiple
+  // of n_tiles: then only that tile's weights need to be resident
+  int dev = 0;
+  cudaGetDevice(&dev);
+  const int total = a.m_tiles * a.n_tiles;
+  const int grid = std::min(total, num_sms(dev));
+  a.b_nslice = (n_tiles > 1 && grid % n_tiles == 0) ? 1 : 0;
+  a.b_total_bytes =
+      (uint32_t)((size_t)a.wterms * a.taps * a.kb_per_tap * (a.b_nslice ? 1 : n_tiles) * BN * kbytes);
   // stages of cps channel blocks each (fewer, larger stages amortise the per-stage waits and
   // commits of the two issuing threads): the largest cps with >= 3 stages, else cps = 1 with >= 2
   bool planned = false;
@@ -444,11 +452,7 @@ int tc_launch(const TcProblem& p, cudaStream_t stream) {
   const size_t smem = smem_bytes(a);
   if (smem > (size_t)TC_SMEM_LIMIT) return set_error(SDX_ERR_NOT_SUPPORTED, "tc: shared memory plan too large");
 
-  const int total = a.m_tiles * a.n_tiles;
   if (total == 0) return SDX_OK;
-  int dev = 0;
-  cudaGetDevice(&dev);
-  const int grid = std::min(total, num_sms(dev));
   int rc = SDX_OK;
   if (argmax) {
     rc = a.egroups == 4 ? launch_tc<ACT_NONE, 5, 4>(dev, grid, smem, stream, mA, mB, mOut, mRes, a)

@@ -93,6 +93,9 @@ struct TcArgs {
   int* arg_i;
   float* arg_s;
   int arg_ld;  // entries between two N tiles' states (>= M)
+  // resident weights of this CTA's N tile only (compact [term][tap][cb] layout): with a grid that
+  // is a multiple of n_tiles every CTA keeps one N tile (tile = m * n_tiles + n, strided by the grid)
+  int b_nslice;
   unsigned int* err;
 };
 

@@ -781,7 +781,8 @@ __global__ void __launch_bounds__(tc_threads(G), 1)
 
   // weight block (term, tap, channel block, n tile) in the resident layout
   auto b_res_off = [&](int term, int tap, int cb, int nt) -> uint32_t {
-    return (uint32_t)((((term * a.taps + tap) * a.kb_per_tap + cb) * a.n_tiles + nt)) * b_tap_bytes;
+    return a.b_nslice ? (uint32_t)((term * a.taps + tap) * a.kb_per_tap + cb) * b_tap_bytes
+                      : (uint32_t)((((term * a.taps + tap) * a.kb_per_tap + cb) * a.n_tiles + nt)) * b_tap_bytes;
   };
   // The producer and MMA loops sit on the critical path of every stage: no integer division inside
   // them (ring slot, phase, tap and channel block advance as counters). Each runs on a whole warp
@@ -799,9 +800,11 @@ __global__ void __launch_bounds__(tc_threads(G), 1)
         for (int term = 0; term < a.wterms; term++)
           for (int tap = 0; tap < a.taps; tap++)
             for (int cb = 0; cb < a.kb_per_tap; cb++)
-              for (int nt = 0; nt < a.n_tiles; nt++)
+              for (int nt = 0; nt < a.n_tiles; nt++) {
+                if (a.b_nslice && nt != (int)(blockIdx.x % (unsigned)a.n_tiles)) continue;
                 tma_load_2d_p(ld, smem_u32(sB) + b_res_off(term, tap, cb, nt), &tmB, bb, cb * a.kblk,
-                            (term * a.taps + tap) * a.b_rows_per_tap + nt * a.BN);
+                              (term * a.taps + tap) * a.b_rows_per_tap + nt * a.BN);
+              }
       }
       int s = 0;
       uint32_t phase = 0;
