@@ -113,8 +113,9 @@ int sdx_selftest_bounded_wait(sdx_ctx* ctx, int wait_ms, sdx_stream s);
 /* ConvP weights w [oc][ic/group][kh][kw] for the kernel sdx_conv2d routes `d` to (Nhwc.Pack,
  * src/Kernels/Nhwc.cs:102-125). The layout depends on the shape and layout fields of `d` (batch and
  * spatial sizes, channels, kernel, strides, pads, dtypes, layouts, y_pix_stride / y_ch_off, add_up,
- * w_terms), not on its pointers: pack with the descriptor that sdx_conv2d will get (thin 1x1 convs
- * over whole fp16 tensors are packed for pixel folding, which depends on batch * ih * iw). */
+ * w_terms) and on whether in_scale is set, not on the pointers' values: pack with the descriptor
+ * that sdx_conv2d will get (thin 1x1 convs over whole fp16 tensors without in_scale are packed for
+ * pixel folding, which depends on batch * ih * iw). */
 struct sdx_conv_desc;
 int sdx_pack_conv(const struct sdx_conv_desc* d, const float* w, void* out, size_t* bytes);
 /* ConvTP weights w [ic][oc][kh][kw] (Nhwc.PackConvT, src/Kernels/Nhwc.Det.cs:26-44). */
@@ -152,7 +153,10 @@ typedef struct sdx_conv_desc {
   int64_t y_pix_stride; /* elements between output pixels (0 = oc); > oc writes into a channel slice */
   int y_ch_off;      /* first output channel in that slice */
   sdx_dptr x, w, bias, add, y;  /* w: packed by sdx_pack_conv; bias fp32 [oc] or 0; add 0 = none */
-  sdx_dptr in_scale; /* fp32 [batch, ic] per-image channel scale applied to x on load (SE gate), or 0 */
+  sdx_dptr in_scale; /* fp32 [batch, ic] per-image channel scale of x (an SE gate's output: the conv reads
+                        x * s without it being stored), or 0. Depthwise: applied to the staged weights.
+                        1x1 tensor-core route: the weights are scaled per image into `w_scaled` first
+                        (needs sdx_conv_scaled_weights_bytes(d) > 0, no gap_sums) */
   int w_terms;       /* tensor-core routes: fp16 weight terms, 1 (w) or 2 (hi + lo, ~22-bit weights);
                         0 = default: 2 for 1x1 kernels with ic < 128 (early narrow layers, whose weight
                         rounding every later layer amplifies), 1 for 1x1 kernels with ic >= 128 and for
@@ -166,8 +170,14 @@ typedef struct sdx_conv_desc {
                         `sums`), or 0. 1x1 tensor-core route with the fp16 TMA-store epilogue
                         (y fp16, oc 16, 32, 64 or a multiple of 128, 16-byte aligned rows);
                         (batch * oh * ow) % 32 == 0 */
+  sdx_dptr w_scaled; /* device scratch of sdx_conv_scaled_weights_bytes(d) bytes for a 1x1 conv with
+                        in_scale (per-image two-term weights), else unused */
 } sdx_conv_desc;
 int sdx_conv2d(sdx_ctx* ctx, const sdx_conv_desc* d, sdx_stream s);
+/* Bytes of the per-image weight scratch a 1x1 tensor-core conv with in_scale needs (batch two-term
+ * copies of its packed weights), or 0 when that form does not apply to the descriptor's shape: it
+ * needs fp16 NHWC x, ic % 8 == 0, oc in [8, 128], ic <= 256 and ih * iw a multiple of 128. */
+size_t sdx_conv_scaled_weights_bytes(const sdx_conv_desc* d);
 
 /* Gemm node: GemmP (src/Engine/ExecPlan.cs:87-93) via Nhwc.Gemm (src/Kernels/Nhwc.Avx512.cs:241-266):
  * y[m, n] = act(a[m, k] . B + bias[n] [+ add[m, n]]), a fp16 row stride lda, y fp16/fp32. */

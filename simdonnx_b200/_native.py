@@ -40,7 +40,7 @@ class ConvDesc(ctypes.Structure):
                                   "x_layout", "y_dtype", "add_dtype", "add_layout", "y_layout", "pad_mode")] + [
         ("pad_value", _f), ("y_pix_stride", _i64), ("y_ch_off", _i),
         ("x", _u64), ("w", _u64), ("bias", _u64), ("add", _u64), ("y", _u64), ("in_scale", _u64), ("w_terms", _i),
-        ("add_up", _i), ("gap_sums", _u64)]
+        ("add_up", _i), ("gap_sums", _u64), ("w_scaled", _u64)]
 
 
 class GemmDesc(ctypes.Structure):
@@ -166,6 +166,7 @@ _SIGS = {
     "sdx_selftest_bounded_wait": (_i, [_p, _i, _p]),
     "sdx_pack_conv": (_i, [ctypes.POINTER(ConvDesc), _p, _p, ctypes.POINTER(_sz)]),
     "sdx_pack_convt": (_i, [_i, _i, _i, _i, _p, _p, ctypes.POINTER(_sz)]),
+    "sdx_conv_scaled_weights_bytes": (_sz, [ctypes.POINTER(ConvDesc)]),
     "sdx_pack_gemm": (_i, [_i, _i, _i, _p, _p, ctypes.POINTER(_sz)]),
     "sdx_conv2d": (_i, [_p, ctypes.POINTER(ConvDesc), _p]),
     "sdx_gemm": (_i, [_p, ctypes.POINTER(GemmDesc), _p]),

@@ -137,8 +137,19 @@ def conv2d(be: CudaBackend, d: N.ConvDesc, x, w_packed, bias=None, add=None, y=N
         shape = (d.batch, d.oc, oh, ow) if d.y_layout == N.NCHW else (d.batch, oh, ow, d.oc)
         y = torch.empty(shape, dtype=dt, device=x.device)
     d.x, d.w, d.bias, d.add, d.y, d.in_scale = ptr(x), ptr(w_packed), ptr(bias), ptr(add), ptr(y), ptr(in_scale)
-    N.call("sdx_conv2d", be.ctx, ctypes.byref(d), cur_stream())
+    scratch = None
+    if in_scale is not None and d.group == 1:
+        # 1x1 tensor-core conv of x * s: per-image scaled weights in a scratch buffer
+        nbytes = conv_scaled_weights_bytes(d)
+        scratch = torch.empty(max(nbytes, 16), dtype=torch.uint8, device=x.device)
+        d.w_scaled = ptr(scratch)
+    N.call("sdx_conv2d", be.ctx, ctypes.byref(d), cur_stream())  # scratch: freed in stream order
     return y
+
+
+def conv_scaled_weights_bytes(d: N.ConvDesc) -> int:
+    """Scratch bytes of a 1x1 conv with in_scale (per-image weights), 0 if that form does not apply."""
+    return int(N.lib().sdx_conv_scaled_weights_bytes(ctypes.byref(d)))
 
 
 def gemm(be: CudaBackend, a, w_packed, n, bias=None, act="none", add=None, y=None, y_dtype=torch.float16):

@@ -104,6 +104,8 @@ static int tc_kpad(int K) {
   return (K + kb - 1) / kb * kb;
 }
 
+int tc_kpad_of(int K) { return tc_kpad(K); }
+
 static CUtensorMapSwizzle swizzle_of(int row_bytes) {
   return row_bytes == 128 ? CU_TENSOR_MAP_SWIZZLE_128B : row_bytes == 64 ? CU_TENSOR_MAP_SWIZZLE_64B
                                                                           : CU_TENSOR_MAP_SWIZZLE_32B;
@@ -134,12 +136,18 @@ int tc_launch(const TcProblem& p, cudaStream_t stream) {
   // epilogue runs four warp groups instead of two; the packed weights are the same 128 rows, and
   // the two tiles of one row block run on neighbouring CTAs, so A's second read hits L2
   if (p.mode == TC_ROWS && !convt && BN == 128 && n_tiles == 1 && p.N == 128 && p.K <= 128 && !p.out_f32 &&
-      p.fold <= 1) {
+      p.fold <= 1 && p.img_rows == 0) {
     BN = 64;
     n_tiles = 2;
   }
   const int kblk = tc_kblk(p.K), kpad = tc_kpad(p.K);
   const int kbytes = kblk * 2;
+  const bool imgw = p.img_rows > 0;
+  if (imgw && (p.mode != TC_ROWS || convt || n_tiles != 1 || p.fold > 1 || p.arg_m || p.gap || p.wterms != 2 ||
+               p.img_rows % TC_BM != 0 || p.M % p.img_rows != 0))
+    return set_error(SDX_ERR_NOT_SUPPORTED,
+                     "tc: per-image weights need a rows-mode conv with one N tile, two terms, no fused sums, and "
+                     "whole 128-row tiles per image");
   TcArgs a;
   memset(&a, 0, sizeof(a));
   a.mode = p.mode;
@@ -292,7 +300,8 @@ int tc_launch(const TcProblem& p, cudaStream_t stream) {
     if (rc) return rc;
   }
   {
-    uint64_t dims[2] = {(uint64_t)kpad, (uint64_t)a.wterms * a.taps * a.b_rows_per_tap};
+    const uint64_t sets = imgw ? (uint64_t)(p.M / p.img_rows) : 1;
+    uint64_t dims[2] = {(uint64_t)kpad, (uint64_t)a.wterms * a.taps * a.b_rows_per_tap * sets};
     uint64_t strides[1] = {(uint64_t)kpad * 2};
     uint32_t box[2] = {(uint32_t)kblk, (uint32_t)BN};
     int rc = encode_map(&mB, p.w, 2, dims, strides, box, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, swizzle_of(kbytes));
@@ -403,7 +412,14 @@ int tc_launch(const TcProblem& p, cudaStream_t stream) {
   int dev = 0;
   cudaGetDevice(&dev);
   const int total = a.m_tiles * a.n_tiles;
-  const int grid = std::min(total, num_sms(dev));
+  int grid = std::min(total, num_sms(dev));
+  if (imgw && total > 0) {
+    // contiguous tile ranges: each CTA crosses few image boundaries (weight reloads)
+    a.img_tiles = p.img_rows / TC_BM;
+    a.b_img_rows = a.wterms * a.taps * a.b_rows_per_tap;
+    a.per_cta = (total + grid - 1) / grid;
+    grid = (total + a.per_cta - 1) / a.per_cta;
+  }
   a.b_nslice = (n_tiles > 1 && grid % n_tiles == 0) ? 1 : 0;
   a.b_total_bytes =
       (uint32_t)((size_t)a.wterms * a.taps * a.kb_per_tap * (a.b_nslice ? 1 : n_tiles) * BN * kbytes);
@@ -426,7 +442,7 @@ int tc_launch(const TcProblem& p, cudaStream_t stream) {
   const bool eg4 = !p.kxn && 4 * BN <= 512 && (BN <= 64 || chain || (!fast && !kxn_fast));
   for (int eg = eg4 ? 4 : 2; eg >= 2 && !planned; eg -= 2) {
   a.egroups = eg;
-  for (int res = 1; res >= 0 && !planned; res--) {
+  for (int res = 1; res >= (imgw ? 1 : 0) && !planned; res--) {
     for (int pass = 0; pass < 2 && !planned; pass++) {
       for (int cps = pass == 0 ? a.kb_per_tap : 1; cps >= 1 && !planned; cps--) {
         if (a.kb_per_tap % cps) continue;
@@ -560,6 +576,37 @@ int tc_fold_factor(int64_t pixels, int IC, int OC) {
   for (int f = 4; f >= 2; f /= 2)
     if (OC * f == 64 && IC * f <= 128 && pixels % (32 * f) == 0) return f;
   return 1;
+}
+
+// One thread per (image, packed element): the scaled weight v = (hi + lo) * s[image, k] split into
+// two fp16 terms again (the padding columns k >= K stay zero).
+__global__ void scale_weights_kernel(const __half* __restrict__ w, int terms, int64_t set, int kpad, int K,
+                                     const float* __restrict__ s, int64_t total, __half* __restrict__ out) {
+  for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < total; i += (int64_t)gridDim.x * blockDim.x) {
+    const int64_t n = i / set, j = i - n * set;
+    const int k = (int)(j % kpad);
+    float v = __half2float(w[j]);
+    if (terms == 2) v += __half2float(w[set + j]);
+    v *= k < K ? __ldg(s + n * K + k) : 0.0f;
+    const __half h = __float2half_rn(v);
+    out[n * 2 * set + j] = h;
+    out[n * 2 * set + set + j] = __float2half_rn(v - __half2float(h));
+  }
+}
+
+int tc_scale_weights_launch(const __half* w, int terms, int rows, int kpad, int K, const float* s, int batch,
+                            __half* out, cudaStream_t st) {
+  if (!aligned16(out) || !aligned16(w)) return set_error(SDX_ERR_INVALID, "scaled weights: 16-byte aligned buffers");
+  const int64_t set = (int64_t)rows * kpad, total = set * batch;
+  if (total <= 0) return SDX_OK;
+  int dev = 0;
+  cudaGetDevice(&dev);
+  const int grid = (int)std::min<int64_t>((total + 255) / 256, (int64_t)num_sms(dev) * 8);
+  scale_weights_kernel<<<grid, 256, 0, st>>>(w, terms, set, kpad, K, s, total, out);
+  cudaError_t e = cudaGetLastError();
+  if (e != cudaSuccess) return set_cuda_error(e, "scale_weights launch");
+  count_launch();
+  return SDX_OK;
 }
 
 size_t tc_fold_weights_halves(int IC, int OC, int fold, int terms) {

@@ -96,6 +96,13 @@ struct TcArgs {
   // resident weights of this CTA's N tile only (compact [term][tap][cb] layout): with a grid that
   // is a multiple of n_tiles every CTA keeps one N tile (tile = m * n_tiles + n, strided by the grid)
   int b_nslice;
+  // per-image weights (rows mode, one N tile): the B map holds one weight set per image, b_img_rows
+  // rows apart, and m tile t belongs to image t / img_tiles. Each CTA then runs the contiguous m-tile
+  // range [blockIdx.x * per_cta, + per_cta) and reloads its resident weights when the image changes.
+  // img_tiles = 0: one weight set, tiles strided by the grid.
+  int img_tiles;
+  int per_cta;
+  int b_img_rows;
   unsigned int* err;
 };
 

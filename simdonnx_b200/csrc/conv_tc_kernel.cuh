@@ -775,6 +775,11 @@ __global__ void __launch_bounds__(tc_threads(G), 1)
   const uint32_t tmem_base = *tmem_slot;
 
   const int total_tiles = a.m_tiles * a.n_tiles;
+  // this CTA's tiles: strided by the grid, or a contiguous range (per-image weights)
+  const bool imgw = a.img_tiles > 0;
+  const int t_begin = imgw ? (int)blockIdx.x * a.per_cta : (int)blockIdx.x;
+  const int t_end = imgw ? min(total_tiles, t_begin + a.per_cta) : total_tiles;
+  const int t_step = imgw ? 1 : (int)gridDim.x;
   // pipeline stages per tile: (tap, channel block), or (kx, channel block) in halo mode
   const int groups = a.kb_per_tap / a.cps;  // channel-block groups per tap
   const int kblocks = (a.halo ? a.kw : a.taps) * groups;
@@ -793,8 +798,8 @@ __global__ void __launch_bounds__(tc_threads(G), 1)
       uint32_t issued_mask = 0;  // ring slots that received at least one copy
       uint32_t last_phase = 0;   // bit s: phase of the last copy into slot s
       bool ok = true;
-      if (a.b_resident) {
-        // every weight block once, onto one barrier
+      // every weight block of weight set `img` once, onto one barrier
+      auto load_b = [&](int img) {
         const uint32_t bb = smem_u32(bres);
         mbar_arrive_expect_tx_p(ld, bb, a.b_total_bytes);
         for (int term = 0; term < a.wterms; term++)
@@ -803,15 +808,23 @@ __global__ void __launch_bounds__(tc_threads(G), 1)
               for (int nt = 0; nt < a.n_tiles; nt++) {
                 if (a.b_nslice && nt != (int)(blockIdx.x % (unsigned)a.n_tiles)) continue;
                 tma_load_2d_p(ld, smem_u32(sB) + b_res_off(term, tap, cb, nt), &tmB, bb, cb * a.kblk,
-                              (term * a.taps + tap) * a.b_rows_per_tap + nt * a.BN);
+                              img * a.b_img_rows + (term * a.taps + tap) * a.b_rows_per_tap + nt * a.BN);
               }
+      };
+      int cur_img = imgw ? t_begin / a.img_tiles : 0;
+      uint32_t b_loads = 0;
+      if (a.b_resident) {
+        load_b(cur_img);
+        b_loads = 1;
       }
       int s = 0;
       uint32_t phase = 0;
+      int s_last = -1;          // ring slot and phase of the most recent stage issued
+      uint32_t ph_last = 0;
       // single-stage tiles with resident weights (pointwise, kx-in-N 3x3, ConvT): the dispatch-free
       // loop; a 4-D box at (ox0 - pad_l, oy0 - pad_t) covers halo mode with one column tap and the
       // one-tap conv mode alike
-      if (kblocks == 1 && a.b_resident && a.cps <= 4 && (a.mode != TC_CONV || a.halo || a.taps == 1)) {
+      if (kblocks == 1 && a.b_resident && a.cps <= 4 && (a.mode != TC_CONV || a.halo || a.taps == 1) && !imgw) {
         ProdSingle ps;
         ps.sA = smem_u32(sA);
         ps.a_stage_bytes = a.a_stage_bytes;
@@ -834,9 +847,21 @@ __global__ void __launch_bounds__(tc_threads(G), 1)
                                  issued_mask, last_phase);
         ok = false;  // every tile issued above
       }
-      for (int tile = blockIdx.x; tile < total_tiles && ok; tile += gridDim.x) {
+      for (int tile = t_begin; tile < t_end && ok; tile += t_step) {
         const int m_tile = a.n_tiles == 1 ? tile : tile / a.n_tiles;
         const int n_tile = tile - m_tile * a.n_tiles;
+        if (imgw && m_tile / a.img_tiles != cur_img) {
+          // a new image's weights: every MMA that read the loaded set has completed once the last
+          // stage issued has been released (tcgen05.commit tracks all earlier MMAs of its thread)
+          if (s_last >= 0 &&
+              !mbar_wait_warp(smem_u32(&empty[s_last]), ph_last, a.err, SDX_DEV_WAIT_EMPTY, abort_flag)) {
+            ok = false;
+            break;
+          }
+          cur_img = m_tile / a.img_tiles;
+          load_b(cur_img);
+          b_loads++;
+        }
         int img = 0, oy0 = 0, ox0 = 0;
         if (a.mode == TC_CONV) {
           const int per_img = a.tiles_h * a.tiles_w;
@@ -881,6 +906,8 @@ __global__ void __launch_bounds__(tc_threads(G), 1)
           }
           issued_mask |= 1u << s;
           last_phase = (last_phase & ~(1u << s)) | (phase << s);
+          s_last = s;
+          ph_last = phase;
           if (++cg == groups) {
             cg = 0;
             tk++;
@@ -895,7 +922,7 @@ __global__ void __launch_bounds__(tc_threads(G), 1)
       for (int q = 0; q < S; q++)
         if (issued_mask & (1u << q))
           mbar_wait_drain(smem_u32(&full[q]), (last_phase >> q) & 1u, a.err, SDX_DEV_WAIT_DRAIN);
-      if (a.b_resident) mbar_wait_drain(smem_u32(bres), 0, a.err, SDX_DEV_WAIT_DRAIN);
+      if (b_loads > 0) mbar_wait_drain(smem_u32(bres), (b_loads - 1) & 1u, a.err, SDX_DEV_WAIT_DRAIN);
     }
     __syncwarp();
   } else if (warp == 1) {
@@ -921,7 +948,7 @@ __global__ void __launch_bounds__(tc_threads(G), 1)
       uint32_t acc = 0, accph = 0;
       // one-tap tiles (pointwise), and the kx-in-N 3x3 convs (three row taps, one weight term)
       const bool single = kblocks == 1 && a.b_resident && (a.b_taps == 1 || (a.b_taps == 3 && a.wterms == 1)) &&
-                          a.cps <= 4 && (nk == 1 || nk == 2 || nk == 4);
+                          a.cps <= 4 && (nk == 1 || nk == 2 || nk == 4) && !imgw;
       if (ok && single) {
         MmaSingle m;
         m.d0 = tmem_base;
@@ -958,8 +985,17 @@ __global__ void __launch_bounds__(tc_threads(G), 1)
         }
         ok = false;  // the loop above ran every tile
       }
-      for (int tile = blockIdx.x; tile < total_tiles && ok; tile += gridDim.x) {
+      int cur_img = imgw ? t_begin / a.img_tiles : 0;
+      uint32_t b_waits = 1;  // weight sets waited for (the first one above)
+      for (int tile = t_begin; tile < t_end && ok; tile += t_step) {
         const int n_tile = a.n_tiles == 1 ? 0 : tile % a.n_tiles;
+        if (imgw && tile / a.img_tiles != cur_img) {
+          // the producer loads the next image's weights once this warp's MMAs on the last set are done
+          if (!mbar_wait_warp(smem_u32(bres), b_waits & 1u, a.err, SDX_DEV_WAIT_FULL, abort_flag)) break;
+          tc_fence_after();
+          cur_img = tile / a.img_tiles;
+          b_waits++;
+        }
         if (!mbar_wait_warp(smem_u32(&acce[acc]), accph ^ 1u, a.err, SDX_DEV_WAIT_ACC_EMPTY, abort_flag)) break;
         tc_fence_after();
         const uint32_t d = tmem_base + acc * (uint32_t)a.acc_stride;
@@ -1015,7 +1051,7 @@ __global__ void __launch_bounds__(tc_threads(G), 1)
     // 1024-aligned slab); 0 when the staging rows are not swizzled
     const uint32_t xr = a.swz ? (((uint32_t)lane * P) >> 7) & (P / 16u - 1u) : 0u;
     const uint32_t stage0 = smem_u32(sStage) + (uint32_t)e * a.nsbuf * a.sbuf_bytes + (uint32_t)q * 32u * P;
-    const int tile0 = blockIdx.x + e * gridDim.x, tstep = G * gridDim.x;
+    const int tile0 = t_begin + e * t_step, tstep = G * t_step;
     uint32_t res_phase = 0;    // bit b: parity of the next wait on buffer b's residual barrier
     bool res_pending = false;  // a residual load is in flight into buffer (lc % nsbuf)
     const uint32_t eld = elect_leader();  // this warp's issuing lane for TMA copies and bulk groups
@@ -1049,13 +1085,13 @@ __global__ void __launch_bounds__(tc_threads(G), 1)
       mbar_arrive_expect_tx_p(eld, rb, (uint32_t)ng * a.slab_tx);
       for (int g = 0; g < ng; g++) warp_copy(eld, a, &tmRes, slab + g * a.group_bytes, g, q, t, true, rb);
     };
-    if (a.tma_res && tile0 < total_tiles) {
+    if (a.tma_res && tile0 < t_end) {
       issue_res(tile0, 0);
       res_pending = true;
     }
 
     uint32_t lc = 0;  // this group's tile count
-    for (int tile = tile0; tile < total_tiles; tile += tstep, lc++) {
+    for (int tile = tile0; tile < t_end; tile += tstep, lc++) {
       const uint32_t lt = G * lc + (uint32_t)e;
       const uint32_t acc = lt & (uint32_t)(a.nacc - 1), ar = lt >> (a.nacc == 4 ? 2 : 1);
       const uint32_t sbi = a.nsbuf == 2 ? (lc & 1u) : 0u;
@@ -1385,7 +1421,7 @@ __global__ void __launch_bounds__(tc_threads(G), 1)
           }
           // the next tile's buffer is free once the store that last read it has read it; then its
           // residual rows can be fetched while this warp waits for the next accumulator
-          if (tile + tstep < total_tiles) {
+          if (tile + tstep < t_end) {
             if (a.nsbuf == 2) bulk_wait_read1(eld);
             else bulk_wait_read0(eld);
             if (a.tma_res) {

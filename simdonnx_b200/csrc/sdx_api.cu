@@ -448,12 +448,13 @@ static int conv_route(const sdx_conv_desc* d) {
     if (d->group == d->ic && d->oc == d->ic) return R_DEPTHWISE;
     return R_INVALID;
   }
-  const bool f16_nhwc = d->x_dtype == SDX_F16 && d->x_layout == SDX_NHWC && d->in_scale == 0;
+  const bool f16_nhwc = d->x_dtype == SDX_F16 && d->x_layout == SDX_NHWC;
   const bool unit = d->sh == 1 && d->sw == 1;
   if (f16_nhwc && d->ic % 8 == 0 && unit && d->oc >= 8 && d->pool == 0 && d->y_layout == SDX_NHWC &&
       d->add_layout == SDX_NHWC) {
+    // 1x1: rows mode (with in_scale: per-image weights, checked at launch)
     if (d->kh == 1 && d->kw == 1 && d->pad_t == 0 && d->pad_l == 0 && d->pad_b == 0 && d->pad_r == 0) return R_TC_ROWS;
-    return R_TC_CONV;
+    if (d->in_scale == 0) return R_TC_CONV;
   }
   if (d->pool == 0 && d->in_scale == 0) return R_DIRECT;
   // conv + fused 2x2/2 max pool: the small stem convs the reference's GPU plans fuse
@@ -473,7 +474,7 @@ static bool conv_kxn(const sdx_conv_desc* d) {
 // output and an fp16 residual read at full resolution. Depends on the shape and these layout
 // fields only (not on pointers), so sdx_pack_conv and sdx_conv2d agree for one descriptor.
 static int conv_fold(const sdx_conv_desc* d) {
-  if (conv_route(d) != R_TC_ROWS) return 1;
+  if (conv_route(d) != R_TC_ROWS || d->in_scale) return 1;
   const int64_t ystride = d->y_pix_stride > 0 ? d->y_pix_stride : d->oc;
   if (d->y_dtype != SDX_F16 || ystride != d->oc || d->y_ch_off != 0 || d->add_dtype != SDX_F16 || d->add_up == 2)
     return 1;
@@ -561,6 +562,18 @@ int sdx_pack_gemm(int k, int n, int trans_b, const float* b, void* out, size_t* 
   return SDX_OK;
 }
 
+// Per-image scaled weights of a 1x1 tensor-core conv with in_scale: batch two-term copies of the
+// rows-mode packed weights. The form needs one N tile (oc <= 128), resident weights (ic <= 256) and
+// 128-row tiles that never straddle two images (ih * iw % 128 == 0).
+size_t sdx_conv_scaled_weights_bytes(const sdx_conv_desc* d) {
+  if (!d || conv_route(d) != R_TC_ROWS || d->oc > 128 || d->ic > 256 || d->batch <= 0 ||
+      ((int64_t)d->ih * d->iw) % 128 != 0)
+    return 0;
+  int BN, nt;
+  tc_plan_n(d->oc, &BN, &nt);
+  return (size_t)d->batch * 2 * (size_t)BN * nt * (size_t)tc_kpad_of(d->ic) * sizeof(__half);
+}
+
 // =========================================================================================
 // ops
 // =========================================================================================
@@ -623,6 +636,21 @@ int sdx_conv2d(sdx_ctx* ctx, const sdx_conv_desc* d, sdx_stream s) {
       p.act = d->act;
       p.gap = P<float>(d->gap_sums);
       p.err = ctx->err_word;
+      if (route == R_TC_ROWS && d->in_scale) {
+        // x * s read as x: the weights scaled per image (two terms) into the caller's scratch
+        if (!d->w_scaled || sdx_conv_scaled_weights_bytes(d) == 0 || d->gap_sums)
+          return set_error(SDX_ERR_NOT_SUPPORTED,
+                           "conv: in_scale on a 1x1 conv needs w_scaled scratch, oc <= 128, ic <= 256, ih*iw %% 128 "
+                           "== 0 and no fused channel sums");
+        int BN, nt;
+        tc_plan_n(d->oc, &BN, &nt);
+        const int rc = tc_scale_weights_launch(P<const __half>(d->w), conv_wterms(d), BN * nt, tc_kpad_of(d->ic), d->ic,
+                                               P<const float>(d->in_scale), d->batch, P<__half>(d->w_scaled), st);
+        if (rc) return rc;
+        p.w = P<const __half>(d->w_scaled);
+        p.wterms = 2;
+        p.img_rows = d->ih * d->iw;
+      }
       if (route == R_TC_ROWS) {
         const int f = conv_fold(d);
         if (f > 1) {

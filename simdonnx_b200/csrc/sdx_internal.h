@@ -80,6 +80,10 @@ struct TcProblem {
   int* arg_i;
   float* arg_s;
   int arg_ld;  // entries between two N tiles' states (>= M)
+  // per-image weights (rows mode, one N tile, two terms): w holds M / img_rows consecutive weight
+  // sets of the packed layout, image i's GEMM rows being [i * img_rows, (i + 1) * img_rows) with
+  // img_rows a multiple of 128; 0 = one weight set for every row
+  int img_rows;
   void* out;
   int out_f32;
   int64_t out_pix_stride;
@@ -111,6 +115,12 @@ void tc_pack_conv(const float* w, int OC, int IC, int KH, int KW, int terms, __h
 // row when OC * F <= 128 and IC * F <= 128 (thin convs: F times the pixels per tile for the same
 // per-tile cost). The caller checks the layout conditions (dense fp16 output and residual).
 int tc_fold_factor(int64_t pixels, int IC, int OC);
+// Per-image weights of a 1x1 conv whose input is x * s (s fp32 [batch, K], an SE gate): out[i] =
+// the two-term fp16 split of (w_hi + w_lo) * s[i, k] over every K column k of the packed rows-mode
+// weights w (terms 1 or 2, `rows` rows of kpad halves per term); out is [batch][2][rows][kpad].
+int tc_scale_weights_launch(const __half* w, int terms, int rows, int kpad, int K, const float* s, int batch,
+                            __half* out, cudaStream_t st);
+int tc_kpad_of(int K);
 size_t tc_fold_weights_halves(int IC, int OC, int fold, int terms);
 // Block-diagonal B operand of the folded GEMM: row j*OC + o, column j*IC + c = w[o][c]
 void tc_pack_conv_fold(const float* w, int OC, int IC, int fold, int terms, __half* out);

@@ -59,8 +59,9 @@ def node_cost(plan: ExecPlan, n) -> tuple:
         sc = getattr(p, "in_scale", None)
         if sc:
             byt += _nb(plan, sc)
-        if len(n.outs) > 1:  # fused 32-pixel channel sums for the SE gate
-            byt += _nb(plan, n.outs[1])
+        for o in n.outs[1:]:  # fused 32-pixel channel sums for the SE gate (not the per-image weight scratch)
+            if o != getattr(p, "w_scaled", None):
+                byt += _nb(plan, o)
         return cls, flops, byt
     if op == "ConvTranspose":
         nb, ih, iw, ic = plan.values[n.ins[0]].shape

@@ -89,7 +89,9 @@ def cuda_rewrite(plan: ExecPlan) -> ExecPlan:
         out_nodes.append(n)
     P.nodes = out_nodes
 
-    # 2. SE product folded into consuming depthwise convs
+    # 2. SE product x * s folded into the convs that consume it: depthwise convs scale their staged
+    #    weights; 1x1 tensor-core convs get per-image scaled weights (sdx_conv_desc.in_scale; the
+    #    scratch is added in the last step, after the rewrites that replace conv nodes)
     keep = []
     for n in P.nodes:
         if n.op == "Elementwise" and n.p.op == "mul" and n.p.act == "none":
@@ -97,7 +99,9 @@ def cuda_rewrite(plan: ExecPlan) -> ExecPlan:
             xs, ss = P.values[x].shape, P.values[s].shape
             cons = P.consumers(n.outs[0])
             if (len(ss) == 2 and len(xs) == 4 and ss == (xs[0], xs[3]) and cons and n.outs[0] != P.output and
-                    all(c.op == "Conv" and c.p.group > 1 and c.ins[0] == n.outs[0] for c in cons)):
+                    P.values[s].dtype == "f32" and
+                    all(c.op == "Conv" and c.ins[0] == n.outs[0] and
+                        (c.p.group > 1 or _scaled_rows_bytes(P, c, x) > 0) for c in cons)):
                 for c in cons:
                     c.ins[0] = x
                     c.p.in_scale = s
@@ -261,7 +265,33 @@ def cuda_rewrite(plan: ExecPlan) -> ExecPlan:
         sums = P.add_value(m.outs[0] + ".gapsums", (nb * h * w // 32, c), "f32", "raw")
         m.outs.append(sums)
         n.ins.append(sums)
+
+    # 9. scratch of the per-image scaled weights of the 1x1 convs that read x * s (step 2): an extra
+    #    output of the conv, live for that node only
+    for n in P.nodes:
+        if n.op == "Conv" and n.p.group == 1 and getattr(n.p, "in_scale", None) is not None:
+            nbytes = _scaled_rows_bytes(P, n, n.ins[0])
+            assert nbytes > 0, n.name
+            w = P.add_value(n.name + ".wscaled", (nbytes,), "u8", "raw")
+            n.outs.append(w)
+            n.p.w_scaled = w
     return P
+
+
+def _scaled_rows_bytes(P: ExecPlan, c: Node, x: str) -> int:
+    """Scratch bytes if conv `c`, reading x * s, runs as a 1x1 tensor-core conv with per-image
+    scaled weights (sdx_conv_scaled_weights_bytes), else 0."""
+    if (c.op != "Conv" or c.p.group != 1 or tuple(c.p.kernel) != (1, 1) or tuple(c.p.strides) != (1, 1) or
+            any(c.p.pads) or c.p.pool is not None):
+        return 0
+    xv, yv = P.values[x], P.values[c.outs[0]]
+    if xv.dtype != "f16" or xv.layout != "nhwc" or yv.layout != "nhwc" or len(xv.shape) != 4:
+        return 0
+    nb, ih, iw, ic = xv.shape
+    oc = P.values[c.ins[1]].const.shape[0]
+    d = B.conv_desc(nb, ih, iw, ic, oc, 1, 1, y_dtype=torch.float16 if yv.dtype == "f16" else torch.float32)
+    d.in_scale = 1  # set: the query only reads whether it is
+    return B.conv_scaled_weights_bytes(d)
 
 
 class CudaInferenceSession:
@@ -349,15 +379,18 @@ class CudaInferenceSession:
                             pool=p.pool is not None, pool_relu=bool(p.pool and p.pool.fuse_relu),
                             y_pix_stride=P.shape(yslice[0])[3] if yslice else 0, y_ch_off=yslice[1] if yslice else 0)
             d.add_up = getattr(p, "add_up", 0)  # a layout field: set before packing (the fold depends on it)
+            scale = getattr(p, "in_scale", None)
+            d.in_scale = self.ptr(scale) if scale else 0  # so is whether in_scale is set
             wt = self._const_dev(("convw", n.name), lambda: B.pack_conv(d, W, self.device))
             d.x = self.ptr(n.ins[0])
             d.w = B.ptr(wt)
             d.bias = self._f32(p.bias) if p.bias else (self._zeros(oc) if p.group > 1 else 0)
             d.add = self.ptr(p.add) if p.add else 0
             d.y = self.ptr(n.outs[0])
-            d.gap_sums = self.ptr(n.outs[1]) if len(n.outs) > 1 else 0
-            scale = getattr(p, "in_scale", None)
-            d.in_scale = self.ptr(scale) if scale else 0
+            wsc = getattr(p, "w_scaled", None)
+            sums = [o for o in n.outs[1:] if o != wsc]
+            d.gap_sums = self.ptr(sums[0]) if sums else 0
+            d.w_scaled = self.ptr(wsc) if wsc else 0
             return N.OP_CONV, d
         if op == "ConvTranspose":
             xv, yv = P.values[n.ins[0]], P.values[n.outs[0]]

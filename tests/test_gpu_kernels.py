@@ -429,6 +429,54 @@ def test_conv_upsampled_residual(be, ic, oc, k, h, w):
     assert be.device_error() == 0
 
 
+@pytest.mark.parametrize("nb,h,w,ic,oc,up,act", [
+    (2, 16, 16, 64, 96, False, "hardswish"),  # two-term source weights (ic < 128)
+    (2, 16, 16, 128, 96, True, "none"),       # one-term source weights, FPN top-down residual
+    (64, 16, 24, 64, 96, True, "none"),       # 3 tiles per image, 2 per CTA: CTA ranges cross images
+    (300, 8, 16, 40, 24, False, "relu"),      # 1 tile per image: a weight reload every tile; K padded
+])
+def test_pointwise_per_image_scale(be, nb, h, w, ic, oc, up, act):
+    """1x1 conv of the SE product x * s (s per image and channel) with the weights scaled per image
+    (sdx_conv_desc.in_scale on the tensor-core route, sdx_conv_scaled_weights_bytes of scratch)
+    against the oracle's conv of the materialised fp32 product."""
+    from simdonnx_b200 import _native as N, backend as B
+    rng = np.random.default_rng(nb + ic + oc)
+    x = rnd(rng, nb, h, w, ic)
+    sc = rng.uniform(0, 1, size=(nb, ic)).astype(np.float32)
+    wt = rnd(rng, oc, ic, 1, 1, scale=1 / np.sqrt(ic))
+    b = rnd(rng, oc)
+    conv = O.conv(O.channel_broadcast(x, sc), O.ConvPlan(wt, b), act=act)
+    d = B.conv_desc(nb, h, w, ic, oc, 1, 1, act=act)
+    sd = dev32(sc)
+    d.in_scale = B.ptr(sd)  # set before packing: the packed layout depends on it
+    r = None
+    if up:
+        r = rnd(rng, nb, h // 2, w // 2, oc)
+        conv = O.resize_nearest(r, (2, 2), add=conv)
+        d.add_up = 2
+    kpad = {40: 48, 64: 64, 128: 128}[ic]
+    assert B.conv_scaled_weights_bytes(d) == nb * 2 * ((oc + 15) // 16 * 16) * kpad * 2  # [nb][2 terms][rows][kpad]
+    wp = B.pack_conv(d, wt)
+    before = int(N.lib().sdx_launch_count())
+    y = B.conv2d(be, d, dev16(x), wp, bias=dev32(b), add=dev16(r) if up else None, in_scale=sd)
+    assert_close(host(y), conv, f"pointwise x*s {nb}x{h}x{w} {ic}->{oc}")
+    assert be.device_error() == 0
+    assert int(N.lib().sdx_launch_count()) - before == 2  # the weight scaling, then the conv
+
+
+def test_pointwise_per_image_scale_rejects_straddling_tiles(be):
+    """40x40 images (1600 pixels, not a multiple of 128): no per-image form, the call is refused."""
+    import ctypes
+    from simdonnx_b200 import _native as N, backend as B
+    d = B.conv_desc(2, 40, 40, 64, 96, 1, 1)
+    d.in_scale = 1
+    assert B.conv_scaled_weights_bytes(d) == 0
+    d.x = d.w = d.y = d.w_scaled = 1 << 20  # never dereferenced: refused before any launch
+    before = int(N.lib().sdx_launch_count())
+    assert N.lib().sdx_conv2d(be.ctx, ctypes.byref(d), None) != 0
+    assert int(N.lib().sdx_launch_count()) == before
+
+
 @pytest.mark.gpu
 @pytest.mark.parametrize("ic,oc,h,w,act", [(16, 32, 32, 40, "hardswish"), (64, 128, 16, 16, "relu"),
                                            (128, 256, 8, 12, "none")])
