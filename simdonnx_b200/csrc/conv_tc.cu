@@ -94,6 +94,9 @@ static bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 
 
 // Channel block of a K-long reduction: 64 channels (128-byte rows) when K pads to a multiple of 64,
 // else 32 or 16, so at most 15 zero channels are padded in.
+// weight bytes above which a k x k conv streams 32-channel blocks (they do not stay resident)
+static constexpr size_t TC_KBLK32_WEIGHTS = 96 * 1024;
+
 int tc_kblk(int K) {
   const int r = (K + 15) / 16 * 16;
   return r % 64 == 0 ? 64 : r % 32 == 0 ? 32 : 16;
@@ -140,7 +143,15 @@ int tc_launch(const TcProblem& p, cudaStream_t stream) {
     BN = 64;
     n_tiles = 2;
   }
-  const int kblk = tc_kblk(p.K), kpad = tc_kpad(p.K);
+  const int kpad = tc_kpad(p.K);
+  int kblk = tc_kblk(p.K);
+  // k x k convs with 128-column tiles whose weights cannot stay resident stream them with every
+  // stage: 32-channel blocks halve the stage (A box + kh weight taps), so that four or more stages
+  // are in flight instead of two (3x3 128->128 at 128x128: 545 -> 764 TFLOP/s; 64->128: 467 -> 628;
+  // 512->256 at 64x64: 609 -> 892). 64-column tiles lose with it (128->64: 570 -> 524).
+  if (p.mode == TC_CONV && !p.kxn && p.kh > 1 && kblk == 64 && p.N >= 128 &&
+      (size_t)(p.wterms == 1 ? 1 : 2) * p.kh * p.kw * kpad * ((p.N + 15) / 16 * 16) * 2 > TC_KBLK32_WEIGHTS)
+    kblk = 32;
   const int kbytes = kblk * 2;
   const bool imgw = p.img_rows > 0;
   if (imgw && (p.mode != TC_ROWS || convt || n_tiles != 1 || p.fold > 1 || p.arg_m || p.gap || p.wterms != 2 ||
