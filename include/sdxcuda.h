@@ -176,7 +176,7 @@ typedef struct sdx_conv_desc {
 int sdx_conv2d(sdx_ctx* ctx, const sdx_conv_desc* d, sdx_stream s);
 /* Bytes of the per-image weight scratch a 1x1 tensor-core conv with in_scale needs (batch two-term
  * copies of its packed weights), or 0 when that form does not apply to the descriptor's shape: it
- * needs fp16 NHWC x, ic % 8 == 0, oc in [8, 128], ic <= 256 and ih * iw a multiple of 128. */
+ * needs fp16 NHWC x, ic % 8 == 0, oc in [8, 128] and ic <= 256. */
 size_t sdx_conv_scaled_weights_bytes(const sdx_conv_desc* d);
 
 /* Gemm node: GemmP (src/Engine/ExecPlan.cs:87-93) via Nhwc.Gemm (src/Kernels/Nhwc.Avx512.cs:241-266):

@@ -898,22 +898,25 @@ int resize_launch(const ResizeArgs& a, cudaStream_t st) {
 // Channel concat of nearest-upsampled inputs (a Concat whose inputs are ResizeNearest outputs or
 // full-size tensors, fused): every output pixel is written whole, in 16-byte chunks, so no
 // partial-sector writes reach HBM. Input i has spatial size (oh / s_i, ow / s_i).
+// One block per output row (n, oy); thread (g, r) copies 16-byte channel group g of the pixels
+// ox = r, r + blockDim.y, ...: the source tensor, its scale and its row (n, oy / s) are fixed per
+// thread, so the loop is one shift (or division), one load and one store per 16 bytes.
 __global__ void concat_nearest_kernel(ConcatNearestArgs a) {
-  const int cg = a.ctot >> 3;
   const int row = blockIdx.x;  // n * oh + oy
   const int n = row / a.oh, oy = row - n * a.oh;
-  __half* yrow = a.y + (int64_t)row * a.ow * a.ctot;
-  const int total = a.ow * cg;
-  for (int t = threadIdx.x; t < total; t += blockDim.x) {
-    const int ox = t / cg, ch = (t - ox * cg) * 8;
-    int i = 0;
+  const int g = threadIdx.x, ch = g * 8;
+  int i = 0;
 #pragma unroll
-    for (int k = 1; k < 8; k++)
-      if (k < a.nin && ch >= a.off[k]) i = k;
-    const int sc = a.s[i];
-    const int ih = a.oh / sc, iw = a.ow / sc;
-    const __half* src = a.x[i] + (((int64_t)n * ih + oy / sc) * iw + ox / sc) * a.c[i] + (ch - a.off[i]);
-    *reinterpret_cast<uint4*>(yrow + (int64_t)t * 8) = __ldg(reinterpret_cast<const uint4*>(src));
+  for (int k = 1; k < 8; k++)
+    if (k < a.nin && ch >= a.off[k]) i = k;
+  const int sc = a.s[i], ci = a.c[i];
+  const int ih = a.oh / sc, iw = a.ow / sc;
+  const int lg = (sc & (sc - 1)) == 0 ? __ffs(sc) - 1 : -1;  // log2 of a power-of-two scale
+  const __half* src = a.x[i] + ((int64_t)n * ih + oy / sc) * iw * ci + (ch - a.off[i]);
+  __half* dst = a.y + (int64_t)row * a.ow * a.ctot + ch;
+  for (int ox = threadIdx.y; ox < a.ow; ox += blockDim.y) {
+    const int sx = lg >= 0 ? ox >> lg : ox / sc;
+    *reinterpret_cast<uint4*>(dst + (int64_t)ox * a.ctot) = __ldg(reinterpret_cast<const uint4*>(src + (int64_t)sx * ci));
   }
 }
 
@@ -928,8 +931,10 @@ int concat_nearest_launch(const ConcatNearestArgs& a, cudaStream_t st) {
   }
   const int64_t rows = (int64_t)a.batch * a.oh;
   if (rows == 0) return SDX_OK;
-  if (rows > INT32_MAX || (int64_t)a.ow * (a.ctot / 8) > INT32_MAX) return set_error(SDX_ERR_NOT_SUPPORTED, "concat nearest: too large");
-  concat_nearest_kernel<<<(unsigned)rows, 256, 0, st>>>(a);
+  const int cg = a.ctot / 8;
+  if (rows > INT32_MAX || cg > 256 || a.ctot % 8) return set_error(SDX_ERR_NOT_SUPPORTED, "concat nearest: too large");
+  const dim3 block((unsigned)cg, (unsigned)std::max(1, 256 / cg));
+  concat_nearest_kernel<<<(unsigned)rows, block, 0, st>>>(a);
   SDX_LAUNCH_CHECK("concat_nearest");
   return SDX_OK;
 }

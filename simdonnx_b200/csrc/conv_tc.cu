@@ -154,11 +154,13 @@ int tc_launch(const TcProblem& p, cudaStream_t stream) {
     kblk = 32;
   const int kbytes = kblk * 2;
   const bool imgw = p.img_rows > 0;
-  if (imgw && (p.mode != TC_ROWS || convt || n_tiles != 1 || p.fold > 1 || p.arg_m || p.gap || p.wterms != 2 ||
-               p.img_rows % TC_BM != 0 || p.M % p.img_rows != 0))
+  // per-image weights: rows mode when whole 128-row tiles fit an image, else the 1x1 conv in pixel-tile
+  // mode (tiles never straddle two images)
+  if (imgw && (convt || n_tiles != 1 || p.fold > 1 || p.arg_m || p.gap || p.wterms != 2 ||
+               (p.mode == TC_ROWS && (p.img_rows % TC_BM != 0 || p.M % p.img_rows != 0)) ||
+               (p.mode == TC_CONV && (p.kh != 1 || p.kw != 1 || p.kxn))))
     return set_error(SDX_ERR_NOT_SUPPORTED,
-                     "tc: per-image weights need a rows-mode conv with one N tile, two terms, no fused sums, and "
-                     "whole 128-row tiles per image");
+                     "tc: per-image weights need a 1x1 conv with one N tile, two terms and no fused sums");
   TcArgs a;
   memset(&a, 0, sizeof(a));
   a.mode = p.mode;
@@ -311,7 +313,7 @@ int tc_launch(const TcProblem& p, cudaStream_t stream) {
     if (rc) return rc;
   }
   {
-    const uint64_t sets = imgw ? (uint64_t)(p.M / p.img_rows) : 1;
+    const uint64_t sets = !imgw ? 1 : p.mode == TC_ROWS ? (uint64_t)(p.M / p.img_rows) : (uint64_t)p.batch;
     uint64_t dims[2] = {(uint64_t)kpad, (uint64_t)a.wterms * a.taps * a.b_rows_per_tap * sets};
     uint64_t strides[1] = {(uint64_t)kpad * 2};
     uint32_t box[2] = {(uint32_t)kblk, (uint32_t)BN};
@@ -426,7 +428,7 @@ int tc_launch(const TcProblem& p, cudaStream_t stream) {
   int grid = std::min(total, num_sms(dev));
   if (imgw && total > 0) {
     // contiguous tile ranges: each CTA crosses few image boundaries (weight reloads)
-    a.img_tiles = p.img_rows / TC_BM;
+    a.img_tiles = p.mode == TC_ROWS ? p.img_rows / TC_BM : a.tiles_h * a.tiles_w;
     a.b_img_rows = a.wterms * a.taps * a.b_rows_per_tap;
     a.per_cta = (total + grid - 1) / grid;
     grid = (total + a.per_cta - 1) / a.per_cta;

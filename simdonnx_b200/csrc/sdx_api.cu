@@ -563,12 +563,9 @@ int sdx_pack_gemm(int k, int n, int trans_b, const float* b, void* out, size_t* 
 }
 
 // Per-image scaled weights of a 1x1 tensor-core conv with in_scale: batch two-term copies of the
-// rows-mode packed weights. The form needs one N tile (oc <= 128), resident weights (ic <= 256) and
-// 128-row tiles that never straddle two images (ih * iw % 128 == 0).
+// packed weights. The form needs one N tile (oc <= 128) and resident weights (ic <= 256).
 size_t sdx_conv_scaled_weights_bytes(const sdx_conv_desc* d) {
-  if (!d || conv_route(d) != R_TC_ROWS || d->oc > 128 || d->ic > 256 || d->batch <= 0 ||
-      ((int64_t)d->ih * d->iw) % 128 != 0)
-    return 0;
+  if (!d || conv_route(d) != R_TC_ROWS || d->oc > 128 || d->ic > 256 || d->batch <= 0) return 0;
   int BN, nt;
   tc_plan_n(d->oc, &BN, &nt);
   return (size_t)d->batch * 2 * (size_t)BN * nt * (size_t)tc_kpad_of(d->ic) * sizeof(__half);
@@ -640,8 +637,8 @@ int sdx_conv2d(sdx_ctx* ctx, const sdx_conv_desc* d, sdx_stream s) {
         // x * s read as x: the weights scaled per image (two terms) into the caller's scratch
         if (!d->w_scaled || sdx_conv_scaled_weights_bytes(d) == 0 || d->gap_sums)
           return set_error(SDX_ERR_NOT_SUPPORTED,
-                           "conv: in_scale on a 1x1 conv needs w_scaled scratch, oc <= 128, ic <= 256, ih*iw %% 128 "
-                           "== 0 and no fused channel sums");
+                           "conv: in_scale on a 1x1 conv needs w_scaled scratch, oc <= 128, ic <= 256 and no fused "
+                           "channel sums");
         int BN, nt;
         tc_plan_n(d->oc, &BN, &nt);
         const int rc = tc_scale_weights_launch(P<const __half>(d->w), conv_wterms(d), BN * nt, tc_kpad_of(d->ic), d->ic,
@@ -650,6 +647,7 @@ int sdx_conv2d(sdx_ctx* ctx, const sdx_conv_desc* d, sdx_stream s) {
         p.w = P<const __half>(d->w_scaled);
         p.wterms = 2;
         p.img_rows = d->ih * d->iw;
+        if (p.img_rows % 128 != 0) p.mode = TC_CONV;  // 128-row tiles would straddle images: pixel tiles
       }
       if (route == R_TC_ROWS) {
         const int f = conv_fold(d);

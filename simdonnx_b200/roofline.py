@@ -36,8 +36,12 @@ def conv_kernel_class(plan: ExecPlan, n) -> str:
     if p.group > 1:
         return "depthwise"
     if (xv.dtype == "f16" and xv.layout == "nhwc" and ic % 8 == 0 and p.strides == (1, 1) and oc >= 8 and
-            p.pool is None and getattr(p, "in_scale", None) is None):
-        return "conv_tc_rows" if p.kernel == (1, 1) and not any(p.pads) else "conv_tc"
+            p.pool is None):
+        pointwise = p.kernel == (1, 1) and not any(p.pads)
+        if pointwise:  # with in_scale too (per-image weights)
+            return "conv_tc_rows"
+        if getattr(p, "in_scale", None) is None:
+            return "conv_tc"
     if ic <= 4 and p.pool is None:
         return "stem"  # graph-input stems: the small-channel tensor-core / TMA stem kernels
     return "direct_conv"

@@ -434,6 +434,8 @@ def test_conv_upsampled_residual(be, ic, oc, k, h, w):
     (2, 16, 16, 128, 96, True, "none"),       # one-term source weights, FPN top-down residual
     (64, 16, 24, 64, 96, True, "none"),       # 3 tiles per image, 2 per CTA: CTA ranges cross images
     (300, 8, 16, 40, 24, False, "relu"),      # 1 tile per image: a weight reload every tile; K padded
+    (5, 40, 40, 256, 96, True, "none"),       # 1600 pixels per image: pixel tiles (rows would straddle)
+    (3, 20, 12, 64, 32, False, "hardswish"),  # 240 pixels per image, thin output
 ])
 def test_pointwise_per_image_scale(be, nb, h, w, ic, oc, up, act):
     """1x1 conv of the SE product x * s (s per image and channel) with the weights scaled per image
@@ -454,7 +456,7 @@ def test_pointwise_per_image_scale(be, nb, h, w, ic, oc, up, act):
         r = rnd(rng, nb, h // 2, w // 2, oc)
         conv = O.resize_nearest(r, (2, 2), add=conv)
         d.add_up = 2
-    kpad = {40: 48, 64: 64, 128: 128}[ic]
+    kpad = {40: 48, 64: 64, 128: 128, 256: 256}[ic]
     assert B.conv_scaled_weights_bytes(d) == nb * 2 * ((oc + 15) // 16 * 16) * kpad * 2  # [nb][2 terms][rows][kpad]
     wp = B.pack_conv(d, wt)
     before = int(N.lib().sdx_launch_count())
@@ -464,11 +466,11 @@ def test_pointwise_per_image_scale(be, nb, h, w, ic, oc, up, act):
     assert int(N.lib().sdx_launch_count()) - before == 2  # the weight scaling, then the conv
 
 
-def test_pointwise_per_image_scale_rejects_straddling_tiles(be):
-    """40x40 images (1600 pixels, not a multiple of 128): no per-image form, the call is refused."""
+def test_pointwise_per_image_scale_rejects_wide_outputs(be):
+    """256 output channels (two N tiles): no per-image form, the call is refused before any launch."""
     import ctypes
     from simdonnx_b200 import _native as N, backend as B
-    d = B.conv_desc(2, 40, 40, 64, 96, 1, 1)
+    d = B.conv_desc(2, 40, 40, 64, 256, 1, 1)
     d.in_scale = 1
     assert B.conv_scaled_weights_bytes(d) == 0
     d.x = d.w = d.y = d.w_scaled = 1 << 20  # never dereferenced: refused before any launch
