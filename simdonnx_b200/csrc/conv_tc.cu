@@ -133,7 +133,7 @@ int tc_launch(const TcProblem& p, cudaStream_t stream) {
   const bool convt = p.convt_oc > 0;
   int BN, n_tiles;
   if (convt) tc_plan_n_convt(p.convt_kh, p.convt_kw, p.convt_oc, &BN, &n_tiles);
-  else if (p.kxn) BN = 96, n_tiles = 1;
+  else if (p.kxn) BN = 3 * tc_kxn_block(p.N), n_tiles = 1;
   else tc_plan_n(p.N, &BN, &n_tiles);
   // 128 output columns of a short reduction (pointwise convs): two 64-column tiles, whose fast
   // epilogue runs four warp groups instead of two; the packed weights are the same 128 rows, and
@@ -236,7 +236,7 @@ int tc_launch(const TcProblem& p, cudaStream_t stream) {
   memset(&mRes, 0, sizeof(mRes));
   if (p.mode == TC_CONV && p.kxn) {
     // kx-in-N: a virtual conv with the 3 row taps as pipeline taps (halo mode, one column block)
-    // and N = 3 x 32 columns (kx, oc); the A box is BW = BWs + 2 input columns wide, starting one
+    // and N = 3 x kb columns (kx, oc), kb = 32 or 64; the A box is BW = BWs + 2 input columns wide, starting one
     // column left of the tile, so row x of the tile holds input column ox0 - 1 + x
     if (p.C % 8 != 0) return set_error(SDX_ERR_INVALID, "tc conv: input channels must be a multiple of 8");
     const int BW = (p.OW + 13) / 14 * 14 <= (p.OW + 29) / 30 * 30 ? 16 : 32;  // less column waste
@@ -413,8 +413,7 @@ int tc_launch(const TcProblem& p, cudaStream_t stream) {
     a.log2G = a.G == 16 ? 4 : a.G == 32 ? 5 : 6;
   }
   // straight-line kx-in-N epilogue: fp16 out with 16-byte rows, no residual, N a multiple of 8
-  const bool kxn_fast = p.kxn && !p.out_f32 && a.vec_ok && !p.res && p.N % 8 == 0 && p.N <= 32 &&
-                        BN * n_tiles <= TC_BIAS_SMEM_MAX;
+  const bool kxn_fast = p.kxn && !p.out_f32 && a.vec_ok && !p.res && p.N % 8 == 0 && BN * n_tiles <= TC_BIAS_SMEM_MAX;
   if (kxn_fast) a.bias_smem = BN * n_tiles;
   // ---- shared-memory plan. Preference: weights resident (loaded once per CTA) with 2 staging
   // buffers and >= 3 A stages, resident with 1 staging buffer and >= 2 stages, then streamed
@@ -426,6 +425,10 @@ int tc_launch(const TcProblem& p, cudaStream_t stream) {
   cudaGetDevice(&dev);
   const int total = a.m_tiles * a.n_tiles;
   int grid = std::min(total, num_sms(dev));
+  // pixel-tile pairs for halo-mode convs whose weights are streamed (decided with the smem plan): the
+  // two tiles' A boxes share each weight stage; only with whole pairs and a pair per SM at least
+  const bool pair_ok = p.mode == TC_CONV && a.halo && !p.kxn && !convt && !chain && !imgw && BN <= 128 &&
+                       a.m_tiles % 2 == 0 && (a.m_tiles / 2) * n_tiles >= num_sms(dev) && !argmax;
   if (imgw && total > 0) {
     // contiguous tile ranges: each CTA crosses few image boundaries (weight reloads)
     a.img_tiles = p.mode == TC_ROWS ? p.img_rows / TC_BM : a.tiles_h * a.tiles_w;
@@ -461,9 +464,10 @@ int tc_launch(const TcProblem& p, cudaStream_t stream) {
         if (a.kb_per_tap % cps) continue;
         for (int nsb = a.tma_out ? 2 : 1; nsb >= 1 && !planned; nsb--) {
           a.b_resident = res;
+          a.mpair = (pair_ok && !res) ? 1 : 0;
           a.nsbuf = nsb;
           a.cps = cps;
-          a.a_stage_bytes = (uint32_t)cps * a.a_blk_bytes;
+          a.a_stage_bytes = (uint32_t)(a.mpair ? 2 : 1) * cps * a.a_blk_bytes;
           const size_t fixed = smem_fixed(a);
           const size_t per = a.a_stage_bytes + b_stage_bytes_of(a);
           if (fixed >= (size_t)TC_SMEM_LIMIT) continue;
@@ -478,6 +482,7 @@ int tc_launch(const TcProblem& p, cudaStream_t stream) {
   }
   }
   if (!planned) return set_error(SDX_ERR_NOT_SUPPORTED, "tc: shared memory plan too large");
+  if (a.mpair) grid = std::min((a.m_tiles / 2) * n_tiles, num_sms(dev));
   const size_t smem = smem_bytes(a);
   if (smem > (size_t)TC_SMEM_LIMIT) return set_error(SDX_ERR_NOT_SUPPORTED, "tc: shared memory plan too large");
 
@@ -547,23 +552,35 @@ void tc_pack_conv(const float* w, int OC, int IC, int KH, int KW, int terms, __h
       }
 }
 
-bool tc_conv_kxn(int kh, int kw, int sh, int sw, int pt, int pl, int pb, int pr, int oc) {
-  return kh == 3 && kw == 3 && sh == 1 && sw == 1 && pt == 1 && pl == 1 && pb == 1 && pr == 1 && oc >= 8 && oc <= 32;
+// columns of one column tap in the kx-in-N layout: 32, or 64 for 33..64 output channels
+int tc_kxn_block(int oc) { return oc <= 32 ? 32 : 64; }
+
+size_t tc_kxn_weights_halves(int K, int OC, int terms) {
+  return (size_t)(terms == 1 ? 1 : 2) * 3 * 3 * tc_kxn_block(OC) * (size_t)tc_kpad(K);
 }
 
-size_t tc_kxn_weights_halves(int K, int terms) {
-  return (size_t)(terms == 1 ? 1 : 2) * 3 * 96 * (size_t)tc_kpad(K);
+// weight bytes up to which a 33..64-output 3x3 conv takes the kx-in-N form (resident weights)
+static constexpr size_t TC_KXN64_WEIGHTS = 150 * 1024;
+
+bool tc_conv_kxn(int kh, int kw, int sh, int sw, int pt, int pl, int pb, int pr, int oc, int ic, int terms) {
+  if (!(kh == 3 && kw == 3 && sh == 1 && sw == 1 && pt == 1 && pl == 1 && pb == 1 && pr == 1 && oc >= 8 && oc <= 64))
+    return false;
+  // 192-column tiles only while their weights stay resident (a streamed 192-column weight stage
+  // leaves no room for a pipeline)
+  return oc <= 32 || tc_kxn_weights_halves(ic, oc, terms) * 2 <= (size_t)TC_KXN64_WEIGHTS;
 }
 
-// kx-in-N weights: [terms][ky][kx * 32 + o][Kpad], rows o >= OC zero.
+
+// kx-in-N weights: [terms][ky][kx * kb + o][Kpad] (kb = tc_kxn_block(OC)), rows o >= OC zero.
 void tc_pack_conv_kxn(const float* w, int OC, int IC, int terms, __half* out) {
-  const size_t kpad = (size_t)tc_kpad(IC), lo = (size_t)3 * 96 * kpad;
+  const int kb = tc_kxn_block(OC);
+  const size_t kpad = (size_t)tc_kpad(IC), lo = (size_t)3 * 3 * kb * kpad;
   memset(out, 0, sizeof(__half) * (terms == 1 ? 1 : 2) * lo);
   for (int o = 0; o < OC; o++)
     for (int c = 0; c < IC; c++)
       for (int ky = 0; ky < 3; ky++)
         for (int kx = 0; kx < 3; kx++) {
-          const size_t idx = ((size_t)ky * 96 + kx * 32 + o) * kpad + c;
+          const size_t idx = ((size_t)ky * 3 * kb + kx * kb + o) * kpad + c;
           const float v = w[((size_t)o * IC + c) * 9 + ky * 3 + kx];
           if (terms == 1) out[idx] = __float2half_rn(v);
           else put2(out, idx, lo, v);

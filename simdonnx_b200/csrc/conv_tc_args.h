@@ -103,6 +103,10 @@ struct TcArgs {
   int img_tiles;
   int per_cta;
   int b_img_rows;
+  // pixel-tile pairs (halo mode, streamed weights, m_tiles even): unit u = (pair u / n_tiles, N tile
+  // u % n_tiles) covers m tiles 2 * pair and 2 * pair + 1, whose A boxes share every weight stage
+  // (half the weight traffic per MMA); units are strided by the grid, tiles of a unit consecutive
+  int mpair;
   unsigned int* err;
 };
 

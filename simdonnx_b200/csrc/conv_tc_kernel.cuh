@@ -847,6 +847,61 @@ __global__ void __launch_bounds__(tc_threads(G), 1)
                                  issued_mask, last_phase);
         ok = false;  // every tile issued above
       }
+      if (a.mpair) {
+        // pixel-tile pairs: each stage holds both tiles' A boxes (halo mode) and one weight stage
+        const int n_units = (a.m_tiles >> 1) * a.n_tiles;
+        const int per_img = a.tiles_h * a.tiles_w;
+        for (int u = blockIdx.x; u < n_units && ok; u += gridDim.x) {
+          const int pi = u / a.n_tiles, n_tile = u - pi * a.n_tiles;
+          int img[2], oy0[2], ox0[2];
+#pragma unroll
+          for (int j = 0; j < 2; j++) {
+            const int m = 2 * pi + j;
+            img[j] = m / per_img;
+            const int r = m - img[j] * per_img;
+            const int ty = r / a.tiles_w;
+            oy0[j] = ty * a.BH;
+            ox0[j] = (r - ty * a.tiles_w) * a.BWs;
+          }
+          int tk = 0, cg = 0;
+          for (int kb = 0; kb < kblocks; kb++) {
+            if (!mbar_wait_warp(smem_u32(&empty[s]), phase ^ 1u, a.err, SDX_DEV_WAIT_EMPTY, abort_flag)) {
+              ok = false;
+              break;
+            }
+            const uint32_t fb = smem_u32(&full[s]);
+            mbar_arrive_expect_tx_p(ld, fb, (uint32_t)(2 * a.cps) * a.a_box_bytes + b_stage_bytes);
+            const uint32_t dA0 = smem_u32(sA) + (uint32_t)s * a.a_stage_bytes;
+            const uint32_t dB0 = smem_u32(sB) + (uint32_t)s * b_stage_bytes;
+            for (int ci = 0; ci < a.cps; ci++) {
+              const int cb = cg * a.cps + ci;
+#pragma unroll
+              for (int j = 0; j < 2; j++)
+                tma_load_4d_p(ld, dA0 + (uint32_t)(j * a.cps + ci) * a.a_blk_bytes, &tmA, fb, cb * a.kblk,
+                              ox0[j] + tk - a.pad_l, oy0[j] - a.pad_t, img[j]);
+              const uint32_t dB = dB0 + (uint32_t)ci * b_cb_bytes;
+              for (int jj = 0; jj < a.b_taps; jj++) {
+                const int brow = (jj * a.kw + tk) * a.b_rows_per_tap + n_tile * a.BN;
+                tma_load_2d_p(ld, dB + jj * b_tap_bytes, &tmB, fb, cb * a.kblk, brow);
+                if (a.wterms == 2)
+                  tma_load_2d_p(ld, dB + b_half_bytes + jj * b_tap_bytes, &tmB, fb, cb * a.kblk,
+                                a.taps * a.b_rows_per_tap + brow);
+              }
+            }
+            issued_mask |= 1u << s;
+            last_phase = (last_phase & ~(1u << s)) | (phase << s);
+            if (++cg == groups) {
+              cg = 0;
+              tk++;
+            }
+            if (++s == S) {
+              s = 0;
+              phase ^= 1u;
+            }
+          }
+        }
+        ok = false;  // every unit issued above
+      }
       for (int tile = t_begin; tile < t_end && ok; tile += t_step) {
         const int m_tile = a.n_tiles == 1 ? tile : tile / a.n_tiles;
         const int n_tile = tile - m_tile * a.n_tiles;
@@ -985,6 +1040,59 @@ __global__ void __launch_bounds__(tc_threads(G), 1)
         }
         ok = false;  // the loop above ran every tile
       }
+      if (ok && a.mpair) {
+        // pixel-tile pairs: per stage and channel block, the same weight descriptor for both tiles'
+        // A blocks into their two accumulators
+        const int n_units = (a.m_tiles >> 1) * a.n_tiles;
+        for (int u = blockIdx.x; u < n_units && ok; u += gridDim.x) {
+          uint32_t dj[2], aj[2];
+#pragma unroll
+          for (int j = 0; j < 2; j++) {
+            if (!mbar_wait_warp(smem_u32(&acce[acc]), accph ^ 1u, a.err, SDX_DEV_WAIT_ACC_EMPTY, abort_flag)) {
+              ok = false;
+              break;
+            }
+            aj[j] = acc;
+            dj[j] = tmem_base + acc * (uint32_t)a.acc_stride;
+            if (++acc == (uint32_t)a.nacc) {
+              acc = 0;
+              accph ^= 1u;
+            }
+          }
+          if (!ok) break;
+          tc_fence_after();
+          uint32_t first = 0;
+          for (int kb = 0; kb < kblocks; kb++) {
+            if (!mbar_wait_warp(smem_u32(&full[s]), phase, a.err, SDX_DEV_WAIT_FULL, abort_flag)) {
+              ok = false;
+              break;
+            }
+            tc_fence_after();
+            const uint32_t sa = smem_u32(sA) + (uint32_t)s * a.a_stage_bytes;
+            uint32_t b0 = sB_addr + (uint32_t)s * b_stage_bytes;
+            for (int ci = 0; ci < a.cps; ci++, b0 += b_cb) {
+              const uint64_t bd = dconst | (uint64_t)((b0 >> 4) & 0x3FFFu);
+#pragma unroll
+              for (int j = 0; j < 2; j++) {
+                const uint32_t saj = sa + (uint32_t)(j * a.cps + ci) * a.a_blk_bytes;
+                const uint64_t ad = dconst | (uint64_t)((saj >> 4) & 0x3FFFu);
+                if (a.wterms == 2) umma_stage_dispatch<true>(ld, a.b_taps, nk, dj[j], ad, bd, a_tap16, b_tap16, b_lo16, idesc, first);
+                else umma_stage_dispatch<false>(ld, a.b_taps, nk, dj[j], ad, bd, a_tap16, b_tap16, b_lo16, idesc, first);
+              }
+              first = 1u;
+            }
+            tc_commit_p(ld, smem_u32(&empty[s]));
+            if (++s == S) {
+              s = 0;
+              phase ^= 1u;
+            }
+          }
+          if (!ok) break;
+          tc_commit_p(ld, smem_u32(&accf[aj[0]]));
+          tc_commit_p(ld, smem_u32(&accf[aj[1]]));
+        }
+        ok = false;  // every unit ran above
+      }
       int cur_img = imgw ? t_begin / a.img_tiles : 0;
       uint32_t b_waits = 1;  // weight sets waited for (the first one above)
       for (int tile = t_begin; tile < t_end && ok; tile += t_step) {
@@ -1051,7 +1159,18 @@ __global__ void __launch_bounds__(tc_threads(G), 1)
     // 1024-aligned slab); 0 when the staging rows are not swizzled
     const uint32_t xr = a.swz ? (((uint32_t)lane * P) >> 7) & (P / 16u - 1u) : 0u;
     const uint32_t stage0 = smem_u32(sStage) + (uint32_t)e * a.nsbuf * a.sbuf_bytes + (uint32_t)q * 32u * P;
-    const int tile0 = t_begin + e * t_step, tstep = G * t_step;
+    // tile of this CTA's ordinal o (the order in which the MMA warp fills the accumulators), or -1
+    auto ord_tile = [&](int o) -> int {
+      if (a.mpair) {
+        const int u = (int)blockIdx.x + (o >> 1) * (int)gridDim.x;
+        if (u >= (a.m_tiles >> 1) * a.n_tiles) return -1;
+        const int pi = u / a.n_tiles;
+        return (2 * pi + (o & 1)) * a.n_tiles + (u - pi * a.n_tiles);
+      }
+      const int t = t_begin + o * t_step;
+      return t < t_end ? t : -1;
+    };
+    const int tile0 = ord_tile(e);
     uint32_t res_phase = 0;    // bit b: parity of the next wait on buffer b's residual barrier
     bool res_pending = false;  // a residual load is in flight into buffer (lc % nsbuf)
     const uint32_t eld = elect_leader();  // this warp's issuing lane for TMA copies and bulk groups
@@ -1085,13 +1204,15 @@ __global__ void __launch_bounds__(tc_threads(G), 1)
       mbar_arrive_expect_tx_p(eld, rb, (uint32_t)ng * a.slab_tx);
       for (int g = 0; g < ng; g++) warp_copy(eld, a, &tmRes, slab + g * a.group_bytes, g, q, t, true, rb);
     };
-    if (a.tma_res && tile0 < t_end) {
+    if (a.tma_res && tile0 >= 0) {
       issue_res(tile0, 0);
       res_pending = true;
     }
 
     uint32_t lc = 0;  // this group's tile count
-    for (int tile = tile0; tile < t_end; tile += tstep, lc++) {
+    for (int o = e;; o += G, lc++) {
+      const int tile = ord_tile(o);
+      if (tile < 0) break;
       const uint32_t lt = G * lc + (uint32_t)e;
       const uint32_t acc = lt & (uint32_t)(a.nacc - 1), ar = lt >> (a.nacc == 4 ? 2 : 1);
       const uint32_t sbi = a.nsbuf == 2 ? (lc & 1u) : 0u;
@@ -1228,14 +1349,15 @@ __global__ void __launch_bounds__(tc_threads(G), 1)
         const bool st_ok = x >= 1 && x <= a.BW - 2 && oy < a.OH && ox < a.OW;
         __half* outp = static_cast<__half*>(a.out) +
                        ((((int64_t)tcd.img * a.OH + oy) * a.OW + ox) * a.out_pix_stride + a.out_ch_off);
-        const int halves = a.N > 16 ? 2 : 1;
+        const int halves = (a.N + 15) >> 4;  // 16-channel chunks
+        const uint32_t kb = (uint32_t)a.BN / 3u;  // columns per column tap (32 or 64)
 #pragma unroll
-        for (int hf = 0; hf < 2; hf++) {
+        for (int hf = 0; hf < 4; hf++) {
           if (hf < halves) {
             float v0[16], v1[16], v2[16];
             tmem_ld16_issue(tbase + (uint32_t)(hf * 16), v0);
-            tmem_ld16_issue(tbase + (uint32_t)(32 + hf * 16), v1);
-            tmem_ld16_issue(tbase + (uint32_t)(64 + hf * 16), v2);
+            tmem_ld16_issue(tbase + kb + (uint32_t)(hf * 16), v1);
+            tmem_ld16_issue(tbase + 2u * kb + (uint32_t)(hf * 16), v2);
             tmem_wait_ld();
             tmem_ld_wait16(v0);
             tmem_ld_wait16(v1);
@@ -1270,70 +1392,75 @@ __global__ void __launch_bounds__(tc_threads(G), 1)
         continue;
       }
       if (a.kxn) {
-        // kx-in-N: columns kx * 32 + oc; row x of the tile is input column ox0 - 1 + x, and the
-        // output at that column is D[x - 1][kx 0] + D[x][kx 1] + D[x + 1][kx 2] (neighbouring
-        // lanes: the 32 rows of a warp are consecutive columns of one or two tile rows)
-        float sum[32];
+        // kx-in-N: columns kx * kb + oc (kb = 32 or 64); row x of the tile is input column ox0 - 1 + x,
+        // and the output at that column is D[x - 1][kx 0] + D[x][kx 1] + D[x + 1][kx 2] (neighbouring
+        // lanes: the 32 rows of a warp are consecutive columns of one or two tile rows); 32 output
+        // channels per pass
+        const int kb = a.BN / 3;
+        for (int c0 = 0; c0 < kb; c0 += 32) {
+          float sum[32];
 #pragma unroll
-        for (int i = 0; i < 32; i++) sum[i] = 0.0f;
+          for (int i = 0; i < 32; i++) sum[i] = 0.0f;
 #pragma unroll
-        for (int kx = 0; kx < 3; kx++) {
-          float v[32];
-          tmem_ld16_issue(tbase + (uint32_t)(kx * 32), v);
-          tmem_ld16_issue(tbase + (uint32_t)(kx * 32 + 16), v + 16);
-          tmem_wait_ld();
-          tmem_ld_wait16(v);
-          tmem_ld_wait16(v + 16);
-          if (kx == 2) {
-            tc_fence_before();
-            mbar_arrive(smem_u32(&acce[acc]));
-          }
-#pragma unroll
-          for (int i = 0; i < 32; i++) {
-            float u = v[i];
-            if (kx == 0) u = __shfl_up_sync(0xffffffffu, u, 1);
-            if (kx == 2) u = __shfl_down_sync(0xffffffffu, u, 1);
-            sum[i] += u;
-          }
-        }
-        const int h = row_in_tile / a.BW, x = row_in_tile - h * a.BW;
-        const int oy = tcd.oy0 + h, ox = tcd.ox0 - 1 + x;
-        if (x >= 1 && x <= a.BW - 2 && oy < a.OH && ox < a.OW) {
-          const int64_t px = ((int64_t)tcd.img * a.OH + oy) * a.OW + ox;
-#pragma unroll
-          for (int o0 = 0; o0 < 32; o0 += 8) {
-            if (o0 >= a.N) break;
-            float r8[8];
-#pragma unroll
-            for (int j = 0; j < 8; j++) {
-              const int o = o0 + j;
-              r8[j] = sum[o0 + j] + (a.bias_smem ? sBias[o] : (a.bias && o < a.N ? __ldg(a.bias + o) : 0.0f));
+          for (int kx = 0; kx < 3; kx++) {
+            float v[32];
+            tmem_ld16_issue(tbase + (uint32_t)(kx * kb + c0), v);
+            tmem_ld16_issue(tbase + (uint32_t)(kx * kb + c0 + 16), v + 16);
+            tmem_wait_ld();
+            tmem_ld_wait16(v);
+            tmem_ld_wait16(v + 16);
+            if (kx == 2 && c0 + 32 >= kb) {
+              tc_fence_before();
+              mbar_arrive(smem_u32(&acce[acc]));
             }
-            if (a.vec_ok && o0 + 8 <= a.N) {
-              if (a.res) {
-                float q8[8];
-                load8_res(a, px * a.res_pix_stride + a.res_ch_off + o0, q8);
 #pragma unroll
-                for (int j = 0; j < 8; j++) r8[j] += q8[j];
-              }
+            for (int i = 0; i < 32; i++) {
+              float u = v[i];
+              if (kx == 0) u = __shfl_up_sync(0xffffffffu, u, 1);
+              if (kx == 2) u = __shfl_down_sync(0xffffffffu, u, 1);
+              sum[i] += u;
+            }
+          }
+          const int h = row_in_tile / a.BW, x = row_in_tile - h * a.BW;
+          const int oy = tcd.oy0 + h, ox = tcd.ox0 - 1 + x;
+          if (x >= 1 && x <= a.BW - 2 && oy < a.OH && ox < a.OW) {
+            const int64_t px = ((int64_t)tcd.img * a.OH + oy) * a.OW + ox;
 #pragma unroll
-              for (int j = 0; j < 8; j++) r8[j] = act_t<ACT>(r8[j]);
-              store8(a, px * a.out_pix_stride + a.out_ch_off + o0, r8);
-            } else {
+            for (int q0 = 0; q0 < 32; q0 += 8) {
+              const int o0 = c0 + q0;
+              if (o0 >= a.N) break;
+              float r8[8];
 #pragma unroll
               for (int j = 0; j < 8; j++) {
                 const int o = o0 + j;
-                if (o >= a.N) continue;
-                float y = r8[j];
+                r8[j] = sum[q0 + j] + (a.bias_smem ? sBias[o] : (a.bias && o < a.N ? __ldg(a.bias + o) : 0.0f));
+              }
+              if (a.vec_ok && o0 + 8 <= a.N) {
                 if (a.res) {
-                  const int64_t ro = px * a.res_pix_stride + a.res_ch_off + o;
-                  y += a.res_f32 ? static_cast<const float*>(a.res)[ro]
-                                 : __half2float(static_cast<const __half*>(a.res)[ro]);
+                  float q8[8];
+                  load8_res(a, px * a.res_pix_stride + a.res_ch_off + o0, q8);
+#pragma unroll
+                  for (int j = 0; j < 8; j++) r8[j] += q8[j];
                 }
-                y = act_t<ACT>(y);
-                const int64_t oo = px * a.out_pix_stride + a.out_ch_off + o;
-                if (a.out_f32) static_cast<float*>(a.out)[oo] = y;
-                else static_cast<__half*>(a.out)[oo] = __float2half_rn(y);
+#pragma unroll
+                for (int j = 0; j < 8; j++) r8[j] = act_t<ACT>(r8[j]);
+                store8(a, px * a.out_pix_stride + a.out_ch_off + o0, r8);
+              } else {
+#pragma unroll
+                for (int j = 0; j < 8; j++) {
+                  const int o = o0 + j;
+                  if (o >= a.N) continue;
+                  float y = r8[j];
+                  if (a.res) {
+                    const int64_t ro = px * a.res_pix_stride + a.res_ch_off + o;
+                    y += a.res_f32 ? static_cast<const float*>(a.res)[ro]
+                                   : __half2float(static_cast<const __half*>(a.res)[ro]);
+                  }
+                  y = act_t<ACT>(y);
+                  const int64_t oo = px * a.out_pix_stride + a.out_ch_off + o;
+                  if (a.out_f32) static_cast<float*>(a.out)[oo] = y;
+                  else static_cast<__half*>(a.out)[oo] = __float2half_rn(y);
+                }
               }
             }
           }
@@ -1421,11 +1548,11 @@ __global__ void __launch_bounds__(tc_threads(G), 1)
           }
           // the next tile's buffer is free once the store that last read it has read it; then its
           // residual rows can be fetched while this warp waits for the next accumulator
-          if (tile + tstep < t_end) {
+          if (ord_tile(o + G) >= 0) {
             if (a.nsbuf == 2) bulk_wait_read1(eld);
             else bulk_wait_read0(eld);
             if (a.tma_res) {
-              issue_res(tile + tstep, a.nsbuf == 2 ? ((lc + 1) & 1u) : 0u);
+              issue_res(ord_tile(o + G), a.nsbuf == 2 ? ((lc + 1) & 1u) : 0u);
               res_pending = true;
             }
           }

@@ -466,8 +466,11 @@ static int conv_route(const sdx_conv_desc* d) {
   return R_INVALID;
 }
 
+static int conv_wterms(const sdx_conv_desc* d);
+
 static bool conv_kxn(const sdx_conv_desc* d) {
-  return tc_conv_kxn(d->kh, d->kw, d->sh, d->sw, d->pad_t, d->pad_l, d->pad_b, d->pad_r, d->oc);
+  // the kx-in-N epilogues read no upsampled residual
+  return d->add_up != 2 && tc_conv_kxn(d->kh, d->kw, d->sh, d->sw, d->pad_t, d->pad_l, d->pad_b, d->pad_r, d->oc, d->ic, conv_wterms(d));
 }
 
 // Pixel folding factor of a 1x1 tensor-core conv (tc_fold_factor): only for a dense fp16 NHWC
@@ -502,7 +505,7 @@ int sdx_pack_conv(const sdx_conv_desc* d, const float* w, void* out, size_t* byt
   switch (route) {
     case R_TC_CONV:
     case R_TC_ROWS:
-      need = (route == R_TC_CONV && conv_kxn(d) ? tc_kxn_weights_halves(d->ic, conv_wterms(d))
+      need = (route == R_TC_CONV && conv_kxn(d) ? tc_kxn_weights_halves(d->ic, d->oc, conv_wterms(d))
               : conv_fold(d) > 1                ? tc_fold_weights_halves(d->ic, d->oc, conv_fold(d), conv_wterms(d))
                                                 : tc_weights_halves(d->oc, d->ic, taps, conv_wterms(d))) *
              sizeof(__half);

@@ -103,10 +103,12 @@ struct TcProblem {
 void tc_plan_n(int N, int* BN, int* n_tiles);
 int tc_launch(const TcProblem& p, cudaStream_t stream);
 size_t tc_weights_halves(int N, int K, int taps, int terms);
-// 3x3 stride-1 SAME convs with at most 32 output channels run with the three column taps kx as
-// GEMM columns (N = 3 x 32): a third of the thin MMAs; the epilogue adds the column-shifted parts.
-bool tc_conv_kxn(int kh, int kw, int sh, int sw, int pt, int pl, int pb, int pr, int oc);
-size_t tc_kxn_weights_halves(int K, int terms);
+// 3x3 stride-1 SAME convs with at most 64 output channels run with the three column taps kx as
+// GEMM columns (N = 3 x 32, or 3 x 64 above 32 outputs): a third of the thin MMAs; the epilogue adds
+// the column-shifted parts.
+bool tc_conv_kxn(int kh, int kw, int sh, int sw, int pt, int pl, int pb, int pr, int oc, int ic, int terms);
+int tc_kxn_block(int oc);
+size_t tc_kxn_weights_halves(int K, int OC, int terms);
 void tc_pack_conv_kxn(const float* w, int OC, int IC, int terms, __half* out);
 size_t tc_convt_weights_halves(int IC, int OC, int KH, int KW);
 void tc_plan_n_convt(int kh, int kw, int OC, int* BN, int* n_tiles);

@@ -72,6 +72,9 @@ CONV_CASES = [
     (128, 64, 3, 1, 30, 41, False, "relu"),
     (96, 24, 3, 1, 20, 20, False, "none"),
     (256, 256, 3, 1, 8, 8, True, "relu"),
+    # kx-in-N with 64-column tap blocks (33..64 outputs)
+    (64, 64, 3, 1, 40, 36, False, "relu"),
+    (32, 40, 3, 1, 21, 50, False, "hardswish"),
 ]
 
 
@@ -90,6 +93,29 @@ def test_conv_shapes(be, ic, oc, k, s, h, w, residual, act, w_terms):
     d = B.conv_desc(n, h, w, ic, oc, k, k, stride=(s, s), pads=(p, p, p, p), act=act, w_terms=w_terms)
     y = B.conv2d(be, d, dev16(x), B.pack_conv(d, wt), bias=dev32(b), add=None if res is None else dev16(res))
     assert_close(host(y), ref, f"conv {ic}->{oc} k{k} s{s} terms {w_terms}")
+
+
+@pytest.mark.parametrize("nb,h,w,ic,oc,residual,act", [
+    (4, 128, 128, 128, 128, False, "relu"),  # the UNet 128->128 level: 512 tiles, weights streamed
+    (10, 64, 64, 192, 128, True, "none"),    # residual through the TMA-staged epilogue
+    (10, 64, 64, 256, 256, False, "relu"),   # two N tiles per pixel-tile pair
+    (6, 40, 36, 128, 96, False, "hardswish"),
+    (4, 64, 64, 64, 64, False, "relu"),      # kx-in-N, 192-column tiles
+])
+def test_conv3x3_streamed_weights(be, nb, h, w, ic, oc, residual, act):
+    """3x3 convs whose weights do not stay in shared memory: 32-channel stages, and (with enough
+    tiles) two pixel tiles per weight stage into two accumulators."""
+    from simdonnx_b200 import backend as B
+    rng = np.random.default_rng(nb * 7 + ic + oc)
+    x = rnd(rng, nb, h, w, ic)
+    wt = rnd(rng, oc, ic, 3, 3, scale=1.0 / np.sqrt(ic * 9))
+    b = rnd(rng, oc)
+    res = rnd(rng, nb, h, w, oc) if residual else None
+    ref = O.conv(x, O.ConvPlan(wt, b, winograd=False), pads=(1, 1, 1, 1), act=act, add=res)
+    d = B.conv_desc(nb, h, w, ic, oc, 3, 3, pads=(1, 1, 1, 1), act=act)
+    y = B.conv2d(be, d, dev16(x), B.pack_conv(d, wt), bias=dev32(b), add=None if res is None else dev16(res))
+    assert_close(host(y), ref, f"conv3x3 {nb}x{h}x{w} {ic}->{oc}")
+    assert be.device_error() == 0
 
 
 def test_conv_into_channel_slice(be):
