@@ -228,6 +228,12 @@ def measure_extras(args, local, N, configs, roofline, torch, CudaInferenceSessio
     return out
 
 
+# DRAM bytes (ncu dram__bytes_read.sum + dram__bytes_write.sum) per launch of a kernel class of the
+# det step, from one ncu capture of the session's eager pass at 64 images per GPU (every launch of the
+# class averaged), scaled by 4 to the benchmark's 256 images (per-launch work is linear in images).
+TRAFFIC_PER_LAUNCH = {"conv_tc_rows": 691.4e6}
+
+
 def peaks_sustained() -> float:
     path = os.path.join(ROOT, "MEASURED_PEAKS.json")
     if os.path.exists(path):
@@ -357,7 +363,10 @@ def main() -> None:
         roof = {"bound": "hbm", "achieved": achieved, "peak": hbm, "unit": "GB/s", "frac": achieved / hbm}
     roof.update({"kernel": dom, "launches_per_step": dc["launches"], "ms_per_step": dc["ms"],
                  "algorithmic_bytes_per_step": dc["bytes"], "algorithmic_flops_per_step": dc["flops"],
-                 "peak_source": src, "traffic": None,
+                 "peak_source": src, "traffic": TRAFFIC_PER_LAUNCH.get(dom) if args.batch == 256 else None,
+                 "traffic_unit": "bytes per launch",
+                 "traffic_source": "ncu dram__bytes_read.sum + dram__bytes_write.sum, det eager pass at 64 images, "
+                                   "class average per launch x4",
                  "timing": "per-node CUDA events on the session stream, eager pass after the timed region"})
     tot = roofline.plan_totals(sess.plan)
     step_s = ms / 1e3 / args.steps

@@ -900,7 +900,8 @@ int resize_launch(const ResizeArgs& a, cudaStream_t st) {
 // partial-sector writes reach HBM. Input i has spatial size (oh / s_i, ow / s_i).
 // One block per output row (n, oy); thread (g, r) copies 16-byte channel group g of the pixels
 // ox = r, r + blockDim.y, ...: the source tensor, its scale and its row (n, oy / s) are fixed per
-// thread, so the loop is one shift (or division), one load and one store per 16 bytes.
+// thread, so the loop is one shift (or division), one load and one store per 16 bytes (unrolled
+// by four so that four loads are in flight).
 __global__ void concat_nearest_kernel(ConcatNearestArgs a) {
   const int row = blockIdx.x;  // n * oh + oy
   const int n = row / a.oh, oy = row - n * a.oh;
@@ -914,10 +915,19 @@ __global__ void concat_nearest_kernel(ConcatNearestArgs a) {
   const int lg = (sc & (sc - 1)) == 0 ? __ffs(sc) - 1 : -1;  // log2 of a power-of-two scale
   const __half* src = a.x[i] + ((int64_t)n * ih + oy / sc) * iw * ci + (ch - a.off[i]);
   __half* dst = a.y + (int64_t)row * a.ow * a.ctot + ch;
-  for (int ox = threadIdx.y; ox < a.ow; ox += blockDim.y) {
-    const int sx = lg >= 0 ? ox >> lg : ox / sc;
-    *reinterpret_cast<uint4*>(dst + (int64_t)ox * a.ctot) = __ldg(reinterpret_cast<const uint4*>(src + (int64_t)sx * ci));
+  auto sxo = [&](int ox) { return (int64_t)(lg >= 0 ? ox >> lg : ox / sc) * ci; };
+  const int by = blockDim.y;
+  int ox = threadIdx.y;
+  // four loads in flight per thread before their stores
+  for (; ox + 3 * by < a.ow; ox += 4 * by) {
+    uint4 v[4];
+#pragma unroll
+    for (int u = 0; u < 4; u++) v[u] = __ldg(reinterpret_cast<const uint4*>(src + sxo(ox + u * by)));
+#pragma unroll
+    for (int u = 0; u < 4; u++) *reinterpret_cast<uint4*>(dst + (int64_t)(ox + u * by) * a.ctot) = v[u];
   }
+  for (; ox < a.ow; ox += by)
+    *reinterpret_cast<uint4*>(dst + (int64_t)ox * a.ctot) = __ldg(reinterpret_cast<const uint4*>(src + sxo(ox)));
 }
 
 int concat_nearest_launch(const ConcatNearestArgs& a, cudaStream_t st) {
