@@ -235,6 +235,8 @@ typedef struct sdx_pool_desc {
   int batch, ih, iw, c, oh, ow, kh, kw, sh, sw, pad_t, pad_l;
   int is_avg, relu, count_include_pad;
   sdx_dptr x, y;
+  int64_t x_pix_stride; /* elements between input pixels (0 = c): x is a channel slice of a wider tensor */
+  int x_ch_off;         /* first channel of that slice */
 } sdx_pool_desc;
 int sdx_pool(sdx_ctx* ctx, const sdx_pool_desc* d, sdx_stream s);
 
@@ -292,7 +294,9 @@ typedef struct sdx_resize_desc {
 } sdx_resize_desc;
 int sdx_resize_nearest(sdx_ctx* ctx, const sdx_resize_desc* d, sdx_stream s);
 
-/* NHWC channel concat (Nhwc.ConcatInner, src/Kernels/Nhwc.Det.cs:354-370), fp16, up to 8 inputs. */
+/* NHWC channel concat (Nhwc.ConcatInner, src/Kernels/Nhwc.Det.cs:354-370), fp16, up to 8 inputs. An
+ * input pointer of 0 means that input's producer already wrote its slice of y (its channels still
+ * count for the slice offsets). */
 int sdx_concat_channels(sdx_ctx* ctx, int64_t pixels, int nin, const int* counts, const sdx_dptr* ins,
                         sdx_dptr y, sdx_stream s);
 /* Image-session preprocessing (the reference's Vulkan image session, src/Backends/Vulkan/
@@ -402,6 +406,10 @@ int sdx_matmul(sdx_ctx* ctx, const sdx_matmul_desc* d, sdx_stream s);
  * staging, src/Backends/Vulkan/VkSession.cs:286-310). */
 int sdx_convert(sdx_ctx* ctx, int batch, int c, int64_t hw, int x_dtype, int x_layout, int y_dtype, int y_layout,
                 sdx_dptr x, sdx_dptr y, sdx_stream s);
+/* The same with the channels zero-padded to c_out >= c (a 3-channel graph input widened to 8 so that
+ * a tensor-core conv reads it). Session node SDX_OP_CONVERT: misc.aux[0] = c_out, or 0 for c. */
+int sdx_convert_pad(sdx_ctx* ctx, int batch, int c, int c_out, int64_t hw, int x_dtype, int x_layout, int y_dtype,
+                    int y_layout, sdx_dptr x, sdx_dptr y, sdx_stream s);
 
 /* LayerNorm over the last dim (LnP, Ops.LayerNorm src/Kernels/Ops.cs:544-575), fp16 in/out, fp32 w/b. */
 int sdx_layernorm(sdx_ctx* ctx, int64_t rows, int c, float eps, sdx_dptr x, sdx_dptr w, sdx_dptr b, sdx_dptr y,

@@ -56,7 +56,8 @@ class ConvtDesc(ctypes.Structure):
 
 class PoolDesc(ctypes.Structure):
     _fields_ = [(n, _i) for n in ("batch", "ih", "iw", "c", "oh", "ow", "kh", "kw", "sh", "sw", "pad_t", "pad_l",
-                                  "is_avg", "relu", "count_include_pad")] + [("x", _u64), ("y", _u64)]
+                                  "is_avg", "relu", "count_include_pad")] + [("x", _u64), ("y", _u64),
+                                                                              ("x_pix_stride", _i64), ("x_ch_off", _i)]
 
 
 class GateDesc(ctypes.Structure):
@@ -186,6 +187,7 @@ _SIGS = {
     "sdx_binary": (_i, [_p, _i64, _i, _i, _u64, _u64, _u64, _p]),
     "sdx_act": (_i, [_p, _i64, _i, _u64, _u64, _p]),
     "sdx_convert": (_i, [_p, _i, _i, _i64, _i, _i, _i, _i, _u64, _u64, _p]),
+    "sdx_convert_pad": (_i, [_p, _i, _i, _i, _i64, _i, _i, _i, _i, _u64, _u64, _p]),
     "sdx_layernorm": (_i, [_p, _i64, _i, _f, _u64, _u64, _u64, _u64, _p]),
     "sdx_softmax": (_i, [_p, _i64, _i, _i, _u64, _u64, _p]),
     "sdx_attention": (_i, [_p, _i, _i, _i, _i, _f, _u64, _u64, _p]),

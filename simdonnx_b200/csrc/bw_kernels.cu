@@ -249,7 +249,83 @@ __global__ void conv_pool_direct_kernel(DirectArgs a) {
   }
 }
 
+// 1x1 conv to at most 8 outputs over an fp16 NHWC tensor (e.g. a network's final 32 -> 3 projection
+// with the fp32 input image as residual): thread = one pixel, its ic channels read as 16-byte words,
+// oc accumulators (bias first, channels ascending, one FMA each), then the residual in either layout,
+// the activation and oc stores. Weights [ic][oc] and bias staged in shared memory.
+template <int OC>
+__global__ void __launch_bounds__(256) pw_small_kernel(DirectArgs a) {
+  extern __shared__ float sw[];
+  for (int i = threadIdx.x; i < a.ic * OC; i += blockDim.x) sw[i] = __ldg(a.w + i);
+  if (threadIdx.x < OC) sw[a.ic * OC + threadIdx.x] = a.bias ? __ldg(a.bias + threadIdx.x) : 0.0f;
+  __syncthreads();
+  const int64_t hw = (int64_t)a.oh * a.ow, pixels = (int64_t)a.batch * hw;
+  const int c8n = a.ic >> 3;
+  for (int64_t p = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; p < pixels; p += (int64_t)gridDim.x * blockDim.x) {
+    float acc[OC];
+#pragma unroll
+    for (int o = 0; o < OC; o++) acc[o] = sw[a.ic * OC + o];
+    const uint4* xp = reinterpret_cast<const uint4*>(static_cast<const __half*>(a.x) + p * a.ic);
+    for (int c8 = 0; c8 < c8n; c8++) {
+      const uint4 u = __ldg(xp + c8);
+      const __half2* h = reinterpret_cast<const __half2*>(&u);
+      const float* w0 = sw + c8 * 8 * OC;
+#pragma unroll
+      for (int j = 0; j < 4; j++) {
+        const float2 f = __half22float2(h[j]);
+#pragma unroll
+        for (int o = 0; o < OC; o++) acc[o] = fmaf(f.x, w0[(2 * j) * OC + o], acc[o]);
+#pragma unroll
+        for (int o = 0; o < OC; o++) acc[o] = fmaf(f.y, w0[(2 * j + 1) * OC + o], acc[o]);
+      }
+    }
+    const int64_t n = p / hw, r = p - n * hw;
+    if (a.add) {
+#pragma unroll
+      for (int o = 0; o < OC; o++) {
+        const int64_t ro = a.add_nchw ? (n * OC + o) * hw + r : p * OC + o;
+        acc[o] += a.add_f32 ? __ldg(static_cast<const float*>(a.add) + ro)
+                            : __half2float(static_cast<const __half*>(a.add)[ro]);
+      }
+    }
+#pragma unroll
+    for (int o = 0; o < OC; o++) {
+      const float v = act_apply(acc[o], a.act);
+      const int64_t yo = a.y_nchw ? (n * OC + o) * hw + r : p * a.y_pix_stride + a.y_ch_off + o;
+      if (a.y_f32) static_cast<float*>(a.y)[yo] = v;
+      else static_cast<__half*>(a.y)[yo] = __float2half_rn(v);
+    }
+  }
+}
+
+static bool pw_small_ok(const DirectArgs& a) {
+  return a.kh == 1 && a.kw == 1 && a.sh == 1 && a.sw == 1 && a.pt == 0 && a.pl == 0 && !a.pool && !a.x_f32 &&
+         !a.x_nchw && a.ic % 8 == 0 && a.oc >= 1 && a.oc <= 8 && a.ih == a.oh && a.iw == a.ow &&
+         (reinterpret_cast<uintptr_t>(a.x) & 15) == 0 && (size_t)(a.ic + 1) * a.oc * sizeof(float) <= 48 * 1024;
+}
+
+template <int OC>
+static void pw_small_run(const DirectArgs& a, int64_t pixels, cudaStream_t st) {
+  pw_small_kernel<OC><<<grid_for(pixels, 256), 256, sizeof(float) * (size_t)(a.ic + 1) * OC, st>>>(a);
+}
+
 int direct_conv_launch(const DirectArgs& a, cudaStream_t st) {
+  if (pw_small_ok(a)) {
+    const int64_t pixels = (int64_t)a.batch * a.oh * a.ow;
+    if (pixels == 0) return SDX_OK;
+    switch (a.oc) {
+      case 1: pw_small_run<1>(a, pixels, st); break;
+      case 2: pw_small_run<2>(a, pixels, st); break;
+      case 3: pw_small_run<3>(a, pixels, st); break;
+      case 4: pw_small_run<4>(a, pixels, st); break;
+      case 5: pw_small_run<5>(a, pixels, st); break;
+      case 6: pw_small_run<6>(a, pixels, st); break;
+      case 7: pw_small_run<7>(a, pixels, st); break;
+      default: pw_small_run<8>(a, pixels, st); break;
+    }
+    SDX_LAUNCH_CHECK("pw_small");
+    return SDX_OK;
+  }
   const size_t wbytes = sizeof(float) * a.kh * a.kw * a.ic * a.oc;
   if (wbytes > 96 * 1024) return set_error(SDX_ERR_NOT_SUPPORTED, "direct conv: weights exceed the smem stage");
   if (a.pool) {
@@ -437,7 +513,7 @@ __global__ void pool_kernel(PoolArgs a) {
         const int ix = ox * a.sw + kx - a.pl;
         if ((unsigned)ix >= (unsigned)a.iw) continue;
         float v[8];
-        h8_to_f(__ldg(reinterpret_cast<const uint4*>(a.x + (((int64_t)n * a.ih + iy) * a.iw + ix) * a.c + g * 8)), v);
+        h8_to_f(__ldg(reinterpret_cast<const uint4*>(a.x + (((int64_t)n * a.ih + iy) * a.iw + ix) * a.x_ps + a.x_co + g * 8)), v);
         if (a.is_avg) {
 #pragma unroll
           for (int j = 0; j < 8; j++) acc[j] += v[j];
@@ -1018,33 +1094,72 @@ int act_launch(int64_t n, int act, const __half* x, __half* y, cudaStream_t st) 
 }
 
 // fp32 <-> fp16 and NCHW <-> NHWC in one pass. Thread = one element of the output.
-__global__ void convert_kernel(int batch, int c, int64_t hw, int x_f32, int x_nchw, int y_f32, int y_nchw,
+// y[n, ch, p] (layout of y) = x[n, ch, p] for ch < c, 0 for c <= ch < c_out (channel padding of a
+// graph input so that a tensor-core conv can read it: channel counts there are multiples of 8).
+__global__ void convert_kernel(int batch, int c, int c_out, int64_t hw, int x_f32, int x_nchw, int y_f32, int y_nchw,
                                const void* __restrict__ x, void* __restrict__ y) {
-  const int64_t total = (int64_t)batch * c * hw;
+  const int64_t total = (int64_t)batch * c_out * hw;
   for (int64_t idx = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; idx < total;
        idx += (int64_t)gridDim.x * blockDim.x) {
     int64_t n, ch, p;
     if (y_nchw) {
       p = idx % hw;
-      ch = (idx / hw) % c;
-      n = idx / hw / c;
+      ch = (idx / hw) % c_out;
+      n = idx / hw / c_out;
     } else {
-      ch = idx % c;
-      p = (idx / c) % hw;
-      n = idx / c / hw;
+      ch = idx % c_out;
+      p = (idx / c_out) % hw;
+      n = idx / c_out / hw;
     }
-    const int64_t xi = x_nchw ? (n * c + ch) * hw + p : (n * hw + p) * c + ch;
-    const float v = x_f32 ? __ldg(static_cast<const float*>(x) + xi) : __half2float(static_cast<const __half*>(x)[xi]);
+    float v = 0.0f;
+    if (ch < c) {
+      const int64_t xi = x_nchw ? (n * c + ch) * hw + p : (n * hw + p) * c + ch;
+      v = x_f32 ? __ldg(static_cast<const float*>(x) + xi) : __half2float(static_cast<const __half*>(x)[xi]);
+    }
     if (y_f32) static_cast<float*>(y)[idx] = v;
     else static_cast<__half*>(y)[idx] = __float2half_rn(v);
   }
 }
 
-int convert_launch(int batch, int c, int64_t hw, int x_f32, int x_nchw, int y_f32, int y_nchw, const void* x, void* y,
-                   cudaStream_t st) {
-  const int64_t total = (int64_t)batch * c * hw;
+// NCHW (fp32 or fp16) -> NHWC fp16 with c_out a multiple of 8: thread = one pixel's 8 output
+// channels, read plane by plane (coalesced across the warp's pixels), written as one 16-byte word.
+__global__ void convert_nchw_nhwc8_kernel(int batch, int c, int c_out, int64_t hw, int x_f32, const void* __restrict__ x,
+                                          __half* __restrict__ y) {
+  const int g8 = c_out >> 3;
+  const int64_t total = (int64_t)batch * hw * g8;
+  for (int64_t idx = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; idx < total;
+       idx += (int64_t)gridDim.x * blockDim.x) {
+    const int g = (int)(idx % g8);
+    const int64_t q = idx / g8, n = q / hw, p = q - n * hw;
+    uint4 u;
+    __half2* h = reinterpret_cast<__half2*>(&u);
+#pragma unroll
+    for (int j = 0; j < 4; j++) {
+      float v[2];
+#pragma unroll
+      for (int k = 0; k < 2; k++) {
+        const int ch = g * 8 + 2 * j + k;
+        const int64_t xi = (n * c + ch) * hw + p;
+        v[k] = ch >= c ? 0.0f : x_f32 ? __ldg(static_cast<const float*>(x) + xi) : __half2float(static_cast<const __half*>(x)[xi]);
+      }
+      h[j] = __floats2half2_rn(v[0], v[1]);
+    }
+    reinterpret_cast<uint4*>(y)[idx] = u;
+  }
+}
+
+int convert_launch(int batch, int c, int c_out, int64_t hw, int x_f32, int x_nchw, int y_f32, int y_nchw,
+                   const void* x, void* y, cudaStream_t st) {
+  if (c <= 0 || c_out < c) return set_error(SDX_ERR_INVALID, "convert: output channels below input channels");
+  const int64_t total = (int64_t)batch * c_out * hw;
   if (total == 0) return SDX_OK;
-  convert_kernel<<<grid_for(total, 256), 256, 0, st>>>(batch, c, hw, x_f32, x_nchw, y_f32, y_nchw, x, y);
+  if (x_nchw && !y_nchw && !y_f32 && c_out % 8 == 0 && (reinterpret_cast<uintptr_t>(y) & 15) == 0) {
+    convert_nchw_nhwc8_kernel<<<grid_for(total / 8, 256), 256, 0, st>>>(batch, c, c_out, hw, x_f32, x,
+                                                                         static_cast<__half*>(y));
+    SDX_LAUNCH_CHECK("convert_nchw_nhwc8");
+    return SDX_OK;
+  }
+  convert_kernel<<<grid_for(total, 256), 256, 0, st>>>(batch, c, c_out, hw, x_f32, x_nchw, y_f32, y_nchw, x, y);
   SDX_LAUNCH_CHECK("convert");
   return SDX_OK;
 }

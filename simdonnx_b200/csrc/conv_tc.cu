@@ -455,7 +455,10 @@ int tc_launch(const TcProblem& p, cudaStream_t stream) {
                      "tc: fused channel sums need a 1x1 conv with the fp16 TMA-store epilogue, rows % 32 == 0, "
                      "oc 16, 32, 64 or a multiple of 128 and an 8-byte aligned sums buffer");
   if (chain) a.bias_smem = BN + 4 * p.convt_oc + 4;  // first bias, second ConvT's weights and bias
-  const bool eg4 = !p.kxn && 4 * BN <= 512 && (BN <= 64 || chain || (!fast && !kxn_fast));
+  // (96-column tiles of a short reduction, e.g. the largest FPN lateral: 0.75 -> 0.70 ms; with longer
+  // reductions the fewer A stages that four staging groups leave cost more than they save)
+  const bool eg4 = !p.kxn && 4 * BN <= 512 &&
+                   (BN <= 64 || chain || (!fast && !kxn_fast) || (fast && BN <= 96 && p.K <= 64));
   for (int eg = eg4 ? 4 : 2; eg >= 2 && !planned; eg -= 2) {
   a.egroups = eg;
   for (int res = 1; res >= (imgw ? 1 : 0) && !planned; res--) {

@@ -894,6 +894,10 @@ int sdx_pool(sdx_ctx* ctx, const sdx_pool_desc* d, sdx_stream s) {
   a.incl = d->count_include_pad;
   a.x = P<const __half>(d->x);
   a.y = P<__half>(d->y);
+  a.x_ps = d->x_pix_stride > 0 ? d->x_pix_stride : d->c;
+  a.x_co = d->x_ch_off;
+  if (a.x_ps < d->c + d->x_ch_off || a.x_ps % 8 || a.x_co % 8)
+    return set_error(SDX_ERR_INVALID, "pool: input slice stride/offset must be multiples of 8 covering c channels");
   return pool_launch(a, S(ctx, s));
 }
 
@@ -976,8 +980,10 @@ int sdx_concat_channels(sdx_ctx* ctx, int64_t pixels, int nin, const int* counts
   for (int i = 0; i < nin; i++) total += counts[i];
   int off = 0;
   for (int i = 0; i < nin; i++) {
-    int rc = slice_copy_launch(pixels, counts[i], P<const __half>(ins[i]), total, off, P<__half>(y), S(ctx, s));
-    if (rc) return rc;
+    if (ins[i]) {  // 0: the producer wrote this slice in place
+      int rc = slice_copy_launch(pixels, counts[i], P<const __half>(ins[i]), total, off, P<__half>(y), S(ctx, s));
+      if (rc) return rc;
+    }
     off += counts[i];
   }
   return SDX_OK;
@@ -1084,7 +1090,15 @@ int sdx_convert(sdx_ctx* ctx, int batch, int c, int64_t hw, int x_dtype, int x_l
                 sdx_dptr x, sdx_dptr y, sdx_stream s) {
   USE(ctx);
   LAUNCH_GUARD();
-  return convert_launch(batch, c, hw, x_dtype == SDX_F32, x_layout == SDX_NCHW, y_dtype == SDX_F32,
+  return convert_launch(batch, c, c, hw, x_dtype == SDX_F32, x_layout == SDX_NCHW, y_dtype == SDX_F32,
+                        y_layout == SDX_NCHW, P<const void>(x), P<void>(y), S(ctx, s));
+}
+
+int sdx_convert_pad(sdx_ctx* ctx, int batch, int c, int c_out, int64_t hw, int x_dtype, int x_layout, int y_dtype,
+                    int y_layout, sdx_dptr x, sdx_dptr y, sdx_stream s) {
+  USE(ctx);
+  LAUNCH_GUARD();
+  return convert_launch(batch, c, c_out, hw, x_dtype == SDX_F32, x_layout == SDX_NCHW, y_dtype == SDX_F32,
                         y_layout == SDX_NCHW, P<const void>(x), P<void>(y), S(ctx, s));
 }
 

@@ -177,6 +177,8 @@ struct PoolArgs {
   int batch, ih, iw, c, oh, ow, kh, kw, sh, sw, pt, pl, is_avg, relu, incl;
   const __half* x;
   __half* y;
+  int64_t x_ps;  // elements between input pixels (c, or a wider tensor's when x is a channel slice)
+  int x_co;      // first channel of that slice
 };
 int pool_launch(const PoolArgs& a, cudaStream_t st);
 
@@ -228,8 +230,8 @@ int slice_copy_launch(int64_t pixels, int c, const __half* x, int64_t y_pix_stri
                       cudaStream_t st);
 int binary_launch(int64_t n, int op, int relu, const __half* a, const __half* b, __half* y, cudaStream_t st);
 int act_launch(int64_t n, int act, const __half* x, __half* y, cudaStream_t st);
-int convert_launch(int batch, int c, int64_t hw, int x_f32, int x_nchw, int y_f32, int y_nchw, const void* x, void* y,
-                   cudaStream_t st);
+int convert_launch(int batch, int c, int c_out, int64_t hw, int x_f32, int x_nchw, int y_f32, int y_nchw,
+                   const void* x, void* y, cudaStream_t st);
 int layernorm_launch(int64_t rows, int c, float eps, const __half* x, const float* w, const float* b, __half* y,
                      cudaStream_t st);
 int softmax_launch(int64_t rows, int c, int y_f32, const __half* x, void* y, cudaStream_t st);

@@ -129,7 +129,8 @@ static int run_node(sdx_session* s, const sdx_session::Node& n) {
     case SDX_OP_BINARY: return sdx_binary(c, m->n, m->op, m->relu, m->a, m->b, m->y, st);
     case SDX_OP_ACT: return sdx_act(c, m->n, m->act, m->x, m->y, st);
     case SDX_OP_CONVERT:
-      return sdx_convert(c, m->batch, m->c, m->pixels, m->x_dtype, m->x_layout, m->y_dtype, m->y_layout, m->x, m->y, st);
+      return sdx_convert_pad(c, m->batch, m->c, m->aux[0] > 0 ? m->aux[0] : m->c, m->pixels, m->x_dtype, m->x_layout,
+                             m->y_dtype, m->y_layout, m->x, m->y, st);
     case SDX_OP_LAYERNORM: return sdx_layernorm(c, m->rows, m->c, m->eps, m->x, m->w, m->bias, m->y, st);
     case SDX_OP_SOFTMAX: return sdx_softmax(c, m->rows, m->c, m->y_dtype, m->x, m->y, st);
     case SDX_OP_ATTENTION: return sdx_attention(c, m->batch, m->t, m->heads, m->d, m->scale, m->x, m->y, st);

@@ -76,16 +76,29 @@ def cuda_rewrite(plan: ExecPlan) -> ExecPlan:
         out_nodes.append(n)
     P.nodes = out_nodes
 
-    # 1. fp32 NHWC graph input read by a tensor-core conv -> explicit conversion to fp16
+    # 1. fp32 NHWC graph input read by a tensor-core conv -> explicit conversion to fp16; an fp32
+    #    input with fewer than 8 channels (an RGB image) read by a stride-1 k x k conv with 8 or more
+    #    outputs -> conversion to fp16 NHWC zero-padded to 8 channels, the weights padded to match, so
+    #    that the conv runs on the tensor cores instead of the CUDA-core direct kernel
     out_nodes = []
     for n in P.nodes:
         if n.op == "Conv":
             xv = P.values[n.ins[0]]
-            cin = _nhwc_shape(xv)[3]
+            nb, ih, iw, cin = _nhwc_shape(xv)
+            W = P.values[n.ins[1]].const
             if xv.dtype == "f32" and xv.layout == "nhwc" and cin % 8 == 0 and n.p.group == 1 and n.p.strides == (1, 1):
                 h = P.add_value(n.ins[0] + ".f16", xv.shape, "f16", "nhwc")
                 out_nodes.append(Node("Convert", [n.ins[0]], [h], None, h))
                 n.ins[0] = h
+            elif (xv.dtype == "f32" and cin < 8 and n.p.group == 1 and tuple(n.p.strides) == (1, 1) and
+                  n.p.pool is None and W.shape[0] >= 8 and tuple(n.p.kernel) != (1, 1) and
+                  getattr(n.p, "in_scale", None) is None):
+                h = P.add_value(n.ins[0] + ".f16x8", (nb, ih, iw, 8), "f16", "nhwc")
+                out_nodes.append(Node("Convert", [n.ins[0]], [h], None, h))
+                n.ins[0] = h
+                wpad = np.zeros((W.shape[0], 8) + W.shape[2:], np.float32)
+                wpad[:, :cin] = W
+                n.ins[1] = P.add_const(n.ins[1] + "__pad8", wpad)
         out_nodes.append(n)
     P.nodes = out_nodes
 
@@ -148,23 +161,30 @@ def cuda_rewrite(plan: ExecPlan) -> ExecPlan:
         out_nodes.append(n)
     P.nodes = [n for n in out_nodes if id(n) not in drop]
 
-    # 4. channel concat: producers write into their slice
+    # 4. channel concat: producers write into their slice. An input qualifies when a conv (or a
+    #    nearest resize) produces it and its other readers are pools, which read the slice in place
+    #    (sdx_pool_desc.x_pix_stride); the concat node stays for the other inputs only (their
+    #    pointers; an in-place input is passed as 0)
     keep = []
     for n in P.nodes:
-        if n.op == "Concat":
+        if n.op == "Concat" and P.values[n.outs[0]].dtype == "f16" and not P.values[n.outs[0]].alias:
             prods = {o: m for m in P.nodes for o in m.outs}
-            ok = True
+            inplace = []
             for v in n.ins:
                 m = prods.get(v)
-                if (m is None or m.op not in ("Conv", "ResizeNearest") or len(P.consumers(v)) != 1 or
-                        P.values[v].dtype != "f16" or P.shape(v)[3] % 8 != 0):
-                    ok = False
-            if ok:
-                off = 0
-                for v in n.ins:
+                inplace.append(m is not None and (m.op == "ResizeNearest" or (m.op == "Conv" and m.p.group == 1)) and
+                               v != P.output and
+                               P.values[v].dtype == "f16" and P.shape(v)[3] % 8 == 0 and not P.values[v].alias and
+                               n.ins.count(v) == 1 and
+                               all(c is n or c.op in ("MaxPool", "AvgPool") for c in P.consumers(v)))
+            off = 0
+            for v, ok in zip(n.ins, inplace):
+                if ok:
                     P.values[v].alias = (n.outs[0], off)
-                    off += P.shape(v)[3]
+                off += P.shape(v)[3]
+            if all(inplace):
                 continue
+            n.p = tuple(inplace)  # the lowering skips these inputs
         keep.append(n)
     P.nodes = keep
 
@@ -577,9 +597,10 @@ class CudaInferenceSession:
             first = P.shape(n.ins[0])
             d.pixels = int(np.prod(first[:-1]))
             d.nin = len(n.ins)
+            inplace = p if isinstance(p, tuple) else (False,) * len(n.ins)
             for i, v in enumerate(n.ins):
                 d.counts[i] = P.shape(v)[-1]
-                d.ins[i] = self.ptr(v)
+                d.ins[i] = 0 if inplace[i] else self.ptr(v)  # 0: written in place by its producer
             d.y = self.ptr(n.outs[0])
             return N.OP_CONCAT, d
         if op in ("MaxPool", "AvgPool"):
@@ -592,6 +613,9 @@ class CudaInferenceSession:
             d.pad_t, d.pad_l = p.pads[0], p.pads[1]
             d.is_avg, d.relu, d.count_include_pad = int(op == "AvgPool"), int(p.fuse_relu), int(p.count_include_pad)
             d.x, d.y = self.ptr(n.ins[0]), self.ptr(n.outs[0])
+            xs = P.values[n.ins[0]].alias  # the input is a channel slice of a concat (written in place)
+            if xs:
+                d.x_pix_stride, d.x_ch_off = P.shape(xs[0])[3], xs[1]
             return N.OP_POOL, d
         if op == "Gemm" and getattr(p, "ctc", False):
             # CTC head: indices (int32 [rows]) then probabilities (fp32 [rows]) in the output value
@@ -628,8 +652,10 @@ class CudaInferenceSession:
         if op == "Convert":
             xv, yv = P.values[n.ins[0]], P.values[n.outs[0]]
             nb, h, w, c = _nhwc_shape(xv)
+            c_out = _nhwc_shape(yv)[3]
             d = N.MiscDesc()
             d.batch, d.c, d.pixels = nb, c, h * w
+            d.aux[0] = c_out if c_out != c else 0  # zero-padded channels
             d.x_dtype, d.x_layout, d.y_dtype, d.y_layout = _DT[xv.dtype], _LAY[xv.layout], _DT[yv.dtype], _LAY[yv.layout]
             d.x, d.y = self.ptr(n.ins[0]), self.ptr(n.outs[0])
             return N.OP_CONVERT, d

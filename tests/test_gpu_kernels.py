@@ -118,6 +118,34 @@ def test_conv3x3_streamed_weights(be, nb, h, w, ic, oc, residual, act):
     assert be.device_error() == 0
 
 
+@pytest.mark.parametrize("ic,oc,act,res_nchw,res_f32,y_f32", [
+    (32, 3, "none", True, True, True),     # the UNet's final projection + fp32 NCHW input image
+    (64, 5, "relu", False, False, False),  # fp16 NHWC residual, fp16 output
+    (8, 1, "sigmoid", None, None, True),   # no residual
+])
+def test_pointwise_small_outputs(be, ic, oc, act, res_nchw, res_f32, y_f32):
+    """1x1 convs to at most 8 outputs (per-pixel kernel) against the oracle."""
+    from simdonnx_b200 import _native as N, backend as B
+    rng = np.random.default_rng(ic + oc)
+    nb, h, w = 2, 33, 40
+    x = rnd(rng, nb, h, w, ic)
+    wt = rnd(rng, oc, ic, 1, 1, scale=1.0 / np.sqrt(ic))
+    b = rnd(rng, oc)
+    res = None if res_nchw is None else rnd(rng, nb, h, w, oc)
+    ref = O.conv(x, O.ConvPlan(wt, b), act=act, add=res)
+    d = B.conv_desc(nb, h, w, ic, oc, 1, 1, act=act, y_dtype=torch.float32 if y_f32 else torch.float16,
+                    add_dtype=torch.float32 if res_f32 else torch.float16,
+                    add_layout=N.NCHW if res_nchw else N.NHWC)
+    add = None
+    if res is not None:
+        r = np.ascontiguousarray(res.transpose(0, 3, 1, 2)) if res_nchw else res
+        add = dev32(r) if res_f32 else dev16(r)
+    before = int(N.lib().sdx_launch_count())
+    y = B.conv2d(be, d, dev16(x), B.pack_conv(d, wt), bias=dev32(b), add=add)
+    assert int(N.lib().sdx_launch_count()) - before == 1
+    assert_close(host(y), ref, f"pointwise {ic}->{oc}")
+
+
 def test_conv_into_channel_slice(be):
     """Epilogue writing into a channel slice of a wider tensor (fused concat)."""
     from simdonnx_b200 import backend as B
@@ -344,6 +372,23 @@ def test_convert_layouts(be):
     assert_close(host(y).reshape(2, 7, 5, 3), x.transpose(0, 2, 3, 1), "nchw->nhwc")
     z = B.convert(be, y, 2, 3, 35, N.NHWC, torch.float32, N.NCHW)
     assert_close(host(z).reshape(x.shape), x, "roundtrip")
+
+
+@pytest.mark.parametrize("c,c_out,x32", [(3, 8, True), (3, 16, False), (8, 8, True), (5, 8, False)])
+def test_convert_channel_padding(be, c, c_out, x32):
+    """NCHW -> NHWC fp16 zero-padded to c_out channels (sdx_convert_pad): values exact to fp16, pad zero."""
+    import ctypes
+    from simdonnx_b200 import backend as B, _native as N
+    rng = np.random.default_rng(c * c_out)
+    x = rnd(rng, 3, c, 9, 13)
+    xd = dev32(x) if x32 else dev16(x)
+    y = torch.full((3, 9, 13, c_out), 7.0, dtype=torch.float16, device="cuda")
+    N.call("sdx_convert_pad", be.ctx, 3, c, c_out, 9 * 13, N.F32 if x32 else N.F16, N.NCHW, N.F16, N.NHWC,
+           B.ptr(xd), B.ptr(y), B.cur_stream())
+    got = host(y)
+    want = np.zeros((3, 9, 13, c_out), np.float32)
+    want[..., :c] = x.transpose(0, 2, 3, 1).astype(np.float16).astype(np.float32)
+    np.testing.assert_array_equal(got, want)
 
 
 def test_bounded_wait_reports_and_recovers(be):

@@ -66,6 +66,29 @@ def test_det_rewrites():
     assert not any(n.op == "ResizeNearest" and n.outs[0] in ("fpn.p5u", "fpn.p4u", "fpn.p3u") for n in P.nodes)
 
 
+def test_concat_partial_aliasing_with_pool_reader():
+    """UNet skip: a conv output read by a max pool and a concat is written into its concat slice
+    (the pool reads the slice in place); a ConvTranspose input is still copied by the concat node."""
+    from simdonnx_b200.plan import PoolP
+    P = configs.build_unet(batch=1, hw=64)
+    R = cuda_rewrite(P)
+    cats = [n for n in R.nodes if n.op == "Concat"]
+    assert len(cats) == 4
+    for n in cats:
+        skip, up = n.ins[1], n.ins[0]
+        assert n.p == (False, True)
+        assert R.values[skip].alias == (n.outs[0], R.shape(up)[3])
+        assert R.values[up].alias is None
+    pools = [n for n in R.nodes if n.op == "MaxPool"]
+    assert all(R.values[p.ins[0]].alias for p in pools)
+    # the RGB input widened to 8 fp16 channels for the first (tensor-core) conv, weights padded
+    cv = R.nodes[0]
+    assert cv.op == "Convert" and R.values[cv.outs[0]].shape == (1, 64, 64, 8) and R.values[cv.outs[0]].dtype == "f16"
+    c1 = R.nodes[1]
+    assert c1.name == "e0.c1" and c1.ins[0] == cv.outs[0] and R.values[c1.ins[1]].const.shape == (32, 8, 3, 3)
+    assert not R.values[c1.ins[1]].const[:, 3:].any()
+
+
 def test_concat_slice_aliasing_without_upsampling():
     """A Concat of conv outputs is written in place by its producers (slice offsets 0, c0, ...)."""
     b = configs._Builder(3)
