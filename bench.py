@@ -216,6 +216,14 @@ def measure_extras(args, local, N, configs, roofline, torch, CudaInferenceSessio
             rec["conv3x3_tc"] = {"launches": len(convs), "ms": tc_ms, "tflops": tc_fl / tc_ms / 1e9,
                                  "frac_of_sustained_bf16": tc_fl / tc_ms / 1e9 / tc_peak,
                                  "peak_tflops_sustained": tc_peak}
+            # the ones above the ridge (FLOPs per byte > bf16 peak / HBM peak): the tensor-bound set
+            ridge = tc_peak * 1e12 / (hbm * 1e9)
+            tb = [r for r in convs if r["flops"] > ridge * r["bytes"]]
+            tb_ms, tb_fl = sum(r["ms"] for r in tb), sum(r["flops"] for r in tb)
+            if tb_ms > 0:
+                rec["conv3x3_tensor_bound"] = {"launches": len(tb), "ms": tb_ms, "tflops": tb_fl / tb_ms / 1e9,
+                                               "frac_of_sustained_bf16": tb_fl / tb_ms / 1e9 / tc_peak,
+                                               "ridge_flop_per_byte": ridge}
             rec["per_conv"] = [{"node": r["node"], "out": r["out"], "ms": round(r["ms"], 4),
                                 "tflops": round(r["tflops"], 1),
                                 "frac_of_sustained_bf16": round(r["tflops"] / tc_peak, 3)} for r in convs]
