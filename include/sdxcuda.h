@@ -174,6 +174,19 @@ typedef struct sdx_conv_desc {
                         in_scale (per-image two-term weights), else unused */
 } sdx_conv_desc;
 int sdx_conv2d(sdx_ctx* ctx, const sdx_conv_desc* d, sdx_stream s);
+/* Fused depthwise -> pointwise (no reference counterpart; equals the two ConvP nodes it replaces): a
+ * depthwise 3x3 conv, stride 1, pads 1 (`dw`: group == ic == oc, fp16 NHWC, bias, act, in_scale allowed;
+ * its y is not written) whose output only the 1x1 conv `pw` reads (its x is ignored; bias, act and
+ * gap_sums as sdx_conv2d; fp16 output, no residual). The depthwise output is built per 32 x 4 pixel
+ * tile in shared memory and fed to the tensor cores; it never reaches HBM. dw.w: sdx_pack_conv(&dw),
+ * pw.w: sdx_pack_conv(&pw). sdx_dw_pw_supported: 1 when the shapes take this form (64 or 128
+ * channels, at most 128 outputs), else 0; pw.gap_sums further needs ow a multiple of 32 and oh of 4. */
+typedef struct sdx_dwpw_desc {
+  sdx_conv_desc dw, pw;
+} sdx_dwpw_desc;
+int sdx_dw_pw_supported(const sdx_dwpw_desc* d);
+int sdx_dw_pw(sdx_ctx* ctx, const sdx_dwpw_desc* d, sdx_stream s);
+
 /* Bytes of the per-image weight scratch a 1x1 tensor-core conv with in_scale needs (batch two-term
  * copies of its packed weights), or 0 when that form does not apply to the descriptor's shape: it
  * needs fp16 NHWC x, ic % 8 == 0, oc in [8, 128] and ic <= 256. */
@@ -434,7 +447,7 @@ enum sdx_op_kind {
   SDX_OP_CONVERT = 11, SDX_OP_LAYERNORM = 12, SDX_OP_SOFTMAX = 13, SDX_OP_ATTENTION = 14,
   SDX_OP_CONCAT_NEAREST = 15, SDX_OP_IMAGE = 16, SDX_OP_IMAGE_CONV = 17, SDX_OP_CONVT_CHAIN = 18,
   SDX_OP_BINARY_BCAST = 19, SDX_OP_SAFE_DIV = 20, SDX_OP_CHANNEL_SHIFT = 21, SDX_OP_UPHEAD = 22,
-  SDX_OP_MATMUL = 23, SDX_OP_GEMM_ARGMAX = 24
+  SDX_OP_MATMUL = 23, SDX_OP_GEMM_ARGMAX = 24, SDX_OP_DW_PW = 25
 };
 /* Generic argument block for the ops without a descriptor struct. */
 typedef struct sdx_misc_desc {

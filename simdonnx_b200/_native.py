@@ -27,6 +27,7 @@ OP_IMAGE = 16
 OP_IMAGE_CONV = 17
 OP_CONVT_CHAIN = 18
 OP_BINARY_BCAST, OP_SAFE_DIV, OP_CHANNEL_SHIFT, OP_UPHEAD, OP_MATMUL, OP_GEMM_ARGMAX = 19, 20, 21, 22, 23, 24
+OP_DW_PW = 25
 BCAST_MAX_RANK = 6
 
 FAULT_MALLOC, FAULT_LAUNCH, FAULT_GRAPH, FAULT_D2H, FAULT_SYNC = 1, 2, 3, 4, 5
@@ -123,13 +124,17 @@ class GemmArgmaxDesc(ctypes.Structure):
     _fields_ = [("gemm", GemmDesc), ("indices", _u64), ("probs", _u64), ("scratch", _u64)]
 
 
+class DwPwDesc(ctypes.Structure):
+    _fields_ = [("dw", ConvDesc), ("pw", ConvDesc)]
+
+
 DESC_OF_OP = {OP_CONV: ConvDesc, OP_GEMM: GemmDesc, OP_CONVT: ConvtDesc, OP_POOL: PoolDesc,
               OP_CHANNEL_GATE: GateDesc, OP_RESIZE_NEAREST: ResizeDesc, OP_CHANNEL_BROADCAST: MiscDesc,
               OP_CONCAT: MiscDesc, OP_BINARY: MiscDesc, OP_ACT: MiscDesc, OP_CONVERT: MiscDesc,
               OP_LAYERNORM: MiscDesc, OP_SOFTMAX: MiscDesc, OP_ATTENTION: MiscDesc, OP_CONCAT_NEAREST: MiscDesc,
               OP_IMAGE: ImageDesc, OP_IMAGE_CONV: ImageConvDesc, OP_CONVT_CHAIN: ConvtChainDesc,
               OP_BINARY_BCAST: BcastDesc, OP_SAFE_DIV: SafeDivDesc, OP_CHANNEL_SHIFT: ShiftDesc, OP_UPHEAD: UpHeadDesc,
-              OP_MATMUL: MatMulDesc, OP_GEMM_ARGMAX: GemmArgmaxDesc}
+              OP_MATMUL: MatMulDesc, OP_GEMM_ARGMAX: GemmArgmaxDesc, OP_DW_PW: DwPwDesc}
 
 _SIGS = {
     "sdx_abi_version": (_i, []),
@@ -198,6 +203,8 @@ _SIGS = {
     "sdx_matmul": (_i, [_p, ctypes.POINTER(MatMulDesc), _p]),
     "sdx_gemm_argmax_scratch_bytes": (_sz, [_i, _i]),
     "sdx_gemm_argmax": (_i, [_p, ctypes.POINTER(GemmArgmaxDesc), _p]),
+    "sdx_dw_pw_supported": (_i, [ctypes.POINTER(DwPwDesc)]),
+    "sdx_dw_pw": (_i, [_p, ctypes.POINTER(DwPwDesc), _p]),
     "sdx_desc_size": (_sz, [_i]),
     "sdx_session_create": (_i, [_p, _sz, ctypes.POINTER(_p)]),
     "sdx_session_arena": (_i, [_p, ctypes.POINTER(_u64), ctypes.POINTER(_sz)]),

@@ -381,3 +381,23 @@ def gemm_argmax(be: CudaBackend, a, w_packed, n, bias=None):
     d.indices, d.probs, d.scratch = ptr(idx), ptr(prob), ptr(scratch)
     N.call("sdx_gemm_argmax", be.ctx, ctypes.byref(d), cur_stream())
     return idx, prob
+
+
+def dw_pw(be: CudaBackend, dwd: N.ConvDesc, pwd: N.ConvDesc, x, w_dw, b_dw, w_pw, b_pw=None, in_scale=None, gap=None,
+          y=None) -> torch.Tensor:
+    """Fused depthwise 3x3 -> 1x1 conv (sdx_dw_pw): the depthwise output is never stored. w_dw / w_pw
+    packed by pack_conv for their descriptors; gap: fp32 [pixels / 32, oc] channel sums, or None."""
+    if y is None:
+        y = torch.empty((pwd.batch, pwd.oh, pwd.ow, pwd.oc), dtype=torch.float16, device=x.device)
+    d = N.DwPwDesc()
+    d.dw, d.pw = dwd, pwd
+    d.dw.x, d.dw.w, d.dw.bias, d.dw.in_scale = ptr(x), ptr(w_dw), ptr(b_dw), ptr(in_scale)
+    d.pw.w, d.pw.bias, d.pw.y, d.pw.gap_sums = ptr(w_pw), ptr(b_pw), ptr(y), ptr(gap)
+    N.call("sdx_dw_pw", be.ctx, ctypes.byref(d), cur_stream())
+    return y
+
+
+def dw_pw_supported(dwd: N.ConvDesc, pwd: N.ConvDesc) -> bool:
+    d = N.DwPwDesc()
+    d.dw, d.pw = dwd, pwd
+    return bool(N.lib().sdx_dw_pw_supported(ctypes.byref(d)))

@@ -120,11 +120,18 @@ static size_t b_stage_bytes_of(const TcArgs& a) {
 
 static size_t smem_fixed(const TcArgs& a) {
   return 1024 + (size_t)a.egroups * a.nsbuf * a.sbuf_bytes + (((size_t)a.bias_smem * 4 + 15) & ~(size_t)15) +
-         8 * (2 * TC_MAX_STAGES + 10 + 8 * TC_EPI_GROUPS_MAX) + 16 + (a.b_resident ? (size_t)a.b_total_bytes : 0);
+         8 * (2 * TC_MAX_STAGES + 10 + 8 * TC_EPI_GROUPS_MAX) + 16 + (a.b_resident ? (size_t)a.b_total_bytes : 0) +
+         a.dw_extra;
 }
 
 static size_t smem_bytes(const TcArgs& a) {
   return smem_fixed(a) + (size_t)a.stages * (a.a_stage_bytes + b_stage_bytes_of(a));
+}
+
+// end (from the 1024-aligned base) of the kernel's regular shared-memory layout: A stages, weights,
+// staging, bias, barriers; the fused depthwise area follows at the next 1024-byte boundary
+static size_t smem_layout_end(const TcArgs& a) {
+  return smem_bytes(a) - 1024 - a.dw_extra;
 }
 
 int tc_launch(const TcProblem& p, cudaStream_t stream) {
@@ -161,6 +168,12 @@ int tc_launch(const TcProblem& p, cudaStream_t stream) {
                (p.mode == TC_CONV && (p.kh != 1 || p.kw != 1 || p.kxn))))
     return set_error(SDX_ERR_NOT_SUPPORTED,
                      "tc: per-image weights need a 1x1 conv with one N tile, two terms and no fused sums");
+  const bool dwf = p.dw_w != nullptr;
+  if (dwf && (p.mode != TC_CONV || p.kh != 1 || p.kw != 1 || p.kxn || convt || p.chain_w2 || p.arg_m || p.res ||
+              p.fold > 1 || imgw || p.K % 64 != 0 || p.K > 128 || n_tiles != 1 || BN > 128 || p.out_f32 || !p.dw_b))
+    return set_error(SDX_ERR_NOT_SUPPORTED,
+                     "tc: the fused depthwise form needs a 1x1 conv over 64 or 128 channels to at most 128 fp16 "
+                     "outputs, no residual");
   TcArgs a;
   memset(&a, 0, sizeof(a));
   a.mode = p.mode;
@@ -263,6 +276,38 @@ int tc_launch(const TcProblem& p, cudaStream_t stream) {
     uint64_t dims[4] = {(uint64_t)p.C, (uint64_t)p.W, (uint64_t)p.H, (uint64_t)p.batch};
     uint64_t strides[3] = {(uint64_t)p.C * 2, (uint64_t)p.W * p.C * 2, (uint64_t)p.H * p.W * p.C * 2};
     uint32_t box[4] = {(uint32_t)kblk, (uint32_t)BW, (uint32_t)box_h, 1};
+    int rc = encode_map(&mA, p.a, 4, dims, strides, box, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, swizzle_of(kbytes));
+    if (rc) return rc;
+  } else if (dwf) {
+    // fused depthwise: 32 x 4 pixel tiles (a warp's 32 rows are one 32-pixel run of an image row);
+    // tmA is the depthwise input, one {64, 34, 6, 1} halo box per channel block (zero fill = the
+    // depthwise padding); the A blocks are written by the depthwise warps, not by TMA
+    const int BW = 32, BH = TC_BM / BW;
+    a.halo = 0;
+    a.taps = 1;
+    a.kw = 1;
+    a.b_taps = 1;
+    a.BH = BH;
+    a.BW = BW;
+    a.BWs = BW;
+    a.OH = p.OH;
+    a.OW = p.OW;
+    a.tiles_h = (p.OH + BH - 1) / BH;
+    a.tiles_w = (p.OW + BW - 1) / BW;
+    a.m_tiles = p.batch * a.tiles_h * a.tiles_w;
+    a.a_box_bytes = (uint32_t)(TC_BM * kbytes);
+    a.a_blk_bytes = (a.a_box_bytes + 1023u) & ~1023u;
+    a.dw_box_bytes = (uint32_t)((BW + 2) * (BH + 2) * kbytes);
+    a.dw_blk_bytes = (a.dw_box_bytes + 1023u) & ~1023u;
+    a.dw_slot_bytes = a.dw_blk_bytes * (uint32_t)a.kb_per_tap;
+    a.dw_c = p.K;
+    a.dw_w = p.dw_w;
+    a.dw_b = p.dw_b;
+    a.dw_scale = p.dw_scale;
+    a.dw_act = p.dw_act;
+    uint64_t dims[4] = {(uint64_t)p.C, (uint64_t)p.W, (uint64_t)p.H, (uint64_t)p.batch};
+    uint64_t strides[3] = {(uint64_t)p.C * 2, (uint64_t)p.W * p.C * 2, (uint64_t)p.H * p.W * p.C * 2};
+    uint32_t box[4] = {(uint32_t)kblk, (uint32_t)(BW + 2), (uint32_t)(BH + 2), 1};
     int rc = encode_map(&mA, p.a, 4, dims, strides, box, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, swizzle_of(kbytes));
     if (rc) return rc;
   } else if (p.mode == TC_CONV) {
@@ -448,7 +493,10 @@ int tc_launch(const TcProblem& p, cudaStream_t stream) {
     return set_error(SDX_ERR_NOT_SUPPORTED, "tc: upsampled residual needs the fp16 TMA-store epilogue");
   if (p.gap && a.fold > 1 && (!fast || BN != 64 || n_tiles != 1 || a.G != 64 || p.M % 32 != 0))
     return set_error(SDX_ERR_NOT_SUPPORTED, "tc: folded channel sums need one 128-column tile, fast epilogue");
-  if (p.gap && a.fold == 1 && (!fast || p.mode == TC_CONV || convt || p.M % 32 != 0 || p.N % 16 != 0 ||
+  if (dwf && (!fast || (p.gap && (p.OW % 32 != 0 || p.OH % 4 != 0))))
+    return set_error(SDX_ERR_NOT_SUPPORTED, "tc: the fused depthwise form needs the fp16 TMA-store epilogue "
+                                            "(channel sums: width a multiple of 32, height of 4)");
+  if (p.gap && a.fold == 1 && !dwf && (!fast || p.mode == TC_CONV || convt || p.M % 32 != 0 || p.N % 16 != 0 ||
                 (BN != 16 && BN != 32 && BN != 64 && BN != 128) || a.G != (BN < 64 ? BN : 64) ||
                 (reinterpret_cast<uintptr_t>(p.gap) & 7)))
     return set_error(SDX_ERR_NOT_SUPPORTED,
@@ -459,12 +507,19 @@ int tc_launch(const TcProblem& p, cudaStream_t stream) {
   // reductions the fewer A stages that four staging groups leave cost more than they save)
   const bool eg4 = !p.kxn && 4 * BN <= 512 &&
                    (BN <= 64 || chain || (!fast && !kxn_fast) || (fast && BN <= 96 && p.K <= 64));
-  for (int eg = eg4 ? 4 : 2; eg >= 2 && !planned; eg -= 2) {
+  // fused depthwise: two halo slots (the next tile's box lands while this one is consumed), else one
+  for (int slots = dwf ? 2 : 0; slots >= (dwf ? 1 : 0) && !planned; slots--) {
+  if (dwf) {
+    a.dw_slots = slots;
+    a.dw_extra = 1024u + (uint32_t)slots * a.dw_slot_bytes + 40u * (uint32_t)p.K + 64u;
+  }
+  for (int eg = (eg4 && !dwf) ? 4 : 2; eg >= 2 && !planned; eg -= 2) {
   a.egroups = eg;
   for (int res = 1; res >= (imgw ? 1 : 0) && !planned; res--) {
     for (int pass = 0; pass < 2 && !planned; pass++) {
       for (int cps = pass == 0 ? a.kb_per_tap : 1; cps >= 1 && !planned; cps--) {
         if (a.kb_per_tap % cps) continue;
+        if (dwf && (!res || cps != a.kb_per_tap)) continue;  // resident weights, one stage per tile
         for (int nsb = a.tma_out ? 2 : 1; nsb >= 1 && !planned; nsb--) {
           a.b_resident = res;
           a.mpair = (pair_ok && !res) ? 1 : 0;
@@ -475,7 +530,7 @@ int tc_launch(const TcProblem& p, cudaStream_t stream) {
           const size_t per = a.a_stage_bytes + b_stage_bytes_of(a);
           if (fixed >= (size_t)TC_SMEM_LIMIT) continue;
           const int st = (int)std::min<size_t>(TC_MAX_STAGES, ((size_t)TC_SMEM_LIMIT - fixed) / per);
-          if (st >= (pass == 0 ? 3 : (nsb == 2 ? 3 : 2))) {
+          if (st >= (dwf ? 2 : pass == 0 ? 3 : (nsb == 2 ? 3 : 2))) {
             a.stages = st;
             planned = true;
           }
@@ -484,14 +539,21 @@ int tc_launch(const TcProblem& p, cudaStream_t stream) {
     }
   }
   }
+  }
   if (!planned) return set_error(SDX_ERR_NOT_SUPPORTED, "tc: shared memory plan too large");
   if (a.mpair) grid = std::min((a.m_tiles / 2) * n_tiles, num_sms(dev));
-  const size_t smem = smem_bytes(a);
+  size_t smem = smem_bytes(a);
+  if (dwf) {
+    a.dw_off = (uint32_t)((smem_layout_end(a) + 1023) & ~(size_t)1023);
+    smem = 1024 + (size_t)a.dw_off + (size_t)a.dw_slots * a.dw_slot_bytes + 40 * (size_t)p.K + 64;
+  }
   if (smem > (size_t)TC_SMEM_LIMIT) return set_error(SDX_ERR_NOT_SUPPORTED, "tc: shared memory plan too large");
 
   if (total == 0) return SDX_OK;
   int rc = SDX_OK;
-  if (argmax) {
+  if (dwf) {
+    SDX_ACT_DISPATCH(a.act, ACTC, rc = (launch_tc<ACTC, 6, 2>(dev, grid, smem, stream, mA, mB, mOut, mRes, a)));
+  } else if (argmax) {
     rc = a.egroups == 4 ? launch_tc<ACT_NONE, 5, 4>(dev, grid, smem, stream, mA, mB, mOut, mRes, a)
                         : launch_tc<ACT_NONE, 5, 2>(dev, grid, smem, stream, mA, mB, mOut, mRes, a);
   } else if (chain && a.egroups == 4) {

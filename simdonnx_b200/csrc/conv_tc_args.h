@@ -13,6 +13,9 @@ constexpr int TC_BM = 128;
 // hide the per-tile latency of thin tiles); a CTA is the producer warp, the MMA warp and G groups.
 constexpr int TC_EPI_GROUPS_MAX = 4;
 constexpr int tc_threads(int groups) { return 64 + 128 * groups; }
+constexpr int TC_DW_WARPS = 4;  // depthwise warps of the fused depthwise -> pointwise form (EPI = 6): one
+                                // per scheduler, so that the CTA stays within 128 registers a thread
+constexpr int tc_threads_epi(int groups, int epi) { return tc_threads(groups) + (epi == 6 ? 32 * TC_DW_WARPS : 0); }
 constexpr int TC_MAX_STAGES = 8;  // <= 32 (ring slots are tracked in 32-bit masks)
 constexpr int TC_SMEM_LIMIT = 227 * 1024;
 constexpr int TC_BIAS_SMEM_MAX = 4096;  // bias floats staged in shared memory
@@ -107,6 +110,18 @@ struct TcArgs {
   // u % n_tiles) covers m tiles 2 * pair and 2 * pair + 1, whose A boxes share every weight stage
   // (half the weight traffic per MMA); units are strided by the grid, tiles of a unit consecutive
   int mpair;
+  // fused depthwise 3x3 (stride 1, pad 1) in front of a 1x1 conv (kernel template EPI = 6): TC_DW_WARPS
+  // extra warps compute each tile's A block from a TMA-loaded halo box of the depthwise input (tmA:
+  // box {64, BW + 2, BH + 2, 1}, 128-byte swizzle) and write it, swizzled, into the A stage; the
+  // depthwise output never leaves the SM. Shared memory at dw_off: dw_slots halo slots, the [9][C] scaled
+  // weights and [C] bias, four mbarriers (halo full / empty).
+  const float* dw_w;      // [9][C] fp32
+  const float* dw_b;      // [C] fp32
+  const float* dw_scale;  // [batch][C] per-image input scale (an SE gate), or null
+  int dw_act;
+  int dw_c;
+  uint32_t dw_off, dw_slot_bytes, dw_blk_bytes, dw_box_bytes, dw_extra;
+  int dw_slots;           // halo slots: 2, or 1 when two do not fit (128 channels)
   unsigned int* err;
 };
 

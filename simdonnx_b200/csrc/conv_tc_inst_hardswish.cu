@@ -17,4 +17,6 @@ template int launch_tc<ACT_HARDSWISH, 0, 4>(int, int, size_t, cudaStream_t, cons
                                     const CUtensorMap&, const CUtensorMap&, const TcArgs&);
 template int launch_tc<ACT_HARDSWISH, 0, 2>(int, int, size_t, cudaStream_t, const CUtensorMap&, const CUtensorMap&,
                                     const CUtensorMap&, const CUtensorMap&, const TcArgs&);
+template int launch_tc<ACT_HARDSWISH, 6, 2>(int, int, size_t, cudaStream_t, const CUtensorMap&, const CUtensorMap&,
+                                    const CUtensorMap&, const CUtensorMap&, const TcArgs&);
 }  // namespace sdx

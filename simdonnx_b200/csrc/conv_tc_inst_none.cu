@@ -22,4 +22,6 @@ template int launch_tc<ACT_NONE, 5, 4>(int, int, size_t, cudaStream_t, const CUt
                                     const CUtensorMap&, const CUtensorMap&, const TcArgs&);
 template int launch_tc<ACT_NONE, 5, 2>(int, int, size_t, cudaStream_t, const CUtensorMap&, const CUtensorMap&,
                                     const CUtensorMap&, const CUtensorMap&, const TcArgs&);
+template int launch_tc<ACT_NONE, 6, 2>(int, int, size_t, cudaStream_t, const CUtensorMap&, const CUtensorMap&,
+                                    const CUtensorMap&, const CUtensorMap&, const TcArgs&);
 }  // namespace sdx

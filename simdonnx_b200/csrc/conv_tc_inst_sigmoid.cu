@@ -17,4 +17,6 @@ template int launch_tc<ACT_SIGMOID, 0, 4>(int, int, size_t, cudaStream_t, const 
                                     const CUtensorMap&, const CUtensorMap&, const TcArgs&);
 template int launch_tc<ACT_SIGMOID, 0, 2>(int, int, size_t, cudaStream_t, const CUtensorMap&, const CUtensorMap&,
                                     const CUtensorMap&, const CUtensorMap&, const TcArgs&);
+template int launch_tc<ACT_SIGMOID, 6, 2>(int, int, size_t, cudaStream_t, const CUtensorMap&, const CUtensorMap&,
+                                    const CUtensorMap&, const CUtensorMap&, const TcArgs&);
 }  // namespace sdx

@@ -168,6 +168,23 @@ struct TileCoord {
   int img, oy0, ox0, m0, n0;
 };
 
+// Named barrier `id` over `n` threads (a whole number of warps) that also ORs a predicate across them.
+__device__ __forceinline__ bool named_bar_or(int id, int n, bool pred) {
+  uint32_t r;
+  asm volatile(
+      "{\n\t.reg .pred p, q;\n\t"
+      "setp.ne.u32 p, %1, 0;\n\t"
+      "barrier.red.or.pred q, %2, %3, p;\n\t"
+      "selp.u32 %0, 1, 0, q;\n\t}"
+      : "=r"(r)
+      : "r"((uint32_t)pred), "r"(id), "r"(n)
+      : "memory");
+  return r != 0;
+}
+__device__ __forceinline__ void named_bar_sync(int id, int n) {
+  asm volatile("barrier.sync %0, %1;" ::"r"(id), "r"(n) : "memory");
+}
+
 // TMA store (or residual load) of column group g of warp q's 32 tile rows. Tile pixel rows
 // 32q..32q+31 form one box: BW >= 32 gives a run of 32 pixels inside one tile row, BW < 32 gives
 // 32/BW whole tile rows (tile widths are powers of two, so BW divides 32 or 32 divides BW).
@@ -705,12 +722,14 @@ __device__ __forceinline__ void chain_row(const TcArgs& a, uint32_t tbase, const
 }
 
 template <int ACT, int EPI, int G>
-__global__ void __launch_bounds__(tc_threads(G), 1)
+__global__ void __launch_bounds__(tc_threads_epi(G, EPI), 1)
     conv_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
                    const __grid_constant__ CUtensorMap tmOut, const __grid_constant__ CUtensorMap tmRes,
                    const TcArgs a) {
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  constexpr bool DWF = EPI == 6;               // A tiles from the fused depthwise warps
+  constexpr bool FAST = EPI == 1 || EPI == 6;  // the straight-line fp16 TMA-store epilogue
   const int S = a.stages;
   const uint32_t kbytes = (uint32_t)a.kblk * 2;                          // operand row bytes
   const uint32_t b_tap_bytes = (uint32_t)a.BN * kbytes;                  // one tap, one weight term
@@ -746,6 +765,11 @@ __global__ void __launch_bounds__(tc_threads(G), 1)
     for (int i = 0; i < G * 2 * 4; i++) mbar_init(smem_u32(&resb[i]), 1);
     mbar_init(smem_u32(drain), 1);
     mbar_init(smem_u32(bres), 1);
+    if (DWF) {
+      uint64_t* hb = reinterpret_cast<uint64_t*>(smem + a.dw_off + (size_t)a.dw_slots * a.dw_slot_bytes +
+                                                 (size_t)10 * a.dw_c * 4);
+      for (int i = 0; i < 4; i++) mbar_init(smem_u32(&hb[i]), 1);  // halo full [2], halo empty [2]
+    }
     *abort_flag = 0;
     mbar_fence_init();
   }
@@ -822,10 +846,41 @@ __global__ void __launch_bounds__(tc_threads(G), 1)
       uint32_t phase = 0;
       int s_last = -1;          // ring slot and phase of the most recent stage issued
       uint32_t ph_last = 0;
+      uint32_t h_issued[2] = {0, 0};  // fused depthwise: halo boxes issued per slot
+      if (DWF) {
+        // the depthwise input's halo box of every tile (all channel blocks) into dw_slots slots, freed
+        // by the depthwise warps once they have built the tile's A block from it
+        uint64_t* hfull = reinterpret_cast<uint64_t*>(smem + a.dw_off + (size_t)a.dw_slots * a.dw_slot_bytes +
+                                                      (size_t)10 * a.dw_c * 4);
+        uint64_t* hempty = hfull + 2;
+        const int per_img = a.tiles_h * a.tiles_w;
+        int hs = 0;
+        uint32_t hph = 0;
+        for (int tile = t_begin; tile < t_end; tile += t_step) {
+          const int img = tile / per_img;
+          const int r = tile - img * per_img;
+          const int ty = r / a.tiles_w;
+          const int oy0 = ty * a.BH, ox0 = (r - ty * a.tiles_w) * a.BWs;
+          if (!mbar_wait_warp(smem_u32(&hempty[hs]), hph ^ 1u, a.err, SDX_DEV_WAIT_EMPTY, abort_flag)) break;
+          const uint32_t hb = smem_u32(&hfull[hs]);
+          mbar_arrive_expect_tx_p(ld, hb, (uint32_t)a.kb_per_tap * a.dw_box_bytes);
+          const uint32_t dst = smem_u32(smem + a.dw_off) + (uint32_t)hs * a.dw_slot_bytes;
+          for (int cb = 0; cb < a.kb_per_tap; cb++)
+            tma_load_4d_p(ld, dst + (uint32_t)cb * a.dw_blk_bytes, &tmA, hb, cb * a.kblk, ox0 - 1, oy0 - 1, img);
+          h_issued[hs]++;
+          if (++hs == a.dw_slots) {
+            hs = 0;
+            hph ^= 1u;
+          }
+        }
+        for (int q = 0; q < a.dw_slots; q++)
+          if (h_issued[q] > 0) mbar_wait_drain(smem_u32(&hfull[q]), (h_issued[q] - 1) & 1u, a.err, SDX_DEV_WAIT_DRAIN);
+        ok = false;  // the A stages are the depthwise warps'
+      }
       // single-stage tiles with resident weights (pointwise, kx-in-N 3x3, ConvT): the dispatch-free
       // loop; a 4-D box at (ox0 - pad_l, oy0 - pad_t) covers halo mode with one column tap and the
       // one-tap conv mode alike
-      if (kblocks == 1 && a.b_resident && a.cps <= 4 && (a.mode != TC_CONV || a.halo || a.taps == 1) && !imgw) {
+      if (ok && kblocks == 1 && a.b_resident && a.cps <= 4 && (a.mode != TC_CONV || a.halo || a.taps == 1) && !imgw) {
         ProdSingle ps;
         ps.sA = smem_u32(sA);
         ps.a_stage_bytes = a.a_stage_bytes;
@@ -1149,6 +1204,91 @@ __global__ void __launch_bounds__(tc_threads(G), 1)
       mbar_wait_drain(smem_u32(drain), 0, a.err, SDX_DEV_WAIT_DRAIN);
     }
     __syncwarp();
+  } else if (DWF && warp >= 2 + 4 * G) {
+    // fused depthwise: thread (row, part) builds channel part `part` of GEMM row `row` (tile pixel
+    // (row / BW, row % BW)): bias, the nine taps in (ky, kx) order as one FMA each with the per-image
+    // scaled weights, the activation, fp16; written into the 128-byte-swizzled A rows of the stage the
+    // MMA warp released. The halo box rows are 128-byte swizzled the same way.
+    constexpr int NDW = 32 * TC_DW_WARPS, PARTS = NDW / 128;
+    const int t = (int)threadIdx.x - tc_threads(G);
+    const int row = t & 127, part = t >> 7;
+    const int py = row / a.BW, px = row - py * a.BW;
+    const int C = a.dw_c, gper = C / (8 * PARTS);  // 8-channel groups per thread
+    const int HW = a.BW + 2;
+    float* sw = reinterpret_cast<float*>(smem + a.dw_off + (size_t)a.dw_slots * a.dw_slot_bytes);  // [9][C], bias [C]
+    float* sbias = sw + 9 * C;
+    uint64_t* hfull = reinterpret_cast<uint64_t*>(sbias + C);
+    uint64_t* hempty = hfull + 2;
+    for (int i = t; i < C; i += NDW) sbias[i] = __ldg(a.dw_b + i);
+    const int per_img = a.tiles_h * a.tiles_w;
+    int s = 0, hs = 0, cur_img = -1;
+    uint32_t phase = 0, hph = 0;
+    for (int tile = t_begin; tile < t_end; tile += t_step) {
+      const int img = tile / per_img;
+      if (img != cur_img) {
+        // every thread is past its reads of the previous image's weights (barrier at the tile end)
+        for (int i = t; i < 9 * C; i += NDW)
+          sw[i] = __ldg(a.dw_w + i) * (a.dw_scale ? __ldg(a.dw_scale + (int64_t)img * C + i % C) : 1.0f);
+        named_bar_sync(1, NDW);
+        cur_img = img;
+      }
+      bool ok = mbar_wait(smem_u32(&hfull[hs]), hph, a.err, SDX_DEV_WAIT_FULL, abort_flag);
+      ok = ok && mbar_wait(smem_u32(&empty[s]), phase ^ 1u, a.err, SDX_DEV_WAIT_EMPTY, abort_flag);
+      if (named_bar_or(1, NDW, !ok)) break;
+      const uint32_t hbase = smem_u32(smem + a.dw_off) + (uint32_t)hs * a.dw_slot_bytes;
+      const uint32_t abase = smem_u32(sA) + (uint32_t)s * a.a_stage_bytes;
+      for (int gi = 0; gi < gper; gi++) {
+        const int g8 = part * gper + gi;  // 8-channel group: block g8 / 8, 16-byte chunk g8 % 8
+        const int cb = g8 >> 3, ch = g8 & 7, c0 = g8 * 8;
+        float acc[8];
+        {
+          const float4 b0 = *reinterpret_cast<const float4*>(sbias + c0);
+          const float4 b1 = *reinterpret_cast<const float4*>(sbias + c0 + 4);
+          acc[0] = b0.x; acc[1] = b0.y; acc[2] = b0.z; acc[3] = b0.w;
+          acc[4] = b1.x; acc[5] = b1.y; acc[6] = b1.z; acc[7] = b1.w;
+        }
+        const uint32_t hblk = hbase + (uint32_t)cb * a.dw_blk_bytes;
+#pragma unroll
+        for (int ky = 0; ky < 3; ky++)
+#pragma unroll
+          for (int kx = 0; kx < 3; kx++) {
+            const uint32_t pix = (uint32_t)((py + ky) * HW + px + kx);
+            uint4 u;
+            lds16(hblk + pix * 128u + (((uint32_t)ch ^ (pix & 7u)) << 4), u);
+            const __half2* h2 = reinterpret_cast<const __half2*>(&u);
+            const float* wp = sw + (ky * 3 + kx) * C + c0;
+            const float4 w0 = *reinterpret_cast<const float4*>(wp);
+            const float4 w1 = *reinterpret_cast<const float4*>(wp + 4);
+            const float wv[8] = {w0.x, w0.y, w0.z, w0.w, w1.x, w1.y, w1.z, w1.w};
+#pragma unroll
+            for (int j = 0; j < 4; j++) {
+              const float2 f = __half22float2(h2[j]);
+              acc[2 * j] = fmaf(f.x, wv[2 * j], acc[2 * j]);
+              acc[2 * j + 1] = fmaf(f.y, wv[2 * j + 1], acc[2 * j + 1]);
+            }
+          }
+        uint4 o;
+        __half2* oh = reinterpret_cast<__half2*>(&o);
+#pragma unroll
+        for (int j = 0; j < 4; j++)
+          oh[j] = __floats2half2_rn(act_apply(acc[2 * j], a.dw_act), act_apply(acc[2 * j + 1], a.dw_act));
+        sts16(abase + (uint32_t)cb * a.a_blk_bytes + (uint32_t)row * 128u + (((uint32_t)ch ^ ((uint32_t)row & 7u)) << 4), o);
+      }
+      fence_async_smem();  // the generic-proxy A writes, before the MMAs (async proxy) read them
+      named_bar_sync(1, NDW);
+      if (t == 0) {
+        mbar_arrive(smem_u32(&full[s]));
+        mbar_arrive(smem_u32(&hempty[hs]));
+      }
+      if (++s == S) {
+        s = 0;
+        phase ^= 1u;
+      }
+      if (++hs == a.dw_slots) {
+        hs = 0;
+        hph ^= 1u;
+      }
+    }
   } else {
     // epilogue: group e (warps 2+4e .. 5+4e) takes the tiles lt = e, e+G, ... of this CTA (G groups); warp q
     // reads TMEM lanes 32q..32q+31 (the lane quadrant it may access), i.e. tile rows 32q..32q+31
@@ -1225,7 +1365,7 @@ __global__ void __launch_bounds__(tc_threads(G), 1)
       // thread copies its row's residual into its staging row (cp.async, the staging swizzle) before
       // waiting for the accumulator, so the loads overlap the wait; the chunks read it from smem
       bool res_smem = a.tma_res != 0;
-      if (EPI == 1 && a.res && !a.tma_res) {
+      if (FAST && a.res && !a.tma_res) {
         int64_t rpix = -1;
         if (a.mode == TC_CONV) {
           const int oy = tcd.oy0 + row_in_tile / a.BW, ox = tcd.ox0 + row_in_tile % a.BW;
@@ -1266,7 +1406,7 @@ __global__ void __launch_bounds__(tc_threads(G), 1)
           res_pending = false;
         }
       }
-      if (EPI == 1 && a.res && !a.tma_res) cp_async_wait_all();
+      if (FAST && a.res && !a.tma_res) cp_async_wait_all();
       if (!ok) break;
       __syncwarp();
       tc_fence_after();
@@ -1474,7 +1614,14 @@ __global__ void __launch_bounds__(tc_threads(G), 1)
       // channel sums of this warp's 32 rows (rows mode): its row of a.gap, warp-uniform
       float* gp = nullptr;
       int nlim = 0;
-      if (EPI == 1 && a.gap) {
+      if (DWF && a.gap) {
+        // 32-pixel tile rows (BW = 32, OW a multiple of 32): the warp's rows are one 32-pixel run
+        const int oy = tcd.oy0 + q;
+        if (oy < a.OH) {
+          gp = a.gap + ((((int64_t)tcd.img * a.OH + oy) * a.OW + tcd.ox0) >> 5) * a.N + tcd.n0;
+          nlim = a.N - tcd.n0;
+        }
+      } else if (FAST && a.gap) {
         const int64_t r0 = (int64_t)tcd.m0 + q * 32;
         if (r0 < a.M) {
           if (a.fold > 1) {
@@ -1486,7 +1633,7 @@ __global__ void __launch_bounds__(tc_threads(G), 1)
           }
         }
       }
-      if (EPI == 1 && nch <= 2) {
+      if (FAST && nch <= 2) {
         // thin tiles: both chunks' TMEM loads in flight under one wait, the accumulator handed
         // back before any arithmetic
         float v0[16], v1[16];
@@ -1513,7 +1660,7 @@ __global__ void __launch_bounds__(tc_threads(G), 1)
           tc_fence_before();
           mbar_arrive(smem_u32(&acce[acc]));
         }
-        if (EPI == 1) epi_chunk_fast<ACT>(a, va, c, srow, xr, sBias + tcd.n0, res_smem);
+        if (FAST) epi_chunk_fast<ACT>(a, va, c, srow, xr, sBias + tcd.n0, res_smem);
         else epi_chunk<ACT>(a, va, c, srow, xr, sBias, tcd, valid, pix, g, cg);
         if (c + 1 < nch) {
           tmem_wait_ld();
@@ -1524,7 +1671,7 @@ __global__ void __launch_bounds__(tc_threads(G), 1)
             tc_fence_before();
             mbar_arrive(smem_u32(&acce[acc]));
           }
-          if (EPI == 1) epi_chunk_fast<ACT>(a, vb, c + 1, srow, xr, sBias + tcd.n0, res_smem);
+          if (FAST) epi_chunk_fast<ACT>(a, vb, c + 1, srow, xr, sBias + tcd.n0, res_smem);
           else epi_chunk<ACT>(a, vb, c + 1, srow, xr, sBias, tcd, valid, pix, g, cg);
         }
       }
@@ -1538,10 +1685,10 @@ __global__ void __launch_bounds__(tc_threads(G), 1)
           for (int gg = 0; gg < ng; gg++) warp_copy(eld, a, &tmOut, slab + gg * a.group_bytes, gg, q, tcd, false, 0);
           bulk_commit(eld);
           // channel sums of the staged rows (read alongside the store's own reads of them)
-          if (EPI == 1 && gp && a.fold > 1) {
+          if (FAST && gp && a.fold > 1) {
             if (a.fold == 4) gap_warp_rows_fold<4, 16, 1>(slab, a.group_bytes, lane, gp);
             else gap_warp_rows_fold<2, 32, 1>(slab, a.group_bytes, lane, gp);
-          } else if (EPI == 1 && gp) {
+          } else if (FAST && gp) {
             if (a.BN == 16) gap_warp_rows<16>(slab, a.group_bytes, lane, gp, nlim);
             else if (a.BN == 32) gap_warp_rows<32>(slab, a.group_bytes, lane, gp, nlim);
             else if (a.BN == 64) gap_warp_rows<64>(slab, a.group_bytes, lane, gp, nlim);
@@ -1584,7 +1731,7 @@ int launch_tc(int dev, int grid, size_t smem, cudaStream_t stream, const CUtenso
   const int rc = raise_smem_limit(attr, (const void*)conv_tc_kernel<ACT, EPI, G>, TC_SMEM_LIMIT,
                                   "cudaFuncSetAttribute(conv_tc)");
   if (rc) return rc;
-  conv_tc_kernel<ACT, EPI, G><<<grid, tc_threads(G), smem, stream>>>(mA, mB, mOut, mRes, a);
+  conv_tc_kernel<ACT, EPI, G><<<grid, tc_threads_epi(G, EPI), smem, stream>>>(mA, mB, mOut, mRes, a);
   cudaError_t e = cudaGetLastError();
   if (e != cudaSuccess) return set_cuda_error(e, "conv_tc launch");
   return SDX_OK;

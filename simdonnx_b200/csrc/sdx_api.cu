@@ -577,6 +577,64 @@ size_t sdx_conv_scaled_weights_bytes(const sdx_conv_desc* d) {
 // =========================================================================================
 // ops
 // =========================================================================================
+int sdx_dw_pw_supported(const sdx_dwpw_desc* d) {
+  if (!d) return 0;
+  const sdx_conv_desc& w = d->dw;
+  const sdx_conv_desc& p = d->pw;
+  const bool dw_ok = conv_route(&w) == R_DEPTHWISE && w.kh == 3 && w.kw == 3 && w.sh == 1 && w.sw == 1 &&
+                     w.pad_t == 1 && w.pad_l == 1 && w.pad_b == 1 && w.pad_r == 1 && w.x_dtype == SDX_F16 &&
+                     w.x_layout == SDX_NHWC && w.y_dtype == SDX_F16 && w.pool == 0 && (w.ic == 64 || w.ic == 128);
+  const int64_t ystride = p.y_pix_stride > 0 ? p.y_pix_stride : p.oc;
+  const bool pw_ok = conv_route(&p) == R_TC_ROWS && p.in_scale == 0 && p.ic == w.oc && p.batch == w.batch &&
+                     p.ih == w.oh && p.iw == w.ow && p.oc <= 128 && p.y_dtype == SDX_F16 && p.add_up == 0 &&
+                     ystride % 8 == 0 && p.y_ch_off % 8 == 0 && (p.oc % 16 == 0);
+  return dw_ok && pw_ok ? 1 : 0;
+}
+
+int sdx_dw_pw(sdx_ctx* ctx, const sdx_dwpw_desc* d, sdx_stream s) {
+  USE(ctx);
+  if (!d) return set_error(SDX_ERR_INVALID, "null desc");
+  LAUNCH_GUARD();
+  if (!sdx_dw_pw_supported(d))
+    return set_error(SDX_ERR_NOT_SUPPORTED, "dw+pw: needs a 3x3 s1 depthwise over 64 or 128 fp16 channels and a 1x1 "
+                                            "conv to at most 128 fp16 outputs (multiples of 16)");
+  if (d->pw.add || d->dw.add) return set_error(SDX_ERR_NOT_SUPPORTED, "dw+pw: no residuals");
+  if (!d->dw.bias) return set_error(SDX_ERR_INVALID, "dw+pw: depthwise bias required (zeros when absent)");
+  const sdx_conv_desc& w = d->dw;
+  const sdx_conv_desc& pw = d->pw;
+  TcProblem p;
+  memset(&p, 0, sizeof(p));
+  p.mode = TC_CONV;
+  p.a = P<const __half>(w.x);
+  p.lda = w.ic;
+  p.M = w.batch * w.oh * w.ow;
+  p.K = w.ic;
+  p.batch = w.batch;
+  p.H = w.ih;
+  p.W = w.iw;
+  p.C = w.ic;
+  p.OH = w.oh;
+  p.OW = w.ow;
+  p.kh = 1;
+  p.kw = 1;
+  p.w = P<const __half>(pw.w);
+  p.wterms = conv_wterms(&pw);
+  p.N = pw.oc;
+  p.bias = P<const float>(pw.bias);
+  p.out = P<void>(pw.y);
+  p.out_f32 = 0;
+  p.out_pix_stride = pw.y_pix_stride > 0 ? pw.y_pix_stride : pw.oc;
+  p.out_ch_off = pw.y_ch_off;
+  p.act = pw.act;
+  p.gap = P<float>(pw.gap_sums);
+  p.err = ctx->err_word;
+  p.dw_w = P<const float>(w.w);
+  p.dw_b = P<const float>(w.bias);
+  p.dw_scale = P<const float>(w.in_scale);
+  p.dw_act = w.act;
+  return tc_launch(p, S(ctx, s));
+}
+
 int sdx_conv2d(sdx_ctx* ctx, const sdx_conv_desc* d, sdx_stream s) {
   USE(ctx);
   if (!d) return set_error(SDX_ERR_INVALID, "null desc");

@@ -84,6 +84,14 @@ struct TcProblem {
   // sets of the packed layout, image i's GEMM rows being [i * img_rows, (i + 1) * img_rows) with
   // img_rows a multiple of 128; 0 = one weight set for every row
   int img_rows;
+  // fused depthwise 3x3 stride 1 pad 1 in front of this 1x1 conv (TC_CONV mode, kh = kw = 1): `a` is the
+  // depthwise input [batch, H, W, C] (fp16 NHWC, C a multiple of 64, at most 128), dw_w [9][C] and
+  // dw_b [C] its weights and bias, dw_scale [batch][C] a per-image input scale or null, dw_act its
+  // activation; the depthwise output is built per tile in shared memory and never stored
+  const float* dw_w;
+  const float* dw_b;
+  const float* dw_scale;
+  int dw_act;
   void* out;
   int out_f32;
   int64_t out_pix_stride;

@@ -103,6 +103,7 @@ static size_t desc_size(int kind) {
     case SDX_OP_UPHEAD: return sizeof(sdx_uphead_desc);
     case SDX_OP_MATMUL: return sizeof(sdx_matmul_desc);
     case SDX_OP_GEMM_ARGMAX: return sizeof(sdx_gemm_argmax_desc);
+    case SDX_OP_DW_PW: return sizeof(sdx_dwpw_desc);
     default: return 0;
   }
 }
@@ -140,6 +141,7 @@ static int run_node(sdx_session* s, const sdx_session::Node& n) {
     case SDX_OP_UPHEAD: return sdx_uphead(c, static_cast<const sdx_uphead_desc*>(d), st);
     case SDX_OP_MATMUL: return sdx_matmul(c, static_cast<const sdx_matmul_desc*>(d), st);
     case SDX_OP_GEMM_ARGMAX: return sdx_gemm_argmax(c, static_cast<const sdx_gemm_argmax_desc*>(d), st);
+    case SDX_OP_DW_PW: return sdx_dw_pw(c, static_cast<const sdx_dwpw_desc*>(d), st);
     default: return set_error(SDX_ERR_INVALID, "unknown op kind %d", n.kind);
   }
 }

@@ -265,6 +265,8 @@ class ExecPlan:
 
 def _param_refs(p) -> list:
     """Value ids read through op params (ExecNode.ParamRefs, src/Engine/ExecPlan.cs:246-262)."""
+    if isinstance(p, tuple):  # fused nodes carry the params of the nodes they replace
+        return [v for q in p for v in _param_refs(q)]
     refs = []
     for attr in ("bias", "add", "b1", "b2", "in_scale", "gamma", "beta", "mean", "var"):
         v = getattr(p, attr, None)

@@ -75,6 +75,20 @@ def node_cost(plan: ExecPlan, n) -> tuple:
         flops = 2 * nb * ih * iw * ic * oc * kh * kw
         byt = _nb(plan, n.ins[0]) + W.size * (2 if oc >= 8 else 4) + 4 * oc + _nb(plan, out)
         return cls, flops, byt
+    if op == "DwPw":
+        # depthwise 3x3 + 1x1 with the depthwise output kept on chip: input, weights, output (+ sums)
+        pd, pp, (oh, ow) = p
+        nb, ih, iw, c = _nhwc(plan, n.ins[0])
+        Wd, Wp = plan.values[n.ins[1]].const, plan.values[n.ins[2]].const
+        oc = Wp.shape[0]
+        flops = 2 * nb * oh * ow * c * Wd.shape[2] * Wd.shape[3] + 2 * nb * oh * ow * oc * c
+        byt = _nb(plan, n.ins[0]) + Wd.size * 4 + 4 * c + Wp.size * 2 + (4 * oc if pp.bias else 0) + _nb(plan, out)
+        sc = getattr(pd, "in_scale", None)
+        if sc:
+            byt += _nb(plan, sc)
+        for o in n.outs[1:]:
+            byt += _nb(plan, o)
+        return "dw_pw", flops, byt
     if op == "ConvTChain":
         # two ConvTs with the intermediate kept on chip: traffic = input, weights, final output
         nb, ih, iw, ic = plan.values[n.ins[0]].shape

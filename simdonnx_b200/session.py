@@ -286,7 +286,38 @@ def cuda_rewrite(plan: ExecPlan) -> ExecPlan:
         m.outs.append(sums)
         n.ins.append(sums)
 
-    # 9. scratch of the per-image scaled weights of the 1x1 convs that read x * s (step 2): an extra
+    # 9. depthwise 3x3 (stride 1) whose output only a 1x1 tensor-core conv reads -> one DwPw node
+    #    (sdx_dw_pw: the depthwise output is built tile by tile in shared memory, never stored)
+    prods = {o: m for m in P.nodes for o in m.outs}
+    fused, drop = {}, set()
+    for n in P.nodes:
+        if n.op != "Conv" or n.p.group != 1 or getattr(n.p, "in_scale", None) is not None:
+            continue
+        d = prods.get(n.ins[0])
+        if (d is None or d.op != "Conv" or d.p.group == 1 or len(P.consumers(n.ins[0])) != 1 or
+                n.ins[0] == P.output or P.values[n.ins[0]].alias or d.p.add or n.p.add or n.p.pool is not None or
+                getattr(n.p, "add_up", 0) or P.values[n.outs[0]].alias):
+            continue
+        if not _dw_pw_ok(P, d, n):
+            continue
+        outs = list(n.outs)
+        oh, ow = P.values[d.outs[0]].shape[1:3]
+        if len(outs) > 1 and (ow % 32 or oh % 4):
+            # the fused form's channel sums need whole 32-pixel runs per tile row: the gate reads the
+            # tensor instead (step 8's sums dropped)
+            sums = outs.pop()
+            for g in P.consumers(sums):
+                g.ins.remove(sums)
+            del P.values[sums]
+        fused[id(n)] = Node("DwPw", [d.ins[0], d.ins[1], n.ins[1]], outs, (d.p, n.p, (oh, ow)), n.name)
+        drop.add(id(d))
+    if fused:
+        for n in P.nodes:
+            if id(n) in drop:
+                del P.values[n.outs[0]]  # the depthwise output is never stored
+        P.nodes = [fused.get(id(n), n) for n in P.nodes if id(n) not in drop]
+
+    # 10. scratch of the per-image scaled weights of the 1x1 convs that read x * s (step 2): an extra
     #    output of the conv, live for that node only
     for n in P.nodes:
         if n.op == "Conv" and n.p.group == 1 and getattr(n.p, "in_scale", None) is not None:
@@ -296,6 +327,30 @@ def cuda_rewrite(plan: ExecPlan) -> ExecPlan:
             n.outs.append(w)
             n.p.w_scaled = w
     return P
+
+
+def _dw_pw_descs(P: ExecPlan, x: str, dp, pp, oc: int, mid_hw: tuple, out: str):
+    """(depthwise desc, 1x1 desc) of a depthwise conv (params dp) over `x` feeding a 1x1 conv (params pp,
+    oc outputs) that writes `out`; shape and layout fields only."""
+    nb, ih, iw, c = _nhwc_shape(P.values[x])
+    oh, ow = mid_hw
+    k = dp.kernel
+    dwd = B.conv_desc(nb, ih, iw, c, c, k[0], k[1], stride=dp.strides, pads=dp.pads, group=c, act=dp.act)
+    if getattr(dp, "in_scale", None) is not None:
+        dwd.in_scale = 1  # set: the support query reads whether it is
+    yslice = P.values[out].alias
+    pwd = B.conv_desc(nb, oh, ow, c, oc, 1, 1, act=pp.act,
+                      y_pix_stride=P.shape(yslice[0])[3] if yslice else 0, y_ch_off=yslice[1] if yslice else 0)
+    return dwd, pwd
+
+
+def _dw_pw_ok(P: ExecPlan, d: Node, n: Node) -> bool:
+    xv, mv, yv = P.values[d.ins[0]], P.values[d.outs[0]], P.values[n.outs[0]]
+    if xv.dtype != "f16" or xv.layout != "nhwc" or mv.dtype != "f16" or yv.dtype != "f16" or yv.layout != "nhwc":
+        return False
+    oc = P.values[n.ins[1]].const.shape[0]
+    dwd, pwd = _dw_pw_descs(P, d.ins[0], d.p, n.p, oc, mv.shape[1:3], n.outs[0])
+    return B.dw_pw_supported(dwd, pwd)
 
 
 def _scaled_rows_bytes(P: ExecPlan, c: Node, x: str) -> int:
@@ -412,6 +467,23 @@ class CudaInferenceSession:
             d.gap_sums = self.ptr(sums[0]) if sums else 0
             d.w_scaled = self.ptr(wsc) if wsc else 0
             return N.OP_CONV, d
+        if op == "DwPw":
+            pd, pp, mid_hw = p
+            Wd, Wp = P.values[n.ins[1]].const, P.values[n.ins[2]].const
+            dwd, pwd = _dw_pw_descs(P, n.ins[0], pd, pp, Wp.shape[0], mid_hw, n.outs[0])
+            wd = self._const_dev(("dww", n.name), lambda: B.pack_conv(dwd, Wd, self.device))
+            wp = self._const_dev(("pww", n.name), lambda: B.pack_conv(pwd, Wp, self.device))
+            d = N.DwPwDesc()
+            d.dw, d.pw = dwd, pwd
+            d.dw.x, d.dw.w = self.ptr(n.ins[0]), B.ptr(wd)
+            d.dw.bias = self._f32(pd.bias) if pd.bias else self._zeros(dwd.oc)
+            scale = getattr(pd, "in_scale", None)
+            d.dw.in_scale = self.ptr(scale) if scale else 0
+            d.pw.w = B.ptr(wp)
+            d.pw.bias = self._f32(pp.bias) if pp.bias else 0
+            d.pw.y = self.ptr(n.outs[0])
+            d.pw.gap_sums = self.ptr(n.outs[1]) if len(n.outs) > 1 else 0
+            return N.OP_DW_PW, d
         if op == "ConvTranspose":
             xv, yv = P.values[n.ins[0]], P.values[n.outs[0]]
             nb, ih, iw, ic = xv.shape

@@ -146,6 +146,44 @@ def test_pointwise_small_outputs(be, ic, oc, act, res_nchw, res_f32, y_f32):
     assert_close(host(y), ref, f"pointwise {ic}->{oc}")
 
 
+@pytest.mark.parametrize("nb,h,w,c,oc,scale,gap", [
+    (3, 16, 64, 64, 64, True, True),     # the det b3 block's shape class, SE scale in, SE sums out
+    (2, 20, 32, 128, 128, True, True),   # b5: 128 channels (two channel blocks)
+    (2, 13, 40, 64, 96, False, False),   # ragged tiles: 40 columns, 13 rows
+    (2, 160, 160, 64, 64, True, True),   # b3 at full resolution
+])
+def test_depthwise_pointwise_fused(be, nb, h, w, c, oc, scale, gap):
+    """Depthwise 3x3 (+hardswish, per-image input scale) computed tile by tile in shared memory and fed
+    to the 1x1 tensor-core conv (sdx_dw_pw) against the oracle's two convs; the fused channel sums
+    against sums of the output."""
+    from simdonnx_b200 import backend as B
+    rng = np.random.default_rng(nb * 100 + c + oc)
+    x = rnd(rng, nb, h, w, c)
+    sc = rng.uniform(0.2, 1, size=(nb, c)).astype(np.float32) if scale else None
+    wdw = rnd(rng, c, 1, 3, 3, scale=0.4)
+    bdw = rnd(rng, c)
+    wpw = rnd(rng, oc, c, 1, 1, scale=1.0 / np.sqrt(c))
+    bpw = rnd(rng, oc)
+    xin = O.channel_broadcast(x, sc) if scale else x
+    mid = O.conv(xin, O.ConvPlan(wdw, bdw, group=c), pads=(1, 1, 1, 1), act="hardswish")
+    mid = mid.astype(np.float16).astype(np.float32)  # the depthwise output is fp16 (as when stored)
+    ref = O.conv(mid, O.ConvPlan(wpw, bpw), act="hardswish")
+    dwd = B.conv_desc(nb, h, w, c, c, 3, 3, pads=(1, 1, 1, 1), group=c, act="hardswish")
+    pwd = B.conv_desc(nb, h, w, c, oc, 1, 1, act="hardswish")
+    if scale:
+        dwd.in_scale = 1
+    assert B.dw_pw_supported(dwd, pwd)
+    g = torch.zeros((nb * h * w // 32, oc), dtype=torch.float32, device="cuda") if gap else None
+    y = B.dw_pw(be, dwd, pwd, dev16(x), B.pack_conv(dwd, wdw), dev32(bdw), B.pack_conv(pwd, wpw), dev32(bpw),
+                in_scale=dev32(sc) if scale else None, gap=g)
+    got = host(y)
+    assert_close(got, ref, f"dw+pw {nb}x{h}x{w} {c}->{oc}")
+    assert be.device_error() == 0
+    if gap:
+        want = got.reshape(nb * h * w // 32, 32, oc).sum(axis=1)
+        np.testing.assert_allclose(host(g), want, rtol=2e-3, atol=2e-2)
+
+
 def test_conv_into_channel_slice(be):
     """Epilogue writing into a channel slice of a wider tensor (fused concat)."""
     from simdonnx_b200 import backend as B
