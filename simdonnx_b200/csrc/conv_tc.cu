@@ -542,6 +542,11 @@ int tc_launch(const TcProblem& p, cudaStream_t stream) {
   }
   if (!planned) return set_error(SDX_ERR_NOT_SUPPORTED, "tc: shared memory plan too large");
   if (a.mpair) grid = std::min((a.m_tiles / 2) * n_tiles, num_sms(dev));
+  if (dwf && total > 0) {
+    a.contig = 1;
+    a.per_cta = (total + grid - 1) / grid;
+    grid = (total + a.per_cta - 1) / a.per_cta;
+  }
   size_t smem = smem_bytes(a);
   if (dwf) {
     a.dw_off = (uint32_t)((smem_layout_end(a) + 1023) & ~(size_t)1023);

@@ -122,6 +122,8 @@ struct TcArgs {
   int dw_c;
   uint32_t dw_off, dw_slot_bytes, dw_blk_bytes, dw_box_bytes, dw_extra;
   int dw_slots;           // halo slots: 2, or 1 when two do not fit (128 channels)
+  int contig;             // 1: each CTA runs the contiguous tile range [blockIdx.x * per_cta, + per_cta)
+                          // (the fused depthwise form: per-image weights change rarely)
   unsigned int* err;
 };
 

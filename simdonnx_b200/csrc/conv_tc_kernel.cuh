@@ -802,9 +802,10 @@ __global__ void __launch_bounds__(tc_threads_epi(G, EPI), 1)
   const int total_tiles = a.m_tiles * a.n_tiles;
   // this CTA's tiles: strided by the grid, or a contiguous range (per-image weights)
   const bool imgw = a.img_tiles > 0;
-  const int t_begin = imgw ? (int)blockIdx.x * a.per_cta : (int)blockIdx.x;
-  const int t_end = imgw ? min(total_tiles, t_begin + a.per_cta) : total_tiles;
-  const int t_step = imgw ? 1 : (int)gridDim.x;
+  const bool contig = imgw || a.contig;
+  const int t_begin = contig ? (int)blockIdx.x * a.per_cta : (int)blockIdx.x;
+  const int t_end = contig ? min(total_tiles, t_begin + a.per_cta) : total_tiles;
+  const int t_step = contig ? 1 : (int)gridDim.x;
   // pipeline stages per tile: (tap, channel block), or (kx, channel block) in halo mode
   const int groups = a.kb_per_tap / a.cps;  // channel-block groups per tap
   const int kblocks = (a.halo ? a.kw : a.taps) * groups;
@@ -1082,17 +1083,17 @@ __global__ void __launch_bounds__(tc_threads_epi(G, EPI), 1)
         m.nt0 = (int)(blockIdx.x % (unsigned)a.n_tiles);
         const int tt = a.m_tiles * a.n_tiles;
         if (a.b_taps == 3) {
-          if (nk == 1) mma_single_cps<3, 1, false>(a.cps, ld, m, blockIdx.x, tt, gridDim.x, full, empty, accf, acce, a.err, abort_flag);
-          else if (nk == 2) mma_single_cps<3, 2, false>(a.cps, ld, m, blockIdx.x, tt, gridDim.x, full, empty, accf, acce, a.err, abort_flag);
-          else mma_single_cps<3, 4, false>(a.cps, ld, m, blockIdx.x, tt, gridDim.x, full, empty, accf, acce, a.err, abort_flag);
+          if (nk == 1) mma_single_cps<3, 1, false>(a.cps, ld, m, t_begin, t_end, t_step, full, empty, accf, acce, a.err, abort_flag);
+          else if (nk == 2) mma_single_cps<3, 2, false>(a.cps, ld, m, t_begin, t_end, t_step, full, empty, accf, acce, a.err, abort_flag);
+          else mma_single_cps<3, 4, false>(a.cps, ld, m, t_begin, t_end, t_step, full, empty, accf, acce, a.err, abort_flag);
         } else if (a.wterms == 2) {
-          if (nk == 1) mma_single_cps<1, 1, true>(a.cps, ld, m, blockIdx.x, tt, gridDim.x, full, empty, accf, acce, a.err, abort_flag);
-          else if (nk == 2) mma_single_cps<1, 2, true>(a.cps, ld, m, blockIdx.x, tt, gridDim.x, full, empty, accf, acce, a.err, abort_flag);
-          else mma_single_cps<1, 4, true>(a.cps, ld, m, blockIdx.x, tt, gridDim.x, full, empty, accf, acce, a.err, abort_flag);
+          if (nk == 1) mma_single_cps<1, 1, true>(a.cps, ld, m, t_begin, t_end, t_step, full, empty, accf, acce, a.err, abort_flag);
+          else if (nk == 2) mma_single_cps<1, 2, true>(a.cps, ld, m, t_begin, t_end, t_step, full, empty, accf, acce, a.err, abort_flag);
+          else mma_single_cps<1, 4, true>(a.cps, ld, m, t_begin, t_end, t_step, full, empty, accf, acce, a.err, abort_flag);
         } else {
-          if (nk == 1) mma_single_cps<1, 1, false>(a.cps, ld, m, blockIdx.x, tt, gridDim.x, full, empty, accf, acce, a.err, abort_flag);
-          else if (nk == 2) mma_single_cps<1, 2, false>(a.cps, ld, m, blockIdx.x, tt, gridDim.x, full, empty, accf, acce, a.err, abort_flag);
-          else mma_single_cps<1, 4, false>(a.cps, ld, m, blockIdx.x, tt, gridDim.x, full, empty, accf, acce, a.err, abort_flag);
+          if (nk == 1) mma_single_cps<1, 1, false>(a.cps, ld, m, t_begin, t_end, t_step, full, empty, accf, acce, a.err, abort_flag);
+          else if (nk == 2) mma_single_cps<1, 2, false>(a.cps, ld, m, t_begin, t_end, t_step, full, empty, accf, acce, a.err, abort_flag);
+          else mma_single_cps<1, 4, false>(a.cps, ld, m, t_begin, t_end, t_step, full, empty, accf, acce, a.err, abort_flag);
         }
         ok = false;  // the loop above ran every tile
       }
@@ -1205,49 +1206,47 @@ __global__ void __launch_bounds__(tc_threads_epi(G, EPI), 1)
     }
     __syncwarp();
   } else if (DWF && warp >= 2 + 4 * G) {
-    // fused depthwise: thread (row, part) builds channel part `part` of GEMM row `row` (tile pixel
-    // (row / BW, row % BW)): bias, the nine taps in (ky, kx) order as one FMA each with the per-image
-    // scaled weights, the activation, fp16; written into the 128-byte-swizzled A rows of the stage the
-    // MMA warp released. The halo box rows are 128-byte swizzled the same way.
-    constexpr int NDW = 32 * TC_DW_WARPS, PARTS = NDW / 128;
+    // fused depthwise: thread t owns 8-channel group g = t % (C / 8) (its 72 per-image scaled weights
+    // and 8 biases in registers) for GEMM rows r = t / (C / 8), + 128 / (C / 8), ... (tile pixel
+    // (r / BW, r % BW)): bias, the nine taps in (ky, kx) order as one FMA each, the activation, fp16,
+    // written into the 128-byte-swizzled A rows of the stage the MMA warp released. A warp reads whole
+    // 128-byte halo rows (the box rows are 128-byte swizzled the same way).
+    constexpr int NDW = 32 * TC_DW_WARPS;
     const int t = (int)threadIdx.x - tc_threads(G);
-    const int row = t & 127, part = t >> 7;
-    const int py = row / a.BW, px = row - py * a.BW;
-    const int C = a.dw_c, gper = C / (8 * PARTS);  // 8-channel groups per thread
+    const int C = a.dw_c, NG = C / 8, RS = NDW / NG;
+    const int g = t % NG, r0 = t / NG;
+    const int cb = g >> 3, ch = g & 7, c0 = g * 8;
     const int HW = a.BW + 2;
-    float* sw = reinterpret_cast<float*>(smem + a.dw_off + (size_t)a.dw_slots * a.dw_slot_bytes);  // [9][C], bias [C]
-    float* sbias = sw + 9 * C;
-    uint64_t* hfull = reinterpret_cast<uint64_t*>(sbias + C);
+    uint64_t* hfull = reinterpret_cast<uint64_t*>(smem + a.dw_off + (size_t)a.dw_slots * a.dw_slot_bytes +
+                                                  (size_t)10 * C * 4);
     uint64_t* hempty = hfull + 2;
-    for (int i = t; i < C; i += NDW) sbias[i] = __ldg(a.dw_b + i);
+    float w[9][8], bias[8];
+#pragma unroll
+    for (int j = 0; j < 8; j++) bias[j] = __ldg(a.dw_b + c0 + j);
     const int per_img = a.tiles_h * a.tiles_w;
     int s = 0, hs = 0, cur_img = -1;
     uint32_t phase = 0, hph = 0;
     for (int tile = t_begin; tile < t_end; tile += t_step) {
       const int img = tile / per_img;
       if (img != cur_img) {
-        // every thread is past its reads of the previous image's weights (barrier at the tile end)
-        for (int i = t; i < 9 * C; i += NDW)
-          sw[i] = __ldg(a.dw_w + i) * (a.dw_scale ? __ldg(a.dw_scale + (int64_t)img * C + i % C) : 1.0f);
-        named_bar_sync(1, NDW);
+#pragma unroll
+        for (int j = 0; j < 8; j++) {
+          const float sc = a.dw_scale ? __ldg(a.dw_scale + (int64_t)img * C + c0 + j) : 1.0f;
+#pragma unroll
+          for (int k = 0; k < 9; k++) w[k][j] = __ldg(a.dw_w + k * C + c0 + j) * sc;
+        }
         cur_img = img;
       }
       bool ok = mbar_wait(smem_u32(&hfull[hs]), hph, a.err, SDX_DEV_WAIT_FULL, abort_flag);
       ok = ok && mbar_wait(smem_u32(&empty[s]), phase ^ 1u, a.err, SDX_DEV_WAIT_EMPTY, abort_flag);
       if (named_bar_or(1, NDW, !ok)) break;
-      const uint32_t hbase = smem_u32(smem + a.dw_off) + (uint32_t)hs * a.dw_slot_bytes;
-      const uint32_t abase = smem_u32(sA) + (uint32_t)s * a.a_stage_bytes;
-      for (int gi = 0; gi < gper; gi++) {
-        const int g8 = part * gper + gi;  // 8-channel group: block g8 / 8, 16-byte chunk g8 % 8
-        const int cb = g8 >> 3, ch = g8 & 7, c0 = g8 * 8;
+      const uint32_t hblk = smem_u32(smem + a.dw_off) + (uint32_t)hs * a.dw_slot_bytes + (uint32_t)cb * a.dw_blk_bytes;
+      const uint32_t ablk = smem_u32(sA) + (uint32_t)s * a.a_stage_bytes + (uint32_t)cb * a.a_blk_bytes;
+      for (int row = r0; row < TC_BM; row += RS) {
+        const int py = row / a.BW, px = row - py * a.BW;
         float acc[8];
-        {
-          const float4 b0 = *reinterpret_cast<const float4*>(sbias + c0);
-          const float4 b1 = *reinterpret_cast<const float4*>(sbias + c0 + 4);
-          acc[0] = b0.x; acc[1] = b0.y; acc[2] = b0.z; acc[3] = b0.w;
-          acc[4] = b1.x; acc[5] = b1.y; acc[6] = b1.z; acc[7] = b1.w;
-        }
-        const uint32_t hblk = hbase + (uint32_t)cb * a.dw_blk_bytes;
+#pragma unroll
+        for (int j = 0; j < 8; j++) acc[j] = bias[j];
 #pragma unroll
         for (int ky = 0; ky < 3; ky++)
 #pragma unroll
@@ -1256,15 +1255,11 @@ __global__ void __launch_bounds__(tc_threads_epi(G, EPI), 1)
             uint4 u;
             lds16(hblk + pix * 128u + (((uint32_t)ch ^ (pix & 7u)) << 4), u);
             const __half2* h2 = reinterpret_cast<const __half2*>(&u);
-            const float* wp = sw + (ky * 3 + kx) * C + c0;
-            const float4 w0 = *reinterpret_cast<const float4*>(wp);
-            const float4 w1 = *reinterpret_cast<const float4*>(wp + 4);
-            const float wv[8] = {w0.x, w0.y, w0.z, w0.w, w1.x, w1.y, w1.z, w1.w};
 #pragma unroll
             for (int j = 0; j < 4; j++) {
               const float2 f = __half22float2(h2[j]);
-              acc[2 * j] = fmaf(f.x, wv[2 * j], acc[2 * j]);
-              acc[2 * j + 1] = fmaf(f.y, wv[2 * j + 1], acc[2 * j + 1]);
+              acc[2 * j] = fmaf(f.x, w[ky * 3 + kx][2 * j], acc[2 * j]);
+              acc[2 * j + 1] = fmaf(f.y, w[ky * 3 + kx][2 * j + 1], acc[2 * j + 1]);
             }
           }
         uint4 o;
@@ -1272,7 +1267,7 @@ __global__ void __launch_bounds__(tc_threads_epi(G, EPI), 1)
 #pragma unroll
         for (int j = 0; j < 4; j++)
           oh[j] = __floats2half2_rn(act_apply(acc[2 * j], a.dw_act), act_apply(acc[2 * j + 1], a.dw_act));
-        sts16(abase + (uint32_t)cb * a.a_blk_bytes + (uint32_t)row * 128u + (((uint32_t)ch ^ ((uint32_t)row & 7u)) << 4), o);
+        sts16(ablk + (uint32_t)row * 128u + (((uint32_t)ch ^ ((uint32_t)row & 7u)) << 4), o);
       }
       fence_async_smem();  // the generic-proxy A writes, before the MMAs (async proxy) read them
       named_bar_sync(1, NDW);

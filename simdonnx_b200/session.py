@@ -46,6 +46,12 @@ def _small_stem_pool(P: ExecPlan, n) -> bool:
             tuple(n.p.strides) == (1, 1) and not n.p.add and P.values[n.outs[0]].layout == "nhwc")
 
 
+# The fused depthwise -> pointwise node (sdx_dw_pw) in the session rewrite: measured slower on B200
+# than the two separate kernels for the det shapes (its depthwise warps cannot keep the pointwise
+# epilogue fed), so the rewrite leaves the pairs unfused; sdx_dw_pw stays available and tested.
+DW_PW_FUSION = False
+
+
 def cuda_rewrite(plan: ExecPlan) -> ExecPlan:
     # the reference's load-time BatchNorm rewrites come first (FoldConvBatchNorm, EmitBatchNorm)
     plan = lower_batchnorm(fold_conv_batchnorm(plan))
@@ -287,10 +293,11 @@ def cuda_rewrite(plan: ExecPlan) -> ExecPlan:
         n.ins.append(sums)
 
     # 9. depthwise 3x3 (stride 1) whose output only a 1x1 tensor-core conv reads -> one DwPw node
-    #    (sdx_dw_pw: the depthwise output is built tile by tile in shared memory, never stored)
+    #    (sdx_dw_pw: the depthwise output is built tile by tile in shared memory, never stored); off
+    #    while DW_PW_FUSION is False
     prods = {o: m for m in P.nodes for o in m.outs}
     fused, drop = {}, set()
-    for n in P.nodes:
+    for n in (P.nodes if DW_PW_FUSION else []):
         if n.op != "Conv" or n.p.group != 1 or getattr(n.p, "in_scale", None) is not None:
             continue
         d = prods.get(n.ins[0])

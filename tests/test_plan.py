@@ -52,16 +52,7 @@ def test_det_rewrites():
     # in2-in4 (per-image scaled weights, with their scratch as a second output); the product at the
     # 20x20 tap stays (in5 reads 512 channels: its per-image weights would not stay resident)
     fused = [n for n in P.nodes if n.op == "Conv" and getattr(n.p, "in_scale", None)]
-    dwpw = [n for n in P.nodes if n.op == "DwPw"]
-    # the 3x3 stride-1 depthwise convs over 64 / 128 channels are fused into their pointwise convs
-    assert [n.name for n in dwpw] == ["b3.pw", "b5.pw"]
-    assert all(getattr(n.p[0], "in_scale", None) for n in dwpw)
-    assert "b3.dw" not in P.values and "b5.dw" not in P.values  # never stored
-    # b3 (160x160) keeps its fused SE sums; b5 (80 wide: no whole 32-pixel runs per tile row) does not
-    assert len(dwpw[0].outs) == 2 and len(dwpw[1].outs) == 1
-    gate5 = [n for n in P.nodes if n.name == "b5.se"][0]
-    assert len(gate5.ins) == 3
-    assert len(fused) + len(dwpw) == 14
+    assert len(fused) == 14
     lat = sorted(n.name for n in fused if n.p.group == 1)
     assert lat == ["fpn.in2", "fpn.in3", "fpn.in4"]
     for n in fused:
@@ -73,6 +64,27 @@ def test_det_rewrites():
     cn = [n for n in P.nodes if n.op == "ConcatNearest"]
     assert len(cn) == 1 and cn[0].ins == ["fpn.p5", "fpn.p4", "fpn.p3", "fpn.p2"] and cn[0].p == (8, 4, 2, 1)
     assert not any(n.op == "ResizeNearest" and n.outs[0] in ("fpn.p5u", "fpn.p4u", "fpn.p3u") for n in P.nodes)
+
+
+def test_dw_pw_fusion_rewrite():
+    """With the fusion on, the 3x3 stride-1 depthwise convs over 64 / 128 channels become DwPw nodes with
+    their pointwise convs; the depthwise outputs are never stored; b3 (160 wide) keeps its fused SE sums,
+    b5 (80 wide: no whole 32-pixel runs per tile row) gives them up and its gate reads the tensor."""
+    from simdonnx_b200 import session as S
+    old = S.DW_PW_FUSION
+    S.DW_PW_FUSION = True
+    try:
+        P = cuda_rewrite(configs.build_det(batch=1))
+    finally:
+        S.DW_PW_FUSION = old
+    dwpw = [n for n in P.nodes if n.op == "DwPw"]
+    assert [n.name for n in dwpw] == ["b3.pw", "b5.pw"]
+    assert all(getattr(n.p[0], "in_scale", None) for n in dwpw)
+    assert "b3.dw" not in P.values and "b5.dw" not in P.values
+    assert len(dwpw[0].outs) == 2 and len(dwpw[1].outs) == 1
+    gate5 = [n for n in P.nodes if n.name == "b5.se"][0]
+    assert len(gate5.ins) == 3
+    P.plan_arena()
 
 
 def test_concat_partial_aliasing_with_pool_reader():
