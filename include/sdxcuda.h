@@ -180,7 +180,7 @@ int sdx_conv2d(sdx_ctx* ctx, const sdx_conv_desc* d, sdx_stream s);
  * gap_sums as sdx_conv2d; fp16 output, no residual). The depthwise output is built per 32 x 4 pixel
  * tile in shared memory and fed to the tensor cores; it never reaches HBM. dw.w: sdx_pack_conv(&dw),
  * pw.w: sdx_pack_conv(&pw). sdx_dw_pw_supported: 1 when the shapes take this form (64 or 128
- * channels, at most 128 outputs), else 0; pw.gap_sums further needs ow a multiple of 32 and oh of 4. */
+ * channels, dw.act none, relu or hardswish, at most 128 outputs), else 0; pw.gap_sums further needs ow a multiple of 32 and oh of 4. */
 typedef struct sdx_dwpw_desc {
   sdx_conv_desc dw, pw;
 } sdx_dwpw_desc;

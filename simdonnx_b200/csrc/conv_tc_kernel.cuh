@@ -484,6 +484,15 @@ __device__ __forceinline__ void ffma2_pair(float& a0, float& a1, float h, float 
       : "f"(h), "f"(w0), "f"(w1));
 }
 
+// (a0, a1) += (x0, x1) * (w0, w1) as one packed f32x2 FMA; each lane is the single-rounding fmaf.
+__device__ __forceinline__ void ffma2_vec(float& a0, float& a1, float x0, float x1, float w0, float w1) {
+  asm("{\n\t.reg .b64 ra, rx, rw;\n\t"
+      "mov.b64 ra, {%0, %1};\n\tmov.b64 rx, {%2, %3};\n\tmov.b64 rw, {%4, %5};\n\t"
+      "fma.rn.f32x2 ra, rx, rw, ra;\n\tmov.b64 {%0, %1}, ra;\n\t}"
+      : "+f"(a0), "+f"(a1)
+      : "f"(x0), "f"(x1), "f"(w0), "f"(w1));
+}
+
 // Two-float packed add (sm_100 f32x2 pipe: one instruction for both lanes of the pair).
 __device__ __forceinline__ float2 add_f32x2(float2 a, float2 b) {
   uint64_t x, y, d;
@@ -1223,6 +1232,11 @@ __global__ void __launch_bounds__(tc_threads_epi(G, EPI), 1)
     float w[9][8], bias[8];
 #pragma unroll
     for (int j = 0; j < 8; j++) bias[j] = __ldg(a.dw_b + c0 + j);
+    // activation without a per-value branch: v * sat(v * act_s + act_o) is hardswish (1/6, 1/2),
+    // relu (+inf, 0: the factor is 1 for v > 0 and 0 otherwise, sat(NaN) being 0) or none (0, 1);
+    // sdx_dw_pw admits only these three
+    const float act_s = a.dw_act == ACT_HARDSWISH ? 1.0f / 6.0f : a.dw_act == ACT_RELU ? INFINITY : 0.0f;
+    const float act_o = a.dw_act == ACT_HARDSWISH ? 0.5f : a.dw_act == ACT_RELU ? 0.0f : 1.0f;
     const int per_img = a.tiles_h * a.tiles_w;
     int s = 0, hs = 0, cur_img = -1;
     uint32_t phase = 0, hph = 0;
@@ -1242,6 +1256,7 @@ __global__ void __launch_bounds__(tc_threads_epi(G, EPI), 1)
       if (named_bar_or(1, NDW, !ok)) break;
       const uint32_t hblk = smem_u32(smem + a.dw_off) + (uint32_t)hs * a.dw_slot_bytes + (uint32_t)cb * a.dw_blk_bytes;
       const uint32_t ablk = smem_u32(sA) + (uint32_t)s * a.a_stage_bytes + (uint32_t)cb * a.a_blk_bytes;
+#pragma unroll 1
       for (int row = r0; row < TC_BM; row += RS) {
         const int py = row / a.BW, px = row - py * a.BW;
         float acc[8];
@@ -1265,8 +1280,11 @@ __global__ void __launch_bounds__(tc_threads_epi(G, EPI), 1)
         uint4 o;
         __half2* oh = reinterpret_cast<__half2*>(&o);
 #pragma unroll
-        for (int j = 0; j < 4; j++)
-          oh[j] = __floats2half2_rn(act_apply(acc[2 * j], a.dw_act), act_apply(acc[2 * j + 1], a.dw_act));
+        for (int j = 0; j < 4; j++) {
+          const float v0 = acc[2 * j] * __saturatef(fmaf(acc[2 * j], act_s, act_o));
+          const float v1 = acc[2 * j + 1] * __saturatef(fmaf(acc[2 * j + 1], act_s, act_o));
+          oh[j] = __floats2half2_rn(v0, v1);
+        }
         sts16(ablk + (uint32_t)row * 128u + (((uint32_t)ch ^ ((uint32_t)row & 7u)) << 4), o);
       }
       fence_async_smem();  // the generic-proxy A writes, before the MMAs (async proxy) read them

@@ -583,7 +583,8 @@ int sdx_dw_pw_supported(const sdx_dwpw_desc* d) {
   const sdx_conv_desc& p = d->pw;
   const bool dw_ok = conv_route(&w) == R_DEPTHWISE && w.kh == 3 && w.kw == 3 && w.sh == 1 && w.sw == 1 &&
                      w.pad_t == 1 && w.pad_l == 1 && w.pad_b == 1 && w.pad_r == 1 && w.x_dtype == SDX_F16 &&
-                     w.x_layout == SDX_NHWC && w.y_dtype == SDX_F16 && w.pool == 0 && (w.ic == 64 || w.ic == 128);
+                     w.x_layout == SDX_NHWC && w.y_dtype == SDX_F16 && w.pool == 0 && (w.ic == 64 || w.ic == 128) &&
+                     (w.act == SDX_ACT_NONE || w.act == SDX_ACT_RELU || w.act == SDX_ACT_HARDSWISH);
   const int64_t ystride = p.y_pix_stride > 0 ? p.y_pix_stride : p.oc;
   const bool pw_ok = conv_route(&p) == R_TC_ROWS && p.in_scale == 0 && p.ic == w.oc && p.batch == w.batch &&
                      p.ih == w.oh && p.iw == w.ow && p.oc <= 128 && p.y_dtype == SDX_F16 && p.add_up == 0 &&
@@ -596,8 +597,8 @@ int sdx_dw_pw(sdx_ctx* ctx, const sdx_dwpw_desc* d, sdx_stream s) {
   if (!d) return set_error(SDX_ERR_INVALID, "null desc");
   LAUNCH_GUARD();
   if (!sdx_dw_pw_supported(d))
-    return set_error(SDX_ERR_NOT_SUPPORTED, "dw+pw: needs a 3x3 s1 depthwise over 64 or 128 fp16 channels and a 1x1 "
-                                            "conv to at most 128 fp16 outputs (multiples of 16)");
+    return set_error(SDX_ERR_NOT_SUPPORTED, "dw+pw: needs a 3x3 s1 depthwise over 64 or 128 fp16 channels (act none, relu or "
+                                            "hardswish) and a 1x1 conv to at most 128 fp16 outputs (multiples of 16)");
   if (d->pw.add || d->dw.add) return set_error(SDX_ERR_NOT_SUPPORTED, "dw+pw: no residuals");
   if (!d->dw.bias) return set_error(SDX_ERR_INVALID, "dw+pw: depthwise bias required (zeros when absent)");
   const sdx_conv_desc& w = d->dw;

@@ -4,7 +4,8 @@ GB/s and TFLOP/s against the algorithmic work. Small enough to run under ncu.
 
     python -m simdonnx_b200.kernel_bench --op pw --batch 64 --hw 80 --cin 64 --cout 128 --iters 20
 ops: pw (1x1 conv, tensor cores), conv3 (3x3 s1, tensor cores), dw (depthwise), stem (3x3 s2 from
-fp32 NCHW), convt (2x2 s2 ConvTranspose), gate (squeeze-excitation gate), copy (torch copy, the
+fp32 NCHW), convt (2x2 s2 ConvTranspose), gate (squeeze-excitation gate), dwpw (depthwise 3x3 ->
+1x1 fused, sdx_dw_pw; --unfused: the same two convs as two launches), copy (torch copy, the
 HBM reference point), fill (write-only reference), expand (1:2 read:write reference, torch cat)
 """
 from __future__ import annotations
@@ -30,6 +31,8 @@ def main():
     ap.add_argument("--stride", type=int, default=1)
     ap.add_argument("--act", default="hardswish")
     ap.add_argument("--gap", action="store_true", help="pw: also write the 32-pixel channel sums (SE pooling)")
+    ap.add_argument("--scale", action="store_true", help="dwpw: per-image SE scale on the depthwise input")
+    ap.add_argument("--unfused", action="store_true", help="dwpw: depthwise and pointwise as two launches")
     ap.add_argument("--iters", type=int, default=20)
     ap.add_argument("--warmup", type=int, default=3)
     a = ap.parse_args()
@@ -68,6 +71,26 @@ def main():
         if sums is not None:
             byts += sums.numel() * 4
         shape = dict(n=n, h=hw, w=hw, cin=ci, cout=co, k=k, stride=s, oh=d.oh, ow=d.ow)
+    elif a.op == "dwpw":
+        x = torch.randn((n, hw, hw, ci), device=dev).half()
+        dwd = B.conv_desc(n, hw, hw, ci, ci, 3, 3, pads=(1,) * 4, group=ci, act=a.act)
+        pwd = B.conv_desc(n, hw, hw, ci, co, 1, 1, act=a.act)
+        pdw = B.pack_conv(dwd, (rng.standard_normal((ci, 1, 3, 3)) * 0.3).astype(np.float32))
+        ppw = B.pack_conv(pwd, (rng.standard_normal((co, ci, 1, 1)) * 0.1).astype(np.float32))
+        bdw, bpw = torch.zeros(ci, device=dev), torch.zeros(co, device=dev)
+        scale = torch.rand((n, ci), device=dev) if a.scale else None
+        sums = torch.empty((n * hw * hw // 32, co), dtype=torch.float32, device=dev) if a.gap else None
+        y = torch.empty((n, hw, hw, co), dtype=torch.float16, device=dev)
+        byts = x.numel() * 2 + y.numel() * 2 + (sums.numel() * 4 if a.gap else 0)
+        if a.unfused:
+            mid = torch.empty_like(x)
+            pwd.gap_sums = B.ptr(sums)
+            run = lambda: (B.conv2d(be, dwd, x, pdw, bias=bdw, y=mid, in_scale=scale),
+                           B.conv2d(be, pwd, mid, ppw, bias=bpw, y=y))
+        else:
+            run = lambda: B.dw_pw(be, dwd, pwd, x, pdw, bdw, ppw, bpw, in_scale=scale, gap=sums, y=y)
+        flops = 2 * n * hw * hw * ci * (9 + co)
+        shape = dict(n=n, h=hw, w=hw, cin=ci, cout=co, unfused=a.unfused)
     elif a.op == "convt":
         x = torch.randn((n, hw, hw, ci), device=dev).half()
         w = (rng.standard_normal((ci, co, 2, 2)) * 0.1).astype(np.float32)

@@ -146,14 +146,15 @@ def test_pointwise_small_outputs(be, ic, oc, act, res_nchw, res_f32, y_f32):
     assert_close(host(y), ref, f"pointwise {ic}->{oc}")
 
 
-@pytest.mark.parametrize("nb,h,w,c,oc,scale,gap", [
-    (3, 16, 64, 64, 64, True, True),     # the det b3 block's shape class, SE scale in, SE sums out
-    (2, 20, 32, 128, 128, True, True),   # b5: 128 channels (two channel blocks)
-    (2, 13, 40, 64, 96, False, False),   # ragged tiles: 40 columns, 13 rows
-    (2, 160, 160, 64, 64, True, True),   # b3 at full resolution
+@pytest.mark.parametrize("nb,h,w,c,oc,scale,gap,dact", [
+    (3, 16, 64, 64, 64, True, True, "hardswish"),     # the det b3 block's shape class, SE scale in, sums out
+    (2, 20, 32, 128, 128, True, True, "hardswish"),   # b5: 128 channels (two channel blocks)
+    (2, 13, 40, 64, 96, False, False, "relu"),        # ragged tiles: 40 columns, 13 rows
+    (1, 8, 32, 128, 32, False, False, "none"),        # no depthwise activation
+    (2, 160, 160, 64, 64, True, True, "hardswish"),   # b3 at full resolution
 ])
-def test_depthwise_pointwise_fused(be, nb, h, w, c, oc, scale, gap):
-    """Depthwise 3x3 (+hardswish, per-image input scale) computed tile by tile in shared memory and fed
+def test_depthwise_pointwise_fused(be, nb, h, w, c, oc, scale, gap, dact):
+    """Depthwise 3x3 (+activation, per-image input scale) computed tile by tile in shared memory and fed
     to the 1x1 tensor-core conv (sdx_dw_pw) against the oracle's two convs; the fused channel sums
     against sums of the output."""
     from simdonnx_b200 import backend as B
@@ -165,10 +166,10 @@ def test_depthwise_pointwise_fused(be, nb, h, w, c, oc, scale, gap):
     wpw = rnd(rng, oc, c, 1, 1, scale=1.0 / np.sqrt(c))
     bpw = rnd(rng, oc)
     xin = O.channel_broadcast(x, sc) if scale else x
-    mid = O.conv(xin, O.ConvPlan(wdw, bdw, group=c), pads=(1, 1, 1, 1), act="hardswish")
+    mid = O.conv(xin, O.ConvPlan(wdw, bdw, group=c), pads=(1, 1, 1, 1), act=dact)
     mid = mid.astype(np.float16).astype(np.float32)  # the depthwise output is fp16 (as when stored)
     ref = O.conv(mid, O.ConvPlan(wpw, bpw), act="hardswish")
-    dwd = B.conv_desc(nb, h, w, c, c, 3, 3, pads=(1, 1, 1, 1), group=c, act="hardswish")
+    dwd = B.conv_desc(nb, h, w, c, c, 3, 3, pads=(1, 1, 1, 1), group=c, act=dact)
     pwd = B.conv_desc(nb, h, w, c, oc, 1, 1, act="hardswish")
     if scale:
         dwd.in_scale = 1

@@ -87,6 +87,16 @@ def test_dw_pw_fusion_rewrite():
     P.plan_arena()
 
 
+def test_dw_pw_supported_activations():
+    """sdx_dw_pw applies the depthwise activation as a compile-time constant of its row loop: none,
+    relu and hardswish are admitted, the others refused (the session keeps the two convs)."""
+    from simdonnx_b200 import backend as B
+    for act, ok in [("none", True), ("relu", True), ("hardswish", True), ("sigmoid", False), ("gelu", False)]:
+        dwd = B.conv_desc(2, 16, 64, 64, 64, 3, 3, pads=(1, 1, 1, 1), group=64, act=act)
+        pwd = B.conv_desc(2, 16, 64, 64, 64, 1, 1, act="sigmoid")
+        assert B.dw_pw_supported(dwd, pwd) == ok, act
+
+
 def test_concat_partial_aliasing_with_pool_reader():
     """UNet skip: a conv output read by a max pool and a concat is written into its concat slice
     (the pool reads the slice in place); a ConvTranspose input is still copied by the concat node."""
