@@ -1428,7 +1428,7 @@ __global__ void __launch_bounds__(tc_threads_epi(G, EPI), 1)
       // cannot stage) need it
       bool valid = false;
       int64_t pix = 0;
-      if (!a.tma_out || (a.res && !a.tma_res)) {
+      if (!FAST && (!a.tma_out || (a.res && !a.tma_res))) {
         if (a.mode == TC_CONV) {
           const int h = row_in_tile / a.BW, w = row_in_tile - h * a.BW;
           const int oy = tcd.oy0 + h, ox = tcd.ox0 + w;
@@ -1545,7 +1545,7 @@ __global__ void __launch_bounds__(tc_threads_epi(G, EPI), 1)
         __syncwarp();
         continue;
       }
-      if (a.kxn) {
+      if (!FAST && a.kxn) {
         // kx-in-N: columns kx * kb + oc (kb = 32 or 64); row x of the tile is input column ox0 - 1 + x,
         // and the output at that column is D[x - 1][kx 0] + D[x][kx 1] + D[x + 1][kx 2] (neighbouring
         // lanes: the 32 rows of a warp are consecutive columns of one or two tile rows); 32 output
@@ -1646,19 +1646,25 @@ __global__ void __launch_bounds__(tc_threads_epi(G, EPI), 1)
           }
         }
       }
-      if (FAST && nch <= 2) {
-        // thin tiles: both chunks' TMEM loads in flight under one wait, the accumulator handed
-        // back before any arithmetic
-        float v0[16], v1[16];
-        tmem_ld16_issue(tbase, v0);
-        if (nch == 2) tmem_ld16_issue(tbase + 16u, v1);
-        tmem_wait_ld();
-        tmem_ld_wait16(v0);
-        if (nch == 2) tmem_ld_wait16(v1);
-        tc_fence_before();
-        mbar_arrive(smem_u32(&acce[acc]));
-        epi_chunk_fast<ACT>(a, v0, 0, srow, xr, sBias + tcd.n0, res_smem);
-        if (nch == 2) epi_chunk_fast<ACT>(a, v1, 1, srow, xr, sBias + tcd.n0, res_smem);
+      if (FAST) {
+        // chunk pairs: both chunks' TMEM loads in flight under one wait, the accumulator handed back
+        // after the last pair's loads, before its arithmetic (two 16-float buffers: no spills at the
+        // 96-register cap of four epilogue groups)
+        for (int c = 0; c < nch; c += 2) {
+          float v0[16], v1[16];
+          const bool two = c + 1 < nch;
+          tmem_ld16_issue(tbase + (uint32_t)c * 16u, v0);
+          if (two) tmem_ld16_issue(tbase + (uint32_t)(c + 1) * 16u, v1);
+          tmem_wait_ld();
+          tmem_ld_wait16(v0);
+          if (two) tmem_ld_wait16(v1);
+          if (c + 2 >= nch) {
+            tc_fence_before();
+            mbar_arrive(smem_u32(&acce[acc]));
+          }
+          epi_chunk_fast<ACT>(a, v0, c, srow, xr, sBias + tcd.n0, res_smem);
+          if (two) epi_chunk_fast<ACT>(a, v1, c + 1, srow, xr, sBias + tcd.n0, res_smem);
+        }
       } else {
       // 16-column chunks through two register buffers: the load of chunk c+1 is in flight while
       // chunk c is processed; the accumulator goes back to the MMA warp after its last load
@@ -1673,8 +1679,7 @@ __global__ void __launch_bounds__(tc_threads_epi(G, EPI), 1)
           tc_fence_before();
           mbar_arrive(smem_u32(&acce[acc]));
         }
-        if (FAST) epi_chunk_fast<ACT>(a, va, c, srow, xr, sBias + tcd.n0, res_smem);
-        else epi_chunk<ACT>(a, va, c, srow, xr, sBias, tcd, valid, pix, g, cg);
+        epi_chunk<ACT>(a, va, c, srow, xr, sBias, tcd, valid, pix, g, cg);
         if (c + 1 < nch) {
           tmem_wait_ld();
           tmem_ld_wait16(vb);
@@ -1684,8 +1689,7 @@ __global__ void __launch_bounds__(tc_threads_epi(G, EPI), 1)
             tc_fence_before();
             mbar_arrive(smem_u32(&acce[acc]));
           }
-          if (FAST) epi_chunk_fast<ACT>(a, vb, c + 1, srow, xr, sBias + tcd.n0, res_smem);
-          else epi_chunk<ACT>(a, vb, c + 1, srow, xr, sBias, tcd, valid, pix, g, cg);
+          epi_chunk<ACT>(a, vb, c + 1, srow, xr, sBias, tcd, valid, pix, g, cg);
         }
       }
       }

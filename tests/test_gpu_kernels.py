@@ -520,12 +520,14 @@ def test_convt_chain(be, ic, oc1, h, w, act1, f32):
     assert be.device_error() == 0
 
 
-@pytest.mark.parametrize("ic,oc,k,h,w", [(64, 96, 1, 20, 24), (32, 64, 3, 16, 22), (256, 96, 1, 40, 40)])
-def test_conv_upsampled_residual(be, ic, oc, k, h, w):
+@pytest.mark.parametrize("nb,ic,oc,k,h,w", [
+    (2, 64, 96, 1, 20, 24), (2, 32, 64, 3, 16, 22), (2, 256, 96, 1, 40, 40),
+    (8, 64, 96, 1, 96, 96),  # ~4 tiles per CTA: each epilogue group prefetches its next tile's residual rows
+])
+def test_conv_upsampled_residual(be, nb, ic, oc, k, h, w):
     """FPN top-down add fused into the lateral conv: y = conv(x) + nearest_up2(r), r on the half grid."""
     from simdonnx_b200 import backend as B
     rng = np.random.default_rng(ic + oc + k)
-    nb = 2
     x = rnd(rng, nb, h, w, ic)
     r = rnd(rng, nb, h // 2, w // 2, oc)
     wt = rnd(rng, oc, ic, k, k, scale=1 / np.sqrt(ic * k * k))
