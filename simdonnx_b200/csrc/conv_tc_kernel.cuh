@@ -311,13 +311,16 @@ struct MmaSingle {
   uint64_t dconst, bd0;
   int S, nacc, n_tiles, nt_step, nt0;
 };
+// Tiles of ordinals w, w + nw, ... of the CTA's sequence (nw MMA-issuing warps, this one w < nw <= 2):
+// ordinal o uses ring slot o mod S and accumulator o mod nacc (S >= nw, nacc a multiple of nw).
 template <int BT, int NK, bool TWO, int CPS>
 __device__ __noinline__ void mma_single_loop(uint32_t ld, const MmaSingle m, int tile0, int total_tiles, int tstep,
-                                             uint64_t* full, uint64_t* empty, uint64_t* accf, uint64_t* acce,
-                                             unsigned int* err, volatile int* abort_flag) {
-  int s = 0, nt = m.nt0;
-  uint32_t phase = 0, acc = 0, accph = 0;
-  for (int tile = tile0; tile < total_tiles; tile += tstep) {
+                                             int w, int nw, uint64_t* full, uint64_t* empty, uint64_t* accf,
+                                             uint64_t* acce, unsigned int* err, volatile int* abort_flag) {
+  int s = w, nt = (m.nt0 + w * m.nt_step) % m.n_tiles;
+  const int nt_adv = (nw * m.nt_step) % m.n_tiles;
+  uint32_t phase = 0, acc = (uint32_t)w, accph = 0;
+  for (int tile = tile0 + w * tstep; tile < total_tiles; tile += nw * tstep) {
     if (!mbar_wait_warp(smem_u32(&acce[acc]), accph ^ 1u, err, SDX_DEV_WAIT_ACC_EMPTY, abort_flag)) break;
     if (!mbar_wait_warp(smem_u32(&full[s]), phase, err, SDX_DEV_WAIT_FULL, abort_flag)) break;
     tc_fence_after();
@@ -330,22 +333,29 @@ __device__ __noinline__ void mma_single_loop(uint32_t ld, const MmaSingle m, int
                               m.b_tap16, m.b_lo16, m.idesc, ci == 0 ? 0u : 1u);
     tc_commit_p(ld, smem_u32(&empty[s]));
     tc_commit_p(ld, smem_u32(&accf[acc]));
-    s = s + 1 == m.S ? 0 : s + 1;
-    phase ^= s == 0 ? 1u : 0u;
-    acc = acc + 1 == (uint32_t)m.nacc ? 0u : acc + 1;
-    accph ^= acc == 0 ? 1u : 0u;
-    nt += m.nt_step;
+    s += nw;
+    if (s >= m.S) {
+      s -= m.S;
+      phase ^= 1u;
+    }
+    acc += (uint32_t)nw;
+    if (acc >= (uint32_t)m.nacc) {
+      acc -= (uint32_t)m.nacc;
+      accph ^= 1u;
+    }
+    nt += nt_adv;
     nt = nt >= m.n_tiles ? nt - m.n_tiles : nt;
   }
 }
 template <int BT, int NK, bool TWO>
 __device__ __forceinline__ void mma_single_cps(int cps, uint32_t ld, const MmaSingle& m, int tile0, int total_tiles,
-                                               int tstep, uint64_t* full, uint64_t* empty, uint64_t* accf,
-                                               uint64_t* acce, unsigned int* err, volatile int* abort_flag) {
-  if (cps == 1) mma_single_loop<BT, NK, TWO, 1>(ld, m, tile0, total_tiles, tstep, full, empty, accf, acce, err, abort_flag);
-  else if (cps == 2) mma_single_loop<BT, NK, TWO, 2>(ld, m, tile0, total_tiles, tstep, full, empty, accf, acce, err, abort_flag);
-  else if (cps == 3) mma_single_loop<BT, NK, TWO, 3>(ld, m, tile0, total_tiles, tstep, full, empty, accf, acce, err, abort_flag);
-  else mma_single_loop<BT, NK, TWO, 4>(ld, m, tile0, total_tiles, tstep, full, empty, accf, acce, err, abort_flag);
+                                               int tstep, int w, int nw, uint64_t* full, uint64_t* empty,
+                                               uint64_t* accf, uint64_t* acce, unsigned int* err,
+                                               volatile int* abort_flag) {
+  if (cps == 1) mma_single_loop<BT, NK, TWO, 1>(ld, m, tile0, total_tiles, tstep, w, nw, full, empty, accf, acce, err, abort_flag);
+  else if (cps == 2) mma_single_loop<BT, NK, TWO, 2>(ld, m, tile0, total_tiles, tstep, w, nw, full, empty, accf, acce, err, abort_flag);
+  else if (cps == 3) mma_single_loop<BT, NK, TWO, 3>(ld, m, tile0, total_tiles, tstep, w, nw, full, empty, accf, acce, err, abort_flag);
+  else mma_single_loop<BT, NK, TWO, 4>(ld, m, tile0, total_tiles, tstep, w, nw, full, empty, accf, acce, err, abort_flag);
 }
 
 // One 16-column chunk (tile columns 16c..16c+15) of one accumulator row: bias -> + residual ->
@@ -772,7 +782,7 @@ __global__ void __launch_bounds__(tc_threads_epi(G, EPI), 1)
       mbar_init(smem_u32(&acce[i]), 128);
     }
     for (int i = 0; i < G * 2 * 4; i++) mbar_init(smem_u32(&resb[i]), 1);
-    mbar_init(smem_u32(drain), 1);
+    mbar_init(smem_u32(drain), EPI == 2 ? 2 : 1);  // one commit per MMA-issuing warp
     mbar_init(smem_u32(bres), 1);
     if (DWF) {
       uint64_t* hb = reinterpret_cast<uint64_t*>(smem + a.dw_off + (size_t)a.dw_slots * a.dw_slot_bytes +
@@ -1046,7 +1056,10 @@ __global__ void __launch_bounds__(tc_threads_epi(G, EPI), 1)
       if (b_loads > 0) mbar_wait_drain(smem_u32(bres), (b_loads - 1) & 1u, a.err, SDX_DEV_WAIT_DRAIN);
     }
     __syncwarp();
-  } else if (warp == 1) {
+  } else if (warp == 1 || (EPI == 2 && warp == 2 + 4 * G)) {
+    // MMA issue: warp 1, and for kx-in-N tiles a second warp taking every other tile of the
+    // single-stage loop (mw = 1); every other path runs on warp 1 alone
+    const int mw = warp == 1 ? 0 : 1;
     const uint32_t ld = elect_leader();
     {
       const uint32_t idesc = umma_idesc_f16(TC_BM, a.BN);
@@ -1070,6 +1083,8 @@ __global__ void __launch_bounds__(tc_threads_epi(G, EPI), 1)
       // one-tap tiles (pointwise), and the kx-in-N 3x3 convs (three row taps, one weight term)
       const bool single = kblocks == 1 && a.b_resident && (a.b_taps == 1 || (a.b_taps == 3 && a.wterms == 1)) &&
                           a.cps <= 4 && (nk == 1 || nk == 2 || nk == 4) && !imgw;
+      const int nmw = (EPI == 2 && single && S >= 2 && (a.nacc & 1) == 0) ? 2 : 1;
+      if (mw >= nmw) ok = false;  // the second warp has no tiles: only its drain commit below
       if (ok && single) {
         MmaSingle m;
         m.d0 = tmem_base;
@@ -1092,17 +1107,17 @@ __global__ void __launch_bounds__(tc_threads_epi(G, EPI), 1)
         m.nt0 = (int)(blockIdx.x % (unsigned)a.n_tiles);
         const int tt = a.m_tiles * a.n_tiles;
         if (a.b_taps == 3) {
-          if (nk == 1) mma_single_cps<3, 1, false>(a.cps, ld, m, t_begin, t_end, t_step, full, empty, accf, acce, a.err, abort_flag);
-          else if (nk == 2) mma_single_cps<3, 2, false>(a.cps, ld, m, t_begin, t_end, t_step, full, empty, accf, acce, a.err, abort_flag);
-          else mma_single_cps<3, 4, false>(a.cps, ld, m, t_begin, t_end, t_step, full, empty, accf, acce, a.err, abort_flag);
+          if (nk == 1) mma_single_cps<3, 1, false>(a.cps, ld, m, t_begin, t_end, t_step, mw, nmw, full, empty, accf, acce, a.err, abort_flag);
+          else if (nk == 2) mma_single_cps<3, 2, false>(a.cps, ld, m, t_begin, t_end, t_step, mw, nmw, full, empty, accf, acce, a.err, abort_flag);
+          else mma_single_cps<3, 4, false>(a.cps, ld, m, t_begin, t_end, t_step, mw, nmw, full, empty, accf, acce, a.err, abort_flag);
         } else if (a.wterms == 2) {
-          if (nk == 1) mma_single_cps<1, 1, true>(a.cps, ld, m, t_begin, t_end, t_step, full, empty, accf, acce, a.err, abort_flag);
-          else if (nk == 2) mma_single_cps<1, 2, true>(a.cps, ld, m, t_begin, t_end, t_step, full, empty, accf, acce, a.err, abort_flag);
-          else mma_single_cps<1, 4, true>(a.cps, ld, m, t_begin, t_end, t_step, full, empty, accf, acce, a.err, abort_flag);
+          if (nk == 1) mma_single_cps<1, 1, true>(a.cps, ld, m, t_begin, t_end, t_step, mw, nmw, full, empty, accf, acce, a.err, abort_flag);
+          else if (nk == 2) mma_single_cps<1, 2, true>(a.cps, ld, m, t_begin, t_end, t_step, mw, nmw, full, empty, accf, acce, a.err, abort_flag);
+          else mma_single_cps<1, 4, true>(a.cps, ld, m, t_begin, t_end, t_step, mw, nmw, full, empty, accf, acce, a.err, abort_flag);
         } else {
-          if (nk == 1) mma_single_cps<1, 1, false>(a.cps, ld, m, t_begin, t_end, t_step, full, empty, accf, acce, a.err, abort_flag);
-          else if (nk == 2) mma_single_cps<1, 2, false>(a.cps, ld, m, t_begin, t_end, t_step, full, empty, accf, acce, a.err, abort_flag);
-          else mma_single_cps<1, 4, false>(a.cps, ld, m, t_begin, t_end, t_step, full, empty, accf, acce, a.err, abort_flag);
+          if (nk == 1) mma_single_cps<1, 1, false>(a.cps, ld, m, t_begin, t_end, t_step, mw, nmw, full, empty, accf, acce, a.err, abort_flag);
+          else if (nk == 2) mma_single_cps<1, 2, false>(a.cps, ld, m, t_begin, t_end, t_step, mw, nmw, full, empty, accf, acce, a.err, abort_flag);
+          else mma_single_cps<1, 4, false>(a.cps, ld, m, t_begin, t_end, t_step, mw, nmw, full, empty, accf, acce, a.err, abort_flag);
         }
         ok = false;  // the loop above ran every tile
       }
