@@ -1060,11 +1060,14 @@ __device__ __forceinline__ void stem_tile_compute(const DirectArgs& a, const flo
 }
 
 // ---- tensor-core form of the det stem, warp-specialised like the tensor-core conv: warp 0 streams
-// the fp32 input tiles (TMA, two buffers), warps 2-5 build im2col rows of 128-pixel M blocks into a
-// ring of shared-memory slots, warp 1 issues the MMAs of each block into a ring of TMEM
-// accumulators, warps 6-9 drain them (bias, activation, fp16 NHWC stores). Every hand-off is an
-// mbarrier, so building, MMAs, draining and loading overlap. A row = one output pixel, K = 27 taps
-// (k = (ky*3 + kx)*3 + c, padded to 32) of fp16-rounded inputs in 64-byte rows under the 64-byte
+// the fp32 input tiles (TMA, a ring of buffers), BG groups of four warps build im2col rows of
+// 128-pixel M blocks into a ring of shared-memory slots, warp 1 issues the MMAs of each block into a
+// ring of TMEM accumulators, DG groups of four warps drain them (bias, activation, fp16 NHWC stores).
+// Each group handles every BG-th (DG-th) block: one group per role left each block's work as a
+// single latency chain per warp (N=256: 0.64 ms with one of each, 0.45 with two, 0.42 with two
+// builder and three drain groups; four builder groups gain nothing). Every hand-off
+// is an mbarrier, so building, MMAs, draining and loading overlap. A row = one output pixel, K = 27
+// taps (k = (ky*3 + kx)*3 + c, padded to 32) of fp16-rounded inputs in 64-byte rows under the 64-byte
 // swizzle; B = the 16 filters as fp16 hi and lo terms (the same layout), fp32 accumulation.
 constexpr int STEM_TC_TH = 8;
 constexpr int STEM_TC_IH = 2 * STEM_TC_TH + 1;                   // 17 input rows
@@ -1075,7 +1078,10 @@ constexpr int STEM_TC_NACC = 4;                                   // TMEM accumu
 constexpr uint32_t STEM_TC_A_BYTES = 128u * 64u;                  // one block's im2col rows
 constexpr uint32_t STEM_TC_B_BYTES = 16u * 64u;                   // the filters
 constexpr uint32_t STEM_TC_TMEM_COLS = 64u;
-constexpr int STEM_TC_THREADS = 320;                              // 10 warps
+constexpr int STEM_TC_BG = 2;                                     // im2col builder groups (4 warps each)
+constexpr int STEM_TC_DG = 3;                                     // drain groups (4 warps each)
+constexpr int STEM_TC_THREADS = 64 + 128 * (STEM_TC_BG + STEM_TC_DG);
+static_assert(STEM_TC_BG <= STEM_TC_NB, "every builder group takes a block of each tile");
 
 // Builds the filter rows as fp16 hi and lo terms (w = hi + lo to ~22 bits; one term leaves a
 // weight error common to every pixel, which the det network amplifies past the parity bound): row n,
@@ -1165,7 +1171,7 @@ __global__ void __launch_bounds__(STEM_TC_THREADS, 1) stem_tc_kernel(const __gri
     abort_flag = 0;
     for (int i = 0; i < STEM_TC_NBUF; i++) {
       mbar_init(smem_u32(&tfull[i]), 1);
-      mbar_init(smem_u32(&tempty[i]), 128);
+      mbar_init(smem_u32(&tempty[i]), 128 * STEM_TC_BG);
     }
     for (int i = 0; i < STEM_TC_NA; i++) {
       mbar_init(smem_u32(&afull[i]), 128);
@@ -1231,16 +1237,17 @@ __global__ void __launch_bounds__(STEM_TC_THREADS, 1) stem_tc_kernel(const __gri
       tc_commit_p(ld, smem_u32(&accf[ac]));
       mma_done = g + 1;
     }
-  } else if (warp >= 2 && warp < 6) {
-    // ---- im2col rows: thread = one row of every block
-    const int row = tid - 64;
+  } else if (warp < 2 + 4 * STEM_TC_BG) {
+    // ---- im2col rows: BG groups of four warps take the blocks of each tile round-robin; thread =
+    // one row of its group's blocks
+    const int bg = (warp - 2) >> 2, row = tid - 64 - 128 * bg;
     for (int i = 0; i < ntiles; i++) {
       const int b = i % STEM_TC_NBUF;
       bool ok = mbar_wait(smem_u32(&tfull[b]), (uint32_t)(i / STEM_TC_NBUF) & 1u, a.err, SDX_DEV_WAIT_FULL,
                           &abort_flag);
       if (!ok) break;
       const float* tile = bufs + b * (kBufBytes / 4);
-      for (int blk = 0; blk < STEM_TC_NB && ok; blk++) {
+      for (int blk = bg; blk < STEM_TC_NB && ok; blk += STEM_TC_BG) {
         const int g = i * STEM_TC_NB + blk, sl = g % STEM_TC_NA;
         if (g >= STEM_TC_NA)
           ok = mbar_wait(smem_u32(&aempty[sl]), (uint32_t)(g / STEM_TC_NA - 1) & 1u, a.err, SDX_DEV_WAIT_EMPTY,
@@ -1253,10 +1260,11 @@ __global__ void __launch_bounds__(STEM_TC_THREADS, 1) stem_tc_kernel(const __gri
       if (!ok) break;
       mbar_arrive(smem_u32(&tempty[b]));
     }
-  } else if (warp >= 6 && warp < 10) {
-    // ---- drain: warp w reads TMEM lanes 32 (w % 4) .. of each accumulator
-    const int q = warp & 3;
-    for (int g = 0; g < nblk; g++) {
+  } else {
+    // ---- drain: DG groups of four warps take the blocks round-robin (each block's TMEM load, bias,
+    // activation and stores are one latency chain per warp); warp w reads TMEM lanes 32 (w % 4) ..
+    const int q = warp & 3, dg = (warp - 2 - 4 * STEM_TC_BG) >> 2;
+    for (int g = dg; g < nblk; g += STEM_TC_DG) {
       const int ac = g % STEM_TC_NACC;
       const bool ok = __all_sync(0xffffffffu, mbar_wait(smem_u32(&accf[ac]), (uint32_t)(g / STEM_TC_NACC) & 1u, a.err,
                                                         SDX_DEV_WAIT_ACC_FULL, &abort_flag));
