@@ -15,12 +15,10 @@ constexpr int TC_EPI_GROUPS_MAX = 4;
 constexpr int tc_threads(int groups) { return 64 + 128 * groups; }
 constexpr int TC_DW_WARPS = 4;  // depthwise warps of the fused depthwise -> pointwise form (EPI = 6): one
                                 // per scheduler, so that the CTA stays within 128 registers a thread
-// kx-in-N 3x3 convs (EPI = 2) add TC_KXN_MMA_WARPS - 1 MMA-issuing warps: their thin N = 96 MMAs
-// are issue bound from one warp; the warps take the tiles round-robin (FPN p2 at N=256: one warp
-// 0.46 ms, two 0.37, three 0.39)
-constexpr int TC_KXN_MMA_WARPS = 2;
+// kx-in-N 3x3 convs (EPI = 2) add a second MMA-issuing warp: their thin N = 96 MMAs are issue
+// bound from one warp; two warps take alternate tiles
 constexpr int tc_threads_epi(int groups, int epi) {
-  return tc_threads(groups) + (epi == 6 ? 32 * TC_DW_WARPS : epi == 2 ? 32 * (TC_KXN_MMA_WARPS - 1) : 0);
+  return tc_threads(groups) + (epi == 6 ? 32 * TC_DW_WARPS : epi == 2 ? 32 : 0);
 }
 constexpr int TC_MAX_STAGES = 8;  // <= 32 (ring slots are tracked in 32-bit masks)
 constexpr int TC_SMEM_LIMIT = 227 * 1024;

@@ -311,8 +311,8 @@ struct MmaSingle {
   uint64_t dconst, bd0;
   int S, nacc, n_tiles, nt_step, nt0;
 };
-// Tiles of ordinals w, w + nw, ... of the CTA's sequence (nw MMA-issuing warps, this one w < nw):
-// ordinal o uses ring slot o mod S and accumulator o mod nacc (S >= nw, nacc >= nw).
+// Tiles of ordinals w, w + nw, ... of the CTA's sequence (nw MMA-issuing warps, this one w < nw <= 2):
+// ordinal o uses ring slot o mod S and accumulator o mod nacc (S >= nw, nacc a multiple of nw).
 template <int BT, int NK, bool TWO, int CPS>
 __device__ __noinline__ void mma_single_loop(uint32_t ld, const MmaSingle m, int tile0, int total_tiles, int tstep,
                                              int w, int nw, uint64_t* full, uint64_t* empty, uint64_t* accf,
@@ -782,7 +782,7 @@ __global__ void __launch_bounds__(tc_threads_epi(G, EPI), 1)
       mbar_init(smem_u32(&acce[i]), 128);
     }
     for (int i = 0; i < G * 2 * 4; i++) mbar_init(smem_u32(&resb[i]), 1);
-    mbar_init(smem_u32(drain), EPI == 2 ? TC_KXN_MMA_WARPS : 1);  // one commit per MMA-issuing warp
+    mbar_init(smem_u32(drain), EPI == 2 ? 2 : 1);  // one commit per MMA-issuing warp
     mbar_init(smem_u32(bres), 1);
     if (DWF) {
       uint64_t* hb = reinterpret_cast<uint64_t*>(smem + a.dw_off + (size_t)a.dw_slots * a.dw_slot_bytes +
@@ -1056,10 +1056,10 @@ __global__ void __launch_bounds__(tc_threads_epi(G, EPI), 1)
       if (b_loads > 0) mbar_wait_drain(smem_u32(bres), (b_loads - 1) & 1u, a.err, SDX_DEV_WAIT_DRAIN);
     }
     __syncwarp();
-  } else if (warp == 1 || (EPI == 2 && warp >= 2 + 4 * G)) {
-    // MMA issue: warp 1, and for kx-in-N tiles more warps taking the tiles of the single-stage loop
-    // round-robin (mw = 1, 2, ...); every other path runs on warp 1 alone
-    const int mw = warp == 1 ? 0 : warp - (2 + 4 * G) + 1;
+  } else if (warp == 1 || (EPI == 2 && warp == 2 + 4 * G)) {
+    // MMA issue: warp 1, and for kx-in-N tiles a second warp taking every other tile of the
+    // single-stage loop (mw = 1); every other path runs on warp 1 alone
+    const int mw = warp == 1 ? 0 : 1;
     const uint32_t ld = elect_leader();
     {
       const uint32_t idesc = umma_idesc_f16(TC_BM, a.BN);
@@ -1083,8 +1083,8 @@ __global__ void __launch_bounds__(tc_threads_epi(G, EPI), 1)
       // one-tap tiles (pointwise), and the kx-in-N 3x3 convs (three row taps, one weight term)
       const bool single = kblocks == 1 && a.b_resident && (a.b_taps == 1 || (a.b_taps == 3 && a.wterms == 1)) &&
                           a.cps <= 4 && (nk == 1 || nk == 2 || nk == 4) && !imgw;
-      const int nmw = (EPI == 2 && single && S >= TC_KXN_MMA_WARPS && a.nacc >= TC_KXN_MMA_WARPS) ? TC_KXN_MMA_WARPS : 1;
-      if (mw >= nmw) ok = false;  // a warp without tiles: only its drain commit below
+      const int nmw = (EPI == 2 && single && S >= 2 && (a.nacc & 1) == 0) ? 2 : 1;
+      if (mw >= nmw) ok = false;  // the second warp has no tiles: only its drain commit below
       if (ok && single) {
         MmaSingle m;
         m.d0 = tmem_base;
