@@ -1065,7 +1065,7 @@ __device__ __forceinline__ void stem_tile_compute(const DirectArgs& a, const flo
 // ring of TMEM accumulators, DG groups of four warps drain them (bias, activation, fp16 NHWC stores).
 // Each group handles every BG-th (DG-th) block: one group per role left each block's work as a
 // single latency chain per warp (N=256: 0.64 ms with one of each, 0.45 with two, 0.42 with two
-// builder and three drain groups; four builder groups gain nothing). Every hand-off
+// builder and three drain groups; four builder or four drain groups gain nothing). Every hand-off
 // is an mbarrier, so building, MMAs, draining and loading overlap. A row = one output pixel, K = 27
 // taps (k = (ky*3 + kx)*3 + c, padded to 32) of fp16-rounded inputs in 64-byte rows under the 64-byte
 // swizzle; B = the 16 filters as fp16 hi and lo terms (the same layout), fp32 accumulation.
